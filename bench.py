@@ -1,0 +1,420 @@
+#!/usr/bin/env python3
+"""Benchmark of the token loop on the BASELINE.json configs[1] workload.
+
+One step = one chat turn of the Qwen3-1.7B-shaped Q4_K_M synthetic model:
+a 2811-token seeded prompt prefill, then three rounds of (append 40 seeded
+tokens, 64-token decode) with T=0.7, top_k=20, top_p=0.8 and a fixed seed.
+
+* value    decode tok/s, device time from CUDA events on the session stream;
+           weights (1.1 GB per token, > L2) and KV resident in HBM.
+* e2e      the same decode tok/s measured on the host around the C-ABI calls
+           (rpgb_prefill / rpgb_generate with host buffers: the H2D of the
+           token ids and the D2H of the generated ids are inside).
+* roofline the decode matvec (96.8 % of the reference's decode kernel time):
+           every matrix of the model plus lm_head, one launch each, CUDA events
+           on the launching stream, algorithmic bytes = M*K/256*{144,210} + x + y.
+* cpu_baseline  the CPU restatement of the reference loop (oracle/, the
+           reference's own CPU engine is not vendored), bounded sample.
+
+Multi-GPU (torchrun): one independent session per GPU (the path shards by
+session, no collective on the data path); value = all ranks' decode tokens /
+max over ranks of the decode time.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PROMPT_LEN = 2811
+ROUNDS = 3
+APPEND = 40
+DECODE = 64
+SAMPLE = (0.7, 20, 0.8)
+SEED = 1234
+MODEL = "qwen3-1.7b"
+METRIC = "batch-1 decode tok/s + prefill tok/s (Qwen3-1.7B Q4_K_M); matvec % HBM peak"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--model", default=MODEL)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-roofline", action="store_true")
+    ap.add_argument("--with-ref-gpu", action="store_true",
+                    help="also time the reference's own CUDA engine (built from its sources) on the same turn")
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = tempfile.mktemp(suffix=".csv")
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        try:
+            rows = [ln.split(",") for ln in open(self.path).read().strip().splitlines()]
+        except Exception:
+            return None
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx = max(mx, float(r[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def cpu_baseline(path, n_prompt=64, n_decode=8):
+    """The oracle (CPU restatement of the reference loop) on all host cores, bounded sample."""
+    from oracle.oracle import OracleModel, OracleSession
+    from rpgbarenginecuda_b200 import synthetic
+
+    cores = os.cpu_count()
+    om = OracleModel(path, 4096)
+    s = OracleSession(om, 4096, cores)
+    prompt = synthetic.seeded_tokens(n_prompt, 0, om.vocab)
+    t0 = time.perf_counter()
+    s.prefill(prompt)
+    t1 = time.perf_counter()
+    s.generate(*SAMPLE, SEED, n_decode)
+    t2 = time.perf_counter()
+    s.close()
+    om.close()
+    return {"decode_tok_s": n_decode / (t2 - t1), "prefill_tok_s": n_prompt / (t1 - t0), "cores": cores,
+            "sample": f"{n_prompt}-token prefill + {n_decode}-token decode (T=0.7,k=20,p=0.8) of the {MODEL} turn",
+            "seconds": t2 - t0}
+
+
+def reference_arm(args):
+    world, rank, _ = dist()
+    if rank != 0:
+        return 0
+    from rpgbarenginecuda_b200 import synthetic
+
+    path = synthetic.cached_model(args.model, seed=0)
+    vals, pre = [], []
+    for i in range(args.warmup + args.steps):
+        r = cpu_baseline(path, 32, 4)
+        if i >= args.warmup:
+            vals.append(r["decode_tok_s"])
+            pre.append(r["prefill_tok_s"])
+    v = statistics.mean(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000.0 * 4 / v, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "prefill_tok_s": round(statistics.mean(pre), 4),
+        "config": {"workload": f"{MODEL} turn sample: 32-token prefill + 4-token decode per step, "
+                               "T=0.7 top_k=20 top_p=0.8", "model": args.model},
+        "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": "32-token prefill + 4-token decode per step (the reference's CPU engine "
+                                   "tools/cpu_ref_gen links sources that are not vendored)"},
+        "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def matvec_roofline(path, device, peak):
+    """Decode matvec over every matrix of the model (one decode's weight stream)."""
+    import numpy as np
+    import torch
+    from gguf import GGUFReader
+
+    from rpgbarenginecuda_b200 import Matrix
+
+    rd = GGUFReader(path)
+    mats = []
+    for t in rd.tensors:
+        if len(t.shape) != 2 or int(t.tensor_type) not in (12, 14):
+            continue
+        cols, rows = int(t.shape[0]), int(t.shape[1])
+        mats.append((t.name, int(t.tensor_type), rows, cols, np.asarray(t.data).view(np.uint8).reshape(-1)))
+    handles = [(Matrix(q, r, c, b, device), q, r, c) for (_, q, r, c, b) in mats]
+    del mats, rd
+    kmax = max(c for _, _, _, c in handles)
+    rmax = max(r for _, _, r, _ in handles)
+    x = torch.randn(kmax, device=f"cuda:{device}")
+    y = torch.empty(rmax, device=f"cuda:{device}")
+    stream = torch.cuda.current_stream(device)
+    sp = stream.cuda_stream
+    for m, _, _, _ in handles:  # warm-up pass
+        m.matvec(x.data_ptr(), 1, y.data_ptr(), sp)
+    torch.cuda.synchronize(device)
+    total_ms, total_bytes, launches, per = 0.0, 0, 0, {}
+    for _ in range(3):
+        for m, q, r, c in handles:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            m.matvec(x.data_ptr(), 1, y.data_ptr(), sp)
+            e1.record(stream)
+            e1.synchronize()
+            ms = e0.elapsed_time(e1)
+            b = r * c // 256 * (144 if q == 12 else 210) + 4 * (r + c)
+            total_ms += ms
+            total_bytes += b
+            launches += 1
+            key = f"{'q4k' if q == 12 else 'q6k'}_{r}x{c}"
+            per.setdefault(key, [0.0, 0, 0])
+            per[key][0] += ms
+            per[key][1] += b
+            per[key][2] += 1
+    for m, _, _, _ in handles:
+        m.close()
+    achieved = total_bytes / (total_ms * 1e-3) / 1e9
+    shapes = {k: round(v[1] / (v[0] * 1e-3) / 1e9, 1) for k, v in per.items()}
+    return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "traffic": None,
+            "kernel": "MatvecKernel (decode Q4_K/Q6_K dequant-matvec, n=1)",
+            "bytes_per_launch": round(total_bytes / launches), "avg_launch_us": round(1000 * total_ms / launches, 2),
+            "per_shape_gbs": shapes}
+
+
+def ours(args):
+    import numpy as np
+    import torch
+
+    from rpgbarenginecuda_b200 import Model, SampleOptions, Session, launch_count, synthetic
+
+    world, rank, local = dist()
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as tdist
+
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                 device_id=torch.device(f"cuda:{local}"))
+        pg = tdist
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+        torch.cuda.synchronize()
+
+    path = synthetic.cached_model(args.model, seed=0)
+    model = Model(path, device=local, max_pos=4096)
+    sess = Session(model, 4096)
+    V = model.vocab
+    stream = torch.cuda.ExternalStream(sess.stream_ptr, device=local)
+    prompt = synthetic.seeded_tokens(PROMPT_LEN, 1000 + rank, V)
+    appends = [synthetic.seeded_tokens(APPEND, 2000 + 10 * rank + r, V) for r in range(ROUNDS)]
+    opts = SampleOptions(*SAMPLE)
+
+    def turn(timing):
+        sess.set_len(0)
+        ev = []
+        h0 = time.perf_counter()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        sess.prefill(prompt, want_logits=False)
+        e1.record(stream)
+        ev.append(("prefill", e0, e1, PROMPT_LEN))
+        host_prefill = time.perf_counter() - h0
+        host_decode, n_dec = 0.0, 0
+        for r in range(ROUNDS):
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a0.record(stream)
+            sess.prefill(appends[r], want_logits=False)
+            a1.record(stream)
+            ev.append(("append", a0, a1, APPEND))
+            d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            h1 = time.perf_counter()
+            d0.record(stream)
+            ids = sess.generate(opts, SEED, DECODE)
+            d1.record(stream)
+            host_decode += time.perf_counter() - h1
+            n_dec += len(ids)
+            ev.append(("decode", d0, d1, len(ids)))
+        torch.cuda.synchronize()
+        for kind, a, b, n in ev:
+            timing[kind][0] += a.elapsed_time(b)
+            timing[kind][1] += n
+        timing["host_decode"][0] += host_decode * 1e3
+        timing["host_decode"][1] += n_dec
+        timing["host_prefill"][0] += host_prefill * 1e3
+        timing["host_prefill"][1] += PROMPT_LEN
+
+    for _ in range(args.warmup):
+        turn({k: [0.0, 0] for k in ("prefill", "append", "decode", "host_decode", "host_prefill")})
+    barrier()
+    timing = {k: [0.0, 0] for k in ("prefill", "append", "decode", "host_decode", "host_prefill")}
+    l0 = launch_count()
+    with Clocks(local) as clk:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        w0 = time.perf_counter()
+        for _ in range(args.steps):
+            turn(timing)
+        t1.record()
+        barrier()
+        wall = time.perf_counter() - w0
+    launches = launch_count() - l0
+    total_ms = t0.elapsed_time(t1)
+    dec_ms, dec_tok = timing["decode"]
+    # max over ranks of the decode time, sum of tokens
+    agg = np.array([dec_ms, dec_tok, timing["prefill"][0], timing["host_decode"][0], total_ms], dtype=np.float64)
+    if pg is not None:
+        t = torch.tensor(agg, device=f"cuda:{local}")
+        mx = t.clone()
+        pg.all_reduce(mx, op=pg.ReduceOp.MAX)
+        sm = t.clone()
+        pg.all_reduce(sm, op=pg.ReduceOp.SUM)
+        dec_ms_max, pre_ms_max, host_dec_max, total_max = float(mx[0]), float(mx[2]), float(mx[3]), float(mx[4])
+        dec_tok_all = float(sm[1])
+    else:
+        dec_ms_max, pre_ms_max, host_dec_max, total_max = dec_ms, timing["prefill"][0], timing["host_decode"][0], total_ms
+        dec_tok_all = dec_tok
+    value = dec_tok_all / (dec_ms_max * 1e-3)
+    prefill_tok_s = world * PROMPT_LEN * args.steps / (pre_ms_max * 1e-3)
+    e2e = dec_tok_all / (host_dec_max * 1e-3)
+    clocks = clk.summary()
+    stats = sess.stats()
+
+    roof = None
+    if rank == 0 and not args.no_roofline:
+        sess.close()
+        model.close()
+        torch.cuda.empty_cache()
+        hbm, kind = peaks()
+        roof = matvec_roofline(path, local, hbm)
+        roof["peak_kind"] = kind
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        c = cpu_baseline(path)
+        cpu = {"value": round(c["decode_tok_s"], 4), "unit": "tok/s", "cores": c["cores"], "kind": "port",
+               "sample": c["sample"], "prefill_tok_s": round(c["prefill_tok_s"], 3)}
+    ref_gpu = None
+    if rank == 0 and args.with_ref_gpu:
+        ref_gpu = reference_gpu_turn(path, prompt, appends)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(total_max / args.steps, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,0.02) weights quantised to Q4_K/Q6_K, seeded token ids)",
+            "prefill_tok_s": round(prefill_tok_s, 1),
+            "config": {"workload": f"{args.model} turn: {PROMPT_LEN}-token prefill + {ROUNDS} x ({APPEND} appended "
+                                   f"+ {DECODE} decoded) tokens, T=0.7 top_k=20 top_p=0.8",
+                       "model": args.model, "global_batch": world, "seq_len": PROMPT_LEN + ROUNDS * (APPEND + DECODE),
+                       "parallelism": f"sessions x{world}",
+                       "l2": "inputs larger than L2 (1.1 GB of weights streamed per token)"},
+            "e2e": {"value": round(e2e, 2), "unit": "tok/s",
+                    "h2d_bytes_per_step": 4 * (PROMPT_LEN + ROUNDS * APPEND) + 8 * (1 + 2 * ROUNDS),
+                    "d2h_bytes_per_step": 4 * ROUNDS * DECODE},
+            "gpu_launches": int(launches),
+            "kernels_per_decode_step": stats["kernels_per_step"],
+            "wall_s": round(wall, 3),
+        }
+        if clocks is not None:
+            line["clocks"] = clocks
+        if roof is not None:
+            line["roofline"] = roof
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        if ref_gpu is not None:
+            line["reference_gpu"] = ref_gpu
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.destroy_process_group()
+    return 0
+
+
+def reference_gpu_turn(path, prompt, appends):
+    """The reference's own CUDA engine (compiled from its sources) on one turn."""
+    from oracle.oracle import RefShim
+
+    rs = RefShim()
+    s = rs.session(path, 4096, 4096)
+    V = 151936
+    t0 = time.perf_counter()
+    s.prefill(prompt, V)
+    t1 = time.perf_counter()
+    dec_t, dec_n = 0.0, 0
+    for a in appends:
+        s.prefill(a, V)
+        d0 = time.perf_counter()
+        ids = s.generate(*SAMPLE, SEED, DECODE, use_graph=True)
+        dec_t += time.perf_counter() - d0
+        dec_n += len(ids)
+    s.close()
+    return {"prefill_tok_s": round(PROMPT_LEN / (t1 - t0), 2), "decode_tok_s": round(dec_n / dec_t, 2),
+            "note": "reference GpuForwardFull / GpuGenerate(use_graph) built for sm_100a, host wall clock"}
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return reference_arm(args)
+    return ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,135 @@
+/* rpg_b200.h -- C ABI of the B200 token loop (model, session, prefill, generate)
+ * and of its operators.  Plain pointers and sizes only; every function is
+ * exported from librpg_engine_b200.so next to the ten rpg_engine_* functions.
+ *
+ * These are the entry points the reference's own tools bind to its internal
+ * C++ API (tools/gen_check.cu, tools/graph_check.cu, tools/sample_check.cu,
+ * tools/dequant_check.cu, tools/matmul_bench.cu).  The public rpg_engine_*
+ * ABI (rpg_engine.h) cannot carry raw token ids or top_k / top_p
+ * (src/engine.cc:459-469, 552-553), so parity and benchmarking go through
+ * these, exactly as the reference's tools bypass its ABI.
+ *
+ * Conventions (same as the reference ABI, include/rpg_engine.h:46-48):
+ * handles are >= 0 when valid; functions returning int32_t return 0 (or a
+ * handle) on success and a negative value on failure with the message in
+ * rpgb_last_error() (thread-local).  No C++ exception crosses this boundary.
+ * Host buffers are plain host memory; "_dev" arguments are device pointers on
+ * the model's device and `stream` is a cudaStream_t (NULL = legacy stream).
+ */
+#ifndef RPG_B200_H
+#define RPG_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define RPGB_API __attribute__((visibility("default")))
+#else
+#define RPGB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Sampling parameters; same fields and defaults as the reference's
+ * SampleOptions (src/sampler.h:35-44): temperature <= 0 is greedy, top_k is
+ * active iff 1 < top_k < vocab, top_p is active iff 0 < top_p < 1. */
+typedef struct rpgb_sample_options {
+  float temperature;
+  int32_t top_k;
+  float top_p;
+} rpgb_sample_options;
+
+RPGB_API const char* rpgb_version(void);
+RPGB_API const char* rpgb_last_error(void);
+
+/* ------------------------------------------------------------------ model */
+
+/* Loads a GGUF (qwen3, Q4_K / Q6_K matrices) onto `device` with a RoPE table
+ * of min(max_pos, context_length) positions.  Replaces GpuModel::Load
+ * (src/gpu_model.cu:148-246).  Returns a model handle. */
+RPGB_API int32_t rpgb_model_load(const char* gguf_path, int32_t device, int32_t max_pos);
+RPGB_API void rpgb_model_free(int32_t model);
+
+/* Shape of a loaded model, written to out[0..11]: n_layers, hidden, n_heads,
+ * n_kv_heads, head_dim, ffn, vocab, context_length, rope_positions, eos_id,
+ * device, num_sms.  Mirrors ModelMeta (src/model_meta.h:27-62). */
+RPGB_API int32_t rpgb_model_shape(int32_t model, int32_t* out, int32_t n_out);
+/* Device bytes of the resident weights (GpuModel::device_bytes). */
+RPGB_API int64_t rpgb_model_device_bytes(int32_t model);
+
+/* ------------------------------------------------------------------ session */
+
+/* A session owns an fp16 KV cache of max_seq positions, scratch buffers, a
+ * stream and its decode graph (GpuKvCache + GpuScratch,
+ * src/kv_cache_gpu.cu:16-36, src/qwen3_gpu.h:79-98). */
+RPGB_API int32_t rpgb_session_create(int32_t model, int64_t max_seq);
+RPGB_API void rpgb_session_free(int32_t session);
+RPGB_API int64_t rpgb_session_len(int32_t session);
+/* GpuKvCache::SetLen (src/kv_cache_gpu.cu:54-58): positions >= len are
+ * forgotten; the next generate needs a prefill first. */
+RPGB_API int32_t rpgb_session_set_len(int32_t session, int64_t len);
+
+/* GpuForwardFull with a KV cache (src/qwen3_gpu.cu:236-276): appends n
+ * tokens at positions len .. len+n-1; the logits of the last position stay on
+ * the device for rpgb_generate and are copied to last_logits[vocab] when that
+ * pointer is not NULL. */
+RPGB_API int32_t rpgb_prefill(int32_t session, const int32_t* tokens, int64_t n, float* last_logits);
+
+/* GpuGenerate (src/qwen3_gpu.cu:599-640): samples from the current logits
+ * with counter = absolute position, forwards every returned token (the stop
+ * token included), stops after max_tokens or at the first id in stop_ids.
+ * out_ids[max_tokens] receives the tokens, *n_out their count.  step_logits,
+ * when not NULL, receives [max_tokens][vocab]: the distribution each token was
+ * sampled from (GpuGenerateOptions::step_logits). */
+RPGB_API int32_t rpgb_generate(int32_t session, const rpgb_sample_options* opt, uint64_t seed, int32_t max_tokens,
+                               const int32_t* stop_ids, int32_t n_stop, int32_t* out_ids, int32_t* n_out,
+                               float* step_logits);
+
+/* Kernel launches per decode step and whether the step graph is recorded
+ * (the reference's graph_check asserts graph_exec != nullptr). */
+RPGB_API int32_t rpgb_session_stats(int32_t session, int32_t* kernels_per_step, int32_t* graph_ready,
+                                    int64_t* graph_launches);
+
+/* The session's CUDA stream (a cudaStream_t), so a caller can time the
+ * session's work with CUDA events recorded on that stream. */
+RPGB_API void* rpgb_session_stream(int32_t session);
+
+/* Kernels this library has launched so far in the process, counting every
+ * node of a replayed decode graph (instrumentation for benchmarks). */
+RPGB_API int64_t rpgb_launch_count(void);
+
+/* ------------------------------------------------------------------ operators */
+
+/* Uploads one GGUF matrix (Q4_K or Q6_K bytes, rows x cols) to `device` in
+ * the engine's layout; returns a matrix handle (GpuModel::UploadMatrix,
+ * src/gpu_model.cu:44-57). */
+RPGB_API int32_t rpgb_matrix_upload(int32_t device, uint32_t ggml_type, int64_t rows, int64_t cols,
+                                    const void* gguf_bytes);
+RPGB_API void rpgb_matrix_free(int32_t matrix);
+
+/* dst_dev[r][c] = dequant(row0 + r, c): bit-exact per element
+ * (GpuDequantRow, src/kernels_gpu.cu:929-937). */
+RPGB_API int32_t rpgb_matrix_dequant(int32_t matrix, int64_t row0, int64_t n_rows, float* dst_dev, void* stream);
+
+/* out_dev[t][r] = sum_c W[r][c] * x_dev[t][c] (GpuMatMulQuant,
+ * src/kernels_gpu.cu:939-975): n_tok == 1 uses the decode matvec, larger n
+ * the prefill GEMM. */
+RPGB_API int32_t rpgb_matrix_matvec(int32_t matrix, const float* x_dev, int64_t n_tok, float* out_dev,
+                                    void* stream);
+
+/* GpuSampleToken / GpuFilterToProbs (src/sampler_gpu.cu:393-440): samples
+ * one token of logits_dev[n] with u = counter_uniform(seed, counter) into
+ * *out_tok_dev.  When probs_dev is not NULL it receives the filtered
+ * distribution (the general path runs; otherwise the fast top-k path may). */
+RPGB_API int32_t rpgb_sample(const float* logits_dev, int32_t n, const rpgb_sample_options* opt, uint64_t seed,
+                             uint64_t counter, float* probs_dev, int32_t* out_tok_dev, void* stream);
+
+/* u = H(seed, counter) in [0, 1) (DevCounterUniform, src/sampler_gpu.cu:364). */
+RPGB_API float rpgb_counter_uniform(uint64_t seed, uint64_t counter);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RPG_B200_H */

@@ -1,0 +1,155 @@
+"""B200-native (sm_100a) token loop of RPGBarEngineCUDA.
+
+Python view of the C ABI in include/rpg_b200.h.  Names follow the reference's
+internal API that its own tools drive (tools/gen_check.cu, sample_check.cu,
+matmul_bench.cu): a Model is GpuModel::Load, a Session is the KV cache plus
+scratch (GpuKvCache + GpuScratch), ``prefill`` is GpuForwardFull with a cache,
+``generate`` is GpuGenerate, ``Matrix.matvec`` is GpuMatMulQuant and
+``sample`` is GpuSampleToken / GpuFilterToProbs.  The ten-function public ABI
+(include/rpg_engine.h) is exported by the same library.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from ._lib import EngineError, SampleOptions, check, load_engine  # noqa: F401
+
+__all__ = ["Model", "Session", "Matrix", "SampleOptions", "EngineError", "sample", "counter_uniform", "launch_count",
+           "library_path", "GGML_Q4_K", "GGML_Q6_K"]
+
+GGML_Q4_K = 12
+GGML_Q6_K = 14
+
+
+def library_path() -> str:
+    from ._lib import ENGINE_SO
+    return ENGINE_SO
+
+
+class Model:
+    """Weights of one GGUF resident on one device."""
+
+    def __init__(self, path: str, device: int = 0, max_pos: int = 4096):
+        self._lib = load_engine()
+        self.path = path
+        self.handle = check(self._lib.rpgb_model_load(path.encode(), device, max_pos), "model_load")
+        out = (ctypes.c_int32 * 12)()
+        check(self._lib.rpgb_model_shape(self.handle, out, 12), "model_shape")
+        keys = ["n_layers", "hidden", "n_heads", "n_kv_heads", "head_dim", "ffn", "vocab", "context_length",
+                "rope_positions", "eos_id", "device", "num_sms"]
+        self.shape = dict(zip(keys, list(out)))
+        self.vocab = self.shape["vocab"]
+
+    @property
+    def device_bytes(self) -> int:
+        return int(self._lib.rpgb_model_device_bytes(self.handle))
+
+    def close(self):
+        if self.handle is not None and self.handle >= 0:
+            self._lib.rpgb_model_free(self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+
+class Session:
+    """fp16 KV cache + decode state of one conversation."""
+
+    def __init__(self, model: Model, max_seq: int = 4096):
+        self._lib = load_engine()
+        self.model = model
+        self.max_seq = max_seq
+        self.handle = check(self._lib.rpgb_session_create(model.handle, max_seq), "session_create")
+
+    def __len__(self) -> int:
+        return int(self._lib.rpgb_session_len(self.handle))
+
+    def set_len(self, n: int):
+        check(self._lib.rpgb_session_set_len(self.handle, n), "session_set_len")
+
+    def prefill(self, tokens, want_logits: bool = True):
+        toks = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        out = np.empty(self.model.vocab, dtype=np.float32) if want_logits else None
+        check(self._lib.rpgb_prefill(self.handle, toks.ctypes.data, toks.size,
+                                     out.ctypes.data if out is not None else None), "prefill")
+        return out
+
+    def generate(self, opts: SampleOptions | None = None, seed: int = 0, max_tokens: int = 32, stop=(),
+                 step_logits: bool = False):
+        opts = opts or SampleOptions(0.0, 0, 1.0)
+        stop_arr = np.ascontiguousarray(np.asarray(list(stop), dtype=np.int32))
+        ids = np.empty(max_tokens, dtype=np.int32)
+        n_out = ctypes.c_int32(0)
+        steps = np.empty((max_tokens, self.model.vocab), dtype=np.float32) if step_logits else None
+        check(self._lib.rpgb_generate(self.handle, ctypes.byref(opts), seed, max_tokens,
+                                      stop_arr.ctypes.data if stop_arr.size else None, stop_arr.size,
+                                      ids.ctypes.data, ctypes.byref(n_out),
+                                      steps.ctypes.data if steps is not None else None), "generate")
+        n = n_out.value
+        return (ids[:n].copy(), steps[:n].copy()) if step_logits else ids[:n].copy()
+
+    def stats(self):
+        k, g, n = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int64()
+        check(self._lib.rpgb_session_stats(self.handle, ctypes.byref(k), ctypes.byref(g), ctypes.byref(n)),
+              "session_stats")
+        return {"kernels_per_step": k.value, "graph_ready": bool(g.value), "graph_launches": n.value}
+
+    @property
+    def stream_ptr(self) -> int:
+        """The session's cudaStream_t (for CUDA-event timing of its work)."""
+        return int(self._lib.rpgb_session_stream(self.handle) or 0)
+
+    def close(self):
+        if self.handle is not None and self.handle >= 0:
+            self._lib.rpgb_session_free(self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+
+class Matrix:
+    """One quantised matrix in the engine's device layout (operator entry)."""
+
+    def __init__(self, qtype: int, rows: int, cols: int, gguf_bytes: np.ndarray, device: int = 0):
+        self._lib = load_engine()
+        b = np.ascontiguousarray(gguf_bytes, dtype=np.uint8)
+        self.rows, self.cols, self.qtype = rows, cols, qtype
+        self.handle = check(self._lib.rpgb_matrix_upload(device, qtype, rows, cols, b.ctypes.data), "matrix_upload")
+
+    def dequant(self, row0: int, n_rows: int, dst_ptr: int, stream: int = 0):
+        check(self._lib.rpgb_matrix_dequant(self.handle, row0, n_rows, dst_ptr, stream or None), "matrix_dequant")
+
+    def matvec(self, x_ptr: int, n_tok: int, out_ptr: int, stream: int = 0):
+        check(self._lib.rpgb_matrix_matvec(self.handle, x_ptr, n_tok, out_ptr, stream or None), "matrix_matvec")
+
+    def close(self):
+        if self.handle is not None and self.handle >= 0:
+            self._lib.rpgb_matrix_free(self.handle)
+            self.handle = None
+
+
+def sample(logits_ptr: int, n: int, opts: SampleOptions, seed: int, counter: int, tok_ptr: int,
+           probs_ptr: int | None = None, stream: int = 0):
+    lib = load_engine()
+    check(lib.rpgb_sample(logits_ptr, n, ctypes.byref(opts), seed, counter, probs_ptr, tok_ptr, stream or None),
+          "sample")
+
+
+def launch_count() -> int:
+    """Kernels launched by the engine library so far (graph nodes counted per replay)."""
+    return int(load_engine().rpgb_launch_count())
+
+
+def counter_uniform(seed: int, counter: int) -> float:
+    return float(load_engine().rpgb_counter_uniform(seed, counter))

@@ -1,0 +1,480 @@
+// engine.cu -- session state, prefill, decode step graph, generate loop.
+#include "engine.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+
+#include "common.h"
+
+namespace rpgb {
+
+namespace {
+
+constexpr size_t kAlign = 256;
+size_t AlignUp(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+
+// Positions handled per attention split in decode; a graph is recorded once per
+// session, so the split count is fixed from max_seq and short contexts simply
+// leave the tail splits empty.
+constexpr int kPositionsPerSplit = 256;
+
+class Carver {
+ public:
+  void Add(size_t bytes) { total_ += AlignUp(bytes); }
+  size_t total() const { return total_; }
+  void Begin(uint8_t* base) {
+    base_ = base;
+    off_ = 0;
+  }
+  template <typename T>
+  T* Take(size_t count) {
+    T* p = reinterpret_cast<T*>(base_ + off_);
+    off_ += AlignUp(count * sizeof(T));
+    return p;
+  }
+
+ private:
+  size_t total_ = 0, off_ = 0;
+  uint8_t* base_ = nullptr;
+};
+
+bool SameOpts(const SampleOpts& a, const SampleOpts& b) {
+  return a.temperature == b.temperature && a.top_k == b.top_k && a.top_p == b.top_p;
+}
+
+}  // namespace
+
+Session::Session(const Model* m, int64_t max_seq) : m_(m), max_seq_(max_seq) {
+  const ModelMeta& c = m->meta();
+  RPGB_CHECK(max_seq > 0, "max_seq must be positive (got %lld)", static_cast<long long>(max_seq));
+  RPGB_CHECK(max_seq <= m->rope_positions(), "max_seq %lld exceeds the %d positions of the RoPE table",
+             static_cast<long long>(max_seq), m->rope_positions());
+  RPGB_CUDA(cudaSetDevice(m->device()));
+  RPGB_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+
+  layer_elems_ = static_cast<size_t>(c.n_kv_heads) * static_cast<size_t>(max_seq) * c.head_dim;
+  const size_t kv_bytes = layer_elems_ * c.n_layers * sizeof(__half);
+  RPGB_CUDA(cudaMalloc(&kc_, kv_bytes));
+  RPGB_CUDA(cudaMalloc(&vc_, kv_bytes));
+  // Positions >= len are never read, but zero the cache once so stale memory
+  // from another allocation can never leak into a result.
+  RPGB_CUDA(cudaMemsetAsync(kc_, 0, kv_bytes, stream_));
+  RPGB_CUDA(cudaMemsetAsync(vc_, 0, kv_bytes, stream_));
+
+  n_splits_ = static_cast<int>(std::max<int64_t>(1, (max_seq + kPositionsPerSplit - 1) / kPositionsPerSplit));
+  const int am_grid = MatvecGrid(c.vocab, 4, m->num_sms());
+  const int qkv = c.q_dim() + 2 * c.kv_dim();
+  Carver cv;
+  cv.Add(sizeof(float) * c.hidden);   // x
+  cv.Add(sizeof(float) * qkv);        // qkv
+  cv.Add(sizeof(float) * c.q_dim());  // attn
+  cv.Add(sizeof(float) * c.ffn);      // h
+  cv.Add(sizeof(float) * c.vocab);    // logits
+  cv.Add(sizeof(float) * c.vocab);    // probs
+  cv.Add(sizeof(int64_t));            // pos
+  cv.Add(sizeof(int32_t));            // tok
+  cv.Add(sizeof(int32_t) * (max_seq + 1));
+  cv.Add(sizeof(float) * AttentionPartialFloats(c.n_kv_heads, c.group(), n_splits_));
+  cv.Add(sizeof(uint32_t) * (c.n_kv_heads + 1));
+  cv.Add(sizeof(float) * am_grid);
+  cv.Add(sizeof(int32_t) * am_grid);
+  cv.Add(sizeof(float) * kCandBlocks * kFastTopK);
+  cv.Add(sizeof(int32_t) * kCandBlocks * kFastTopK);
+  cv.Add(sizeof(int32_t) * kCandBlocks);
+  cv.Add(sizeof(int32_t));
+  RPGB_CUDA(cudaMalloc(&dec_arena_, cv.total()));
+  RPGB_CUDA(cudaMemsetAsync(dec_arena_, 0, cv.total(), stream_));
+  cv.Begin(dec_arena_);
+  x_ = cv.Take<float>(c.hidden);
+  qkv_ = cv.Take<float>(qkv);
+  attn_ = cv.Take<float>(c.q_dim());
+  h_ = cv.Take<float>(c.ffn);
+  logits_ = cv.Take<float>(c.vocab);
+  probs_ = cv.Take<float>(c.vocab);
+  pos_ = cv.Take<int64_t>(1);
+  tok_ = cv.Take<int32_t>(1);
+  out_ids_ = cv.Take<int32_t>(max_seq + 1);
+  attn_part_ = cv.Take<float>(AttentionPartialFloats(c.n_kv_heads, c.group(), n_splits_));
+  tickets_ = cv.Take<uint32_t>(c.n_kv_heads + 1);
+  am_val_ = cv.Take<float>(am_grid);
+  am_idx_ = cv.Take<int32_t>(am_grid);
+  cand_val_ = cv.Take<float>(kCandBlocks * kFastTopK);
+  cand_idx_ = cv.Take<int32_t>(kCandBlocks * kFastTopK);
+  cand_cnt_ = cv.Take<int32_t>(kCandBlocks);
+  flag_ = cv.Take<int32_t>(1);
+  RPGB_CUDA(cudaStreamSynchronize(stream_));
+}
+
+Session::~Session() {
+  cudaSetDevice(m_->device());
+  if (stream_ != nullptr) cudaStreamSynchronize(stream_);
+  DropGraph();
+  cudaFree(kc_);
+  cudaFree(vc_);
+  cudaFree(dec_arena_);
+  cudaFree(pf_arena_);
+  if (host_ids_ != nullptr) cudaFreeHost(host_ids_);
+  if (stream_ != nullptr) cudaStreamDestroy(stream_);
+}
+
+void Session::DropGraph() {
+  if (graph_ != nullptr) {
+    cudaGraphExecDestroy(graph_);
+    graph_ = nullptr;
+  }
+}
+
+void Session::SetLen(int64_t n) {
+  RPGB_CHECK(n >= 0 && n <= max_seq_, "length %lld out of range [0, %lld]", static_cast<long long>(n),
+             static_cast<long long>(max_seq_));
+  if (n != len_) logits_valid_ = false;
+  len_ = n;
+}
+
+void Session::EnsurePrefill(int64_t n) {
+  if (n <= pf_cap_) return;
+  const ModelMeta& c = m_->meta();
+  int64_t cap = std::max<int64_t>(n, 64);
+  cap = (cap + 63) / 64 * 64;
+  Carver cv;
+  const int qkv = c.q_dim() + 2 * c.kv_dim();
+  cv.Add(sizeof(float) * cap * c.hidden);
+  cv.Add(sizeof(float) * cap * c.hidden);
+  cv.Add(sizeof(float) * cap * qkv);
+  cv.Add(sizeof(float) * cap * c.q_dim());
+  cv.Add(sizeof(float) * cap * c.q_dim());
+  cv.Add(sizeof(float) * cap * c.ffn);
+  cv.Add(sizeof(int32_t) * cap);
+  RPGB_CUDA(cudaStreamSynchronize(stream_));
+  cudaFree(pf_arena_);
+  pf_arena_ = nullptr;
+  RPGB_CUDA(cudaMalloc(&pf_arena_, cv.total()));
+  cv.Begin(pf_arena_);
+  pf_x_ = cv.Take<float>(cap * c.hidden);
+  pf_xn_ = cv.Take<float>(cap * c.hidden);
+  pf_qkv_ = cv.Take<float>(cap * qkv);
+  pf_q_ = cv.Take<float>(cap * c.q_dim());
+  pf_attn_ = cv.Take<float>(cap * c.q_dim());
+  pf_h_ = cv.Take<float>(cap * c.ffn);
+  pf_tok_ = cv.Take<int32_t>(cap);
+  pf_cap_ = cap;
+}
+
+void Session::Prefill(const int32_t* tokens, int64_t n, float* last_logits) {
+  const ModelMeta& c = m_->meta();
+  RPGB_CHECK(n > 0, "prompt is empty");
+  RPGB_CHECK(len_ + n <= max_seq_, "position %lld exceeds the KV cache capacity %lld",
+             static_cast<long long>(len_ + n), static_cast<long long>(max_seq_));
+  for (int64_t t = 0; t < n; ++t) {
+    RPGB_CHECK(tokens[t] >= 0 && tokens[t] < c.vocab, "token #%lld has id %d, out of range (vocab %d)",
+               static_cast<long long>(t), tokens[t], c.vocab);
+  }
+  RPGB_CUDA(cudaSetDevice(m_->device()));
+  EnsurePrefill(n);
+  const cudaStream_t s = stream_;
+  const int64_t pos0 = len_;
+  RPGB_CUDA(cudaMemcpyAsync(pf_tok_, tokens, sizeof(int32_t) * n, cudaMemcpyHostToDevice, s));
+  RPGB_CUDA(cudaMemcpyAsync(pos_, &pos0, sizeof(int64_t), cudaMemcpyHostToDevice, s));
+
+  const int H = c.hidden, qd = c.q_dim(), kvd = c.kv_dim(), qkv = qd + 2 * kvd;
+  const int nt = static_cast<int>(n);
+  LaunchEmbed(m_->embd(), pf_tok_, nt, pf_x_, nullptr, nullptr, s);
+  for (int l = 0; l < c.n_layers; ++l) {
+    const DevLayer& L = m_->layers()[static_cast<size_t>(l)];
+    __half* kc = kc_ + layer_elems_ * l;
+    __half* vc = vc_ + layer_elems_ * l;
+    LaunchRmsNormRows(pf_x_, L.attn_norm, nt, H, c.rms_eps, pf_xn_, s);
+    GemmParams g;
+    g.X = pf_xn_;
+    g.n_tok = nt;
+    g.ldx = H;
+    g.out = pf_qkv_;
+    g.ldo = qkv;
+    g.w = L.q;
+    g.out_off = 0;
+    LaunchGemm(g, Epi::kStore, s);
+    g.w = L.k;
+    g.out_off = qd;
+    LaunchGemm(g, Epi::kStore, s);
+    g.w = L.v;
+    g.out_off = qd + kvd;
+    LaunchGemm(g, Epi::kStore, s);
+    LaunchQkRopeKv(pf_qkv_, nt, qd, kvd, L.q_norm, L.k_norm, m_->rope(), c.rms_eps, pos_, kc, vc,
+                   static_cast<int32_t>(max_seq_), c.n_heads, c.n_kv_heads, pf_q_, s);
+    AttnParams a;
+    a.q = pf_q_;
+    a.q_stride = qd;
+    a.kc = kc;
+    a.vc = vc;
+    a.max_seq = static_cast<int32_t>(max_seq_);
+    a.pos = pos_;
+    a.n_heads = c.n_heads;
+    a.n_kv = c.n_kv_heads;
+    a.scale = 1.0f / sqrtf(static_cast<float>(c.head_dim));
+    a.out = pf_attn_;
+    a.n_splits = 1;
+    a.fused = 0;
+    LaunchAttention(a, nt, s);
+    GemmParams o;
+    o.w = L.o;
+    o.X = pf_attn_;
+    o.n_tok = nt;
+    o.ldx = qd;
+    o.out = pf_x_;
+    o.ldo = H;
+    o.resid = pf_x_;
+    o.ldr = H;
+    LaunchGemm(o, Epi::kResid, s);
+    LaunchRmsNormRows(pf_x_, L.ffn_norm, nt, H, c.rms_eps, pf_xn_, s);
+    GemmParams gu;
+    gu.w = L.gateup;
+    gu.X = pf_xn_;
+    gu.n_tok = nt;
+    gu.ldx = H;
+    gu.out = pf_h_;
+    gu.ldo = c.ffn;
+    LaunchGemm(gu, Epi::kSilu, s);
+    GemmParams dn;
+    dn.w = L.down;
+    dn.X = pf_h_;
+    dn.n_tok = nt;
+    dn.ldx = c.ffn;
+    dn.out = pf_x_;
+    dn.ldo = H;
+    dn.resid = pf_x_;
+    dn.ldr = H;
+    LaunchGemm(dn, Epi::kResid, s);
+  }
+  // final norm + lm_head on the last position only (the reference computes all
+  // rows and keeps the last one, src/qwen3_gpu.cu:163-170)
+  MvParams mv;
+  mv.seg[0].w = m_->lm_head();
+  mv.n_seg = 1;
+  mv.total_rows = c.vocab;
+  mv.x = pf_x_ + static_cast<int64_t>(n - 1) * H;
+  mv.norm_w = m_->out_norm();
+  mv.eps = c.rms_eps;
+  mv.out = logits_;
+  LaunchMatvec(mv, Epi::kStore, 4, m_->num_sms(), s);
+  if (last_logits != nullptr) {
+    RPGB_CUDA(cudaMemcpyAsync(last_logits, logits_, sizeof(float) * c.vocab, cudaMemcpyDeviceToHost, s));
+  }
+  RPGB_CUDA(cudaStreamSynchronize(s));
+  len_ = pos0 + n;
+  logits_valid_ = true;
+}
+
+void Session::EnqueueSample(const SampleOpts& opt, uint64_t seed, int pos_bump) {
+  const ModelMeta& c = m_->meta();
+  SampleParams sp;
+  sp.logits = logits_;
+  sp.n = c.vocab;
+  sp.temperature = opt.temperature;
+  sp.top_k = opt.top_k;
+  sp.top_p = opt.top_p;
+  sp.seed = seed;
+  sp.pos = pos_;
+  sp.pos_bump = pos_bump;
+  sp.probs = probs_;
+  sp.tok_out = tok_;
+  sp.cand_val = cand_val_;
+  sp.cand_idx = cand_idx_;
+  sp.cand_cnt = cand_cnt_;
+  sp.flag = flag_;
+  LaunchSample(sp, false, stream_);
+}
+
+void Session::EnqueueStep(const SampleOpts& opt, uint64_t seed) {
+  const ModelMeta& c = m_->meta();
+  const cudaStream_t s = stream_;
+  const int H = c.hidden, qd = c.q_dim(), kvd = c.kv_dim();
+  const int sms = m_->num_sms();
+  int launches = 0;
+  LaunchEmbed(m_->embd(), tok_, 1, x_, pos_, out_ids_, s);
+  ++launches;
+  for (int l = 0; l < c.n_layers; ++l) {
+    const DevLayer& L = m_->layers()[static_cast<size_t>(l)];
+    MvParams q;
+    q.seg[0].w = L.q;
+    q.seg[0].out_off = 0;
+    q.seg[1].w = L.k;
+    q.seg[1].out_off = qd;
+    q.seg[2].w = L.v;
+    q.seg[2].out_off = qd + kvd;
+    q.n_seg = 3;
+    q.total_rows = qd + 2 * kvd;
+    q.x = x_;
+    q.norm_w = L.attn_norm;
+    q.eps = c.rms_eps;
+    q.out = qkv_;
+    LaunchMatvec(q, Epi::kStore, 2, sms, s);
+
+    AttnParams a;
+    a.q = qkv_;
+    a.q_stride = 0;
+    a.k_raw = qkv_ + qd;
+    a.v_raw = qkv_ + qd + kvd;
+    a.q_norm = L.q_norm;
+    a.k_norm = L.k_norm;
+    a.rope = m_->rope();
+    a.eps = c.rms_eps;
+    a.kc = kc_ + layer_elems_ * l;
+    a.vc = vc_ + layer_elems_ * l;
+    a.max_seq = static_cast<int32_t>(max_seq_);
+    a.pos = pos_;
+    a.n_heads = c.n_heads;
+    a.n_kv = c.n_kv_heads;
+    a.scale = 1.0f / sqrtf(static_cast<float>(c.head_dim));
+    a.out = attn_;
+    a.part = attn_part_;
+    a.ticket = tickets_;
+    a.n_splits = n_splits_;
+    a.fused = 1;
+    LaunchAttention(a, 1, s);
+
+    MvParams o;
+    o.seg[0].w = L.o;
+    o.total_rows = H;
+    o.x = attn_;
+    o.out = x_;
+    o.resid = x_;
+    LaunchMatvec(o, Epi::kResid, 1, sms, s);
+
+    MvParams gu;
+    gu.seg[0].w = L.gateup;
+    gu.total_rows = 2 * c.ffn;
+    gu.x = x_;
+    gu.norm_w = L.ffn_norm;
+    gu.eps = c.rms_eps;
+    gu.out = h_;
+    LaunchMatvec(gu, Epi::kSilu, 2, sms, s);
+
+    MvParams dn;
+    dn.seg[0].w = L.down;
+    dn.total_rows = H;
+    dn.x = h_;
+    dn.out = x_;
+    dn.resid = x_;
+    LaunchMatvec(dn, Epi::kResid, 1, sms, s);
+    launches += 5;
+  }
+  MvParams lm;
+  lm.seg[0].w = m_->lm_head();
+  lm.total_rows = c.vocab;
+  lm.x = x_;
+  lm.norm_w = m_->out_norm();
+  lm.eps = c.rms_eps;
+  lm.out = logits_;
+  if (!(opt.temperature > 0.0f)) {
+    lm.part_val = am_val_;
+    lm.part_idx = am_idx_;
+    lm.ticket = tickets_ + c.n_kv_heads;
+    lm.tok_out = tok_;
+    lm.pos = pos_;
+    lm.pos_bump = 1;
+    LaunchMatvec(lm, Epi::kArgmax, 4, sms, s);
+    launches += 1;
+  } else {
+    LaunchMatvec(lm, Epi::kStore, 4, sms, s);
+    EnqueueSample(opt, seed, 1);
+    const bool fast = opt.top_k > 1 && opt.top_k <= kFastTopK && opt.top_k < c.vocab;
+    launches += fast ? 4 : 2;
+  }
+  kernels_per_step_ = launches;
+}
+
+int Session::Generate(const SampleOpts& opt, uint64_t seed, int32_t max_tokens, const int32_t* stop, int32_t n_stop,
+                      int32_t* out, float* step_logits) {
+  const ModelMeta& c = m_->meta();
+  RPGB_CHECK(max_tokens > 0, "max_tokens must be positive, got %d", max_tokens);
+  RPGB_CHECK(logits_valid_, "no logits for the next position: run a prefill first");
+  RPGB_CHECK(len_ + max_tokens <= max_seq_,
+             "context is full: %lld positions + %d tokens exceed max_seq %lld (use a larger max_seq or reset)",
+             static_cast<long long>(len_), max_tokens, static_cast<long long>(max_seq_));
+  RPGB_CUDA(cudaSetDevice(m_->device()));
+  const cudaStream_t s = stream_;
+  const int64_t start = len_;
+
+  // first token: sampled from the current logits with counter = len
+  RPGB_CUDA(cudaMemcpyAsync(pos_, &start, sizeof(int64_t), cudaMemcpyHostToDevice, s));
+  if (step_logits != nullptr) {
+    RPGB_CUDA(cudaMemcpyAsync(step_logits, logits_, sizeof(float) * c.vocab, cudaMemcpyDeviceToHost, s));
+  }
+  EnqueueSample(opt, seed, 0);
+
+  // (re)record the step graph when the sampling parameters change
+  if (graph_ == nullptr || !SameOpts(opt, graph_opt_) || seed != graph_seed_) {
+    DropGraph();
+    cudaGraph_t g = nullptr;
+    RPGB_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    const int64_t before = LaunchCount();
+    try {
+      EnqueueStep(opt, seed);
+      CountLaunches(before - LaunchCount());  // recorded, not launched
+    } catch (...) {
+      cudaStreamEndCapture(s, &g);
+      if (g != nullptr) cudaGraphDestroy(g);
+      throw;
+    }
+    RPGB_CUDA(cudaStreamEndCapture(s, &g));
+    const cudaError_t ie = cudaGraphInstantiateWithFlags(&graph_, g, 0);
+    cudaGraphDestroy(g);
+    RPGB_CUDA(ie);
+    graph_opt_ = opt;
+    graph_seed_ = seed;
+  }
+
+  if (host_ids_cap_ < max_tokens) {
+    if (host_ids_ != nullptr) cudaFreeHost(host_ids_);
+    host_ids_ = nullptr;
+    RPGB_CUDA(cudaMallocHost(&host_ids_, sizeof(int32_t) * max_tokens));
+    host_ids_cap_ = max_tokens;
+  }
+
+  // Steps are launched in chunks without a host round trip; with stop ids the
+  // chunk is small so little work runs past a stop token.
+  const int chunk = step_logits != nullptr ? 1 : (n_stop > 0 ? 8 : max_tokens);
+  int produced = 0, launched = 0;
+  bool stopped = false;
+  while (produced < max_tokens && !stopped) {
+    const int todo = std::min(chunk, max_tokens - produced);
+    launched += todo;
+    for (int i = 0; i < todo; ++i) {
+      RPGB_CUDA(cudaGraphLaunch(graph_, s));
+      ++graph_launches_;
+      CountLaunches(kernels_per_step_);
+      if (step_logits != nullptr && produced + i + 1 < max_tokens) {
+        RPGB_CUDA(cudaMemcpyAsync(step_logits + static_cast<int64_t>(produced + i + 1) * c.vocab, logits_,
+                                  sizeof(float) * c.vocab, cudaMemcpyDeviceToHost, s));
+      }
+    }
+    RPGB_CUDA(cudaMemcpyAsync(host_ids_ + produced, out_ids_ + start + produced, sizeof(int32_t) * todo,
+                              cudaMemcpyDeviceToHost, s));
+    RPGB_CUDA(cudaStreamSynchronize(s));
+    for (int i = 0; i < todo; ++i) {
+      const int32_t id = host_ids_[produced + i];
+      bool is_stop = false;
+      for (int j = 0; j < n_stop; ++j) is_stop = is_stop || stop[j] == id;
+      if (is_stop) {
+        produced += i + 1;
+        stopped = true;
+        break;
+      }
+    }
+    if (!stopped) produced += todo;
+  }
+  std::memcpy(out, host_ids_, sizeof(int32_t) * produced);
+  // Every returned token (stop included) was forwarded: len = prompt + generated.
+  const bool ran_past = launched > produced;
+  len_ = start + produced;
+  // after a stop inside a chunk the device logits belong to a later step
+  logits_valid_ = !ran_past;
+  if (ran_past) {
+    RPGB_CUDA(cudaMemcpyAsync(pos_, &len_, sizeof(int64_t), cudaMemcpyHostToDevice, s));
+    RPGB_CUDA(cudaStreamSynchronize(s));
+  }
+  return produced;
+}
+
+}  // namespace rpgb

@@ -1,0 +1,113 @@
+// engine.h -- a decoding session: fp16 KV cache, scratch, stream, decode graph.
+//
+// Reference counterparts: GpuKvCache (src/kv_cache_gpu.h:50-100), GpuScratch
+// (src/qwen3_gpu.h:79-98), GpuForwardFull (src/qwen3_gpu.cu:236-276),
+// GpuGenerate / GenerateGraph / GenerateNoGraph (src/qwen3_gpu.cu:451-640).
+//
+// Differences by design:
+//  * every session owns its stream, position counter and graph (the reference
+//    keeps a process-global stream and pos0 staging), so sessions on several
+//    GPUs run concurrently;
+//  * one decode step = embedding -> 5 fused launches per layer -> lm_head with a
+//    fused argmax (or the sampler), recorded once as a CUDA graph;
+//  * the sampled token, its position and the position counter never leave the
+//    device inside the loop; the host reads the generated ids once per chunk.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <vector>
+
+#include "kernels.h"
+#include "model.h"
+
+namespace rpgb {
+
+struct SampleOpts {
+  float temperature = 0.f;
+  int32_t top_k = 0;
+  float top_p = 1.f;
+};
+
+class Session {
+ public:
+  Session(const Model* m, int64_t max_seq);
+  ~Session();
+  Session(const Session&) = delete;
+  Session& operator=(const Session&) = delete;
+
+  const Model& model() const { return *m_; }
+  int64_t len() const { return len_; }
+  int64_t max_seq() const { return max_seq_; }
+  void SetLen(int64_t n);
+  cudaStream_t stream() const { return stream_; }
+
+  // Appends tokens at positions len .. len+n-1 and leaves the logits of the
+  // last position on the device (optionally copied to last_logits[vocab]).
+  void Prefill(const int32_t* tokens, int64_t n, float* last_logits);
+
+  // Samples from the current logits and forwards every returned token (stop
+  // token included), exactly the reference's GpuGenerate loop.  Returns the
+  // number of ids written to out.
+  int Generate(const SampleOpts& opt, uint64_t seed, int32_t max_tokens, const int32_t* stop, int32_t n_stop,
+               int32_t* out, float* step_logits);
+
+  // Device pointers for instrumentation / tests.
+  const float* logits_dev() const { return logits_; }
+  int graph_launches() const { return graph_launches_; }
+  bool graph_ready() const { return graph_ != nullptr; }
+  int kernels_per_step() const { return kernels_per_step_; }
+
+ private:
+  void EnqueueStep(const SampleOpts& opt, uint64_t seed);
+  void EnqueueSample(const SampleOpts& opt, uint64_t seed, int pos_bump);
+  void EnsurePrefill(int64_t n);
+  void DropGraph();
+
+  const Model* m_;
+  int64_t max_seq_ = 0;
+  int64_t len_ = 0;
+  bool logits_valid_ = false;
+  cudaStream_t stream_ = nullptr;
+
+  // KV cache [layer][kv_head][max_seq][128] fp16
+  __half* kc_ = nullptr;
+  __half* vc_ = nullptr;
+  size_t layer_elems_ = 0;
+
+  // decode state (device)
+  uint8_t* dec_arena_ = nullptr;
+  float *x_ = nullptr, *qkv_ = nullptr, *attn_ = nullptr, *h_ = nullptr, *logits_ = nullptr, *probs_ = nullptr;
+  int64_t* pos_ = nullptr;
+  int32_t* tok_ = nullptr;
+  int32_t* out_ids_ = nullptr;  // [max_seq]: token forwarded at each position
+  float* attn_part_ = nullptr;
+  uint32_t* tickets_ = nullptr;  // [n_kv] attention + [1] argmax
+  float* am_val_ = nullptr;
+  int32_t* am_idx_ = nullptr;
+  float* cand_val_ = nullptr;
+  int32_t* cand_idx_ = nullptr;
+  int32_t* cand_cnt_ = nullptr;
+  int32_t* flag_ = nullptr;
+  int n_splits_ = 1;
+
+  // prefill scratch (grow-only)
+  int64_t pf_cap_ = 0;
+  uint8_t* pf_arena_ = nullptr;
+  float *pf_x_ = nullptr, *pf_xn_ = nullptr, *pf_qkv_ = nullptr, *pf_q_ = nullptr, *pf_attn_ = nullptr,
+        *pf_h_ = nullptr;
+  int32_t* pf_tok_ = nullptr;
+  int32_t* host_ids_ = nullptr;  // pinned staging
+  int64_t host_ids_cap_ = 0;
+
+  // decode graph
+  cudaGraphExec_t graph_ = nullptr;
+  SampleOpts graph_opt_;
+  uint64_t graph_seed_ = 0;
+  int graph_launches_ = 0;
+  int kernels_per_step_ = 0;
+};
+
+}  // namespace rpgb

@@ -1,0 +1,329 @@
+// k_attn.cu -- GQA attention over the fp16 KV cache, plus the prefill helpers.
+//
+// Replaces AttentionFromCacheKernel (src/kernels_gpu.cu:737-823), KvWriteKernel
+// (708-727), RopeKernel (598-621) and the per-head RmsNorm launches of
+// GpuForwardLayer (src/qwen3_gpu.cu:74-94).
+//
+// One block owns (position split s, KV head h, query t) and all G query heads
+// of that group, so each K/V row is read once per group instead of once per
+// query head.  Positions are processed 128 at a time with an online softmax;
+// with n_splits > 1 (decode) every split writes (m, l, acc) and the last block
+// of a head to finish merges them (ticket counter, no spin-wait).
+//
+// Cache layout is the reference's: [layer][kv_head][max_seq][128] fp16, RNE
+// rounding (__float2half_rn, src/kernels_gpu.cu:725).
+#include <cfloat>
+
+#include "common.h"
+#include "kernels.cuh"
+#include "kernels.h"
+
+namespace rpgb {
+namespace {
+
+constexpr int D = 128;
+
+template <int G>
+__device__ __forceinline__ void BlockMaxG(float (&v)[G], float* sh) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    v[g] = dev::WarpMax(v[g]);
+    if (lane == 0) sh[warp * G + g] = v[g];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < G; ++g) v[g] = fmaxf(fmaxf(sh[g], sh[G + g]), fmaxf(sh[2 * G + g], sh[3 * G + g]));
+}
+
+template <int G>
+__device__ __forceinline__ void BlockSumG(double (&v)[G], double* sh) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    v[g] = dev::WarpSumD(v[g]);
+    if (lane == 0) sh[warp * G + g] = v[g];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < G; ++g) v[g] = ((sh[g] + sh[G + g]) + sh[2 * G + g]) + sh[3 * G + g];
+}
+
+// In-place per-head RMSNorm + rotate-half RoPE of G vectors held one element
+// per thread (thread = dimension).  Returns the transformed element.
+template <int G>
+__device__ __forceinline__ void NormRope(float (&v)[G], const float* __restrict__ w, float eps,
+                                         const float* __restrict__ rope_row, float (*buf)[D], double* dsh) {
+  const int tid = threadIdx.x;
+  double ss[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) ss[g] = static_cast<double>(v[g]) * v[g];
+  BlockSumG<G>(ss, dsh);
+  const float wt = w[tid];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const float scale = static_cast<float>(1.0 / sqrt(ss[g] / static_cast<double>(D) + static_cast<double>(eps)));
+    buf[g][tid] = v[g] * scale * wt;
+  }
+  __syncthreads();
+  if (tid < D / 2) {
+    const float c = rope_row[tid], sn = rope_row[D / 2 + tid];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float a = buf[g][tid], b = buf[g][tid + D / 2];
+      buf[g][tid] = a * c - b * sn;
+      buf[g][tid + D / 2] = b * c + a * sn;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < G; ++g) v[g] = buf[g][tid];
+}
+
+template <int G>
+__global__ void __launch_bounds__(128) AttnKernel(const AttnParams p) {
+  __shared__ __align__(16) float qs[G][D];
+  __shared__ __align__(16) float kb[1][D];
+  __shared__ float sc[G][128];
+  __shared__ double dsh[4 * G];
+  __shared__ float fsh[4 * G];
+  __shared__ int s_last;
+
+  const int s = blockIdx.x, h = blockIdx.y, t = blockIdx.z;
+  const int tid = threadIdx.x;
+  const int64_t pos = *p.pos + t;
+  const int64_t L = pos + 1;
+  const int64_t chunk = (L + p.n_splits - 1) / p.n_splits;
+  const int64_t p0 = static_cast<int64_t>(s) * chunk;
+  const int64_t p1 = p0 + chunk < L ? p0 + chunk : L;
+  const int q_dim = p.n_heads * D;
+  __half* kbase = p.kc + static_cast<int64_t>(h) * p.max_seq * D;
+  __half* vbase = p.vc + static_cast<int64_t>(h) * p.max_seq * D;
+
+  // ---- the G query vectors of this group
+  {
+    float v[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) v[g] = p.q[static_cast<int64_t>(t) * p.q_stride + (h * G + g) * D + tid];
+    if (p.fused) {
+      NormRope<G>(v, p.q_norm, p.eps, p.rope + pos * D, qs, dsh);
+      if (p0 <= pos && pos < p1) {
+        // This split owns the new position: write its K/V (fp16, RNE) first.
+        float kv1[1] = {p.k_raw[h * D + tid]};
+        NormRope<1>(kv1, p.k_norm, p.eps, p.rope + pos * D, kb, dsh);
+        kbase[pos * D + tid] = __float2half_rn(kv1[0]);
+        vbase[pos * D + tid] = __float2half_rn(p.v_raw[h * D + tid]);
+      }
+    } else {
+#pragma unroll
+      for (int g = 0; g < G; ++g) qs[g][tid] = v[g];
+    }
+  }
+  __syncthreads();
+
+  float m[G], acc[G];
+  double l[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.0;
+    acc[g] = 0.f;
+  }
+
+  for (int64_t c0 = p0; c0 < p1; c0 += 128) {
+    const int64_t pp = c0 + tid;
+    float sg[G];
+    if (pp < p1) {
+      const uint4* kr = reinterpret_cast<const uint4*>(kbase + pp * D);
+      float dot[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) dot[g] = 0.f;
+#pragma unroll 4
+      for (int i = 0; i < D / 8; ++i) {
+        const uint4 kw = kr[i];
+        const __half2* h2 = reinterpret_cast<const __half2*>(&kw);
+        float kf[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __half22float2(h2[e]);
+          kf[2 * e] = f.x;
+          kf[2 * e + 1] = f.y;
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) dot[g] = fmaf(qs[g][i * 8 + e], kf[e], dot[g]);
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) sg[g] = dot[g] * p.scale;
+    } else {
+#pragma unroll
+      for (int g = 0; g < G; ++g) sg[g] = -INFINITY;
+    }
+    float cm[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) cm[g] = sg[g];
+    BlockMaxG<G>(cm, fsh);
+    double cs[G];
+    float alpha[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float nm = fmaxf(m[g], cm[g]);
+      const float e = pp < p1 ? expf(sg[g] - nm) : 0.f;
+      sc[g][tid] = e;
+      cs[g] = static_cast<double>(e);
+      alpha[g] = m[g] == -INFINITY ? 0.f : expf(m[g] - nm);
+      m[g] = nm;
+    }
+    BlockSumG<G>(cs, dsh);  // also orders the sc[] writes before the reads below
+    const int nv = static_cast<int>(p1 - c0 < 128 ? p1 - c0 : 128);
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      l[g] = l[g] * static_cast<double>(alpha[g]) + cs[g];
+      acc[g] *= alpha[g];
+    }
+    const __half* vr = vbase + c0 * D + tid;
+    for (int j = 0; j < nv; ++j) {
+      const float vv = __half2float(vr[static_cast<int64_t>(j) * D]);
+#pragma unroll
+      for (int g = 0; g < G; ++g) acc[g] = fmaf(sc[g][j], vv, acc[g]);
+    }
+    __syncthreads();
+  }
+
+  if (p.n_splits == 1) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      p.out[static_cast<int64_t>(t) * q_dim + (h * G + g) * D + tid] = acc[g] * static_cast<float>(1.0 / l[g]);
+    }
+    return;
+  }
+
+  // ---- split-K: publish (m, l, acc) and let the last block of this head merge
+  constexpr int kRec = D + 2;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float* rec = p.part + (static_cast<int64_t>(h * p.n_splits + s) * G + g) * kRec;
+    if (tid == 0) {
+      rec[0] = m[g];
+      rec[1] = static_cast<float>(l[g]);
+    }
+    rec[2 + tid] = acc[g];
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned tk = atomicAdd(p.ticket + h, 1u);
+    s_last = tk == static_cast<unsigned>(p.n_splits - 1) ? 1 : 0;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float M = -INFINITY;
+    for (int sp = 0; sp < p.n_splits; ++sp) {
+      M = fmaxf(M, __ldcg(p.part + (static_cast<int64_t>(h * p.n_splits + sp) * G + g) * kRec));
+    }
+    double den = 0.0;
+    float num = 0.f;
+    for (int sp = 0; sp < p.n_splits; ++sp) {
+      const float* rec = p.part + (static_cast<int64_t>(h * p.n_splits + sp) * G + g) * kRec;
+      const float ms = __ldcg(rec);
+      const float w = ms == -INFINITY ? 0.f : expf(ms - M);
+      den += static_cast<double>(w) * static_cast<double>(__ldcg(rec + 1));
+      num = fmaf(w, __ldcg(rec + 2 + tid), num);
+    }
+    p.out[(h * G + g) * D + tid] = num * static_cast<float>(1.0 / den);
+  }
+  if (tid == 0) p.ticket[h] = 0u;
+}
+
+// Prefill: per token, q heads -> q_out (normalised + rotated), k heads -> cache
+// (normalised + rotated, fp16), v heads -> cache (fp16).
+__global__ void __launch_bounds__(128) QkRopeKvKernel(const float* __restrict__ qkv, int q_dim, int kv_dim,
+                                                      const float* __restrict__ q_norm,
+                                                      const float* __restrict__ k_norm,
+                                                      const float* __restrict__ rope, float eps,
+                                                      const int64_t* __restrict__ pos0, __half* kc, __half* vc,
+                                                      int32_t max_seq, int n_heads, int n_kv,
+                                                      float* __restrict__ q_out) {
+  __shared__ __align__(16) float buf[1][D];
+  __shared__ double dsh[4];
+  const int t = blockIdx.x, tid = threadIdx.x;
+  const int64_t pos = *pos0 + t;
+  const float* row = qkv + static_cast<int64_t>(t) * (q_dim + 2 * kv_dim);
+  const float* rr = rope + pos * D;
+  for (int hq = 0; hq < n_heads; ++hq) {
+    float v[1] = {row[hq * D + tid]};
+    NormRope<1>(v, q_norm, eps, rr, buf, dsh);
+    q_out[static_cast<int64_t>(t) * q_dim + hq * D + tid] = v[0];
+  }
+  for (int hk = 0; hk < n_kv; ++hk) {
+    float v[1] = {row[q_dim + hk * D + tid]};
+    NormRope<1>(v, k_norm, eps, rr, buf, dsh);
+    const int64_t off = (static_cast<int64_t>(hk) * max_seq + pos) * D + tid;
+    kc[off] = __float2half_rn(v[0]);
+    vc[off] = __float2half_rn(row[q_dim + kv_dim + hk * D + tid]);
+  }
+}
+
+__global__ void __launch_bounds__(256) RmsNormRowsKernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                         int n, float eps, float* __restrict__ out) {
+  __shared__ double dsh[32];
+  const float* xr = x + static_cast<int64_t>(blockIdx.x) * n;
+  float* orow = out + static_cast<int64_t>(blockIdx.x) * n;
+  double ss = 0.0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const double v = static_cast<double>(xr[i]);
+    ss += v * v;
+  }
+  const double tot = dev::BlockSumD(ss, dsh);
+  const float scale = static_cast<float>(1.0 / sqrt(tot / static_cast<double>(n) + static_cast<double>(eps)));
+  for (int i = threadIdx.x; i < n; i += blockDim.x) orow[i] = xr[i] * scale * w[i];
+}
+
+}  // namespace
+
+size_t AttentionPartialFloats(int n_kv, int group, int n_splits) {
+  return static_cast<size_t>(n_kv) * n_splits * group * (D + 2);
+}
+
+void LaunchAttention(const AttnParams& p, int n_queries, cudaStream_t s) {
+  RPGB_CHECK(n_queries >= 1 && n_queries < 65536, "attention: bad query count %d", n_queries);
+  RPGB_CHECK(p.n_splits >= 1 && (p.n_splits == 1 || n_queries == 1), "attention: split-K is decode only");
+  RPGB_CHECK(p.n_heads % p.n_kv == 0, "attention: bad head counts");
+  const int G = p.n_heads / p.n_kv;
+  const dim3 grid(p.n_splits, p.n_kv, n_queries);
+  switch (G) {
+    case 1: AttnKernel<1><<<grid, 128, 0, s>>>(p); break;
+    case 2: AttnKernel<2><<<grid, 128, 0, s>>>(p); break;
+    case 4: AttnKernel<4><<<grid, 128, 0, s>>>(p); break;
+    case 8: AttnKernel<8><<<grid, 128, 0, s>>>(p); break;
+    default: Throw("attention: GQA group %d is not supported (1, 2, 4, 8)", G);
+  }
+  RPGB_CUDA(cudaGetLastError());
+  CountLaunches(1);
+}
+
+void LaunchQkRopeKv(const float* qkv, int n_tok, int q_dim, int kv_dim, const float* q_norm, const float* k_norm,
+                    const float* rope, float eps, const int64_t* pos0, __half* kc, __half* vc, int32_t max_seq,
+                    int n_heads, int n_kv, float* q_out, cudaStream_t s) {
+  RPGB_CHECK(n_tok > 0, "qk_rope: empty");
+  QkRopeKvKernel<<<n_tok, 128, 0, s>>>(qkv, q_dim, kv_dim, q_norm, k_norm, rope, eps, pos0, kc, vc, max_seq,
+                                       n_heads, n_kv, q_out);
+  RPGB_CUDA(cudaGetLastError());
+  CountLaunches(1);
+}
+
+void LaunchRmsNormRows(const float* x, const float* w, int n_rows, int n, float eps, float* out, cudaStream_t s) {
+  RPGB_CHECK(n_rows > 0 && n > 0, "rmsnorm: empty");
+  RmsNormRowsKernel<<<n_rows, 256, 0, s>>>(x, w, n, eps, out);
+  RPGB_CUDA(cudaGetLastError());
+  CountLaunches(1);
+}
+
+}  // namespace rpgb

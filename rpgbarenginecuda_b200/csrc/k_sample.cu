@@ -1,0 +1,509 @@
+// k_sample.cu -- on-device temperature / top-k / top-p sampling.
+//
+// Semantics are the reference's (src/sampler.h:35-44, src/sampler_gpu.cu:161-348):
+//   T <= 0      argmax, ties -> lowest index, no random number consumed
+//   v = logit * (1/T)                        (only when T != 1)
+//   top_k       active iff 1 < k < n; threshold = k-th largest value, v < thr dropped
+//   softmax     e = expf(v - max), sum in double, p = e * float(1/sum)
+//   top_p       active iff 0 < p < 1: cut = largest key t with sum{p_i : key_i <= t}
+//               <= 1 - top_p; p <= cut dropped; keep >= 1 (argmax -> 1.0); renormalise
+//   draw        u = SplitMix64 counter uniform; first i with serial double cumsum > u
+//
+// The reference finds both thresholds by 32-step bisection over the uint32 key
+// space (64 full passes) and draws with a single-thread scan.  Here:
+//  * general kernel (one 1024-thread block): exact radix selects (4 passes for
+//    top-k with integer counts, 4 for top-p with 2^-60 fixed-point masses), a
+//    blocked prefix scan for the draw that falls back to the exact serial scan
+//    whenever u lies within 1e-9 of a prefix boundary;
+//  * fast path (T > 0, 1 < top_k <= 64): every block of a 148-block grid keeps
+//    its slice's top-k candidates (a superset of the global top-k survivors);
+//    one small block then does the whole pipeline on the survivors only.  With
+//    the tail at zero probability, the serial cumsum over survivors in index
+//    order is bit-identical to the reference's full serial cumsum.
+#include <cfloat>
+#include <climits>
+
+#include "common.h"
+#include "kernels.cuh"
+#include "kernels.h"
+
+namespace rpgb {
+namespace {
+
+constexpr int kGenThreads = 1024;
+constexpr int kCandThreads = 256;
+constexpr int kSliceMax = 2048;
+constexpr int kSmallThreads = 256;
+constexpr int kMaxCand = kCandBlocks * kFastTopK;
+constexpr double kFix = 1152921504606846976.0;  // 2^60
+
+__device__ __forceinline__ int64_t Counter(const SampleParams& p) {
+  if (p.counter_override != nullptr) return *p.counter_override;
+  return *p.pos + p.pos_bump;
+}
+
+__device__ __forceinline__ void Finish(const SampleParams& p, int32_t tok) {
+  *p.tok_out = tok;
+  if (p.pos != nullptr) *p.pos += p.pos_bump;
+}
+
+// Block argmax over a global array, ties -> lowest index.  All threads return it.
+__device__ int BlockArgmax(const float* x, int n, float* fsh, int* ish) {
+  float bv = -FLT_MAX;
+  int bi = INT_MAX;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = x[i];
+    if (v > bv || (v == bv && i < bi)) {
+      bv = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
+    const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (lane == 0) {
+    fsh[warp] = bv;
+    ish[warp] = bi;
+  }
+  __syncthreads();
+  bv = fsh[0];
+  bi = ish[0];
+  for (int w = 1; w < nw; ++w) {
+    if (fsh[w] > bv || (fsh[w] == bv && ish[w] < bi)) {
+      bv = fsh[w];
+      bi = ish[w];
+    }
+  }
+  __syncthreads();
+  return bi == INT_MAX ? 0 : bi;
+}
+
+// Key of the k-th largest element of x[0..n) (multiplicity counted).
+__device__ uint32_t RadixKth(const float* x, int n, int k, unsigned* hist, uint32_t* s_sel) {
+  uint32_t prefix = 0, mask = 0;
+  int rem = k;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const uint32_t key = dev::OrderKey(x[i]);
+      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int cum = 0, d = 0;
+      for (d = 255; d >= 0; --d) {
+        if (cum + static_cast<int>(hist[d]) >= rem) break;
+        cum += static_cast<int>(hist[d]);
+      }
+      s_sel[0] = static_cast<uint32_t>(d < 0 ? 0 : d);
+      s_sel[1] = static_cast<uint32_t>(rem - cum);
+    }
+    __syncthreads();
+    prefix |= s_sel[0] << shift;
+    mask |= 255u << shift;
+    rem = static_cast<int>(s_sel[1]);
+    __syncthreads();
+  }
+  return prefix;
+}
+
+__global__ void __launch_bounds__(kGenThreads) SampleGeneralKernel(const SampleParams p, int skip_if_flag) {
+  __shared__ double dsh[32];
+  __shared__ float fsh[32];
+  __shared__ int ish[32];
+  __shared__ unsigned hist[256];
+  __shared__ unsigned long long mhist[256];
+  __shared__ uint32_t s_sel[2];
+  __shared__ unsigned long long s_below;
+  __shared__ double wsc[32];
+  __shared__ int s_idx, s_amb;
+
+  if (skip_if_flag && p.flag != nullptr && *p.flag == 1) return;
+  const int n = p.n, tid = threadIdx.x;
+  float* probs = p.probs;
+  const int64_t counter = Counter(p);
+
+  if (!(p.temperature > 0.0f)) {
+    const int best = BlockArgmax(p.logits, n, fsh, ish);
+    for (int i = tid; i < n; i += kGenThreads) probs[i] = i == best ? 1.0f : 0.0f;
+    if (tid == 0) Finish(p, best);
+    return;
+  }
+  const float inv_t = 1.0f / p.temperature;
+  for (int i = tid; i < n; i += kGenThreads) {
+    float v = p.logits[i];
+    if (p.temperature != 1.0f) v *= inv_t;
+    probs[i] = v;
+  }
+  __syncthreads();
+
+  if (p.top_k > 1 && p.top_k < n) {
+    const float kth = dev::FromOrderKey(RadixKth(probs, n, p.top_k, hist, s_sel));
+    for (int i = tid; i < n; i += kGenThreads) {
+      if (probs[i] < kth) probs[i] = -INFINITY;
+    }
+    __syncthreads();
+  }
+
+  float lmax = -INFINITY;
+  for (int i = tid; i < n; i += kGenThreads) lmax = fmaxf(lmax, probs[i]);
+  const float mx = dev::BlockMax(lmax, fsh);
+  double ls = 0.0;
+  for (int i = tid; i < n; i += kGenThreads) {
+    const float e = expf(probs[i] - mx);
+    probs[i] = e;
+    ls += static_cast<double>(e);
+  }
+  const double sum = dev::BlockSumD(ls, dsh);
+  const float inv = static_cast<float>(1.0 / sum);
+  for (int i = tid; i < n; i += kGenThreads) probs[i] *= inv;
+  __syncthreads();
+
+  if (p.top_p > 0.0f && p.top_p < 1.0f) {
+    const double theta = 1.0 - static_cast<double>(p.top_p);
+    const unsigned long long theta_fx = static_cast<unsigned long long>(theta * kFix);
+    uint32_t prefix = 0, mask = 0;
+    bool none = false;
+    if (tid == 0) s_below = 0ull;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int i = tid; i < 256; i += kGenThreads) mhist[i] = 0ull;
+      __syncthreads();
+      for (int i = tid; i < n; i += kGenThreads) {
+        const float v = probs[i];
+        const uint32_t key = dev::OrderKey(v);
+        if ((key & mask) == prefix) {
+          atomicAdd(&mhist[(key >> shift) & 255u], static_cast<unsigned long long>(static_cast<double>(v) * kFix));
+        }
+      }
+      __syncthreads();
+      if (tid == 0) {
+        unsigned long long cum = s_below;
+        int d = 0;
+        for (d = 0; d < 256; ++d) {
+          if (cum + mhist[d] > theta_fx) break;
+          cum += mhist[d];
+        }
+        s_sel[0] = static_cast<uint32_t>(d);
+        s_below = cum;
+      }
+      __syncthreads();
+      if (s_sel[0] >= 256u) {
+        none = true;  // the whole distribution fits under 1 - top_p: nothing is cut
+        break;
+      }
+      prefix |= s_sel[0] << shift;
+      mask |= 255u << shift;
+      __syncthreads();
+    }
+    const float cut = none ? dev::FromOrderKey(0xFFFFFFFFu) : dev::FromOrderKey(prefix - 1u);
+    for (int i = tid; i < n; i += kGenThreads) {
+      if (probs[i] <= cut) probs[i] = 0.0f;
+    }
+    __syncthreads();
+    const int best = BlockArgmax(probs, n, fsh, ish);
+    if (tid == 0 && probs[best] == 0.0f) probs[best] = 1.0f;
+    __syncthreads();
+    double l2 = 0.0;
+    for (int i = tid; i < n; i += kGenThreads) l2 += static_cast<double>(probs[i]);
+    const double sum2 = dev::BlockSumD(l2, dsh);
+    if (sum2 > 0.0) {
+      const float inv2 = static_cast<float>(1.0 / sum2);
+      for (int i = tid; i < n; i += kGenThreads) probs[i] *= inv2;
+    }
+    __syncthreads();
+  }
+
+  // ---- draw: blocked prefix sums, exact serial fallback near a boundary
+  const double u = static_cast<double>(dev::CounterUniform(p.seed, static_cast<uint64_t>(counter)));
+  const int per = (n + kGenThreads - 1) / kGenThreads;
+  const int a = tid * per, b = a + per < n ? a + per : n;
+  double local = 0.0;
+  for (int i = a; i < b; ++i) local += static_cast<double>(probs[i]);
+  // exclusive scan over threads in index order
+  const int lane = tid & 31, warp = tid >> 5;
+  double incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (tid == 0) {
+    s_idx = INT_MAX;
+    s_amb = 0;
+  }
+  if (lane == 31) wsc[warp] = incl;
+  __syncthreads();
+  double wbase = 0.0;
+  for (int w = 0; w < warp; ++w) wbase += wsc[w];
+  const double prefix0 = wbase + incl - local;
+  const double kMargin = 1e-9;
+  if (a < b && prefix0 <= u + kMargin && prefix0 + local > u - kMargin) {
+    double cum = prefix0;
+    for (int i = a; i < b; ++i) {
+      const double before = cum;
+      cum += static_cast<double>(probs[i]);
+      if (cum > u) {
+        if (fabs(cum - u) < kMargin || fabs(before - u) < kMargin) atomicExch(&s_amb, 1);
+        atomicMin(&s_idx, i);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int tok = s_idx;
+    if (s_amb) {
+      // exact reference order: one serial double cumsum
+      tok = INT_MAX;
+      double cum = 0.0;
+      for (int i = 0; i < n; ++i) {
+        cum += static_cast<double>(probs[i]);
+        if (cum > u) {
+          tok = i;
+          break;
+        }
+      }
+    }
+    if (tok == INT_MAX) {
+      float bv = probs[0];
+      tok = 0;
+      for (int i = 1; i < n; ++i) {
+        if (probs[i] > bv) {
+          bv = probs[i];
+          tok = i;
+        }
+      }
+    }
+    Finish(p, tok);
+  }
+}
+
+// Per-slice top-k candidates on raw logits (temperature scaling is monotone).
+__global__ void __launch_bounds__(kCandThreads) CandKernel(const SampleParams p) {
+  __shared__ float vals[kSliceMax];
+  __shared__ unsigned hist[256];
+  __shared__ uint32_t s_sel[2];
+  __shared__ int s_cnt;
+  const int n = p.n;
+  const int per = (n + kCandBlocks - 1) / kCandBlocks;
+  const int a = blockIdx.x * per;
+  const int len = a < n ? min(per, n - a) : 0;
+  for (int i = threadIdx.x; i < len; i += kCandThreads) vals[i] = p.logits[a + i];
+  if (threadIdx.x == 0) s_cnt = 0;
+  __syncthreads();
+  const int k = p.top_k;
+  uint32_t thr = 0u;  // keep everything when the slice is not larger than k
+  if (len > k) thr = RadixKth(vals, len, k, hist, s_sel);
+  __syncthreads();
+  float* cv = p.cand_val + blockIdx.x * kFastTopK;
+  int32_t* ci = p.cand_idx + blockIdx.x * kFastTopK;
+  for (int i = threadIdx.x; i < len; i += kCandThreads) {
+    if (dev::OrderKey(vals[i]) >= thr) {
+      const int slot = atomicAdd(&s_cnt, 1);
+      if (slot < kFastTopK) {
+        cv[slot] = vals[i];
+        ci[slot] = a + i;
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) p.cand_cnt[blockIdx.x] = s_cnt <= kFastTopK ? s_cnt : -1;
+}
+
+__global__ void __launch_bounds__(kSmallThreads) SampleSmallKernel(const SampleParams p) {
+  extern __shared__ __align__(16) unsigned char sm[];
+  float* cv = reinterpret_cast<float*>(sm);                       // [kMaxCand]
+  int* ci = reinterpret_cast<int*>(cv + kMaxCand);                // [kMaxCand]
+  float* kv = reinterpret_cast<float*>(ci + kMaxCand);            // kept values / probs [kMaxCand]
+  int* kix = reinterpret_cast<int*>(kv + kMaxCand);               // kept indices
+  __shared__ unsigned hist[256];
+  __shared__ uint32_t s_sel[2];
+  __shared__ int s_off[kCandBlocks + 1];
+  __shared__ int s_bad, s_m, s_c;
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    int off = 0, bad = 0;
+    for (int b = 0; b < kCandBlocks; ++b) {
+      const int c = p.cand_cnt[b];
+      s_off[b] = off;
+      if (c < 0) bad = 1;
+      off += c < 0 ? 0 : c;
+    }
+    s_off[kCandBlocks] = off;
+    s_bad = bad;
+    s_m = off;
+  }
+  __syncthreads();
+  if (s_bad) {
+    if (tid == 0) *p.flag = 0;
+    return;
+  }
+  const int m = s_m;
+  const float inv_t = 1.0f / p.temperature;
+  for (int b = 0; b < kCandBlocks; ++b) {
+    const int c = s_off[b + 1] - s_off[b];
+    for (int i = tid; i < c; i += kSmallThreads) {
+      float v = p.cand_val[b * kFastTopK + i];
+      if (p.temperature != 1.0f) v *= inv_t;
+      cv[s_off[b] + i] = v;
+      ci[s_off[b] + i] = p.cand_idx[b * kFastTopK + i];
+    }
+  }
+  __syncthreads();
+  const float kth = dev::FromOrderKey(RadixKth(cv, m, p.top_k, hist, s_sel));
+  // survivors, ordered by vocabulary index
+  if (tid == 0) s_c = 0;
+  __syncthreads();
+  for (int i = tid; i < m; i += kSmallThreads) {
+    if (cv[i] >= kth) {
+      const int slot = atomicAdd(&s_c, 1);
+      kv[slot] = cv[i];
+      kix[slot] = ci[i];
+    }
+  }
+  __syncthreads();
+  const int c = s_c;
+  // rank sort by index (c is small: k plus ties)
+  for (int i = tid; i < c; i += kSmallThreads) {
+    int rank = 0;
+    for (int j = 0; j < c; ++j) rank += kix[j] < kix[i];
+    cv[rank] = kv[i];
+    ci[rank] = kix[i];
+  }
+  __syncthreads();
+  // ---- softmax over the survivors (serial, index order; c is k plus ties)
+  float* v = cv;  // probabilities, index-ordered
+  const int* ix = ci;
+  __shared__ int s_forced;
+  if (tid == 0) {
+    float mx = -INFINITY;
+    for (int i = 0; i < c; ++i) mx = fmaxf(mx, v[i]);
+    double sum = 0.0;
+    for (int i = 0; i < c; ++i) {
+      const float e = expf(v[i] - mx);
+      v[i] = e;
+      sum += static_cast<double>(e);
+    }
+    const float inv = static_cast<float>(1.0 / sum);
+    for (int i = 0; i < c; ++i) v[i] *= inv;
+    s_forced = 0;
+  }
+  __syncthreads();
+  if (p.top_p > 0.0f && p.top_p < 1.0f) {
+    // ascending (key, index) order of the survivors' probabilities
+    for (int i = tid; i < c; i += kSmallThreads) {
+      const uint32_t ki = dev::OrderKey(v[i]);
+      int rank = 0;
+      for (int j = 0; j < c; ++j) {
+        const uint32_t kj = dev::OrderKey(v[j]);
+        rank += (kj < ki) || (kj == ki && j < i);
+      }
+      kv[rank] = v[i];
+    }
+    __syncthreads();
+    if (tid == 0) {
+      // smallest key K* whose cumulative mass S(K*) exceeds 1 - top_p; everything
+      // at or below the float just under K* is cut (reference: largest t with
+      // S(t) <= 1 - top_p, drop p <= FromOrderKey(t)).
+      const double theta = 1.0 - static_cast<double>(p.top_p);
+      double cum = 0.0;
+      bool found = false;
+      uint32_t kstar = 0u;
+      int i = 0;
+      while (i < c) {
+        const uint32_t key = dev::OrderKey(kv[i]);
+        double grp = 0.0;
+        int j = i;
+        while (j < c && dev::OrderKey(kv[j]) == key) grp += static_cast<double>(kv[j++]);
+        if (cum + grp > theta) {
+          kstar = key;
+          found = true;
+          break;
+        }
+        cum += grp;
+        i = j;
+      }
+      const float cut = found ? dev::FromOrderKey(kstar - 1u) : dev::FromOrderKey(0xFFFFFFFFu);
+      bool any = false;
+      for (int q = 0; q < c; ++q) {
+        if (v[q] <= cut) v[q] = 0.0f;
+        any = any || v[q] > 0.0f;
+      }
+      if (!any) s_forced = 1;  // every survivor cut: the reference then samples index 0
+      double s2 = 0.0;
+      for (int q = 0; q < c; ++q) s2 += static_cast<double>(v[q]);
+      if (s2 > 0.0) {
+        const float inv2 = static_cast<float>(1.0 / s2);
+        for (int q = 0; q < c; ++q) v[q] *= inv2;
+      }
+    }
+    __syncthreads();
+  }
+  if (tid == 0) {
+    int tok;
+    if (s_forced) {
+      tok = 0;
+    } else {
+      const double u = static_cast<double>(dev::CounterUniform(p.seed, static_cast<uint64_t>(Counter(p))));
+      tok = -1;
+      double cum = 0.0;
+      for (int i = 0; i < c; ++i) {
+        cum += static_cast<double>(v[i]);
+        if (cum > u) {
+          tok = ix[i];
+          break;
+        }
+      }
+      if (tok < 0) {
+        float bv = -1.0f;
+        for (int i = 0; i < c; ++i) {
+          if (v[i] > bv) {
+            bv = v[i];
+            tok = ix[i];
+          }
+        }
+      }
+    }
+    *p.flag = 1;
+    Finish(p, tok);
+  }
+}
+
+}  // namespace
+
+void PrepareSampleKernels() {
+  RPGB_CUDA(cudaFuncSetAttribute(SampleSmallKernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(static_cast<size_t>(kMaxCand) * 16)));
+}
+
+void LaunchSample(const SampleParams& p, bool want_probs, cudaStream_t s) {
+  RPGB_CHECK(p.n > 0, "sample: empty vocabulary");
+  RPGB_CHECK(p.tok_out != nullptr && p.probs != nullptr, "sample: null buffers");
+  const bool fast = !want_probs && p.temperature > 0.0f && p.top_k > 1 && p.top_k <= kFastTopK &&
+                    p.top_k < p.n && p.n <= kCandBlocks * kSliceMax && p.cand_val != nullptr &&
+                    p.flag != nullptr;
+  if (fast) {
+    CandKernel<<<kCandBlocks, kCandThreads, 0, s>>>(p);
+    RPGB_CUDA(cudaGetLastError());
+    const size_t smem = static_cast<size_t>(kMaxCand) * 16;
+    SampleSmallKernel<<<1, kSmallThreads, smem, s>>>(p);
+    RPGB_CUDA(cudaGetLastError());
+    SampleGeneralKernel<<<1, kGenThreads, 0, s>>>(p, 1);
+    CountLaunches(3);
+  } else {
+    SampleGeneralKernel<<<1, kGenThreads, 0, s>>>(p, 0);
+    CountLaunches(1);
+  }
+  RPGB_CUDA(cudaGetLastError());
+}
+
+}  // namespace rpgb

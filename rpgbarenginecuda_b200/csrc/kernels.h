@@ -1,0 +1,143 @@
+// kernels.h -- host-side launchers for the sm_100a kernels.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "model.h"
+
+namespace rpgb {
+
+// Process-wide count of kernel launches issued by this library (graph nodes
+// count once per replay, added by the engine when it launches a graph).
+void CountLaunches(int64_t n);
+int64_t LaunchCount();
+
+// ------------------------------------------------------------------ decode matvec (n = 1)
+//
+// out = W x with W one to three row segments of the same width (the q, k and v
+// projections run as one launch).  Prologue: optional RMSNorm of x.  Epilogue:
+//   kStore   out[r] = acc
+//   kResid   out[r] = resid[r] + acc              (attn_o, ffn_down: x += W h)
+//   kSilu    rows interleaved gate/up: out[i] = silu(acc[2i]) * acc[2i+1]
+//   kArgmax  logits[r] = acc, plus argmax (ties -> lowest index) -> *tok_out
+enum class Epi : int { kStore = 0, kResid = 1, kSilu = 2, kArgmax = 3 };
+
+struct MvSeg {
+  DevMat w;
+  int32_t out_off = 0;
+};
+
+struct MvParams {
+  MvSeg seg[3];
+  int32_t n_seg = 1;
+  int32_t total_rows = 0;
+  const float* x = nullptr;
+  const float* norm_w = nullptr;  // non-null: RMSNorm prologue
+  float eps = 1e-6f;
+  float* out = nullptr;
+  const float* resid = nullptr;
+  // kArgmax bookkeeping
+  float* part_val = nullptr;
+  int32_t* part_idx = nullptr;
+  uint32_t* ticket = nullptr;
+  int32_t* tok_out = nullptr;
+  int64_t* pos = nullptr;  // incremented by pos_bump by the reducing block
+  int32_t pos_bump = 0;
+};
+
+// Sets the dynamic shared-memory limits of every kernel instantiation on the
+// current device.  Called once per device before any launch or graph capture
+// (cudaFuncSetAttribute cannot be recorded into a graph).
+void PrepareMatvecKernels();
+void PrepareSampleKernels();
+
+// Rows handled per warp: 1, 2 or 4 (kSilu needs an even value).
+void LaunchMatvec(const MvParams& p, Epi epi, int rows_per_warp, int num_sms, cudaStream_t s);
+// Scratch sizes needed by kArgmax for a given launch.
+int MatvecGrid(int total_rows, int rows_per_warp, int num_sms);
+
+// ------------------------------------------------------------------ embedding
+
+// x[t, :] = dequant(embd row tok[t]); if out_ids != nullptr also out_ids[*pos + t] = tok[t].
+void LaunchEmbed(const DevMat& embd, const int32_t* tok, int n_tok, float* x, const int64_t* pos,
+                 int32_t* out_ids, cudaStream_t s);
+
+// dst[i] = dequant(W row `row`, element i) for a whole row (bit-exact dequant entry).
+void LaunchDequantRows(const DevMat& w, int64_t row0, int64_t n_rows, float* dst, cudaStream_t s);
+
+// ------------------------------------------------------------------ attention
+
+struct AttnParams {
+  const float* q = nullptr;  // decode: raw qkv row; prefill: normalised + rotated q [n][q_dim]
+  int32_t q_stride = 0;      // floats between consecutive tokens in q
+  const float* k_raw = nullptr;  // decode only: raw k / v rows of the current token
+  const float* v_raw = nullptr;
+  const float* q_norm = nullptr;
+  const float* k_norm = nullptr;
+  const float* rope = nullptr;
+  float eps = 1e-6f;
+  __half* kc = nullptr;  // layer base, [n_kv][max_seq][128]
+  __half* vc = nullptr;
+  int32_t max_seq = 0;
+  const int64_t* pos = nullptr;  // position of query 0
+  int32_t n_heads = 0, n_kv = 0;
+  float scale = 0.f;
+  float* out = nullptr;  // [n][q_dim]
+  float* part = nullptr;
+  uint32_t* ticket = nullptr;  // [n_kv]
+  int32_t n_splits = 1;
+  int32_t fused = 0;  // 1: decode (norm + rope + cache write of the current token inside)
+};
+void LaunchAttention(const AttnParams& p, int n_queries, cudaStream_t s);
+size_t AttentionPartialFloats(int n_kv, int group, int n_splits);
+
+// Prefill helpers: per-head RMSNorm + RoPE for q and k, fp16 cache write of k and v.
+void LaunchQkRopeKv(const float* qkv, int n_tok, int q_dim, int kv_dim, const float* q_norm,
+                    const float* k_norm, const float* rope, float eps, const int64_t* pos0, __half* kc,
+                    __half* vc, int32_t max_seq, int n_heads, int n_kv, float* q_out, cudaStream_t s);
+
+// Row-wise RMSNorm (double sum of squares, as src/kernels_gpu.cu:564-591).
+void LaunchRmsNormRows(const float* x, const float* w, int n_rows, int n, float eps, float* out, cudaStream_t s);
+
+// ------------------------------------------------------------------ prefill GEMM
+struct GemmParams {
+  DevMat w;
+  const float* X = nullptr;  // [n][ldx]
+  int32_t n_tok = 0, ldx = 0;
+  float* out = nullptr;
+  int32_t ldo = 0, out_off = 0;
+  const float* resid = nullptr;
+  int32_t ldr = 0;
+};
+void LaunchGemm(const GemmParams& p, Epi epi, cudaStream_t s);
+
+// ------------------------------------------------------------------ sampler
+struct SampleParams {
+  const float* logits = nullptr;
+  int32_t n = 0;
+  float temperature = 0.f;
+  int32_t top_k = 0;
+  float top_p = 1.f;
+  uint64_t seed = 0;
+  int64_t* pos = nullptr;  // counter = *pos + pos_bump; then *pos += pos_bump
+  int32_t pos_bump = 0;
+  const int64_t* counter_override = nullptr;  // optional explicit counter
+  float* probs = nullptr;  // [n] scratch (also the filtered distribution output)
+  int32_t* tok_out = nullptr;
+  uint64_t* fixed_hist = nullptr;  // scratch for the general path
+  // fast path scratch
+  float* cand_val = nullptr;
+  int32_t* cand_idx = nullptr;
+  int32_t* cand_cnt = nullptr;
+  int32_t* flag = nullptr;  // fast path result flag (1 = done)
+};
+// Fast path (1 < top_k <= kFastTopK, T > 0): candidates + one small block.  Falls
+// back to the general kernel on the device if a block overflowed.
+constexpr int kFastTopK = 64;
+constexpr int kCandBlocks = 148;
+void LaunchSample(const SampleParams& p, bool want_probs, cudaStream_t s);
+
+}  // namespace rpgb

@@ -1,0 +1,103 @@
+// model.h -- Qwen3 metadata and the device-resident, repacked weights.
+//
+// Reference counterparts: ModelMeta / ReadModelMeta (src/model_meta.h:27-62,
+// src/model_meta.cc:11-77), GpuModel::Load (src/gpu_model.cu:148-246) and
+// BuildRopeTable (src/gpu_model.cu:90-120).
+//
+// Difference by design: the reference uploads raw GGUF blocks (144 B Q4_K,
+// 210 B Q6_K) and reads them byte by byte.  Here every super-block is split at
+// load time into separately strided arrays so a warp reads 16-byte aligned,
+// fully coalesced chunks and the 210-byte Q6_K block needs no padding:
+//
+//   Q4_K  q: qs[128] per block      s: d|dmin|scales[12] (16 B) per block
+//   Q6_K  q: ql[128]|qh[64] per block  s: sc[16] per block   d: f16 per block
+//
+// Arrays are [rows][nb][bytes] row-major, nb = cols / 256.  The bytes inside
+// each piece are the GGUF bytes, so decoding follows src/quant.cc exactly.
+#pragma once
+
+#include <cstdint>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "gguf.h"
+
+namespace rpgb {
+
+struct ModelMeta {
+  std::string arch, name;
+  int32_t n_layers = 0, hidden = 0, n_heads = 0, n_kv_heads = 0, head_dim = 0, ffn = 0;
+  int32_t vocab = 0, context_length = 0;
+  float rope_theta = 10000.0f, rms_eps = 1e-6f;
+  int32_t bos_id = -1, eos_id = -1, pad_id = -1;
+  bool add_bos = false, tied = true;
+  int64_t weight_bytes = 0;
+  int32_t q_dim() const { return n_heads * head_dim; }
+  int32_t kv_dim() const { return n_kv_heads * head_dim; }
+  int32_t group() const { return n_heads / n_kv_heads; }
+};
+
+ModelMeta ReadModelMeta(const GgufFile& g);
+
+// One quantised matrix in the repacked device layout (passed to kernels by value).
+struct DevMat {
+  uint32_t type = 0;  // kGgmlQ4_K or kGgmlQ6_K
+  int32_t rows = 0, cols = 0, nb = 0;
+  const uint8_t* q = nullptr;
+  const uint8_t* s = nullptr;
+  const uint16_t* d = nullptr;
+};
+
+struct DevLayer {
+  const float* attn_norm = nullptr;
+  const float* ffn_norm = nullptr;
+  const float* q_norm = nullptr;
+  const float* k_norm = nullptr;
+  DevMat q, k, v, o;
+  DevMat gateup;  // rows interleaved: 2i = ffn_gate row i, 2i+1 = ffn_up row i
+  DevMat down;
+};
+
+// Host-side repack of GGUF blocks into the device layout (exposed for tests).
+// dst_q / dst_s / dst_d sizes: see DevMatBytes.
+void RepackRows(uint32_t type, const uint8_t* src, int64_t rows, int64_t cols, uint8_t* dst_q,
+                uint8_t* dst_s, uint16_t* dst_d);
+void DevMatBytes(uint32_t type, int64_t rows, int64_t cols, size_t* q, size_t* s, size_t* d);
+
+class Model {
+ public:
+  // Loads weights onto `device`, builds the RoPE table for min(max_pos, context).
+  static std::unique_ptr<Model> Load(const std::string& path, int device, int32_t max_pos);
+  ~Model();
+
+  const ModelMeta& meta() const { return meta_; }
+  const GgufFile& gguf() const { return *gguf_; }
+  int device() const { return device_; }
+  int num_sms() const { return num_sms_; }
+  const std::vector<DevLayer>& layers() const { return layers_; }
+  const DevMat& embd() const { return embd_; }
+  const DevMat& lm_head() const { return lm_head_; }
+  const float* out_norm() const { return out_norm_; }
+  const float* rope() const { return rope_; }
+  int32_t rope_positions() const { return rope_pos_; }
+  int64_t device_bytes() const { return arena_bytes_; }
+
+ private:
+  Model() = default;
+  std::unique_ptr<GgufFile> gguf_;
+  ModelMeta meta_;
+  int device_ = 0;
+  int num_sms_ = 0;
+  uint8_t* arena_ = nullptr;
+  int64_t arena_bytes_ = 0;
+  std::vector<DevLayer> layers_;
+  DevMat embd_, lm_head_;
+  const float* out_norm_ = nullptr;
+  float* rope_ = nullptr;
+  int32_t rope_pos_ = 0;
+};
+
+}  // namespace rpgb
