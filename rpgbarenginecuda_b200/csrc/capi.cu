@@ -7,6 +7,7 @@
 
 #include <cuda_runtime.h>
 
+#include <cstring>
 #include <map>
 #include <vector>
 #include <memory>
@@ -16,6 +17,7 @@
 #include "engine.h"
 #include "kernels.cuh"
 #include "kernels.h"
+#include "gguf.h"
 #include "model.h"
 
 namespace rpgb {
@@ -24,6 +26,7 @@ namespace {
 struct MatrixEntry {
   int device = 0;
   int num_sms = 0;
+  int64_t rows = 0;  // logical rows (storage is padded to whole 32-row groups)
   DevMat m;
   void* mem = nullptr;
 };
@@ -230,23 +233,29 @@ int32_t rpgb_matrix_upload(int32_t device, uint32_t type, int64_t rows, int64_t 
     RPGB_CHECK(bytes != nullptr, "matrix bytes are NULL");
     RPGB_CHECK(rows > 0 && cols > 0 && cols % 256 == 0 && rows < (1 << 30), "bad matrix shape %lld x %lld",
                static_cast<long long>(rows), static_cast<long long>(cols));
+    // storage holds whole 32-row groups; padding rows are zero blocks
+    const int64_t prow = (rows + 31) / 32 * 32;
     size_t qb, sb, db;
-    DevMatBytes(type, rows, cols, &qb, &sb, &db);
+    DevMatBytes(type, prow, cols, &qb, &sb, &db);
     auto e = std::make_shared<MatrixEntry>();
+    e->rows = rows;
     e->device = device;
     RPGB_CUDA(cudaSetDevice(device));
     RPGB_CUDA(cudaDeviceGetAttribute(&e->num_sms, cudaDevAttrMultiProcessorCount, device));
     PrepareMatvecKernels();
     PrepareSampleKernels();
     const size_t qa = (qb + 255) / 256 * 256, sa = (sb + 255) / 256 * 256;
-    std::vector<uint8_t> host(qa + sa + db);
-    RepackRows(type, static_cast<const uint8_t*>(bytes), rows, cols, host.data(), host.data() + qa,
+    const int64_t rb = GgmlRowBytes(type, cols);
+    std::vector<uint8_t> src(static_cast<size_t>(prow * rb), 0);
+    std::memcpy(src.data(), bytes, static_cast<size_t>(rows * rb));
+    std::vector<uint8_t> host(qa + sa + db + 256, 0);
+    RepackRows(type, src.data(), prow, cols, host.data(), host.data() + qa,
                db ? reinterpret_cast<uint16_t*>(host.data() + qa + sa) : nullptr);
     RPGB_CUDA(cudaMalloc(&e->mem, host.size()));
     RPGB_CUDA(cudaMemcpy(e->mem, host.data(), host.size(), cudaMemcpyHostToDevice));
     uint8_t* base = static_cast<uint8_t*>(e->mem);
     e->m.type = type;
-    e->m.rows = static_cast<int32_t>(rows);
+    e->m.rows = static_cast<int32_t>(prow);
     e->m.cols = static_cast<int32_t>(cols);
     e->m.nb = static_cast<int32_t>(cols / 256);
     e->m.q = base;
@@ -281,6 +290,8 @@ int32_t rpgb_matrix_dequant(int32_t matrix, int64_t row0, int64_t n_rows, float*
     SetLastError("");
     auto e = GetMatrix(matrix);
     RPGB_CUDA(cudaSetDevice(e->device));
+    RPGB_CHECK(row0 >= 0 && n_rows > 0 && row0 + n_rows <= e->rows, "dequant: rows [%lld, %lld) out of range",
+               static_cast<long long>(row0), static_cast<long long>(row0 + n_rows));
     LaunchDequantRows(e->m, row0, n_rows, dst_dev, static_cast<cudaStream_t>(stream));
     return 0;
   }
@@ -295,6 +306,8 @@ int32_t rpgb_matrix_matvec(int32_t matrix, const float* x_dev, int64_t n_tok, fl
     RPGB_CHECK(n_tok > 0 && n_tok < (1 << 24), "bad token count");
     RPGB_CUDA(cudaSetDevice(e->device));
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    RPGB_CHECK(e->rows % 32 == 0, "matvec: %lld rows; the kernels need a multiple of 32 rows",
+               static_cast<long long>(e->rows));
     if (n_tok == 1) {
       MvParams p;
       p.seg[0].w = e->m;

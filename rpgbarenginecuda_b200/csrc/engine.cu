@@ -83,6 +83,7 @@ Session::Session(const Model* m, int64_t max_seq) : m_(m), max_seq_(max_seq) {
   cv.Add(sizeof(int32_t) * kCandBlocks * kFastTopK);
   cv.Add(sizeof(int32_t) * kCandBlocks);
   cv.Add(sizeof(int32_t));
+  cv.Add(sizeof(unsigned));
   RPGB_CUDA(cudaMalloc(&dec_arena_, cv.total()));
   RPGB_CUDA(cudaMemsetAsync(dec_arena_, 0, cv.total(), stream_));
   cv.Begin(dec_arena_);
@@ -103,6 +104,7 @@ Session::Session(const Model* m, int64_t max_seq) : m_(m), max_seq_(max_seq) {
   cand_idx_ = cv.Take<int32_t>(kCandBlocks * kFastTopK);
   cand_cnt_ = cv.Take<int32_t>(kCandBlocks);
   flag_ = cv.Take<int32_t>(1);
+  err_ = cv.Take<unsigned>(1);
   RPGB_CUDA(cudaStreamSynchronize(stream_));
 }
 
@@ -265,7 +267,7 @@ void Session::Prefill(const int32_t* tokens, int64_t n, float* last_logits) {
   logits_valid_ = true;
 }
 
-void Session::EnqueueSample(const SampleOpts& opt, uint64_t seed, int pos_bump) {
+void Session::EnqueueSample(const SampleOpts& opt, uint64_t seed, int pos_bump, bool pdl) {
   const ModelMeta& c = m_->meta();
   SampleParams sp;
   sp.logits = logits_;
@@ -282,7 +284,7 @@ void Session::EnqueueSample(const SampleOpts& opt, uint64_t seed, int pos_bump) 
   sp.cand_idx = cand_idx_;
   sp.cand_cnt = cand_cnt_;
   sp.flag = flag_;
-  LaunchSample(sp, false, stream_);
+  LaunchSample(sp, false, stream_, pdl);
 }
 
 void Session::EnqueueStep(const SampleOpts& opt, uint64_t seed) {
@@ -308,7 +310,8 @@ void Session::EnqueueStep(const SampleOpts& opt, uint64_t seed) {
     q.norm_w = L.attn_norm;
     q.eps = c.rms_eps;
     q.out = qkv_;
-    LaunchMatvec(q, Epi::kStore, 2, sms, s);
+    q.err = err_;
+    LaunchMatvec(q, Epi::kStore, 2, sms, s, true);
 
     AttnParams a;
     a.q = qkv_;
@@ -331,7 +334,7 @@ void Session::EnqueueStep(const SampleOpts& opt, uint64_t seed) {
     a.ticket = tickets_;
     a.n_splits = n_splits_;
     a.fused = 1;
-    LaunchAttention(a, 1, s);
+    LaunchAttention(a, 1, s, true);
 
     MvParams o;
     o.seg[0].w = L.o;
@@ -339,7 +342,8 @@ void Session::EnqueueStep(const SampleOpts& opt, uint64_t seed) {
     o.x = attn_;
     o.out = x_;
     o.resid = x_;
-    LaunchMatvec(o, Epi::kResid, 1, sms, s);
+    o.err = err_;
+    LaunchMatvec(o, Epi::kResid, 1, sms, s, true);
 
     MvParams gu;
     gu.seg[0].w = L.gateup;
@@ -348,7 +352,8 @@ void Session::EnqueueStep(const SampleOpts& opt, uint64_t seed) {
     gu.norm_w = L.ffn_norm;
     gu.eps = c.rms_eps;
     gu.out = h_;
-    LaunchMatvec(gu, Epi::kSilu, 2, sms, s);
+    gu.err = err_;
+    LaunchMatvec(gu, Epi::kSilu, 2, sms, s, true);
 
     MvParams dn;
     dn.seg[0].w = L.down;
@@ -356,7 +361,8 @@ void Session::EnqueueStep(const SampleOpts& opt, uint64_t seed) {
     dn.x = h_;
     dn.out = x_;
     dn.resid = x_;
-    LaunchMatvec(dn, Epi::kResid, 1, sms, s);
+    dn.err = err_;
+    LaunchMatvec(dn, Epi::kResid, 1, sms, s, true);
     launches += 5;
   }
   MvParams lm;
@@ -366,6 +372,7 @@ void Session::EnqueueStep(const SampleOpts& opt, uint64_t seed) {
   lm.norm_w = m_->out_norm();
   lm.eps = c.rms_eps;
   lm.out = logits_;
+  lm.err = err_;
   if (!(opt.temperature > 0.0f)) {
     lm.part_val = am_val_;
     lm.part_idx = am_idx_;
@@ -373,11 +380,11 @@ void Session::EnqueueStep(const SampleOpts& opt, uint64_t seed) {
     lm.tok_out = tok_;
     lm.pos = pos_;
     lm.pos_bump = 1;
-    LaunchMatvec(lm, Epi::kArgmax, 4, sms, s);
+    LaunchMatvec(lm, Epi::kArgmax, 4, sms, s, true);
     launches += 1;
   } else {
-    LaunchMatvec(lm, Epi::kStore, 4, sms, s);
-    EnqueueSample(opt, seed, 1);
+    LaunchMatvec(lm, Epi::kStore, 4, sms, s, true);
+    EnqueueSample(opt, seed, 1, true);
     const bool fast = opt.top_k > 1 && opt.top_k <= kFastTopK && opt.top_k < c.vocab;
     launches += fast ? 4 : 2;
   }
@@ -463,6 +470,12 @@ int Session::Generate(const SampleOpts& opt, uint64_t seed, int32_t max_tokens, 
       }
     }
     if (!stopped) produced += todo;
+  }
+  unsigned err = 0;
+  RPGB_CUDA(cudaMemcpy(&err, err_, sizeof(unsigned), cudaMemcpyDeviceToHost));
+  if (err != 0) {
+    RPGB_CUDA(cudaMemset(err_, 0, sizeof(unsigned)));
+    Throw("a device-side wait for streamed weights timed out during decode (results discarded)");
   }
   std::memcpy(out, host_ids_, sizeof(int32_t) * produced);
   // Every returned token (stop included) was forwarded: len = prompt + generated.

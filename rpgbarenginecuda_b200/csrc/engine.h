@@ -62,7 +62,7 @@ class Session {
 
  private:
   void EnqueueStep(const SampleOpts& opt, uint64_t seed);
-  void EnqueueSample(const SampleOpts& opt, uint64_t seed, int pos_bump);
+  void EnqueueSample(const SampleOpts& opt, uint64_t seed, int pos_bump, bool pdl = false);
   void EnsurePrefill(int64_t n);
   void DropGraph();
 
@@ -91,6 +91,7 @@ class Session {
   int32_t* cand_idx_ = nullptr;
   int32_t* cand_cnt_ = nullptr;
   int32_t* flag_ = nullptr;
+  unsigned* err_ = nullptr;  // set by a bounded device wait that gave up
   int n_splits_ = 1;
 
   // prefill scratch (grow-only)

@@ -17,6 +17,7 @@
 #include "common.h"
 #include "kernels.cuh"
 #include "kernels.h"
+#include "launch.h"
 
 namespace rpgb {
 namespace {
@@ -87,12 +88,15 @@ __global__ void __launch_bounds__(128) AttnKernel(const AttnParams p) {
   __shared__ __align__(16) float qs[G][D];
   __shared__ __align__(16) float kb[1][D];
   __shared__ float sc[G][128];
+  __shared__ __align__(16) float vred[4][G][D];
   __shared__ double dsh[4 * G];
   __shared__ float fsh[4 * G];
   __shared__ int s_last;
 
   const int s = blockIdx.x, h = blockIdx.y, t = blockIdx.z;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // The position counter of this step was written before the step started
+  // (previous graph launch / host copy), so it may be read before the wait.
   const int64_t pos = *p.pos + t;
   const int64_t L = pos + 1;
   const int64_t chunk = (L + p.n_splits - 1) / p.n_splits;
@@ -101,6 +105,19 @@ __global__ void __launch_bounds__(128) AttnKernel(const AttnParams p) {
   const int q_dim = p.n_heads * D;
   __half* kbase = p.kc + static_cast<int64_t>(h) * p.max_seq * D;
   __half* vbase = p.vc + static_cast<int64_t>(h) * p.max_seq * D;
+
+  // Rows before `pos` were written by earlier steps: pull them toward L2 while
+  // the previous kernel (the q/k/v projection) is still running.
+  if (p.fused && tid == 0) {
+    const int64_t pe = p1 < pos ? p1 : pos;
+    if (pe > p0) {
+      const uint32_t bytes = static_cast<uint32_t>((pe - p0) * D * 2);
+      dev::PrefetchL2(kbase + p0 * D, bytes);
+      dev::PrefetchL2(vbase + p0 * D, bytes);
+    }
+  }
+  dev::GridLaunchDependents();
+  dev::GridWait();
 
   // ---- the G query vectors of this group
   {
@@ -123,19 +140,22 @@ __global__ void __launch_bounds__(128) AttnKernel(const AttnParams p) {
   }
   __syncthreads();
 
-  float m[G], acc[G];
+  float m[G];
   double l[G];
+  float acc[G][4];  // dims 4*lane .. 4*lane+3, positions of this warp
 #pragma unroll
   for (int g = 0; g < G; ++g) {
     m[g] = -INFINITY;
     l[g] = 0.0;
-    acc[g] = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[g][e] = 0.f;
   }
 
   for (int64_t c0 = p0; c0 < p1; c0 += 128) {
     const int64_t pp = c0 + tid;
     float sg[G];
     if (pp < p1) {
+      // one position per thread: 256 B of K, dot in ascending d (src/kernels_gpu.cu:772-777)
       const uint4* kr = reinterpret_cast<const uint4*>(kbase + pp * D);
       float dot[G];
 #pragma unroll
@@ -178,26 +198,47 @@ __global__ void __launch_bounds__(128) AttnKernel(const AttnParams p) {
       alpha[g] = m[g] == -INFINITY ? 0.f : expf(m[g] - nm);
       m[g] = nm;
     }
-    BlockSumG<G>(cs, dsh);  // also orders the sc[] writes before the reads below
+    BlockSumG<G>(cs, dsh);  // its barriers also publish sc[] to all warps
     const int nv = static_cast<int>(p1 - c0 < 128 ? p1 - c0 : 128);
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       l[g] = l[g] * static_cast<double>(alpha[g]) + cs[g];
-      acc[g] *= alpha[g];
-    }
-    const __half* vr = vbase + c0 * D + tid;
-    for (int j = 0; j < nv; ++j) {
-      const float vv = __half2float(vr[static_cast<int64_t>(j) * D]);
 #pragma unroll
-      for (int g = 0; g < G; ++g) acc[g] = fmaf(sc[g][j], vv, acc[g]);
+      for (int e = 0; e < 4; ++e) acc[g][e] *= alpha[g];
+    }
+    // V: warp w takes positions w, w+4, ...; lane holds 4 consecutive dims (8 B loads)
+    const __half* vr = vbase + c0 * D + 4 * lane;
+#pragma unroll 4
+    for (int j = warp; j < nv; j += 4) {
+      const uint2 raw = *reinterpret_cast<const uint2*>(vr + static_cast<int64_t>(j) * D);
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float e = sc[g][j];
+        acc[g][0] = fmaf(e, a.x, acc[g][0]);
+        acc[g][1] = fmaf(e, a.y, acc[g][1]);
+        acc[g][2] = fmaf(e, b.x, acc[g][2]);
+        acc[g][3] = fmaf(e, b.y, acc[g][3]);
+      }
     }
     __syncthreads();
   }
 
+  // combine the 4 warps' partial V sums: thread tid ends up with dim tid
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    *reinterpret_cast<float4*>(&vred[warp][g][4 * lane]) = make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
+  }
+  __syncthreads();
+  float o[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) o[g] = ((vred[0][g][tid] + vred[1][g][tid]) + vred[2][g][tid]) + vred[3][g][tid];
+
   if (p.n_splits == 1) {
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      p.out[static_cast<int64_t>(t) * q_dim + (h * G + g) * D + tid] = acc[g] * static_cast<float>(1.0 / l[g]);
+      p.out[static_cast<int64_t>(t) * q_dim + (h * G + g) * D + tid] = o[g] * static_cast<float>(1.0 / l[g]);
     }
     return;
   }
@@ -211,7 +252,7 @@ __global__ void __launch_bounds__(128) AttnKernel(const AttnParams p) {
       rec[0] = m[g];
       rec[1] = static_cast<float>(l[g]);
     }
-    rec[2 + tid] = acc[g];
+    rec[2 + tid] = o[g];
   }
   __threadfence();
   __syncthreads();
@@ -292,20 +333,21 @@ size_t AttentionPartialFloats(int n_kv, int group, int n_splits) {
   return static_cast<size_t>(n_kv) * n_splits * group * (D + 2);
 }
 
-void LaunchAttention(const AttnParams& p, int n_queries, cudaStream_t s) {
+void LaunchAttention(const AttnParams& p, int n_queries, cudaStream_t s, bool pdl) {
   RPGB_CHECK(n_queries >= 1 && n_queries < 65536, "attention: bad query count %d", n_queries);
   RPGB_CHECK(p.n_splits >= 1 && (p.n_splits == 1 || n_queries == 1), "attention: split-K is decode only");
   RPGB_CHECK(p.n_heads % p.n_kv == 0, "attention: bad head counts");
   const int G = p.n_heads / p.n_kv;
   const dim3 grid(p.n_splits, p.n_kv, n_queries);
+  const void* fn = nullptr;
   switch (G) {
-    case 1: AttnKernel<1><<<grid, 128, 0, s>>>(p); break;
-    case 2: AttnKernel<2><<<grid, 128, 0, s>>>(p); break;
-    case 4: AttnKernel<4><<<grid, 128, 0, s>>>(p); break;
-    case 8: AttnKernel<8><<<grid, 128, 0, s>>>(p); break;
+    case 1: fn = reinterpret_cast<const void*>(AttnKernel<1>); break;
+    case 2: fn = reinterpret_cast<const void*>(AttnKernel<2>); break;
+    case 4: fn = reinterpret_cast<const void*>(AttnKernel<4>); break;
+    case 8: fn = reinterpret_cast<const void*>(AttnKernel<8>); break;
     default: Throw("attention: GQA group %d is not supported (1, 2, 4, 8)", G);
   }
-  RPGB_CUDA(cudaGetLastError());
+  LaunchKernelArgs(fn, grid, dim3(128), 0, s, pdl, p);
   CountLaunches(1);
 }
 

@@ -36,15 +36,15 @@ __global__ void __launch_bounds__(256) GemmKernel(const GemmParams p) {
 
   for (int kb = 0; kb < K / BK; ++kb) {
     float wv[8], xv[8];
-    const int64_t blk = row * w.nb + (kb >> 3);
+    const int b = kb >> 3;
     if (w.type == 12u) {
       const int j = kb & 7;
-      const uint4 hd = *reinterpret_cast<const uint4*>(w.s + blk * 16);
+      const uint4 hd = *reinterpret_cast<const uint4*>(w.s + dev::SByte(w, row, b));
       int sc, m;
       dev::Q4kScaleMin(hd.y, hd.z, hd.w, j, &sc, &m);
       const float d1 = __fmul_rn(dev::Half(hd.x & 0xFFFFu), static_cast<float>(sc));
       const float m1 = __fmul_rn(dev::Half(hd.x >> 16), static_cast<float>(m));
-      const uint2 qb = *reinterpret_cast<const uint2*>(w.q + blk * 128 + 32 * (j >> 1) + lk);
+      const uint2 qb = *reinterpret_cast<const uint2*>(w.q + dev::QByte(w, row, b, 32 * (j >> 1) + lk));
       const uint32_t qw[2] = {qb.x, qb.y};
       const int sh = (j & 1) * 4;
 #pragma unroll
@@ -55,11 +55,11 @@ __global__ void __launch_bounds__(256) GemmKernel(const GemmParams p) {
     } else {
       const int e0 = (kb & 7) * 32 + lk;
       const int hh = e0 >> 7, r = e0 & 127, quarter = r >> 5, l0 = r & 31;
-      const uint8_t* base = w.q + blk * 192;
-      const uint2 qlb = *reinterpret_cast<const uint2*>(base + hh * 64 + l0 + ((quarter & 1) ? 32 : 0));
-      const uint2 qhb = *reinterpret_cast<const uint2*>(base + 128 + hh * 32 + l0);
-      const int8_t sc = static_cast<int8_t>(w.s[blk * 16 + hh * 8 + (l0 >> 4) + 2 * quarter]);
-      const float ds = __fmul_rn(dev::Half(w.d[blk]), static_cast<float>(sc));
+      const uint2 qlb =
+          *reinterpret_cast<const uint2*>(w.q + dev::QByte(w, row, b, hh * 64 + l0 + ((quarter & 1) ? 32 : 0)));
+      const uint2 qhb = *reinterpret_cast<const uint2*>(w.q + dev::QByte(w, row, b, 128 + hh * 32 + l0));
+      const int8_t sc = static_cast<int8_t>(w.s[dev::SByte(w, row, b) + hh * 8 + (l0 >> 4) + 2 * quarter]);
+      const float ds = __fmul_rn(dev::Half(w.d[dev::DIndex(w, row, b)]), static_cast<float>(sc));
       const uint32_t ql[2] = {qlb.x, qlb.y}, qh[2] = {qhb.x, qhb.y};
       const int nsh = quarter < 2 ? 0 : 4;
 #pragma unroll

@@ -26,6 +26,7 @@
 #include "common.h"
 #include "kernels.cuh"
 #include "kernels.h"
+#include "launch.h"
 
 namespace rpgb {
 namespace {
@@ -127,6 +128,8 @@ __global__ void __launch_bounds__(kGenThreads) SampleGeneralKernel(const SampleP
   __shared__ double wsc[32];
   __shared__ int s_idx, s_amb;
 
+  dev::GridLaunchDependents();
+  dev::GridWait();
   if (skip_if_flag && p.flag != nullptr && *p.flag == 1) return;
   const int n = p.n, tid = threadIdx.x;
   float* probs = p.probs;
@@ -293,6 +296,8 @@ __global__ void __launch_bounds__(kCandThreads) CandKernel(const SampleParams p)
   __shared__ unsigned hist[256];
   __shared__ uint32_t s_sel[2];
   __shared__ int s_cnt;
+  dev::GridLaunchDependents();
+  dev::GridWait();
   const int n = p.n;
   const int per = (n + kCandBlocks - 1) / kCandBlocks;
   const int a = blockIdx.x * per;
@@ -330,6 +335,8 @@ __global__ void __launch_bounds__(kSmallThreads) SampleSmallKernel(const SampleP
   __shared__ int s_off[kCandBlocks + 1];
   __shared__ int s_bad, s_m, s_c;
   const int tid = threadIdx.x;
+  dev::GridLaunchDependents();
+  dev::GridWait();
   if (tid == 0) {
     int off = 0, bad = 0;
     for (int b = 0; b < kCandBlocks; ++b) {
@@ -485,25 +492,22 @@ void PrepareSampleKernels() {
                                  static_cast<int>(static_cast<size_t>(kMaxCand) * 16)));
 }
 
-void LaunchSample(const SampleParams& p, bool want_probs, cudaStream_t s) {
+void LaunchSample(const SampleParams& p, bool want_probs, cudaStream_t s, bool pdl) {
   RPGB_CHECK(p.n > 0, "sample: empty vocabulary");
   RPGB_CHECK(p.tok_out != nullptr && p.probs != nullptr, "sample: null buffers");
   const bool fast = !want_probs && p.temperature > 0.0f && p.top_k > 1 && p.top_k <= kFastTopK &&
                     p.top_k < p.n && p.n <= kCandBlocks * kSliceMax && p.cand_val != nullptr &&
                     p.flag != nullptr;
   if (fast) {
-    CandKernel<<<kCandBlocks, kCandThreads, 0, s>>>(p);
-    RPGB_CUDA(cudaGetLastError());
+    LaunchKernelArgs(reinterpret_cast<const void*>(CandKernel), dim3(kCandBlocks), dim3(kCandThreads), 0, s, pdl, p);
     const size_t smem = static_cast<size_t>(kMaxCand) * 16;
-    SampleSmallKernel<<<1, kSmallThreads, smem, s>>>(p);
-    RPGB_CUDA(cudaGetLastError());
-    SampleGeneralKernel<<<1, kGenThreads, 0, s>>>(p, 1);
+    LaunchKernelArgs(reinterpret_cast<const void*>(SampleSmallKernel), dim3(1), dim3(kSmallThreads), smem, s, pdl, p);
+    LaunchKernelArgs(reinterpret_cast<const void*>(SampleGeneralKernel), dim3(1), dim3(kGenThreads), 0, s, pdl, p, 1);
     CountLaunches(3);
   } else {
-    SampleGeneralKernel<<<1, kGenThreads, 0, s>>>(p, 0);
+    LaunchKernelArgs(reinterpret_cast<const void*>(SampleGeneralKernel), dim3(1), dim3(kGenThreads), 0, s, pdl, p, 0);
     CountLaunches(1);
   }
-  RPGB_CUDA(cudaGetLastError());
 }
 
 }  // namespace rpgb

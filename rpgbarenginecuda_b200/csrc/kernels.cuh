@@ -50,41 +50,107 @@ __device__ __forceinline__ int Q6kScale(const uint4& s, int i) {
   return static_cast<int>(static_cast<int8_t>(ByteOf(w, i & 3)));
 }
 
+// ------------------------------------------------------------------ weight layout
+//
+// Matrices are stored in 32-row groups.  Inside a group, block b (256
+// weights) of every row is cut into 16-byte chunks (Q4_K: 8 chunks = qs[128];
+// Q6_K: 12 chunks = ql[128] | qh[64]) and chunk c of the 32 rows is stored
+// contiguously (512 bytes).  The 16-byte scale record of (row, block) and the
+// Q6_K d follow the same row-interleaved order.  A warp whose lane r owns row
+// r of a group therefore reads 512 contiguous bytes per chunk, and a stage of
+// (group, block range) is one contiguous byte range per array (one TMA bulk
+// copy each).
+constexpr int kGroupRows = 32;
+__host__ __device__ __forceinline__ int QChunks(uint32_t type) { return type == 12u ? 8 : 12; }
+
+__device__ __forceinline__ int64_t QByte(const DevMat& w, int64_t row, int b, int i) {
+  return (((row >> 5) * w.nb + b) * QChunks(w.type) + (i >> 4)) * 512 + (row & 31) * 16 + (i & 15);
+}
+__device__ __forceinline__ int64_t SByte(const DevMat& w, int64_t row, int b) {
+  return (((row >> 5) * w.nb + b) * 32 + (row & 31)) * 16;
+}
+__device__ __forceinline__ int64_t DIndex(const DevMat& w, int64_t row, int b) {
+  return ((row >> 5) * w.nb + b) * 32 + (row & 31);
+}
+
 // ------------------------------------------------------------------ element dequant (bit-exact)
 
-// Element e (0..255) of Q4_K block `blk` of a repacked matrix.
-__device__ __forceinline__ float DeqQ4K(const DevMat& w, int64_t blk, int e) {
-  const uint8_t* hd = w.s + blk * 16;
-  const uint32_t d_dm = *reinterpret_cast<const uint32_t*>(hd);
-  const uint4 h = *reinterpret_cast<const uint4*>(hd);
+// Element e (0..255) of Q4_K block b of `row`.
+__device__ __forceinline__ float DeqQ4K(const DevMat& w, int64_t row, int b, int e) {
+  const uint4 h = *reinterpret_cast<const uint4*>(w.s + SByte(w, row, b));
   const int sub = e >> 5, l = e & 31;
   int sc, m;
   Q4kScaleMin(h.y, h.z, h.w, sub, &sc, &m);
-  const uint8_t byte = w.q[blk * 128 + (sub >> 1) * 32 + l];
+  const uint8_t byte = w.q[QByte(w, row, b, (sub >> 1) * 32 + l)];
   const int raw = (sub & 1) ? (byte >> 4) : (byte & 15);
-  const float d = Half(d_dm & 0xFFFFu), dmin = Half(d_dm >> 16);
+  const float d = Half(h.x & 0xFFFFu), dmin = Half(h.x >> 16);
   const float d1 = __fmul_rn(d, static_cast<float>(sc));
   const float m1 = __fmul_rn(dmin, static_cast<float>(m));
   return __fsub_rn(__fmul_rn(d1, static_cast<float>(raw)), m1);
 }
 
-// Element e (0..255) of Q6_K block `blk` of a repacked matrix.
-__device__ __forceinline__ float DeqQ6K(const DevMat& w, int64_t blk, int e) {
+// Element e (0..255) of Q6_K block b of `row`.
+__device__ __forceinline__ float DeqQ6K(const DevMat& w, int64_t row, int b, int e) {
   const int hh = e >> 7, r = e & 127, quarter = r >> 5, l = r & 31;
-  const uint8_t* base = w.q + blk * 192;
-  const uint8_t byte = base[hh * 64 + l + ((quarter & 1) ? 32 : 0)];
+  const uint8_t byte = w.q[QByte(w, row, b, hh * 64 + l + ((quarter & 1) ? 32 : 0))];
   const int nib = quarter < 2 ? (byte & 15) : (byte >> 4);
-  const int hi = (base[128 + hh * 32 + l] >> (2 * quarter)) & 3;
+  const int hi = (w.q[QByte(w, row, b, 128 + hh * 32 + l)] >> (2 * quarter)) & 3;
   const int raw = (nib | (hi << 4)) - 32;
-  const int8_t sc = static_cast<int8_t>(w.s[blk * 16 + hh * 8 + (l >> 4) + 2 * quarter]);
-  const float d = Half(w.d[blk]);
+  const int8_t sc = static_cast<int8_t>(w.s[SByte(w, row, b) + hh * 8 + (l >> 4) + 2 * quarter]);
+  const float d = Half(w.d[DIndex(w, row, b)]);
   return __fmul_rn(__fmul_rn(d, static_cast<float>(sc)), static_cast<float>(raw));
 }
 
 __device__ __forceinline__ float DeqElem(const DevMat& w, int64_t row, int col) {
-  const int64_t blk = row * w.nb + (col >> 8);
-  return w.type == 12u ? DeqQ4K(w, blk, col & 255) : DeqQ6K(w, blk, col & 255);
+  return w.type == 12u ? DeqQ4K(w, row, col >> 8, col & 255) : DeqQ6K(w, row, col >> 8, col & 255);
 }
+
+// ------------------------------------------------------------------ async copy / PDL primitives
+
+__device__ __forceinline__ uint32_t SmemAddr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void MbarInit(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(SmemAddr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void MbarInitFence() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void MbarExpectTx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(SmemAddr(bar)), "r"(bytes) : "memory");
+}
+// 1-D bulk copy global -> shared, completion counted on `bar` (16-byte aligned,
+// size a multiple of 16).  No multicast.
+__device__ __forceinline__ void BulkG2S(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   SmemAddr(dst)),
+               "l"(src), "r"(bytes), "r"(SmemAddr(bar))
+               : "memory");
+}
+__device__ __forceinline__ void PrefetchL2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void FenceProxyAsync() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ bool MbarTryWait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(SmemAddr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait (each try_wait suspends for a hardware-bounded time): returns
+// false after `limit` attempts instead of spinning forever.
+__device__ __forceinline__ bool MbarWait(uint64_t* bar, uint32_t parity, uint32_t limit = 1u << 22) {
+  for (uint32_t i = 0; i < limit; ++i) {
+    if (MbarTryWait(bar, parity)) return true;
+  }
+  return false;
+}
+// Programmatic dependent launch: let the next kernel in the stream start its
+// prologue / wait until the previous kernel's results are visible.  Both are
+// no-ops for a launch without the programmatic-serialization attribute.
+__device__ __forceinline__ void GridLaunchDependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void GridWait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // ------------------------------------------------------------------ reductions
 

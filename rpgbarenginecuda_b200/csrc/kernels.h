@@ -46,6 +46,9 @@ struct MvParams {
   int32_t* tok_out = nullptr;
   int64_t* pos = nullptr;  // incremented by pos_bump by the reducing block
   int32_t pos_bump = 0;
+  unsigned* err = nullptr;  // set to nonzero if a bounded device wait gave up
+  // launch geometry, filled in by LaunchMatvec
+  int32_t n_groups = 0, kb = 0, n_chunks = 0, slots = 0, slot_bytes = 0;
 };
 
 // Sets the dynamic shared-memory limits of every kernel instantiation on the
@@ -54,8 +57,10 @@ struct MvParams {
 void PrepareMatvecKernels();
 void PrepareSampleKernels();
 
-// Rows handled per warp: 1, 2 or 4 (kSilu needs an even value).
-void LaunchMatvec(const MvParams& p, Epi epi, int rows_per_warp, int num_sms, cudaStream_t s);
+// Rows handled per warp is fixed by the layout (one row per lane); the
+// argument is kept for call-site compatibility.  `pdl`: launch with
+// programmatic dependent launch (see launch.h).
+void LaunchMatvec(const MvParams& p, Epi epi, int rows_per_warp, int num_sms, cudaStream_t s, bool pdl = false);
 // Scratch sizes needed by kArgmax for a given launch.
 int MatvecGrid(int total_rows, int rows_per_warp, int num_sms);
 
@@ -63,7 +68,7 @@ int MatvecGrid(int total_rows, int rows_per_warp, int num_sms);
 
 // x[t, :] = dequant(embd row tok[t]); if out_ids != nullptr also out_ids[*pos + t] = tok[t].
 void LaunchEmbed(const DevMat& embd, const int32_t* tok, int n_tok, float* x, const int64_t* pos,
-                 int32_t* out_ids, cudaStream_t s);
+                 int32_t* out_ids, cudaStream_t s, bool pdl = false);
 
 // dst[i] = dequant(W row `row`, element i) for a whole row (bit-exact dequant entry).
 void LaunchDequantRows(const DevMat& w, int64_t row0, int64_t n_rows, float* dst, cudaStream_t s);
@@ -91,7 +96,7 @@ struct AttnParams {
   int32_t n_splits = 1;
   int32_t fused = 0;  // 1: decode (norm + rope + cache write of the current token inside)
 };
-void LaunchAttention(const AttnParams& p, int n_queries, cudaStream_t s);
+void LaunchAttention(const AttnParams& p, int n_queries, cudaStream_t s, bool pdl = false);
 size_t AttentionPartialFloats(int n_kv, int group, int n_splits);
 
 // Prefill helpers: per-head RMSNorm + RoPE for q and k, fp16 cache write of k and v.
@@ -138,6 +143,6 @@ struct SampleParams {
 // back to the general kernel on the device if a block overflowed.
 constexpr int kFastTopK = 64;
 constexpr int kCandBlocks = 148;
-void LaunchSample(const SampleParams& p, bool want_probs, cudaStream_t s);
+void LaunchSample(const SampleParams& p, bool want_probs, cudaStream_t s, bool pdl = false);
 
 }  // namespace rpgb

@@ -145,25 +145,38 @@ void DevMatBytes(uint32_t type, int64_t rows, int64_t cols, size_t* q, size_t* s
   }
 }
 
+void RepackGroup(uint32_t type, const uint8_t* const* src, int64_t nb, uint8_t* dq, uint8_t* ds, uint16_t* dd) {
+  RPGB_CHECK(type == kGgmlQ4_K || type == kGgmlQ6_K, "matrix type %s is not supported (Q4_K and Q6_K are)",
+             GgmlTypeName(type));
+  const bool q4 = type == kGgmlQ4_K;
+  const int nc = q4 ? 8 : 12;
+  const int bb = q4 ? 144 : 210;
+  for (int64_t b = 0; b < nb; ++b) {
+    for (int r = 0; r < 32; ++r) {
+      const uint8_t* blk = src[r] + b * bb;
+      const uint8_t* qbytes = q4 ? blk + 16 : blk;  // Q4_K qs follow the 16-byte header
+      for (int c = 0; c < nc; ++c) std::memcpy(dq + ((b * nc + c) * 512 + r * 16), qbytes + 16 * c, 16);
+      if (q4) {
+        std::memcpy(ds + (b * 32 + r) * 16, blk, 16);
+      } else {
+        std::memcpy(ds + (b * 32 + r) * 16, blk + 192, 16);
+        std::memcpy(dd + b * 32 + r, blk + 208, 2);
+      }
+    }
+  }
+}
+
 void RepackRows(uint32_t type, const uint8_t* src, int64_t rows, int64_t cols, uint8_t* dq, uint8_t* ds,
                 uint16_t* dd) {
+  RPGB_CHECK(rows % 32 == 0, "rows %lld are not a multiple of 32", static_cast<long long>(rows));
   const int64_t nb = cols / 256;
-  const int64_t n = rows * nb;
-  if (type == kGgmlQ4_K) {
-    for (int64_t i = 0; i < n; ++i) {
-      const uint8_t* b = src + i * 144;
-      std::memcpy(ds + i * 16, b, 16);
-      std::memcpy(dq + i * 128, b + 16, 128);
-    }
-  } else if (type == kGgmlQ6_K) {
-    for (int64_t i = 0; i < n; ++i) {
-      const uint8_t* b = src + i * 210;
-      std::memcpy(dq + i * 192, b, 192);
-      std::memcpy(ds + i * 16, b + 192, 16);
-      std::memcpy(dd + i, b + 208, 2);
-    }
-  } else {
-    Throw("matrix type %s is not supported (Q4_K and Q6_K are)", GgmlTypeName(type));
+  const int64_t rb = GgmlRowBytes(type, cols);
+  size_t qg, sg, dg;
+  DevMatBytes(type, 32, cols, &qg, &sg, &dg);
+  for (int64_t g = 0; g < rows / 32; ++g) {
+    const uint8_t* ptrs[32];
+    for (int r = 0; r < 32; ++r) ptrs[r] = src + (g * 32 + r) * rb;
+    RepackGroup(type, ptrs, nb, dq + g * qg, ds + g * sg, dd ? dd + g * (dg / 2) : nullptr);
   }
 }
 
@@ -335,31 +348,37 @@ std::unique_ptr<Model> Model::Load(const std::string& path, int device, int32_t 
     *j.dst = dm;
 
     const int64_t row_src_bytes = GgmlRowBytes(type, cols);
-    size_t qr, sr, dr;
-    DevMatBytes(type, 1, cols, &qr, &sr, &dr);
-    const int64_t rows_per_chunk = std::max<int64_t>(2, static_cast<int64_t>(up.cap() / (qr + sr + dr)) / 2 * 2);
-    for (int64_t r0 = 0; r0 < rows; r0 += rows_per_chunk) {
-      const int64_t nr = std::min(rows_per_chunk, rows - r0);
-      uint8_t* st = up.buf();
-      uint8_t* sq = st;
-      uint8_t* ss = st + nr * qr;
-      uint16_t* sd = reinterpret_cast<uint16_t*>(ss + nr * sr);
-      ParallelRows(nr, [&](int64_t a, int64_t b) {
-        for (int64_t r = a; r < b; ++r) {
-          const int64_t dst_row = r0 + r;
-          const GgufTensor* src_t = j.a;
-          int64_t src_row = dst_row;
-          if (j.b != nullptr) {
-            src_t = (dst_row & 1) ? j.b : j.a;
-            src_row = dst_row >> 1;
+    size_t qg, sg, dg;  // bytes of one 32-row group
+    DevMatBytes(type, 32, cols, &qg, &sg, &dg);
+    RPGB_CHECK(rows % 32 == 0, "tensor %s: %lld rows are not a multiple of 32", j.a->name.c_str(),
+               static_cast<long long>(rows));
+    const int64_t groups = rows / 32;
+    const int64_t groups_per_chunk = std::max<int64_t>(1, static_cast<int64_t>(up.cap() / (qg + sg + dg)));
+    for (int64_t g0 = 0; g0 < groups; g0 += groups_per_chunk) {
+      const int64_t ng = std::min(groups_per_chunk, groups - g0);
+      uint8_t* sq = up.buf();
+      uint8_t* ss = sq + ng * qg;
+      uint16_t* sd = reinterpret_cast<uint16_t*>(ss + ng * sg);
+      ParallelRows(ng * 32, [&](int64_t a, int64_t b) {
+        for (int64_t gi = a / 32; gi * 32 < b; ++gi) {
+          if (gi * 32 < a) continue;
+          const uint8_t* ptrs[32];
+          for (int r = 0; r < 32; ++r) {
+            const int64_t dst_row = (g0 + gi) * 32 + r;
+            const GgufTensor* src_t = j.a;
+            int64_t src_row = dst_row;
+            if (j.b != nullptr) {  // gate/up interleave: 2i = gate row i, 2i+1 = up row i
+              src_t = (dst_row & 1) ? j.b : j.a;
+              src_row = dst_row >> 1;
+            }
+            ptrs[r] = g.TensorData(*src_t) + src_row * row_src_bytes;
           }
-          RepackRows(type, g.TensorData(*src_t) + src_row * row_src_bytes, 1, cols, sq + r * qr, ss + r * sr,
-                     dr ? sd + r * (dr / 2) : nullptr);
+          RepackGroup(type, ptrs, cols / 256, sq + gi * qg, ss + gi * sg, dg ? sd + gi * (dg / 2) : nullptr);
         }
       });
-      up.Push(dq + r0 * qr, sq, nr * qr);
-      up.Push(ds + r0 * sr, ss, nr * sr);
-      if (dr) up.Push(dd + r0 * dr, reinterpret_cast<const uint8_t*>(sd), nr * dr);
+      up.Push(dq + g0 * qg, sq, ng * qg);
+      up.Push(ds + g0 * sg, ss, ng * sg);
+      if (dg) up.Push(dd + g0 * dg, reinterpret_cast<const uint8_t*>(sd), ng * dg);
       up.Wait();
     }
   }

@@ -61,8 +61,12 @@ struct DevLayer {
   DevMat down;
 };
 
-// Host-side repack of GGUF blocks into the device layout (exposed for tests).
-// dst_q / dst_s / dst_d sizes: see DevMatBytes.
+// Host-side repack of GGUF blocks into the device layout: 32-row groups with
+// 16-byte chunks interleaved across the rows (see kernels.cuh).  RepackGroup
+// takes the 32 source rows by pointer (gate/up interleave); RepackRows takes
+// `rows` (a multiple of 32) contiguous GGUF rows.  Sizes: see DevMatBytes.
+void RepackGroup(uint32_t type, const uint8_t* const* src_rows, int64_t nb, uint8_t* dst_q, uint8_t* dst_s,
+                 uint16_t* dst_d);
 void RepackRows(uint32_t type, const uint8_t* src, int64_t rows, int64_t cols, uint8_t* dst_q,
                 uint8_t* dst_s, uint16_t* dst_d);
 void DevMatBytes(uint32_t type, int64_t rows, int64_t cols, size_t* q, size_t* s, size_t* d);
