@@ -95,6 +95,20 @@ RPGB_API int32_t rpgb_session_stats(int32_t session, int32_t* kernels_per_step, 
  * session's work with CUDA events recorded on that stream. */
 RPGB_API void* rpgb_session_stream(int32_t session);
 
+/* Device timeline of the decode step (no counterpart in the reference, which
+ * times whole steps only): every block of every launch recorded in the step
+ * graph appends one record {launch index within the step, block, start,
+ * ready = after the wait on the previous launch, end}, times in %globaltimer
+ * nanoseconds.  trace_enable(cap) sets room for `cap` records (0 = off) and
+ * re-records the graph; trace_take copies up to `cap` records into `out`
+ * (host memory, 32 bytes each), clears the buffer and returns the count. */
+typedef struct rpgb_trace_rec {
+  uint32_t launch, block;
+  uint64_t t_start, t_ready, t_end;
+} rpgb_trace_rec;
+RPGB_API int32_t rpgb_session_trace_enable(int32_t session, int32_t cap);
+RPGB_API int32_t rpgb_session_trace_take(int32_t session, rpgb_trace_rec* out, int32_t cap);
+
 /* Kernels this library has launched so far in the process, counting every
  * node of a replayed decode graph (instrumentation for benchmarks). */
 RPGB_API int64_t rpgb_launch_count(void);

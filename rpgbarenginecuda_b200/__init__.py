@@ -101,6 +101,19 @@ class Session:
               "session_stats")
         return {"kernels_per_step": k.value, "graph_ready": bool(g.value), "graph_launches": n.value}
 
+    def trace_enable(self, cap: int = 1 << 16):
+        """Record a device timeline of every decode-step launch (0 turns it off)."""
+        check(self._lib.rpgb_session_trace_enable(self.handle, cap), "session_trace_enable")
+
+    TRACE_DTYPE = np.dtype([("launch", np.uint32), ("block", np.uint32), ("t_start", np.uint64),
+                            ("t_ready", np.uint64), ("t_end", np.uint64)])
+
+    def trace_take(self, cap: int = 1 << 16) -> np.ndarray:
+        """Records gathered since the last take (structured array, ns times)."""
+        out = np.zeros(cap, dtype=self.TRACE_DTYPE)
+        n = check(self._lib.rpgb_session_trace_take(self.handle, out.ctypes.data, cap), "session_trace_take")
+        return out[:n].copy()
+
     @property
     def stream_ptr(self) -> int:
         """The session's cudaStream_t (for CUDA-event timing of its work)."""

@@ -45,6 +45,8 @@ _SIGS = {
     "rpgb_generate": (c_i32, [c_i32, ctypes.POINTER(SampleOptions), c_u64, c_i32, c_p, c_i32, c_p, c_p, c_p]),
     "rpgb_session_stats": (c_i32, [c_i32, c_p, c_p, c_p]),
     "rpgb_session_stream": (c_p, [c_i32]),
+    "rpgb_session_trace_enable": (c_i32, [c_i32, c_i32]),
+    "rpgb_session_trace_take": (c_i32, [c_i32, c_p, c_i32]),
     "rpgb_launch_count": (c_i64, []),
     "rpgb_matrix_upload": (c_i32, [c_i32, c_u32, c_i64, c_i64, c_p]),
     "rpgb_matrix_free": (None, [c_i32]),

@@ -218,6 +218,25 @@ int32_t rpgb_session_stats(int32_t session, int32_t* kernels_per_step, int32_t* 
   RPGB_CATCH(-1)
 }
 
+int32_t rpgb_session_trace_enable(int32_t session, int32_t cap) {
+  try {
+    SetLastError("");
+    GetSession(session)->EnableTrace(cap);
+    return 0;
+  }
+  RPGB_CATCH(-1)
+}
+
+int32_t rpgb_session_trace_take(int32_t session, rpgb_trace_rec* out, int32_t cap) {
+  try {
+    SetLastError("");
+    static_assert(sizeof(rpgb_trace_rec) == sizeof(TraceRec), "trace record layout");
+    RPGB_CHECK(out != nullptr || cap == 0, "null trace buffer");
+    return GetSession(session)->TakeTrace(reinterpret_cast<TraceRec*>(out), cap);
+  }
+  RPGB_CATCH(-1)
+}
+
 void* rpgb_session_stream(int32_t session) {
   try {
     return GetSession(session)->stream();
@@ -233,10 +252,9 @@ int32_t rpgb_matrix_upload(int32_t device, uint32_t type, int64_t rows, int64_t 
     RPGB_CHECK(bytes != nullptr, "matrix bytes are NULL");
     RPGB_CHECK(rows > 0 && cols > 0 && cols % 256 == 0 && rows < (1 << 30), "bad matrix shape %lld x %lld",
                static_cast<long long>(rows), static_cast<long long>(cols));
-    // storage holds whole 32-row groups; padding rows are zero blocks
-    const int64_t prow = (rows + 31) / 32 * 32;
-    size_t qb, sb, db;
-    DevMatBytes(type, prow, cols, &qb, &sb, &db);
+    // storage holds whole 16-row tiles; padding rows are zero blocks
+    const int64_t prow = (rows + kTileRows - 1) / kTileRows * kTileRows;
+    const size_t bytes_dev = DevMatBytes(type, prow, cols);
     auto e = std::make_shared<MatrixEntry>();
     e->rows = rows;
     e->device = device;
@@ -244,23 +262,18 @@ int32_t rpgb_matrix_upload(int32_t device, uint32_t type, int64_t rows, int64_t 
     RPGB_CUDA(cudaDeviceGetAttribute(&e->num_sms, cudaDevAttrMultiProcessorCount, device));
     PrepareMatvecKernels();
     PrepareSampleKernels();
-    const size_t qa = (qb + 255) / 256 * 256, sa = (sb + 255) / 256 * 256;
     const int64_t rb = GgmlRowBytes(type, cols);
     std::vector<uint8_t> src(static_cast<size_t>(prow * rb), 0);
     std::memcpy(src.data(), bytes, static_cast<size_t>(rows * rb));
-    std::vector<uint8_t> host(qa + sa + db + 256, 0);
-    RepackRows(type, src.data(), prow, cols, host.data(), host.data() + qa,
-               db ? reinterpret_cast<uint16_t*>(host.data() + qa + sa) : nullptr);
+    std::vector<uint8_t> host(bytes_dev, 0);
+    RepackRows(type, src.data(), prow, cols, host.data());
     RPGB_CUDA(cudaMalloc(&e->mem, host.size()));
     RPGB_CUDA(cudaMemcpy(e->mem, host.data(), host.size(), cudaMemcpyHostToDevice));
-    uint8_t* base = static_cast<uint8_t*>(e->mem);
     e->m.type = type;
     e->m.rows = static_cast<int32_t>(prow);
     e->m.cols = static_cast<int32_t>(cols);
     e->m.nb = static_cast<int32_t>(cols / 256);
-    e->m.q = base;
-    e->m.s = base + qa;
-    e->m.d = db ? reinterpret_cast<const uint16_t*>(base + qa + sa) : nullptr;
+    e->m.q = static_cast<uint8_t*>(e->mem);
     std::lock_guard<std::mutex> lk(g_mu);
     const int32_t h = g_next++;
     g_mats[h] = e;
@@ -306,8 +319,8 @@ int32_t rpgb_matrix_matvec(int32_t matrix, const float* x_dev, int64_t n_tok, fl
     RPGB_CHECK(n_tok > 0 && n_tok < (1 << 24), "bad token count");
     RPGB_CUDA(cudaSetDevice(e->device));
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
-    RPGB_CHECK(e->rows % 32 == 0, "matvec: %lld rows; the kernels need a multiple of 32 rows",
-               static_cast<long long>(e->rows));
+    RPGB_CHECK(e->rows % kTileRows == 0, "matvec: %lld rows; the kernels need a multiple of %d rows",
+               static_cast<long long>(e->rows), kTileRows);
     if (n_tok == 1) {
       MvParams p;
       p.seg[0].w = e->m;

@@ -116,6 +116,8 @@ Session::~Session() {
   cudaFree(vc_);
   cudaFree(dec_arena_);
   cudaFree(pf_arena_);
+  cudaFree(trace_rec_);
+  cudaFree(trace_count_);
   if (host_ids_ != nullptr) cudaFreeHost(host_ids_);
   if (stream_ != nullptr) cudaStreamDestroy(stream_);
 }
@@ -125,6 +127,36 @@ void Session::DropGraph() {
     cudaGraphExecDestroy(graph_);
     graph_ = nullptr;
   }
+}
+
+void Session::EnableTrace(int32_t cap) {
+  RPGB_CHECK(cap >= 0 && cap <= (1 << 24), "trace capacity %d out of range", cap);
+  RPGB_CUDA(cudaSetDevice(m_->device()));
+  RPGB_CUDA(cudaStreamSynchronize(stream_));
+  DropGraph();
+  cudaFree(trace_rec_);
+  cudaFree(trace_count_);
+  trace_rec_ = nullptr;
+  trace_count_ = nullptr;
+  trace_cap_ = 0;
+  if (cap == 0) return;
+  RPGB_CUDA(cudaMalloc(&trace_rec_, sizeof(TraceRec) * static_cast<size_t>(cap)));
+  RPGB_CUDA(cudaMalloc(&trace_count_, sizeof(uint32_t)));
+  RPGB_CUDA(cudaMemset(trace_count_, 0, sizeof(uint32_t)));
+  trace_cap_ = static_cast<uint32_t>(cap);
+}
+
+int32_t Session::TakeTrace(TraceRec* out, int32_t cap) {
+  if (trace_rec_ == nullptr) return 0;
+  RPGB_CUDA(cudaSetDevice(m_->device()));
+  RPGB_CUDA(cudaStreamSynchronize(stream_));
+  uint32_t n = 0;
+  RPGB_CUDA(cudaMemcpy(&n, trace_count_, sizeof(uint32_t), cudaMemcpyDeviceToHost));
+  n = std::min<uint32_t>(n, trace_cap_);
+  const uint32_t m = std::min<uint32_t>(n, static_cast<uint32_t>(std::max(cap, 0)));
+  if (m > 0) RPGB_CUDA(cudaMemcpy(out, trace_rec_, sizeof(TraceRec) * m, cudaMemcpyDeviceToHost));
+  RPGB_CUDA(cudaMemset(trace_count_, 0, sizeof(uint32_t)));
+  return static_cast<int32_t>(m);
 }
 
 void Session::SetLen(int64_t n) {
@@ -267,7 +299,7 @@ void Session::Prefill(const int32_t* tokens, int64_t n, float* last_logits) {
   logits_valid_ = true;
 }
 
-void Session::EnqueueSample(const SampleOpts& opt, uint64_t seed, int pos_bump, bool pdl) {
+void Session::EnqueueSample(const SampleOpts& opt, uint64_t seed, int pos_bump, bool pdl, int32_t trace_id) {
   const ModelMeta& c = m_->meta();
   SampleParams sp;
   sp.logits = logits_;
@@ -284,6 +316,7 @@ void Session::EnqueueSample(const SampleOpts& opt, uint64_t seed, int pos_bump, 
   sp.cand_idx = cand_idx_;
   sp.cand_cnt = cand_cnt_;
   sp.flag = flag_;
+  if (trace_id >= 0) sp.trace = NextTrace(&trace_id);
   LaunchSample(sp, false, stream_, pdl);
 }
 
@@ -293,7 +326,8 @@ void Session::EnqueueStep(const SampleOpts& opt, uint64_t seed) {
   const int H = c.hidden, qd = c.q_dim(), kvd = c.kv_dim();
   const int sms = m_->num_sms();
   int launches = 0;
-  LaunchEmbed(m_->embd(), tok_, 1, x_, pos_, out_ids_, s);
+  int32_t tid = 0;  // trace id of the next launch
+  LaunchEmbed(m_->embd(), tok_, 1, x_, pos_, out_ids_, s, false, NextTrace(&tid));
   ++launches;
   for (int l = 0; l < c.n_layers; ++l) {
     const DevLayer& L = m_->layers()[static_cast<size_t>(l)];
@@ -311,6 +345,7 @@ void Session::EnqueueStep(const SampleOpts& opt, uint64_t seed) {
     q.eps = c.rms_eps;
     q.out = qkv_;
     q.err = err_;
+    q.trace = NextTrace(&tid);
     LaunchMatvec(q, Epi::kStore, 2, sms, s, true);
 
     AttnParams a;
@@ -334,6 +369,7 @@ void Session::EnqueueStep(const SampleOpts& opt, uint64_t seed) {
     a.ticket = tickets_;
     a.n_splits = n_splits_;
     a.fused = 1;
+    a.trace = NextTrace(&tid);
     LaunchAttention(a, 1, s, true);
 
     MvParams o;
@@ -343,6 +379,7 @@ void Session::EnqueueStep(const SampleOpts& opt, uint64_t seed) {
     o.out = x_;
     o.resid = x_;
     o.err = err_;
+    o.trace = NextTrace(&tid);
     LaunchMatvec(o, Epi::kResid, 1, sms, s, true);
 
     MvParams gu;
@@ -353,6 +390,7 @@ void Session::EnqueueStep(const SampleOpts& opt, uint64_t seed) {
     gu.eps = c.rms_eps;
     gu.out = h_;
     gu.err = err_;
+    gu.trace = NextTrace(&tid);
     LaunchMatvec(gu, Epi::kSilu, 2, sms, s, true);
 
     MvParams dn;
@@ -362,6 +400,7 @@ void Session::EnqueueStep(const SampleOpts& opt, uint64_t seed) {
     dn.out = x_;
     dn.resid = x_;
     dn.err = err_;
+    dn.trace = NextTrace(&tid);
     LaunchMatvec(dn, Epi::kResid, 1, sms, s, true);
     launches += 5;
   }
@@ -373,6 +412,7 @@ void Session::EnqueueStep(const SampleOpts& opt, uint64_t seed) {
   lm.eps = c.rms_eps;
   lm.out = logits_;
   lm.err = err_;
+  lm.trace = NextTrace(&tid);
   if (!(opt.temperature > 0.0f)) {
     lm.part_val = am_val_;
     lm.part_idx = am_idx_;
@@ -384,7 +424,7 @@ void Session::EnqueueStep(const SampleOpts& opt, uint64_t seed) {
     launches += 1;
   } else {
     LaunchMatvec(lm, Epi::kStore, 4, sms, s, true);
-    EnqueueSample(opt, seed, 1, true);
+    EnqueueSample(opt, seed, 1, true, trace_rec_ != nullptr ? tid : -1);
     const bool fast = opt.top_k > 1 && opt.top_k <= kFastTopK && opt.top_k < c.vocab;
     launches += fast ? 4 : 2;
   }

@@ -60,9 +60,16 @@ class Session {
   bool graph_ready() const { return graph_ != nullptr; }
   int kernels_per_step() const { return kernels_per_step_; }
 
+  // Device timeline of the decode-step launches (see Trace in kernels.h).
+  // EnableTrace(cap) allocates room for `cap` records and re-records the step
+  // graph with tracing on (cap 0 turns it off); TakeTrace copies the records
+  // gathered so far and clears them.
+  void EnableTrace(int32_t cap);
+  int32_t TakeTrace(TraceRec* out, int32_t cap);
+
  private:
   void EnqueueStep(const SampleOpts& opt, uint64_t seed);
-  void EnqueueSample(const SampleOpts& opt, uint64_t seed, int pos_bump, bool pdl = false);
+  void EnqueueSample(const SampleOpts& opt, uint64_t seed, int pos_bump, bool pdl = false, int32_t trace_id = -1);
   void EnsurePrefill(int64_t n);
   void DropGraph();
 
@@ -109,6 +116,21 @@ class Session {
   uint64_t graph_seed_ = 0;
   int graph_launches_ = 0;
   int kernels_per_step_ = 0;
+
+  // timeline trace (off unless EnableTrace)
+  TraceRec* trace_rec_ = nullptr;
+  uint32_t* trace_count_ = nullptr;
+  uint32_t trace_cap_ = 0;
+  Trace NextTrace(int32_t* id) const {
+    Trace t;
+    if (trace_rec_ != nullptr) {
+      t.rec = trace_rec_;
+      t.count = trace_count_;
+      t.cap = trace_cap_;
+      t.id = (*id)++;
+    }
+    return t;
+  }
 };
 
 }  // namespace rpgb

@@ -93,6 +93,7 @@ __global__ void __launch_bounds__(128) AttnKernel(const AttnParams p) {
   __shared__ float fsh[4 * G];
   __shared__ int s_last;
 
+  dev::TraceScope trace(p.trace);
   const int s = blockIdx.x, h = blockIdx.y, t = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   // The position counter of this step was written before the step started
@@ -118,6 +119,7 @@ __global__ void __launch_bounds__(128) AttnKernel(const AttnParams p) {
   }
   dev::GridLaunchDependents();
   dev::GridWait();
+  trace.Ready();
 
   // ---- the G query vectors of this group
   {

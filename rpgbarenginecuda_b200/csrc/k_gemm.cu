@@ -37,15 +37,19 @@ __global__ void __launch_bounds__(256) GemmKernel(const GemmParams p) {
   for (int kb = 0; kb < K / BK; ++kb) {
     float wv[8], xv[8];
     const int b = kb >> 3;
+    const uint8_t* grp = dev::GroupPtr(w, row, b);
+    const int r16 = static_cast<int>(row & 15), g = r16 & 7, rs = r16 >> 3;
     if (w.type == 12u) {
       const int j = kb & 7;
-      const uint4 hd = *reinterpret_cast<const uint4*>(w.s + dev::SByte(w, row, b));
+      const uint4 hd = *reinterpret_cast<const uint4*>(grp + 2048 + 16 * r16);
       int sc, m;
       dev::Q4kScaleMin(hd.y, hd.z, hd.w, j, &sc, &m);
       const float d1 = __fmul_rn(dev::Half(hd.x & 0xFFFFu), static_cast<float>(sc));
       const float m1 = __fmul_rn(dev::Half(hd.x >> 16), static_cast<float>(m));
-      const uint2 qb = *reinterpret_cast<const uint2*>(w.q + dev::QByte(w, row, b, 32 * (j >> 1) + lk));
-      const uint32_t qw[2] = {qb.x, qb.y};
+      // positions lk .. lk+7 of sub-block j: words of lanes (g, t0) and (g, t0 + 1)
+      const int c = j >> 1, h = lk >> 4, t0 = (lk >> 2) & 3;
+      const uint32_t* wp = reinterpret_cast<const uint32_t*>(grp + (c * 32 + 4 * g + t0) * 16 + (2 * h + rs) * 4);
+      const uint32_t qw[2] = {wp[0], wp[4]};
       const int sh = (j & 1) * 4;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -53,20 +57,31 @@ __global__ void __launch_bounds__(256) GemmKernel(const GemmParams p) {
         wv[i] = __fsub_rn(__fmul_rn(d1, static_cast<float>(q)), m1);
       }
     } else {
-      const int e0 = (kb & 7) * 32 + lk;
-      const int hh = e0 >> 7, r = e0 & 127, quarter = r >> 5, l0 = r & 31;
-      const uint2 qlb =
-          *reinterpret_cast<const uint2*>(w.q + dev::QByte(w, row, b, hh * 64 + l0 + ((quarter & 1) ? 32 : 0)));
-      const uint2 qhb = *reinterpret_cast<const uint2*>(w.q + dev::QByte(w, row, b, 128 + hh * 32 + l0));
-      const int8_t sc = static_cast<int8_t>(w.s[dev::SByte(w, row, b) + hh * 8 + (l0 >> 4) + 2 * quarter]);
-      const float ds = __fmul_rn(dev::Half(w.d[dev::DIndex(w, row, b)]), static_cast<float>(sc));
-      const uint32_t ql[2] = {qlb.x, qlb.y}, qh[2] = {qhb.x, qhb.y};
-      const int nsh = quarter < 2 ? 0 : 4;
+      // Q6_K sub-block j16 = 2 (kb & 7) + (lk >> 4), positions (lk & 15) .. +7
+      const int j16 = 2 * (kb & 7) + (lk >> 4);
+      const int8_t sc = static_cast<int8_t>(grp[3072 + 16 * r16 + j16]);
+      const float dd = dev::Half(*reinterpret_cast<const uint16_t*>(grp + 3328 + 2 * (2 * g + rs)));
+      const float ds = __fmul_rn(dd, static_cast<float>(sc));
+      const int c = j16 >> 2, h = j16 & 1, hb = (j16 >> 1) & 1, m = 2 * c + h;
+      const int t0 = (lk & 15) >> 2;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int nib = static_cast<int>((ql[i >> 2] >> (8 * (i & 3) + nsh)) & 15u);
-        const int hi = static_cast<int>((qh[i >> 2] >> (8 * (i & 3) + 2 * quarter)) & 3u);
-        wv[i] = __fmul_rn(ds, static_cast<float>((nib | (hi << 4)) - 32));
+      for (int tt = 0; tt < 2; ++tt) {
+        const uint32_t* wq =
+            reinterpret_cast<const uint32_t*>(grp + ((m >> 2) * 32 + 4 * g + t0 + tt) * 48 + (m & 3) * 12);
+        const uint32_t X = wq[0], Y = wq[1], Z = wq[2];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          int q;
+          if (hb == 0) {
+            q = static_cast<int>(((rs == 0 ? X : Y) >> (8 * e)) & 63u);
+          } else if (rs == 0) {
+            q = static_cast<int>((Z >> (8 * e)) & 63u);
+          } else {
+            q = static_cast<int>(((X >> (8 * e + 6)) & 3u) | (((Y >> (8 * e + 6)) & 3u) << 2) |
+                                 (((Z >> (8 * e + 6)) & 3u) << 4));
+          }
+          wv[4 * tt + e] = __fmul_rn(ds, static_cast<float>(q - 32));
+        }
       }
     }
     if (tok < p.n_tok) {

@@ -5,20 +5,36 @@
 // GpuForwardLayer (src/qwen3_gpu.cu:47-109): one launch computes
 // prologue(x) -> W x -> epilogue.
 //
-// Structure (one persistent block per SM, 8 warps):
-//  * the block owns a contiguous range of 32-row groups; its weights stream
-//    through a ring of shared-memory slots filled by 1-D TMA bulk copies
-//    (cp.async.bulk + mbarrier), one slot = (group, up to `kb` blocks);
-//  * the first ring slots are requested BEFORE griddepcontrol.wait: with
+// Arithmetic.  A decode matvec streams 4.5-6.6 bits per weight, so at HBM
+// speed an SM has a budget of well under one instruction per weight.  The
+// products therefore run on the integer tensor cores (mma.sync m16n8k32,
+// u8 x s8 -> s32) and stay exact:
+//  * the A operand is the quantised weight itself (Q4_K nibble, or 16x the
+//    nibble for the high half; Q6_K 6-bit value, or 4x it), unpacked from the
+//    block group with one or two logical ops per 4 weights;
+//  * x is split per 256-column super-block into four signed 8-bit digits,
+//    x = s * (x0 + x1/64 + x2/8192 + x3/2^20), s a power of two, which is
+//    exact to 2^-27 of the super-block's largest |x|.  The digits are the
+//    columns of the B operand: columns 0-3 carry the digits of the first 16
+//    positions of an MMA, columns 4-7 those of the next sub-block half, so one
+//    MMA yields two sub-block partial sums;
+//  * integer partial sums are scaled by the 6-bit (Q4_K) or 8-bit (Q6_K)
+//    sub-block scale with IMAD; Q6_K's "-32" offset is a second MMA with a
+//    constant A; d, dmin and the Q4_K min term (dmin*m*sum(x), sums of x per
+//    32 columns precomputed) are applied in FP32 once per super-block.
+// Results differ from the reference's per-element FP32 dequant + FMA only by
+// rounding (relative 1e-7 level); DeqQ4K / DeqQ6K stay the bit-exact path.
+//
+// Data movement (one persistent block of 8 warps per SM):
+//  * the block owns a contiguous range of 16-row tiles; its (tile, super-block)
+//    units are split into 8 contiguous per-warp ranges;
+//  * every warp streams its units through its own ring of shared-memory slots
+//    with 1-D TMA bulk copies (cp.async.bulk + mbarrier, bounded waits);
+//  * the first slots are requested BEFORE griddepcontrol.wait, so with
 //    programmatic dependent launch the weights of this kernel stream in while
-//    the previous kernel of the decode step is still computing;
-//  * lane r of every warp owns row r of the group (row-interleaved layout, see
-//    kernels.cuh), the 8 warps split the block units of a slot, x is read from
-//    shared memory as broadcast float4 loads, and the 8 partial sums of a row
-//    are combined once per group -- no per-row shuffles;
-//  * Q4_K regroups (d*sc)*sum(q*x) - (dmin*m)*sum(x) per 32-element sub-block,
-//    Q6_K (d*sc)*sum((q-32)*x) per 16-element sub-block; the 4- and 6-bit
-//    values become floats exactly via the 2^23 mantissa trick (PRMT + FADD).
+//    the previous kernel of the decode step still runs;
+//  * partial row sums of a warp are combined per tile in shared memory in a
+//    fixed order (results are deterministic), then the epilogue runs.
 #include <algorithm>
 #include <cfloat>
 
@@ -30,287 +46,478 @@
 namespace rpgb {
 namespace {
 
-using dev::kGroupRows;
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kMaxSlots = 8;
+constexpr int kTile = 16;
+constexpr int kMaxRing = 6;
 // Dynamic shared memory budget per block: leaves room for the next kernel's
 // block on the same SM (programmatic launch overlap needs co-residency).
-constexpr size_t kSmemBudget = 110 * 1024;
-constexpr size_t kSmemLimit = kSmemBudget + 8192;
+constexpr size_t kSmemBudget = 108 * 1024;
+constexpr size_t kSmemLimit = 200 * 1024;
 
 struct Layout {
-  size_t ring, xs, sx, red, bars, total;
+  size_t ring, bfrag, sx, sscale, red, sq, bars, total;
 };
 
-__host__ __device__ inline Layout SmemLayout(int K, int slots, int slot_bytes) {
+__host__ __device__ inline Layout SmemLayout(int nb, int ring, int slot_bytes, int max_tiles) {
   Layout l;
   l.ring = 0;
-  l.xs = static_cast<size_t>(slots) * slot_bytes;
-  l.sx = l.xs + static_cast<size_t>(K) * 4;
-  l.red = l.sx + static_cast<size_t>(K / 32) * 4;
-  l.bars = l.red + kWarps * 32 * 4;
-  l.total = l.bars + kMaxSlots * 8;
+  l.bfrag = static_cast<size_t>(kWarps) * ring * slot_bytes;
+  l.sx = l.bfrag + static_cast<size_t>(nb) * 1024;
+  l.sscale = l.sx + static_cast<size_t>(nb) * 32;
+  l.red = l.sscale + static_cast<size_t>(nb) * 4;
+  l.sq = l.red + static_cast<size_t>(max_tiles + kWarps) * kTile * 4;
+  l.sq = (l.sq + 7) & ~static_cast<size_t>(7);
+  l.bars = l.sq + kWarps * 8;
+  l.total = l.bars + static_cast<size_t>(kWarps) * ring * 8;
   return l;
 }
 
-__device__ __forceinline__ int SegOf(const MvParams& p, int row) {
+__device__ __forceinline__ int SegOfTile(const MvParams& p, int tile) {
+  const int row = tile * kTile;
   int si = 0;
   if (p.n_seg > 1 && row >= p.seg[1].out_off) si = 1;
   if (p.n_seg > 2 && row >= p.seg[2].out_off) si = 2;
   return si;
 }
 
-// Issues the bulk copies of stage `st` (group gb + st / n_chunks, chunk st % n_chunks).
-__device__ __forceinline__ void IssueStage(const MvParams& p, int st, int gb, uint8_t* ring, uint64_t* bars) {
-  const int g = gb + st / p.n_chunks, c = st % p.n_chunks;
-  const int si = SegOf(p, g * kGroupRows);
+// Source of the units a warp requests, advanced one unit at a time.
+struct IssueCursor {
+  const uint8_t* src;
+  uint32_t bytes;
+  int tile, b, seg_end_tile;
+};
+
+__device__ __forceinline__ void CursorSeek(const MvParams& p, int tile, int b, int nb, IssueCursor& c) {
+  const int si = SegOfTile(p, tile);
   const DevMat& w = p.seg[si].w;
-  const int lg = g - p.seg[si].out_off / kGroupRows;
-  const int nb = w.nb, b0 = c * p.kb, kbn = min(p.kb, nb - b0);
-  const int nc = dev::QChunks(w.type);
-  const uint32_t qb = static_cast<uint32_t>(kbn * nc * 512), sb = static_cast<uint32_t>(kbn * 512);
-  const uint32_t db = w.type == 14u ? static_cast<uint32_t>(kbn * 64) : 0u;
-  const int slot = st % p.slots;
-  uint8_t* dst = ring + static_cast<size_t>(slot) * p.slot_bytes;
-  uint64_t* bar = bars + slot;
-  const int64_t gblk = static_cast<int64_t>(lg) * nb + b0;
-  dev::MbarExpectTx(bar, qb + sb + db);
-  dev::BulkG2S(dst, w.q + gblk * nc * 512, qb, bar);
-  dev::BulkG2S(dst + p.kb * nc * 512, w.s + gblk * 512, sb, bar);
-  if (db) dev::BulkG2S(dst + p.kb * nc * 512 + p.kb * 512, w.d + gblk * 32, db, bar);
+  const int t0 = p.seg[si].out_off / kTile;
+  c.bytes = static_cast<uint32_t>(dev::GroupBytesOf(w.type));
+  c.src = w.q + (static_cast<int64_t>(tile - t0) * nb + b) * c.bytes;
+  c.tile = tile;
+  c.b = b;
+  c.seg_end_tile = t0 + w.rows / kTile;
 }
 
-// One 64-weight Q4_K unit (block bl of the slot, qs bytes [32j, 32j+32)) for the lane's row.
-__device__ __forceinline__ float UnitQ4K(const uint8_t* slot, int kb, int bl, int j, int lane,
-                                         const float* __restrict__ xs, const float* __restrict__ sx, int b) {
-  const uint4 q0 = *reinterpret_cast<const uint4*>(slot + (bl * 8 + 2 * j) * 512 + lane * 16);
-  const uint4 q1 = *reinterpret_cast<const uint4*>(slot + (bl * 8 + 2 * j + 1) * 512 + lane * 16);
-  const uint4 hd = *reinterpret_cast<const uint4*>(slot + kb * 8 * 512 + bl * 512 + lane * 16);
-  const float4* xp = reinterpret_cast<const float4*>(xs + b * 256 + 64 * j);
-  const uint32_t wd[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-  float sa = 0.f, sb = 0.f;
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const uint32_t lo = wd[k] & 0x0F0F0F0Fu;
-    const uint32_t hi = (wd[k] >> 4) & 0x0F0F0F0Fu;
-    const float4 a = xp[k], c = xp[8 + k];
-    sa = fmaf(dev::ByteBiased<0>(lo) - 8388608.f, a.x, sa);
-    sb = fmaf(dev::ByteBiased<0>(hi) - 8388608.f, c.x, sb);
-    sa = fmaf(dev::ByteBiased<1>(lo) - 8388608.f, a.y, sa);
-    sb = fmaf(dev::ByteBiased<1>(hi) - 8388608.f, c.y, sb);
-    sa = fmaf(dev::ByteBiased<2>(lo) - 8388608.f, a.z, sa);
-    sb = fmaf(dev::ByteBiased<2>(hi) - 8388608.f, c.z, sb);
-    sa = fmaf(dev::ByteBiased<3>(lo) - 8388608.f, a.w, sa);
-    sb = fmaf(dev::ByteBiased<3>(hi) - 8388608.f, c.w, sb);
+__device__ __forceinline__ void IssueNext(const MvParams& p, int nb, IssueCursor& c, uint8_t* dst, uint64_t* bar) {
+  dev::MbarExpectTx(bar, c.bytes);
+  dev::BulkG2S(dst, c.src, c.bytes, bar);
+  // block groups of one segment are contiguous in tile-major order
+  c.src += c.bytes;
+  if (++c.b == nb) {
+    c.b = 0;
+    if (++c.tile == c.seg_end_tile) CursorSeek(p, c.tile, 0, nb, c);
   }
-  int sca, ma, scb, mb;
-  dev::Q4kScaleMin(hd.y, hd.z, hd.w, 2 * j, &sca, &ma);
-  dev::Q4kScaleMin(hd.y, hd.z, hd.w, 2 * j + 1, &scb, &mb);
-  const float d = dev::Half(hd.x & 0xFFFFu), dmin = dev::Half(hd.x >> 16);
-  const float da = d * static_cast<float>(sca), db = d * static_cast<float>(scb);
-  const float ma_f = dmin * static_cast<float>(ma), mb_f = dmin * static_cast<float>(mb);
-  return da * sa + db * sb - (ma_f * sx[b * 8 + 2 * j] + mb_f * sx[b * 8 + 2 * j + 1]);
 }
 
-// One 64-weight Q6_K unit (block bl, half hh, 16-run bb) for the lane's row.
-__device__ __forceinline__ float UnitQ6K(const uint8_t* slot, int kb, int bl, int hh, int bb, int lane,
-                                         const float* __restrict__ xs, int b) {
-  const uint8_t* qp = slot + bl * 12 * 512 + lane * 16;
-  const uint4 A = *reinterpret_cast<const uint4*>(qp + (4 * hh + bb) * 512);
-  const uint4 B = *reinterpret_cast<const uint4*>(qp + (4 * hh + 2 + bb) * 512);
-  const uint4 H = *reinterpret_cast<const uint4*>(qp + (8 + 2 * hh + bb) * 512);
-  const uint4 S = *reinterpret_cast<const uint4*>(slot + kb * 12 * 512 + bl * 512 + lane * 16);
-  const uint16_t dh = *reinterpret_cast<const uint16_t*>(slot + kb * 12 * 512 + kb * 512 + bl * 64 + lane * 2);
-  const float* xb = xs + b * 256 + 128 * hh + 16 * bb;
-  const uint32_t Aw[4] = {A.x, A.y, A.z, A.w};
-  const uint32_t Bw[4] = {B.x, B.y, B.z, B.w};
-  const uint32_t Hw[4] = {H.x, H.y, H.z, H.w};
-  float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const uint32_t u0 = (Aw[k] & 0x0F0F0F0Fu) | ((Hw[k] << 4) & 0x30303030u);
-    const uint32_t u1 = (Bw[k] & 0x0F0F0F0Fu) | ((Hw[k] << 2) & 0x30303030u);
-    const uint32_t u2 = ((Aw[k] >> 4) & 0x0F0F0F0Fu) | (Hw[k] & 0x30303030u);
-    const uint32_t u3 = ((Bw[k] >> 4) & 0x0F0F0F0Fu) | ((Hw[k] >> 2) & 0x30303030u);
-    const float4 x0 = reinterpret_cast<const float4*>(xb)[k];
-    const float4 x1 = reinterpret_cast<const float4*>(xb + 32)[k];
-    const float4 x2 = reinterpret_cast<const float4*>(xb + 64)[k];
-    const float4 x3 = reinterpret_cast<const float4*>(xb + 96)[k];
-    // 8388640 = 2^23 + 32 turns the 6-bit value into (q - 32).
-    t0 = fmaf(dev::ByteBiased<0>(u0) - 8388640.f, x0.x, t0);
-    t1 = fmaf(dev::ByteBiased<0>(u1) - 8388640.f, x1.x, t1);
-    t2 = fmaf(dev::ByteBiased<0>(u2) - 8388640.f, x2.x, t2);
-    t3 = fmaf(dev::ByteBiased<0>(u3) - 8388640.f, x3.x, t3);
-    t0 = fmaf(dev::ByteBiased<1>(u0) - 8388640.f, x0.y, t0);
-    t1 = fmaf(dev::ByteBiased<1>(u1) - 8388640.f, x1.y, t1);
-    t2 = fmaf(dev::ByteBiased<1>(u2) - 8388640.f, x2.y, t2);
-    t3 = fmaf(dev::ByteBiased<1>(u3) - 8388640.f, x3.y, t3);
-    t0 = fmaf(dev::ByteBiased<2>(u0) - 8388640.f, x0.z, t0);
-    t1 = fmaf(dev::ByteBiased<2>(u1) - 8388640.f, x1.z, t1);
-    t2 = fmaf(dev::ByteBiased<2>(u2) - 8388640.f, x2.z, t2);
-    t3 = fmaf(dev::ByteBiased<2>(u3) - 8388640.f, x3.z, t3);
-    t0 = fmaf(dev::ByteBiased<3>(u0) - 8388640.f, x0.w, t0);
-    t1 = fmaf(dev::ByteBiased<3>(u1) - 8388640.f, x1.w, t1);
-    t2 = fmaf(dev::ByteBiased<3>(u2) - 8388640.f, x2.w, t2);
-    t3 = fmaf(dev::ByteBiased<3>(u3) - 8388640.f, x3.w, t3);
+__device__ __forceinline__ uint4 Lds128(const void* p) { return *reinterpret_cast<const uint4*>(p); }
+
+// Predicated 16-byte shared load into four loop-carried registers (registers
+// of lanes with pred == 0 keep their value).
+__device__ __forceinline__ void Lds128If(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3, uint32_t pred,
+                                         uint32_t saddr) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.u32 p, %4, 0;\n"
+      "  @p ld.shared.v4.u32 {%0,%1,%2,%3}, [%5]; }"
+      : "+r"(r0), "+r"(r1), "+r"(r2), "+r"(r3)
+      : "r"(pred), "r"(saddr));
+}
+
+__device__ __forceinline__ void MmaU8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                      uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void MmaS8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                      uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// PRMT in its default mode: selector nibble bits 0-2 pick a byte of {b, a},
+// bit 3 replicates that byte's sign (the __byte_perm intrinsic masks bit 3
+// away, so signed extraction needs the instruction itself).
+__device__ __forceinline__ uint32_t Prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+__device__ __forceinline__ int ByteU(uint32_t w, uint32_t sel) { return static_cast<int>(Prmt(w, 0u, sel)); }
+
+// Per-lane constants of the fragment geometry.
+struct LaneK {
+  int g, tig, p;
+  uint32_t sel_q4[2];  // Q4_K scale byte of sub-block 2c + p inside SC_lo / SC_hi (c & 1 = 0, 1)
+  uint32_t sel_m[2];   // Q4_K min bytes of sub-blocks 2 tig, 2 tig + 1
+  uint32_t sel_q6[2];  // Q6_K signed scale byte h + 2p of word c (h = 0, 1), sign-extended
+  float w4[2];         // Q4_K digit weights of the lane's two columns (1/16 for the high nibble half)
+  float w6g[2], w6g8[2];  // Q6_K digit weights for rows g and g + 8 (1/4 for a3)
+};
+
+__device__ __forceinline__ LaneK MakeLane(int lane) {
+  LaneK k;
+  k.g = lane >> 2;
+  k.tig = lane & 3;
+  k.p = k.tig >> 1;
+  for (int c = 0; c < 2; ++c) k.sel_q4[c] = 0x4440u | static_cast<uint32_t>(2 * c + k.p);
+  k.sel_m[0] = 0x4440u | static_cast<uint32_t>(2 * (k.tig & 1));
+  k.sel_m[1] = 0x4440u | static_cast<uint32_t>(2 * (k.tig & 1) + 1);
+  for (int h = 0; h < 2; ++h) {
+    const uint32_t b = static_cast<uint32_t>(h + 2 * k.p), s = b | 8u;
+    k.sel_q6[h] = b | (s << 4) | (s << 8) | (s << 12);
   }
-  const float d = dev::Half(dh);
-  const int si = 8 * hh + bb;
-  return (d * static_cast<float>(dev::Q6kScale(S, si))) * t0 + (d * static_cast<float>(dev::Q6kScale(S, si + 2))) * t1 +
-         (d * static_cast<float>(dev::Q6kScale(S, si + 4))) * t2 +
-         (d * static_cast<float>(dev::Q6kScale(S, si + 6))) * t3;
+  const float w0 = (k.tig & 1) ? 1.0f / 8192.0f : 1.0f;
+  const float w1 = (k.tig & 1) ? 1.0f / 1048576.0f : 1.0f / 64.0f;
+  const float f4 = k.p ? 1.0f / 16.0f : 1.0f;
+  const float f6 = k.p ? 0.25f : 1.0f;
+  k.w4[0] = w0 * f4;
+  k.w4[1] = w1 * f4;
+  k.w6g[0] = w0;
+  k.w6g[1] = w1;
+  k.w6g8[0] = w0 * f6;
+  k.w6g8[1] = w1 * f6;
+  return k;
+}
+
+// One Q4_K (tile, super-block) unit: adds the lane's share of rows g, g + 8.
+__device__ __forceinline__ void UnitQ4K(const uint8_t* grp, const uint32_t (&bA)[8], const uint32_t (&bB)[8],
+                                        const float* sx, float s, const LaneK& k, int lane, float& rg, float& rg8) {
+  const uint4 R0 = Lds128(grp + 2048 + 16 * k.g);
+  const uint4 R1 = Lds128(grp + 2048 + 16 * (k.g + 8));
+  const uint32_t sclo0 = R0.y & 0x3F3F3F3Fu, sclo1 = R1.y & 0x3F3F3F3Fu;
+  const uint32_t schi0 = (R0.w & 0x0F0F0F0Fu) | ((R0.y >> 2) & 0x30303030u);
+  const uint32_t schi1 = (R1.w & 0x0F0F0F0Fu) | ((R1.y >> 2) & 0x30303030u);
+  int acc[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const uint4 W = Lds128(grp + (c * 32 + lane) * 16);
+    int d[4] = {0, 0, 0, 0};
+    MmaU8(d, W.x & 0x0F0F0F0Fu, W.y & 0x0F0F0F0Fu, W.x & 0xF0F0F0F0u, W.y & 0xF0F0F0F0u, bA[2 * c], bB[2 * c]);
+    MmaU8(d, W.z & 0x0F0F0F0Fu, W.w & 0x0F0F0F0Fu, W.z & 0xF0F0F0F0u, W.w & 0xF0F0F0F0u, bA[2 * c + 1],
+          bB[2 * c + 1]);
+    const int s0 = ByteU(c < 2 ? sclo0 : schi0, k.sel_q4[c & 1]);
+    const int s1 = ByteU(c < 2 ? sclo1 : schi1, k.sel_q4[c & 1]);
+    acc[0] += s0 * d[0];
+    acc[1] += s0 * d[1];
+    acc[2] += s1 * d[2];
+    acc[3] += s1 * d[3];
+  }
+  // min term of sub-blocks 2 tig and 2 tig + 1
+  const uint32_t mlo0 = R0.z & 0x3F3F3F3Fu, mlo1 = R1.z & 0x3F3F3F3Fu;
+  const uint32_t mhi0 = ((R0.w >> 4) & 0x0F0F0F0Fu) | ((R0.z >> 2) & 0x30303030u);
+  const uint32_t mhi1 = ((R1.w >> 4) & 0x0F0F0F0Fu) | ((R1.z >> 2) & 0x30303030u);
+  const uint32_t m0 = k.p ? mhi0 : mlo0, m1 = k.p ? mhi1 : mlo1;
+  const float2 sxv = *reinterpret_cast<const float2*>(sx + 2 * k.tig);
+  const float mn0 =
+      static_cast<float>(ByteU(m0, k.sel_m[0])) * sxv.x + static_cast<float>(ByteU(m0, k.sel_m[1])) * sxv.y;
+  const float mn1 =
+      static_cast<float>(ByteU(m1, k.sel_m[0])) * sxv.x + static_cast<float>(ByteU(m1, k.sel_m[1])) * sxv.y;
+  const float d0 = dev::Half(R0.x & 0xFFFFu), dm0 = dev::Half(R0.x >> 16);
+  const float d1 = dev::Half(R1.x & 0xFFFFu), dm1 = dev::Half(R1.x >> 16);
+  const float f0 = s * k.w4[0], f1 = s * k.w4[1];
+  rg += d0 * (static_cast<float>(acc[0]) * f0 + static_cast<float>(acc[1]) * f1) - dm0 * mn0;
+  rg8 += d1 * (static_cast<float>(acc[2]) * f0 + static_cast<float>(acc[3]) * f1) - dm1 * mn1;
+}
+
+// One Q6_K (tile, super-block) unit.
+__device__ __forceinline__ void UnitQ6K(const uint8_t* grp, const uint32_t (&bA)[8], const uint32_t (&bB)[8], float s,
+                                        const LaneK& k, int lane, float& rg, float& rg8) {
+  const uint4 S0 = Lds128(grp + 3072 + 16 * k.g);
+  const uint4 S1 = Lds128(grp + 3072 + 16 * (k.g + 8));
+  const uint32_t dd = *reinterpret_cast<const uint32_t*>(grp + 3328 + 4 * k.g);
+  const uint32_t s0w[4] = {S0.x, S0.y, S0.z, S0.w}, s1w[4] = {S1.x, S1.y, S1.z, S1.w};
+  int acc[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const uint8_t* base = grp + (q * 32 + lane) * 48;
+    const uint4 V0 = Lds128(base), V1 = Lds128(base + 16), V2 = Lds128(base + 32);
+    const uint32_t v[12] = {V0.x, V0.y, V0.z, V0.w, V1.x, V1.y, V1.z, V1.w, V2.x, V2.y, V2.z, V2.w};
+#pragma unroll
+    for (int mm = 0; mm < 4; ++mm) {
+      const int m = 4 * q + mm, c = m >> 1, h = m & 1;
+      const uint32_t X = v[3 * mm], Y = v[3 * mm + 1], Z = v[3 * mm + 2];
+      const uint32_t a0 = X & 0x3F3F3F3Fu, a1 = Y & 0x3F3F3F3Fu, a2 = Z & 0x3F3F3F3Fu;
+      const uint32_t a3 = ((X >> 4) & 0x0C0C0C0Cu) | ((Y >> 2) & 0x30303030u) | (Z & 0xC0C0C0C0u);
+      int d[4] = {0, 0, 0, 0};
+      // -32 per weight (x4 for the a3 quarter): d = -32 * sum(B) first
+      MmaS8(d, 0xE0E0E0E0u, 0xE0E0E0E0u, 0xE0E0E0E0u, 0x80808080u, bA[m], bB[m]);
+      MmaU8(d, a0, a1, a2, a3, bA[m], bB[m]);
+      const int sc0 = static_cast<int>(Prmt(s0w[c], 0u, k.sel_q6[h]));
+      const int sc1 = static_cast<int>(Prmt(s1w[c], 0u, k.sel_q6[h]));
+      acc[0] += sc0 * d[0];
+      acc[1] += sc0 * d[1];
+      acc[2] += sc1 * d[2];
+      acc[3] += sc1 * d[3];
+    }
+  }
+  const float dg = dev::Half(dd & 0xFFFFu), dg8 = dev::Half(dd >> 16);
+  rg += dg * s * (static_cast<float>(acc[0]) * k.w6g[0] + static_cast<float>(acc[1]) * k.w6g[1]);
+  rg8 += dg8 * s * (static_cast<float>(acc[2]) * k.w6g8[0] + static_cast<float>(acc[3]) * k.w6g8[1]);
+}
+
+__device__ __forceinline__ void FlushPiece(float* red, int piece, const LaneK& k, float& rg, float& rg8) {
+  rg += __shfl_xor_sync(0xFFFFFFFFu, rg, 1);
+  rg += __shfl_xor_sync(0xFFFFFFFFu, rg, 2);
+  rg8 += __shfl_xor_sync(0xFFFFFFFFu, rg8, 1);
+  rg8 += __shfl_xor_sync(0xFFFFFFFFu, rg8, 2);
+  if (k.tig == 0) {
+    red[piece * kTile + k.g] = rg;
+    red[piece * kTile + k.g + 8] = rg8;
+  }
+  rg = rg8 = 0.f;
 }
 
 template <bool NORM, int EPI>
-__global__ void __launch_bounds__(kThreads, 1) MatvecKernel(const MvParams p) {
+__global__ void __launch_bounds__(kThreads, 2) MatvecKernel(const MvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ double dred[32];
   __shared__ float s_bv[kWarps];
   __shared__ int s_bi[kWarps];
   __shared__ int s_last;
+  dev::TraceScope trace(p.trace);
 
-  const int K = p.seg[0].w.cols;
-  const Layout L = SmemLayout(K, p.slots, p.slot_bytes);
-  uint8_t* ring = smem + L.ring;
-  float* xs = reinterpret_cast<float*>(smem + L.xs);
+  const int K = p.seg[0].w.cols, nb = K >> 8;
+  const Layout L = SmemLayout(nb, p.ring, p.slot_bytes, p.max_tiles);
+  uint8_t* bfrag = smem + L.bfrag;
   float* sx = reinterpret_cast<float*>(smem + L.sx);
+  float* sscale = reinterpret_cast<float*>(smem + L.sscale);
   float* red = reinterpret_cast<float*>(smem + L.red);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
+  double* sq = reinterpret_cast<double*>(smem + L.sq);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-  const int G = p.n_groups;
-  const int gb = static_cast<int>((static_cast<int64_t>(blockIdx.x) * G) / gridDim.x);
-  const int ge = static_cast<int>((static_cast<int64_t>(blockIdx.x + 1) * G) / gridDim.x);
-  const int n_stages = (ge - gb) * p.n_chunks;
+  const int T = p.n_tiles;
+  const int t0 = static_cast<int>((static_cast<int64_t>(blockIdx.x) * T) / gridDim.x);
+  const int t1 = static_cast<int>((static_cast<int64_t>(blockIdx.x + 1) * T) / gridDim.x);
+  const int U = (t1 - t0) * nb;
+  const int u0 = warp * U / kWarps, u1 = (warp + 1) * U / kWarps;
+  const int n_units = u1 - u0;
+  const int R = p.ring;
+  uint8_t* ring = smem + L.ring + static_cast<size_t>(warp) * R * p.slot_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars) + warp * R;
 
   // ---- weights first: they do not depend on the previous kernel
-  if (tid == 0) {
-    for (int s = 0; s < p.slots; ++s) dev::MbarInit(bars + s, 1);
+  IssueCursor cur;
+  int issued = 0;
+  if (lane == 0) {
+    for (int s = 0; s < R; ++s) dev::MbarInit(bars + s, 1);
     dev::MbarInitFence();
+    if (n_units > 0) {
+      CursorSeek(p, t0 + u0 / nb, u0 % nb, nb, cur);
+      const int pre = n_units < R ? n_units : R;
+      for (; issued < pre; ++issued) IssueNext(p, nb, cur, ring + issued * p.slot_bytes, bars + issued);
+    }
   }
-  __syncthreads();
-  if (tid == 0) {
-    const int pre = n_stages < p.slots ? n_stages : p.slots;
-    for (int st = 0; st < pre; ++st) IssueStage(p, st, gb, ring, bars);
-  }
+  __syncwarp();
   dev::GridLaunchDependents();
   dev::GridWait();
+  trace.Ready();
 
-  // ---- prologue: x (optionally RMSNorm'ed) and 32-element sums
-  double ss = 0.0;
-  for (int i = tid * 4; i < K; i += kThreads * 4) {
-    const float4 v = *reinterpret_cast<const float4*>(p.x + i);
-    *reinterpret_cast<float4*>(xs + i) = v;
+  // ---- prologue: x (times the RMSNorm weight) as 4 signed 8-bit digits per
+  // super-block, laid out as B fragments; 32-column sums for the Q4_K min term.
+  double ssq = 0.0;
+  for (int b = warp; b < nb; b += kWarps) {
+    const float4 xa = *reinterpret_cast<const float4*>(p.x + b * 256 + 8 * lane);
+    const float4 xb = *reinterpret_cast<const float4*>(p.x + b * 256 + 8 * lane + 4);
+    float v[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
     if (NORM) {
-      ss += static_cast<double>(v.x) * v.x;
-      ss += static_cast<double>(v.y) * v.y;
-      ss += static_cast<double>(v.z) * v.z;
-      ss += static_cast<double>(v.w) * v.w;
+      const float4 wa = *reinterpret_cast<const float4*>(p.norm_w + b * 256 + 8 * lane);
+      const float4 wb = *reinterpret_cast<const float4*>(p.norm_w + b * 256 + 8 * lane + 4);
+      const float w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        ssq += static_cast<double>(v[i]) * v[i];
+        v[i] *= w[i];
+      }
     }
+    float mx = 0.f, su = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      mx = fmaxf(mx, fabsf(v[i]));
+      su += v[i];
+    }
+    mx = dev::WarpMax(mx);
+    const int E = static_cast<int>((__float_as_uint(mx) >> 23) & 0xFFu);
+    // s = 2^(e(mx) - 6): |x / s| < 128 and the leading digit is a truncation.
+    float s = 0.f, inv = 0.f;
+    if (E >= 8 && E < 255) {
+      s = __uint_as_float(static_cast<uint32_t>(E - 6) << 23);
+      inv = __uint_as_float(static_cast<uint32_t>(254 - (E - 6)) << 23);
+    }
+    uint32_t dw[4][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}, {0u, 0u}};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float y = v[i] * inv;
+      const float x0 = truncf(y);
+      const float r1 = (y - x0) * 64.f;
+      const float x1 = rintf(r1);
+      const float r2 = (r1 - x1) * 128.f;
+      const float x2 = rintf(r2);
+      const float r3 = (r2 - x2) * 128.f;
+      const float x3 = rintf(r3);
+      const int sh = 8 * (i & 3);
+      dw[0][i >> 2] |= (static_cast<uint32_t>(static_cast<int>(x0)) & 0xFFu) << sh;
+      dw[1][i >> 2] |= (static_cast<uint32_t>(static_cast<int>(x1)) & 0xFFu) << sh;
+      dw[2][i >> 2] |= (static_cast<uint32_t>(static_cast<int>(x2)) & 0xFFu) << sh;
+      dw[3][i >> 2] |= (static_cast<uint32_t>(static_cast<int>(x3)) & 0xFFu) << sh;
+    }
+    // positions 8 lane .. 8 lane + 7 = 64c + 32hb + 16h + 8(lane & 1) + i
+    const int c = lane >> 3, hb = (lane >> 2) & 1, h = (lane >> 1) & 1, tb = 2 * (lane & 1);
+    const int m = 2 * c + h;
+    uint32_t* bw = reinterpret_cast<uint32_t*>(bfrag + static_cast<size_t>(b) * 1024);
+#pragma unroll
+    for (int dg = 0; dg < 4; ++dg) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int Lp = 4 * (dg + 4 * hb) + tb + j;
+        bw[((m >> 2) * 32 + Lp) * 4 + (m & 3)] = dw[dg][j];
+      }
+    }
+    su += __shfl_xor_sync(0xFFFFFFFFu, su, 1);
+    su += __shfl_xor_sync(0xFFFFFFFFu, su, 2);
+    if ((lane & 3) == 0) sx[b * 8 + (lane >> 2)] = su;
+    if (lane == 0) sscale[b] = s;
   }
   if (NORM) {
-    // RMSNorm as src/kernels_gpu.cu:564-591: double sum of squares,
-    // scale = float(1/sqrt(mean + eps)), out = x * scale * w.
-    const double tot = dev::BlockSumD(ss, dred);
-    const float scale = static_cast<float>(1.0 / sqrt(tot / static_cast<double>(K) + static_cast<double>(p.eps)));
-    for (int i = tid * 4; i < K; i += kThreads * 4) {
-      float4 v = *reinterpret_cast<float4*>(xs + i);
-      const float4 g = *reinterpret_cast<const float4*>(p.norm_w + i);
-      v.x = v.x * scale * g.x;
-      v.y = v.y * scale * g.y;
-      v.z = v.z * scale * g.z;
-      v.w = v.w * scale * g.w;
-      *reinterpret_cast<float4*>(xs + i) = v;
-    }
-  }
-  __syncthreads();
-  for (int j = warp; j < K / 32; j += kWarps) {
-    const float v = dev::WarpSum(xs[32 * j + lane]);
-    if (lane == 0) sx[j] = v;
+    ssq = dev::WarpSumD(ssq);
+    if (lane == 0) sq[warp] = ssq;
   }
   __syncthreads();
 
-  // ---- stream the stages
-  float acc = 0.f;
-  float best_v = -FLT_MAX;
-  int best_i = 0;
+  // ---- stream the units
+  const LaneK lk = MakeLane(lane);
+  uint32_t bA[8], bB[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) bA[i] = bB[i] = 0u;
+  const uint32_t lo_half = lk.g < 4 ? 1u : 0u, hi_half = 1u - lo_half;
+  float rg = 0.f, rg8 = 0.f;
   bool timed_out = false;
-  for (int st = 0; st < n_stages; ++st) {
-    const int slot = st % p.slots;
-    if (!timed_out && !dev::MbarWait(bars + slot, static_cast<uint32_t>((st / p.slots) & 1))) timed_out = true;
-    const int g = gb + st / p.n_chunks, c = st % p.n_chunks;
-    const int si = SegOf(p, g * kGroupRows);
-    const uint32_t type = p.seg[si].w.type;
-    const int nb = p.seg[si].w.nb;
-    const int b0 = c * p.kb, kbn = min(p.kb, nb - b0);
-    const uint8_t* sl = ring + static_cast<size_t>(slot) * p.slot_bytes;
+  int stalled = 0;  // first unit whose copy did not arrive
+  int tl = n_units > 0 ? u0 / nb : 0, b = n_units > 0 ? u0 % nb : 0;
+  uint32_t type = n_units > 0 ? p.seg[SegOfTile(p, t0 + tl)].w.type : 12u;
+  for (int i = 0; i < n_units; ++i) {
+    const int slot = i % R;
     if (!timed_out) {
+      const bool ok = dev::MbarWait(bars + slot, static_cast<uint32_t>((i / R) & 1));
+      timed_out = !__all_sync(0xFFFFFFFFu, ok);
+      if (timed_out) stalled = i;
+    }
+    if (!timed_out) {
+      const uint8_t* grp = ring + static_cast<size_t>(slot) * p.slot_bytes;
+      const uint32_t baddr = dev::SmemAddr(bfrag + static_cast<size_t>(b) * 1024 + lane * 16);
+      // lanes g < 4 own columns 0-3 (B rows 0..15, register b0), lanes g >= 4
+      // columns 4-7 (rows 16..31, register b1); the other register stays 0
+      Lds128If(bA[0], bA[1], bA[2], bA[3], lo_half, baddr);
+      Lds128If(bA[4], bA[5], bA[6], bA[7], lo_half, baddr + 512);
+      Lds128If(bB[0], bB[1], bB[2], bB[3], hi_half, baddr);
+      Lds128If(bB[4], bB[5], bB[6], bB[7], hi_half, baddr + 512);
+      const float s = sscale[b];
       if (type == 12u) {
-        for (int u = warp; u < kbn * 4; u += kWarps) {
-          acc += UnitQ4K(sl, p.kb, u >> 2, u & 3, lane, xs, sx, b0 + (u >> 2));
-        }
+        UnitQ4K(grp, bA, bB, sx + b * 8, s, lk, lane, rg, rg8);
       } else {
-        for (int u = warp; u < kbn * 4; u += kWarps) {
-          acc += UnitQ6K(sl, p.kb, u >> 2, (u >> 1) & 1, u & 1, lane, xs, b0 + (u >> 2));
-        }
+        UnitQ6K(grp, bA, bB, s, lk, lane, rg, rg8);
+      }
+      __syncwarp();
+      if (lane == 0 && issued < n_units) {
+        dev::FenceProxyAsync();
+        IssueNext(p, nb, cur, ring + static_cast<size_t>(issued % R) * p.slot_bytes, bars + (issued % R));
+        ++issued;
       }
     }
-    const bool last = c == p.n_chunks - 1;
-    if (last) {
-      red[warp * 32 + lane] = acc;
-      acc = 0.f;
-    }
-    __syncthreads();
-    if (tid == 0 && !timed_out && st + p.slots < n_stages) {
-      dev::FenceProxyAsync();
-      IssueStage(p, st + p.slots, gb, ring, bars);
-    }
-    if (last && warp == 0) {
-      float v = 0.f;
-#pragma unroll
-      for (int w = 0; w < kWarps; ++w) v += red[w * 32 + lane];
-      const int row = g * kGroupRows + lane;
-      if (EPI == static_cast<int>(Epi::kStore)) {
-        p.out[row] = v;
-      } else if (EPI == static_cast<int>(Epi::kResid)) {
-        p.out[row] = p.resid[row] + v;
-      } else if (EPI == static_cast<int>(Epi::kSilu)) {
-        // rows 2i (gate) and 2i+1 (up) sit on adjacent lanes
-        const float up = __shfl_down_sync(0xFFFFFFFFu, v, 1);
-        // (g / (1 + exp(-g))) * u, as src/kernels_gpu.cu:863-869
-        if ((lane & 1) == 0) p.out[row >> 1] = (v / (1.0f + expf(-v))) * up;
-      } else {
-        p.out[row] = v;
-        if (v > best_v) {  // a lane's rows increase: strict > keeps the lowest index
-          best_v = v;
-          best_i = row;
-        }
+    if (++b == nb || i + 1 == n_units) {
+      FlushPiece(red, tl + warp, lk, rg, rg8);
+      if (b == nb) {
+        b = 0;
+        ++tl;
+        if (i + 1 < n_units) type = p.seg[SegOfTile(p, t0 + tl)].w.type;
       }
     }
   }
-  if (timed_out && p.err != nullptr) atomicOr(p.err, 1);
+  if (timed_out) {
+    // drain copies still in flight into this warp's ring (bounded) before the
+    // shared memory can be handed to another block
+    if (lane == 0) {
+      for (int j = stalled; j < issued; ++j) dev::MbarWait(bars + (j % R), static_cast<uint32_t>((j / R) & 1));
+      if (p.err != nullptr) atomicOr(p.err, 1u);
+    }
+  }
+  __syncthreads();
+
+  // ---- epilogue: combine the per-warp pieces of every row in warp order
+  float scale = 1.f;
+  if (NORM) {
+    double tot = 0.0;
+    for (int w = 0; w < kWarps; ++w) tot += sq[w];
+    // RMSNorm as src/kernels_gpu.cu:564-591: double sum of squares,
+    // scale = float(1/sqrt(mean + eps)); applied to W (x * w) here.
+    scale = static_cast<float>(1.0 / sqrt(tot / static_cast<double>(K) + static_cast<double>(p.eps)));
+  }
+  const int n_rows = (t1 - t0) * kTile;
+  float best_v = -FLT_MAX;
+  int best_i = 0x7FFFFFFF;
+  const int step = EPI == static_cast<int>(Epi::kSilu) ? 2 : 1;
+  for (int lr = tid * step; lr < n_rows; lr += kThreads * step) {
+    const int ti = lr / kTile, r = lr - ti * kTile;
+    float v = 0.f, v2 = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const int a = w * U / kWarps, e = (w + 1) * U / kWarps;
+      if (a < e && a < (ti + 1) * nb && e > ti * nb) {
+        v += red[(ti + w) * kTile + r];
+        if (EPI == static_cast<int>(Epi::kSilu)) v2 += red[(ti + w) * kTile + r + 1];
+      }
+    }
+    if (NORM) {
+      v *= scale;
+      v2 *= scale;
+    }
+    const int row = t0 * kTile + lr;
+    if (EPI == static_cast<int>(Epi::kStore)) {
+      p.out[row] = v;
+    } else if (EPI == static_cast<int>(Epi::kResid)) {
+      p.out[row] = p.resid[row] + v;
+    } else if (EPI == static_cast<int>(Epi::kSilu)) {
+      // rows 2i (gate) and 2i+1 (up): (g / (1 + exp(-g))) * u, as src/kernels_gpu.cu:863-869
+      p.out[row >> 1] = (v / (1.0f + expf(-v))) * v2;
+    } else {
+      p.out[row] = v;
+      if (v > best_v) {  // a thread's rows increase: strict > keeps the lowest index
+        best_v = v;
+        best_i = row;
+      }
+    }
+  }
 
   if (EPI == static_cast<int>(Epi::kArgmax)) {
     // Ties go to the lowest index at every level (src/kernels_gpu.cu:827-859).
-    if (warp == 0) {
-      if (n_stages == 0) best_i = 0x7FFFFFFF;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xFFFFFFFFu, best_v, o);
-        const int oi = __shfl_xor_sync(0xFFFFFFFFu, best_i, o);
-        if (ov > best_v || (ov == best_v && oi < best_i)) {
-          best_v = ov;
-          best_i = oi;
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xFFFFFFFFu, best_v, o);
+      const int oi = __shfl_xor_sync(0xFFFFFFFFu, best_i, o);
+      if (ov > best_v || (ov == best_v && oi < best_i)) {
+        best_v = ov;
+        best_i = oi;
+      }
+    }
+    if (lane == 0) {
+      s_bv[warp] = best_v;
+      s_bi[warp] = best_i;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      float bv = s_bv[0];
+      int bi = s_bi[0];
+      for (int i = 1; i < kWarps; ++i) {
+        if (s_bv[i] > bv || (s_bv[i] == bv && s_bi[i] < bi)) {
+          bv = s_bv[i];
+          bi = s_bi[i];
         }
       }
-      if (lane == 0) {
-        p.part_val[blockIdx.x] = best_v;
-        p.part_idx[blockIdx.x] = best_i;
-        __threadfence();
-        const unsigned t = atomicAdd(p.ticket, 1u);
-        s_last = (t == gridDim.x - 1) ? 1 : 0;
-      }
+      p.part_val[blockIdx.x] = bv;
+      p.part_idx[blockIdx.x] = bi;
+      __threadfence();
+      const unsigned t = atomicAdd(p.ticket, 1u);
+      s_last = (t == gridDim.x - 1) ? 1 : 0;
     }
     __syncthreads();
     if (s_last) {
@@ -334,6 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1) MatvecKernel(const MvParams p) {
           bi = oi;
         }
       }
+      __syncthreads();
       if (lane == 0) {
         s_bv[warp] = bv;
         s_bi[warp] = bi;
@@ -357,9 +565,11 @@ __global__ void __launch_bounds__(kThreads, 1) MatvecKernel(const MvParams p) {
 }
 
 __global__ void EmbedKernel(const DevMat e, const int32_t* __restrict__ tok, float* __restrict__ x,
-                            const int64_t* __restrict__ pos, int32_t* __restrict__ out_ids) {
+                            const int64_t* __restrict__ pos, int32_t* __restrict__ out_ids, const Trace tr) {
+  dev::TraceScope trace(tr);
   dev::GridLaunchDependents();
   dev::GridWait();
+  trace.Ready();
   const int t = blockIdx.y;
   int32_t id = tok[t];
   if (out_ids != nullptr && blockIdx.x == 0 && threadIdx.x == 0) out_ids[*pos + t] = id;
@@ -402,8 +612,8 @@ void PrepareMatvecKernels() {
 }
 
 int MatvecGrid(int total_rows, int /*rows_per_warp*/, int num_sms) {
-  const int groups = total_rows / kGroupRows;
-  return std::max(1, std::min(groups, num_sms));
+  const int tiles = total_rows / kTile;
+  return std::max(1, std::min(tiles, num_sms));
 }
 
 void LaunchMatvec(const MvParams& in, Epi epi, int /*rows_per_warp*/, int num_sms, cudaStream_t s, bool pdl) {
@@ -411,41 +621,40 @@ void LaunchMatvec(const MvParams& in, Epi epi, int /*rows_per_warp*/, int num_sm
   const int K = p.seg[0].w.cols;
   RPGB_CHECK(p.n_seg >= 1 && p.n_seg <= 3, "matvec: 1..3 segments");
   RPGB_CHECK(K % 256 == 0 && K > 0 && K <= 16384, "matvec: width %d must be a multiple of 256 up to 16384", K);
-  int rows = 0;
-  size_t per_block = 0;
+  int rows = 0, slot = 0;
   for (int i = 0; i < p.n_seg; ++i) {
     const DevMat& w = p.seg[i].w;
     RPGB_CHECK(w.cols == K, "matvec: segments differ in width");
     RPGB_CHECK(p.seg[i].out_off == rows, "matvec: segments must be contiguous");
-    RPGB_CHECK(w.rows % kGroupRows == 0, "matvec: rows %d not a multiple of %d", w.rows, kGroupRows);
+    RPGB_CHECK(w.rows % kTile == 0, "matvec: rows %d not a multiple of %d", w.rows, kTile);
     RPGB_CHECK(w.type == kGgmlQ4_K || w.type == kGgmlQ6_K, "matvec: unsupported type");
-    const size_t pb = w.type == kGgmlQ4_K ? (8 * 512 + 512) : (12 * 512 + 512 + 64);
-    per_block = std::max(per_block, pb);
+    slot = std::max(slot, GroupBytes(w.type));
     rows += w.rows;
   }
   RPGB_CHECK(rows == p.total_rows, "matvec: total_rows mismatch");
+  if (epi == Epi::kSilu) RPGB_CHECK(rows % 2 == 0, "matvec: gate/up rows must pair up");
   const int nb = K / 256;
-  p.kb = std::min(nb, 4);
-  p.n_chunks = (nb + p.kb - 1) / p.kb;
-  p.slot_bytes = static_cast<int32_t>(per_block * p.kb);
-  const size_t xbytes = static_cast<size_t>(K) * 4 + static_cast<size_t>(K / 32) * 4;
-  const int slots = static_cast<int>((kSmemBudget > xbytes ? kSmemBudget - xbytes : 0) / p.slot_bytes);
-  p.slots = std::max(2, std::min(kMaxSlots, slots));
-  p.n_groups = rows / kGroupRows;
-  const Layout L = SmemLayout(K, p.slots, p.slot_bytes);
+  p.n_tiles = rows / kTile;
+  const int grid = MatvecGrid(rows, 1, num_sms);
+  p.max_tiles = (p.n_tiles + grid - 1) / grid;
+  p.slot_bytes = slot;
+  const Layout L0 = SmemLayout(nb, 0, slot, p.max_tiles);
+  const size_t per_ring = static_cast<size_t>(kWarps) * (slot + 8);
+  const int ring = static_cast<int>((kSmemBudget > L0.total ? kSmemBudget - L0.total : 0) / per_ring);
+  p.ring = std::max(2, std::min(kMaxRing, ring));
+  const Layout L = SmemLayout(nb, p.ring, slot, p.max_tiles);
   RPGB_CHECK(L.total <= kSmemLimit, "matvec: shared memory plan %zu exceeds the limit", L.total);
   MvFn fn = p.norm_w != nullptr ? PickEpi<true>(epi) : PickEpi<false>(epi);
-  const int grid = MatvecGrid(rows, 1, num_sms);
   LaunchKernelArgs(reinterpret_cast<const void*>(fn), dim3(grid), dim3(kThreads), L.total, s, pdl, p);
   CountLaunches(1);
 }
 
 void LaunchEmbed(const DevMat& embd, const int32_t* tok, int n_tok, float* x, const int64_t* pos,
-                 int32_t* out_ids, cudaStream_t s, bool pdl) {
+                 int32_t* out_ids, cudaStream_t s, bool pdl, const Trace& trace) {
   RPGB_CHECK(n_tok > 0 && n_tok < 65536, "embed: bad token count %d", n_tok);
   const dim3 grid((embd.cols + 255) / 256, n_tok);
   LaunchKernelArgs(reinterpret_cast<const void*>(EmbedKernel), grid, dim3(256), 0, s, pdl, embd, tok, x, pos,
-                   out_ids);
+                   out_ids, trace);
   CountLaunches(1);
 }
 

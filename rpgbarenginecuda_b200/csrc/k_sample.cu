@@ -128,8 +128,10 @@ __global__ void __launch_bounds__(kGenThreads) SampleGeneralKernel(const SampleP
   __shared__ double wsc[32];
   __shared__ int s_idx, s_amb;
 
+  dev::TraceScope trace(p.trace);
   dev::GridLaunchDependents();
   dev::GridWait();
+  trace.Ready();
   if (skip_if_flag && p.flag != nullptr && *p.flag == 1) return;
   const int n = p.n, tid = threadIdx.x;
   float* probs = p.probs;
@@ -296,8 +298,10 @@ __global__ void __launch_bounds__(kCandThreads) CandKernel(const SampleParams p)
   __shared__ unsigned hist[256];
   __shared__ uint32_t s_sel[2];
   __shared__ int s_cnt;
+  dev::TraceScope trace(p.trace);
   dev::GridLaunchDependents();
   dev::GridWait();
+  trace.Ready();
   const int n = p.n;
   const int per = (n + kCandBlocks - 1) / kCandBlocks;
   const int a = blockIdx.x * per;
@@ -335,8 +339,10 @@ __global__ void __launch_bounds__(kSmallThreads) SampleSmallKernel(const SampleP
   __shared__ int s_off[kCandBlocks + 1];
   __shared__ int s_bad, s_m, s_c;
   const int tid = threadIdx.x;
+  dev::TraceScope trace(p.trace);
   dev::GridLaunchDependents();
   dev::GridWait();
+  trace.Ready();
   if (tid == 0) {
     int off = 0, bad = 0;
     for (int b = 0; b < kCandBlocks; ++b) {
@@ -499,10 +505,13 @@ void LaunchSample(const SampleParams& p, bool want_probs, cudaStream_t s, bool p
                     p.top_k < p.n && p.n <= kCandBlocks * kSliceMax && p.cand_val != nullptr &&
                     p.flag != nullptr;
   if (fast) {
-    LaunchKernelArgs(reinterpret_cast<const void*>(CandKernel), dim3(kCandBlocks), dim3(kCandThreads), 0, s, pdl, p);
+    SampleParams q = p;
+    LaunchKernelArgs(reinterpret_cast<const void*>(CandKernel), dim3(kCandBlocks), dim3(kCandThreads), 0, s, pdl, q);
     const size_t smem = static_cast<size_t>(kMaxCand) * 16;
-    LaunchKernelArgs(reinterpret_cast<const void*>(SampleSmallKernel), dim3(1), dim3(kSmallThreads), smem, s, pdl, p);
-    LaunchKernelArgs(reinterpret_cast<const void*>(SampleGeneralKernel), dim3(1), dim3(kGenThreads), 0, s, pdl, p, 1);
+    if (q.trace.rec != nullptr) ++q.trace.id;
+    LaunchKernelArgs(reinterpret_cast<const void*>(SampleSmallKernel), dim3(1), dim3(kSmallThreads), smem, s, pdl, q);
+    if (q.trace.rec != nullptr) ++q.trace.id;
+    LaunchKernelArgs(reinterpret_cast<const void*>(SampleGeneralKernel), dim3(1), dim3(kGenThreads), 0, s, pdl, q, 1);
     CountLaunches(3);
   } else {
     LaunchKernelArgs(reinterpret_cast<const void*>(SampleGeneralKernel), dim3(1), dim3(kGenThreads), 0, s, pdl, p, 0);

@@ -14,6 +14,7 @@
 #include <cuda_fp16.h>
 #include <cstdint>
 
+#include "kernels.h"
 #include "model.h"
 
 namespace rpgb {
@@ -52,37 +53,48 @@ __device__ __forceinline__ int Q6kScale(const uint4& s, int i) {
 
 // ------------------------------------------------------------------ weight layout
 //
-// Matrices are stored in 32-row groups.  Inside a group, block b (256
-// weights) of every row is cut into 16-byte chunks (Q4_K: 8 chunks = qs[128];
-// Q6_K: 12 chunks = ql[128] | qh[64]) and chunk c of the 32 rows is stored
-// contiguously (512 bytes).  The 16-byte scale record of (row, block) and the
-// Q6_K d follow the same row-interleaved order.  A warp whose lane r owns row
-// r of a group therefore reads 512 contiguous bytes per chunk, and a stage of
-// (group, block range) is one contiguous byte range per array (one TMA bulk
-// copy each).
-constexpr int kGroupRows = 32;
-__host__ __device__ __forceinline__ int QChunks(uint32_t type) { return type == 12u ? 8 : 12; }
+// Matrices are 16-row tiles; block group (tile, super-block b) holds the 16
+// GGUF blocks in the byte order documented at RepackTile (model.cu).  Lane
+// L = 4g + t of a warp owns tile rows g and g + 8 in the integer MMA
+// fragments; the accessors below address single elements for the bit-exact
+// dequant paths.
+__host__ __device__ __forceinline__ int GroupBytesOf(uint32_t type) { return type == 12u ? 2304 : 3360; }
 
-__device__ __forceinline__ int64_t QByte(const DevMat& w, int64_t row, int b, int i) {
-  return (((row >> 5) * w.nb + b) * QChunks(w.type) + (i >> 4)) * 512 + (row & 31) * 16 + (i & 15);
+__device__ __forceinline__ const uint8_t* GroupPtr(const DevMat& w, int64_t row, int b) {
+  return w.q + ((row >> 4) * w.nb + b) * GroupBytesOf(w.type);
 }
-__device__ __forceinline__ int64_t SByte(const DevMat& w, int64_t row, int b) {
-  return (((row >> 5) * w.nb + b) * 32 + (row & 31)) * 16;
+
+// 4-bit value of element e (0..255) of Q4_K tile row r (0..15).
+__device__ __forceinline__ int Q4kNibble(const uint8_t* grp, int r, int e) {
+  const int j = e >> 5, p = e & 31;
+  const int c = j >> 1, h = p >> 4, t = (p >> 2) & 3, ee = p & 3;
+  const int g = r & 7, rs = r >> 3;
+  const uint8_t byte = grp[(c * 32 + 4 * g + t) * 16 + (2 * h + rs) * 4 + ee];
+  return (j & 1) ? (byte >> 4) : (byte & 15);
 }
-__device__ __forceinline__ int64_t DIndex(const DevMat& w, int64_t row, int b) {
-  return ((row >> 5) * w.nb + b) * 32 + (row & 31);
+
+// 6-bit value of element e (0..255) of a Q6_K tile row r (0..15).
+__device__ __forceinline__ int Q6kValue(const uint8_t* grp, int r, int e) {
+  const int j = e >> 4, pos = e & 15;
+  const int c = j >> 2, h = j & 1, hb = (j >> 1) & 1;
+  const int m = 2 * c + h, t = pos >> 2, ee = pos & 3;
+  const int g = r & 7, rs = r >> 3;
+  const uint8_t* w = grp + ((m >> 2) * 32 + 4 * g + t) * 48 + (m & 3) * 12;
+  if (hb == 0) return (rs == 0 ? w[ee] : w[4 + ee]) & 63;
+  if (rs == 0) return w[8 + ee] & 63;
+  return (w[ee] >> 6) | ((w[4 + ee] >> 6) << 2) | ((w[8 + ee] >> 6) << 4);
 }
 
 // ------------------------------------------------------------------ element dequant (bit-exact)
 
 // Element e (0..255) of Q4_K block b of `row`.
 __device__ __forceinline__ float DeqQ4K(const DevMat& w, int64_t row, int b, int e) {
-  const uint4 h = *reinterpret_cast<const uint4*>(w.s + SByte(w, row, b));
-  const int sub = e >> 5, l = e & 31;
+  const uint8_t* grp = GroupPtr(w, row, b);
+  const int r = static_cast<int>(row & 15);
+  const uint4 h = *reinterpret_cast<const uint4*>(grp + 2048 + 16 * r);
   int sc, m;
-  Q4kScaleMin(h.y, h.z, h.w, sub, &sc, &m);
-  const uint8_t byte = w.q[QByte(w, row, b, (sub >> 1) * 32 + l)];
-  const int raw = (sub & 1) ? (byte >> 4) : (byte & 15);
+  Q4kScaleMin(h.y, h.z, h.w, e >> 5, &sc, &m);
+  const int raw = Q4kNibble(grp, r, e);
   const float d = Half(h.x & 0xFFFFu), dmin = Half(h.x >> 16);
   const float d1 = __fmul_rn(d, static_cast<float>(sc));
   const float m1 = __fmul_rn(dmin, static_cast<float>(m));
@@ -91,13 +103,11 @@ __device__ __forceinline__ float DeqQ4K(const DevMat& w, int64_t row, int b, int
 
 // Element e (0..255) of Q6_K block b of `row`.
 __device__ __forceinline__ float DeqQ6K(const DevMat& w, int64_t row, int b, int e) {
-  const int hh = e >> 7, r = e & 127, quarter = r >> 5, l = r & 31;
-  const uint8_t byte = w.q[QByte(w, row, b, hh * 64 + l + ((quarter & 1) ? 32 : 0))];
-  const int nib = quarter < 2 ? (byte & 15) : (byte >> 4);
-  const int hi = (w.q[QByte(w, row, b, 128 + hh * 32 + l)] >> (2 * quarter)) & 3;
-  const int raw = (nib | (hi << 4)) - 32;
-  const int8_t sc = static_cast<int8_t>(w.s[SByte(w, row, b) + hh * 8 + (l >> 4) + 2 * quarter]);
-  const float d = Half(w.d[DIndex(w, row, b)]);
+  const uint8_t* grp = GroupPtr(w, row, b);
+  const int r = static_cast<int>(row & 15);
+  const int raw = Q6kValue(grp, r, e) - 32;
+  const int8_t sc = static_cast<int8_t>(grp[3072 + 16 * r + (e >> 4)]);
+  const float d = Half(*reinterpret_cast<const uint16_t*>(grp + 3328 + 2 * (2 * (r & 7) + (r >> 3))));
   return __fmul_rn(__fmul_rn(d, static_cast<float>(sc)), static_cast<float>(raw));
 }
 
@@ -151,6 +161,43 @@ __device__ __forceinline__ bool MbarWait(uint64_t* bar, uint32_t parity, uint32_
 // no-ops for a launch without the programmatic-serialization attribute.
 __device__ __forceinline__ void GridLaunchDependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void GridWait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// ------------------------------------------------------------------ timeline trace
+
+__device__ __forceinline__ uint64_t GlobalTimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Records one TraceRec per block (thread 0) when the trace buffer is set:
+// construct at kernel entry, call Ready() after GridWait(); the record is
+// written when the scope ends (every return path included).
+struct TraceScope {
+  const Trace& t;
+  uint64_t t0 = 0, tr = 0;
+  __device__ explicit TraceScope(const Trace& tr_) : t(tr_) {
+    if (t.rec != nullptr && threadIdx.x == 0) t0 = GlobalTimer();
+  }
+  __device__ void Ready() {
+    if (t.rec != nullptr && threadIdx.x == 0) tr = GlobalTimer();
+  }
+  __device__ ~TraceScope() {
+    if (t.rec != nullptr && threadIdx.x == 0) {
+      const uint64_t t1 = GlobalTimer();
+      const uint32_t i = atomicAdd(t.count, 1u);
+      if (i < t.cap) {
+        TraceRec r;
+        r.id = static_cast<uint32_t>(t.id);
+        r.block = blockIdx.x + gridDim.x * blockIdx.y;
+        r.t_start = t0;
+        r.t_ready = tr ? tr : t0;
+        r.t_end = t1;
+        t.rec[i] = r;
+      }
+    }
+  }
+};
 
 // ------------------------------------------------------------------ reductions
 

@@ -15,6 +15,21 @@ namespace rpgb {
 void CountLaunches(int64_t n);
 int64_t LaunchCount();
 
+// Optional device-side timeline: when `rec` is set, thread 0 of every block
+// appends {launch id, block, start, ready (after the programmatic-dependency
+// wait), end} in %globaltimer nanoseconds.  Used by the trace entry point to
+// see the real overlap of the launches inside a decode-step graph.
+struct TraceRec {
+  uint32_t id, block;
+  uint64_t t_start, t_ready, t_end;
+};
+struct Trace {
+  TraceRec* rec = nullptr;
+  uint32_t* count = nullptr;
+  uint32_t cap = 0;
+  int32_t id = -1;
+};
+
 // ------------------------------------------------------------------ decode matvec (n = 1)
 //
 // out = W x with W one to three row segments of the same width (the q, k and v
@@ -27,7 +42,7 @@ enum class Epi : int { kStore = 0, kResid = 1, kSilu = 2, kArgmax = 3 };
 
 struct MvSeg {
   DevMat w;
-  int32_t out_off = 0;
+  int32_t out_off = 0;  // first output row of the segment (a multiple of 16)
 };
 
 struct MvParams {
@@ -48,7 +63,8 @@ struct MvParams {
   int32_t pos_bump = 0;
   unsigned* err = nullptr;  // set to nonzero if a bounded device wait gave up
   // launch geometry, filled in by LaunchMatvec
-  int32_t n_groups = 0, kb = 0, n_chunks = 0, slots = 0, slot_bytes = 0;
+  int32_t n_tiles = 0, ring = 0, slot_bytes = 0, max_tiles = 0;
+  Trace trace;
 };
 
 // Sets the dynamic shared-memory limits of every kernel instantiation on the
@@ -57,9 +73,9 @@ struct MvParams {
 void PrepareMatvecKernels();
 void PrepareSampleKernels();
 
-// Rows handled per warp is fixed by the layout (one row per lane); the
-// argument is kept for call-site compatibility.  `pdl`: launch with
-// programmatic dependent launch (see launch.h).
+// The tile shape is fixed by the layout (16 rows per warp fragment); the
+// rows_per_warp argument is kept for call-site compatibility.  `pdl`: launch
+// with programmatic dependent launch (see launch.h).
 void LaunchMatvec(const MvParams& p, Epi epi, int rows_per_warp, int num_sms, cudaStream_t s, bool pdl = false);
 // Scratch sizes needed by kArgmax for a given launch.
 int MatvecGrid(int total_rows, int rows_per_warp, int num_sms);
@@ -68,7 +84,7 @@ int MatvecGrid(int total_rows, int rows_per_warp, int num_sms);
 
 // x[t, :] = dequant(embd row tok[t]); if out_ids != nullptr also out_ids[*pos + t] = tok[t].
 void LaunchEmbed(const DevMat& embd, const int32_t* tok, int n_tok, float* x, const int64_t* pos,
-                 int32_t* out_ids, cudaStream_t s, bool pdl = false);
+                 int32_t* out_ids, cudaStream_t s, bool pdl = false, const Trace& trace = Trace());
 
 // dst[i] = dequant(W row `row`, element i) for a whole row (bit-exact dequant entry).
 void LaunchDequantRows(const DevMat& w, int64_t row0, int64_t n_rows, float* dst, cudaStream_t s);
@@ -95,6 +111,7 @@ struct AttnParams {
   uint32_t* ticket = nullptr;  // [n_kv]
   int32_t n_splits = 1;
   int32_t fused = 0;  // 1: decode (norm + rope + cache write of the current token inside)
+  Trace trace;
 };
 void LaunchAttention(const AttnParams& p, int n_queries, cudaStream_t s, bool pdl = false);
 size_t AttentionPartialFloats(int n_kv, int group, int n_splits);
@@ -138,6 +155,7 @@ struct SampleParams {
   int32_t* cand_idx = nullptr;
   int32_t* cand_cnt = nullptr;
   int32_t* flag = nullptr;  // fast path result flag (1 = done)
+  Trace trace;  // id of the first launch; the sampler's launches use id, id + 1, ...
 };
 // Fast path (1 < top_k <= kFastTopK, T > 0): candidates + one small block.  Falls
 // back to the general kernel on the device if a block overflowed.

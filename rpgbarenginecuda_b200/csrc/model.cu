@@ -71,7 +71,7 @@ void ParallelRows(int64_t rows, const std::function<void(int64_t, int64_t)>& fn)
   unsigned nt = std::thread::hardware_concurrency();
   if (nt == 0) nt = 4;
   if (nt > 16) nt = 16;
-  if (rows < 4096) nt = 1;
+  if (rows < 64) nt = 1;
   std::vector<std::thread> th;
   const int64_t per = (rows + nt - 1) / nt;
   for (unsigned i = 0; i < nt; ++i) {
@@ -130,53 +130,98 @@ ModelMeta ReadModelMeta(const GgufFile& g) {
   return m;
 }
 
-void DevMatBytes(uint32_t type, int64_t rows, int64_t cols, size_t* q, size_t* s, size_t* d) {
-  const size_t blocks = static_cast<size_t>(rows) * static_cast<size_t>(cols / 256);
-  if (type == kGgmlQ4_K) {
-    *q = blocks * 128;
-    *s = blocks * 16;
-    *d = 0;
-  } else if (type == kGgmlQ6_K) {
-    *q = blocks * 192;
-    *s = blocks * 16;
-    *d = blocks * 2;
-  } else {
-    Throw("matrix type %s is not supported (Q4_K and Q6_K are)", GgmlTypeName(type));
-  }
+int GroupBytes(uint32_t type) {
+  if (type == kGgmlQ4_K) return 16 * 144;
+  if (type == kGgmlQ6_K) return 16 * 210;
+  Throw("matrix type %s is not supported (Q4_K and Q6_K are)", GgmlTypeName(type));
 }
 
-void RepackGroup(uint32_t type, const uint8_t* const* src, int64_t nb, uint8_t* dq, uint8_t* ds, uint16_t* dd) {
-  RPGB_CHECK(type == kGgmlQ4_K || type == kGgmlQ6_K, "matrix type %s is not supported (Q4_K and Q6_K are)",
-             GgmlTypeName(type));
-  const bool q4 = type == kGgmlQ4_K;
-  const int nc = q4 ? 8 : 12;
-  const int bb = q4 ? 144 : 210;
+size_t DevMatBytes(uint32_t type, int64_t rows, int64_t cols) {
+  RPGB_CHECK(rows % kTileRows == 0 && cols % 256 == 0, "matrix %lld x %lld is not whole 16-row tiles",
+             static_cast<long long>(rows), static_cast<long long>(cols));
+  return static_cast<size_t>(rows / kTileRows) * static_cast<size_t>(cols / 256) * GroupBytes(type);
+}
+
+namespace {
+
+// 6-bit value (0..63) of element e of a GGUF Q6_K block (src/quant.cc:321-354 layout).
+inline int Q6kRaw(const uint8_t* blk, int e) {
+  const int hh = e >> 7, r = e & 127, quarter = r >> 5, l = r & 31;
+  const uint8_t byte = blk[hh * 64 + l + ((quarter & 1) ? 32 : 0)];
+  const int nib = quarter < 2 ? (byte & 15) : (byte >> 4);
+  const int hi = (blk[128 + hh * 32 + l] >> (2 * quarter)) & 3;
+  return nib | (hi << 4);
+}
+
+}  // namespace
+
+// Block-group byte order (lane = 4 * g + t, g = 0..7, t = 0..3; rows g and g + 8
+// of the tile belong to lane group g):
+//   Q4_K  [0, 2048)     per pair c (0..3) and lane, 16 B = words (h, rs) for
+//                       h, rs in {0,1}: qs[32c + 16h + 4t .. +3] of row g + 8rs
+//         [2048, 2304)  row r: the 16 GGUF header bytes (d, dmin, scales[12])
+//   Q6_K  [0, 3072)     per MMA m (0..7) and lane, 12 B = words X, Y, Z holding
+//                       the 6-bit values a0 (row g, sub-block 4(m>>1) + (m&1)),
+//                       a1 (row g + 8, same), a2 (row g, sub-block + 2), a3 (row
+//                       g + 8, sub-block + 2) at positions 4t .. 4t+3: byte e of
+//                       X = a0 | a3[1:0] << 6, Y = a1 | a3[3:2] << 6, Z = a2 |
+//                       a3[5:4] << 6.  Lane records of MMAs 4q .. 4q+3 are
+//                       adjacent (48 B), so a lane reads them as 3 x 16 B.
+//         [3072, 3328)  row r: sc[16] (int8)
+//         [3328, 3360)  d (f16) of row g + 8rs at index 2g + rs
+void RepackTile(uint32_t type, const uint8_t* const* src, int64_t nb, uint8_t* dst) {
+  const int gb = GroupBytes(type);
   for (int64_t b = 0; b < nb; ++b) {
-    for (int r = 0; r < 32; ++r) {
-      const uint8_t* blk = src[r] + b * bb;
-      const uint8_t* qbytes = q4 ? blk + 16 : blk;  // Q4_K qs follow the 16-byte header
-      for (int c = 0; c < nc; ++c) std::memcpy(dq + ((b * nc + c) * 512 + r * 16), qbytes + 16 * c, 16);
-      if (q4) {
-        std::memcpy(ds + (b * 32 + r) * 16, blk, 16);
-      } else {
-        std::memcpy(ds + (b * 32 + r) * 16, blk + 192, 16);
-        std::memcpy(dd + b * 32 + r, blk + 208, 2);
+    uint8_t* o = dst + b * gb;
+    if (type == kGgmlQ4_K) {
+      for (int r = 0; r < 16; ++r) std::memcpy(o + 2048 + 16 * r, src[r] + b * 144, 16);
+      for (int c = 0; c < 4; ++c) {
+        for (int lane = 0; lane < 32; ++lane) {
+          const int g = lane >> 2, t = lane & 3;
+          for (int h = 0; h < 2; ++h) {
+            for (int rs = 0; rs < 2; ++rs) {
+              const uint8_t* qs = src[g + 8 * rs] + b * 144 + 16;
+              std::memcpy(o + (c * 32 + lane) * 16 + (2 * h + rs) * 4, qs + 32 * c + 16 * h + 4 * t, 4);
+            }
+          }
+        }
+      }
+    } else {
+      int v[16][256];
+      for (int r = 0; r < 16; ++r) {
+        const uint8_t* blk = src[r] + b * 210;
+        for (int e = 0; e < 256; ++e) v[r][e] = Q6kRaw(blk, e);
+        std::memcpy(o + 3072 + 16 * r, blk + 192, 16);
+        const int g = r & 7, rs = r >> 3;
+        std::memcpy(o + 3328 + 2 * (2 * g + rs), blk + 208, 2);
+      }
+      for (int m = 0; m < 8; ++m) {
+        const int sb0 = 4 * (m >> 1) + (m & 1), sb1 = sb0 + 2;
+        for (int lane = 0; lane < 32; ++lane) {
+          const int g = lane >> 2, t = lane & 3;
+          uint8_t* w = o + ((m >> 2) * 32 + lane) * 48 + (m & 3) * 12;
+          for (int e = 0; e < 4; ++e) {
+            const int a0 = v[g][16 * sb0 + 4 * t + e], a1 = v[g + 8][16 * sb0 + 4 * t + e];
+            const int a2 = v[g][16 * sb1 + 4 * t + e], a3 = v[g + 8][16 * sb1 + 4 * t + e];
+            w[e] = static_cast<uint8_t>(a0 | ((a3 & 3) << 6));
+            w[4 + e] = static_cast<uint8_t>(a1 | (((a3 >> 2) & 3) << 6));
+            w[8 + e] = static_cast<uint8_t>(a2 | (((a3 >> 4) & 3) << 6));
+          }
+        }
       }
     }
   }
 }
 
-void RepackRows(uint32_t type, const uint8_t* src, int64_t rows, int64_t cols, uint8_t* dq, uint8_t* ds,
-                uint16_t* dd) {
-  RPGB_CHECK(rows % 32 == 0, "rows %lld are not a multiple of 32", static_cast<long long>(rows));
+void RepackRows(uint32_t type, const uint8_t* src, int64_t rows, int64_t cols, uint8_t* dst) {
+  RPGB_CHECK(rows % kTileRows == 0, "rows %lld are not a multiple of %d", static_cast<long long>(rows), kTileRows);
   const int64_t nb = cols / 256;
   const int64_t rb = GgmlRowBytes(type, cols);
-  size_t qg, sg, dg;
-  DevMatBytes(type, 32, cols, &qg, &sg, &dg);
-  for (int64_t g = 0; g < rows / 32; ++g) {
-    const uint8_t* ptrs[32];
-    for (int r = 0; r < 32; ++r) ptrs[r] = src + (g * 32 + r) * rb;
-    RepackGroup(type, ptrs, nb, dq + g * qg, ds + g * sg, dd ? dd + g * (dg / 2) : nullptr);
+  const size_t tile_bytes = static_cast<size_t>(nb) * GroupBytes(type);
+  for (int64_t t = 0; t < rows / kTileRows; ++t) {
+    const uint8_t* ptrs[kTileRows];
+    for (int r = 0; r < kTileRows; ++r) ptrs[r] = src + (t * kTileRows + r) * rb;
+    RepackTile(type, ptrs, nb, dst + t * tile_bytes);
   }
 }
 
@@ -295,10 +340,10 @@ std::unique_ptr<Model> Model::Load(const std::string& path, int device, int32_t 
 
   size_t total = 0;
   for (const MatJob& j : mats) {
-    size_t q, s, d;
     const int64_t rows = j.a->rows() * (j.b ? 2 : 1);
-    DevMatBytes(j.a->type, rows, j.a->cols(), &q, &s, &d);
-    total += AlignUp(q) + AlignUp(s) + AlignUp(d);
+    RPGB_CHECK(rows % kTileRows == 0, "tensor %s: %lld rows are not a multiple of %d", j.a->name.c_str(),
+               static_cast<long long>(rows), kTileRows);
+    total += AlignUp(DevMatBytes(j.a->type, rows, j.a->cols()));
   }
   for (const NormJob& n : norms) total += AlignUp(static_cast<size_t>(n.t->n_elements) * 4);
   m->rope_pos_ = std::max<int32_t>(1, std::min<int32_t>(max_pos, c.context_length));
@@ -332,39 +377,27 @@ std::unique_ptr<Model> Model::Load(const std::string& path, int device, int32_t 
     const int64_t cols = j.a->cols();
     const int64_t src_rows = j.a->rows();
     const int64_t rows = src_rows * (j.b ? 2 : 1);
-    size_t qb, sb, db;
-    DevMatBytes(type, rows, cols, &qb, &sb, &db);
     DevMat dm;
     dm.type = type;
     dm.rows = static_cast<int32_t>(rows);
     dm.cols = static_cast<int32_t>(cols);
     dm.nb = static_cast<int32_t>(cols / 256);
-    uint8_t* dq = carve(qb);
-    uint8_t* ds = carve(sb);
-    uint8_t* dd = db ? carve(db) : nullptr;
+    uint8_t* dq = carve(DevMatBytes(type, rows, cols));
     dm.q = dq;
-    dm.s = ds;
-    dm.d = reinterpret_cast<const uint16_t*>(dd);
     *j.dst = dm;
 
     const int64_t row_src_bytes = GgmlRowBytes(type, cols);
-    size_t qg, sg, dg;  // bytes of one 32-row group
-    DevMatBytes(type, 32, cols, &qg, &sg, &dg);
-    RPGB_CHECK(rows % 32 == 0, "tensor %s: %lld rows are not a multiple of 32", j.a->name.c_str(),
-               static_cast<long long>(rows));
-    const int64_t groups = rows / 32;
-    const int64_t groups_per_chunk = std::max<int64_t>(1, static_cast<int64_t>(up.cap() / (qg + sg + dg)));
-    for (int64_t g0 = 0; g0 < groups; g0 += groups_per_chunk) {
-      const int64_t ng = std::min(groups_per_chunk, groups - g0);
+    const size_t tile_bytes = static_cast<size_t>(dm.nb) * GroupBytes(type);
+    const int64_t tiles = rows / kTileRows;
+    const int64_t tiles_per_chunk = std::max<int64_t>(1, static_cast<int64_t>(up.cap() / tile_bytes));
+    for (int64_t t0 = 0; t0 < tiles; t0 += tiles_per_chunk) {
+      const int64_t nt = std::min(tiles_per_chunk, tiles - t0);
       uint8_t* sq = up.buf();
-      uint8_t* ss = sq + ng * qg;
-      uint16_t* sd = reinterpret_cast<uint16_t*>(ss + ng * sg);
-      ParallelRows(ng * 32, [&](int64_t a, int64_t b) {
-        for (int64_t gi = a / 32; gi * 32 < b; ++gi) {
-          if (gi * 32 < a) continue;
-          const uint8_t* ptrs[32];
-          for (int r = 0; r < 32; ++r) {
-            const int64_t dst_row = (g0 + gi) * 32 + r;
+      ParallelRows(nt, [&](int64_t a, int64_t b) {
+        for (int64_t ti = a; ti < b; ++ti) {
+          const uint8_t* ptrs[kTileRows];
+          for (int r = 0; r < kTileRows; ++r) {
+            const int64_t dst_row = (t0 + ti) * kTileRows + r;
             const GgufTensor* src_t = j.a;
             int64_t src_row = dst_row;
             if (j.b != nullptr) {  // gate/up interleave: 2i = gate row i, 2i+1 = up row i
@@ -373,12 +406,10 @@ std::unique_ptr<Model> Model::Load(const std::string& path, int device, int32_t 
             }
             ptrs[r] = g.TensorData(*src_t) + src_row * row_src_bytes;
           }
-          RepackGroup(type, ptrs, cols / 256, sq + gi * qg, ss + gi * sg, dg ? sd + gi * (dg / 2) : nullptr);
+          RepackTile(type, ptrs, dm.nb, sq + ti * tile_bytes);
         }
       });
-      up.Push(dq + g0 * qg, sq, ng * qg);
-      up.Push(ds + g0 * sg, ss, ng * sg);
-      if (dg) up.Push(dd + g0 * dg, reinterpret_cast<const uint8_t*>(sd), ng * dg);
+      up.Push(dq + t0 * tile_bytes, sq, static_cast<size_t>(nt) * tile_bytes);
       up.Wait();
     }
   }

@@ -5,15 +5,12 @@
 // BuildRopeTable (src/gpu_model.cu:90-120).
 //
 // Difference by design: the reference uploads raw GGUF blocks (144 B Q4_K,
-// 210 B Q6_K) and reads them byte by byte.  Here every super-block is split at
-// load time into separately strided arrays so a warp reads 16-byte aligned,
-// fully coalesced chunks and the 210-byte Q6_K block needs no padding:
-//
-//   Q4_K  q: qs[128] per block      s: d|dmin|scales[12] (16 B) per block
-//   Q6_K  q: ql[128]|qh[64] per block  s: sc[16] per block   d: f16 per block
-//
-// Arrays are [rows][nb][bytes] row-major, nb = cols / 256.  The bytes inside
-// each piece are the GGUF bytes, so decoding follows src/quant.cc exactly.
+// 210 B Q6_K) and reads them byte by byte.  Here a matrix is stored as 16-row
+// tiles; the 16 blocks of one tile and one 256-column super-block form a
+// contiguous "block group" (Q4_K 2304 B, Q6_K 3360 B -- exactly 16 GGUF
+// blocks) whose bytes are laid out in the register order of the integer
+// tensor-core fragments used by the decode matvec (see kernels.cuh).  The
+// repack is lossless: dequantisation reproduces src/quant.cc bit for bit.
 #pragma once
 
 #include <cstdint>
@@ -43,12 +40,11 @@ struct ModelMeta {
 ModelMeta ReadModelMeta(const GgufFile& g);
 
 // One quantised matrix in the repacked device layout (passed to kernels by value).
+// Block group (tile t, super-block b) starts at q + (t * nb + b) * GroupBytes(type).
 struct DevMat {
   uint32_t type = 0;  // kGgmlQ4_K or kGgmlQ6_K
   int32_t rows = 0, cols = 0, nb = 0;
   const uint8_t* q = nullptr;
-  const uint8_t* s = nullptr;
-  const uint16_t* d = nullptr;
 };
 
 struct DevLayer {
@@ -61,15 +57,15 @@ struct DevLayer {
   DevMat down;
 };
 
-// Host-side repack of GGUF blocks into the device layout: 32-row groups with
-// 16-byte chunks interleaved across the rows (see kernels.cuh).  RepackGroup
-// takes the 32 source rows by pointer (gate/up interleave); RepackRows takes
-// `rows` (a multiple of 32) contiguous GGUF rows.  Sizes: see DevMatBytes.
-void RepackGroup(uint32_t type, const uint8_t* const* src_rows, int64_t nb, uint8_t* dst_q, uint8_t* dst_s,
-                 uint16_t* dst_d);
-void RepackRows(uint32_t type, const uint8_t* src, int64_t rows, int64_t cols, uint8_t* dst_q,
-                uint8_t* dst_s, uint16_t* dst_d);
-void DevMatBytes(uint32_t type, int64_t rows, int64_t cols, size_t* q, size_t* s, size_t* d);
+// Host-side repack of GGUF blocks into the device layout.  RepackTile takes
+// the 16 source rows of one tile by pointer (gate/up interleave) and writes
+// nb block groups; RepackRows takes `rows` (a multiple of 16) contiguous GGUF
+// rows.  DevMatBytes = rows / 16 * nb * GroupBytes(type).
+constexpr int kTileRows = 16;
+int GroupBytes(uint32_t type);
+void RepackTile(uint32_t type, const uint8_t* const* src_rows, int64_t nb, uint8_t* dst);
+void RepackRows(uint32_t type, const uint8_t* src, int64_t rows, int64_t cols, uint8_t* dst);
+size_t DevMatBytes(uint32_t type, int64_t rows, int64_t cols);
 
 class Model {
  public:
