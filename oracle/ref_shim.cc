@@ -72,6 +72,7 @@ int ref_gpu_dequant(uint32_t type, const uint8_t* host_bytes, int64_t n_elems, f
   rpg::DeviceBuffer src(static_cast<size_t>(nb)), dst(static_cast<size_t>(n_elems) * 4);
   src.Upload(host_bytes, static_cast<size_t>(nb));
   rpg::GpuDequantRow(type, static_cast<const uint8_t*>(src.data()), n_elems, static_cast<float*>(dst.data()));
+  RPG_CUDA_CHECK(cudaDeviceSynchronize());
   dst.Download(out_host, static_cast<size_t>(n_elems) * 4);
   return 0;
   SHIM_CATCH
@@ -92,6 +93,7 @@ int ref_gpu_matmul(uint32_t type, const uint8_t* host_bytes, int64_t rows, int64
   rpg::DeviceBuffer x(static_cast<size_t>(n_tok * cols) * 4), out(static_cast<size_t>(n_tok * rows) * 4);
   x.Upload(x_host, static_cast<size_t>(n_tok * cols) * 4);
   rpg::GpuMatMulQuant(w, static_cast<const float*>(x.data()), n_tok, static_cast<float*>(out.data()));
+  RPG_CUDA_CHECK(cudaDeviceSynchronize());
   out.Download(out_host, static_cast<size_t>(n_tok * rows) * 4);
   return 0;
   SHIM_CATCH
@@ -108,10 +110,14 @@ int ref_gpu_sample(const float* logits_host, int64_t n, float temperature, int32
   lg.Upload(logits_host, static_cast<size_t>(n) * 4);
   if (probs_host != nullptr) {
     rpg::GpuFilterToProbs(static_cast<const float*>(lg.data()), n, opt, static_cast<float*>(pr.data()));
+    // the reference launches on its own engine stream; the download below is a
+    // plain cudaMemcpy, so wait for the device first
+    RPG_CUDA_CHECK(cudaDeviceSynchronize());
     pr.Download(probs_host, static_cast<size_t>(n) * 4);
   }
   rpg::GpuSampleToken(static_cast<const float*>(lg.data()), n, opt, seed, counter, static_cast<float*>(pr.data()),
                       static_cast<int32_t*>(idx.data()));
+  RPG_CUDA_CHECK(cudaDeviceSynchronize());
   idx.Download(tok, 4);
   return 0;
   SHIM_CATCH
@@ -137,6 +143,7 @@ int ref_session_prefill(int h, const int32_t* toks, int64_t n, float* last_logit
   const int32_t V = s->model->config().vocab;
   s->last = static_cast<const float*>(s->scratch.logits.data()) + (n - 1) * V;
   if (last_logits != nullptr) {
+    RPG_CUDA_CHECK(cudaDeviceSynchronize());
     RPG_CUDA_CHECK(cudaMemcpy(last_logits, s->last, static_cast<size_t>(V) * 4, cudaMemcpyDeviceToHost));
   }
   return 0;
