@@ -139,6 +139,21 @@ RPGB_API int32_t rpgb_matrix_matvec(int32_t matrix, const float* x_dev, int64_t 
 RPGB_API int32_t rpgb_sample(const float* logits_dev, int32_t n, const rpgb_sample_options* opt, uint64_t seed,
                              uint64_t counter, float* probs_dev, int32_t* out_tok_dev, void* stream);
 
+/* rpgb_sample without any device-memory allocation.  No counterpart in the
+ * reference: it exists for hosts that cannot allocate GPU memory when they
+ * sample -- a game or UI thread that must never block (cudaMalloc and
+ * cudaFree synchronise the whole device), or a process whose GPU memory is
+ * already fully owned by another allocator's pool.  Same sampling as
+ * rpgb_sample with probs_dev == NULL; its scratch is a fixed array inside the
+ * library (about 1.1 MiB, held on every GPU that loads the library), so n must
+ * not exceed RPGB_SAMPLE_NOALLOC_MAX_VOCAB.  All calls on a device share that
+ * array: calls whose GPU work overlaps race and must be serialised.  The first
+ * call on a device looks up the array's address and should come before any
+ * stream capture begins. */
+#define RPGB_SAMPLE_NOALLOC_MAX_VOCAB 262144
+RPGB_API int32_t rpgb_sample_noalloc(const float* logits_dev, int32_t n, const rpgb_sample_options* opt,
+                                     uint64_t seed, uint64_t counter, int32_t* out_tok_dev, void* stream);
+
 /* u = H(seed, counter) in [0, 1) (DevCounterUniform, src/sampler_gpu.cu:364). */
 RPGB_API float rpgb_counter_uniform(uint64_t seed, uint64_t counter);
 

@@ -53,6 +53,7 @@ _SIGS = {
     "rpgb_matrix_dequant": (c_i32, [c_i32, c_i64, c_i64, c_p, c_p]),
     "rpgb_matrix_matvec": (c_i32, [c_i32, c_p, c_i64, c_p, c_p]),
     "rpgb_sample": (c_i32, [c_p, c_i32, ctypes.POINTER(SampleOptions), c_u64, c_u64, c_p, c_p, c_p]),
+    "rpgb_sample_noalloc": (c_i32, [c_p, c_i32, ctypes.POINTER(SampleOptions), c_u64, c_u64, c_p, c_p]),
     "rpgb_counter_uniform": (c_f32, [c_u64, c_u64]),
     # the public ten-function ABI (include/rpg_engine.h)
     "rpg_engine_version": (ctypes.c_char_p, []),
