@@ -17,7 +17,7 @@ size_t AlignUp(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 // Positions handled per attention split in decode; a graph is recorded once per
 // session, so the split count is fixed from max_seq and short contexts simply
 // leave the tail splits empty.
-constexpr int kPositionsPerSplit = 256;
+constexpr int kPositionsPerSplit = kAttnSplitPositions;
 
 class Carver {
  public:
@@ -369,6 +369,7 @@ void Session::EnqueueStep(const SampleOpts& opt, uint64_t seed) {
     a.ticket = tickets_;
     a.n_splits = n_splits_;
     a.fused = 1;
+    a.err = err_;
     a.trace = NextTrace(&tid);
     LaunchAttention(a, 1, s, true);
 

@@ -52,27 +52,26 @@ __device__ __forceinline__ void BlockSumG(double (&v)[G], double* sh) {
   for (int g = 0; g < G; ++g) v[g] = ((sh[g] + sh[G + g]) + sh[2 * G + g]) + sh[3 * G + g];
 }
 
-// In-place per-head RMSNorm + rotate-half RoPE of G vectors held one element
-// per thread (thread = dimension).  Returns the transformed element.
-template <int G>
-__device__ __forceinline__ void NormRope(float (&v)[G], const float* __restrict__ w, float eps,
-                                         const float* __restrict__ rope_row, float (*buf)[D], double* dsh) {
+// In-place per-head RMSNorm + rotate-half RoPE of N vectors held one element
+// per thread (thread = dimension); vector i is scaled by weight row w[i].
+template <int N>
+__device__ __forceinline__ void NormRopeW(float (&v)[N], const float* const (&w)[N], float eps,
+                                          const float* __restrict__ rope_row, float (*buf)[D], double* dsh) {
   const int tid = threadIdx.x;
-  double ss[G];
+  double ss[N];
 #pragma unroll
-  for (int g = 0; g < G; ++g) ss[g] = static_cast<double>(v[g]) * v[g];
-  BlockSumG<G>(ss, dsh);
-  const float wt = w[tid];
+  for (int g = 0; g < N; ++g) ss[g] = static_cast<double>(v[g]) * v[g];
+  BlockSumG<N>(ss, dsh);
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
+  for (int g = 0; g < N; ++g) {
     const float scale = static_cast<float>(1.0 / sqrt(ss[g] / static_cast<double>(D) + static_cast<double>(eps)));
-    buf[g][tid] = v[g] * scale * wt;
+    buf[g][tid] = v[g] * scale * w[g][tid];
   }
   __syncthreads();
   if (tid < D / 2) {
     const float c = rope_row[tid], sn = rope_row[D / 2 + tid];
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
+    for (int g = 0; g < N; ++g) {
       const float a = buf[g][tid], b = buf[g][tid + D / 2];
       buf[g][tid] = a * c - b * sn;
       buf[g][tid + D / 2] = b * c + a * sn;
@@ -80,17 +79,37 @@ __device__ __forceinline__ void NormRope(float (&v)[G], const float* __restrict_
   }
   __syncthreads();
 #pragma unroll
-  for (int g = 0; g < G; ++g) v[g] = buf[g][tid];
+  for (int g = 0; g < N; ++g) v[g] = buf[g][tid];
+}
+
+template <int G>
+__device__ __forceinline__ void NormRope(float (&v)[G], const float* __restrict__ w, float eps,
+                                         const float* __restrict__ rope_row, float (*buf)[D], double* dsh) {
+  const float* ws[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) ws[g] = w;
+  NormRopeW<G>(v, ws, eps, rope_row, buf, dsh);
+}
+
+// Positions per split at least this many: short contexts run one split per
+// KV head and skip the merge.
+constexpr int64_t kMinSplit = 256;
+constexpr int kMaxSplits = 64;
+
+// Positions of the split starting at p0: min(128, L - p0).
+__device__ __forceinline__ int64_t p1_of(int64_t p0, int64_t L) {
+  return L - p0 < kAttnSplitPositions ? L - p0 : kAttnSplitPositions;
 }
 
 template <int G>
 __global__ void __launch_bounds__(128) AttnKernel(const AttnParams p) {
-  __shared__ __align__(16) float qs[G][D];
-  __shared__ __align__(16) float kb[1][D];
+  __shared__ __align__(16) float qs[G + 1][D];  // G query vectors (+ the new key while fusing)
   __shared__ float sc[G][128];
   __shared__ __align__(16) float vred[4][G][D];
-  __shared__ double dsh[4 * G];
+  __shared__ double dsh[4 * (G + 1)];
   __shared__ float fsh[4 * G];
+  __shared__ float s_wm[kMaxSplits][G];
+  __shared__ double s_wl[kMaxSplits][G];
   __shared__ int s_last;
 
   dev::TraceScope trace(p.trace);
@@ -100,7 +119,10 @@ __global__ void __launch_bounds__(128) AttnKernel(const AttnParams p) {
   // (previous graph launch / host copy), so it may be read before the wait.
   const int64_t pos = *p.pos + t;
   const int64_t L = pos + 1;
-  const int64_t chunk = (L + p.n_splits - 1) / p.n_splits;
+  int64_t chunk = (L + p.n_splits - 1) / p.n_splits;
+  if (chunk < kMinSplit) chunk = kMinSplit;
+  const int active = static_cast<int>((L + chunk - 1) / chunk);
+  if (s >= active) return;  // nothing to do at this length (no memory touched)
   const int64_t p0 = static_cast<int64_t>(s) * chunk;
   const int64_t p1 = p0 + chunk < L ? p0 + chunk : L;
   const int q_dim = p.n_heads * D;
@@ -127,12 +149,20 @@ __global__ void __launch_bounds__(128) AttnKernel(const AttnParams p) {
 #pragma unroll
     for (int g = 0; g < G; ++g) v[g] = p.q[static_cast<int64_t>(t) * p.q_stride + (h * G + g) * D + tid];
     if (p.fused) {
-      NormRope<G>(v, p.q_norm, p.eps, p.rope + pos * D, qs, dsh);
+      // q heads and the new key normalised and rotated together (one block sum)
+      float vk[G + 1];
+      const float* ws[G + 1];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        vk[g] = v[g];
+        ws[g] = p.q_norm;
+      }
+      vk[G] = p.k_raw[h * D + tid];
+      ws[G] = p.k_norm;
+      NormRopeW<G + 1>(vk, ws, p.eps, p.rope + pos * D, qs, dsh);
       if (p0 <= pos && pos < p1) {
         // This split owns the new position: write its K/V (fp16, RNE) first.
-        float kv1[1] = {p.k_raw[h * D + tid]};
-        NormRope<1>(kv1, p.k_norm, p.eps, p.rope + pos * D, kb, dsh);
-        kbase[pos * D + tid] = __float2half_rn(kv1[0]);
+        kbase[pos * D + tid] = __float2half_rn(vk[G]);
         vbase[pos * D + tid] = __float2half_rn(p.v_raw[h * D + tid]);
       }
     } else {
@@ -237,7 +267,7 @@ __global__ void __launch_bounds__(128) AttnKernel(const AttnParams p) {
 #pragma unroll
   for (int g = 0; g < G; ++g) o[g] = ((vred[0][g][tid] + vred[1][g][tid]) + vred[2][g][tid]) + vred[3][g][tid];
 
-  if (p.n_splits == 1) {
+  if (active == 1) {
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       p.out[static_cast<int64_t>(t) * q_dim + (h * G + g) * D + tid] = o[g] * static_cast<float>(1.0 / l[g]);
@@ -260,25 +290,252 @@ __global__ void __launch_bounds__(128) AttnKernel(const AttnParams p) {
   __syncthreads();
   if (tid == 0) {
     const unsigned tk = atomicAdd(p.ticket + h, 1u);
-    s_last = tk == static_cast<unsigned>(p.n_splits - 1) ? 1 : 0;
+    s_last = tk == static_cast<unsigned>(active - 1) ? 1 : 0;
   }
   __syncthreads();
   if (!s_last) return;
   __threadfence();
+  // split maxima and masses, one thread per split (loads in parallel)
+  if (tid < active) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float* rec = p.part + (static_cast<int64_t>(h * p.n_splits + tid) * G + g) * kRec;
+      s_wm[tid][g] = __ldcg(rec);
+      s_wl[tid][g] = static_cast<double>(__ldcg(rec + 1));
+    }
+  }
+  __syncthreads();
 #pragma unroll
   for (int g = 0; g < G; ++g) {
     float M = -INFINITY;
-    for (int sp = 0; sp < p.n_splits; ++sp) {
-      M = fmaxf(M, __ldcg(p.part + (static_cast<int64_t>(h * p.n_splits + sp) * G + g) * kRec));
-    }
+    for (int sp = 0; sp < active; ++sp) M = fmaxf(M, s_wm[sp][g]);
     double den = 0.0;
     float num = 0.f;
-    for (int sp = 0; sp < p.n_splits; ++sp) {
-      const float* rec = p.part + (static_cast<int64_t>(h * p.n_splits + sp) * G + g) * kRec;
-      const float ms = __ldcg(rec);
+#pragma unroll 4
+    for (int sp = 0; sp < active; ++sp) {
+      const float ms = s_wm[sp][g];
       const float w = ms == -INFINITY ? 0.f : expf(ms - M);
-      den += static_cast<double>(w) * static_cast<double>(__ldcg(rec + 1));
-      num = fmaf(w, __ldcg(rec + 2 + tid), num);
+      den += static_cast<double>(w) * s_wl[sp][g];
+      num = fmaf(w, __ldcg(p.part + (static_cast<int64_t>(h * p.n_splits + sp) * G + g) * kRec + 2 + tid), num);
+    }
+    p.out[(h * G + g) * D + tid] = num * static_cast<float>(1.0 / den);
+  }
+  if (tid == 0) p.ticket[h] = 0u;
+}
+
+}  // namespace
+
+namespace {
+
+// ---- decode attention with the split's K/V staged in shared memory
+//
+// Block (split s, KV head h): positions [128 s, min(128 s + 128, L)).  Rows
+// below the current position were written by earlier steps, so thread 0
+// requests them with two 1-D TMA bulk copies before griddepcontrol.wait; the
+// current row is normalised, rotated and written by this kernel itself.
+// Scores: thread = position, the 16-byte chunks of the key row visited in a
+// per-thread rotated order (conflict-free shared loads).  V: thread = dimension.
+constexpr int kSP = kAttnSplitPositions;
+constexpr size_t kAttnDynSmem = 2 * static_cast<size_t>(kSP) * D * sizeof(__half) + 16;
+
+template <int G>
+__global__ void __launch_bounds__(128) AttnDecodeKernel(const AttnParams p) {
+  extern __shared__ __align__(128) uint8_t dsm[];
+  __half* Ks = reinterpret_cast<__half*>(dsm);
+  __half* Vs = Ks + kSP * D;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(Vs + kSP * D);
+  __shared__ __align__(16) float qs[G + 1][D];
+  __shared__ float sc[G][kSP];
+  __shared__ double dsh[4 * (G + 1)];
+  __shared__ float fsh[4 * G];
+  __shared__ float s_wm[kMaxSplits][G];
+  __shared__ double s_wl[kMaxSplits][G];
+  __shared__ int s_last;
+
+  dev::TraceScope trace(p.trace);
+  const int s = blockIdx.x, h = blockIdx.y;
+  const int tid = threadIdx.x;
+  // The position counter of this step was written before the step started
+  // (previous graph launch / host copy), so it may be read before the wait.
+  const int64_t pos = *p.pos;
+  const int64_t L = pos + 1;
+  const int active = static_cast<int>((L + kSP - 1) / kSP);
+  if (s >= active) return;  // nothing to do at this length (no memory touched)
+  const int64_t p0 = static_cast<int64_t>(s) * kSP;
+  const int n = static_cast<int>(p1_of(p0, L));
+  const int q_dim = p.n_heads * D;
+  __half* kbase = p.kc + static_cast<int64_t>(h) * p.max_seq * D;
+  __half* vbase = p.vc + static_cast<int64_t>(h) * p.max_seq * D;
+  const int n_old = static_cast<int>(pos - p0 < n ? pos - p0 : n);  // rows already in the cache
+
+  if (tid == 0) {
+    dev::MbarInit(bar, 1);
+    dev::MbarInitFence();
+    if (n_old > 0) {
+      const uint32_t bytes = static_cast<uint32_t>(n_old) * D * 2;
+      dev::MbarExpectTx(bar, 2 * bytes);
+      dev::BulkG2S(Ks, kbase + p0 * D, bytes, bar);
+      dev::BulkG2S(Vs, vbase + p0 * D, bytes, bar);
+    }
+  }
+  __syncthreads();
+  dev::GridLaunchDependents();
+  dev::GridWait();
+  trace.Ready();
+
+  // ---- q heads and the new key: RMSNorm + RoPE in one pass
+  {
+    float vk[G + 1];
+    const float* ws[G + 1];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      vk[g] = p.q[(h * G + g) * D + tid];
+      ws[g] = p.q_norm;
+    }
+    vk[G] = p.k_raw[h * D + tid];
+    ws[G] = p.k_norm;
+    const float vv = p.v_raw[h * D + tid];
+    NormRopeW<G + 1>(vk, ws, p.eps, p.rope + pos * D, qs, dsh);
+    if (n_old < n) {  // this split owns the new position (fp16, RNE)
+      const __half kh = __float2half_rn(vk[G]), vh = __float2half_rn(vv);
+      kbase[pos * D + tid] = kh;
+      vbase[pos * D + tid] = vh;
+      Ks[n_old * D + tid] = kh;
+      Vs[n_old * D + tid] = vh;
+    }
+  }
+  if (n_old > 0) {
+    bool ok = dev::MbarWait(bar, 0);
+    if (!ok) {
+      if (tid == 0 && p.err != nullptr) atomicOr(p.err, 2u);
+      dev::MbarWait(bar, 0);  // give the copy one more bounded chance before the buffer is read
+    }
+  }
+  __syncthreads();
+
+  // ---- scores: thread = position
+  float sg[G];
+  if (tid < n) {
+    float dot[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) dot[g] = 0.f;
+    const uint4* kr = reinterpret_cast<const uint4*>(Ks + tid * D);
+#pragma unroll 4
+    for (int i = 0; i < D / 8; ++i) {
+      const int c = (i + tid) & (D / 8 - 1);
+      const uint4 kw = kr[c];
+      const __half2* h2 = reinterpret_cast<const __half2*>(&kw);
+      float kf[8];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __half22float2(h2[e]);
+        kf[2 * e] = f.x;
+        kf[2 * e + 1] = f.y;
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float4 qa = *reinterpret_cast<const float4*>(&qs[g][c * 8]);
+        const float4 qb = *reinterpret_cast<const float4*>(&qs[g][c * 8 + 4]);
+        dot[g] = fmaf(qa.x, kf[0], dot[g]);
+        dot[g] = fmaf(qa.y, kf[1], dot[g]);
+        dot[g] = fmaf(qa.z, kf[2], dot[g]);
+        dot[g] = fmaf(qa.w, kf[3], dot[g]);
+        dot[g] = fmaf(qb.x, kf[4], dot[g]);
+        dot[g] = fmaf(qb.y, kf[5], dot[g]);
+        dot[g] = fmaf(qb.z, kf[6], dot[g]);
+        dot[g] = fmaf(qb.w, kf[7], dot[g]);
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) sg[g] = dot[g] * p.scale;
+  } else {
+#pragma unroll
+    for (int g = 0; g < G; ++g) sg[g] = -INFINITY;
+  }
+  float m[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) m[g] = sg[g];
+  BlockMaxG<G>(m, fsh);
+  double l[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const float e = tid < n ? expf(sg[g] - m[g]) : 0.f;
+    sc[g][tid] = e;
+    l[g] = static_cast<double>(e);
+  }
+  BlockSumG<G>(l, dsh);  // its barriers also publish sc[] to all threads
+
+  // ---- V: thread = dimension, two accumulators per head
+  float o[G];
+  {
+    float a0[G], a1[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) a0[g] = a1[g] = 0.f;
+    int j = 0;
+    for (; j + 1 < n; j += 2) {
+      const float v0 = __half2float(Vs[j * D + tid]), v1 = __half2float(Vs[(j + 1) * D + tid]);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        a0[g] = fmaf(sc[g][j], v0, a0[g]);
+        a1[g] = fmaf(sc[g][j + 1], v1, a1[g]);
+      }
+    }
+    if (j < n) {
+      const float v0 = __half2float(Vs[j * D + tid]);
+#pragma unroll
+      for (int g = 0; g < G; ++g) a0[g] = fmaf(sc[g][j], v0, a0[g]);
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) o[g] = a0[g] + a1[g];
+  }
+
+  if (active == 1) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) p.out[(h * G + g) * D + tid] = o[g] * static_cast<float>(1.0 / l[g]);
+    return;
+  }
+
+  // ---- split-K: publish (m, l, acc) and let the last block of this head merge
+  constexpr int kRec = D + 2;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float* rec = p.part + (static_cast<int64_t>(h * p.n_splits + s) * G + g) * kRec;
+    if (tid == 0) {
+      rec[0] = m[g];
+      rec[1] = static_cast<float>(l[g]);
+    }
+    rec[2 + tid] = o[g];
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned tk = atomicAdd(p.ticket + h, 1u);
+    s_last = tk == static_cast<unsigned>(active - 1) ? 1 : 0;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  if (tid < active) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float* rec = p.part + (static_cast<int64_t>(h * p.n_splits + tid) * G + g) * kRec;
+      s_wm[tid][g] = __ldcg(rec);
+      s_wl[tid][g] = static_cast<double>(__ldcg(rec + 1));
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float M = -INFINITY;
+    for (int sp = 0; sp < active; ++sp) M = fmaxf(M, s_wm[sp][g]);
+    double den = 0.0;
+    float num = 0.f;
+#pragma unroll 4
+    for (int sp = 0; sp < active; ++sp) {
+      const float ms = s_wm[sp][g];
+      const float w = ms == -INFINITY ? 0.f : expf(ms - M);
+      den += static_cast<double>(w) * s_wl[sp][g];
+      num = fmaf(w, __ldcg(p.part + (static_cast<int64_t>(h * p.n_splits + sp) * G + g) * kRec + 2 + tid), num);
     }
     p.out[(h * G + g) * D + tid] = num * static_cast<float>(1.0 / den);
   }
@@ -335,13 +592,39 @@ size_t AttentionPartialFloats(int n_kv, int group, int n_splits) {
   return static_cast<size_t>(n_kv) * n_splits * group * (D + 2);
 }
 
+void PrepareAttentionKernels() {
+  const void* fns[4] = {reinterpret_cast<const void*>(AttnDecodeKernel<1>),
+                        reinterpret_cast<const void*>(AttnDecodeKernel<2>),
+                        reinterpret_cast<const void*>(AttnDecodeKernel<4>),
+                        reinterpret_cast<const void*>(AttnDecodeKernel<8>)};
+  for (const void* f : fns) {
+    RPGB_CUDA(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kAttnDynSmem)));
+  }
+}
+
 void LaunchAttention(const AttnParams& p, int n_queries, cudaStream_t s, bool pdl) {
   RPGB_CHECK(n_queries >= 1 && n_queries < 65536, "attention: bad query count %d", n_queries);
   RPGB_CHECK(p.n_splits >= 1 && (p.n_splits == 1 || n_queries == 1), "attention: split-K is decode only");
   RPGB_CHECK(p.n_heads % p.n_kv == 0, "attention: bad head counts");
+  RPGB_CHECK(p.n_splits <= kMaxSplits, "attention: %d splits exceed %d", p.n_splits, kMaxSplits);
   const int G = p.n_heads / p.n_kv;
-  const dim3 grid(p.n_splits, p.n_kv, n_queries);
   const void* fn = nullptr;
+  if (p.fused) {
+    RPGB_CHECK(n_queries == 1, "attention: the fused decode kernel takes one query");
+    RPGB_CHECK(static_cast<int64_t>(p.n_splits) * kSP >= p.max_seq, "attention: %d splits cannot cover %d positions",
+               p.n_splits, p.max_seq);
+    switch (G) {
+      case 1: fn = reinterpret_cast<const void*>(AttnDecodeKernel<1>); break;
+      case 2: fn = reinterpret_cast<const void*>(AttnDecodeKernel<2>); break;
+      case 4: fn = reinterpret_cast<const void*>(AttnDecodeKernel<4>); break;
+      case 8: fn = reinterpret_cast<const void*>(AttnDecodeKernel<8>); break;
+      default: Throw("attention: GQA group %d is not supported (1, 2, 4, 8)", G);
+    }
+    LaunchKernelArgs(fn, dim3(p.n_splits, p.n_kv), dim3(128), kAttnDynSmem, s, pdl, p);
+    CountLaunches(1);
+    return;
+  }
+  const dim3 grid(p.n_splits, p.n_kv, n_queries);
   switch (G) {
     case 1: fn = reinterpret_cast<const void*>(AttnKernel<1>); break;
     case 2: fn = reinterpret_cast<const void*>(AttnKernel<2>); break;

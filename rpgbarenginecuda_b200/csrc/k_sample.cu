@@ -87,27 +87,65 @@ __device__ int BlockArgmax(const float* x, int n, float* fsh, int* ish) {
   return bi == INT_MAX ? 0 : bi;
 }
 
-// Key of the k-th largest element of x[0..n) (multiplicity counted).
+// Warp 0 finds the digit d of the k-th largest key among the histogram's 256
+// bins (bins taken from the top): s_sel = {d, rank of the k-th inside bin d}.
+// Lane L owns bins 8L .. 8L+7; a suffix scan over the lanes replaces a serial
+// 256-step walk.
+__device__ __forceinline__ void SelectBin(const unsigned* hist, int rem, uint32_t* s_sel) {
+  if (threadIdx.x >= 32) return;
+  const int lane = threadIdx.x;
+  unsigned h[8];
+  unsigned sum = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    h[j] = hist[8 * lane + j];
+    sum += h[j];
+  }
+  unsigned incl = sum;  // count of bins >= 8 lane
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned v = __shfl_down_sync(0xFFFFFFFFu, incl, o);
+    if (lane + o < 32) incl += v;
+  }
+  const unsigned excl = incl - sum;  // count of bins >= 8 (lane + 1)
+  const unsigned r = static_cast<unsigned>(rem);
+  if (excl < r && r <= incl) {
+    unsigned cum = excl;
+    int d = 8 * lane;
+#pragma unroll
+    for (int j = 7; j >= 0; --j) {
+      if (cum + h[j] >= r) {
+        d = 8 * lane + j;
+        break;
+      }
+      cum += h[j];
+    }
+    s_sel[0] = static_cast<uint32_t>(d);
+    s_sel[1] = r - cum;
+  }
+}
+
+// Key of the k-th largest element of x[0..n) (multiplicity counted), 1 <= k <= n.
 __device__ uint32_t RadixKth(const float* x, int n, int k, unsigned* hist, uint32_t* s_sel) {
   uint32_t prefix = 0, mask = 0;
   int rem = k;
   for (int shift = 24; shift >= 0; shift -= 8) {
     for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
     __syncthreads();
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-      const uint32_t key = dev::OrderKey(x[i]);
-      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+    // Keys near the k-th share their leading bytes, so most increments hit the
+    // same bin: lanes with equal bins are combined first (one atomic per group).
+    const int n_up = (n + 31) & ~31;
+    for (int i = threadIdx.x; i < n_up; i += blockDim.x) {
+      uint32_t bin = 0xFFFFFFFFu;
+      if (i < n) {
+        const uint32_t key = dev::OrderKey(x[i]);
+        if ((key & mask) == prefix) bin = (key >> shift) & 255u;
+      }
+      const unsigned same = __match_any_sync(0xFFFFFFFFu, bin);
+      if (bin != 0xFFFFFFFFu && (threadIdx.x & 31) == __ffs(same) - 1) atomicAdd(&hist[bin], __popc(same));
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-      int cum = 0, d = 0;
-      for (d = 255; d >= 0; --d) {
-        if (cum + static_cast<int>(hist[d]) >= rem) break;
-        cum += static_cast<int>(hist[d]);
-      }
-      s_sel[0] = static_cast<uint32_t>(d < 0 ? 0 : d);
-      s_sel[1] = static_cast<uint32_t>(rem - cum);
-    }
+    SelectBin(hist, rem, s_sel);
     __syncthreads();
     prefix |= s_sel[0] << shift;
     mask |= 255u << shift;
@@ -343,17 +381,39 @@ __global__ void __launch_bounds__(kSmallThreads) SampleSmallKernel(const SampleP
   dev::GridLaunchDependents();
   dev::GridWait();
   trace.Ready();
-  if (tid == 0) {
-    int off = 0, bad = 0;
-    for (int b = 0; b < kCandBlocks; ++b) {
-      const int c = p.cand_cnt[b];
-      s_off[b] = off;
-      if (c < 0) bad = 1;
-      off += c < 0 ? 0 : c;
+  // candidate counts of the slices -> offsets (warp 0 scans; counts are loaded in parallel)
+  __shared__ int s_cnt[kCandBlocks];
+  for (int b = tid; b < kCandBlocks; b += kSmallThreads) s_cnt[b] = p.cand_cnt[b];
+  __syncthreads();
+  if (tid < 32) {
+    constexpr int kPer = (kCandBlocks + 31) / 32;
+    int c[kPer], sum = 0, bad = 0;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int b = tid * kPer + j;
+      c[j] = b < kCandBlocks ? s_cnt[b] : 0;
+      bad |= c[j] < 0;
+      sum += c[j] < 0 ? 0 : c[j];
     }
-    s_off[kCandBlocks] = off;
-    s_bad = bad;
-    s_m = off;
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (tid >= o) incl += v;
+    }
+    int off = incl - sum;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int b = tid * kPer + j;
+      if (b < kCandBlocks) s_off[b] = off;
+      off += c[j] < 0 ? 0 : c[j];
+    }
+    bad = __any_sync(0xFFFFFFFFu, bad);
+    if (tid == 31) {
+      s_off[kCandBlocks] = incl;
+      s_m = incl;
+    }
+    if (tid == 0) s_bad = bad;
   }
   __syncthreads();
   if (s_bad) {
@@ -362,13 +422,14 @@ __global__ void __launch_bounds__(kSmallThreads) SampleSmallKernel(const SampleP
   }
   const int m = s_m;
   const float inv_t = 1.0f / p.temperature;
-  for (int b = 0; b < kCandBlocks; ++b) {
-    const int c = s_off[b + 1] - s_off[b];
-    for (int i = tid; i < c; i += kSmallThreads) {
-      float v = p.cand_val[b * kFastTopK + i];
+  // gather all slices at once (one pass, independent loads)
+  for (int j = tid; j < kCandBlocks * kFastTopK; j += kSmallThreads) {
+    const int b = j / kFastTopK, i = j - b * kFastTopK;
+    if (i < s_off[b + 1] - s_off[b]) {
+      float v = p.cand_val[j];
       if (p.temperature != 1.0f) v *= inv_t;
       cv[s_off[b] + i] = v;
-      ci[s_off[b] + i] = p.cand_idx[b * kFastTopK + i];
+      ci[s_off[b] + i] = p.cand_idx[j];
     }
   }
   __syncthreads();
@@ -397,18 +458,27 @@ __global__ void __launch_bounds__(kSmallThreads) SampleSmallKernel(const SampleP
   float* v = cv;  // probabilities, index-ordered
   const int* ix = ci;
   __shared__ int s_forced;
-  if (tid == 0) {
+  __shared__ float s_mx;
+  __shared__ double s_sum;
+  if (tid < 32) {
     float mx = -INFINITY;
-    for (int i = 0; i < c; ++i) mx = fmaxf(mx, v[i]);
+    for (int i = tid; i < c; i += 32) mx = fmaxf(mx, v[i]);
+    mx = dev::WarpMax(mx);
+    if (tid == 0) s_mx = mx;
+  }
+  __syncthreads();
+  for (int i = tid; i < c; i += kSmallThreads) v[i] = expf(v[i] - s_mx);
+  __syncthreads();
+  if (tid == 0) {  // double sum in index order, as the serial reference loop
     double sum = 0.0;
-    for (int i = 0; i < c; ++i) {
-      const float e = expf(v[i] - mx);
-      v[i] = e;
-      sum += static_cast<double>(e);
-    }
-    const float inv = static_cast<float>(1.0 / sum);
-    for (int i = 0; i < c; ++i) v[i] *= inv;
+    for (int i = 0; i < c; ++i) sum += static_cast<double>(v[i]);
+    s_sum = sum;
     s_forced = 0;
+  }
+  __syncthreads();
+  {
+    const float inv = static_cast<float>(1.0 / s_sum);
+    for (int i = tid; i < c; i += kSmallThreads) v[i] *= inv;
   }
   __syncthreads();
   if (p.top_p > 0.0f && p.top_p < 1.0f) {

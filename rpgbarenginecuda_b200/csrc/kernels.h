@@ -111,9 +111,15 @@ struct AttnParams {
   uint32_t* ticket = nullptr;  // [n_kv]
   int32_t n_splits = 1;
   int32_t fused = 0;  // 1: decode (norm + rope + cache write of the current token inside)
+  unsigned* err = nullptr;  // decode: set when a bounded wait for the staged K/V gave up
   Trace trace;
 };
+// Decode (fused, n_queries == 1) uses one block per (128-position split, KV
+// head) with the cached K/V rows staged into shared memory by TMA before the
+// programmatic wait; n_splits must be >= ceil(max_seq / 128).
+constexpr int kAttnSplitPositions = 128;
 void LaunchAttention(const AttnParams& p, int n_queries, cudaStream_t s, bool pdl = false);
+void PrepareAttentionKernels();
 size_t AttentionPartialFloats(int n_kv, int group, int n_splits);
 
 // Prefill helpers: per-head RMSNorm + RoPE for q and k, fp16 cache write of k and v.

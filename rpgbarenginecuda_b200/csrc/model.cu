@@ -251,6 +251,7 @@ std::unique_ptr<Model> Model::Load(const std::string& path, int device, int32_t 
   RPGB_CUDA(cudaDeviceGetAttribute(&m->num_sms_, cudaDevAttrMultiProcessorCount, device));
   PrepareMatvecKernels();
   PrepareSampleKernels();
+  PrepareAttentionKernels();
 
   auto require = [&](const std::string& name) -> const GgufTensor& {
     const GgufTensor* t = g.Find(name);
