@@ -13,8 +13,8 @@
 //    nibble for the high half; Q6_K 6-bit value, or 4x it), unpacked from the
 //    block group with one or two logical ops per 4 weights;
 //  * x is split per 256-column super-block into four signed 8-bit digits,
-//    x = s * (x0 + x1/64 + x2/8192 + x3/2^20), s a power of two, which is
-//    exact to 2^-27 of the super-block's largest |x|.  The digits are the
+//    x = s * (x0 + x1/64 + x2/8192 + x3/2^20), s a power of two with
+//    |x / s| < 64, exact to 2^-26 of the super-block's largest |x|.  The digits are the
 //    columns of the B operand: columns 0-3 carry the digits of the first 16
 //    positions of an MMA, columns 4-7 those of the next sub-block half, so one
 //    MMA yields two sub-block partial sums;
@@ -338,29 +338,31 @@ __global__ void __launch_bounds__(kThreads, 2) MatvecKernel(const MvParams p) {
     }
     mx = dev::WarpMax(mx);
     const int E = static_cast<int>((__float_as_uint(mx) >> 23) & 0xFFu);
-    // s = 2^(e(mx) - 6): |x / s| < 128 and the leading digit is a truncation.
-    float s = 0.f, inv = 0.f;
-    if (E >= 8 && E < 255) {
-      s = __uint_as_float(static_cast<uint32_t>(E - 6) << 23);
-      inv = __uint_as_float(static_cast<uint32_t>(254 - (E - 6)) << 23);
+    // s = 2^(e(mx) - 5) so |x / s| < 64; Y = round(x / s * 2^20) splits
+    // exactly into balanced digits x0 (|x0| <= 64), x1 (6 bits), x2, x3 (7 bits).
+    float s = 0.f, inv20 = 0.f;
+    if (E >= 25 && E < 255) {
+      s = __uint_as_float(static_cast<uint32_t>(E - 5) << 23);
+      inv20 = __uint_as_float(static_cast<uint32_t>(279 - E) << 23);
     }
-    uint32_t dw[4][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}, {0u, 0u}};
+    int d0[8], d1[8], d2[8], d3[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float y = v[i] * inv;
-      const float x0 = truncf(y);
-      const float r1 = (y - x0) * 64.f;
-      const float x1 = rintf(r1);
-      const float r2 = (r1 - x1) * 128.f;
-      const float x2 = rintf(r2);
-      const float r3 = (r2 - x2) * 128.f;
-      const float x3 = rintf(r3);
-      const int sh = 8 * (i & 3);
-      dw[0][i >> 2] |= (static_cast<uint32_t>(static_cast<int>(x0)) & 0xFFu) << sh;
-      dw[1][i >> 2] |= (static_cast<uint32_t>(static_cast<int>(x1)) & 0xFFu) << sh;
-      dw[2][i >> 2] |= (static_cast<uint32_t>(static_cast<int>(x2)) & 0xFFu) << sh;
-      dw[3][i >> 2] |= (static_cast<uint32_t>(static_cast<int>(x3)) & 0xFFu) << sh;
+      int Y = __float2int_rn(v[i] * inv20);
+      d3[i] = (Y << 25) >> 25;
+      Y = (Y - d3[i]) >> 7;
+      d2[i] = (Y << 25) >> 25;
+      Y = (Y - d2[i]) >> 7;
+      d1[i] = (Y << 26) >> 26;
+      d0[i] = (Y - d1[i]) >> 6;
     }
+    auto pack = [](int a, int b, int c, int d) {
+      return __byte_perm(__byte_perm(a, b, 0x0040u), __byte_perm(c, d, 0x0040u), 0x5410u);
+    };
+    const uint32_t dw[4][2] = {{pack(d0[0], d0[1], d0[2], d0[3]), pack(d0[4], d0[5], d0[6], d0[7])},
+                               {pack(d1[0], d1[1], d1[2], d1[3]), pack(d1[4], d1[5], d1[6], d1[7])},
+                               {pack(d2[0], d2[1], d2[2], d2[3]), pack(d2[4], d2[5], d2[6], d2[7])},
+                               {pack(d3[0], d3[1], d3[2], d3[3]), pack(d3[4], d3[5], d3[6], d3[7])}};
     // positions 8 lane .. 8 lane + 7 = 64c + 32hb + 16h + 8(lane & 1) + i
     const int c = lane >> 3, hb = (lane >> 2) & 1, h = (lane >> 1) & 1, tb = 2 * (lane & 1);
     const int m = 2 * c + h;

@@ -344,7 +344,20 @@ __global__ void __launch_bounds__(kCandThreads) CandKernel(const SampleParams p)
   const int per = (n + kCandBlocks - 1) / kCandBlocks;
   const int a = blockIdx.x * per;
   const int len = a < n ? min(per, n - a) : 0;
-  for (int i = threadIdx.x; i < len; i += kCandThreads) vals[i] = p.logits[a + i];
+  {
+    constexpr int kR = kSliceMax / kCandThreads;
+    float lv[kR];
+#pragma unroll
+    for (int r = 0; r < kR; ++r) {
+      const int i = threadIdx.x + r * kCandThreads;
+      lv[r] = i < len ? p.logits[a + i] : 0.f;
+    }
+#pragma unroll
+    for (int r = 0; r < kR; ++r) {
+      const int i = threadIdx.x + r * kCandThreads;
+      if (i < len) vals[i] = lv[r];
+    }
+  }
   if (threadIdx.x == 0) s_cnt = 0;
   __syncthreads();
   const int k = p.top_k;
@@ -422,14 +435,30 @@ __global__ void __launch_bounds__(kSmallThreads) SampleSmallKernel(const SampleP
   }
   const int m = s_m;
   const float inv_t = 1.0f / p.temperature;
-  // gather all slices at once (one pass, independent loads)
-  for (int j = tid; j < kCandBlocks * kFastTopK; j += kSmallThreads) {
-    const int b = j / kFastTopK, i = j - b * kFastTopK;
-    if (i < s_off[b + 1] - s_off[b]) {
-      float v = p.cand_val[j];
-      if (p.temperature != 1.0f) v *= inv_t;
-      cv[s_off[b] + i] = v;
-      ci[s_off[b] + i] = p.cand_idx[j];
+  // gather all slices at once: every thread first issues all of its loads
+  // (independent, so their latencies overlap), then stores
+  {
+    constexpr int kSlots = (kCandBlocks * kFastTopK + kSmallThreads - 1) / kSmallThreads;
+    float vv[kSlots];
+    int vi[kSlots];
+#pragma unroll
+    for (int r = 0; r < kSlots; ++r) {
+      const int j = tid + r * kSmallThreads;
+      const int b = j / kFastTopK, i = j - b * kFastTopK;
+      const bool use = j < kCandBlocks * kFastTopK && i < s_off[b + 1] - s_off[b];
+      vv[r] = use ? __ldcg(p.cand_val + j) : 0.f;
+      vi[r] = use ? __ldcg(p.cand_idx + j) : -1;
+    }
+#pragma unroll
+    for (int r = 0; r < kSlots; ++r) {
+      const int j = tid + r * kSmallThreads;
+      if (vi[r] >= 0) {
+        const int b = j / kFastTopK, i = j - b * kFastTopK;
+        float v = vv[r];
+        if (p.temperature != 1.0f) v *= inv_t;
+        cv[s_off[b] + i] = v;
+        ci[s_off[b] + i] = vi[r];
+      }
     }
   }
   __syncthreads();

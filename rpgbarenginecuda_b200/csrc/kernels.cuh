@@ -141,16 +141,19 @@ __device__ __forceinline__ void PrefetchL2(const void* src, uint32_t bytes) {
 __device__ __forceinline__ void FenceProxyAsync() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ bool MbarTryWait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
+  // The suspend-time hint (ns) lets a waiting warp sleep until the phase
+  // completes instead of re-issuing the test, which frees issue slots for
+  // the warps that have data.
   asm volatile(
-      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
       : "=r"(ok)
-      : "r"(SmemAddr(bar)), "r"(parity)
+      : "r"(SmemAddr(bar)), "r"(parity), "r"(20000u)
       : "memory");
   return ok != 0;
 }
-// Bounded wait (each try_wait suspends for a hardware-bounded time): returns
-// false after `limit` attempts instead of spinning forever.
-__device__ __forceinline__ bool MbarWait(uint64_t* bar, uint32_t parity, uint32_t limit = 1u << 22) {
+// Bounded wait: returns false after `limit` attempts (each suspends for at
+// most ~20 us) instead of waiting forever.
+__device__ __forceinline__ bool MbarWait(uint64_t* bar, uint32_t parity, uint32_t limit = 1u << 16) {
   for (uint32_t i = 0; i < limit; ++i) {
     if (MbarTryWait(bar, parity)) return true;
   }
