@@ -62,7 +62,12 @@ Session::Session(const Model* m, int64_t max_seq) : m_(m), max_seq_(max_seq) {
   RPGB_CUDA(cudaMemsetAsync(kc_, 0, kv_bytes, stream_));
   RPGB_CUDA(cudaMemsetAsync(vc_, 0, kv_bytes, stream_));
 
-  n_splits_ = static_cast<int>(std::max<int64_t>(1, (max_seq + kPositionsPerSplit - 1) / kPositionsPerSplit));
+  // about one attention block per SM at full length, never more stages than positions
+  {
+    const int64_t stages = (max_seq + kPositionsPerSplit - 1) / kPositionsPerSplit;
+    const int64_t per_head = std::max(1, m->num_sms() / c.n_kv_heads);
+    n_splits_ = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({stages, per_head, kMaxAttnSplits})));
+  }
   const int am_grid = MatvecGrid(c.vocab, 4, m->num_sms());
   const int qkv = c.q_dim() + 2 * c.kv_dim();
   Carver cv;

@@ -94,12 +94,8 @@ __device__ __forceinline__ void NormRope(float (&v)[G], const float* __restrict_
 // Positions per split at least this many: short contexts run one split per
 // KV head and skip the merge.
 constexpr int64_t kMinSplit = 256;
-constexpr int kMaxSplits = 64;
+constexpr int kMaxSplits = kMaxAttnSplits;
 
-// Positions of the split starting at p0: min(128, L - p0).
-__device__ __forceinline__ int64_t p1_of(int64_t p0, int64_t L) {
-  return L - p0 < kAttnSplitPositions ? L - p0 : kAttnSplitPositions;
-}
 
 template <int G>
 __global__ void __launch_bounds__(128) AttnKernel(const AttnParams p) {
@@ -329,182 +325,332 @@ namespace {
 
 // ---- decode attention with the split's K/V staged in shared memory
 //
-// Block (split s, KV head h): positions [128 s, min(128 s + 128, L)).  Rows
-// below the current position were written by earlier steps, so thread 0
-// requests them with two 1-D TMA bulk copies before griddepcontrol.wait; the
-// current row is normalised, rotated and written by this kernel itself.
-// Scores: thread = position, the 16-byte chunks of the key row visited in a
-// per-thread rotated order (conflict-free shared loads).  V: thread = dimension.
+// Block (split s, KV head h), 8 warps, owns a run of 128-position stages; the
+// number of splits is bounded by the engine (about one block per SM), so
+// long contexts give each block several stages, processed with an online
+// softmax.  K and V of a stage arrive by two 1-D TMA bulk copies into single
+// K / V buffers: the first stage is requested before griddepcontrol.wait
+// (rows below the current position were written by earlier steps), the next
+// stage's K as soon as the scores of the current stage are done, its V after
+// the V pass.  The current position's row is normalised, rotated and written
+// by this kernel.  Scores and V: warp w takes positions w, w + 8, ...; lane l
+// holds dimensions 4l .. 4l+3 (8-byte row loads, a warp reads a whole row),
+// so the positions of a warp are independent chains; the per-warp V partials
+// are combined once at the end.
 constexpr int kSP = kAttnSplitPositions;
-constexpr size_t kAttnDynSmem = 2 * static_cast<size_t>(kSP) * D * sizeof(__half) + 16;
+constexpr int kAT = 256;  // threads of the decode attention block
+constexpr int kAW = kAT / 32;
+
+__host__ __device__ constexpr size_t AttnDynSmem(int G) {
+  return 2 * static_cast<size_t>(kSP) * D * sizeof(__half) + static_cast<size_t>(kAW) * G * D * sizeof(float) + 16;
+}
 
 template <int G>
-__global__ void __launch_bounds__(128) AttnDecodeKernel(const AttnParams p) {
+__device__ __forceinline__ void BlockMax8(float (&v)[G], float* sh) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    v[g] = dev::WarpMax(v[g]);
+    if (lane == 0) sh[warp * G + g] = v[g];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float m = sh[g];
+#pragma unroll
+    for (int w = 1; w < kAW; ++w) m = fmaxf(m, sh[w * G + g]);
+    v[g] = m;
+  }
+}
+
+template <int G>
+__device__ __forceinline__ void BlockSum8(double (&v)[G], double* sh) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    v[g] = dev::WarpSumD(v[g]);
+    if (lane == 0) sh[warp * G + g] = v[g];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    double t = sh[g];
+#pragma unroll
+    for (int w = 1; w < kAW; ++w) t += sh[w * G + g];
+    v[g] = t;
+  }
+}
+
+template <int G>
+__global__ void __launch_bounds__(kAT) AttnDecodeKernel(const AttnParams p) {
   extern __shared__ __align__(128) uint8_t dsm[];
   __half* Ks = reinterpret_cast<__half*>(dsm);
   __half* Vs = Ks + kSP * D;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(Vs + kSP * D);
+  float* vred = reinterpret_cast<float*>(Vs + kSP * D);  // [kAW][G][D]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(vred + kAW * G * D);  // [0] K, [1] V
   __shared__ __align__(16) float qs[G + 1][D];
   __shared__ float sc[G][kSP];
-  __shared__ double dsh[4 * (G + 1)];
-  __shared__ float fsh[4 * G];
+  __shared__ double dsh[kAW * (G + 1)];
+  __shared__ float fsh[kAW * G];
   __shared__ float s_wm[kMaxSplits][G];
   __shared__ double s_wl[kMaxSplits][G];
   __shared__ int s_last;
 
   dev::TraceScope trace(p.trace);
   const int s = blockIdx.x, h = blockIdx.y;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   // The position counter of this step was written before the step started
   // (previous graph launch / host copy), so it may be read before the wait.
   const int64_t pos = *p.pos;
   const int64_t L = pos + 1;
-  const int active = static_cast<int>((L + kSP - 1) / kSP);
+  const int stages = static_cast<int>((L + kSP - 1) / kSP);
+  const int per = (stages + p.n_splits - 1) / p.n_splits;  // stages per split
+  const int active = (stages + per - 1) / per;
   if (s >= active) return;  // nothing to do at this length (no memory touched)
-  const int64_t p0 = static_cast<int64_t>(s) * kSP;
-  const int n = static_cast<int>(p1_of(p0, L));
-  const int q_dim = p.n_heads * D;
+  const int st0 = s * per, st1 = st0 + per < stages ? st0 + per : stages;
   __half* kbase = p.kc + static_cast<int64_t>(h) * p.max_seq * D;
   __half* vbase = p.vc + static_cast<int64_t>(h) * p.max_seq * D;
-  const int n_old = static_cast<int>(pos - p0 < n ? pos - p0 : n);  // rows already in the cache
+  // rows of stage st already in the cache (below the current position)
+  auto old_rows = [&](int st) -> int {
+    const int64_t r = pos - static_cast<int64_t>(st) * kSP;
+    return static_cast<int>(r < kSP ? r : kSP);
+  };
+  auto issue = [&](int which, int st) {  // thread 0 only
+    const int n_old = old_rows(st);
+    if (n_old <= 0) return;
+    const uint32_t bytes = static_cast<uint32_t>(n_old) * D * 2;
+    __half* src = (which == 0 ? kbase : vbase) + static_cast<int64_t>(st) * kSP * D;
+    dev::MbarExpectTx(bars + which, bytes);
+    dev::BulkG2S(which == 0 ? Ks : Vs, src, bytes, bars + which);
+  };
 
   if (tid == 0) {
-    dev::MbarInit(bar, 1);
+    dev::MbarInit(bars + 0, 1);
+    dev::MbarInit(bars + 1, 1);
     dev::MbarInitFence();
-    if (n_old > 0) {
-      const uint32_t bytes = static_cast<uint32_t>(n_old) * D * 2;
-      dev::MbarExpectTx(bar, 2 * bytes);
-      dev::BulkG2S(Ks, kbase + p0 * D, bytes, bar);
-      dev::BulkG2S(Vs, vbase + p0 * D, bytes, bar);
-    }
+    issue(0, st0);
+    issue(1, st0);
   }
+  // constants of this step (norm weights, the RoPE row of pos): before the wait
+  const bool dimt = tid < D;
+  const float wq = dimt ? p.q_norm[tid] : 0.f, wk = dimt ? p.k_norm[tid] : 0.f;
+  const float rc = tid < D / 2 ? p.rope[pos * D + tid] : 0.f, rs = tid < D / 2 ? p.rope[pos * D + D / 2 + tid] : 0.f;
   __syncthreads();
   dev::GridLaunchDependents();
   dev::GridWait();
   trace.Ready();
 
-  // ---- q heads and the new key: RMSNorm + RoPE in one pass
+  // ---- q heads and the new key: RMSNorm + RoPE (threads 0..127 = dimensions)
+  __half kh = __float2half_rn(0.f), vh = kh;
   {
     float vk[G + 1];
-    const float* ws[G + 1];
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      vk[g] = p.q[(h * G + g) * D + tid];
-      ws[g] = p.q_norm;
+    for (int g = 0; g < G; ++g) vk[g] = dimt ? p.q[(h * G + g) * D + tid] : 0.f;
+    vk[G] = dimt ? p.k_raw[h * D + tid] : 0.f;
+    const float vv = dimt ? p.v_raw[h * D + tid] : 0.f;
+    double ss[G + 1];
+#pragma unroll
+    for (int g = 0; g <= G; ++g) ss[g] = static_cast<double>(vk[g]) * vk[g];
+    BlockSum8<G + 1>(ss, dsh);
+    if (dimt) {
+#pragma unroll
+      for (int g = 0; g <= G; ++g) {
+        const float scale = static_cast<float>(1.0 / sqrt(ss[g] / static_cast<double>(D) + static_cast<double>(p.eps)));
+        qs[g][tid] = vk[g] * scale * (g < G ? wq : wk);
+      }
     }
-    vk[G] = p.k_raw[h * D + tid];
-    ws[G] = p.k_norm;
-    const float vv = p.v_raw[h * D + tid];
-    NormRopeW<G + 1>(vk, ws, p.eps, p.rope + pos * D, qs, dsh);
-    if (n_old < n) {  // this split owns the new position (fp16, RNE)
-      const __half kh = __float2half_rn(vk[G]), vh = __float2half_rn(vv);
-      kbase[pos * D + tid] = kh;
-      vbase[pos * D + tid] = vh;
-      Ks[n_old * D + tid] = kh;
-      Vs[n_old * D + tid] = vh;
+    __syncthreads();
+    if (tid < D / 2) {
+      const float c = rc, sn = rs;
+#pragma unroll
+      for (int g = 0; g <= G; ++g) {
+        const float a = qs[g][tid], b = qs[g][tid + D / 2];
+        qs[g][tid] = a * c - b * sn;
+        qs[g][tid + D / 2] = b * c + a * sn;
+      }
+    }
+    __syncthreads();
+    if (dimt) {
+      kh = __float2half_rn(qs[G][tid]);
+      vh = __float2half_rn(vv);
+      if (pos < static_cast<int64_t>(st1) * kSP) {  // this block owns the new position (fp16, RNE)
+        kbase[pos * D + tid] = kh;
+        vbase[pos * D + tid] = vh;
+      }
     }
   }
-  if (n_old > 0) {
-    bool ok = dev::MbarWait(bar, 0);
-    if (!ok) {
-      if (tid == 0 && p.err != nullptr) atomicOr(p.err, 2u);
-      dev::MbarWait(bar, 0);  // give the copy one more bounded chance before the buffer is read
-    }
-  }
-  __syncthreads();
+  trace.Mark(1);  // q/k normalised and rotated
 
-  // ---- scores: thread = position
-  float sg[G];
-  if (tid < n) {
-    float dot[G];
+  // scores: 8 lanes per position (4 positions per warp pass); lane sub = lane & 7
+  // holds dimensions 8 sub .. 8 sub + 7 and 64 + 8 sub .. +7 of every query head
+  const int sub = lane & 7, pp = lane >> 3;
+  float qv[G][16];
 #pragma unroll
-    for (int g = 0; g < G; ++g) dot[g] = 0.f;
-    const uint4* kr = reinterpret_cast<const uint4*>(Ks + tid * D);
-#pragma unroll 4
-    for (int i = 0; i < D / 8; ++i) {
-      const int c = (i + tid) & (D / 8 - 1);
-      const uint4 kw = kr[c];
-      const __half2* h2 = reinterpret_cast<const __half2*>(&kw);
-      float kf[8];
+  for (int g = 0; g < G; ++g) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __half22float2(h2[e]);
-        kf[2 * e] = f.x;
-        kf[2 * e + 1] = f.y;
-      }
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float4 qa = *reinterpret_cast<const float4*>(&qs[g][c * 8]);
-        const float4 qb = *reinterpret_cast<const float4*>(&qs[g][c * 8 + 4]);
-        dot[g] = fmaf(qa.x, kf[0], dot[g]);
-        dot[g] = fmaf(qa.y, kf[1], dot[g]);
-        dot[g] = fmaf(qa.z, kf[2], dot[g]);
-        dot[g] = fmaf(qa.w, kf[3], dot[g]);
-        dot[g] = fmaf(qb.x, kf[4], dot[g]);
-        dot[g] = fmaf(qb.y, kf[5], dot[g]);
-        dot[g] = fmaf(qb.z, kf[6], dot[g]);
-        dot[g] = fmaf(qb.w, kf[7], dot[g]);
-      }
+    for (int hf = 0; hf < 2; ++hf) {
+      const float4 qa = *reinterpret_cast<const float4*>(&qs[g][64 * hf + 8 * sub]);
+      const float4 qb = *reinterpret_cast<const float4*>(&qs[g][64 * hf + 8 * sub + 4]);
+      qv[g][8 * hf + 0] = qa.x * p.scale;
+      qv[g][8 * hf + 1] = qa.y * p.scale;
+      qv[g][8 * hf + 2] = qa.z * p.scale;
+      qv[g][8 * hf + 3] = qa.w * p.scale;
+      qv[g][8 * hf + 4] = qb.x * p.scale;
+      qv[g][8 * hf + 5] = qb.y * p.scale;
+      qv[g][8 * hf + 6] = qb.z * p.scale;
+      qv[g][8 * hf + 7] = qb.w * p.scale;
     }
-#pragma unroll
-    for (int g = 0; g < G; ++g) sg[g] = dot[g] * p.scale;
-  } else {
-#pragma unroll
-    for (int g = 0; g < G; ++g) sg[g] = -INFINITY;
   }
-  float m[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) m[g] = sg[g];
-  BlockMaxG<G>(m, fsh);
+  float m[G], acc[G][4];
   double l[G];
 #pragma unroll
   for (int g = 0; g < G; ++g) {
-    const float e = tid < n ? expf(sg[g] - m[g]) : 0.f;
-    sc[g][tid] = e;
-    l[g] = static_cast<double>(e);
+    m[g] = -INFINITY;
+    l[g] = 0.0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[g][e] = 0.f;
   }
-  BlockSumG<G>(l, dsh);  // its barriers also publish sc[] to all threads
+  for (int st = st0; st < st1; ++st) {
+    const uint32_t par = static_cast<uint32_t>((st - st0) & 1);
+    const int n_old = old_rows(st);
+    const int n = static_cast<int>(L - static_cast<int64_t>(st) * kSP < kSP ? L - static_cast<int64_t>(st) * kSP : kSP);
+    if (n_old > 0 && !dev::MbarWait(bars + 0, par)) {
+      if (tid == 0 && p.err != nullptr) atomicOr(p.err, 2u);
+    }
+    if (n_old < n && tid < D) Ks[n_old * D + tid] = kh;  // the current position (last stage only)
+    __syncthreads();
 
-  // ---- V: thread = dimension, two accumulators per head
-  float o[G];
-  {
-    float a0[G], a1[G];
+    // ---- scores: warp w, positions w + 8 (4 t + pp) (independent per position)
+#pragma unroll 2
+    for (int t = 0; t < kSP / (4 * kAW); ++t) {
+      const int j = warp + kAW * (4 * t + pp);
+      float d[G];
 #pragma unroll
-    for (int g = 0; g < G; ++g) a0[g] = a1[g] = 0.f;
-    int j = 0;
-    for (; j + 1 < n; j += 2) {
-      const float v0 = __half2float(Vs[j * D + tid]), v1 = __half2float(Vs[(j + 1) * D + tid]);
+      for (int g = 0; g < G; ++g) d[g] = 0.f;
+      if (j < n) {
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        a0[g] = fmaf(sc[g][j], v0, a0[g]);
-        a1[g] = fmaf(sc[g][j + 1], v1, a1[g]);
+        for (int hf = 0; hf < 2; ++hf) {
+          const uint4 raw = *reinterpret_cast<const uint4*>(Ks + j * D + 64 * hf + 8 * sub);
+          const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __half22float2(h2[e]);
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+              d[g] = fmaf(qv[g][8 * hf + 2 * e], f.x, d[g]);
+              d[g] = fmaf(qv[g][8 * hf + 2 * e + 1], f.y, d[g]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) d[g] += __shfl_xor_sync(0xFFFFFFFFu, d[g], o);
+      }
+      if (sub == 0 && j < n) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) sc[g][j] = d[g];
       }
     }
-    if (j < n) {
-      const float v0 = __half2float(Vs[j * D + tid]);
-#pragma unroll
-      for (int g = 0; g < G; ++g) a0[g] = fmaf(sc[g][j], v0, a0[g]);
+    __syncthreads();  // scores published; all reads of Ks done
+    if (tid == 0 && st + 1 < st1) {
+      dev::FenceProxyAsync();
+      issue(0, st + 1);
     }
+    float cm[G];
 #pragma unroll
-    for (int g = 0; g < G; ++g) o[g] = a0[g] + a1[g];
+    for (int g = 0; g < G; ++g) cm[g] = tid < n ? sc[g][tid] : -INFINITY;
+    BlockMax8<G>(cm, fsh);
+    double cs[G];
+    float alpha[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float nm = fmaxf(m[g], cm[g]);
+      float e = 0.f;
+      if (tid < n) {
+        e = expf(sc[g][tid] - nm);
+      }
+      cs[g] = static_cast<double>(e);
+      alpha[g] = m[g] == -INFINITY ? 0.f : expf(m[g] - nm);
+      m[g] = nm;
+      if (tid < kSP) sc[g][tid] = e;  // own slot only: no other thread reads it before the barrier below
+    }
+    if (n_old > 0 && !dev::MbarWait(bars + 1, par)) {
+      if (tid == 0 && p.err != nullptr) atomicOr(p.err, 2u);
+    }
+    if (n_old < n && tid < D) Vs[n_old * D + tid] = vh;
+    BlockSum8<G>(cs, dsh);  // its barriers also publish sc[] and the V row
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      l[g] = l[g] * static_cast<double>(alpha[g]) + cs[g];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[g][e] *= alpha[g];
+    }
+    // ---- V: warp w, positions w, w + 8, ...; lane holds 4 dimensions
+#pragma unroll 4
+    for (int j = warp; j < n; j += kAW) {
+      const uint2 raw = *reinterpret_cast<const uint2*>(Vs + j * D + 4 * lane);
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float e = sc[g][j];
+        acc[g][0] = fmaf(e, a.x, acc[g][0]);
+        acc[g][1] = fmaf(e, a.y, acc[g][1]);
+        acc[g][2] = fmaf(e, b.x, acc[g][2]);
+        acc[g][3] = fmaf(e, b.y, acc[g][3]);
+      }
+    }
+    if (st + 1 < st1) {
+      __syncthreads();  // all reads of Vs and sc done
+      if (tid == 0) {
+        dev::FenceProxyAsync();
+        issue(1, st + 1);
+      }
+    }
+  }
+  // combine the warps' V partials: thread d (< 128) ends up with dimension d
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    *reinterpret_cast<float4*>(vred + (warp * G + g) * D + 4 * lane) =
+        make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
+  }
+  __syncthreads();
+  trace.Mark(2);  // all stages done
+  float o[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float t = 0.f;
+    if (tid < D) {
+#pragma unroll
+      for (int w = 0; w < kAW; ++w) t += vred[(w * G + g) * D + tid];
+    }
+    o[g] = t;
   }
 
   if (active == 1) {
+    if (tid < D) {
 #pragma unroll
-    for (int g = 0; g < G; ++g) p.out[(h * G + g) * D + tid] = o[g] * static_cast<float>(1.0 / l[g]);
+      for (int g = 0; g < G; ++g) p.out[(h * G + g) * D + tid] = o[g] * static_cast<float>(1.0 / l[g]);
+    }
     return;
   }
 
   // ---- split-K: publish (m, l, acc) and let the last block of this head merge
   constexpr int kRec = D + 2;
+  if (tid < D) {
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float* rec = p.part + (static_cast<int64_t>(h * p.n_splits + s) * G + g) * kRec;
-    if (tid == 0) {
-      rec[0] = m[g];
-      rec[1] = static_cast<float>(l[g]);
+    for (int g = 0; g < G; ++g) {
+      float* rec = p.part + (static_cast<int64_t>(h * p.n_splits + s) * G + g) * kRec;
+      if (tid == 0) {
+        rec[0] = m[g];
+        rec[1] = static_cast<float>(l[g]);
+      }
+      rec[2 + tid] = o[g];
     }
-    rec[2 + tid] = o[g];
   }
   __threadfence();
   __syncthreads();
@@ -515,29 +661,39 @@ __global__ void __launch_bounds__(128) AttnDecodeKernel(const AttnParams p) {
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  if (tid < active) {
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float* rec = p.part + (static_cast<int64_t>(h * p.n_splits + tid) * G + g) * kRec;
-      s_wm[tid][g] = __ldcg(rec);
-      s_wl[tid][g] = static_cast<double>(__ldcg(rec + 1));
-    }
+  for (int i = tid; i < active * G; i += kAT) {
+    const int sp = i / G, g = i - sp * G;
+    const float* rec = p.part + (static_cast<int64_t>(h * p.n_splits + sp) * G + g) * kRec;
+    s_wm[sp][g] = __ldcg(rec);
+    s_wl[sp][g] = static_cast<double>(__ldcg(rec + 1));
   }
   __syncthreads();
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
+  // thread = (head, dimension) pairs; the split partials are loaded in batches
+  for (int i = tid; i < G * D; i += kAT) {
+    const int g = i / D, d = i - g * D;
     float M = -INFINITY;
     for (int sp = 0; sp < active; ++sp) M = fmaxf(M, s_wm[sp][g]);
     double den = 0.0;
     float num = 0.f;
-#pragma unroll 4
-    for (int sp = 0; sp < active; ++sp) {
-      const float ms = s_wm[sp][g];
-      const float w = ms == -INFINITY ? 0.f : expf(ms - M);
-      den += static_cast<double>(w) * s_wl[sp][g];
-      num = fmaf(w, __ldcg(p.part + (static_cast<int64_t>(h * p.n_splits + sp) * G + g) * kRec + 2 + tid), num);
+    for (int sp0 = 0; sp0 < active; sp0 += 8) {
+      float pv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int sp = sp0 + u;
+        pv[u] = sp < active ? __ldcg(p.part + (static_cast<int64_t>(h * p.n_splits + sp) * G + g) * kRec + 2 + d) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int sp = sp0 + u;
+        if (sp < active) {
+          const float ms = s_wm[sp][g];
+          const float w = ms == -INFINITY ? 0.f : expf(ms - M);
+          den += static_cast<double>(w) * s_wl[sp][g];
+          num = fmaf(w, pv[u], num);
+        }
+      }
     }
-    p.out[(h * G + g) * D + tid] = num * static_cast<float>(1.0 / den);
+    p.out[(h * G + g) * D + d] = num * static_cast<float>(1.0 / den);
   }
   if (tid == 0) p.ticket[h] = 0u;
 }
@@ -597,8 +753,10 @@ void PrepareAttentionKernels() {
                         reinterpret_cast<const void*>(AttnDecodeKernel<2>),
                         reinterpret_cast<const void*>(AttnDecodeKernel<4>),
                         reinterpret_cast<const void*>(AttnDecodeKernel<8>)};
-  for (const void* f : fns) {
-    RPGB_CUDA(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kAttnDynSmem)));
+  const int gs[4] = {1, 2, 4, 8};
+  for (int i = 0; i < 4; ++i) {
+    RPGB_CUDA(cudaFuncSetAttribute(fns[i], cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(AttnDynSmem(gs[i]))));
   }
 }
 
@@ -611,8 +769,6 @@ void LaunchAttention(const AttnParams& p, int n_queries, cudaStream_t s, bool pd
   const void* fn = nullptr;
   if (p.fused) {
     RPGB_CHECK(n_queries == 1, "attention: the fused decode kernel takes one query");
-    RPGB_CHECK(static_cast<int64_t>(p.n_splits) * kSP >= p.max_seq, "attention: %d splits cannot cover %d positions",
-               p.n_splits, p.max_seq);
     switch (G) {
       case 1: fn = reinterpret_cast<const void*>(AttnDecodeKernel<1>); break;
       case 2: fn = reinterpret_cast<const void*>(AttnDecodeKernel<2>); break;
@@ -620,7 +776,7 @@ void LaunchAttention(const AttnParams& p, int n_queries, cudaStream_t s, bool pd
       case 8: fn = reinterpret_cast<const void*>(AttnDecodeKernel<8>); break;
       default: Throw("attention: GQA group %d is not supported (1, 2, 4, 8)", G);
     }
-    LaunchKernelArgs(fn, dim3(p.n_splits, p.n_kv), dim3(128), kAttnDynSmem, s, pdl, p);
+    LaunchKernelArgs(fn, dim3(p.n_splits, p.n_kv), dim3(kAT), AttnDynSmem(G), s, pdl, p);
     CountLaunches(1);
     return;
   }

@@ -46,30 +46,30 @@
 namespace rpgb {
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
 constexpr int kTile = 16;
 constexpr int kMaxRing = 6;
+constexpr int kBatch = 3;  // prologue super-blocks whose loads a warp issues together
 // Dynamic shared memory budget per block: leaves room for the next kernel's
 // block on the same SM (programmatic launch overlap needs co-residency).
 constexpr size_t kSmemBudget = 108 * 1024;
+constexpr size_t kSmemBudgetWide = 190 * 1024;
 constexpr size_t kSmemLimit = 200 * 1024;
 
 struct Layout {
   size_t ring, bfrag, sx, sscale, red, sq, bars, total;
 };
 
-__host__ __device__ inline Layout SmemLayout(int nb, int ring, int slot_bytes, int max_tiles) {
+__host__ __device__ inline Layout SmemLayout(int nb, int ring, int slot_bytes, int max_tiles, int nw) {
   Layout l;
   l.ring = 0;
-  l.bfrag = static_cast<size_t>(kWarps) * ring * slot_bytes;
+  l.bfrag = static_cast<size_t>(nw) * ring * slot_bytes;
   l.sx = l.bfrag + static_cast<size_t>(nb) * 1024;
   l.sscale = l.sx + static_cast<size_t>(nb) * 32;
   l.red = l.sscale + static_cast<size_t>(nb) * 4;
-  l.sq = l.red + static_cast<size_t>(max_tiles + kWarps) * kTile * 4;
+  l.sq = l.red + static_cast<size_t>(max_tiles + nw) * kTile * 4;
   l.sq = (l.sq + 7) & ~static_cast<size_t>(7);
-  l.bars = l.sq + kWarps * 8;
-  l.total = l.bars + static_cast<size_t>(kWarps) * ring * 8;
+  l.bars = l.sq + nw * 8;
+  l.total = l.bars + static_cast<size_t>(nw) * ring * 8;
   return l;
 }
 
@@ -269,8 +269,10 @@ __device__ __forceinline__ void FlushPiece(float* red, int piece, const LaneK& k
   rg = rg8 = 0.f;
 }
 
-template <bool NORM, int EPI>
-__global__ void __launch_bounds__(kThreads, 2) MatvecKernel(const MvParams p) {
+template <bool NORM, int EPI, int NW>
+__global__ void __launch_bounds__(32 * NW, NW == 8 ? 2 : 1) MatvecKernel(const MvParams p) {
+  constexpr int kWarps = NW;
+  constexpr int kThreads = 32 * NW;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ float s_bv[kWarps];
   __shared__ int s_bi[kWarps];
@@ -278,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 2) MatvecKernel(const MvParams p) {
   dev::TraceScope trace(p.trace);
 
   const int K = p.seg[0].w.cols, nb = K >> 8;
-  const Layout L = SmemLayout(nb, p.ring, p.slot_bytes, p.max_tiles);
+  const Layout L = SmemLayout(nb, p.ring, p.slot_bytes, p.max_tiles, NW);
   uint8_t* bfrag = smem + L.bfrag;
   float* sx = reinterpret_cast<float*>(smem + L.sx);
   float* sscale = reinterpret_cast<float*>(smem + L.sscale);
@@ -309,82 +311,127 @@ __global__ void __launch_bounds__(kThreads, 2) MatvecKernel(const MvParams p) {
     }
   }
   __syncwarp();
+  // norm weights of the first prologue batch: constant, so loaded before the wait
+  float wpre[kBatch][8];
+  if (NORM) {
+#pragma unroll
+    for (int q = 0; q < kBatch; ++q) {
+      const int b = warp + q * kWarps;
+      if (b < nb) {
+        const float4 wa = *reinterpret_cast<const float4*>(p.norm_w + b * 256 + 8 * lane);
+        const float4 wb = *reinterpret_cast<const float4*>(p.norm_w + b * 256 + 8 * lane + 4);
+        wpre[q][0] = wa.x; wpre[q][1] = wa.y; wpre[q][2] = wa.z; wpre[q][3] = wa.w;
+        wpre[q][4] = wb.x; wpre[q][5] = wb.y; wpre[q][6] = wb.z; wpre[q][7] = wb.w;
+      }
+    }
+  }
   dev::GridLaunchDependents();
   dev::GridWait();
   trace.Ready();
+  // residual of this thread's first epilogue row, fetched with the prologue loads
+  float resid0 = 0.f;
+  if (EPI == static_cast<int>(Epi::kResid) && tid < (t1 - t0) * kTile) resid0 = p.resid[t0 * kTile + tid];
 
   // ---- prologue: x (times the RMSNorm weight) as 4 signed 8-bit digits per
   // super-block, laid out as B fragments; 32-column sums for the Q4_K min term.
+  // A warp handles super-blocks warp, warp + 8, ...; the loads of up to
+  // kBatch of them are issued together, and the norm weights of the first
+  // batch were loaded before the dependency wait (they are constant).
   double ssq = 0.0;
-  for (int b = warp; b < nb; b += kWarps) {
-    const float4 xa = *reinterpret_cast<const float4*>(p.x + b * 256 + 8 * lane);
-    const float4 xb = *reinterpret_cast<const float4*>(p.x + b * 256 + 8 * lane + 4);
-    float v[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-    if (NORM) {
-      const float4 wa = *reinterpret_cast<const float4*>(p.norm_w + b * 256 + 8 * lane);
-      const float4 wb = *reinterpret_cast<const float4*>(p.norm_w + b * 256 + 8 * lane + 4);
-      const float w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+  for (int bb = 0; bb < nb; bb += kBatch * kWarps) {
+    float xv[kBatch][8], wv[kBatch][8];
+#pragma unroll
+    for (int q = 0; q < kBatch; ++q) {
+      const int b = bb + warp + q * kWarps;
+      if (b < nb) {
+        const float4 xa = *reinterpret_cast<const float4*>(p.x + b * 256 + 8 * lane);
+        const float4 xb = *reinterpret_cast<const float4*>(p.x + b * 256 + 8 * lane + 4);
+        xv[q][0] = xa.x; xv[q][1] = xa.y; xv[q][2] = xa.z; xv[q][3] = xa.w;
+        xv[q][4] = xb.x; xv[q][5] = xb.y; xv[q][6] = xb.z; xv[q][7] = xb.w;
+        if (NORM) {
+          if (bb == 0) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) wv[q][i] = wpre[q][i];
+          } else {
+            const float4 wa = *reinterpret_cast<const float4*>(p.norm_w + b * 256 + 8 * lane);
+            const float4 wb = *reinterpret_cast<const float4*>(p.norm_w + b * 256 + 8 * lane + 4);
+            wv[q][0] = wa.x; wv[q][1] = wa.y; wv[q][2] = wa.z; wv[q][3] = wa.w;
+            wv[q][4] = wb.x; wv[q][5] = wb.y; wv[q][6] = wb.z; wv[q][7] = wb.w;
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < kBatch; ++q) {
+      const int b = bb + warp + q * kWarps;
+      if (b >= nb) break;
+      float v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = xv[q][i];
+      if (NORM) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          ssq += static_cast<double>(v[i]) * v[i];
+          v[i] *= wv[q][i];
+        }
+      }
+      float mx = 0.f, su = 0.f;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        ssq += static_cast<double>(v[i]) * v[i];
-        v[i] *= w[i];
+        mx = fmaxf(mx, fabsf(v[i]));
+        su += v[i];
       }
-    }
-    float mx = 0.f, su = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      mx = fmaxf(mx, fabsf(v[i]));
-      su += v[i];
-    }
-    mx = dev::WarpMax(mx);
-    const int E = static_cast<int>((__float_as_uint(mx) >> 23) & 0xFFu);
-    // s = 2^(e(mx) - 5) so |x / s| < 64; Y = round(x / s * 2^20) splits
-    // exactly into balanced digits x0 (|x0| <= 64), x1 (6 bits), x2, x3 (7 bits).
-    float s = 0.f, inv20 = 0.f;
-    if (E >= 25 && E < 255) {
-      s = __uint_as_float(static_cast<uint32_t>(E - 5) << 23);
-      inv20 = __uint_as_float(static_cast<uint32_t>(279 - E) << 23);
-    }
-    int d0[8], d1[8], d2[8], d3[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      int Y = __float2int_rn(v[i] * inv20);
-      d3[i] = (Y << 25) >> 25;
-      Y = (Y - d3[i]) >> 7;
-      d2[i] = (Y << 25) >> 25;
-      Y = (Y - d2[i]) >> 7;
-      d1[i] = (Y << 26) >> 26;
-      d0[i] = (Y - d1[i]) >> 6;
-    }
-    auto pack = [](int a, int b, int c, int d) {
-      return __byte_perm(__byte_perm(a, b, 0x0040u), __byte_perm(c, d, 0x0040u), 0x5410u);
-    };
-    const uint32_t dw[4][2] = {{pack(d0[0], d0[1], d0[2], d0[3]), pack(d0[4], d0[5], d0[6], d0[7])},
-                               {pack(d1[0], d1[1], d1[2], d1[3]), pack(d1[4], d1[5], d1[6], d1[7])},
-                               {pack(d2[0], d2[1], d2[2], d2[3]), pack(d2[4], d2[5], d2[6], d2[7])},
-                               {pack(d3[0], d3[1], d3[2], d3[3]), pack(d3[4], d3[5], d3[6], d3[7])}};
-    // positions 8 lane .. 8 lane + 7 = 64c + 32hb + 16h + 8(lane & 1) + i
-    const int c = lane >> 3, hb = (lane >> 2) & 1, h = (lane >> 1) & 1, tb = 2 * (lane & 1);
-    const int m = 2 * c + h;
-    uint32_t* bw = reinterpret_cast<uint32_t*>(bfrag + static_cast<size_t>(b) * 1024);
-#pragma unroll
-    for (int dg = 0; dg < 4; ++dg) {
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int Lp = 4 * (dg + 4 * hb) + tb + j;
-        bw[((m >> 2) * 32 + Lp) * 4 + (m & 3)] = dw[dg][j];
+      mx = dev::WarpMax(mx);
+      const int E = static_cast<int>((__float_as_uint(mx) >> 23) & 0xFFu);
+      // s = 2^(e(mx) - 5) so |x / s| < 64; Y = round(x / s * 2^20) splits
+      // exactly into balanced digits x0 (|x0| <= 64), x1 (6 bits), x2, x3 (7 bits).
+      float s = 0.f, inv20 = 0.f;
+      if (E >= 25 && E < 255) {
+        s = __uint_as_float(static_cast<uint32_t>(E - 5) << 23);
+        inv20 = __uint_as_float(static_cast<uint32_t>(279 - E) << 23);
       }
+      int d0[8], d1[8], d2[8], d3[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        int Y = __float2int_rn(v[i] * inv20);
+        d3[i] = (Y << 25) >> 25;
+        Y = (Y - d3[i]) >> 7;
+        d2[i] = (Y << 25) >> 25;
+        Y = (Y - d2[i]) >> 7;
+        d1[i] = (Y << 26) >> 26;
+        d0[i] = (Y - d1[i]) >> 6;
+      }
+      auto pack = [](int a, int b, int c, int d) {
+        return __byte_perm(__byte_perm(a, b, 0x0040u), __byte_perm(c, d, 0x0040u), 0x5410u);
+      };
+      const uint32_t dw[4][2] = {{pack(d0[0], d0[1], d0[2], d0[3]), pack(d0[4], d0[5], d0[6], d0[7])},
+                                 {pack(d1[0], d1[1], d1[2], d1[3]), pack(d1[4], d1[5], d1[6], d1[7])},
+                                 {pack(d2[0], d2[1], d2[2], d2[3]), pack(d2[4], d2[5], d2[6], d2[7])},
+                                 {pack(d3[0], d3[1], d3[2], d3[3]), pack(d3[4], d3[5], d3[6], d3[7])}};
+      // positions 8 lane .. 8 lane + 7 = 64c + 32hb + 16h + 8(lane & 1) + i
+      const int c = lane >> 3, hb = (lane >> 2) & 1, h = (lane >> 1) & 1, tb = 2 * (lane & 1);
+      const int m = 2 * c + h;
+      uint32_t* bw = reinterpret_cast<uint32_t*>(bfrag + static_cast<size_t>(b) * 1024);
+#pragma unroll
+      for (int dg = 0; dg < 4; ++dg) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int Lp = 4 * (dg + 4 * hb) + tb + j;
+          bw[((m >> 2) * 32 + Lp) * 4 + (m & 3)] = dw[dg][j];
+        }
+      }
+      su += __shfl_xor_sync(0xFFFFFFFFu, su, 1);
+      su += __shfl_xor_sync(0xFFFFFFFFu, su, 2);
+      if ((lane & 3) == 0) sx[b * 8 + (lane >> 2)] = su;
+      if (lane == 0) sscale[b] = s;
     }
-    su += __shfl_xor_sync(0xFFFFFFFFu, su, 1);
-    su += __shfl_xor_sync(0xFFFFFFFFu, su, 2);
-    if ((lane & 3) == 0) sx[b * 8 + (lane >> 2)] = su;
-    if (lane == 0) sscale[b] = s;
   }
   if (NORM) {
     ssq = dev::WarpSumD(ssq);
     if (lane == 0) sq[warp] = ssq;
   }
   __syncthreads();
+  trace.Mark(1);  // prologue done
 
   // ---- stream the units
   const LaneK lk = MakeLane(lane);
@@ -444,6 +491,7 @@ __global__ void __launch_bounds__(kThreads, 2) MatvecKernel(const MvParams p) {
     }
   }
   __syncthreads();
+  trace.Mark(2);  // all units done
 
   // ---- epilogue: combine the per-warp pieces of every row in warp order
   float scale = 1.f;
@@ -477,7 +525,7 @@ __global__ void __launch_bounds__(kThreads, 2) MatvecKernel(const MvParams p) {
     if (EPI == static_cast<int>(Epi::kStore)) {
       p.out[row] = v;
     } else if (EPI == static_cast<int>(Epi::kResid)) {
-      p.out[row] = p.resid[row] + v;
+      p.out[row] = (lr == tid ? resid0 : p.resid[row]) + v;
     } else if (EPI == static_cast<int>(Epi::kSilu)) {
       // rows 2i (gate) and 2i+1 (up): (g / (1 + exp(-g))) * u, as src/kernels_gpu.cu:863-869
       p.out[row >> 1] = (v / (1.0f + expf(-v))) * v2;
@@ -590,15 +638,20 @@ __global__ void DequantRowsKernel(const DevMat w, int64_t row0, float* __restric
 
 using MvFn = void (*)(const MvParams);
 
-template <bool NORM>
+template <bool NORM, int NW>
 MvFn PickEpi(Epi epi) {
   switch (epi) {
-    case Epi::kStore: return MatvecKernel<NORM, 0>;
-    case Epi::kResid: return MatvecKernel<NORM, 1>;
-    case Epi::kSilu: return MatvecKernel<NORM, 2>;
-    case Epi::kArgmax: return MatvecKernel<NORM, 3>;
+    case Epi::kStore: return MatvecKernel<NORM, 0, NW>;
+    case Epi::kResid: return MatvecKernel<NORM, 1, NW>;
+    case Epi::kSilu: return MatvecKernel<NORM, 2, NW>;
+    case Epi::kArgmax: return MatvecKernel<NORM, 3, NW>;
   }
   Throw("bad epilogue");
+}
+
+MvFn Pick(bool norm, int nw, Epi epi) {
+  if (nw == 16) return norm ? PickEpi<true, 16>(epi) : PickEpi<false, 16>(epi);
+  return norm ? PickEpi<true, 8>(epi) : PickEpi<false, 8>(epi);
 }
 
 }  // namespace
@@ -606,9 +659,11 @@ MvFn PickEpi(Epi epi) {
 void PrepareMatvecKernels() {
   const Epi epis[4] = {Epi::kStore, Epi::kResid, Epi::kSilu, Epi::kArgmax};
   for (int norm = 0; norm < 2; ++norm) {
-    for (Epi e : epis) {
-      MvFn f = norm ? PickEpi<true>(e) : PickEpi<false>(e);
-      RPGB_CUDA(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemLimit)));
+    for (int nw : {8, 16}) {
+      for (Epi e : epis) {
+        RPGB_CUDA(cudaFuncSetAttribute(Pick(norm != 0, nw, e), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(kSmemLimit)));
+      }
     }
   }
 }
@@ -640,14 +695,19 @@ void LaunchMatvec(const MvParams& in, Epi epi, int /*rows_per_warp*/, int num_sm
   const int grid = MatvecGrid(rows, 1, num_sms);
   p.max_tiles = (p.n_tiles + grid - 1) / grid;
   p.slot_bytes = slot;
-  const Layout L0 = SmemLayout(nb, 0, slot, p.max_tiles);
-  const size_t per_ring = static_cast<size_t>(kWarps) * (slot + 8);
-  const int ring = static_cast<int>((kSmemBudget > L0.total ? kSmemBudget - L0.total : 0) / per_ring);
+  // Long streams per block (the lm_head: ~64 tiles) are compute-bound with 8
+  // warps: they get 16 warps and a deeper ring (one block per SM; the kernels
+  // after the lm_head are small, so co-residency buys nothing there).
+  const int nw = p.max_tiles >= 24 ? 16 : 8;
+  const size_t budget = nw == 16 ? kSmemBudgetWide : kSmemBudget;
+  const Layout L0 = SmemLayout(nb, 0, slot, p.max_tiles, nw);
+  const size_t per_ring = static_cast<size_t>(nw) * (slot + 8);
+  const int ring = static_cast<int>((budget > L0.total ? budget - L0.total : 0) / per_ring);
   p.ring = std::max(2, std::min(kMaxRing, ring));
-  const Layout L = SmemLayout(nb, p.ring, slot, p.max_tiles);
+  const Layout L = SmemLayout(nb, p.ring, slot, p.max_tiles, nw);
   RPGB_CHECK(L.total <= kSmemLimit, "matvec: shared memory plan %zu exceeds the limit", L.total);
-  MvFn fn = p.norm_w != nullptr ? PickEpi<true>(epi) : PickEpi<false>(epi);
-  LaunchKernelArgs(reinterpret_cast<const void*>(fn), dim3(grid), dim3(kThreads), L.total, s, pdl, p);
+  MvFn fn = Pick(p.norm_w != nullptr, nw, epi);
+  LaunchKernelArgs(reinterpret_cast<const void*>(fn), dim3(grid), dim3(32 * nw), L.total, s, pdl, p);
   CountLaunches(1);
 }
 

@@ -34,7 +34,7 @@ namespace {
 constexpr int kGenThreads = 1024;
 constexpr int kCandThreads = 256;
 constexpr int kSliceMax = 2048;
-constexpr int kSmallThreads = 256;
+constexpr int kSmallThreads = 1024;
 constexpr int kMaxCand = kCandBlocks * kFastTopK;
 constexpr double kFix = 1152921504606846976.0;  // 2^60
 
@@ -125,6 +125,89 @@ __device__ __forceinline__ void SelectBin(const unsigned* hist, int rem, uint32_
   }
 }
 
+// As SelectBin for NB (a multiple of 32) bins: s_sel = {d, rank inside bin d,
+// count of elements in the bins above d}.
+template <int NB>
+__device__ __forceinline__ void SelectBinN(const unsigned* hist, int rem, uint32_t* s_sel) {
+  if (threadIdx.x >= 32) return;
+  constexpr int PER = NB / 32;
+  const int lane = threadIdx.x;
+  unsigned sum = 0;
+#pragma unroll 16
+  for (int j = 0; j < PER; ++j) sum += hist[PER * lane + j];
+  unsigned incl = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned v = __shfl_down_sync(0xFFFFFFFFu, incl, o);
+    if (lane + o < 32) incl += v;
+  }
+  const unsigned excl = incl - sum;
+  const unsigned r = static_cast<unsigned>(rem);
+  if (excl < r && r <= incl) {
+    unsigned cum = excl;
+    int d = PER * lane;
+    for (int j = PER - 1; j >= 0; --j) {
+      const unsigned h = hist[PER * lane + j];
+      if (cum + h >= r) {
+        d = PER * lane + j;
+        break;
+      }
+      cum += h;
+    }
+    s_sel[0] = static_cast<uint32_t>(d);
+    s_sel[1] = r - cum;
+    s_sel[2] = cum;
+  }
+}
+
+// A radix-bin lower edge t with k <= #{OrderKey(x) >= t} <= kFastTopK (1 <= k
+// <= n), found with 11-, 11- and 10-bit passes that stop as soon as the bin
+// holding the k-th largest leaves few enough elements at or above it; *cnt
+// receives #{key >= t} (more than kFastTopK only when ties at one exact key
+// make the bound impossible).  hist holds 2048 bins.
+__device__ uint32_t SliceBound(const float* x, int n, int k, unsigned* hist, uint32_t* s_sel, int* cnt) {
+  uint32_t prefix = 0, mask = 0;
+  int rem = k, above = 0;
+  const int n_up = (n + 31) & ~31;
+#pragma unroll 1
+  for (int pass = 0; pass < 3; ++pass) {
+    const int shift = pass == 0 ? 21 : (pass == 1 ? 10 : 0);
+    const uint32_t nbm = pass == 2 ? 1023u : 2047u;
+    for (int i = threadIdx.x; i <= static_cast<int>(nbm); i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n_up; i += blockDim.x) {
+      uint32_t bin = 0xFFFFFFFFu;
+      if (i < n) {
+        const uint32_t key = dev::OrderKey(x[i]);
+        if ((key & mask) == prefix) bin = (key >> shift) & nbm;
+      }
+      const unsigned same = __match_any_sync(0xFFFFFFFFu, bin);
+      if (bin != 0xFFFFFFFFu && (threadIdx.x & 31) == __ffs(same) - 1) atomicAdd(&hist[bin], __popc(same));
+    }
+    __syncthreads();
+    if (pass < 2) {
+      SelectBinN<2048>(hist, rem, s_sel);
+    } else {
+      SelectBinN<1024>(hist, rem, s_sel);
+    }
+    __syncthreads();
+    const uint32_t d = s_sel[0];
+    const int ge = above + static_cast<int>(s_sel[2]) + static_cast<int>(hist[d]);
+    const uint32_t t = prefix | (d << shift);
+    if (ge <= kFastTopK || pass == 2) {
+      *cnt = ge;
+      __syncthreads();
+      return t;
+    }
+    prefix = t;
+    mask |= nbm << shift;
+    above += static_cast<int>(s_sel[2]);
+    rem = static_cast<int>(s_sel[1]);
+    __syncthreads();
+  }
+  return prefix;  // not reached
+}
+
 // Key of the k-th largest element of x[0..n) (multiplicity counted), 1 <= k <= n.
 __device__ uint32_t RadixKth(const float* x, int n, int k, unsigned* hist, uint32_t* s_sel) {
   uint32_t prefix = 0, mask = 0;
@@ -161,7 +244,7 @@ __global__ void __launch_bounds__(kGenThreads) SampleGeneralKernel(const SampleP
   __shared__ int ish[32];
   __shared__ unsigned hist[256];
   __shared__ unsigned long long mhist[256];
-  __shared__ uint32_t s_sel[2];
+  __shared__ uint32_t s_sel[3];
   __shared__ unsigned long long s_below;
   __shared__ double wsc[32];
   __shared__ int s_idx, s_amb;
@@ -333,8 +416,8 @@ __global__ void __launch_bounds__(kGenThreads) SampleGeneralKernel(const SampleP
 // Per-slice top-k candidates on raw logits (temperature scaling is monotone).
 __global__ void __launch_bounds__(kCandThreads) CandKernel(const SampleParams p) {
   __shared__ float vals[kSliceMax];
-  __shared__ unsigned hist[256];
-  __shared__ uint32_t s_sel[2];
+  __shared__ unsigned hist[2048];
+  __shared__ uint32_t s_sel[3];
   __shared__ int s_cnt;
   dev::TraceScope trace(p.trace);
   dev::GridLaunchDependents();
@@ -362,8 +445,12 @@ __global__ void __launch_bounds__(kCandThreads) CandKernel(const SampleParams p)
   __syncthreads();
   const int k = p.top_k;
   uint32_t thr = 0u;  // keep everything when the slice is not larger than k
-  if (len > k) thr = RadixKth(vals, len, k, hist, s_sel);
-  __syncthreads();
+  int ge = len;
+  if (len > k) thr = SliceBound(vals, len, k, hist, s_sel, &ge);
+  if (ge > kFastTopK) {  // ties at one exact key: let the general kernel run
+    if (threadIdx.x == 0) p.cand_cnt[blockIdx.x] = -1;
+    return;
+  }
   float* cv = p.cand_val + blockIdx.x * kFastTopK;
   int32_t* ci = p.cand_idx + blockIdx.x * kFastTopK;
   for (int i = threadIdx.x; i < len; i += kCandThreads) {
@@ -387,82 +474,78 @@ __global__ void __launch_bounds__(kSmallThreads) SampleSmallKernel(const SampleP
   int* kix = reinterpret_cast<int*>(kv + kMaxCand);               // kept indices
   __shared__ unsigned hist[256];
   __shared__ uint32_t s_sel[2];
-  __shared__ int s_off[kCandBlocks + 1];
   __shared__ int s_bad, s_m, s_c;
   const int tid = threadIdx.x;
   dev::TraceScope trace(p.trace);
   dev::GridLaunchDependents();
   dev::GridWait();
   trace.Ready();
-  // candidate counts of the slices -> offsets (warp 0 scans; counts are loaded in parallel)
+  // slice counts; an overflowed slice sends this draw to the general kernel
   __shared__ int s_cnt[kCandBlocks];
-  for (int b = tid; b < kCandBlocks; b += kSmallThreads) s_cnt[b] = p.cand_cnt[b];
-  __syncthreads();
-  if (tid < 32) {
-    constexpr int kPer = (kCandBlocks + 31) / 32;
-    int c[kPer], sum = 0, bad = 0;
-#pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-      const int b = tid * kPer + j;
-      c[j] = b < kCandBlocks ? s_cnt[b] : 0;
-      bad |= c[j] < 0;
-      sum += c[j] < 0 ? 0 : c[j];
-    }
-    int incl = sum;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-      if (tid >= o) incl += v;
-    }
-    int off = incl - sum;
-#pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-      const int b = tid * kPer + j;
-      if (b < kCandBlocks) s_off[b] = off;
-      off += c[j] < 0 ? 0 : c[j];
-    }
-    bad = __any_sync(0xFFFFFFFFu, bad);
-    if (tid == 31) {
-      s_off[kCandBlocks] = incl;
-      s_m = incl;
-    }
-    if (tid == 0) s_bad = bad;
+  __shared__ float s_hmin[(kCandBlocks * kFastTopK + 31) / 32];
+  __shared__ float s_t0;
+  if (tid < kCandBlocks) s_cnt[tid] = p.cand_cnt[tid];
+  if (tid == 0) {
+    s_bad = 0;
+    s_m = 0;
   }
+  __syncthreads();
+  if (tid < kCandBlocks && s_cnt[tid] < 0) s_bad = 1;
   __syncthreads();
   if (s_bad) {
     if (tid == 0) *p.flag = 0;
     return;
   }
-  const int m = s_m;
-  const float inv_t = 1.0f / p.temperature;
-  // gather all slices at once: every thread first issues all of its loads
-  // (independent, so their latencies overlap), then stores
-  {
-    constexpr int kSlots = (kCandBlocks * kFastTopK + kSmallThreads - 1) / kSmallThreads;
-    float vv[kSlots];
-    int vi[kSlots];
+  // Every slice with at least k candidates holds k values >= its smallest
+  // candidate, so the largest such minimum bounds the k-th largest logit from
+  // below: candidates under it cannot survive top_k and are dropped here.
+  constexpr int kTotal = kCandBlocks * kFastTopK;
+  constexpr int kRounds = (kTotal + kSmallThreads - 1) / kSmallThreads;
+  float rv[kRounds];
+  int ri[kRounds];
 #pragma unroll
-    for (int r = 0; r < kSlots; ++r) {
-      const int j = tid + r * kSmallThreads;
-      const int b = j / kFastTopK, i = j - b * kFastTopK;
-      const bool use = j < kCandBlocks * kFastTopK && i < s_off[b + 1] - s_off[b];
-      vv[r] = use ? __ldcg(p.cand_val + j) : 0.f;
-      vi[r] = use ? __ldcg(p.cand_idx + j) : -1;
+  for (int r = 0; r < kRounds; ++r) {
+    const int j = tid + r * kSmallThreads;
+    const int b = j / kFastTopK, i = j - b * kFastTopK;
+    const bool use = j < kTotal && i < s_cnt[b];
+    rv[r] = use ? __ldcg(p.cand_val + j) : INFINITY;
+    ri[r] = use ? __ldcg(p.cand_idx + j) : -1;
+  }
+#pragma unroll
+  for (int r = 0; r < kRounds; ++r) {
+    const int j = tid + r * kSmallThreads;
+    float mn = rv[r];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mn = fminf(mn, __shfl_xor_sync(0xFFFFFFFFu, mn, o));
+    if ((tid & 31) == 0 && j < kTotal) s_hmin[j >> 5] = mn;  // one half slice per warp
+  }
+  __syncthreads();
+  if (tid < 32) {
+    float t0 = -INFINITY;
+    for (int b = tid; b < kCandBlocks; b += 32) {
+      if (s_cnt[b] >= p.top_k) t0 = fmaxf(t0, fminf(s_hmin[2 * b], s_hmin[2 * b + 1]));
     }
+    t0 = dev::WarpMax(t0);
+    if (tid == 0) s_t0 = t0;
+  }
+  __syncthreads();
+  const float t0 = s_t0;
+  const float inv_t = 1.0f / p.temperature;
 #pragma unroll
-    for (int r = 0; r < kSlots; ++r) {
-      const int j = tid + r * kSmallThreads;
-      if (vi[r] >= 0) {
-        const int b = j / kFastTopK, i = j - b * kFastTopK;
-        float v = vv[r];
-        if (p.temperature != 1.0f) v *= inv_t;
-        cv[s_off[b] + i] = v;
-        ci[s_off[b] + i] = vi[r];
-      }
+  for (int r = 0; r < kRounds; ++r) {
+    if (ri[r] >= 0 && rv[r] >= t0) {
+      float v = rv[r];
+      if (p.temperature != 1.0f) v *= inv_t;
+      const int slot = atomicAdd(&s_m, 1);
+      cv[slot] = v;
+      ci[slot] = ri[r];
     }
   }
   __syncthreads();
+  const int m = s_m;
+  trace.Mark(1);  // candidates gathered
   const float kth = dev::FromOrderKey(RadixKth(cv, m, p.top_k, hist, s_sel));
+  trace.Mark(2);  // k-th candidate found
   // survivors, ordered by vocabulary index
   if (tid == 0) s_c = 0;
   __syncthreads();
@@ -483,6 +566,7 @@ __global__ void __launch_bounds__(kSmallThreads) SampleSmallKernel(const SampleP
     ci[rank] = kix[i];
   }
   __syncthreads();
+  trace.Mark(3);  // survivors sorted
   // ---- softmax over the survivors (serial, index order; c is k plus ties)
   float* v = cv;  // probabilities, index-ordered
   const int* ix = ci;
@@ -510,6 +594,7 @@ __global__ void __launch_bounds__(kSmallThreads) SampleSmallKernel(const SampleP
     for (int i = tid; i < c; i += kSmallThreads) v[i] *= inv;
   }
   __syncthreads();
+  trace.Mark(4);  // softmax done
   if (p.top_p > 0.0f && p.top_p < 1.0f) {
     // ascending (key, index) order of the survivors' probabilities
     for (int i = tid; i < c; i += kSmallThreads) {

@@ -174,30 +174,50 @@ __device__ __forceinline__ uint64_t GlobalTimer() {
 }
 
 // Records one TraceRec per block (thread 0) when the trace buffer is set:
-// construct at kernel entry, call Ready() after GridWait(); the record is
-// written when the scope ends (every return path included).
+// construct at kernel entry, call Ready() after GridWait(); Mark(k) notes the
+// time of phase k (1..4).  Everything is written when the scope ends (every
+// return path included), with one atomic per block, so the marks do not slow
+// the block down.
 struct TraceScope {
+  static constexpr int kMaxMarks = 4;
   const Trace& t;
   uint64_t t0 = 0, tr = 0;
+  uint64_t mt[kMaxMarks];
+  uint32_t mk[kMaxMarks];
+  int nm = 0;
   __device__ explicit TraceScope(const Trace& tr_) : t(tr_) {
     if (t.rec != nullptr && threadIdx.x == 0) t0 = GlobalTimer();
   }
   __device__ void Ready() {
     if (t.rec != nullptr && threadIdx.x == 0) tr = GlobalTimer();
   }
+  // Phase mark k: a record whose block field carries k << 24 and whose t_end
+  // is the time of the mark (thread 0's view; callers place marks after a
+  // barrier so the whole block has reached them).
+  __device__ void Mark(uint32_t k) {
+    if (t.rec != nullptr && threadIdx.x == 0 && nm < kMaxMarks) {
+      mt[nm] = GlobalTimer();
+      mk[nm] = k;
+      ++nm;
+    }
+  }
   __device__ ~TraceScope() {
     if (t.rec != nullptr && threadIdx.x == 0) {
       const uint64_t t1 = GlobalTimer();
-      const uint32_t i = atomicAdd(t.count, 1u);
-      if (i < t.cap) {
-        TraceRec r;
-        r.id = static_cast<uint32_t>(t.id);
-        r.block = blockIdx.x + gridDim.x * blockIdx.y;
-        r.t_start = t0;
-        r.t_ready = tr ? tr : t0;
-        r.t_end = t1;
-        t.rec[i] = r;
-      }
+      const uint32_t i = atomicAdd(t.count, 1u + static_cast<uint32_t>(nm));
+      Put(i, 0u, t1);
+      for (int j = 0; j < nm; ++j) Put(i + 1 + j, mk[j], mt[j]);
+    }
+  }
+  __device__ void Put(uint32_t i, uint32_t k, uint64_t t1) const {
+    if (i < t.cap) {
+      TraceRec r;
+      r.id = static_cast<uint32_t>(t.id);
+      r.block = (blockIdx.x + gridDim.x * blockIdx.y) | (k << 24);
+      r.t_start = t0;
+      r.t_ready = tr ? tr : t0;
+      r.t_end = t1;
+      t.rec[i] = r;
     }
   }
 };

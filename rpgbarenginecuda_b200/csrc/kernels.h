@@ -114,10 +114,12 @@ struct AttnParams {
   unsigned* err = nullptr;  // decode: set when a bounded wait for the staged K/V gave up
   Trace trace;
 };
-// Decode (fused, n_queries == 1) uses one block per (128-position split, KV
-// head) with the cached K/V rows staged into shared memory by TMA before the
-// programmatic wait; n_splits must be >= ceil(max_seq / 128).
+// Decode (fused, n_queries == 1) uses one block per (split, KV head); a split
+// owns a run of 128-position stages whose cached K/V rows are staged into
+// shared memory by TMA (the first before the programmatic wait).  n_splits
+// bounds the block count (about one block per SM); at most kMaxAttnSplits.
 constexpr int kAttnSplitPositions = 128;
+constexpr int kMaxAttnSplits = 64;
 void LaunchAttention(const AttnParams& p, int n_queries, cudaStream_t s, bool pdl = false);
 void PrepareAttentionKernels();
 size_t AttentionPartialFloats(int n_kv, int group, int n_splits);
