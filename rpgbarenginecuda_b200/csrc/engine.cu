@@ -3,6 +3,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 
 #include "common.h"
@@ -67,6 +68,12 @@ Session::Session(const Model* m, int64_t max_seq) : m_(m), max_seq_(max_seq) {
     const int64_t stages = (max_seq + kPositionsPerSplit - 1) / kPositionsPerSplit;
     const int64_t per_head = std::max(1, m->num_sms() / c.n_kv_heads);
     n_splits_ = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({stages, per_head, kMaxAttnSplits})));
+    // RPGB_ATTN_SPLITS caps the split count (more 128-position stages per
+    // block); used by tests to exercise multi-stage blocks on short models.
+    if (const char* e = std::getenv("RPGB_ATTN_SPLITS")) {
+      const int cap = std::atoi(e);
+      if (cap >= 1) n_splits_ = std::min(n_splits_, cap);
+    }
   }
   const int am_grid = MatvecGrid(c.vocab, 4, m->num_sms());
   const int qkv = c.q_dim() + 2 * c.kv_dim();

@@ -146,3 +146,25 @@ def test_vs_reference_engine(pair):
     assert len(rsess) == len(s)
     rsess.close()
     s.close()
+
+
+@pytest.mark.parametrize("splits", ["1", "2", "3"])
+def test_decode_attention_multi_stage(tiny_model, monkeypatch, splits):
+    """Decode attention with several 128-position stages per block (and split-K
+    merges across blocks) against the oracle at a context of ~430 positions."""
+    monkeypatch.setenv("RPGB_ATTN_SPLITS", splits)
+    m = Model(tiny_model, 0, 512)
+    om = OracleModel(tiny_model, 512)
+    toks = synthetic.seeded_tokens(420, 3, m.vocab)
+    s, os_ = Session(m, 512), OracleSession(om, 512)
+    s.prefill(toks)
+    os_.prefill(toks)
+    ids, steps = s.generate(SampleOptions(0.0, 0, 1.0), 0, 12, step_logits=True)
+    rids, rsteps = os_.generate(0.0, 0, 1.0, 0, 12, step_logits=True)
+    for i in range(len(ids)):
+        assert full_scale_err(steps[i], rsteps[i]) <= FULL_SCALE, (splits, i)
+    ok, at = tokens_agree(ids, rids, rsteps)
+    assert ok, (splits, at)
+    s.close()
+    m.close()
+    om.close()
