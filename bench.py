@@ -55,6 +55,9 @@ def parse():
     ap.add_argument("--model", default=MODEL)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-roofline", action="store_true")
+    ap.add_argument("--matvec-shapes", action="store_true",
+                    help="launch the decode matvec once per distinct matrix shape of the model and exit "
+                         "(the command profiled by ncu for profiles/)")
     ap.add_argument("--with-ref-gpu", action="store_true",
                     help="also time the reference's own CUDA engine (built from its sources) on the same turn")
     return ap.parse_args()
@@ -180,7 +183,11 @@ def reference_arm(args):
 
 
 def matvec_roofline(path, device, peak):
-    """Decode matvec over every matrix of the model (one decode's weight stream)."""
+    """Decode matvec roofline: every matrix of the model launched back to back
+    on one stream (one decode's weight stream, 1.1 GB > L2), three passes,
+    CUDA events around each pass; algorithmic bytes = M*K/256*{144,210} +
+    4(M+K) per launch.  The lm_head shape (151936 x 2048 Q6_K, 255 MB) is also
+    timed alone, 20 launches back to back."""
     import numpy as np
     import torch
     from gguf import GGUFReader
@@ -194,44 +201,85 @@ def matvec_roofline(path, device, peak):
             continue
         cols, rows = int(t.shape[0]), int(t.shape[1])
         mats.append((t.name, int(t.tensor_type), rows, cols, np.asarray(t.data).view(np.uint8).reshape(-1)))
-    handles = [(Matrix(q, r, c, b, device), q, r, c) for (_, q, r, c, b) in mats]
+    handles = [(Matrix(q, r, c, b, device), q, r, c, name) for (name, q, r, c, b) in mats]
     del mats, rd
-    kmax = max(c for _, _, _, c in handles)
-    rmax = max(r for _, _, r, _ in handles)
+    kmax = max(c for _, _, _, c, _ in handles)
+    rmax = max(r for _, _, r, _, _ in handles)
     x = torch.randn(kmax, device=f"cuda:{device}")
     y = torch.empty(rmax, device=f"cuda:{device}")
     stream = torch.cuda.current_stream(device)
     sp = stream.cuda_stream
-    for m, _, _, _ in handles:  # warm-up pass
+    nbytes = lambda q, r, c: r * c // 256 * (144 if q == 12 else 210) + 4 * (r + c)
+    for m, _, _, _, _ in handles:  # warm-up pass
         m.matvec(x.data_ptr(), 1, y.data_ptr(), sp)
     torch.cuda.synchronize(device)
-    total_ms, total_bytes, launches, per = 0.0, 0, 0, {}
-    for _ in range(3):
-        for m, q, r, c in handles:
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    passes = 3
+    e0.record(stream)
+    for _ in range(passes):
+        for m, _, _, _, _ in handles:
             m.matvec(x.data_ptr(), 1, y.data_ptr(), sp)
-            e1.record(stream)
-            e1.synchronize()
-            ms = e0.elapsed_time(e1)
-            b = r * c // 256 * (144 if q == 12 else 210) + 4 * (r + c)
-            total_ms += ms
-            total_bytes += b
-            launches += 1
-            key = f"{'q4k' if q == 12 else 'q6k'}_{r}x{c}"
-            per.setdefault(key, [0.0, 0, 0])
-            per[key][0] += ms
-            per[key][1] += b
-            per[key][2] += 1
-    for m, _, _, _ in handles:
-        m.close()
-    achieved = total_bytes / (total_ms * 1e-3) / 1e9
-    shapes = {k: round(v[1] / (v[0] * 1e-3) / 1e9, 1) for k, v in per.items()}
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    total_bytes = passes * sum(nbytes(q, r, c) for _, q, r, c, _ in handles)
+    launches = passes * len(handles)
+    achieved = total_bytes / (ms * 1e-3) / 1e9
+    big = max(handles, key=lambda h: h[2] * h[3])
+    m, q, r, c, _ = big
+    e0.record(stream)
+    for _ in range(20):
+        m.matvec(x.data_ptr(), 1, y.data_ptr(), sp)
+    e1.record(stream)
+    e1.synchronize()
+    big_ms = e0.elapsed_time(e1) / 20
+    big_gbs = nbytes(q, r, c) / (big_ms * 1e-3) / 1e9
+    for h in handles:
+        h[0].close()
+    traffic = None
+    tf = os.path.join(ROOT, "profiles", "matvec_traffic.json")
+    if os.path.exists(tf):  # dram bytes per launch of each shape, from the committed ncu capture
+        with open(tf) as f:
+            per = json.load(f).get("dram_bytes_per_launch", {})
+        keys = [f"{'q4k' if q == 12 else 'q6k'}_{r}x{c}" for _, q, r, c, _ in handles]
+        if keys and all(k in per for k in keys):
+            traffic = round(sum(per[k] for k in keys) / len(keys))
     return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-            "frac": round(achieved / peak, 4), "traffic": None,
-            "kernel": "MatvecKernel (decode Q4_K/Q6_K dequant-matvec, n=1)",
-            "bytes_per_launch": round(total_bytes / launches), "avg_launch_us": round(1000 * total_ms / launches, 2),
-            "per_shape_gbs": shapes}
+            "frac": round(achieved / peak, 4), "traffic": traffic,
+            "kernel": "MatvecKernel (decode Q4_K/Q6_K dequant-matvec, n=1): all matrices of the model, back to back",
+            "bytes_per_launch": round(total_bytes / launches), "avg_launch_us": round(1000 * ms / launches, 2),
+            "lm_head": {"shape": f"{'q4k' if q == 12 else 'q6k'}_{r}x{c}", "bytes": nbytes(q, r, c),
+                        "avg_launch_us": round(1000 * big_ms, 2), "gbs": round(big_gbs, 1),
+                        "frac": round(big_gbs / peak, 4)}}
+
+
+def matvec_shapes(args):
+    """One decode-matvec launch per distinct (type, rows, cols) of the model, after one warm-up launch each."""
+    import numpy as np
+    import torch
+    from gguf import GGUFReader
+
+    from rpgbarenginecuda_b200 import Matrix, synthetic
+
+    path = synthetic.cached_model(args.model, seed=0)
+    rd = GGUFReader(path)
+    seen = {}
+    for t in rd.tensors:
+        if len(t.shape) != 2 or int(t.tensor_type) not in (12, 14):
+            continue
+        key = (int(t.tensor_type), int(t.shape[1]), int(t.shape[0]))
+        if key not in seen:
+            seen[key] = np.asarray(t.data).view(np.uint8).reshape(-1).copy()
+    x = torch.randn(max(k[2] for k in seen), device="cuda")
+    y = torch.empty(max(k[1] for k in seen), device="cuda")
+    sp = torch.cuda.current_stream().cuda_stream
+    for (q, r, c), b in sorted(seen.items()):
+        m = Matrix(q, r, c, b, 0)
+        m.matvec(x.data_ptr(), 1, y.data_ptr(), sp)  # warm-up
+        m.matvec(x.data_ptr(), 1, y.data_ptr(), sp)
+        torch.cuda.synchronize()
+        print(f"{'q4k' if q == 12 else 'q6k'}_{r}x{c}", flush=True)
+        m.close()
 
 
 def ours(args):
@@ -411,6 +459,9 @@ def reference_gpu_turn(path, prompt, appends):
 
 def main():
     args = parse()
+    if args.matvec_shapes:
+        matvec_shapes(args)
+        return
     if args.impl == "reference":
         return reference_arm(args)
     return ours(args)
