@@ -67,7 +67,7 @@ Session::Session(const Model* m, int64_t max_seq) : m_(m), max_seq_(max_seq) {
   {
     const int64_t stages = (max_seq + kPositionsPerSplit - 1) / kPositionsPerSplit;
     const int64_t per_head = std::max(1, m->num_sms() / c.n_kv_heads);
-    n_splits_ = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({stages, per_head, kMaxAttnSplits})));
+    n_splits_ = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({stages, per_head, kMaxAttnCluster})));
     // RPGB_ATTN_SPLITS caps the split count (more 128-position stages per
     // block); used by tests to exercise multi-stage blocks on short models.
     if (const char* e = std::getenv("RPGB_ATTN_SPLITS")) {
@@ -75,7 +75,15 @@ Session::Session(const Model* m, int64_t max_seq) : m_(m), max_seq_(max_seq) {
       if (cap >= 1) n_splits_ = std::min(n_splits_, cap);
     }
   }
-  const int am_grid = MatvecGrid(c.vocab, 4, m->num_sms());
+  loop_splits_ = LoopSplits(c.n_kv_heads, m->num_sms(), max_seq);
+  if (const char* e = std::getenv("RPGB_ATTN_SPLITS")) {
+    const int cap = std::atoi(e);
+    if (cap >= 1) loop_splits_ = std::min(loop_splits_, cap);
+  }
+  const size_t part_floats = AttentionPartialFloats(c.n_kv_heads, c.group(), n_splits_);
+  ll_words_ = static_cast<size_t>(c.hidden) + (c.q_dim() + 2 * c.kv_dim()) + c.ffn +
+              LoopPartialWords(c.n_kv_heads, c.group(), loop_splits_);
+  const int am_grid = std::max(MatvecGrid(c.vocab, 4, m->num_sms()), m->num_sms());
   const int qkv = c.q_dim() + 2 * c.kv_dim();
   Carver cv;
   cv.Add(sizeof(float) * c.hidden);   // x
@@ -87,7 +95,7 @@ Session::Session(const Model* m, int64_t max_seq) : m_(m), max_seq_(max_seq) {
   cv.Add(sizeof(int64_t));            // pos
   cv.Add(sizeof(int32_t));            // tok
   cv.Add(sizeof(int32_t) * (max_seq + 1));
-  cv.Add(sizeof(float) * AttentionPartialFloats(c.n_kv_heads, c.group(), n_splits_));
+  cv.Add(sizeof(float) * part_floats);
   cv.Add(sizeof(uint32_t) * (c.n_kv_heads + 1));
   cv.Add(sizeof(float) * am_grid);
   cv.Add(sizeof(int32_t) * am_grid);
@@ -96,6 +104,10 @@ Session::Session(const Model* m, int64_t max_seq) : m_(m), max_seq_(max_seq) {
   cv.Add(sizeof(int32_t) * kCandBlocks);
   cv.Add(sizeof(int32_t));
   cv.Add(sizeof(unsigned));
+  cv.Add(sizeof(unsigned));                   // grid barrier word
+  cv.Add(sizeof(int32_t));                    // steps done
+  cv.Add(sizeof(int32_t) * kLoopMaxStop);     // stop ids
+  cv.Add(sizeof(uint64_t) * ll_words_);       // tagged words of the decode loop
   RPGB_CUDA(cudaMalloc(&dec_arena_, cv.total()));
   RPGB_CUDA(cudaMemsetAsync(dec_arena_, 0, cv.total(), stream_));
   cv.Begin(dec_arena_);
@@ -108,7 +120,7 @@ Session::Session(const Model* m, int64_t max_seq) : m_(m), max_seq_(max_seq) {
   pos_ = cv.Take<int64_t>(1);
   tok_ = cv.Take<int32_t>(1);
   out_ids_ = cv.Take<int32_t>(max_seq + 1);
-  attn_part_ = cv.Take<float>(AttentionPartialFloats(c.n_kv_heads, c.group(), n_splits_));
+  attn_part_ = cv.Take<float>(part_floats);
   tickets_ = cv.Take<uint32_t>(c.n_kv_heads + 1);
   am_val_ = cv.Take<float>(am_grid);
   am_idx_ = cv.Take<int32_t>(am_grid);
@@ -117,6 +129,11 @@ Session::Session(const Model* m, int64_t max_seq) : m_(m), max_seq_(max_seq) {
   cand_cnt_ = cv.Take<int32_t>(kCandBlocks);
   flag_ = cv.Take<int32_t>(1);
   err_ = cv.Take<unsigned>(1);
+  bar_ = cv.Take<unsigned>(1);
+  steps_done_ = cv.Take<int32_t>(1);
+  stop_dev_ = cv.Take<int32_t>(kLoopMaxStop);
+  ll_ = cv.Take<uint64_t>(ll_words_);  // zeroed with the arena: tag 0 is never a valid tag
+  RPGB_CUDA(cudaMallocHost(&loop_host_, sizeof(int32_t)));
   RPGB_CUDA(cudaStreamSynchronize(stream_));
 }
 
@@ -131,6 +148,7 @@ Session::~Session() {
   cudaFree(trace_rec_);
   cudaFree(trace_count_);
   if (host_ids_ != nullptr) cudaFreeHost(host_ids_);
+  if (loop_host_ != nullptr) cudaFreeHost(loop_host_);
   if (stream_ != nullptr) cudaStreamDestroy(stream_);
 }
 
@@ -463,6 +481,10 @@ int Session::Generate(const SampleOpts& opt, uint64_t seed, int32_t max_tokens, 
   }
   EnqueueSample(opt, seed, 0);
 
+  if (LoopSupportsGroup(c.group()) && std::getenv("RPGB_DECODE_GRAPH") == nullptr) {
+    return GenerateLoop(opt, seed, max_tokens, stop, n_stop, out, step_logits, start);
+  }
+
   // (re)record the step graph when the sampling parameters change
   if (graph_ == nullptr || !SameOpts(opt, graph_opt_) || seed != graph_seed_) {
     DropGraph();
@@ -535,6 +557,150 @@ int Session::Generate(const SampleOpts& opt, uint64_t seed, int32_t max_tokens, 
   const bool ran_past = launched > produced;
   len_ = start + produced;
   // after a stop inside a chunk the device logits belong to a later step
+  logits_valid_ = !ran_past;
+  if (ran_past) {
+    RPGB_CUDA(cudaMemcpyAsync(pos_, &len_, sizeof(int64_t), cudaMemcpyHostToDevice, s));
+    RPGB_CUDA(cudaStreamSynchronize(s));
+  }
+  return produced;
+}
+
+LoopParams Session::MakeLoopParams(const SampleOpts& opt, uint64_t seed) const {
+  const ModelMeta& c = m_->meta();
+  LoopParams lp;
+  lp.layers = m_->layers_dev();
+  lp.n_layers = c.n_layers;
+  lp.embd = m_->embd();
+  lp.lm_head = m_->lm_head();
+  lp.out_norm = m_->out_norm();
+  lp.rope = m_->rope();
+  lp.hidden = c.hidden;
+  lp.n_heads = c.n_heads;
+  lp.n_kv = c.n_kv_heads;
+  lp.ffn = c.ffn;
+  lp.vocab = c.vocab;
+  lp.max_seq = static_cast<int32_t>(max_seq_);
+  lp.eps = c.rms_eps;
+  lp.scale = 1.0f / sqrtf(static_cast<float>(c.head_dim));
+  lp.kc = kc_;
+  lp.vc = vc_;
+  lp.layer_elems = static_cast<int64_t>(layer_elems_);
+  lp.v_minus_k = reinterpret_cast<const char*>(vc_) - reinterpret_cast<const char*>(kc_);
+  lp.llx = ll_;
+  lp.llqkv = lp.llx + c.hidden;
+  lp.llh = lp.llqkv + (c.q_dim() + 2 * c.kv_dim());
+  lp.llrec = lp.llh + c.ffn;
+  lp.logits = logits_;
+  lp.probs = probs_;
+  lp.pos = pos_;
+  lp.tok = tok_;
+  lp.out_ids = out_ids_;
+  lp.temperature = opt.temperature;
+  lp.top_k = opt.top_k;
+  lp.top_p = opt.top_p;
+  lp.seed = seed;
+  const int sms = m_->num_sms();
+  const int lm_rows_per_block = (m_->lm_head().rows / 16 + sms - 1) / sms * 16;
+  if (!(opt.temperature > 0.0f)) {
+    lp.mode = 0;
+  } else if (opt.top_k > 1 && opt.top_k <= kFastTopK && opt.top_k < c.vocab && sms <= kCandBlocks &&
+             lm_rows_per_block <= 2048) {
+    lp.mode = 1;
+  } else {
+    lp.mode = 2;
+  }
+  lp.cand_val = cand_val_;
+  lp.cand_idx = cand_idx_;
+  lp.cand_cnt = cand_cnt_;
+  lp.am_val = am_val_;
+  lp.am_idx = am_idx_;
+  lp.steps_done = steps_done_;
+  lp.stop = stop_dev_;
+  lp.bar = bar_;
+  lp.err = err_;
+  lp.splits = loop_splits_;
+  if (trace_rec_ != nullptr) {
+    lp.trace.rec = trace_rec_;
+    lp.trace.count = trace_count_;
+    lp.trace.cap = trace_cap_;
+    lp.trace.id = 0;
+  }
+  return lp;
+}
+
+// The decode loop in one cooperative kernel per chunk of steps (k_step.cu).
+// The first token is sampled from the current logits by the standalone
+// sampler (counter = len); the kernel then forwards it and every following
+// token, stopping on a stop id by itself when the list fits on the device.
+int Session::GenerateLoop(const SampleOpts& opt, uint64_t seed, int32_t max_tokens, const int32_t* stop,
+                          int32_t n_stop, int32_t* out, float* step_logits, int64_t start) {
+  const ModelMeta& c = m_->meta();
+  const cudaStream_t s = stream_;
+  if (host_ids_cap_ < max_tokens) {
+    if (host_ids_ != nullptr) cudaFreeHost(host_ids_);
+    host_ids_ = nullptr;
+    RPGB_CUDA(cudaMallocHost(&host_ids_, sizeof(int32_t) * max_tokens));
+    host_ids_cap_ = max_tokens;
+  }
+  LoopParams lp = MakeLoopParams(opt, seed);
+  const bool dev_stop = n_stop <= kLoopMaxStop;
+  if (dev_stop && n_stop > 0) {
+    RPGB_CUDA(cudaMemcpyAsync(stop_dev_, stop, sizeof(int32_t) * n_stop, cudaMemcpyHostToDevice, s));
+  }
+  lp.n_stop = dev_stop ? n_stop : 0;
+  // With stop ids the device cannot see, chunks stay short so little work runs past a stop.
+  const int chunk = step_logits != nullptr ? 1 : (dev_stop ? max_tokens : 8);
+  int produced = 0, launched = 0;
+  bool stopped = false;
+  while (produced < max_tokens && !stopped) {
+    const int todo = std::min(chunk, max_tokens - produced);
+    lp.n_steps = todo;
+    const uint32_t need = LoopTagsPerLaunch(c.n_layers, todo);
+    if (epoch_ > 0xFFFFFFFFu - need) {  // tags would wrap: clear every tag and start over
+      RPGB_CUDA(cudaMemsetAsync(ll_, 0, sizeof(uint64_t) * ll_words_, s));
+      epoch_ = 1;
+    }
+    lp.epoch0 = epoch_;
+    epoch_ += need;
+    LaunchDecodeLoop(lp, c.group(), m_->num_sms(), s);
+    loop_ready_ = true;
+    if (step_logits != nullptr && produced + 1 < max_tokens) {
+      RPGB_CUDA(cudaMemcpyAsync(step_logits + static_cast<int64_t>(produced + 1) * c.vocab, logits_,
+                                sizeof(float) * c.vocab, cudaMemcpyDeviceToHost, s));
+    }
+    RPGB_CUDA(cudaMemcpyAsync(loop_host_, steps_done_, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    RPGB_CUDA(cudaMemcpyAsync(host_ids_ + produced, out_ids_ + start + produced, sizeof(int32_t) * todo,
+                              cudaMemcpyDeviceToHost, s));
+    RPGB_CUDA(cudaStreamSynchronize(s));
+    const int done = *loop_host_;
+    unsigned err = 0;
+    RPGB_CUDA(cudaMemcpy(&err, err_, sizeof(unsigned), cudaMemcpyDeviceToHost));
+    if (err != 0 || done < 1 || done > todo) {
+      RPGB_CUDA(cudaMemset(err_, 0, sizeof(unsigned)));
+      len_ = start + produced;
+      logits_valid_ = false;
+      Throw("decode loop failed (device error flags 0x%x, %d of %d steps): a bounded device wait gave up", err,
+            done, todo);
+    }
+    graph_launches_ += done;
+    launched += done;
+    int take = done;
+    for (int i = 0; i < done; ++i) {
+      const int32_t id = host_ids_[produced + i];
+      bool is_stop = false;
+      for (int j = 0; j < n_stop; ++j) is_stop = is_stop || stop[j] == id;
+      if (is_stop) {
+        take = i + 1;
+        stopped = true;
+        break;
+      }
+    }
+    produced += take;
+  }
+  kernels_per_step_ = 1;
+  std::memcpy(out, host_ids_, sizeof(int32_t) * produced);
+  const bool ran_past = launched > produced;
+  len_ = start + produced;
   logits_valid_ = !ran_past;
   if (ran_past) {
     RPGB_CUDA(cudaMemcpyAsync(pos_, &len_, sizeof(int64_t), cudaMemcpyHostToDevice, s));

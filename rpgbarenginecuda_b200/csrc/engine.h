@@ -57,7 +57,7 @@ class Session {
   // Device pointers for instrumentation / tests.
   const float* logits_dev() const { return logits_; }
   int graph_launches() const { return graph_launches_; }
-  bool graph_ready() const { return graph_ != nullptr; }
+  bool graph_ready() const { return graph_ != nullptr || loop_ready_; }
   int kernels_per_step() const { return kernels_per_step_; }
 
   // Device timeline of the decode-step launches (see Trace in kernels.h).
@@ -69,6 +69,9 @@ class Session {
 
  private:
   void EnqueueStep(const SampleOpts& opt, uint64_t seed);
+  int GenerateLoop(const SampleOpts& opt, uint64_t seed, int32_t max_tokens, const int32_t* stop, int32_t n_stop,
+                   int32_t* out, float* step_logits, int64_t start);
+  LoopParams MakeLoopParams(const SampleOpts& opt, uint64_t seed) const;
   void EnqueueSample(const SampleOpts& opt, uint64_t seed, int pos_bump, bool pdl = false, int32_t trace_id = -1);
   void EnsurePrefill(int64_t n);
   void DropGraph();
@@ -100,6 +103,16 @@ class Session {
   int32_t* flag_ = nullptr;
   unsigned* err_ = nullptr;  // set by a bounded device wait that gave up
   int n_splits_ = 1;
+  // decode loop kernel state
+  unsigned* bar_ = nullptr;       // grid barrier word
+  int32_t* steps_done_ = nullptr;
+  int32_t* stop_dev_ = nullptr;   // [kLoopMaxStop]
+  int32_t* loop_host_ = nullptr;  // pinned: steps done
+  int loop_splits_ = 1;
+  bool loop_ready_ = false;
+  uint64_t* ll_ = nullptr;  // tagged words (x, qkv, ffn activation, attention records)
+  size_t ll_words_ = 0;
+  uint32_t epoch_ = 1;      // first tag base of the next launch
 
   // prefill scratch (grow-only)
   int64_t pf_cap_ = 0;

@@ -323,83 +323,100 @@ __global__ void __launch_bounds__(128) AttnKernel(const AttnParams p) {
 
 namespace {
 
-// ---- decode attention with the split's K/V staged in shared memory
+// ---- decode attention: one thread-block cluster per KV head
 //
-// Block (split s, KV head h), 8 warps, owns a run of 128-position stages; the
-// number of splits is bounded by the engine (about one block per SM), so
-// long contexts give each block several stages, processed with an online
-// softmax.  K and V of a stage arrive by two 1-D TMA bulk copies into single
-// K / V buffers: the first stage is requested before griddepcontrol.wait
-// (rows below the current position were written by earlier steps), the next
-// stage's K as soon as the scores of the current stage are done, its V after
-// the V pass.  The current position's row is normalised, rotated and written
-// by this kernel.  Scores and V: warp w takes positions w, w + 8, ...; lane l
-// holds dimensions 4l .. 4l+3 (8-byte row loads, a warp reads a whole row),
-// so the positions of a warp are independent chains; the per-warp V partials
-// are combined once at the end.
+// The splits of KV head h are the blocks of one cluster (at most 8, one
+// block per split), each owning a run of 128-position stages; long contexts
+// give each block several stages.  K and V of a stage arrive by two 1-D TMA
+// bulk copies into single K / V buffers: the first stage is requested before
+// griddepcontrol.wait (rows below the current position were written by
+// earlier steps), the next stage's K as soon as the scores of the current
+// stage are done, its V after the V pass.  The current position's row is
+// normalised, rotated and written by the block that owns it.
+//
+// Inside a block (8 warps) every warp keeps its own online softmax over its
+// positions w, w + 8, ...: scores use 8 lanes per position (4 positions per
+// pass, 3-step shuffle reductions), the V pass one lane per 4 dimensions.
+// The warps are combined once per block, and the blocks of the cluster once,
+// through distributed shared memory: no partials in global memory, no
+// tickets, no fences.
 constexpr int kSP = kAttnSplitPositions;
-constexpr int kAT = 256;  // threads of the decode attention block
-constexpr int kAW = kAT / 32;
+constexpr int kMaxCluster = kMaxAttnCluster;
+// Threads of the decode attention block: 8 warps at <= 128 registers, so a
+// block shares its SM with a matvec block (programmatic launch overlap).
+__host__ __device__ constexpr int AttnThreads(int /*G*/) { return 256; }
 
-__host__ __device__ constexpr size_t AttnDynSmem(int G) {
-  return 2 * static_cast<size_t>(kSP) * D * sizeof(__half) + static_cast<size_t>(kAW) * G * D * sizeof(float) + 16;
+__host__ __device__ constexpr size_t AttnDynSmem(int /*G*/) {
+  return 2 * static_cast<size_t>(kSP) * D * sizeof(__half) + 16;
 }
 
-template <int G>
-__device__ __forceinline__ void BlockMax8(float (&v)[G], float* sh) {
+template <int N, int NW>
+__device__ __forceinline__ void BlockSumW(double (&v)[N], double* sh) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   __syncthreads();
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    v[g] = dev::WarpMax(v[g]);
-    if (lane == 0) sh[warp * G + g] = v[g];
-  }
-  __syncthreads();
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float m = sh[g];
-#pragma unroll
-    for (int w = 1; w < kAW; ++w) m = fmaxf(m, sh[w * G + g]);
-    v[g] = m;
-  }
-}
-
-template <int G>
-__device__ __forceinline__ void BlockSum8(double (&v)[G], double* sh) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  __syncthreads();
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
+  for (int g = 0; g < N; ++g) {
     v[g] = dev::WarpSumD(v[g]);
-    if (lane == 0) sh[warp * G + g] = v[g];
+    if (lane == 0) sh[warp * N + g] = v[g];
   }
   __syncthreads();
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
+  for (int g = 0; g < N; ++g) {
     double t = sh[g];
 #pragma unroll
-    for (int w = 1; w < kAW; ++w) t += sh[w * G + g];
+    for (int w = 1; w < NW; ++w) t += sh[w * N + g];
     v[g] = t;
   }
 }
 
+__device__ __forceinline__ uint32_t ClusterRank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void ClusterSync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of `p` (this block's shared memory) in block `rank` of the cluster.
+__device__ __forceinline__ uint32_t MapRank(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(dev::SmemAddr(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float LdCluster(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ double LdClusterD(uint32_t addr) {
+  double v;
+  asm volatile("ld.shared::cluster.f64 %0, [%1];" : "=d"(v) : "r"(addr) : "memory");
+  return v;
+}
+
 template <int G>
-__global__ void __launch_bounds__(kAT) AttnDecodeKernel(const AttnParams p) {
+__global__ void __launch_bounds__(AttnThreads(G), 2) AttnDecodeKernel(const AttnParams p) {
+  constexpr int kAT = AttnThreads(G);
+  constexpr int kAW = kAT / 32;
+  static_assert(static_cast<size_t>(kAW) * G * D * sizeof(float) <= 2 * kSP * D * sizeof(__half),
+                "the warp partials must fit in the K/V buffers");
   extern __shared__ __align__(128) uint8_t dsm[];
   __half* Ks = reinterpret_cast<__half*>(dsm);
   __half* Vs = Ks + kSP * D;
-  float* vred = reinterpret_cast<float*>(Vs + kSP * D);  // [kAW][G][D]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(vred + kAW * G * D);  // [0] K, [1] V
+  float* vred = reinterpret_cast<float*>(dsm);  // [kAW][G][D], reuses Ks/Vs after the last stage
+  uint64_t* bars = reinterpret_cast<uint64_t*>(Vs + kSP * D);  // [0] K, [1] V
   __shared__ __align__(16) float qs[G + 1][D];
   __shared__ float sc[G][kSP];
   __shared__ double dsh[kAW * (G + 1)];
   __shared__ float fsh[kAW * G];
-  __shared__ float s_wm[kMaxSplits][G];
-  __shared__ double s_wl[kMaxSplits][G];
-  __shared__ int s_last;
+  // this block's result, read by the cluster's rank 0
+  __shared__ float rec_m[G];
+  __shared__ double rec_l[G];
+  __shared__ __align__(16) float rec_o[G][D];
 
   dev::TraceScope trace(p.trace);
-  const int s = blockIdx.x, h = blockIdx.y;
+  const int h = blockIdx.y;
+  const int s = static_cast<int>(ClusterRank());  // == blockIdx.x (one cluster spans the splits)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   // The position counter of this step was written before the step started
   // (previous graph launch / host copy), so it may be read before the wait.
@@ -407,13 +424,11 @@ __global__ void __launch_bounds__(kAT) AttnDecodeKernel(const AttnParams p) {
   const int64_t L = pos + 1;
   const int stages = static_cast<int>((L + kSP - 1) / kSP);
   const int per = (stages + p.n_splits - 1) / p.n_splits;  // stages per split
-  const int active = (stages + per - 1) / per;
-  if (s >= active) return;  // nothing to do at this length (no memory touched)
-  const int st0 = s * per, st1 = st0 + per < stages ? st0 + per : stages;
+  const int st0 = s * per < stages ? s * per : stages;
+  const int st1 = st0 + per < stages ? st0 + per : stages;  // st0 == st1: idle block (still merges)
   __half* kbase = p.kc + static_cast<int64_t>(h) * p.max_seq * D;
   __half* vbase = p.vc + static_cast<int64_t>(h) * p.max_seq * D;
-  // rows of stage st already in the cache (below the current position)
-  auto old_rows = [&](int st) -> int {
+  auto old_rows = [&](int st) -> int {  // rows of stage st already in the cache
     const int64_t r = pos - static_cast<int64_t>(st) * kSP;
     return static_cast<int>(r < kSP ? r : kSP);
   };
@@ -430,8 +445,10 @@ __global__ void __launch_bounds__(kAT) AttnDecodeKernel(const AttnParams p) {
     dev::MbarInit(bars + 0, 1);
     dev::MbarInit(bars + 1, 1);
     dev::MbarInitFence();
-    issue(0, st0);
-    issue(1, st0);
+    if (st0 < st1) {
+      issue(0, st0);
+      issue(1, st0);
+    }
   }
   // constants of this step (norm weights, the RoPE row of pos): before the wait
   const bool dimt = tid < D;
@@ -453,7 +470,7 @@ __global__ void __launch_bounds__(kAT) AttnDecodeKernel(const AttnParams p) {
     double ss[G + 1];
 #pragma unroll
     for (int g = 0; g <= G; ++g) ss[g] = static_cast<double>(vk[g]) * vk[g];
-    BlockSum8<G + 1>(ss, dsh);
+    BlockSumW<G + 1, kAW>(ss, dsh);
     if (dimt) {
 #pragma unroll
       for (int g = 0; g <= G; ++g) {
@@ -463,19 +480,18 @@ __global__ void __launch_bounds__(kAT) AttnDecodeKernel(const AttnParams p) {
     }
     __syncthreads();
     if (tid < D / 2) {
-      const float c = rc, sn = rs;
 #pragma unroll
       for (int g = 0; g <= G; ++g) {
         const float a = qs[g][tid], b = qs[g][tid + D / 2];
-        qs[g][tid] = a * c - b * sn;
-        qs[g][tid + D / 2] = b * c + a * sn;
+        qs[g][tid] = a * rc - b * rs;
+        qs[g][tid + D / 2] = b * rc + a * rs;
       }
     }
     __syncthreads();
     if (dimt) {
       kh = __float2half_rn(qs[G][tid]);
       vh = __float2half_rn(vv);
-      if (pos < static_cast<int64_t>(st1) * kSP) {  // this block owns the new position (fp16, RNE)
+      if (st0 < st1 && pos < static_cast<int64_t>(st1) * kSP) {  // this block owns the new position
         kbase[pos * D + tid] = kh;
         vbase[pos * D + tid] = vh;
       }
@@ -483,8 +499,8 @@ __global__ void __launch_bounds__(kAT) AttnDecodeKernel(const AttnParams p) {
   }
   trace.Mark(1);  // q/k normalised and rotated
 
-  // scores: 8 lanes per position (4 positions per warp pass); lane sub = lane & 7
-  // holds dimensions 8 sub .. 8 sub + 7 and 64 + 8 sub .. +7 of every query head
+  // scores: 8 lanes per position; lane sub holds dimensions 8 sub .. +7 and
+  // 64 + 8 sub .. +7 of every query head (scaled by 1/sqrt(128))
   const int sub = lane & 7, pp = lane >> 3;
   float qv[G][16];
 #pragma unroll
@@ -503,6 +519,8 @@ __global__ void __launch_bounds__(kAT) AttnDecodeKernel(const AttnParams p) {
       qv[g][8 * hf + 7] = qb.w * p.scale;
     }
   }
+  constexpr int kPasses = kSP / (4 * kAW);  // score passes per stage
+  constexpr int kPerWarp = kSP / kAW;       // positions per warp per stage
   float m[G], acc[G][4];
   double l[G];
 #pragma unroll
@@ -515,16 +533,22 @@ __global__ void __launch_bounds__(kAT) AttnDecodeKernel(const AttnParams p) {
   for (int st = st0; st < st1; ++st) {
     const uint32_t par = static_cast<uint32_t>((st - st0) & 1);
     const int n_old = old_rows(st);
-    const int n = static_cast<int>(L - static_cast<int64_t>(st) * kSP < kSP ? L - static_cast<int64_t>(st) * kSP : kSP);
+    const int64_t rem = L - static_cast<int64_t>(st) * kSP;
+    const int n = static_cast<int>(rem < kSP ? rem : kSP);
     if (n_old > 0 && !dev::MbarWait(bars + 0, par)) {
       if (tid == 0 && p.err != nullptr) atomicOr(p.err, 2u);
     }
-    if (n_old < n && tid < D) Ks[n_old * D + tid] = kh;  // the current position (last stage only)
-    __syncthreads();
-
-    // ---- scores: warp w, positions w + 8 (4 t + pp) (independent per position)
-#pragma unroll 2
-    for (int t = 0; t < kSP / (4 * kAW); ++t) {
+    if (n_old < n) {  // the stage holding the current position: publish its row
+      if (dimt) {
+        Ks[n_old * D + tid] = kh;
+        Vs[n_old * D + tid] = vh;
+      }
+      __syncthreads();
+    }
+    // ---- scores of this warp's positions w + kAW (4 t + pp)
+    float sv[G][kPasses];
+#pragma unroll
+    for (int t = 0; t < kPasses; ++t) {
       const int j = warp + kAW * (4 * t + pp);
       float d[G];
 #pragma unroll
@@ -550,152 +574,131 @@ __global__ void __launch_bounds__(kAT) AttnDecodeKernel(const AttnParams p) {
 #pragma unroll
         for (int g = 0; g < G; ++g) d[g] += __shfl_xor_sync(0xFFFFFFFFu, d[g], o);
       }
-      if (sub == 0 && j < n) {
 #pragma unroll
-        for (int g = 0; g < G; ++g) sc[g][j] = d[g];
+      for (int g = 0; g < G; ++g) sv[g][t] = j < n ? d[g] : -INFINITY;
+    }
+    if (st + 1 < st1) {
+      __syncthreads();  // all reads of Ks done
+      if (tid == 0) {
+        dev::FenceProxyAsync();
+        issue(0, st + 1);
       }
     }
-    __syncthreads();  // scores published; all reads of Ks done
-    if (tid == 0 && st + 1 < st1) {
-      dev::FenceProxyAsync();
-      issue(0, st + 1);
-    }
-    float cm[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) cm[g] = tid < n ? sc[g][tid] : -INFINITY;
-    BlockMax8<G>(cm, fsh);
-    double cs[G];
-    float alpha[G];
+    // ---- this warp's online softmax
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      const float nm = fmaxf(m[g], cm[g]);
-      float e = 0.f;
-      if (tid < n) {
-        e = expf(sc[g][tid] - nm);
-      }
-      cs[g] = static_cast<double>(e);
-      alpha[g] = m[g] == -INFINITY ? 0.f : expf(m[g] - nm);
+      float mx = sv[g][0];
+#pragma unroll
+      for (int t = 1; t < kPasses; ++t) mx = fmaxf(mx, sv[g][t]);
+      mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 8));
+      mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 16));
+      const float nm = fmaxf(m[g], mx);
+      const float alpha = m[g] == -INFINITY ? 0.f : expf(m[g] - nm);
       m[g] = nm;
-      if (tid < kSP) sc[g][tid] = e;  // own slot only: no other thread reads it before the barrier below
+      double ps = 0.0;
+#pragma unroll
+      for (int t = 0; t < kPasses; ++t) {
+        const float e = sv[g][t] == -INFINITY ? 0.f : expf(sv[g][t] - nm);
+        if (sub == 0) {
+          sc[g][warp + kAW * (4 * t + pp)] = e;
+          ps += static_cast<double>(e);
+        }
+      }
+      ps = dev::WarpSumD(ps);
+      l[g] = l[g] * static_cast<double>(alpha) + ps;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[g][e] *= alpha;
     }
     if (n_old > 0 && !dev::MbarWait(bars + 1, par)) {
       if (tid == 0 && p.err != nullptr) atomicOr(p.err, 2u);
     }
-    if (n_old < n && tid < D) Vs[n_old * D + tid] = vh;
-    BlockSum8<G>(cs, dsh);  // its barriers also publish sc[] and the V row
+    __syncwarp();  // this warp's weights are visible to its lanes
+    // ---- V: the warp's positions; lane holds 4 dimensions
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      l[g] = l[g] * static_cast<double>(alpha[g]) + cs[g];
+    for (int k = 0; k < kPerWarp; ++k) {
+      const int j = warp + kAW * k;
+      if (j < n) {
+        const uint2 raw = *reinterpret_cast<const uint2*>(Vs + j * D + 4 * lane);
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
 #pragma unroll
-      for (int e = 0; e < 4; ++e) acc[g][e] *= alpha[g];
-    }
-    // ---- V: warp w, positions w, w + 8, ...; lane holds 4 dimensions
-#pragma unroll 4
-    for (int j = warp; j < n; j += kAW) {
-      const uint2 raw = *reinterpret_cast<const uint2*>(Vs + j * D + 4 * lane);
-      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float e = sc[g][j];
-        acc[g][0] = fmaf(e, a.x, acc[g][0]);
-        acc[g][1] = fmaf(e, a.y, acc[g][1]);
-        acc[g][2] = fmaf(e, b.x, acc[g][2]);
-        acc[g][3] = fmaf(e, b.y, acc[g][3]);
+        for (int g = 0; g < G; ++g) {
+          const float e = sc[g][j];
+          acc[g][0] = fmaf(e, a.x, acc[g][0]);
+          acc[g][1] = fmaf(e, a.y, acc[g][1]);
+          acc[g][2] = fmaf(e, b.x, acc[g][2]);
+          acc[g][3] = fmaf(e, b.y, acc[g][3]);
+        }
       }
     }
+    __syncwarp();
     if (st + 1 < st1) {
-      __syncthreads();  // all reads of Vs and sc done
+      __syncthreads();  // all reads of Vs done
       if (tid == 0) {
         dev::FenceProxyAsync();
         issue(1, st + 1);
       }
     }
   }
-  // combine the warps' V partials: thread d (< 128) ends up with dimension d
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    *reinterpret_cast<float4*>(vred + (warp * G + g) * D + 4 * lane) =
-        make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
-  }
+  // ---- combine this block's warps (Ks / Vs are free now: vred reuses them)
   __syncthreads();
-  trace.Mark(2);  // all stages done
-  float o[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float t = 0.f;
-    if (tid < D) {
-#pragma unroll
-      for (int w = 0; w < kAW; ++w) t += vred[(w * G + g) * D + tid];
-    }
-    o[g] = t;
-  }
-
-  if (active == 1) {
-    if (tid < D) {
-#pragma unroll
-      for (int g = 0; g < G; ++g) p.out[(h * G + g) * D + tid] = o[g] * static_cast<float>(1.0 / l[g]);
-    }
-    return;
-  }
-
-  // ---- split-K: publish (m, l, acc) and let the last block of this head merge
-  constexpr int kRec = D + 2;
-  if (tid < D) {
+  if (lane == 0) {
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      float* rec = p.part + (static_cast<int64_t>(h * p.n_splits + s) * G + g) * kRec;
-      if (tid == 0) {
-        rec[0] = m[g];
-        rec[1] = static_cast<float>(l[g]);
-      }
-      rec[2 + tid] = o[g];
+      fsh[warp * G + g] = m[g];
+      dsh[warp * G + g] = l[g];
     }
   }
-  __threadfence();
   __syncthreads();
-  if (tid == 0) {
-    const unsigned tk = atomicAdd(p.ticket + h, 1u);
-    s_last = tk == static_cast<unsigned>(active - 1) ? 1 : 0;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float M = fsh[g];
+#pragma unroll
+    for (int w = 1; w < kAW; ++w) M = fmaxf(M, fsh[w * G + g]);
+    const float sw = m[g] == -INFINITY ? 0.f : expf(m[g] - M);
+    *reinterpret_cast<float4*>(vred + (warp * G + g) * D + 4 * lane) =
+        make_float4(acc[g][0] * sw, acc[g][1] * sw, acc[g][2] * sw, acc[g][3] * sw);
+    if (tid == 0) {
+      double Lg = 0.0;
+#pragma unroll
+      for (int w = 0; w < kAW; ++w) {
+        const float mw = fsh[w * G + g];
+        Lg += mw == -INFINITY ? 0.0 : static_cast<double>(expf(mw - M)) * dsh[w * G + g];
+      }
+      rec_m[g] = M;
+      rec_l[g] = Lg;
+    }
   }
   __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  for (int i = tid; i < active * G; i += kAT) {
-    const int sp = i / G, g = i - sp * G;
-    const float* rec = p.part + (static_cast<int64_t>(h * p.n_splits + sp) * G + g) * kRec;
-    s_wm[sp][g] = __ldcg(rec);
-    s_wl[sp][g] = static_cast<double>(__ldcg(rec + 1));
-  }
-  __syncthreads();
-  // thread = (head, dimension) pairs; the split partials are loaded in batches
   for (int i = tid; i < G * D; i += kAT) {
     const int g = i / D, d = i - g * D;
-    float M = -INFINITY;
-    for (int sp = 0; sp < active; ++sp) M = fmaxf(M, s_wm[sp][g]);
-    double den = 0.0;
-    float num = 0.f;
-    for (int sp0 = 0; sp0 < active; sp0 += 8) {
-      float pv[8];
+    float t = 0.f;
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int sp = sp0 + u;
-        pv[u] = sp < active ? __ldcg(p.part + (static_cast<int64_t>(h * p.n_splits + sp) * G + g) * kRec + 2 + d) : 0.f;
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int sp = sp0 + u;
-        if (sp < active) {
-          const float ms = s_wm[sp][g];
-          const float w = ms == -INFINITY ? 0.f : expf(ms - M);
-          den += static_cast<double>(w) * s_wl[sp][g];
-          num = fmaf(w, pv[u], num);
-        }
-      }
-    }
-    p.out[(h * G + g) * D + d] = num * static_cast<float>(1.0 / den);
+    for (int w = 0; w < kAW; ++w) t += vred[(w * G + g) * D + d];
+    rec_o[g][d] = t;
   }
-  if (tid == 0) p.ticket[h] = 0u;
+  trace.Mark(2);  // this block's part done
+  // ---- combine the cluster's blocks in rank 0 through distributed shared memory
+  ClusterSync();
+  if (s == 0) {
+    const int nb = static_cast<int>(gridDim.x);
+    for (int i = tid; i < G * D; i += kAT) {
+      const int g = i / D, d = i - g * D;
+      float M = -INFINITY;
+      for (int r = 0; r < nb; ++r) M = fmaxf(M, LdCluster(MapRank(&rec_m[g], r)));
+      double den = 0.0;
+      float num = 0.f;
+      for (int r = 0; r < nb; ++r) {
+        const float mr = LdCluster(MapRank(&rec_m[g], r));
+        if (mr == -INFINITY) continue;
+        const float w = expf(mr - M);
+        den += static_cast<double>(w) * LdClusterD(MapRank(&rec_l[g], r));
+        num = fmaf(w, LdCluster(MapRank(&rec_o[g][d], r)), num);
+      }
+      p.out[(h * G + g) * D + d] = num * static_cast<float>(1.0 / den);
+    }
+  }
+  ClusterSync();  // no block leaves while rank 0 still reads its shared memory
 }
 
 // Prefill: per token, q heads -> q_out (normalised + rotated), k heads -> cache
@@ -776,7 +779,10 @@ void LaunchAttention(const AttnParams& p, int n_queries, cudaStream_t s, bool pd
       case 8: fn = reinterpret_cast<const void*>(AttnDecodeKernel<8>); break;
       default: Throw("attention: GQA group %d is not supported (1, 2, 4, 8)", G);
     }
-    LaunchKernelArgs(fn, dim3(p.n_splits, p.n_kv), dim3(kAT), AttnDynSmem(G), s, pdl, p);
+    RPGB_CHECK(p.n_splits <= kMaxCluster, "attention: %d splits exceed the cluster limit %d", p.n_splits,
+               kMaxCluster);
+    LaunchKernelClusterArgs(fn, dim3(p.n_splits, p.n_kv), dim3(AttnThreads(G)), AttnDynSmem(G), s, pdl,
+                            static_cast<unsigned>(p.n_splits), p);
     CountLaunches(1);
     return;
   }

@@ -1,0 +1,1354 @@
+// k_step.cu -- the decode loop: n steps of the token loop in one persistent,
+// cooperative kernel launch (one block of 16 warps per SM).
+//
+// Replaces, per step, GpuForwardStepDev's launches (src/qwen3_gpu.cu:289-330,
+// GpuForwardLayer at 47-113: RMSNorm, q/k/v projections, QK-norm, RoPE, KV
+// write, attention, o projection + residual, RMSNorm, gate/up, SiLU*up, down
+// + residual; final norm and lm_head) and the sampler launch of the graph /
+// no-graph generate loops (src/qwen3_gpu.cu:451-598).  The arithmetic of every
+// op is the one of the standalone kernels (k_matvec.cu, k_attn.cu,
+// k_sample.cu); what changes is how the step is scheduled:
+//
+//  * phases instead of launches.  A step is 5 phases per layer (qkv,
+//    attention, o, gate/up, down) plus lm_head and the sampler.  Blocks meet
+//    at a grid barrier between phases (one release-add and an acquire poll on
+//    one word per block); the launch is cooperative, so all blocks are
+//    resident and every barrier completes.  Every wait is bounded and reports
+//    through `err`.
+//  * one weight stream per warp across phases and steps.  Each warp owns a
+//    ring of shared-memory slots fed by 1-D TMA bulk copies.  Its lane 0
+//    walks the warp's units of every phase in order -- matvec block groups
+//    of its unit range, or the cached K / V rows of its attention chunks --
+//    and refills a slot as soon as it is consumed, so while a warp waits at a
+//    barrier its ring already holds the next phase's weights.  Weights and
+//    the K/V rows of earlier positions never depend on the running step.
+//  * attention: the blocks of KV head h are `splits` consecutive blocks, each
+//    owning a range of 12-position chunks; warps keep their own online
+//    softmax over their chunks and the block folds them into one partial
+//    record (m, l, o).  The o phase merges the records of all splits while it
+//    builds its input, so there is no ticket and no extra barrier.
+//  * sampling: the lm_head epilogue leaves each block's argmax (greedy) or
+//    the top-k candidates of its own rows (fast path); after one barrier
+//    every block reduces them itself (the result is identical in every
+//    block), so the next step starts without another barrier.  The general
+//    sampler runs in block 0 followed by a barrier.
+#include <algorithm>
+#include <cfloat>
+#include <climits>
+
+#include "common.h"
+#include "kernels.cuh"
+#include "kernels.h"
+#include "mv_dev.cuh"
+#include "sample_dev.cuh"
+
+namespace rpgb {
+namespace {
+
+using namespace mv;
+
+constexpr int kNW = 16;        // warps per block
+constexpr int kNT = 32 * kNW;  // threads per block
+constexpr int kSlot = 3360;    // ring slot: one Q6_K block group (Q4_K 2304 B, a K or V chunk 3072 B)
+constexpr int kChunk = 4;      // attention positions per unit (their K rows, then their V rows at +1024 B)
+constexpr int kD = 128;        // head dimension
+constexpr int kMaxRing = 8;
+constexpr int kSmallCap = 2048;  // fast-path candidates above the lower bound kept in shared memory
+// Tagged words of one attention partial record: o[G][128], m[G], and the
+// denominator l[G] as a float pair (hi, lo = l - hi), padded to an even count
+// so consecutive records stay 16-byte aligned.
+__host__ __device__ constexpr int RecWords(int G) { return (131 * G + 1) & ~1; }
+constexpr int kSliceRows = 2048;
+constexpr int kMaxOwnRows = 64;  // rows of x one block owns in the o / down phases
+constexpr int kMaxLayers = 40;  // lm_head rows of one block for the candidate slices
+constexpr uint32_t kBarLimit = 1u << 22;  // polls of a grid barrier before giving up (seconds)
+
+enum Kind : int { kQkv = 0, kAttn = 1, kO = 2, kGu = 3, kDown = 4, kLm = 5 };
+
+// ------------------------------------------------------------------ shared memory plan
+
+struct Plan {
+  size_t bars, scratch, red, total;
+  // inside the scratch union: matvec prologue
+  size_t bfrag, sx, sscale, xs, merge;
+};
+
+__host__ __device__ inline size_t Al(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+__host__ __device__ inline Plan MakePlan(int ring, int nb_max, int x_max, int scratch_bytes, int max_tiles) {
+  Plan l;
+  l.bars = static_cast<size_t>(kNW) * ring * kSlot;
+  l.scratch = Al(l.bars + static_cast<size_t>(kNW) * ring * 8, 128);
+  l.bfrag = 0;
+  l.sx = l.bfrag + static_cast<size_t>(nb_max) * 1024;
+  l.sscale = l.sx + static_cast<size_t>(nb_max) * 32;
+  l.xs = Al(l.sscale + static_cast<size_t>(nb_max) * 4, 16);
+  l.merge = Al(l.xs + static_cast<size_t>(x_max) * 4, 16);
+  l.red = Al(l.scratch + static_cast<size_t>(scratch_bytes), 16);
+  l.total = l.red + static_cast<size_t>(max_tiles + kNW) * kTile * 4;
+  return l;
+}
+
+// Bytes of the split-merge tables: weights (float) and denominators (double)
+// of every (KV head, split, group member), and 1/L per (KV head, member).
+__host__ __device__ inline size_t MergeBytes(int n_kv, int splits, int group) {
+  return static_cast<size_t>(n_kv) * splits * group * 12 + static_cast<size_t>(n_kv) * group * 4 + 16;
+}
+
+// Bytes of the scratch union for a model (the largest phase user).
+size_t ScratchBytes(int nb_max, int x_max, int group, int n_kv, int splits) {
+  const size_t prologue = Al(Al(static_cast<size_t>(nb_max) * (1024 + 32 + 4), 16) + static_cast<size_t>(x_max) * 4, 16) +
+                          MergeBytes(n_kv, splits, group);
+  const size_t attn = static_cast<size_t>(kNW) * group * kD * 4;
+  const size_t lm = static_cast<size_t>(kSliceRows) * 4 + 2048 * 4;
+  const size_t small = static_cast<size_t>(kSmallCap) * 16;
+  size_t m = prologue;
+  if (attn > m) m = attn;
+  if (lm > m) m = lm;
+  if (small > m) m = small;
+  return Al(m, 128);
+}
+
+// ------------------------------------------------------------------ geometry
+
+struct MvShape {
+  int rows, K;
+};
+
+__device__ __forceinline__ MvShape ShapeOf(const LoopParams& p, int kind) {
+  const int qd = p.n_heads * kD, kvd = p.n_kv * kD;
+  switch (kind) {
+    case kQkv: return {qd + 2 * kvd, p.hidden};
+    case kO: return {p.hidden, qd};
+    case kGu: return {2 * p.ffn, p.hidden};
+    case kDown: return {p.hidden, p.ffn};
+    default: return {p.lm_head.rows, p.hidden};
+  }
+}
+
+struct Geo {
+  int t0, t1, nb, u0, u1;
+  int seg0, uoff0, run0;  // first unit of the warp: segment, unit offset inside it, units to the segment's end
+};
+
+// Segments of a phase's row space: q, k, v for the qkv phase, one matrix otherwise.
+__device__ __forceinline__ int SegTiles(const LoopParams& p, int kind, int seg) {
+  if (kind == kQkv) return seg == 0 ? p.n_heads * kD / kTile : p.n_kv * kD / kTile;
+  return ShapeOf(p, kind).rows / kTile;
+}
+__device__ __forceinline__ int SegOfTile(const LoopParams& p, int kind, int tile, int* seg_t0) {
+  int seg = 0, t0 = 0;
+  if (kind == kQkv) {
+    const int tq = p.n_heads * kD / kTile, tkv = p.n_kv * kD / kTile;
+    if (tile >= tq + tkv) {
+      seg = 2;
+      t0 = tq + tkv;
+    } else if (tile >= tq) {
+      seg = 1;
+      t0 = tq;
+    }
+  }
+  *seg_t0 = t0;
+  return seg;
+}
+
+// Tile range of this block and unit range of `warp` in a matvec phase.
+__device__ __forceinline__ Geo MvGeo(const LoopParams& p, int kind, int warp) {
+  const MvShape sh = ShapeOf(p, kind);
+  Geo g;
+  const int T = sh.rows / kTile;
+  g.t0 = static_cast<int>(static_cast<int64_t>(blockIdx.x) * T / gridDim.x);
+  g.t1 = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * T / gridDim.x);
+  g.nb = sh.K >> 8;
+  const int U = (g.t1 - g.t0) * g.nb;
+  g.u0 = warp * U / kNW;
+  g.u1 = (warp + 1) * U / kNW;
+  const int tile = g.t0 + g.u0 / g.nb, b = g.u0 % g.nb;
+  int st0 = 0;
+  g.seg0 = SegOfTile(p, kind, tile, &st0);
+  g.uoff0 = (tile - st0) * g.nb + b;
+  g.run0 = (st0 + SegTiles(p, kind, g.seg0) - tile) * g.nb - b;
+  return g;
+}
+
+// The geometry of every matvec phase for every warp of this block, computed
+// once per launch (it is the same for all layers and steps).
+struct GeoTable {
+  Geo g[6][kNW];  // indexed by Kind (the attention row is unused)
+};
+
+// Per layer: block-group bases of q, k, v, o, gate/up, down, the four norm
+// weights and which matrices are Q6_K -- a copy of the layer table in shared
+// memory, so the weight stream never waits on a global load.
+struct LayerRow {
+  const uint8_t* w[6];
+  const float* norm[4];  // attn, ffn, q, k
+  uint32_t q6;           // bit i: matrix i is Q6_K (else Q4_K)
+};
+
+__shared__ GeoTable g_geo;
+__shared__ LayerRow g_layers[kMaxLayers];
+
+__device__ __forceinline__ void FillTables(const LoopParams& p) {
+  const int tid = threadIdx.x;
+  if (tid < 6 * kNW) {
+    const int kind = tid / kNW, warp = tid - kind * kNW;
+    if (kind != kAttn) g_geo.g[kind][warp] = MvGeo(p, kind, warp);
+  } else if (tid - 6 * kNW < p.n_layers) {
+    const int l = tid - 6 * kNW;
+    const DevLayer& L = p.layers[l];
+    const DevMat* m[6] = {&L.q, &L.k, &L.v, &L.o, &L.gateup, &L.down};
+    LayerRow r;
+    r.q6 = 0;
+    for (int i = 0; i < 6; ++i) {
+      r.w[i] = m[i]->q;
+      if (m[i]->type != 12u) r.q6 |= 1u << i;
+    }
+    r.norm[0] = L.attn_norm;
+    r.norm[1] = L.ffn_norm;
+    r.norm[2] = L.q_norm;
+    r.norm[3] = L.k_norm;
+    g_layers[l] = r;
+  }
+}
+
+// Matrix `seg` of a phase in layer `layer`: its block groups and type.
+__device__ __forceinline__ int MatIdx(int kind, int seg) {
+  return kind == kQkv ? seg : (kind == kO ? 3 : (kind == kGu ? 4 : 5));
+}
+__device__ __forceinline__ uint32_t SegType(const LoopParams& p, int kind, int layer, int seg) {
+  if (kind == kLm) return p.lm_head.type;
+  return (g_layers[layer].q6 >> MatIdx(kind, seg)) & 1u ? 14u : 12u;
+}
+__device__ __forceinline__ const uint8_t* SegBase(const LoopParams& p, int kind, int layer, int seg) {
+  if (kind == kLm) return p.lm_head.q;
+  return g_layers[layer].w[MatIdx(kind, seg)];
+}
+
+// Splits of a KV head that hold positions at this step: at least two chunks
+// each, so short contexts use few blocks (and the o phase merges few records).
+__device__ __forceinline__ int EffSplits(const LoopParams& p, int64_t pos) {
+  const int n_ch = static_cast<int>((pos + kChunk) / kChunk);  // chunks covering positions 0..pos
+  const int se = (n_ch + 1) / 2;
+  return se < p.splits ? se : p.splits;
+}
+
+struct AttnGeo {
+  int h, c0, c1;  // KV head, chunk range of this block (empty for an idle block)
+};
+
+__device__ __forceinline__ AttnGeo AttnOf(const LoopParams& p, int64_t pos) {
+  AttnGeo a;
+  const int S = p.splits;
+  const int c = static_cast<int>(blockIdx.x);
+  a.h = c / S;
+  const int s = c - a.h * S;
+  const int se = EffSplits(p, pos);
+  if (c >= p.n_kv * S || s >= se) {
+    a.c0 = a.c1 = 0;
+    return a;
+  }
+  const int n_ch = static_cast<int>((pos + kChunk) / kChunk);
+  a.c0 = s * n_ch / se;
+  a.c1 = (s + 1) * n_ch / se;
+  return a;
+}
+
+__device__ __forceinline__ int WarpChunks(const AttnGeo& a, int warp) {
+  const int n = a.c1 - a.c0 - warp;
+  return n > 0 ? (n + kNW - 1) / kNW : 0;
+}
+
+// ------------------------------------------------------------------ the per-warp weight stream
+
+struct Cursor {
+  int step, layer, kind, j, n;
+  int seg, run;        // matvec: segment and units left in the current contiguous run of block groups
+  uint32_t bytes;      // matvec: bytes of one unit of the run
+  const uint8_t* src;  // matvec: next block group; attention: K row 0 of (layer, head)
+  int c0;              // attention: first chunk of this block
+};
+
+// Enters the next phase with units (lane 0).
+__device__ __forceinline__ void NextPhase(const LoopParams& p, const GeoTable& gt, Cursor& c, int64_t pos0,
+                                          int warp) {
+  while (c.j >= c.n && c.step < p.n_steps) {
+    if (c.kind == kLm) {
+      ++c.step;
+      c.layer = 0;
+      c.kind = kQkv;
+    } else if (c.kind == kDown) {
+      ++c.layer;
+      c.kind = c.layer == p.n_layers ? kLm : kQkv;
+    } else {
+      ++c.kind;
+    }
+    c.j = 0;
+    c.n = 0;
+    if (c.step >= p.n_steps) break;
+    if (c.kind == kAttn) {
+      const AttnGeo a = AttnOf(p, pos0 + c.step);
+      c.n = WarpChunks(a, warp);
+      c.c0 = a.c0;
+      c.src = reinterpret_cast<const uint8_t*>(p.kc + static_cast<int64_t>(c.layer) * p.layer_elems +
+                                               static_cast<int64_t>(a.h) * p.max_seq * kD);
+    } else {
+      const Geo& g = gt.g[c.kind][warp];
+      c.n = g.u1 - g.u0;
+      c.run = 0;
+    }
+  }
+}
+
+// Requests unit c.j of the cursor's phase into `dst` and advances (lane 0 only).
+__device__ __forceinline__ void IssueUnit(const LoopParams& p, const GeoTable& gt, Cursor& c, int64_t pos0, int warp,
+                                          uint8_t* dst, uint64_t* bar) {
+  if (c.kind == kAttn) {
+    // K rows then V rows (at +1024 B) of the chunk's positions from earlier steps
+    const int64_t pos = pos0 + c.step;
+    const int64_t r0 = static_cast<int64_t>(c.c0 + warp + kNW * c.j) * kChunk;
+    int64_t n_old = pos - r0;
+    n_old = n_old < 0 ? 0 : (n_old > kChunk ? kChunk : n_old);
+    const uint32_t bytes = static_cast<uint32_t>(n_old) * kD * 2;
+    dev::MbarExpectTx(bar, 2 * bytes);
+    if (bytes > 0) {
+      const uint8_t* src = c.src + r0 * (kD * 2);
+      dev::BulkG2S(dst, src, bytes, bar);
+      dev::BulkG2S(dst + kChunk * kD * 2, src + p.v_minus_k, bytes, bar);
+    }
+  } else {
+    if (c.run == 0) {  // start of the warp's units in this phase, or of the next segment
+      const Geo& g = gt.g[c.kind][warp];
+      int uoff;
+      if (c.j == 0) {
+        c.seg = g.seg0;
+        uoff = g.uoff0;
+        c.run = g.run0;
+      } else {
+        ++c.seg;
+        uoff = 0;
+        c.run = SegTiles(p, c.kind, c.seg) * g.nb;
+      }
+      c.bytes = static_cast<uint32_t>(dev::GroupBytesOf(SegType(p, c.kind, c.layer, c.seg)));
+      c.src = SegBase(p, c.kind, c.layer, c.seg) + static_cast<int64_t>(uoff) * c.bytes;
+    }
+    dev::MbarExpectTx(bar, c.bytes);
+    dev::BulkG2S(dst, c.src, c.bytes, bar);
+    c.src += c.bytes;  // block groups of one matrix are contiguous in tile-major order
+    --c.run;
+  }
+  ++c.j;
+  NextPhase(p, gt, c, pos0, warp);
+}
+
+struct Ring {
+  uint8_t* base;
+  uint64_t* bars;
+  int R;
+  uint32_t kc, ki;  // units consumed / issued by this warp
+  int cs, is;       // ring slots of the next unit to consume / issue
+  uint32_t cpar;    // mbarrier parity of the next unit to consume
+  Cursor cur;       // next unit to issue (meaningful in lane 0)
+  int step;         // the step being consumed
+  bool bad;         // a wait gave up: later waits are skipped (the launch is failing)
+};
+
+// Lane 0: fills free slots with the next units of the stream.  Attention
+// units of a later step are held back until that step runs: they read the
+// cache row that the running step writes in the same layer.
+__device__ __forceinline__ void RingPump(Ring& r, const LoopParams& p, const GeoTable& gt, int64_t pos0, int warp) {
+  while (r.ki - r.kc < static_cast<uint32_t>(r.R) && r.cur.step < p.n_steps &&
+         !(r.cur.kind == kAttn && r.cur.step > r.step)) {
+    IssueUnit(p, gt, r.cur, pos0, warp, r.base + static_cast<size_t>(r.is) * kSlot, r.bars + r.is);
+    ++r.ki;
+    if (++r.is == r.R) r.is = 0;
+  }
+}
+
+// Waits for the next unit; returns its slot.  A wait that gives up sets err
+// and turns the later waits of this warp into no-ops, so a failing launch
+// reaches its next grid barrier (where every block stops) quickly.
+__device__ __forceinline__ const uint8_t* RingWait(Ring& r, const LoopParams& p) {
+  const int slot = r.cs;
+  if (!r.bad) {
+    const bool ok = dev::MbarWait(r.bars + slot, r.cpar);
+    if (!__all_sync(0xFFFFFFFFu, ok)) {
+      r.bad = true;
+      if ((threadIdx.x & 31) == 0) atomicOr(p.err, 1u);
+    }
+  }
+  return r.base + static_cast<size_t>(slot) * kSlot;
+}
+
+// Marks the current unit consumed and refills free slots from the stream.
+__device__ __forceinline__ void RingRelease(Ring& r, const LoopParams& p, const GeoTable& gt, int64_t pos0,
+                                            int warp) {
+  __syncwarp();
+  ++r.kc;
+  if (++r.cs == r.R) {
+    r.cs = 0;
+    r.cpar ^= 1u;
+  }
+  if ((threadIdx.x & 31) == 0) {
+    dev::FenceProxyAsync();
+    RingPump(r, p, gt, pos0, warp);
+  }
+}
+
+// ------------------------------------------------------------------ grid barrier
+
+__device__ __forceinline__ unsigned AtomAddRelease(unsigned* a, unsigned v) {
+  unsigned old;
+  asm volatile("atom.add.release.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(a), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ unsigned LdAcquire(const unsigned* a) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned LdRelaxed(const unsigned* a) {
+  unsigned v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ void FenceAcquire() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+__device__ __forceinline__ void FenceProxyAsyncGlobal() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+// ------------------------------------------------------------------ tagged words
+//
+// Between the phases of a layer, data moves as 64-bit words {float bits,
+// tag}: a producer stores each value together with the tag of the phase that
+// made it (one single-copy-atomic 8-byte store), a consumer spins on exactly
+// the words it needs until every tag matches.  The value itself carries the
+// "ready" signal, so no barrier and no second round trip is needed (the
+// low-latency protocol of NCCL's LL transport, applied inside one GPU).
+// Every consumer of a buffer has read it completely before its own output
+// exists, and the next writer of the buffer needs that output: one buffer
+// per kind of data suffices.
+
+__device__ __forceinline__ uint64_t Pack(float v, uint32_t tag) {
+  return (static_cast<uint64_t>(tag) << 32) | __float_as_uint(v);
+}
+__device__ __forceinline__ void StLL(uint64_t* a, float v, uint32_t tag) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(a), "l"(Pack(v, tag)) : "memory");
+}
+__device__ __forceinline__ void LdLL2(const uint64_t* a, uint64_t& w0, uint64_t& w1) {
+  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(w0), "=l"(w1) : "l"(a) : "memory");
+}
+__device__ __forceinline__ uint64_t LdLL(const uint64_t* a) {
+  uint64_t w;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(a) : "memory");
+  return w;
+}
+__device__ __forceinline__ bool TagOk(uint64_t w, uint32_t tag) { return static_cast<uint32_t>(w >> 32) == tag; }
+__device__ __forceinline__ float ValOf(uint64_t w) { return __uint_as_float(static_cast<uint32_t>(w)); }
+
+constexpr uint32_t kLLLimit = 1u << 21;  // polls of one tagged word group before giving up
+
+// A wait gives up after kLLLimit polls, or early once another block has
+// reported an error (checked every 512 polls).
+__device__ __forceinline__ bool LLGiveUp(const LoopParams& p, uint32_t it) {
+  if (it == kLLLimit) {
+    atomicOr(p.err, 8u);
+    return true;
+  }
+  return (it & 511u) == 511u && *reinterpret_cast<volatile unsigned*>(p.err) != 0u;
+}
+
+// Eight consecutive tagged words (16-byte aligned) -> v[8], waiting for `tag`.
+__device__ __forceinline__ void WaitLL8(const LoopParams& p, const uint64_t* a, uint32_t tag, float (&v)[8]) {
+  uint64_t w[8];
+  for (uint32_t it = 0;; ++it) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) LdLL2(a + 2 * i, w[2 * i], w[2 * i + 1]);
+    bool ok = true;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ok = ok && TagOk(w[i], tag);
+    if (ok || LLGiveUp(p, it)) break;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = ValOf(w[i]);
+}
+
+// One tagged word, waiting for `tag`.
+__device__ __forceinline__ float WaitLL1(const LoopParams& p, const uint64_t* a, uint32_t tag) {
+  uint64_t w;
+  for (uint32_t it = 0;; ++it) {
+    w = LdLL(a);
+    if (TagOk(w, tag) || LLGiveUp(p, it)) break;
+  }
+  return ValOf(w);
+}
+
+// Four consecutive tagged words (16-byte aligned), waiting for `tag`.
+__device__ __forceinline__ float4 WaitLL4(const LoopParams& p, const uint64_t* a, uint32_t tag) {
+  uint64_t w0, w1, w2, w3;
+  for (uint32_t it = 0;; ++it) {
+    LdLL2(a, w0, w1);
+    LdLL2(a + 2, w2, w3);
+    if ((TagOk(w0, tag) && TagOk(w1, tag) && TagOk(w2, tag) && TagOk(w3, tag)) || LLGiveUp(p, it)) break;
+  }
+  return make_float4(ValOf(w0), ValOf(w1), ValOf(w2), ValOf(w3));
+}
+
+// Tag of the output of (step, layer, kind); the lm_head phase is kind 5 of layer n_layers - 1.
+__device__ __forceinline__ uint32_t TagOf(const LoopParams& p, int step, int layer, int kind) {
+  return p.epoch0 + static_cast<uint32_t>(step) * static_cast<uint32_t>(5 * p.n_layers + 2) +
+         static_cast<uint32_t>(5 * layer + kind) + 1u;
+}
+
+// All blocks arrive; bit 31 of the word flips when the last one does (block 0
+// adds 2^31 - (n - 1), the others 1, so the low bits return to their start).
+// Returns false in every thread of the block if the wait gave up or another
+// block reported an error.
+__device__ __forceinline__ bool GridBarrier(const LoopParams& p, int* s_flag) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned inc = blockIdx.x == 0 ? 0x80000000u - (gridDim.x - 1u) : 1u;
+    const unsigned old = AtomAddRelease(p.bar, inc);
+    int ok = 0;
+    for (uint32_t i = 0; i < kBarLimit; ++i) {
+      if ((LdRelaxed(p.bar) ^ old) & 0x80000000u) {
+        FenceAcquire();
+        ok = 1;
+        break;
+      }
+      if ((i & 255u) == 255u && *reinterpret_cast<volatile unsigned*>(p.err) != 0u) break;
+    }
+    if (!ok) atomicOr(p.err, 4u);
+    if (ok && *reinterpret_cast<volatile unsigned*>(p.err) != 0u) ok = 0;
+    *s_flag = ok;
+  }
+  __syncthreads();
+  // cached K/V rows written by other blocks are read by TMA (async proxy) later
+  if ((threadIdx.x & 31) == 0) FenceProxyAsyncGlobal();
+  return *reinterpret_cast<volatile int*>(s_flag) != 0;
+}
+
+// ------------------------------------------------------------------ trace
+
+// Thread 0 of each block records, per phase: t_start = end of its previous
+// phase (barrier arrival), t_ready = barrier release, t_end = end of the
+// phase; up to two marks inside a phase become extra records whose block
+// field carries k << 24 and whose t_end is the time of mark k.
+constexpr int kMarks = 4;
+struct PhaseClock {
+  uint64_t t_prev, t_ready;
+  uint64_t mk[kMarks];
+};
+__device__ __forceinline__ void TraceReady(const LoopParams& p, PhaseClock& c) {
+  if (p.trace.rec != nullptr && threadIdx.x == 0) c.t_ready = dev::GlobalTimer();
+}
+__device__ __forceinline__ void TraceMark(const LoopParams& p, PhaseClock& c, int k) {
+  if (p.trace.rec != nullptr && threadIdx.x == 0) c.mk[k - 1] = dev::GlobalTimer();
+}
+// As TraceMark, from lane 0 of warp 0 without requiring thread 0's control flow.
+__device__ __forceinline__ void TraceMarkW0(const LoopParams& p, PhaseClock& c, int k) {
+  if (p.trace.rec != nullptr && threadIdx.x == 0) c.mk[k - 1] = dev::GlobalTimer();
+}
+__device__ __forceinline__ void TraceEnd(const LoopParams& p, PhaseClock& c, uint32_t id) {
+  if (p.trace.rec != nullptr && threadIdx.x == 0) {
+    const uint64_t t = dev::GlobalTimer();
+    const uint32_t i = atomicAdd(p.trace.count, 1u + kMarks);
+    for (uint32_t k = 0; k <= kMarks; ++k) {
+      if (i + k >= p.trace.cap) break;
+      const uint64_t te = k == 0 ? t : c.mk[k - 1];
+      if (k > 0 && te == 0) {
+        p.trace.rec[i + k] = TraceRec{0xFFFFFFFFu, 0u, 0ull, 0ull, 0ull};
+        continue;
+      }
+      TraceRec r;
+      r.id = id;
+      r.block = blockIdx.x | (k << 24);
+      r.t_start = c.t_prev;
+      r.t_ready = c.t_ready ? c.t_ready : c.t_prev;
+      r.t_end = te;
+      p.trace.rec[i + k] = r;
+    }
+    c.t_prev = t;
+    c.t_ready = 0;
+    for (int k = 0; k < kMarks; ++k) c.mk[k] = 0;
+  }
+}
+
+// ------------------------------------------------------------------ matvec phases
+
+// Shared-memory pointers of the dynamic plan, recomputed where used (the
+// kernel keeps no plan in registers).
+struct Smem {
+  uint8_t* base;
+  const LoopParams* p;
+  __device__ __forceinline__ Plan plan() const {
+    return MakePlan(p->ring, p->nb_max, p->x_max, p->scratch_bytes, p->max_tiles);
+  }
+  __device__ __forceinline__ uint8_t* scratch() const { return base + plan().scratch; }
+  __device__ __forceinline__ float* red() const { return reinterpret_cast<float*>(base + plan().red); }
+};
+
+__device__ __forceinline__ void Ld8(const float* src, bool shared, float (&v)[8]) {
+  float4 a, b;
+  if (shared) {
+    a = *reinterpret_cast<const float4*>(src);
+    b = *reinterpret_cast<const float4*>(src + 4);
+  } else {
+    a = __ldcg(reinterpret_cast<const float4*>(src));
+    b = __ldcg(reinterpret_cast<const float4*>(src + 4));
+  }
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+// Merged attention output of all q heads -> xs[q_dim]: the split records of
+// KV head h are combined as in the split-K merge of the standalone kernel
+// (weights exp(m_s - M), double denominator).  Three passes: (m, l) of every
+// record, per (head, member) the weights and 1/L, then the weighted sums of o
+// (each thread: one float4 of one q head, loads in independent batches).
+template <int G>
+__device__ void MergeAttention(const LoopParams& p, int step, int layer, int64_t pos, float* xs, uint8_t* merge) {
+  const int tid = threadIdx.x;
+  const uint32_t tag = TagOf(p, step, layer, kAttn);
+  const int S = p.splits, se = EffSplits(p, pos);
+  constexpr int kRec = RecWords(G);
+  const int nr = p.n_kv * se * G;
+  float* wv = reinterpret_cast<float*>(merge);                                        // [n_kv][se][G]
+  double* lv = reinterpret_cast<double*>(merge + Al(static_cast<size_t>(nr) * 4, 8));  // [n_kv][se][G]
+  float* inv = reinterpret_cast<float*>(lv + nr);                                     // [n_kv][G]
+  for (int i = tid; i < nr; i += kNT) {
+    const int h = i / (se * G), r = i - h * se * G, sp = r / G, g = r - sp * G;
+    const uint64_t* rec = p.llrec + (static_cast<size_t>(h) * S + sp) * kRec;
+    wv[i] = WaitLL1(p, rec + 128 * G + g, tag);
+    lv[i] = static_cast<double>(WaitLL1(p, rec + 129 * G + g, tag)) + WaitLL1(p, rec + 130 * G + g, tag);
+  }
+  __syncthreads();
+  for (int i = tid; i < p.n_kv * G; i += kNT) {
+    const int h = i / G, g = i - h * G;
+    float M = -INFINITY;
+    for (int sp = 0; sp < se; ++sp) M = fmaxf(M, wv[(h * se + sp) * G + g]);
+    double L = 0.0;
+    for (int sp = 0; sp < se; ++sp) {
+      const int k = (h * se + sp) * G + g;
+      const float w = wv[k] == -INFINITY ? 0.f : expf(wv[k] - M);
+      wv[k] = w;
+      L += static_cast<double>(w) * lv[k];
+    }
+    inv[i] = static_cast<float>(1.0 / L);
+  }
+  __syncthreads();
+  for (int e = tid; e < p.n_heads * 32; e += kNT) {
+    const int qh = e >> 5, d4 = e & 31, h = qh / G, g = qh - h * G;
+    const uint64_t* base = p.llrec + static_cast<size_t>(h) * S * kRec + g * kD + 4 * d4;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    constexpr int kB = 2;
+    for (int s0 = 0; s0 < se; s0 += kB) {
+      uint64_t w[kB][4];
+#pragma unroll
+      for (int i = 0; i < kB; ++i) {
+        if (s0 + i < se) {
+          const uint64_t* a = base + static_cast<size_t>(s0 + i) * kRec;
+          LdLL2(a, w[i][0], w[i][1]);
+          LdLL2(a + 2, w[i][2], w[i][3]);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kB; ++i) {
+        if (s0 + i < se) {
+          float4 v;
+          if (TagOk(w[i][0], tag) && TagOk(w[i][1], tag) && TagOk(w[i][2], tag) && TagOk(w[i][3], tag)) {
+            v = make_float4(ValOf(w[i][0]), ValOf(w[i][1]), ValOf(w[i][2]), ValOf(w[i][3]));
+          } else {
+            v = WaitLL4(p, base + static_cast<size_t>(s0 + i) * kRec, tag);
+          }
+          const float wt = wv[(h * se + s0 + i) * G + g];
+          o.x = fmaf(wt, v.x, o.x);
+          o.y = fmaf(wt, v.y, o.y);
+          o.z = fmaf(wt, v.z, o.z);
+          o.w = fmaf(wt, v.w, o.w);
+        }
+      }
+    }
+    const float iv = inv[h * G + g];
+    *reinterpret_cast<float4*>(xs + qh * kD + 4 * d4) = make_float4(o.x * iv, o.y * iv, o.z * iv, o.w * iv);
+  }
+}
+
+struct LmOut {
+  float* vals;  // this block's logits (fast path), kSliceRows
+};
+
+// One matvec phase.  Returns nothing; the epilogue writes its outputs.
+template <int G>
+__device__ void MvPhase(const LoopParams& p, const GeoTable& gt, int kind, int layer, int step, int64_t pos0,
+                        int64_t pos, int tok, Ring& rg_io, const Smem& sm, PhaseClock& clk, float* xown, double* s_sq,
+                        float* s_bv, int* s_bi, int* s_cnt, uint32_t* s_sel) {
+  Ring rg = rg_io;  // in registers for the unit loop
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const MvShape sh = ShapeOf(p, kind);
+  const Geo g = gt.g[kind][warp];
+  const int K = sh.K, nb = g.nb;
+  const Plan pl = sm.plan();
+  uint8_t* const scratch = sm.base + pl.scratch;
+  uint8_t* bfrag = scratch + pl.bfrag;
+  float* sx = reinterpret_cast<float*>(scratch + pl.sx);
+  float* sscale = reinterpret_cast<float*>(scratch + pl.sscale);
+  float* xs = reinterpret_cast<float*>(scratch + pl.xs);
+  float* red = reinterpret_cast<float*>(sm.base + pl.red);
+  const bool any = g.t1 > g.t0;
+  const float* norm_w = kind == kQkv ? g_layers[layer].norm[0]
+                                     : (kind == kGu ? g_layers[layer].norm[1] : (kind == kLm ? p.out_norm : nullptr));
+
+  // ---- input (tagged words of the previous phase, the merged attention, or
+  // the embedding row at layer 0) -> digits of x times the norm weight
+  if (any) {
+    const uint64_t* ll = nullptr;
+    uint32_t tag = 0;
+    if (kind == kQkv && layer == 0) {
+      for (int c = tid; c < p.hidden; c += kNT) xs[c] = dev::DeqElem(p.embd, tok, c);
+      __syncthreads();
+    } else if (kind == kO) {
+      MergeAttention<G>(p, step, layer, pos, xs, scratch + pl.merge);
+      __syncthreads();
+    } else {
+      ll = kind == kDown ? p.llh : p.llx;
+      tag = kind == kQkv ? TagOf(p, step, layer - 1, kDown)
+                         : (kind == kGu ? TagOf(p, step, layer, kO)
+                                        : (kind == kDown ? TagOf(p, step, layer, kGu)
+                                                         : TagOf(p, step, p.n_layers - 1, kDown)));
+    }
+    double ssq = 0.0;
+    for (int b = warp; b < nb; b += kNW) {
+      float v[8];
+      if (ll != nullptr) {
+        WaitLL8(p, ll + b * 256 + 8 * lane, tag, v);
+      } else {
+        Ld8(xs + b * 256 + 8 * lane, true, v);
+      }
+      if (norm_w != nullptr) {
+        float w[8];
+        Ld8(norm_w + b * 256 + 8 * lane, true, w);  // constant: cached loads
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          ssq += static_cast<double>(v[i]) * v[i];
+          v[i] *= w[i];
+        }
+      }
+      PutDigits(v, b, lane, bfrag, sx, sscale);
+      if (b == 0) TraceMarkW0(p, clk, 1);  // warp 0: first input words arrived and split
+    }
+    if (norm_w != nullptr) {
+      ssq = dev::WarpSumD(ssq);
+      if (lane == 0) s_sq[warp] = ssq;
+    }
+    __syncthreads();
+  }
+  TraceMark(p, clk, 2);  // input and digits ready in every warp
+
+  // ---- units
+  const int n_units = g.u1 - g.u0;
+  if (n_units > 0) {
+    const LaneK lk = MakeLane(lane);
+    uint32_t bA[8], bB[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) bA[i] = bB[i] = 0u;
+    const uint32_t lo_half = lk.g < 4 ? 1u : 0u;
+    float rg8 = 0.f, rgv = 0.f;
+    int tl = g.u0 / nb, b = g.u0 % nb;
+    int st0 = 0;
+    uint32_t type = SegType(p, kind, layer, SegOfTile(p, kind, g.t0 + tl, &st0));
+    for (int i = 0; i < n_units; ++i) {
+      const uint8_t* grp = RingWait(rg, p);
+      if (i == 0) TraceMarkW0(p, clk, 3);  // warp 0: first unit in shared memory
+      LoadB(bfrag, b, lane, lo_half, bA, bB);
+      const float s = sscale[b];
+      if (type == 12u) {
+        UnitQ4K(grp, bA, bB, sx + b * 8, s, lk, lane, rgv, rg8);
+      } else {
+        UnitQ6K(grp, bA, bB, s, lk, lane, rgv, rg8);
+      }
+      RingRelease(rg, p, gt, pos0, warp);
+      if (++b == nb || i + 1 == n_units) {
+        FlushPiece(red, tl + warp, lk, rgv, rg8);
+        if (b == nb) {
+          b = 0;
+          ++tl;
+          if (i + 1 < n_units) type = SegType(p, kind, layer, SegOfTile(p, kind, g.t0 + tl, &st0));
+        }
+      }
+    }
+  }
+  rg_io = rg;
+  __syncthreads();
+  TraceMark(p, clk, 4);  // all units done
+
+  // ---- epilogue
+  float scale = 1.f;
+  if (norm_w != nullptr && any) {
+    double tot = 0.0;
+    for (int w = 0; w < kNW; ++w) tot += s_sq[w];
+    scale = static_cast<float>(1.0 / sqrt(tot / static_cast<double>(K) + static_cast<double>(p.eps)));
+  }
+  const int U = (g.t1 - g.t0) * nb;
+  const int n_rows = (g.t1 - g.t0) * kTile;
+  const uint32_t tag_out = TagOf(p, step, layer, kind);
+  const int rstep = kind == kGu ? 2 : 1;
+  float best_v = -FLT_MAX;
+  int best_i = INT_MAX;
+  float* vals = reinterpret_cast<float*>(scratch);  // lm fast path: this block's logits
+  for (int lr = tid * rstep; lr < n_rows; lr += kNT * rstep) {
+    const int ti = lr / kTile, r = lr - ti * kTile;
+    float v = 0.f, v2 = 0.f;
+#pragma unroll
+    for (int w = 0; w < kNW; ++w) {
+      const int a = w * U / kNW, e = (w + 1) * U / kNW;
+      if (a < e && a < (ti + 1) * nb && e > ti * nb) {
+        v += red[(ti + w) * kTile + r];
+        if (kind == kGu) v2 += red[(ti + w) * kTile + r + 1];
+      }
+    }
+    v *= scale;
+    v2 *= scale;
+    const int row = g.t0 * kTile + lr;
+    if (kind == kQkv) {
+      StLL(p.llqkv + row, v, tag_out);
+    } else if (kind == kO || kind == kDown) {
+      // x += W h: this block owns these rows of x in both phases
+      const float xn = xown[lr] + v;
+      xown[lr] = xn;
+      StLL(p.llx + row, xn, tag_out);
+    } else if (kind == kGu) {
+      // rows 2i (gate) and 2i+1 (up): (g / (1 + exp(-g))) * u, as src/kernels_gpu.cu:863-869
+      StLL(p.llh + (row >> 1), (v / (1.0f + expf(-v))) * v2, tag_out);
+    } else if (row < p.vocab) {
+      p.logits[row] = v;
+      if (p.mode == 0) {
+        if (v > best_v) {  // rows increase per thread: strict > keeps the lowest index
+          best_v = v;
+          best_i = row;
+        }
+      } else if (p.mode == 1) {
+        vals[lr] = v;
+      }
+    }
+  }
+  if (kind == kLm && p.mode == 0) {
+    // block argmax, ties -> lowest index (src/kernels_gpu.cu:827-859)
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xFFFFFFFFu, best_v, o);
+      const int oi = __shfl_xor_sync(0xFFFFFFFFu, best_i, o);
+      if (ov > best_v || (ov == best_v && oi < best_i)) {
+        best_v = ov;
+        best_i = oi;
+      }
+    }
+    if (lane == 0) {
+      s_bv[warp] = best_v;
+      s_bi[warp] = best_i;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      float bv = s_bv[0];
+      int bi = s_bi[0];
+      for (int i = 1; i < kNW; ++i) {
+        if (s_bv[i] > bv || (s_bv[i] == bv && s_bi[i] < bi)) {
+          bv = s_bv[i];
+          bi = s_bi[i];
+        }
+      }
+      p.am_val[blockIdx.x] = bv;
+      p.am_idx[blockIdx.x] = bi;
+    }
+  } else if (kind == kLm && p.mode == 1) {
+    __syncthreads();
+    const int row0 = g.t0 * kTile;
+    int len = n_rows;
+    if (row0 + len > p.vocab) len = p.vocab - row0 > 0 ? p.vocab - row0 : 0;
+    unsigned* hist = reinterpret_cast<unsigned*>(scratch + kSliceRows * 4);
+    smp::SliceCandidates(vals, len, row0, p.top_k, hist, s_sel, s_cnt, p.cand_val + blockIdx.x * kFastTopK,
+                         p.cand_idx + blockIdx.x * kFastTopK, p.cand_cnt + blockIdx.x);
+  }
+}
+
+// ------------------------------------------------------------------ attention phase
+
+template <int G>
+struct __align__(16) AttnShared {
+  float qs[G][kD];            // normalised, rotated q heads, times 1/sqrt(128)
+  __half knew[kD], vnew[kD];  // the current position's row
+  double sq[2 * (G + 1)];     // sums of squares, two warps per vector
+  double dsh[kNW * G];
+  float fsh[kNW * G];
+};
+
+template <int G>
+__device__ void AttnPhase(const LoopParams& p, const GeoTable& gt, int layer, int step, int64_t pos0, int64_t pos,
+                          Ring& rg_io, const Smem& sm, PhaseClock& clk, AttnShared<G>& as) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const AttnGeo a = AttnOf(p, pos);
+  if (a.c1 <= a.c0) return;  // no positions for this block at this step
+  Ring rg = rg_io;           // in registers for the chunk loop
+  const int h = a.h, S = p.splits, s = static_cast<int>(blockIdx.x) - h * S;
+  const LayerRow& Ly = g_layers[layer];
+  const int qd = p.n_heads * kD, kvd = p.n_kv * kD;
+  const int pc = static_cast<int>(pos / kChunk);
+  const bool owner = pc >= a.c0 && pc < a.c1;  // this block's chunks hold the current position
+  const int64_t cache_off =
+      static_cast<int64_t>(layer) * p.layer_elems + (static_cast<int64_t>(h) * p.max_seq + pos) * kD;
+
+  // ---- q heads and the new key: RMSNorm + RoPE.  Thread t < 64 (G + 1) owns
+  // dimensions d and d + 64 of vector vi = t / 64 (q heads 0..G-1, then k),
+  // so the rotation stays in registers; the next 128 threads take v.
+  const uint32_t tag = TagOf(p, step, layer, kQkv);
+  const int vi = tid >> 6, d = tid & 63;
+  float e0 = 0.f, e1 = 0.f;
+  if (vi <= G) {
+    const int64_t off = vi < G ? static_cast<int64_t>(h * G + vi) * kD : qd + h * kD;
+    uint64_t w0 = LdLL(p.llqkv + off + d), w1 = LdLL(p.llqkv + off + d + 64);
+    if (!TagOk(w0, tag)) w0 = Pack(WaitLL1(p, p.llqkv + off + d, tag), tag);
+    if (!TagOk(w1, tag)) w1 = Pack(WaitLL1(p, p.llqkv + off + d + 64, tag), tag);
+    e0 = ValOf(w0);
+    e1 = ValOf(w1);
+    double ss = static_cast<double>(e0) * e0 + static_cast<double>(e1) * e1;
+    ss = dev::WarpSumD(ss);
+    if (lane == 0) as.sq[warp] = ss;
+  } else if (tid < 64 * (G + 1) + kD) {
+    const int dv = tid - 64 * (G + 1);
+    const __half vh = __float2half_rn(WaitLL1(p, p.llqkv + qd + kvd + h * kD + dv, tag));
+    as.vnew[dv] = vh;
+    if (owner) {
+      p.vc[cache_off + dv] = vh;
+      FenceProxyAsyncGlobal();
+    }
+  }
+  TraceMarkW0(p, clk, 1);  // q / k / v words arrived
+  __syncthreads();
+  if (vi <= G) {
+    const double tot = as.sq[2 * vi] + as.sq[2 * vi + 1];
+    const float sc = static_cast<float>(1.0 / sqrt(tot / static_cast<double>(kD) + static_cast<double>(p.eps)));
+    const float* nw = vi < G ? Ly.norm[2] : Ly.norm[3];
+    const float x0 = e0 * sc * nw[d], x1 = e1 * sc * nw[d + 64];
+    const float rc = p.rope[pos * kD + d], rs = p.rope[pos * kD + kD / 2 + d];
+    const float y0 = x0 * rc - x1 * rs, y1 = x1 * rc + x0 * rs;
+    if (vi < G) {
+      as.qs[vi][d] = y0 * p.scale;
+      as.qs[vi][d + 64] = y1 * p.scale;
+    } else {
+      const __half k0 = __float2half_rn(y0), k1 = __float2half_rn(y1);
+      as.knew[d] = k0;
+      as.knew[d + 64] = k1;
+      if (owner) {
+        p.kc[cache_off + d] = k0;
+        p.kc[cache_off + d + 64] = k1;
+        FenceProxyAsyncGlobal();
+      }
+    }
+  }
+  __syncthreads();
+  TraceMark(p, clk, 2);  // q / k normalised and rotated
+
+  // ---- this warp's 4-position units.  Scores: 8 lanes per position (lane
+  // sub holds dimensions 8 sub .. +7 and 64 + 8 sub .. +7, position pp = lane / 8);
+  // online softmax over the warp's positions; V with 4 dimensions per lane.
+  const int sub = lane & 7, pp = lane >> 3;
+  float m[G], l[G], acc[G][4];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[g][e] = 0.f;
+  }
+  for (int ch = a.c0 + warp; ch < a.c1; ch += kNW) {
+    const int64_t r0 = static_cast<int64_t>(ch) * kChunk;
+    const int n_valid = static_cast<int>(pos + 1 - r0 < kChunk ? pos + 1 - r0 : kChunk);
+    const int n_old = static_cast<int>(pos - r0 < kChunk ? pos - r0 : kChunk);
+    const uint8_t* slot = RingWait(rg, p);
+    if (ch == a.c0) TraceMarkW0(p, clk, 3);  // warp 0: first unit in shared memory
+    float dd[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) dd[g] = 0.f;
+    if (pp < n_valid) {
+      const __half* krow = pp < n_old ? reinterpret_cast<const __half*>(slot + pp * kD * 2) : as.knew;
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(krow + 64 * hf + 8 * sub);
+        const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+        const float2 f0 = __half22float2(h2[0]), f1 = __half22float2(h2[1]);
+        const float2 f2 = __half22float2(h2[2]), f3 = __half22float2(h2[3]);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float4 qa = *reinterpret_cast<const float4*>(&as.qs[g][64 * hf + 8 * sub]);
+          const float4 qb = *reinterpret_cast<const float4*>(&as.qs[g][64 * hf + 8 * sub + 4]);
+          dd[g] = fmaf(qa.x, f0.x, dd[g]);
+          dd[g] = fmaf(qa.y, f0.y, dd[g]);
+          dd[g] = fmaf(qa.z, f1.x, dd[g]);
+          dd[g] = fmaf(qa.w, f1.y, dd[g]);
+          dd[g] = fmaf(qb.x, f2.x, dd[g]);
+          dd[g] = fmaf(qb.y, f2.y, dd[g]);
+          dd[g] = fmaf(qb.z, f3.x, dd[g]);
+          dd[g] = fmaf(qb.w, f3.y, dd[g]);
+        }
+      }
+    }
+    float ev[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float sc = dd[g];
+      sc += __shfl_xor_sync(0xFFFFFFFFu, sc, 1);
+      sc += __shfl_xor_sync(0xFFFFFFFFu, sc, 2);
+      sc += __shfl_xor_sync(0xFFFFFFFFu, sc, 4);
+      if (pp >= n_valid) sc = -INFINITY;
+      float mx = fmaxf(sc, __shfl_xor_sync(0xFFFFFFFFu, sc, 8));
+      mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 16));
+      const float nm = fmaxf(m[g], mx);
+      const float alpha = m[g] == -INFINITY ? 0.f : expf(m[g] - nm);
+      const float e = pp < n_valid ? expf(sc - nm) : 0.f;
+      float ps = e + __shfl_xor_sync(0xFFFFFFFFu, e, 8);
+      ps += __shfl_xor_sync(0xFFFFFFFFu, ps, 16);
+      m[g] = nm;
+      l[g] = l[g] * alpha + ps;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[g][q] *= alpha;
+      ev[g] = e;
+    }
+#pragma unroll
+    for (int jj = 0; jj < kChunk; ++jj) {
+      if (jj < n_valid) {
+        const __half* vrow =
+            jj < n_old ? reinterpret_cast<const __half*>(slot + (kChunk + jj) * kD * 2) : as.vnew;
+        const uint2 raw = *reinterpret_cast<const uint2*>(vrow + 4 * lane);
+        const float2 x0 = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+        const float2 x1 = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float e = __shfl_sync(0xFFFFFFFFu, ev[g], 8 * jj);
+          acc[g][0] = fmaf(e, x0.x, acc[g][0]);
+          acc[g][1] = fmaf(e, x0.y, acc[g][1]);
+          acc[g][2] = fmaf(e, x1.x, acc[g][2]);
+          acc[g][3] = fmaf(e, x1.y, acc[g][3]);
+        }
+      }
+    }
+    RingRelease(rg, p, gt, pos0, warp);
+  }
+  rg_io = rg;
+
+  // ---- fold the warps into this block's record
+  float* vred = reinterpret_cast<float*>(sm.scratch());  // [kNW][G][128]
+  __syncthreads();
+  TraceMark(p, clk, 4);  // units done
+  if (lane == 0) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      as.fsh[warp * G + g] = m[g];
+      as.dsh[warp * G + g] = static_cast<double>(l[g]);
+    }
+  }
+  __syncthreads();
+  constexpr int kRec = RecWords(G);
+  uint64_t* rec = p.llrec + (static_cast<size_t>(h) * S + s) * kRec;
+  const uint32_t tag_out = TagOf(p, step, layer, kAttn);
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float M = as.fsh[g];
+#pragma unroll
+    for (int w = 1; w < kNW; ++w) M = fmaxf(M, as.fsh[w * G + g]);
+    const float sw = m[g] == -INFINITY ? 0.f : expf(m[g] - M);
+    *reinterpret_cast<float4*>(vred + (warp * G + g) * kD + 4 * lane) =
+        make_float4(acc[g][0] * sw, acc[g][1] * sw, acc[g][2] * sw, acc[g][3] * sw);
+    if (warp == 0) {  // lanes 0..15 weigh the warps' denominators
+      double t = 0.0;
+      if (lane < kNW) {
+        const float mw = as.fsh[lane * G + g];
+        t = mw == -INFINITY ? 0.0 : static_cast<double>(expf(mw - M)) * as.dsh[lane * G + g];
+      }
+      t = dev::WarpSumD(t);
+      if (lane == 0) {
+        const float lhi = static_cast<float>(t);
+        StLL(rec + 128 * G + g, M, tag_out);
+        StLL(rec + 129 * G + g, lhi, tag_out);
+        StLL(rec + 130 * G + g, static_cast<float>(t - static_cast<double>(lhi)), tag_out);
+      }
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < G * kD; i += kNT) {
+    const int g = i / kD, dd2 = i - g * kD;
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < kNW; ++w) t += vred[(w * G + g) * kD + dd2];
+    StLL(rec + g * kD + dd2, t, tag_out);
+  }
+}
+
+// ------------------------------------------------------------------ the kernel
+
+template <int G>
+__global__ void __launch_bounds__(kNT, 1) DecodeLoopKernel(const LoopParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ AttnShared<G> as;
+  __shared__ double s_sq[kNW];
+  __shared__ float s_bv[kNW];
+  __shared__ int s_bi[kNW];
+  __shared__ int s_cnt, s_flag, s_tok;
+  __shared__ uint32_t s_sel[3];
+  const GeoTable& gt = g_geo;
+  __shared__ float s_xown[kMaxOwnRows];
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  Smem sm;
+  sm.base = smem;
+  sm.p = &p;
+  FillTables(p);
+  __syncthreads();
+
+  const int64_t pos0 = *p.pos;
+  int tok = *p.tok;
+
+  Ring rg;
+  rg.R = p.ring;
+  rg.base = smem + static_cast<size_t>(warp) * p.ring * kSlot;
+  rg.bars = reinterpret_cast<uint64_t*>(smem + sm.plan().bars) + warp * p.ring;
+  rg.kc = rg.ki = 0;
+  rg.cs = rg.is = 0;
+  rg.cpar = 0u;
+  rg.bad = false;
+  rg.cur.step = 0;
+  rg.cur.layer = 0;
+  rg.cur.kind = kQkv;
+  rg.cur.j = 0;
+  rg.cur.n = gt.g[kQkv][warp].u1 - gt.g[kQkv][warp].u0;
+  rg.cur.run = 0;
+  rg.cur.bytes = 0;
+  rg.cur.src = nullptr;
+  rg.cur.c0 = 0;
+  rg.step = 0;
+  if (lane == 0) {
+    for (int i = 0; i < rg.R; ++i) dev::MbarInit(rg.bars + i, 1);
+    dev::MbarInitFence();
+    NextPhase(p, gt, rg.cur, pos0, warp);
+    RingPump(rg, p, gt, pos0, warp);
+  }
+  __syncwarp();
+
+  __shared__ PhaseClock clk;  // thread 0's timeline (trace only)
+  if (p.trace.rec != nullptr && tid == 0) {
+    clk.t_prev = dev::GlobalTimer();
+    clk.t_ready = 0;
+    for (int k = 0; k < kMarks; ++k) clk.mk[k] = 0;
+  }
+  const uint32_t n_phase = 5u * static_cast<uint32_t>(p.n_layers) + 2u;
+  int steps = 0;
+  bool alive = true;
+  for (int step = 0; step < p.n_steps && alive; ++step) {
+    const int64_t pos = pos0 + step;
+    const uint32_t id0 = static_cast<uint32_t>(step) * n_phase;
+    if (blockIdx.x == 0 && tid == 0) p.out_ids[pos] = tok;
+    // this step's attention units may be requested now (the previous step
+    // wrote its cache rows before the barriers that led here)
+    rg.step = step;
+    if (lane == 0) RingPump(rg, p, gt, pos0, warp);
+    // the rows of x this block owns in the o / down phases start as the
+    // embedding of the forwarded token
+    {
+      const Geo& go = gt.g[kO][0];
+      for (int r = tid; r < (go.t1 - go.t0) * kTile; r += kNT) s_xown[r] = dev::DeqElem(p.embd, tok, go.t0 * kTile + r);
+    }
+    // Phases of a layer meet through tagged words, not barriers; a block only
+    // synchronises its own threads between phases (shared memory is reused).
+    for (int l = 0; l < p.n_layers; ++l) {
+      MvPhase<G>(p, gt, kQkv, l, step, pos0, pos, tok, rg, sm, clk, s_xown, s_sq, s_bv, s_bi, &s_cnt, s_sel);
+      TraceEnd(p, clk, id0 + 5u * l + 0u);
+      __syncthreads();
+      AttnPhase<G>(p, gt, l, step, pos0, pos, rg, sm, clk, as);
+      TraceEnd(p, clk, id0 + 5u * l + 1u);
+      __syncthreads();
+      MvPhase<G>(p, gt, kO, l, step, pos0, pos, tok, rg, sm, clk, s_xown, s_sq, s_bv, s_bi, &s_cnt, s_sel);
+      TraceEnd(p, clk, id0 + 5u * l + 2u);
+      __syncthreads();
+      MvPhase<G>(p, gt, kGu, l, step, pos0, pos, tok, rg, sm, clk, s_xown, s_sq, s_bv, s_bi, &s_cnt, s_sel);
+      TraceEnd(p, clk, id0 + 5u * l + 3u);
+      __syncthreads();
+      MvPhase<G>(p, gt, kDown, l, step, pos0, pos, tok, rg, sm, clk, s_xown, s_sq, s_bv, s_bi, &s_cnt, s_sel);
+      TraceEnd(p, clk, id0 + 5u * l + 4u);
+      __syncthreads();
+    }
+    MvPhase<G>(p, gt, kLm, p.n_layers - 1, step, pos0, pos, tok, rg, sm, clk, s_xown, s_sq, s_bv, s_bi, &s_cnt,
+               s_sel);
+    TraceEnd(p, clk, id0 + n_phase - 2u);
+    if (!(alive = GridBarrier(p, &s_flag))) break;
+    TraceReady(p, clk);
+
+    // ---- sample the next token (counter = pos + 1); every block gets it
+    int next = -1;
+    if (p.mode == 0) {
+      float bv = -FLT_MAX;
+      int bi = INT_MAX;
+      for (int i = tid; i < static_cast<int>(gridDim.x); i += kNT) {
+        const float v = __ldcg(p.am_val + i);
+        const int ix = __ldcg(p.am_idx + i);
+        if (v > bv || (v == bv && ix < bi)) {
+          bv = v;
+          bi = ix;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
+        const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) {
+          bv = ov;
+          bi = oi;
+        }
+      }
+      if (lane == 0) {
+        s_bv[warp] = bv;
+        s_bi[warp] = bi;
+      }
+      __syncthreads();
+      if (tid == 0) {
+        for (int i = 1; i < kNW; ++i) {
+          if (s_bv[i] > s_bv[0] || (s_bv[i] == s_bv[0] && s_bi[i] < s_bi[0])) {
+            s_bv[0] = s_bv[i];
+            s_bi[0] = s_bi[i];
+          }
+        }
+        s_tok = s_bi[0] == INT_MAX ? 0 : s_bi[0];
+      }
+      __syncthreads();
+      next = s_tok;
+    } else {
+      if (p.mode == 1) {
+        next = smp::SmallSample<kNT>(p.cand_val, p.cand_idx, p.cand_cnt, static_cast<int>(gridDim.x), p.temperature,
+                                     p.top_k, p.top_p, p.seed, pos + 1, sm.scratch(), kSmallCap);
+      }
+      if (next < 0) {  // the same decision in every block
+        if (blockIdx.x == 0) {
+          const int t = smp::GeneralSample<kNT>(p.logits, p.vocab, p.temperature, p.top_k, p.top_p, p.seed, pos + 1,
+                                                p.probs);
+          if (tid == 0) p.tok[0] = t;
+        }
+        if (!(alive = GridBarrier(p, &s_flag))) break;
+        if (tid == 0) s_tok = __ldcg(p.tok);
+        __syncthreads();
+        next = s_tok;
+      }
+    }
+    TraceEnd(p, clk, id0 + n_phase - 1u);
+    steps = step + 1;
+    bool is_stop = false;
+    for (int i = 0; i < p.n_stop; ++i) is_stop = is_stop || p.stop[i] == tok;
+    tok = next;
+    if (is_stop) break;
+  }
+
+  // ---- drain: copies still in flight into this warp's ring land before exit
+  if (lane == 0) {
+    for (uint32_t k = rg.kc; k < rg.ki; ++k) {
+      const uint32_t slot = k % static_cast<uint32_t>(rg.R);
+      if (!dev::MbarWait(rg.bars + slot, (k / static_cast<uint32_t>(rg.R)) & 1u)) atomicOr(p.err, 1u);
+    }
+  }
+  if (blockIdx.x == 0 && tid == 0) {
+    *p.pos = pos0 + steps;
+    *p.tok = tok;
+    *p.steps_done = steps;
+  }
+}
+
+using LoopFn = void (*)(const LoopParams);
+
+LoopFn PickLoop(int group) {
+  switch (group) {
+    case 2: return DecodeLoopKernel<2>;
+    case 4: return DecodeLoopKernel<4>;
+  }
+  Throw("decode loop: group size %d is not built (2 and 4 are)", group);
+}
+
+constexpr int kSmemMax = 227 * 1024;
+
+}  // namespace
+
+bool LoopSupportsGroup(int group) { return group == 2 || group == 4; }
+
+size_t LoopPartialWords(int n_kv, int group, int splits) {
+  return static_cast<size_t>(n_kv) * splits * RecWords(group);
+}
+
+uint32_t LoopTagsPerLaunch(int n_layers, int n_steps) {
+  return static_cast<uint32_t>(n_steps) * static_cast<uint32_t>(5 * n_layers + 2) + 2u;
+}
+
+int LoopSplits(int n_kv, int num_sms, int64_t max_seq) {
+  const int64_t by_blocks = num_sms / std::max(1, n_kv);
+  const int64_t by_len = (max_seq + 4 * kChunk - 1) / (4 * kChunk);
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({by_blocks, by_len, 64})));
+}
+
+void PrepareLoopKernels(int num_sms) {
+  (void)num_sms;
+  for (int g : {2, 4}) {
+    // static + dynamic shared memory of a block may not exceed the opt-in limit
+    cudaFuncAttributes fa;
+    RPGB_CUDA(cudaFuncGetAttributes(&fa, reinterpret_cast<const void*>(PickLoop(g))));
+    RPGB_CUDA(cudaFuncSetAttribute(PickLoop(g), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   kSmemMax - static_cast<int>(fa.sharedSizeBytes)));
+  }
+}
+
+void LaunchDecodeLoop(const LoopParams& in, int group, int num_sms, cudaStream_t s) {
+  LoopParams p = in;
+  const LoopFn fn = PickLoop(group);
+  RPGB_CHECK(p.n_steps > 0, "decode loop: no steps");
+  RPGB_CHECK(p.n_stop >= 0 && p.n_stop <= kLoopMaxStop, "decode loop: at most %d stop ids", kLoopMaxStop);
+  const int qd = p.n_heads * kD;
+  RPGB_CHECK((p.hidden / kTile + num_sms - 1) / num_sms * kTile <= kMaxOwnRows,
+             "decode loop: a block would own more than %d rows of x", kMaxOwnRows);
+  RPGB_CHECK(p.llx != nullptr && p.llqkv != nullptr && p.llh != nullptr && p.llrec != nullptr,
+             "decode loop: tagged buffers missing");
+  RPGB_CHECK(p.n_layers >= 1 && p.n_layers <= kMaxLayers, "decode loop: %d layers (at most %d)", p.n_layers,
+             kMaxLayers);
+  p.nb_max = std::max({p.hidden, qd, p.ffn}) / 256;
+  p.x_max = std::max(p.hidden, qd);
+  // most tiles of one block over the phases' row counts
+  const int kvd = p.n_kv * kD;
+  p.max_tiles = 0;
+  for (const int rows : {qd + 2 * kvd, p.hidden, 2 * p.ffn, p.lm_head.rows}) {
+    RPGB_CHECK(rows % kTile == 0, "decode loop: %d rows are not a multiple of %d", rows, kTile);
+    p.max_tiles = std::max(p.max_tiles, (rows / kTile + num_sms - 1) / num_sms);
+  }
+  p.scratch_bytes = static_cast<int32_t>(ScratchBytes(p.nb_max, p.x_max, group, p.n_kv, p.splits));
+  cudaFuncAttributes fa;
+  RPGB_CUDA(cudaFuncGetAttributes(&fa, reinterpret_cast<const void*>(fn)));
+  const size_t fixed = MakePlan(0, p.nb_max, p.x_max, p.scratch_bytes, p.max_tiles).total;
+  const size_t avail = static_cast<size_t>(kSmemMax) - fa.sharedSizeBytes;
+  RPGB_CHECK(avail > fixed, "decode loop: shared memory plan does not fit");
+  const int ring = static_cast<int>((avail - fixed) / (static_cast<size_t>(kNW) * (kSlot + 8)));
+  RPGB_CHECK(ring >= 2, "decode loop: room for only %d ring slots per warp", ring);
+  p.ring = std::min(ring, kMaxRing);
+  const size_t total = MakePlan(p.ring, p.nb_max, p.x_max, p.scratch_bytes, p.max_tiles).total;
+  if (p.mode == 1) {
+    // the candidate slices are the blocks' lm_head rows
+    RPGB_CHECK(num_sms <= kCandBlocks && p.max_tiles * kTile <= kSliceRows, "decode loop: fast sampler geometry");
+  }
+  int per_sm = 0;
+  RPGB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kNT, total));
+  RPGB_CHECK(per_sm >= 1, "decode loop: a block does not fit on an SM (%zu bytes of shared memory)", total);
+  RPGB_CUDA(cudaMemsetAsync(p.bar, 0, sizeof(unsigned), s));
+  void* args[] = {&p};
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(num_sms);
+  cfg.blockDim = dim3(kNT);
+  cfg.dynamicSmemBytes = total;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  RPGB_CUDA(cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(fn), args));
+  CountLaunches(1);
+}
+
+}  // namespace rpgb

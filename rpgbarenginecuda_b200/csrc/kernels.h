@@ -120,6 +120,7 @@ struct AttnParams {
 // bounds the block count (about one block per SM); at most kMaxAttnSplits.
 constexpr int kAttnSplitPositions = 128;
 constexpr int kMaxAttnSplits = 64;
+constexpr int kMaxAttnCluster = 8;  // decode: the splits of one KV head form one thread-block cluster
 void LaunchAttention(const AttnParams& p, int n_queries, cudaStream_t s, bool pdl = false);
 void PrepareAttentionKernels();
 size_t AttentionPartialFloats(int n_kv, int group, int n_splits);
@@ -170,5 +171,69 @@ struct SampleParams {
 constexpr int kFastTopK = 64;
 constexpr int kCandBlocks = 148;
 void LaunchSample(const SampleParams& p, bool want_probs, cudaStream_t s, bool pdl = false);
+
+// ------------------------------------------------------------------ decode loop
+//
+// n_steps decode steps in one cooperative launch of one block per SM (see
+// k_step.cu).  Step i forwards token *tok at position pos = *pos (+ i): the
+// token is recorded at out_ids[pos], the step's logits land in `logits`, the
+// next token is sampled with counter pos + 1.  The loop ends after n_steps
+// steps or after a step that forwarded one of the n_stop stop ids; then *pos,
+// *tok (the last sampled token) and *steps_done are written.
+struct LoopParams {
+  const DevLayer* layers = nullptr;  // device array [n_layers]
+  int32_t n_layers = 0;
+  DevMat embd, lm_head;
+  const float* out_norm = nullptr;
+  const float* rope = nullptr;
+  int32_t hidden = 0, n_heads = 0, n_kv = 0, ffn = 0, vocab = 0, max_seq = 0;
+  float eps = 1e-6f, scale = 0.f;
+  __half* kc = nullptr;  // [layer][kv_head][max_seq][128]
+  __half* vc = nullptr;
+  int64_t layer_elems = 0;
+  int64_t v_minus_k = 0;  // (char*)vc - (char*)kc
+  // Tagged 64-bit words {float bits, tag} passed between the phases of a layer
+  // (see k_step.cu): x [hidden], q|k|v [q_dim + 2 kv_dim], SiLU(g)*u [ffn],
+  // attention split records [n_kv][splits][LoopRecordWords(group)].
+  uint64_t *llx = nullptr, *llqkv = nullptr, *llh = nullptr, *llrec = nullptr;
+  uint32_t epoch0 = 1;  // tags of this launch start above it; strictly increasing across launches
+  float *logits = nullptr, *probs = nullptr;
+  int64_t* pos = nullptr;
+  int32_t* tok = nullptr;
+  int32_t* out_ids = nullptr;
+  // sampling: mode 0 argmax, 1 candidate fast path, 2 general block
+  int32_t mode = 0;
+  float temperature = 0.f, top_p = 1.f;
+  int32_t top_k = 0;
+  uint64_t seed = 0;
+  float* cand_val = nullptr;
+  int32_t* cand_idx = nullptr;
+  int32_t* cand_cnt = nullptr;
+  float* am_val = nullptr;
+  int32_t* am_idx = nullptr;
+  // control
+  int32_t n_steps = 1;
+  const int32_t* stop = nullptr;  // device [n_stop]
+  int32_t n_stop = 0;
+  int32_t* steps_done = nullptr;
+  unsigned* bar = nullptr;  // grid barrier word
+  unsigned* err = nullptr;  // nonzero after a bounded wait gave up
+  int32_t splits = 1;       // attention blocks per KV head
+  // shared-memory plan, filled in by the launcher
+  int32_t ring = 0, max_tiles = 0, nb_max = 0, x_max = 0;
+  int32_t scratch_bytes = 0;
+  Trace trace;  // records carry id = step * (5 n_layers + 2) + phase
+};
+constexpr int kLoopMaxStop = 16;
+// Tagged words of the attention split records for `splits` blocks per KV head.
+size_t LoopPartialWords(int n_kv, int group, int splits);
+// Tags one launch of n_steps steps consumes (the next launch's epoch0 is at least this much higher).
+uint32_t LoopTagsPerLaunch(int n_layers, int n_steps);
+// Attention blocks per KV head for a grid of num_sms blocks and contexts up to max_seq.
+int LoopSplits(int n_kv, int num_sms, int64_t max_seq);
+// Group sizes (q heads per KV head) the loop kernel is built for.
+bool LoopSupportsGroup(int group);
+void PrepareLoopKernels(int num_sms);
+void LaunchDecodeLoop(const LoopParams& p, int group, int num_sms, cudaStream_t s);
 
 }  // namespace rpgb

@@ -29,4 +29,26 @@ void LaunchKernelArgs(const void* fn, dim3 grid, dim3 block, size_t smem, cudaSt
   RPGB_CUDA(cudaLaunchKernelExC(&cfg, fn, argv));
 }
 
+// As LaunchKernelArgs, with thread-block clusters of `cluster_x` blocks along x.
+template <typename... Args>
+void LaunchKernelClusterArgs(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
+                             unsigned cluster_x, Args... args) {
+  void* argv[] = {static_cast<void*>(&args)...};
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster_x;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2u : 1u;
+  RPGB_CUDA(cudaLaunchKernelExC(&cfg, fn, argv));
+}
+
 }  // namespace rpgb

@@ -252,6 +252,7 @@ std::unique_ptr<Model> Model::Load(const std::string& path, int device, int32_t 
   PrepareMatvecKernels();
   PrepareSampleKernels();
   PrepareAttentionKernels();
+  PrepareLoopKernels(m->num_sms_);
 
   auto require = [&](const std::string& name) -> const GgufTensor& {
     const GgufTensor* t = g.Find(name);
@@ -350,6 +351,8 @@ std::unique_ptr<Model> Model::Load(const std::string& path, int device, int32_t 
   m->rope_pos_ = std::max<int32_t>(1, std::min<int32_t>(max_pos, c.context_length));
   const size_t rope_bytes = static_cast<size_t>(m->rope_pos_) * c.head_dim * 4;
   total += AlignUp(rope_bytes);
+  const size_t layer_table_bytes = sizeof(DevLayer) * static_cast<size_t>(c.n_layers);
+  total += AlignUp(layer_table_bytes);
 
   RPGB_CUDA(cudaMalloc(&m->arena_, total));
   m->arena_bytes_ = static_cast<int64_t>(total);
@@ -450,6 +453,12 @@ std::unique_ptr<Model> Model::Load(const std::string& path, int device, int32_t 
     }
     m->rope_ = reinterpret_cast<float*>(carve(rope_bytes));
     upload_plain(m->rope_, rope.data(), rope_bytes);
+  }
+  // the layer table read by the decode loop kernel (pointers into this arena)
+  {
+    DevLayer* t = reinterpret_cast<DevLayer*>(carve(layer_table_bytes));
+    upload_plain(t, m->layers_.data(), layer_table_bytes);
+    m->layers_dev_ = t;
   }
   up.Wait();
   RPGB_CHECK(cursor <= total, "arena overflow (%zu > %zu)", cursor, total);

@@ -78,6 +78,7 @@ class Model {
   int device() const { return device_; }
   int num_sms() const { return num_sms_; }
   const std::vector<DevLayer>& layers() const { return layers_; }
+  const DevLayer* layers_dev() const { return layers_dev_; }  // the same table in device memory
   const DevMat& embd() const { return embd_; }
   const DevMat& lm_head() const { return lm_head_; }
   const float* out_norm() const { return out_norm_; }
@@ -94,6 +95,7 @@ class Model {
   uint8_t* arena_ = nullptr;
   int64_t arena_bytes_ = 0;
   std::vector<DevLayer> layers_;
+  const DevLayer* layers_dev_ = nullptr;
   DevMat embd_, lm_head_;
   const float* out_norm_ = nullptr;
   float* rope_ = nullptr;
