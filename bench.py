@@ -10,9 +10,15 @@ tokens, 64-token decode) with T=0.7, top_k=20, top_p=0.8 and a fixed seed.
 * e2e      the same decode tok/s measured on the host around the C-ABI calls
            (rpgb_prefill / rpgb_generate with host buffers: the H2D of the
            token ids and the D2H of the generated ids are inside).
-* roofline the decode matvec (96.8 % of the reference's decode kernel time):
-           every matrix of the model plus lm_head, one launch each, CUDA events
-           on the launching stream, algorithmic bytes = M*K/256*{144,210} + x + y.
+* roofline the decode loop kernel (one cooperative launch per generate call
+           runs every decode step): algorithmic bytes per decoded token = the
+           quantised weights of every matrix + lm_head + norms, plus the fp16
+           K/V rows the step's attention reads (2 * layers * kv_dim * 2 bytes
+           per cached position), divided by the decode device time from CUDA
+           events on the session stream.
+* roofline_matvec  the standalone decode matvec: every matrix of the model
+           plus lm_head, one launch each, CUDA events on the launching stream,
+           algorithmic bytes = M*K/256*{144,210} + x + y.
 * cpu_baseline  the CPU restatement of the reference loop (oracle/, the
            reference's own CPU engine is not vendored), bounded sample.
 
@@ -314,6 +320,19 @@ def ours(args):
     appends = [synthetic.seeded_tokens(APPEND, 2000 + 10 * rank + r, V) for r in range(ROUNDS)]
     opts = SampleOptions(*SAMPLE)
 
+    shape = synthetic.PRESETS[args.model]
+    w_tok, kv_pos = shape.weight_bytes_per_token(), shape.kv_bytes_per_position()
+
+    def turn_bytes():
+        """Algorithmic HBM bytes of one turn's decode steps (weights + K/V rows read)."""
+        tot, length = 0, PROMPT_LEN
+        for _ in range(ROUNDS):
+            length += APPEND
+            for i in range(DECODE):  # the step forwarding the token at position length + i reads length + i + 1 rows
+                tot += w_tok + kv_pos * (length + i + 1)
+            length += DECODE
+        return tot
+
     def turn(timing):
         sess.set_len(0)
         ev = []
@@ -385,6 +404,20 @@ def ours(args):
     clocks = clk.summary()
     stats = sess.stats()
 
+    # the decode loop kernel's roofline: algorithmic bytes / decode device time
+    hbm_peak, hbm_kind = peaks()
+    loop_bytes = turn_bytes() * args.steps
+    achieved = loop_bytes / (dec_ms * 1e-3) / 1e9
+    loop_roof = {"kernel": "DecodeLoopKernel", "bound": "hbm", "achieved": round(achieved, 1),
+                 "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
+                 "traffic": None, "peak_kind": hbm_kind,
+                 "bytes_per_token": {"weights": w_tok,
+                                     "kv_mean": round(loop_bytes / args.steps / (ROUNDS * DECODE) - w_tok)}}
+    tf = os.path.join(ROOT, "profiles", "decode_loop_traffic.json")
+    if os.path.exists(tf):  # dram bytes per decoded token from the committed ncu capture
+        with open(tf) as f:
+            loop_roof["traffic"] = json.load(f).get("dram_bytes_per_token")
+
     roof = None
     if rank == 0 and not args.no_roofline:
         sess.close()
@@ -423,8 +456,9 @@ def ours(args):
         }
         if clocks is not None:
             line["clocks"] = clocks
+        line["roofline"] = loop_roof
         if roof is not None:
-            line["roofline"] = roof
+            line["roofline_matvec"] = roof
         if cpu is not None:
             line["cpu_baseline"] = cpu
         if ref_gpu is not None:
