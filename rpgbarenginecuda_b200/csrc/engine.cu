@@ -620,6 +620,9 @@ LoopParams Session::MakeLoopParams(const SampleOpts& opt, uint64_t seed) const {
   lp.err = err_;
   lp.splits = loop_splits_;
   if (trace_rec_ != nullptr) {
+    int khz = 0;
+    RPGB_CUDA(cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, m_->device()));
+    lp.ns_per_cycle = 1.0e6 / static_cast<double>(std::max(khz, 1));
     lp.trace.rec = trace_rec_;
     lp.trace.count = trace_count_;
     lp.trace.cap = trace_cap_;

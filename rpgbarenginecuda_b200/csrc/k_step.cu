@@ -54,10 +54,11 @@ constexpr int kChunk = 4;      // attention positions per unit (their K rows, th
 constexpr int kD = 128;        // head dimension
 constexpr int kMaxRing = 8;
 constexpr int kSmallCap = 2048;  // fast-path candidates above the lower bound kept in shared memory
-// Tagged words of one attention partial record: o[G][128], m[G], and the
-// denominator l[G] as a float pair (hi, lo = l - hi), padded to an even count
-// so consecutive records stay 16-byte aligned.
-__host__ __device__ constexpr int RecWords(int G) { return (131 * G + 1) & ~1; }
+// Tagged words of one attention partial record: o[G][128], then per q head
+// g four words {m, l_hi, l_lo, unused} (the denominator l as a float pair,
+// l_lo = l - l_hi), so one head's (m, l) is a single 32-byte read and
+// consecutive records stay 16-byte aligned.
+__host__ __device__ constexpr int RecWords(int G) { return 132 * G; }
 constexpr int kSliceRows = 2048;
 constexpr int kMaxOwnRows = 64;  // rows of x one block owns in the o / down phases
 constexpr int kMaxLayers = 40;  // lm_head rows of one block for the candidate slices
@@ -225,11 +226,12 @@ __device__ __forceinline__ const uint8_t* SegBase(const LoopParams& p, int kind,
   return g_layers[layer].w[MatIdx(kind, seg)];
 }
 
-// Splits of a KV head that hold positions at this step: at least two chunks
-// each, so short contexts use few blocks (and the o phase merges few records).
+// Splits of a KV head that hold positions at this step: sixteen chunks (one
+// per warp) or more each, so short contexts use few blocks and the o phase
+// merges few records.
 __device__ __forceinline__ int EffSplits(const LoopParams& p, int64_t pos) {
   const int n_ch = static_cast<int>((pos + kChunk) / kChunk);  // chunks covering positions 0..pos
-  const int se = (n_ch + 1) / 2;
+  const int se = (n_ch + 15) / 16;  // at least 16 chunks (one per warp) per split
   return se < p.splits ? se : p.splits;
 }
 
@@ -532,30 +534,44 @@ __device__ __forceinline__ bool GridBarrier(const LoopParams& p, int* s_flag) {
 // phase (barrier arrival), t_ready = barrier release, t_end = end of the
 // phase; up to two marks inside a phase become extra records whose block
 // field carries k << 24 and whose t_end is the time of mark k.
+// Reading %globaltimer costs about a microsecond on this GPU, so the
+// timeline uses the SM's cycle counter and converts it to nanoseconds with
+// one %globaltimer anchor per block (the SM clock rate comes from the host).
 constexpr int kMarks = 4;
 struct PhaseClock {
   uint64_t t_prev, t_ready;
   uint64_t mk[kMarks];
+  uint64_t gt0;  // %globaltimer at the anchor
+  int64_t ck0;   // %clock64 at the anchor
 };
+__device__ __forceinline__ int64_t Clock64() {
+  int64_t c;
+  asm volatile("mov.u64 %0, %%clock64;" : "=l"(c));
+  return c;
+}
+__device__ __forceinline__ uint64_t ClockNs(const LoopParams& p, const PhaseClock& c) {
+  return c.gt0 + static_cast<uint64_t>(static_cast<double>(Clock64() - c.ck0) * p.ns_per_cycle);
+}
 __device__ __forceinline__ void TraceReady(const LoopParams& p, PhaseClock& c) {
-  if (p.trace.rec != nullptr && threadIdx.x == 0) c.t_ready = dev::GlobalTimer();
+  if (p.trace.rec != nullptr && threadIdx.x == 0) c.t_ready = ClockNs(p, c);
 }
 __device__ __forceinline__ void TraceMark(const LoopParams& p, PhaseClock& c, int k) {
-  if (p.trace.rec != nullptr && threadIdx.x == 0) c.mk[k - 1] = dev::GlobalTimer();
+  if (p.trace.rec != nullptr && threadIdx.x == 0) c.mk[k - 1] = ClockNs(p, c);
 }
 // As TraceMark, from lane 0 of warp 0 without requiring thread 0's control flow.
 __device__ __forceinline__ void TraceMarkW0(const LoopParams& p, PhaseClock& c, int k) {
-  if (p.trace.rec != nullptr && threadIdx.x == 0) c.mk[k - 1] = dev::GlobalTimer();
+  if (p.trace.rec != nullptr && threadIdx.x == 0) c.mk[k - 1] = ClockNs(p, c);
 }
+// Records of (phase id, block) go to fixed slots (no atomics on the way).
 __device__ __forceinline__ void TraceEnd(const LoopParams& p, PhaseClock& c, uint32_t id) {
   if (p.trace.rec != nullptr && threadIdx.x == 0) {
-    const uint64_t t = dev::GlobalTimer();
-    const uint32_t i = atomicAdd(p.trace.count, 1u + kMarks);
+    const uint64_t t = ClockNs(p, c);
+    const uint64_t i0 = (static_cast<uint64_t>(id) * gridDim.x + blockIdx.x) * (1 + kMarks);
     for (uint32_t k = 0; k <= kMarks; ++k) {
-      if (i + k >= p.trace.cap) break;
+      if (i0 + k >= p.trace.cap) break;
       const uint64_t te = k == 0 ? t : c.mk[k - 1];
       if (k > 0 && te == 0) {
-        p.trace.rec[i + k] = TraceRec{0xFFFFFFFFu, 0u, 0ull, 0ull, 0ull};
+        p.trace.rec[i0 + k] = TraceRec{0xFFFFFFFFu, 0u, 0ull, 0ull, 0ull};
         continue;
       }
       TraceRec r;
@@ -564,7 +580,7 @@ __device__ __forceinline__ void TraceEnd(const LoopParams& p, PhaseClock& c, uin
       r.t_start = c.t_prev;
       r.t_ready = c.t_ready ? c.t_ready : c.t_prev;
       r.t_end = te;
-      p.trace.rec[i + k] = r;
+      p.trace.rec[i0 + k] = r;
     }
     c.t_prev = t;
     c.t_ready = 0;
@@ -617,8 +633,9 @@ __device__ void MergeAttention(const LoopParams& p, int step, int layer, int64_t
   for (int i = tid; i < nr; i += kNT) {
     const int h = i / (se * G), r = i - h * se * G, sp = r / G, g = r - sp * G;
     const uint64_t* rec = p.llrec + (static_cast<size_t>(h) * S + sp) * kRec;
-    wv[i] = WaitLL1(p, rec + 128 * G + g, tag);
-    lv[i] = static_cast<double>(WaitLL1(p, rec + 129 * G + g, tag)) + WaitLL1(p, rec + 130 * G + g, tag);
+    const float4 ml = WaitLL4(p, rec + 128 * G + 4 * g, tag);  // {m, l_hi, l_lo, -}
+    wv[i] = ml.x;
+    lv[i] = static_cast<double>(ml.y) + ml.z;
   }
   __syncthreads();
   for (int i = tid; i < p.n_kv * G; i += kNT) {
@@ -733,7 +750,6 @@ __device__ void MvPhase(const LoopParams& p, const GeoTable& gt, int kind, int l
         }
       }
       PutDigits(v, b, lane, bfrag, sx, sscale);
-      if (b == 0) TraceMarkW0(p, clk, 1);  // warp 0: first input words arrived and split
     }
     if (norm_w != nullptr) {
       ssq = dev::WarpSumD(ssq);
@@ -741,7 +757,15 @@ __device__ void MvPhase(const LoopParams& p, const GeoTable& gt, int kind, int l
     }
     __syncthreads();
   }
-  TraceMark(p, clk, 2);  // input and digits ready in every warp
+  TraceMark(p, clk, 1);  // input and digits ready in every warp
+  // RMSNorm scale (applied to W x in the epilogue), computed here so its
+  // double-precision latency overlaps the units
+  float scale = 1.f;
+  if (norm_w != nullptr && any) {
+    double tot = 0.0;
+    for (int w = 0; w < kNW; ++w) tot += s_sq[w];
+    scale = static_cast<float>(1.0 / sqrt(tot / static_cast<double>(K) + static_cast<double>(p.eps)));
+  }
 
   // ---- units
   const int n_units = g.u1 - g.u0;
@@ -757,7 +781,6 @@ __device__ void MvPhase(const LoopParams& p, const GeoTable& gt, int kind, int l
     uint32_t type = SegType(p, kind, layer, SegOfTile(p, kind, g.t0 + tl, &st0));
     for (int i = 0; i < n_units; ++i) {
       const uint8_t* grp = RingWait(rg, p);
-      if (i == 0) TraceMarkW0(p, clk, 3);  // warp 0: first unit in shared memory
       LoadB(bfrag, b, lane, lo_half, bA, bB);
       const float s = sscale[b];
       if (type == 12u) {
@@ -778,15 +801,10 @@ __device__ void MvPhase(const LoopParams& p, const GeoTable& gt, int kind, int l
   }
   rg_io = rg;
   __syncthreads();
-  TraceMark(p, clk, 4);  // all units done
+  TraceMark(p, clk, 2);  // all units done
 
   // ---- epilogue
-  float scale = 1.f;
-  if (norm_w != nullptr && any) {
-    double tot = 0.0;
-    for (int w = 0; w < kNW; ++w) tot += s_sq[w];
-    scale = static_cast<float>(1.0 / sqrt(tot / static_cast<double>(K) + static_cast<double>(p.eps)));
-  }
+  TraceMark(p, clk, 3);
   const int U = (g.t1 - g.t0) * nb;
   const int n_rows = (g.t1 - g.t0) * kTile;
   const uint32_t tag_out = TagOf(p, step, layer, kind);
@@ -830,6 +848,7 @@ __device__ void MvPhase(const LoopParams& p, const GeoTable& gt, int kind, int l
       }
     }
   }
+  TraceMark(p, clk, 4);
   if (kind == kLm && p.mode == 0) {
     // block argmax, ties -> lowest index (src/kernels_gpu.cu:827-859)
 #pragma unroll
@@ -1065,9 +1084,10 @@ __device__ void AttnPhase(const LoopParams& p, const GeoTable& gt, int layer, in
       t = dev::WarpSumD(t);
       if (lane == 0) {
         const float lhi = static_cast<float>(t);
-        StLL(rec + 128 * G + g, M, tag_out);
-        StLL(rec + 129 * G + g, lhi, tag_out);
-        StLL(rec + 130 * G + g, static_cast<float>(t - static_cast<double>(lhi)), tag_out);
+        StLL(rec + 128 * G + 4 * g, M, tag_out);
+        StLL(rec + 128 * G + 4 * g + 1, lhi, tag_out);
+        StLL(rec + 128 * G + 4 * g + 2, static_cast<float>(t - static_cast<double>(lhi)), tag_out);
+        StLL(rec + 128 * G + 4 * g + 3, 0.f, tag_out);
       }
     }
   }
@@ -1133,7 +1153,9 @@ __global__ void __launch_bounds__(kNT, 1) DecodeLoopKernel(const LoopParams p) {
 
   __shared__ PhaseClock clk;  // thread 0's timeline (trace only)
   if (p.trace.rec != nullptr && tid == 0) {
-    clk.t_prev = dev::GlobalTimer();
+    clk.gt0 = dev::GlobalTimer();
+    clk.ck0 = Clock64();
+    clk.t_prev = clk.gt0;
     clk.t_ready = 0;
     for (int k = 0; k < kMarks; ++k) clk.mk[k] = 0;
   }
@@ -1248,6 +1270,10 @@ __global__ void __launch_bounds__(kNT, 1) DecodeLoopKernel(const LoopParams p) {
       const uint32_t slot = k % static_cast<uint32_t>(rg.R);
       if (!dev::MbarWait(rg.bars + slot, (k / static_cast<uint32_t>(rg.R)) & 1u)) atomicOr(p.err, 1u);
     }
+  }
+  if (p.trace.rec != nullptr && tid == 0) {
+    const uint64_t n = static_cast<uint64_t>(steps) * (5u * p.n_layers + 2u) * gridDim.x * (1 + kMarks);
+    atomicMax(p.trace.count, static_cast<uint32_t>(n < p.trace.cap ? n : p.trace.cap));
   }
   if (blockIdx.x == 0 && tid == 0) {
     *p.pos = pos0 + steps;

@@ -223,6 +223,7 @@ struct LoopParams {
   int32_t ring = 0, max_tiles = 0, nb_max = 0, x_max = 0;
   int32_t scratch_bytes = 0;
   Trace trace;  // records carry id = step * (5 n_layers + 2) + phase
+  double ns_per_cycle = 0.0;  // SM clock period, to turn cycle counts of the trace into nanoseconds
 };
 constexpr int kLoopMaxStop = 16;
 // Tagged words of the attention split records for `splits` blocks per KV head.
