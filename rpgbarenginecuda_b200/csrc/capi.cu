@@ -29,6 +29,11 @@ struct MatrixEntry {
   int64_t rows = 0;  // logical rows (storage is padded to whole 32-row groups)
   DevMat m;
   void* mem = nullptr;
+  // tensor-core GEMM scratch (grown on demand) and its error word
+  std::mutex tc_mu;
+  __half* tc = nullptr;
+  size_t tc_halves = 0;
+  unsigned* err = nullptr;
 };
 
 std::mutex g_mu;
@@ -262,6 +267,7 @@ int32_t rpgb_matrix_upload(int32_t device, uint32_t type, int64_t rows, int64_t 
     RPGB_CUDA(cudaDeviceGetAttribute(&e->num_sms, cudaDevAttrMultiProcessorCount, device));
     PrepareMatvecKernels();
     PrepareSampleKernels();
+    PrepareTcGemmKernels();
     const int64_t rb = GgmlRowBytes(type, cols);
     std::vector<uint8_t> src(static_cast<size_t>(prow * rb), 0);
     std::memcpy(src.data(), bytes, static_cast<size_t>(rows * rb));
@@ -294,6 +300,8 @@ void rpgb_matrix_free(int32_t matrix) {
     }
     cudaSetDevice(e->device);
     cudaFree(e->mem);
+    cudaFree(e->tc);
+    cudaFree(e->err);
   } catch (...) {
   }
 }
@@ -338,7 +346,37 @@ int32_t rpgb_matrix_matvec(int32_t matrix, const float* x_dev, int64_t n_tok, fl
       g.ldx = e->m.cols;
       g.out = out_dev;
       g.ldo = e->m.rows;
-      LaunchGemm(g, Epi::kStore, s);
+      if (n_tok >= kTcMinTokens && e->m.rows % 128 == 0) {
+        // tensor-core path: fp16 operand scratch kept with the matrix; the
+        // call waits for the GEMM to read its error word
+        std::lock_guard<std::mutex> lk(e->tc_mu);
+        const size_t need = TcGemmScratchHalves(e->m.rows, n_tok, e->m.cols);
+        if (e->tc_halves < need) {
+          RPGB_CUDA(cudaStreamSynchronize(s));
+          cudaFree(e->tc);
+          e->tc = nullptr;
+          e->tc_halves = 0;
+          RPGB_CUDA(cudaMalloc(&e->tc, need * sizeof(__half)));
+          e->tc_halves = need;
+        }
+        if (e->err == nullptr) {
+          RPGB_CUDA(cudaMalloc(&e->err, sizeof(unsigned)));
+          RPGB_CUDA(cudaMemset(e->err, 0, sizeof(unsigned)));
+        }
+        g.tc_scratch = e->tc;
+        g.tc_scratch_halves = e->tc_halves;
+        g.err = e->err;
+        LaunchGemm(g, Epi::kStore, s);
+        unsigned err = 0;
+        RPGB_CUDA(cudaMemcpyAsync(&err, e->err, sizeof(unsigned), cudaMemcpyDeviceToHost, s));
+        RPGB_CUDA(cudaStreamSynchronize(s));
+        if (err != 0) {
+          RPGB_CUDA(cudaMemset(e->err, 0, sizeof(unsigned)));
+          Throw("matvec: a bounded device wait of the tensor-core GEMM gave up (0x%x)", err);
+        }
+      } else {
+        LaunchGemm(g, Epi::kStore, s);
+      }
     }
     return 0;
   }

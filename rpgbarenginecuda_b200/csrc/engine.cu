@@ -210,6 +210,12 @@ void Session::EnsurePrefill(int64_t n) {
   cv.Add(sizeof(float) * cap * c.q_dim());
   cv.Add(sizeof(float) * cap * c.ffn);
   cv.Add(sizeof(int32_t) * cap);
+  // fp16 operands of the tensor-core GEMM: the largest layer matrix and the widest activations
+  const int64_t kmax = std::max<int64_t>(c.hidden, std::max<int64_t>(c.q_dim(), c.ffn));
+  const int64_t wmax = std::max<int64_t>(static_cast<int64_t>(2) * c.ffn * c.hidden,
+                                         static_cast<int64_t>(c.q_dim()) * c.hidden);
+  const size_t tc_halves = 2 * static_cast<size_t>(wmax) + 2 * static_cast<size_t>(cap) * kmax;
+  cv.Add(sizeof(__half) * tc_halves);
   RPGB_CUDA(cudaStreamSynchronize(stream_));
   cudaFree(pf_arena_);
   pf_arena_ = nullptr;
@@ -222,6 +228,8 @@ void Session::EnsurePrefill(int64_t n) {
   pf_attn_ = cv.Take<float>(cap * c.q_dim());
   pf_h_ = cv.Take<float>(cap * c.ffn);
   pf_tok_ = cv.Take<int32_t>(cap);
+  pf_tc_ = cv.Take<__half>(tc_halves);
+  pf_tc_halves_ = tc_halves;
   pf_cap_ = cap;
 }
 
@@ -250,6 +258,9 @@ void Session::Prefill(const int32_t* tokens, int64_t n, float* last_logits) {
     __half* vc = vc_ + layer_elems_ * l;
     LaunchRmsNormRows(pf_x_, L.attn_norm, nt, H, c.rms_eps, pf_xn_, s);
     GemmParams g;
+    g.tc_scratch = pf_tc_;
+    g.tc_scratch_halves = pf_tc_halves_;
+    g.err = err_;
     g.X = pf_xn_;
     g.n_tok = nt;
     g.ldx = H;
@@ -281,6 +292,9 @@ void Session::Prefill(const int32_t* tokens, int64_t n, float* last_logits) {
     a.fused = 0;
     LaunchAttention(a, nt, s);
     GemmParams o;
+    o.tc_scratch = pf_tc_;
+    o.tc_scratch_halves = pf_tc_halves_;
+    o.err = err_;
     o.w = L.o;
     o.X = pf_attn_;
     o.n_tok = nt;
@@ -292,6 +306,9 @@ void Session::Prefill(const int32_t* tokens, int64_t n, float* last_logits) {
     LaunchGemm(o, Epi::kResid, s);
     LaunchRmsNormRows(pf_x_, L.ffn_norm, nt, H, c.rms_eps, pf_xn_, s);
     GemmParams gu;
+    gu.tc_scratch = pf_tc_;
+    gu.tc_scratch_halves = pf_tc_halves_;
+    gu.err = err_;
     gu.w = L.gateup;
     gu.X = pf_xn_;
     gu.n_tok = nt;
@@ -300,6 +317,9 @@ void Session::Prefill(const int32_t* tokens, int64_t n, float* last_logits) {
     gu.ldo = c.ffn;
     LaunchGemm(gu, Epi::kSilu, s);
     GemmParams dn;
+    dn.tc_scratch = pf_tc_;
+    dn.tc_scratch_halves = pf_tc_halves_;
+    dn.err = err_;
     dn.w = L.down;
     dn.X = pf_h_;
     dn.n_tok = nt;
@@ -324,7 +344,14 @@ void Session::Prefill(const int32_t* tokens, int64_t n, float* last_logits) {
   if (last_logits != nullptr) {
     RPGB_CUDA(cudaMemcpyAsync(last_logits, logits_, sizeof(float) * c.vocab, cudaMemcpyDeviceToHost, s));
   }
+  unsigned err = 0;
+  RPGB_CUDA(cudaMemcpyAsync(&err, err_, sizeof(unsigned), cudaMemcpyDeviceToHost, s));
   RPGB_CUDA(cudaStreamSynchronize(s));
+  if (err != 0) {
+    RPGB_CUDA(cudaMemset(err_, 0, sizeof(unsigned)));
+    logits_valid_ = false;
+    Throw("prefill failed: a bounded device wait gave up (error flags 0x%x)", err);
+  }
   len_ = pos0 + n;
   logits_valid_ = true;
 }

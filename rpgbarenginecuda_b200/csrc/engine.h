@@ -120,6 +120,8 @@ class Session {
   float *pf_x_ = nullptr, *pf_xn_ = nullptr, *pf_qkv_ = nullptr, *pf_q_ = nullptr, *pf_attn_ = nullptr,
         *pf_h_ = nullptr;
   int32_t* pf_tok_ = nullptr;
+  __half* pf_tc_ = nullptr;  // fp16 operands of the tensor-core GEMM
+  size_t pf_tc_halves_ = 0;
   int32_t* host_ids_ = nullptr;  // pinned staging
   int64_t host_ids_cap_ = 0;
 

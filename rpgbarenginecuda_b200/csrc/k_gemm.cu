@@ -141,6 +141,10 @@ __global__ void __launch_bounds__(256) GemmKernel(const GemmParams p) {
 }  // namespace
 
 void LaunchGemm(const GemmParams& p, Epi epi, cudaStream_t s) {
+  if (p.tc_scratch != nullptr && p.n_tok >= kTcMinTokens && p.w.rows % 128 == 0) {
+    LaunchTcGemm(p, epi, p.tc_scratch, p.tc_scratch_halves, s);
+    return;
+  }
   RPGB_CHECK(p.w.rows % BM == 0, "gemm: rows %d not a multiple of %d", p.w.rows, BM);
   RPGB_CHECK(p.w.cols % 256 == 0, "gemm: cols %d not a multiple of 256", p.w.cols);
   RPGB_CHECK(p.n_tok > 0, "gemm: no tokens");

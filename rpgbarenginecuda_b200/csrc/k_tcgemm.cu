@@ -1,0 +1,417 @@
+// k_tcgemm.cu -- prefill GEMM on the 5th-generation tensor cores (tcgen05).
+//
+// out[t, r] = sum_k X[t, k] * W[r, k] for a Q4_K / Q6_K weight matrix W, the
+// prompt path of MatMulQ4KKernel / MatMulQ6KKernel with TILE = 8
+// (src/kernels_gpu.cu:325-494) as used by GpuForwardFull.
+//
+// Precision.  The reference dequantises every weight in FP32 and sums FP32
+// products.  Here both operands are split into two fp16 terms,
+//   W = Wh + Wl,  X = Xh + Xl   (Wh = fp16(W), Wl = fp16(W - Wh), same for X)
+// and the tensor cores accumulate Wh*Xh + Wh*Xl + Wl*Xh in FP32 (TMEM): about
+// 22 significant bits of each operand survive, so results differ from the
+// FP32 path at the 1e-6 relative level (the dropped Wl*Xl term is ~2^-22).
+//
+// Pipeline (one 128 x 128 output tile per block of 4 warps):
+//  * DequantSplitKernel writes the layer matrix once per call as Wh / Wl
+//    (row-major, fp16) with the bit-exact per-element dequant formulas;
+//    SplitKernel writes Xh / Xl;
+//  * thread 0 streams 64-column k-slices of Wh, Wl, Xh, Xl into three
+//    shared-memory stages with 2-D TMA tensor copies (128-byte swizzle);
+//  * thread 32 issues tcgen05.mma.cta_group::1.kind::f16 (M 128, N 128,
+//    K 16; 12 per k-slice) into a 128-column TMEM accumulator and frees each
+//    stage with tcgen05.commit on its "empty" mbarrier;
+//  * all four warps read their 32 TMEM lanes (= 32 weight rows) with
+//    tcgen05.ld and apply the epilogue (store, residual add, or SiLU(gate) *
+//    up on interleaved row pairs) with coalesced stores.
+// Every mbarrier wait is bounded; a wait that gives up sets *err, and the
+// block still waits for its own copies and MMAs and frees its TMEM.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "common.h"
+#include "kernels.cuh"
+#include "kernels.h"
+
+namespace rpgb {
+namespace {
+
+constexpr int kBM = 128;     // weight rows per tile (MMA M)
+constexpr int kBN = 128;     // tokens per tile (MMA N)
+constexpr int kBK = 64;      // k per stage: 64 fp16 = one 128-byte swizzle row
+constexpr int kStages = 3;
+constexpr int kThreads = 128;
+constexpr uint32_t kTileBytes = kBM * kBK * 2;  // 16 KB, same for the B tiles (kBN == kBM)
+constexpr uint32_t kStageBytes = 4 * kTileBytes;
+constexpr size_t kSmemBytes = kStages * kStageBytes + 1024;  // + alignment slack
+
+// ------------------------------------------------------------------ operand preparation
+
+__device__ __forceinline__ void SplitStore8(const float (&v)[8], __half* hi, __half* lo) {
+  __align__(16) __half h[8], l[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    h[i] = __float2half_rn(v[i]);
+    l[i] = __float2half_rn(v[i] - __half2float(h[i]));
+  }
+  *reinterpret_cast<uint4*>(hi) = *reinterpret_cast<const uint4*>(h);
+  *reinterpret_cast<uint4*>(lo) = *reinterpret_cast<const uint4*>(l);
+}
+
+// W (repacked Q4_K / Q6_K) -> Wh, Wl [rows][K].  One thread per 8 consecutive
+// columns of a row; the values are those of DeqQ4K / DeqQ6K (separately
+// rounded products, as src/quant.cc).
+__global__ void __launch_bounds__(256) DequantSplitKernel(const DevMat w, __half* __restrict__ hi,
+                                                          __half* __restrict__ lo) {
+  const int K = w.cols;
+  const int64_t items = static_cast<int64_t>(w.rows) * (K / 8);
+  for (int64_t it = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; it < items;
+       it += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = it / (K / 8);
+    const int col = static_cast<int>(it - row * (K / 8)) * 8;
+    const int b = col >> 8, kb = (col & 255) >> 5, lk = col & 31;
+    const uint8_t* grp = dev::GroupPtr(w, row, b);
+    const int r16 = static_cast<int>(row & 15), g = r16 & 7, rs = r16 >> 3;
+    float v[8];
+    if (w.type == 12u) {
+      const uint4 hd = *reinterpret_cast<const uint4*>(grp + 2048 + 16 * r16);
+      int sc, m;
+      dev::Q4kScaleMin(hd.y, hd.z, hd.w, kb, &sc, &m);
+      const float d1 = __fmul_rn(dev::Half(hd.x & 0xFFFFu), static_cast<float>(sc));
+      const float m1 = __fmul_rn(dev::Half(hd.x >> 16), static_cast<float>(m));
+      const int c = kb >> 1, h = lk >> 4, t0 = (lk >> 2) & 3;
+      const uint32_t* wp = reinterpret_cast<const uint32_t*>(grp + (c * 32 + 4 * g + t0) * 16 + (2 * h + rs) * 4);
+      const uint32_t qw[2] = {wp[0], wp[4]};
+      const int sh = (kb & 1) * 4;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int q = static_cast<int>((qw[i >> 2] >> (8 * (i & 3) + sh)) & 15u);
+        v[i] = __fsub_rn(__fmul_rn(d1, static_cast<float>(q)), m1);
+      }
+    } else {
+      const int j16 = 2 * kb + (lk >> 4);
+      const int8_t sc = static_cast<int8_t>(grp[3072 + 16 * r16 + j16]);
+      const float dd = dev::Half(*reinterpret_cast<const uint16_t*>(grp + 3328 + 2 * (2 * g + rs)));
+      const float ds = __fmul_rn(dd, static_cast<float>(sc));
+      const int c = j16 >> 2, h = j16 & 1, hb = (j16 >> 1) & 1, m = 2 * c + h;
+      const int t0 = (lk & 15) >> 2;
+#pragma unroll
+      for (int tt = 0; tt < 2; ++tt) {
+        const uint32_t* wq =
+            reinterpret_cast<const uint32_t*>(grp + ((m >> 2) * 32 + 4 * g + t0 + tt) * 48 + (m & 3) * 12);
+        const uint32_t X = wq[0], Y = wq[1], Z = wq[2];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          int q;
+          if (hb == 0) {
+            q = static_cast<int>(((rs == 0 ? X : Y) >> (8 * e)) & 63u);
+          } else if (rs == 0) {
+            q = static_cast<int>((Z >> (8 * e)) & 63u);
+          } else {
+            q = static_cast<int>(((X >> (8 * e + 6)) & 3u) | (((Y >> (8 * e + 6)) & 3u) << 2) |
+                                 (((Z >> (8 * e + 6)) & 3u) << 4));
+          }
+          v[4 * tt + e] = __fmul_rn(ds, static_cast<float>(q - 32));
+        }
+      }
+    }
+    SplitStore8(v, hi + row * K + col, lo + row * K + col);
+  }
+}
+
+// X [n][ldx] (first K columns) -> Xh, Xl [n][K].
+__global__ void __launch_bounds__(256) SplitKernel(const float* __restrict__ X, int n, int ldx, int K,
+                                                   __half* __restrict__ hi, __half* __restrict__ lo) {
+  const int64_t items = static_cast<int64_t>(n) * (K / 8);
+  for (int64_t it = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; it < items;
+       it += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = it / (K / 8);
+    const int col = static_cast<int>(it - t * (K / 8)) * 8;
+    const float4 a = *reinterpret_cast<const float4*>(X + t * ldx + col);
+    const float4 b = *reinterpret_cast<const float4*>(X + t * ldx + col + 4);
+    const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    SplitStore8(v, hi + t * K + col, lo + t * K + col);
+  }
+}
+
+// ------------------------------------------------------------------ tcgen05 / TMA primitives
+
+__device__ __forceinline__ void TmaLoad2D(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dev::SmemAddr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(dev::SmemAddr(bar))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major tile written by TMA with the
+// 128-byte swizzle: rows of 128 bytes, 8-row groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t DescSw128(const void* tile) {
+  const uint32_t a = dev::SmemAddr(tile);
+  uint64_t d = static_cast<uint64_t>((a >> 4) & 0x3FFFu);  // start address
+  d |= static_cast<uint64_t>(1) << 16;                     // leading byte offset (unused with swizzle)
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;             // stride byte offset: one 8-row group
+  d |= static_cast<uint64_t>(1) << 46;                     // descriptor version
+  d |= static_cast<uint64_t>(2) << 61;                     // 128-byte swizzle
+  return d;
+}
+
+// Instruction descriptor: kind::f16, A and B fp16, D fp32, both K-major.
+__host__ __device__ constexpr uint32_t InstrDesc(int m, int n) {
+  return (1u << 4) | (0u << 7) | (0u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void Mma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void MmaCommit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   dev::SmemAddr(bar))
+               : "memory");
+}
+__device__ __forceinline__ void FenceBeforeSync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void FenceAfterSync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void TmemLoad16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// ------------------------------------------------------------------ the GEMM
+
+struct TcArgs {
+  int32_t n_tok, K;
+  float* out;
+  int32_t ldo, out_off;
+  const float* resid;
+  int32_t ldr;
+  unsigned* err;
+};
+
+template <int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    TcGemmKernel(const __grid_constant__ CUtensorMap mWh, const __grid_constant__ CUtensorMap mWl,
+                 const __grid_constant__ CUtensorMap mXh, const __grid_constant__ CUtensorMap mXl, const TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full[kStages], empty[kStages], accf;
+  __shared__ uint32_t s_tmem;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tok0 = blockIdx.x * kBN, row0 = blockIdx.y * kBM;
+  const int nk = a.K / kBK;
+
+  if (warp == 0) {  // the accumulator: 128 TMEM columns x 128 lanes (fp32)
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dev::SmemAddr(&s_tmem)),
+                 "r"(128u)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      dev::MbarInit(full + s, 1);
+      dev::MbarInit(empty + s, 1);
+    }
+    dev::MbarInit(&accf, 1);
+    dev::MbarInitFence();
+  }
+  FenceBeforeSync();
+  __syncthreads();
+  FenceAfterSync();
+  const uint32_t tmem = s_tmem;
+
+  if (tid == 0) {
+    // ---- producer: k-slices of Wh, Wl, Xh, Xl into the stages
+    int issued = 0;
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % kStages;
+      if (kb >= kStages && !dev::MbarWait(empty + s, static_cast<uint32_t>((kb / kStages - 1) & 1))) {
+        atomicOr(a.err, 16u);
+        break;
+      }
+      uint8_t* st = smem + s * kStageBytes;
+      dev::MbarExpectTx(full + s, kStageBytes);
+      TmaLoad2D(st, &mWh, kb * kBK, row0, full + s);
+      TmaLoad2D(st + kTileBytes, &mWl, kb * kBK, row0, full + s);
+      TmaLoad2D(st + 2 * kTileBytes, &mXh, kb * kBK, tok0, full + s);
+      TmaLoad2D(st + 3 * kTileBytes, &mXl, kb * kBK, tok0, full + s);
+      issued = kb + 1;
+    }
+    // the copies of the last stages land before the block may exit
+    for (int kb = std::max(0, issued - kStages); kb < issued; ++kb) {
+      dev::MbarWait(full + kb % kStages, static_cast<uint32_t>((kb / kStages) & 1));
+    }
+  } else if (tid == 32) {
+    // ---- MMA issuer
+    constexpr uint32_t idesc = InstrDesc(kBM, kBN);
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % kStages;
+      if (!dev::MbarWait(full + s, static_cast<uint32_t>((kb / kStages) & 1))) {
+        atomicOr(a.err, 16u);
+        break;
+      }
+      FenceAfterSync();
+      const uint8_t* st = smem + s * kStageBytes;
+      const uint64_t dWh = DescSw128(st), dWl = DescSw128(st + kTileBytes);
+      const uint64_t dXh = DescSw128(st + 2 * kTileBytes), dXl = DescSw128(st + 3 * kTileBytes);
+#pragma unroll
+      for (int kk = 0; kk < kBK / 16; ++kk) {
+        const uint64_t adv = static_cast<uint64_t>(kk * 32 >> 4);  // 16 fp16 = 32 bytes along K
+        Mma(tmem, dWh + adv, dXh + adv, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+        Mma(tmem, dWh + adv, dXl + adv, idesc, 1u);
+        Mma(tmem, dWl + adv, dXh + adv, idesc, 1u);
+      }
+      MmaCommit(empty + s);  // the stage is free once these MMAs have read it
+    }
+    MmaCommit(&accf);  // the accumulator is complete once every issued MMA is
+  }
+  __syncwarp();
+
+  // ---- epilogue: warp w owns TMEM lanes (weight rows) 32 w .. 32 w + 31
+  const bool ok = dev::MbarWait(&accf, 0u);
+  if (!ok && lane == 0) atomicOr(a.err, 32u);
+  FenceAfterSync();
+  const int r = row0 + 32 * warp + lane;
+  if (ok) {
+    for (int c0 = 0; c0 < kBN; c0 += 16) {
+      uint32_t v[16];
+      TmemLoad16(tmem + (static_cast<uint32_t>(32 * warp) << 16) + static_cast<uint32_t>(c0), v);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int t = tok0 + c0 + j;
+        const float acc = __uint_as_float(v[j]);
+        if (EPI == static_cast<int>(Epi::kSilu)) {
+          // rows 2i (gate) and 2i+1 (up) sit in neighbouring lanes
+          const float u = __shfl_xor_sync(0xFFFFFFFFu, acc, 1);
+          if (t < a.n_tok && (lane & 1) == 0) {
+            a.out[static_cast<int64_t>(t) * a.ldo + (r >> 1)] = (acc / (1.0f + expf(-acc))) * u;
+          }
+        } else if (t < a.n_tok) {
+          if (EPI == static_cast<int>(Epi::kResid)) {
+            float* o = a.out + static_cast<int64_t>(t) * a.ldo + r;
+            *o = a.resid[static_cast<int64_t>(t) * a.ldr + r] + acc;
+          } else {
+            a.out[static_cast<int64_t>(t) * a.ldo + a.out_off + r] = acc;
+          }
+        }
+      }
+    }
+  }
+  FenceBeforeSync();
+  __syncthreads();
+  if (warp == 0) {
+    FenceAfterSync();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(128u) : "memory");
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+PFN_cuTensorMapEncodeTiled_v12000 EncodeFn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+  });
+  RPGB_CHECK(fn != nullptr, "tcgen05 gemm: cuTensorMapEncodeTiled is unavailable");
+  return fn;
+}
+
+// Row-major fp16 [rows][K] as a 2-D tensor map with 64 x 128 boxes, 128-byte swizzle.
+CUtensorMap MapOf(const __half* base, int64_t rows, int K) {
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(kBM)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = EncodeFn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides,
+                                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  RPGB_CHECK(r == CUDA_SUCCESS, "tcgen05 gemm: tensor map encoding failed (%d)", static_cast<int>(r));
+  return m;
+}
+
+using TcFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const TcArgs);
+
+TcFn PickTc(Epi epi) {
+  switch (epi) {
+    case Epi::kStore: return TcGemmKernel<0>;
+    case Epi::kResid: return TcGemmKernel<1>;
+    case Epi::kSilu: return TcGemmKernel<2>;
+    default: Throw("tcgen05 gemm: unsupported epilogue");
+  }
+}
+
+}  // namespace
+
+void PrepareTcGemmKernels() {
+  for (Epi e : {Epi::kStore, Epi::kResid, Epi::kSilu}) {
+    RPGB_CUDA(cudaFuncSetAttribute(PickTc(e), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(kSmemBytes)));
+  }
+}
+
+size_t TcGemmScratchHalves(int64_t rows, int64_t n_tok, int K) {
+  return 2 * static_cast<size_t>(rows) * K + 2 * static_cast<size_t>(n_tok) * K;
+}
+
+void LaunchTcGemm(const GemmParams& p, Epi epi, __half* scratch, size_t scratch_halves, cudaStream_t s) {
+  const DevMat& w = p.w;
+  const int K = w.cols;
+  RPGB_CHECK(w.rows % kBM == 0, "tcgen05 gemm: rows %d not a multiple of %d", w.rows, kBM);
+  RPGB_CHECK(K % 256 == 0, "tcgen05 gemm: cols %d not a multiple of 256", K);
+  RPGB_CHECK(p.n_tok > 0 && p.ldx % 4 == 0, "tcgen05 gemm: bad activations");
+  RPGB_CHECK(p.err != nullptr, "tcgen05 gemm: no error word");
+  const size_t need = TcGemmScratchHalves(w.rows, p.n_tok, K);
+  RPGB_CHECK(scratch != nullptr && scratch_halves >= need, "tcgen05 gemm: scratch of %zu halves < %zu",
+             scratch_halves, need);
+  __half* wh = scratch;
+  __half* wl = wh + static_cast<size_t>(w.rows) * K;
+  __half* xh = wl + static_cast<size_t>(w.rows) * K;
+  __half* xl = xh + static_cast<size_t>(p.n_tok) * K;
+  {
+    const int64_t items = static_cast<int64_t>(w.rows) * (K / 8);
+    const int blocks = static_cast<int>(std::min<int64_t>((items + 255) / 256, 148 * 16));
+    DequantSplitKernel<<<blocks, 256, 0, s>>>(w, wh, wl);
+    RPGB_CUDA(cudaGetLastError());
+  }
+  {
+    const int64_t items = static_cast<int64_t>(p.n_tok) * (K / 8);
+    const int blocks = static_cast<int>(std::min<int64_t>((items + 255) / 256, 148 * 16));
+    SplitKernel<<<blocks, 256, 0, s>>>(p.X, p.n_tok, p.ldx, K, xh, xl);
+    RPGB_CUDA(cudaGetLastError());
+  }
+  const CUtensorMap mWh = MapOf(wh, w.rows, K), mWl = MapOf(wl, w.rows, K);
+  const CUtensorMap mXh = MapOf(xh, p.n_tok, K), mXl = MapOf(xl, p.n_tok, K);
+  TcArgs a;
+  a.n_tok = p.n_tok;
+  a.K = K;
+  a.out = p.out;
+  a.ldo = p.ldo;
+  a.out_off = p.out_off;
+  a.resid = p.resid;
+  a.ldr = p.ldr;
+  a.err = p.err;
+  const dim3 grid((p.n_tok + kBN - 1) / kBN, w.rows / kBM);
+  RPGB_CHECK(grid.y < 65536, "tcgen05 gemm: too many rows");
+  PickTc(epi)<<<grid, kThreads, kSmemBytes, s>>>(mWh, mWl, mXh, mXl, a);
+  RPGB_CUDA(cudaGetLastError());
+  CountLaunches(3);
+}
+
+}  // namespace rpgb

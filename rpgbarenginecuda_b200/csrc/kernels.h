@@ -142,8 +142,19 @@ struct GemmParams {
   int32_t ldo = 0, out_off = 0;
   const float* resid = nullptr;
   int32_t ldr = 0;
+  // tensor-core path (k_tcgemm.cu): fp16 operand scratch of at least
+  // TcGemmScratchHalves(rows, n_tok, cols) halves, and an error word
+  __half* tc_scratch = nullptr;
+  size_t tc_scratch_halves = 0;
+  unsigned* err = nullptr;
 };
+// Prompts of at least kTcMinTokens tokens (and weight rows a multiple of 128)
+// run on the tcgen05 GEMM when scratch is given; others on the FP32 SIMT tile.
+constexpr int kTcMinTokens = 128;
 void LaunchGemm(const GemmParams& p, Epi epi, cudaStream_t s);
+void LaunchTcGemm(const GemmParams& p, Epi epi, __half* scratch, size_t scratch_halves, cudaStream_t s);
+size_t TcGemmScratchHalves(int64_t rows, int64_t n_tok, int K);
+void PrepareTcGemmKernels();
 
 // ------------------------------------------------------------------ sampler
 struct SampleParams {
