@@ -64,6 +64,12 @@ def parse():
     ap.add_argument("--matvec-shapes", action="store_true",
                     help="launch the decode matvec once per distinct matrix shape of the model and exit "
                          "(the command profiled by ncu for profiles/)")
+    ap.add_argument("--tcgemm-shape", action="store_true",
+                    help="run the tcgen05 prefill GEMM twice on a Q4_K 6144x2048 matrix x 1024 tokens and exit "
+                         "(the command profiled by ncu for profiles/)")
+    ap.add_argument("--decode-loop-ctx", type=int, default=0,
+                    help="prefill this many tokens, then two generate calls (2 and 4 decode steps) and exit "
+                         "(the second decode-loop launch is the one profiled for profiles/)")
     ap.add_argument("--with-ref-gpu", action="store_true",
                     help="also time the reference's own CUDA engine (built from its sources) on the same turn")
     return ap.parse_args()
@@ -288,6 +294,39 @@ def matvec_shapes(args):
         m.close()
 
 
+def tcgemm_shape(args):
+    """Two launches of the tensor-core prefill GEMM (operator entry, 1024 tokens)."""
+    import torch
+
+    from rpgbarenginecuda_b200 import GGML_Q4_K, Matrix, synthetic
+
+    rows, cols, n = 6144, 2048, 1024
+    b = synthetic.quantize(synthetic.normal(1, rows * cols, 0.0, 0.02), "q4_k")
+    m = Matrix(GGML_Q4_K, rows, cols, b)
+    x = torch.from_numpy(synthetic.normal(2, n * cols, 0.0, 1.0).reshape(n, cols)).cuda()
+    out = torch.empty((n, rows), dtype=torch.float32, device="cuda")
+    for _ in range(2):
+        m.matvec(x.data_ptr(), n, out.data_ptr())
+    torch.cuda.synchronize()
+    print("tcgemm q4k_6144x2048 n=1024 max|out| %.4f" % float(out.abs().max()), flush=True)
+    m.close()
+
+
+def decode_loop_ctx(args):
+    """Prefill args.decode_loop_ctx tokens, then generate 2 and 4 tokens (two decode-loop launches)."""
+    from rpgbarenginecuda_b200 import Model, SampleOptions, Session, synthetic
+
+    m = Model(synthetic.cached_model(args.model, seed=0), 0, 4096)
+    s = Session(m, 4096)
+    s.prefill(synthetic.seeded_tokens(args.decode_loop_ctx, 0, m.vocab), want_logits=False)
+    opts = SampleOptions(*SAMPLE)
+    s.generate(opts, 1, 2)
+    ids = s.generate(opts, 1, 4)
+    print("decode loop at context %d: %s" % (args.decode_loop_ctx, list(map(int, ids))), flush=True)
+    s.close()
+    m.close()
+
+
 def ours(args):
     import numpy as np
     import torch
@@ -495,6 +534,12 @@ def main():
     args = parse()
     if args.matvec_shapes:
         matvec_shapes(args)
+        return
+    if args.tcgemm_shape:
+        tcgemm_shape(args)
+        return
+    if args.decode_loop_ctx > 0:
+        decode_loop_ctx(args)
         return
     if args.impl == "reference":
         return reference_arm(args)

@@ -128,7 +128,7 @@ RPGB_API int32_t rpgb_matrix_dequant(int32_t matrix, int64_t row0, int64_t n_row
 
 /* out_dev[t][r] = sum_c W[r][c] * x_dev[t][c] (GpuMatMulQuant,
  * src/kernels_gpu.cu:939-975): n_tok == 1 uses the decode matvec, larger n
- * the prefill GEMM -- from 128 tokens (and rows a multiple of 128) the
+ * the prefill GEMM -- from 16 tokens (and rows a multiple of 128) the
  * tcgen05 tensor-core GEMM, which keeps fp16 operand scratch with the matrix
  * and returns only after the GEMM has finished. */
 RPGB_API int32_t rpgb_matrix_matvec(int32_t matrix, const float* x_dev, int64_t n_tok, float* out_dev,

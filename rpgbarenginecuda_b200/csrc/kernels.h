@@ -150,7 +150,7 @@ struct GemmParams {
 };
 // Prompts of at least kTcMinTokens tokens (and weight rows a multiple of 128)
 // run on the tcgen05 GEMM when scratch is given; others on the FP32 SIMT tile.
-constexpr int kTcMinTokens = 128;
+constexpr int kTcMinTokens = 16;
 void LaunchGemm(const GemmParams& p, Epi epi, cudaStream_t s);
 void LaunchTcGemm(const GemmParams& p, Epi epi, __half* scratch, size_t scratch_halves, cudaStream_t s);
 size_t TcGemmScratchHalves(int64_t rows, int64_t n_tok, int K);
