@@ -290,7 +290,12 @@ void Session::Prefill(const int32_t* tokens, int64_t n, float* last_logits) {
     a.out = pf_attn_;
     a.n_splits = 1;
     a.fused = 0;
-    LaunchAttention(a, nt, s);
+    a.err = err_;
+    if (FlashSupports(c.group(), c.head_dim)) {
+      LaunchFlashPrefill(a, nt, pos0, s);
+    } else {
+      LaunchAttention(a, nt, s);
+    }
     GemmParams o;
     o.tc_scratch = pf_tc_;
     o.tc_scratch_halves = pf_tc_halves_;

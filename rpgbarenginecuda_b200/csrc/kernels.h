@@ -124,6 +124,13 @@ constexpr int kMaxAttnCluster = 8;  // decode: the splits of one KV head form on
 void LaunchAttention(const AttnParams& p, int n_queries, cudaStream_t s, bool pdl = false);
 void PrepareAttentionKernels();
 size_t AttentionPartialFloats(int n_kv, int group, int n_splits);
+// Prefill attention on the tensor cores (k_flash.cu): q = p.q (normalised,
+// rotated, stride p.q_stride), queries at positions pos0 .. pos0 + n - 1 over
+// the layer's cache p.kc / p.vc, out = p.out [n][q_dim]; p.err receives
+// bounded-wait failures.  For head_dim 128 and group sizes 1, 2, 4, 8.
+bool FlashSupports(int group, int head_dim);
+void LaunchFlashPrefill(const AttnParams& p, int n_queries, int64_t pos0, cudaStream_t s);
+void PrepareFlashKernels();
 
 // Prefill helpers: per-head RMSNorm + RoPE for q and k, fp16 cache write of k and v.
 void LaunchQkRopeKv(const float* qkv, int n_tok, int q_dim, int kv_dim, const float* q_norm,

@@ -254,6 +254,7 @@ std::unique_ptr<Model> Model::Load(const std::string& path, int device, int32_t 
   PrepareAttentionKernels();
   PrepareLoopKernels(m->num_sms_);
   PrepareTcGemmKernels();
+  PrepareFlashKernels();
 
   auto require = [&](const std::string& name) -> const GgufTensor& {
     const GgufTensor* t = g.Find(name);
