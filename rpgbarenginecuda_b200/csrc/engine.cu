@@ -82,7 +82,7 @@ Session::Session(const Model* m, int64_t max_seq) : m_(m), max_seq_(max_seq) {
   }
   const size_t part_floats = AttentionPartialFloats(c.n_kv_heads, c.group(), n_splits_);
   ll_words_ = static_cast<size_t>(c.hidden) + (c.q_dim() + 2 * c.kv_dim()) + c.ffn +
-              LoopPartialWords(c.n_kv_heads, c.group(), loop_splits_);
+              LoopPartialWords(c.n_kv_heads, c.group(), loop_splits_) + c.q_dim();
   const int am_grid = std::max(MatvecGrid(c.vocab, 4, m->num_sms()), m->num_sms());
   const int qkv = c.q_dim() + 2 * c.kv_dim();
   Carver cv;
@@ -108,6 +108,7 @@ Session::Session(const Model* m, int64_t max_seq) : m_(m), max_seq_(max_seq) {
   cv.Add(sizeof(int32_t));                    // steps done
   cv.Add(sizeof(int32_t) * kLoopMaxStop);     // stop ids
   cv.Add(sizeof(uint64_t) * ll_words_);       // tagged words of the decode loop
+  cv.Add(sizeof(uint32_t) * c.n_kv_heads);    // attention tickets
   RPGB_CUDA(cudaMalloc(&dec_arena_, cv.total()));
   RPGB_CUDA(cudaMemsetAsync(dec_arena_, 0, cv.total(), stream_));
   cv.Begin(dec_arena_);
@@ -133,6 +134,7 @@ Session::Session(const Model* m, int64_t max_seq) : m_(m), max_seq_(max_seq) {
   steps_done_ = cv.Take<int32_t>(1);
   stop_dev_ = cv.Take<int32_t>(kLoopMaxStop);
   ll_ = cv.Take<uint64_t>(ll_words_);  // zeroed with the arena: tag 0 is never a valid tag
+  tickets_loop_ = cv.Take<uint32_t>(c.n_kv_heads);
   RPGB_CUDA(cudaMallocHost(&loop_host_, sizeof(int32_t)));
   RPGB_CUDA(cudaStreamSynchronize(stream_));
 }
@@ -622,6 +624,8 @@ LoopParams Session::MakeLoopParams(const SampleOpts& opt, uint64_t seed) const {
   lp.llqkv = lp.llx + c.hidden;
   lp.llh = lp.llqkv + (c.q_dim() + 2 * c.kv_dim());
   lp.llrec = lp.llh + c.ffn;
+  lp.llattn = lp.llrec + LoopPartialWords(c.n_kv_heads, c.group(), loop_splits_);
+  lp.tickets = tickets_loop_;
   lp.logits = logits_;
   lp.probs = probs_;
   lp.pos = pos_;

@@ -110,7 +110,8 @@ class Session {
   int32_t* loop_host_ = nullptr;  // pinned: steps done
   int loop_splits_ = 1;
   bool loop_ready_ = false;
-  uint64_t* ll_ = nullptr;  // tagged words (x, qkv, ffn activation, attention records)
+  uint64_t* ll_ = nullptr;  // tagged words (x, qkv, ffn activation, attention records, merged attention)
+  uint32_t* tickets_loop_ = nullptr;
   size_t ll_words_ = 0;
   uint32_t epoch_ = 1;      // first tag base of the next launch
 

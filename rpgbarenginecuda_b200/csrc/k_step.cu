@@ -93,7 +93,8 @@ __host__ __device__ inline Plan MakePlan(int ring, int nb_max, int x_max, int sc
 // Bytes of the split-merge tables: weights (float) and denominators (double)
 // of every (KV head, split, group member), and 1/L per (KV head, member).
 __host__ __device__ inline size_t MergeBytes(int n_kv, int splits, int group) {
-  return static_cast<size_t>(n_kv) * splits * group * 12 + static_cast<size_t>(n_kv) * group * 4 + 16;
+  (void)n_kv;  // one head is merged at a time
+  return static_cast<size_t>(splits) * group * 12 + static_cast<size_t>(group) * 4 + 16;
 }
 
 // Bytes of the scratch union for a model (the largest phase user).
@@ -615,77 +616,60 @@ __device__ __forceinline__ void Ld8(const float* src, bool shared, float (&v)[8]
   v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
-// Merged attention output of all q heads -> xs[q_dim]: the split records of
-// KV head h are combined as in the split-K merge of the standalone kernel
-// (weights exp(m_s - M), double denominator).  Three passes: (m, l) of every
-// record, per (head, member) the weights and 1/L, then the weighted sums of o
-// (each thread: one float4 of one q head, loads in independent batches).
+// Merge of KV head h's split records -> the attention output of its G q
+// heads, published as tagged words (tag of the attention phase): weights
+// exp(m_s - M), double denominator, as the split-K merge of the standalone
+// kernel.  Runs in the last block of the head to finish (the records are
+// tagged words, so their arrival order needs no memory ordering).
 template <int G>
-__device__ void MergeAttention(const LoopParams& p, int step, int layer, int64_t pos, float* xs, uint8_t* merge) {
+__device__ void MergeHead(const LoopParams& p, int step, int layer, int64_t pos, int h, uint8_t* merge) {
   const int tid = threadIdx.x;
   const uint32_t tag = TagOf(p, step, layer, kAttn);
   const int S = p.splits, se = EffSplits(p, pos);
   constexpr int kRec = RecWords(G);
-  const int nr = p.n_kv * se * G;
-  float* wv = reinterpret_cast<float*>(merge);                                        // [n_kv][se][G]
-  double* lv = reinterpret_cast<double*>(merge + Al(static_cast<size_t>(nr) * 4, 8));  // [n_kv][se][G]
-  float* inv = reinterpret_cast<float*>(lv + nr);                                     // [n_kv][G]
-  for (int i = tid; i < nr; i += kNT) {
-    const int h = i / (se * G), r = i - h * se * G, sp = r / G, g = r - sp * G;
-    const uint64_t* rec = p.llrec + (static_cast<size_t>(h) * S + sp) * kRec;
-    const float4 ml = WaitLL4(p, rec + 128 * G + 4 * g, tag);  // {m, l_hi, l_lo, -}
+  const uint64_t* recs = p.llrec + static_cast<size_t>(h) * S * kRec;
+  float* wv = reinterpret_cast<float*>(merge);                                             // [se][G]
+  double* lv = reinterpret_cast<double*>(merge + Al(static_cast<size_t>(se * G) * 4, 8));  // [se][G]
+  float* inv = reinterpret_cast<float*>(lv + se * G);                                      // [G]
+  for (int i = tid; i < se * G; i += kNT) {
+    const int sp = i / G, g = i - sp * G;
+    const float4 ml = WaitLL4(p, recs + static_cast<size_t>(sp) * kRec + 128 * G + 4 * g, tag);  // {m, l_hi, l_lo, -}
     wv[i] = ml.x;
     lv[i] = static_cast<double>(ml.y) + ml.z;
   }
   __syncthreads();
-  for (int i = tid; i < p.n_kv * G; i += kNT) {
-    const int h = i / G, g = i - h * G;
+  if (tid < G) {
+    const int g = tid;
     float M = -INFINITY;
-    for (int sp = 0; sp < se; ++sp) M = fmaxf(M, wv[(h * se + sp) * G + g]);
+    for (int sp = 0; sp < se; ++sp) M = fmaxf(M, wv[sp * G + g]);
     double L = 0.0;
     for (int sp = 0; sp < se; ++sp) {
-      const int k = (h * se + sp) * G + g;
+      const int k = sp * G + g;
       const float w = wv[k] == -INFINITY ? 0.f : expf(wv[k] - M);
       wv[k] = w;
       L += static_cast<double>(w) * lv[k];
     }
-    inv[i] = static_cast<float>(1.0 / L);
+    inv[g] = static_cast<float>(1.0 / L);
   }
   __syncthreads();
-  for (int e = tid; e < p.n_heads * 32; e += kNT) {
-    const int qh = e >> 5, d4 = e & 31, h = qh / G, g = qh - h * G;
-    const uint64_t* base = p.llrec + static_cast<size_t>(h) * S * kRec + g * kD + 4 * d4;
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    constexpr int kB = 2;
+  for (int i = tid; i < G * kD; i += kNT) {
+    const int g = i / kD, d = i - g * kD;
+    const uint64_t* base = recs + g * kD + d;
+    float o = 0.f;
+    constexpr int kB = 8;
     for (int s0 = 0; s0 < se; s0 += kB) {
-      uint64_t w[kB][4];
+      uint64_t w[kB];
 #pragma unroll
-      for (int i = 0; i < kB; ++i) {
-        if (s0 + i < se) {
-          const uint64_t* a = base + static_cast<size_t>(s0 + i) * kRec;
-          LdLL2(a, w[i][0], w[i][1]);
-          LdLL2(a + 2, w[i][2], w[i][3]);
-        }
-      }
+      for (int j = 0; j < kB; ++j) w[j] = s0 + j < se ? LdLL(base + static_cast<size_t>(s0 + j) * kRec) : 0ull;
 #pragma unroll
-      for (int i = 0; i < kB; ++i) {
-        if (s0 + i < se) {
-          float4 v;
-          if (TagOk(w[i][0], tag) && TagOk(w[i][1], tag) && TagOk(w[i][2], tag) && TagOk(w[i][3], tag)) {
-            v = make_float4(ValOf(w[i][0]), ValOf(w[i][1]), ValOf(w[i][2]), ValOf(w[i][3]));
-          } else {
-            v = WaitLL4(p, base + static_cast<size_t>(s0 + i) * kRec, tag);
-          }
-          const float wt = wv[(h * se + s0 + i) * G + g];
-          o.x = fmaf(wt, v.x, o.x);
-          o.y = fmaf(wt, v.y, o.y);
-          o.z = fmaf(wt, v.z, o.z);
-          o.w = fmaf(wt, v.w, o.w);
+      for (int j = 0; j < kB; ++j) {
+        if (s0 + j < se) {
+          const float v = TagOk(w[j], tag) ? ValOf(w[j]) : WaitLL1(p, base + static_cast<size_t>(s0 + j) * kRec, tag);
+          o = fmaf(wv[(s0 + j) * G + g], v, o);
         }
       }
     }
-    const float iv = inv[h * G + g];
-    *reinterpret_cast<float4*>(xs + qh * kD + 4 * d4) = make_float4(o.x * iv, o.y * iv, o.z * iv, o.w * iv);
+    StLL(p.llattn + static_cast<size_t>(h * G + g) * kD + d, o * inv[g], tag);
   }
 }
 
@@ -722,15 +706,13 @@ __device__ void MvPhase(const LoopParams& p, const GeoTable& gt, int kind, int l
     if (kind == kQkv && layer == 0) {
       for (int c = tid; c < p.hidden; c += kNT) xs[c] = dev::DeqElem(p.embd, tok, c);
       __syncthreads();
-    } else if (kind == kO) {
-      MergeAttention<G>(p, step, layer, pos, xs, scratch + pl.merge);
-      __syncthreads();
     } else {
-      ll = kind == kDown ? p.llh : p.llx;
+      ll = kind == kDown ? p.llh : (kind == kO ? p.llattn : p.llx);
       tag = kind == kQkv ? TagOf(p, step, layer - 1, kDown)
-                         : (kind == kGu ? TagOf(p, step, layer, kO)
-                                        : (kind == kDown ? TagOf(p, step, layer, kGu)
-                                                         : TagOf(p, step, p.n_layers - 1, kDown)));
+                         : (kind == kO ? TagOf(p, step, layer, kAttn)
+                                       : (kind == kGu ? TagOf(p, step, layer, kO)
+                                                      : (kind == kDown ? TagOf(p, step, layer, kGu)
+                                                                       : TagOf(p, step, p.n_layers - 1, kDown))));
     }
     double ssq = 0.0;
     for (int b = warp; b < nb; b += kNW) {
@@ -897,11 +879,12 @@ struct __align__(16) AttnShared {
   double sq[2 * (G + 1)];     // sums of squares, two warps per vector
   double dsh[kNW * G];
   float fsh[kNW * G];
+  int last;  // this block merges the head's records
 };
 
 template <int G>
 __device__ void AttnPhase(const LoopParams& p, const GeoTable& gt, int layer, int step, int64_t pos0, int64_t pos,
-                          Ring& rg_io, const Smem& sm, PhaseClock& clk, AttnShared<G>& as) {
+                          uint32_t tick_last, Ring& rg_io, const Smem& sm, PhaseClock& clk, AttnShared<G>& as) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const AttnGeo a = AttnOf(p, pos);
   if (a.c1 <= a.c0) return;  // no positions for this block at this step
@@ -1099,6 +1082,11 @@ __device__ void AttnPhase(const LoopParams& p, const GeoTable& gt, int layer, in
     for (int w = 0; w < kNW; ++w) t += vred[(w * G + g) * kD + dd2];
     StLL(rec + g * kD + dd2, t, tag_out);
   }
+  // the last block of this head to get here merges the head's records
+  __syncthreads();
+  if (tid == 0) as.last = atomicAdd(p.tickets + h, 1u) == tick_last ? 1 : 0;
+  __syncthreads();
+  if (as.last) MergeHead<G>(p, step, layer, pos, h, sm.scratch() + sm.plan().merge);
 }
 
 // ------------------------------------------------------------------ the kernel
@@ -1162,6 +1150,7 @@ __global__ void __launch_bounds__(kNT, 1) DecodeLoopKernel(const LoopParams p) {
   const uint32_t n_phase = 5u * static_cast<uint32_t>(p.n_layers) + 2u;
   int steps = 0;
   bool alive = true;
+  uint32_t tick_base = 0;  // tickets taken per KV head before the current attention phase
   for (int step = 0; step < p.n_steps && alive; ++step) {
     const int64_t pos = pos0 + step;
     const uint32_t id0 = static_cast<uint32_t>(step) * n_phase;
@@ -1182,7 +1171,9 @@ __global__ void __launch_bounds__(kNT, 1) DecodeLoopKernel(const LoopParams p) {
       MvPhase<G>(p, gt, kQkv, l, step, pos0, pos, tok, rg, sm, clk, s_xown, s_sq, s_bv, s_bi, &s_cnt, s_sel);
       TraceEnd(p, clk, id0 + 5u * l + 0u);
       __syncthreads();
-      AttnPhase<G>(p, gt, l, step, pos0, pos, rg, sm, clk, as);
+      const uint32_t se = static_cast<uint32_t>(EffSplits(p, pos));
+      AttnPhase<G>(p, gt, l, step, pos0, pos, tick_base + se - 1u, rg, sm, clk, as);
+      tick_base += se;  // every active block of each head took one ticket
       TraceEnd(p, clk, id0 + 5u * l + 1u);
       __syncthreads();
       MvPhase<G>(p, gt, kO, l, step, pos0, pos, tok, rg, sm, clk, s_xown, s_sq, s_bv, s_bi, &s_cnt, s_sel);
@@ -1331,7 +1322,8 @@ void LaunchDecodeLoop(const LoopParams& in, int group, int num_sms, cudaStream_t
   const int qd = p.n_heads * kD;
   RPGB_CHECK((p.hidden / kTile + num_sms - 1) / num_sms * kTile <= kMaxOwnRows,
              "decode loop: a block would own more than %d rows of x", kMaxOwnRows);
-  RPGB_CHECK(p.llx != nullptr && p.llqkv != nullptr && p.llh != nullptr && p.llrec != nullptr,
+  RPGB_CHECK(p.llx != nullptr && p.llqkv != nullptr && p.llh != nullptr && p.llrec != nullptr &&
+                 p.llattn != nullptr && p.tickets != nullptr,
              "decode loop: tagged buffers missing");
   RPGB_CHECK(p.n_layers >= 1 && p.n_layers <= kMaxLayers, "decode loop: %d layers (at most %d)", p.n_layers,
              kMaxLayers);
@@ -1362,6 +1354,7 @@ void LaunchDecodeLoop(const LoopParams& in, int group, int num_sms, cudaStream_t
   RPGB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kNT, total));
   RPGB_CHECK(per_sm >= 1, "decode loop: a block does not fit on an SM (%zu bytes of shared memory)", total);
   RPGB_CUDA(cudaMemsetAsync(p.bar, 0, sizeof(unsigned), s));
+  RPGB_CUDA(cudaMemsetAsync(p.tickets, 0, sizeof(uint32_t) * p.n_kv, s));
   void* args[] = {&p};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(num_sms);

@@ -214,6 +214,8 @@ struct LoopParams {
   // (see k_step.cu): x [hidden], q|k|v [q_dim + 2 kv_dim], SiLU(g)*u [ffn],
   // attention split records [n_kv][splits][LoopRecordWords(group)].
   uint64_t *llx = nullptr, *llqkv = nullptr, *llh = nullptr, *llrec = nullptr;
+  uint64_t* llattn = nullptr;     // merged attention output [q_dim]
+  uint32_t* tickets = nullptr;    // [n_kv]: blocks of each head done with the attention phase
   uint32_t epoch0 = 1;  // tags of this launch start above it; strictly increasing across launches
   float *logits = nullptr, *probs = nullptr;
   int64_t* pos = nullptr;
