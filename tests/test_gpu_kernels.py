@@ -88,3 +88,21 @@ def test_matvec_vs_reference_gpu(qtype, n_tok):
     err = np.abs(out.cpu().numpy() - ref).max() / np.abs(ref).max()
     assert err < 2e-5, err
     m.close()
+
+
+@pytest.mark.parametrize("qtype", [GGML_Q4_K, GGML_Q6_K])
+@pytest.mark.parametrize("rows,cols", [(2048, 2048), (2048, 6144)])
+def test_tcgemm_many_token_tiles(oracle, qtype, rows, cols):
+    """600 tokens: the tcgen05 GEMM over four full 128-token tiles and a ragged fifth."""
+    n_tok = 600
+    b = make_matrix(qtype, rows, cols, 23)
+    x = synthetic.normal(29, n_tok * cols, 0.0, 1.0).reshape(n_tok, cols)
+    m = Matrix(qtype, rows, cols, b)
+    xd = torch.from_numpy(x).cuda()
+    out = torch.empty((n_tok, rows), dtype=torch.float32, device="cuda")
+    m.matvec(xd.data_ptr(), n_tok, out.data_ptr())
+    torch.cuda.synchronize()
+    ref = oracle.matvec(qtype, b, rows, cols, x)
+    err = np.abs(out.cpu().numpy() - ref).max() / np.abs(ref).max()
+    assert err < 5e-5, err  # same bound as the other tensor-core cases
+    m.close()
