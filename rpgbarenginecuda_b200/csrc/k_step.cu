@@ -405,11 +405,6 @@ __device__ __forceinline__ unsigned AtomAddRelease(unsigned* a, unsigned v) {
   asm volatile("atom.add.release.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(a), "r"(v) : "memory");
   return old;
 }
-__device__ __forceinline__ unsigned LdAcquire(const unsigned* a) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
-  return v;
-}
 __device__ __forceinline__ unsigned LdRelaxed(const unsigned* a) {
   unsigned v;
   asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
@@ -600,7 +595,6 @@ struct Smem {
     return MakePlan(p->ring, p->nb_max, p->x_max, p->scratch_bytes, p->max_tiles);
   }
   __device__ __forceinline__ uint8_t* scratch() const { return base + plan().scratch; }
-  __device__ __forceinline__ float* red() const { return reinterpret_cast<float*>(base + plan().red); }
 };
 
 __device__ __forceinline__ void Ld8(const float* src, bool shared, float (&v)[8]) {

@@ -149,12 +149,15 @@ def test_vs_reference_engine(pair):
 
 
 @pytest.mark.parametrize("splits", ["1", "2", "3"])
-def test_decode_attention_multi_stage(tiny_model, monkeypatch, splits):
-    """Decode attention with several 128-position stages per block (and split-K
-    merges across blocks) against the oracle at a context of ~430 positions."""
+@pytest.mark.parametrize("which", ["tiny", "tiny_g4"])
+def test_decode_attention_multi_stage(tiny_model, tiny_g4_model, monkeypatch, splits, which):
+    """Decode attention with many chunks per block (and split merges across
+    blocks) against the oracle at a context of ~430 positions, for 2 and 4 q
+    heads per KV head."""
     monkeypatch.setenv("RPGB_ATTN_SPLITS", splits)
-    m = Model(tiny_model, 0, 512)
-    om = OracleModel(tiny_model, 512)
+    path = tiny_model if which == "tiny" else tiny_g4_model
+    m = Model(path, 0, 512)
+    om = OracleModel(path, 512)
     toks = synthetic.seeded_tokens(420, 3, m.vocab)
     s, os_ = Session(m, 512), OracleSession(om, 512)
     s.prefill(toks)
@@ -168,3 +171,64 @@ def test_decode_attention_multi_stage(tiny_model, monkeypatch, splits):
     s.close()
     m.close()
     om.close()
+
+
+@pytest.mark.parametrize("opts", [(1.0, 0, 0.95), (0.7, 100, 0.9), (1.3, 1, 1.0)])
+def test_sampled_general_paths(pair, opts):
+    """Sampling options the candidate fast path does not take (top_k off, above
+    64, or 1 = off with plain temperature): the decode loop's general sampler,
+    one launch for all steps, against the oracle."""
+    m, om = pair
+    s, os_ = Session(m, 512), OracleSession(om, 512)
+    prompt = synthetic.seeded_tokens(33, 7, m.vocab)
+    s.prefill(prompt, want_logits=False)
+    os_.prefill(prompt)
+    ids = s.generate(SampleOptions(*opts), 99, 16)
+    rids, _ = os_.generate(*opts, 99, 16, step_logits=True)
+    n = 0
+    while n < min(len(ids), len(rids)) and ids[n] == rids[n]:
+        n += 1
+    # a sampled token may only part where u is within float noise of a boundary
+    assert n >= min(8, len(rids)), (opts, list(ids), list(rids))
+    s.close()
+    os_.close()
+
+
+def test_many_stop_ids(pair):
+    """More stop ids than the device-side list holds: the host checks them and
+    the session length and continuation still follow the reference loop."""
+    m, _ = pair
+    s = Session(m, 512)
+    toks = synthetic.seeded_tokens(21, 0, m.vocab)
+    s.prefill(toks)
+    free = s.generate(SampleOptions(0.7, 20, 0.8), 77, 12)
+    stop_at = int(free[6])
+    first = next(i for i, t in enumerate(free) if t == stop_at)
+    stops = [stop_at] + [int(v) for v in synthetic.seeded_tokens(24, 9, m.vocab) if int(v) not in set(free.tolist())][:20]
+    assert len(stops) > 16
+    s.set_len(0)
+    s.prefill(toks)
+    ids = s.generate(SampleOptions(0.7, 20, 0.8), 77, 12, stop=stops)
+    assert list(ids) == list(free[: first + 1])
+    assert len(s) == 21 + first + 1
+    s.close()
+
+
+def test_multi_launch_path(pair, monkeypatch):
+    """The per-step graph path (kept for group sizes the decode loop kernel is
+    not built for), forced on a supported model: greedy tokens and step logits
+    against the oracle."""
+    monkeypatch.setenv("RPGB_DECODE_GRAPH", "1")
+    m, om = pair
+    toks = synthetic.seeded_tokens(21, 0, m.vocab)
+    s, os_ = Session(m, 512), OracleSession(om, 512)
+    s.prefill(toks)
+    os_.prefill(toks)
+    ids, steps = s.generate(SampleOptions(0.0, 0, 1.0), 0, 16, step_logits=True)
+    rids, rsteps = os_.generate(0.0, 0, 1.0, 0, 16, step_logits=True)
+    ok, at = tokens_agree(ids, rids, rsteps)
+    assert ok, (at, ids, rids)
+    for i in range(at):
+        assert full_scale_err(steps[i], rsteps[i]) <= FULL_SCALE
+    s.close()
+    os_.close()
