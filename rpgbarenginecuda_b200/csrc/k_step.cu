@@ -1227,7 +1227,8 @@ __global__ void __launch_bounds__(kNT, 1) DecodeLoopKernel(const LoopParams p) {
     } else {
       if (p.mode == 1) {
         next = smp::SmallSample<kNT>(p.cand_val, p.cand_idx, p.cand_cnt, static_cast<int>(gridDim.x), p.temperature,
-                                     p.top_k, p.top_p, p.seed, pos + 1, sm.scratch(), kSmallCap);
+                                     p.top_k, p.top_p, p.seed, pos + 1, sm.scratch(), kSmallCap,
+                                     [&](int k) { TraceMark(p, clk, k); });
       }
       if (next < 0) {  // the same decision in every block
         if (blockIdx.x == 0) {

@@ -410,11 +410,16 @@ __device__ int GeneralSample(const float* logits, int n, float temperature, int 
 // n_slices slices (cand_cnt[s] candidates at cand_val/cand_idx + 64 s).
 // Returns the token in every thread, or -1 when a slice overflowed or more
 // than `cap` candidates lie above the lower bound (the caller then runs
-// GeneralSample).  scratch: 16 * cap bytes of shared memory.
-template <int NT>
+// GeneralSample).  scratch: 16 * cap bytes of shared memory.  mark(k) is
+// called by every thread after stage k (1: bound and compaction, 2: k-th
+// value, 3: softmax, 4: top_p), for timelines.
+struct NoMark {
+  __device__ void operator()(int) const {}
+};
+template <int NT, class Mark = NoMark>
 __device__ int SmallSample(const float* cand_val, const int32_t* cand_idx, const int32_t* cand_cnt, int n_slices,
                            float temperature, int top_k, float top_p, uint64_t seed, int64_t counter,
-                           unsigned char* scratch, int cap) {
+                           unsigned char* scratch, int cap, Mark mark = Mark()) {
   float* cv = reinterpret_cast<float*>(scratch);  // [cap]
   int* ci = reinterpret_cast<int*>(cv + cap);     // [cap]
   float* kv = reinterpret_cast<float*>(ci + cap);  // kept values / probs [cap]
@@ -487,7 +492,9 @@ __device__ int SmallSample(const float* cand_val, const int32_t* cand_idx, const
   __syncthreads();
   const int m = s_m;
   if (m > cap) return -1;  // too many near-threshold candidates for the scratch
+  mark(1);
   const float kth = dev::FromOrderKey(RadixKth(cv, m, top_k, hist, s_sel));
+  mark(2);
   // survivors, ordered by vocabulary index
   if (tid == 0) s_c = 0;
   __syncthreads();
@@ -535,6 +542,7 @@ __device__ int SmallSample(const float* cand_val, const int32_t* cand_idx, const
     for (int i = tid; i < c; i += NT) v[i] *= inv;
   }
   __syncthreads();
+  mark(3);
   if (top_p > 0.0f && top_p < 1.0f) {
     // ascending (key, index) order of the survivors' probabilities
     for (int i = tid; i < c; i += NT) {
@@ -585,6 +593,7 @@ __device__ int SmallSample(const float* cand_val, const int32_t* cand_idx, const
     }
     __syncthreads();
   }
+  mark(4);
   if (tid == 0) {
     int tok;
     if (s_forced) {
