@@ -58,6 +58,31 @@ RPGB_API int32_t rpgb_model_shape(int32_t model, int32_t* out, int32_t n_out);
 /* Device bytes of the resident weights (GpuModel::device_bytes). */
 RPGB_API int64_t rpgb_model_device_bytes(int32_t model);
 
+/* ------------------------------------------------------------------ tensor parallel */
+
+/* Tensor parallelism over NCCL, one process (or thread) and one GPU per rank.
+ * No counterpart in the reference, which runs one GPU; the split is the one
+ * planned for the 8B configuration: each rank holds 1/size of the query and
+ * KV heads and of the FFN, the embedding and norms in full, 1/size of the
+ * lm_head rows; the ranks sum a partial after attn_output and after ffn_down
+ * and gather the logits, then all sample the same token.
+ *
+ * rpgb_tp_shard_plan: shape = {n_heads, n_kv_heads, head_dim, ffn, vocab};
+ * out[0..4] = this rank's heads, KV heads, ffn columns, first vocabulary row
+ * and vocabulary rows.  Fails when the model does not split evenly (KV heads
+ * by size, attn_output and ffn_down columns into 256-column super-blocks,
+ * vocabulary rows into 16-row tiles).  Host only.
+ * rpgb_tp_unique_id: 128 bytes (ncclGetUniqueId) that rank 0 makes and every
+ * rank passes to rpgb_tp_group_create (collective).  A model loaded with
+ * rpgb_model_load_tp holds its rank's shard; prefill and generate on its
+ * sessions are collective: every rank calls them with the same arguments, in
+ * the same order. */
+RPGB_API int32_t rpgb_tp_shard_plan(const int32_t* shape, int32_t rank, int32_t size, int32_t* out);
+RPGB_API int32_t rpgb_tp_unique_id(uint8_t* id_out);
+RPGB_API int32_t rpgb_tp_group_create(const uint8_t* id, int32_t rank, int32_t size, int32_t device);
+RPGB_API void rpgb_tp_group_free(int32_t group);
+RPGB_API int32_t rpgb_model_load_tp(const char* gguf_path, int32_t device, int32_t max_pos, int32_t group);
+
 /* ------------------------------------------------------------------ session */
 
 /* A session owns an fp16 KV cache of max_seq positions, scratch buffers, a

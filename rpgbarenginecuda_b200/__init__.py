@@ -17,8 +17,8 @@ import numpy as np
 
 from ._lib import EngineError, SampleOptions, check, load_engine  # noqa: F401
 
-__all__ = ["Model", "Session", "Matrix", "SampleOptions", "EngineError", "sample", "counter_uniform", "launch_count",
-           "library_path", "GGML_Q4_K", "GGML_Q6_K"]
+__all__ = ["Model", "Session", "Matrix", "SampleOptions", "EngineError", "TpGroup", "shard_plan", "sample",
+           "counter_uniform", "launch_count", "library_path", "GGML_Q4_K", "GGML_Q6_K"]
 
 GGML_Q4_K = 12
 GGML_Q6_K = 14
@@ -29,13 +29,75 @@ def library_path() -> str:
     return ENGINE_SO
 
 
-class Model:
-    """Weights of one GGUF resident on one device."""
+def shard_plan(shape: dict, rank: int, size: int) -> dict:
+    """This rank's share of a model split over `size` GPUs (rpgb_tp_shard_plan).
 
-    def __init__(self, path: str, device: int = 0, max_pos: int = 4096):
+    `shape` holds n_heads, n_kv_heads, head_dim, ffn and vocab; raises
+    EngineError when the model does not split evenly."""
+    lib = load_engine()
+    src = (ctypes.c_int32 * 5)(shape["n_heads"], shape["n_kv_heads"], shape["head_dim"], shape["ffn"],
+                               shape["vocab"])
+    out = (ctypes.c_int32 * 5)()
+    check(lib.rpgb_tp_shard_plan(src, rank, size, out), "tp_shard_plan")
+    return dict(zip(["heads", "kv_heads", "ffn", "vocab0", "vocab_rows"], list(out)))
+
+
+class TpGroup:
+    """A tensor-parallel group: one rank per GPU, joined over NCCL.
+
+    Every rank constructs it with the same `unique_id` (made once by rank 0
+    with ``TpGroup.unique_id()`` and sent to the others, e.g. with
+    ``torch.distributed.broadcast_object_list``); construction is collective.
+    ``from_process_group`` does that exchange over an initialised
+    torch.distributed group."""
+
+    def __init__(self, unique_id: bytes, rank: int, size: int, device: int):
+        self._lib = load_engine()
+        if len(unique_id) != 128:
+            raise ValueError("a group id is 128 bytes")
+        buf = (ctypes.c_uint8 * 128).from_buffer_copy(unique_id)
+        self.rank, self.size, self.device = rank, size, device
+        self.handle = check(self._lib.rpgb_tp_group_create(buf, rank, size, device), "tp_group_create")
+
+    @staticmethod
+    def unique_id() -> bytes:
+        lib = load_engine()
+        buf = (ctypes.c_uint8 * 128)()
+        check(lib.rpgb_tp_unique_id(buf), "tp_unique_id")
+        return bytes(buf)
+
+    @staticmethod
+    def exchange_id(rank: int, group=None) -> bytes:
+        """Rank 0's fresh id, delivered to every rank of a torch.distributed group."""
+        import torch.distributed as dist
+        obj = [TpGroup.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0, group=group)
+        return obj[0]
+
+    @classmethod
+    def from_process_group(cls, device: int, group=None) -> "TpGroup":
+        import torch.distributed as dist
+        rank, size = dist.get_rank(group), dist.get_world_size(group)
+        return cls(cls.exchange_id(rank, group), rank, size, device)
+
+    def close(self):
+        if self.handle is not None and self.handle >= 0:
+            self._lib.rpgb_tp_group_free(self.handle)
+            self.handle = None
+
+
+class Model:
+    """Weights of one GGUF resident on one device (this rank's shard with `tp`)."""
+
+    def __init__(self, path: str, device: int = 0, max_pos: int = 4096, tp: TpGroup | None = None):
         self._lib = load_engine()
         self.path = path
-        self.handle = check(self._lib.rpgb_model_load(path.encode(), device, max_pos), "model_load")
+        self.tp = tp
+        if tp is None:
+            self.handle = check(self._lib.rpgb_model_load(path.encode(), device, max_pos), "model_load")
+        else:
+            self.handle = check(self._lib.rpgb_model_load_tp(path.encode(), device, max_pos, tp.handle),
+                                "model_load_tp")
         out = (ctypes.c_int32 * 12)()
         check(self._lib.rpgb_model_shape(self.handle, out, 12), "model_shape")
         keys = ["n_layers", "hidden", "n_heads", "n_kv_heads", "head_dim", "ffn", "vocab", "context_length",

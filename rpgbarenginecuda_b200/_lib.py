@@ -35,6 +35,11 @@ _SIGS = {
     "rpgb_last_error": (ctypes.c_char_p, []),
     "rpgb_model_load": (c_i32, [ctypes.c_char_p, c_i32, c_i32]),
     "rpgb_model_free": (None, [c_i32]),
+    "rpgb_tp_shard_plan": (c_i32, [c_p, c_i32, c_i32, c_p]),
+    "rpgb_tp_unique_id": (c_i32, [c_p]),
+    "rpgb_tp_group_create": (c_i32, [c_p, c_i32, c_i32, c_i32]),
+    "rpgb_tp_group_free": (None, [c_i32]),
+    "rpgb_model_load_tp": (c_i32, [ctypes.c_char_p, c_i32, c_i32, c_i32]),
     "rpgb_model_shape": (c_i32, [c_i32, c_p, c_i32]),
     "rpgb_model_device_bytes": (c_i64, [c_i32]),
     "rpgb_session_create": (c_i32, [c_i32, c_i64]),

@@ -19,6 +19,7 @@
 #include "kernels.h"
 #include "gguf.h"
 #include "model.h"
+#include "tp.h"
 
 namespace rpgb {
 namespace {
@@ -40,6 +41,7 @@ std::mutex g_mu;
 std::map<int32_t, std::shared_ptr<Model>> g_models;
 std::map<int32_t, std::shared_ptr<Session>> g_sessions;
 std::map<int32_t, std::shared_ptr<MatrixEntry>> g_mats;
+std::map<int32_t, std::shared_ptr<TpGroup>> g_groups;
 std::map<int32_t, int32_t> g_session_model;
 int32_t g_next = 1;
 
@@ -107,6 +109,78 @@ int32_t rpgb_model_load(const char* path, int32_t device, int32_t max_pos) {
   RPGB_CATCH(-1)
 }
 
+int32_t rpgb_tp_shard_plan(const int32_t* shape, int32_t rank, int32_t size, int32_t* out) {
+  try {
+    SetLastError("");
+    RPGB_CHECK(shape != nullptr && out != nullptr, "tp_shard_plan: null argument");
+    const ShardPlan p = MakeShardPlan(shape[0], shape[1], shape[2], shape[3], shape[4], rank, size);
+    out[0] = p.heads;
+    out[1] = p.kv_heads;
+    out[2] = p.ffn;
+    out[3] = p.vocab0;
+    out[4] = p.vocab_rows;
+    return 0;
+  }
+  RPGB_CATCH(-1)
+}
+
+int32_t rpgb_tp_unique_id(uint8_t* id_out) {
+  try {
+    SetLastError("");
+    RPGB_CHECK(id_out != nullptr, "tp_unique_id: null buffer");
+    TpUniqueId(id_out);
+    return 0;
+  }
+  RPGB_CATCH(-1)
+}
+
+int32_t rpgb_tp_group_create(const uint8_t* id, int32_t rank, int32_t size, int32_t device) {
+  try {
+    SetLastError("");
+    std::shared_ptr<TpGroup> grp = TpGroup::Create(id, rank, size, device);
+    std::lock_guard<std::mutex> lk(g_mu);
+    const int32_t h = g_next++;
+    g_groups[h] = grp;
+    return h;
+  }
+  RPGB_CATCH(-1)
+}
+
+void rpgb_tp_group_free(int32_t group) {
+  try {
+    std::shared_ptr<TpGroup> grp;
+    {
+      std::lock_guard<std::mutex> lk(g_mu);
+      auto it = g_groups.find(group);
+      if (it == g_groups.end()) return;
+      grp = it->second;
+      g_groups.erase(it);
+    }
+    // models on the group hold it until they are freed
+  } catch (...) {
+  }
+}
+
+int32_t rpgb_model_load_tp(const char* path, int32_t device, int32_t max_pos, int32_t group) {
+  try {
+    SetLastError("");
+    RPGB_CHECK(path != nullptr && *path != '\0', "model path is empty");
+    std::shared_ptr<TpGroup> grp;
+    {
+      std::lock_guard<std::mutex> lk(g_mu);
+      auto it = g_groups.find(group);
+      RPGB_CHECK(it != g_groups.end(), "invalid tensor-parallel group handle %d", group);
+      grp = it->second;
+    }
+    std::shared_ptr<Model> m(Model::Load(path, device, max_pos > 0 ? max_pos : 4096, grp).release());
+    std::lock_guard<std::mutex> lk(g_mu);
+    const int32_t h = g_next++;
+    g_models[h] = m;
+    return h;
+  }
+  RPGB_CATCH(-1)
+}
+
 void rpgb_model_free(int32_t model) {
   try {
     std::lock_guard<std::mutex> lk(g_mu);
@@ -127,7 +201,7 @@ int32_t rpgb_model_shape(int32_t model, int32_t* out, int32_t n_out) {
   try {
     SetLastError("");
     auto m = GetModel(model);
-    const ModelMeta& c = m->meta();
+    const ModelMeta& c = m->global_meta();
     const int32_t v[12] = {c.n_layers, c.hidden, c.n_heads, c.n_kv_heads, c.head_dim, c.ffn,
                            c.vocab, c.context_length, m->rope_positions(), c.eos_id, m->device(), m->num_sms()};
     for (int i = 0; i < n_out && i < 12; ++i) out[i] = v[i];

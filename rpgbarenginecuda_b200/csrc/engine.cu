@@ -87,6 +87,7 @@ Session::Session(const Model* m, int64_t max_seq) : m_(m), max_seq_(max_seq) {
   const int qkv = c.q_dim() + 2 * c.kv_dim();
   Carver cv;
   cv.Add(sizeof(float) * c.hidden);   // x
+  cv.Add(sizeof(float) * c.hidden);   // y
   cv.Add(sizeof(float) * qkv);        // qkv
   cv.Add(sizeof(float) * c.q_dim());  // attn
   cv.Add(sizeof(float) * c.ffn);      // h
@@ -113,6 +114,7 @@ Session::Session(const Model* m, int64_t max_seq) : m_(m), max_seq_(max_seq) {
   RPGB_CUDA(cudaMemsetAsync(dec_arena_, 0, cv.total(), stream_));
   cv.Begin(dec_arena_);
   x_ = cv.Take<float>(c.hidden);
+  y_ = cv.Take<float>(c.hidden);
   qkv_ = cv.Take<float>(qkv);
   attn_ = cv.Take<float>(c.q_dim());
   h_ = cv.Take<float>(c.ffn);
@@ -211,6 +213,7 @@ void Session::EnsurePrefill(int64_t n) {
   cv.Add(sizeof(float) * cap * c.q_dim());
   cv.Add(sizeof(float) * cap * c.q_dim());
   cv.Add(sizeof(float) * cap * c.ffn);
+  cv.Add(sizeof(float) * (m_->tp() != nullptr ? cap * c.hidden : 0));
   cv.Add(sizeof(int32_t) * cap);
   // fp16 operands of the tensor-core GEMM: the largest layer matrix and the widest activations
   const int64_t kmax = std::max<int64_t>(c.hidden, std::max<int64_t>(c.q_dim(), c.ffn));
@@ -229,6 +232,7 @@ void Session::EnsurePrefill(int64_t n) {
   pf_q_ = cv.Take<float>(cap * c.q_dim());
   pf_attn_ = cv.Take<float>(cap * c.q_dim());
   pf_h_ = cv.Take<float>(cap * c.ffn);
+  pf_y_ = m_->tp() != nullptr ? cv.Take<float>(cap * c.hidden) : nullptr;
   pf_tok_ = cv.Take<int32_t>(cap);
   pf_tc_ = cv.Take<__half>(tc_halves);
   pf_tc_halves_ = tc_halves;
@@ -306,11 +310,17 @@ void Session::Prefill(const int32_t* tokens, int64_t n, float* last_logits) {
     o.X = pf_attn_;
     o.n_tok = nt;
     o.ldx = qd;
-    o.out = pf_x_;
     o.ldo = H;
-    o.resid = pf_x_;
-    o.ldr = H;
-    LaunchGemm(o, Epi::kResid, s);
+    if (m_->tp() != nullptr) {
+      o.out = pf_y_;
+      LaunchGemm(o, Epi::kStore, s);
+      ReduceIntoResidual(pf_x_, pf_y_, n, s);
+    } else {
+      o.out = pf_x_;
+      o.resid = pf_x_;
+      o.ldr = H;
+      LaunchGemm(o, Epi::kResid, s);
+    }
     LaunchRmsNormRows(pf_x_, L.ffn_norm, nt, H, c.rms_eps, pf_xn_, s);
     GemmParams gu;
     gu.tc_scratch = pf_tc_;
@@ -331,23 +341,30 @@ void Session::Prefill(const int32_t* tokens, int64_t n, float* last_logits) {
     dn.X = pf_h_;
     dn.n_tok = nt;
     dn.ldx = c.ffn;
-    dn.out = pf_x_;
     dn.ldo = H;
-    dn.resid = pf_x_;
-    dn.ldr = H;
-    LaunchGemm(dn, Epi::kResid, s);
+    if (m_->tp() != nullptr) {
+      dn.out = pf_y_;
+      LaunchGemm(dn, Epi::kStore, s);
+      ReduceIntoResidual(pf_x_, pf_y_, n, s);
+    } else {
+      dn.out = pf_x_;
+      dn.resid = pf_x_;
+      dn.ldr = H;
+      LaunchGemm(dn, Epi::kResid, s);
+    }
   }
   // final norm + lm_head on the last position only (the reference computes all
   // rows and keeps the last one, src/qwen3_gpu.cu:163-170)
   MvParams mv;
   mv.seg[0].w = m_->lm_head();
   mv.n_seg = 1;
-  mv.total_rows = c.vocab;
+  mv.total_rows = m_->lm_head().rows;  // the vocabulary, or this rank's rows of it
   mv.x = pf_x_ + static_cast<int64_t>(n - 1) * H;
   mv.norm_w = m_->out_norm();
   mv.eps = c.rms_eps;
-  mv.out = logits_;
+  mv.out = logits_ + m_->shard().vocab0;
   LaunchMatvec(mv, Epi::kStore, 4, m_->num_sms(), s);
+  if (m_->tp() != nullptr) GatherLogits(s);
   if (last_logits != nullptr) {
     RPGB_CUDA(cudaMemcpyAsync(last_logits, logits_, sizeof(float) * c.vocab, cudaMemcpyDeviceToHost, s));
   }
@@ -361,6 +378,16 @@ void Session::Prefill(const int32_t* tokens, int64_t n, float* last_logits) {
   }
   len_ = pos0 + n;
   logits_valid_ = true;
+}
+
+void Session::ReduceIntoResidual(float* x, float* y, int64_t n, cudaStream_t s) {
+  const int64_t count = n * m_->meta().hidden;
+  m_->tp()->AllReduceSum(y, static_cast<size_t>(count), s);
+  LaunchAddInPlace(x, y, count, s);
+}
+
+void Session::GatherLogits(cudaStream_t s) {
+  m_->tp()->AllGatherInPlace(logits_, static_cast<size_t>(m_->shard().vocab_rows), s);
 }
 
 void Session::EnqueueSample(const SampleOpts& opt, uint64_t seed, int pos_bump, bool pdl, int32_t trace_id) {
@@ -389,6 +416,7 @@ void Session::EnqueueStep(const SampleOpts& opt, uint64_t seed) {
   const cudaStream_t s = stream_;
   const int H = c.hidden, qd = c.q_dim(), kvd = c.kv_dim();
   const int sms = m_->num_sms();
+  const bool tp = m_->tp() != nullptr;
   int launches = 0;
   int32_t tid = 0;  // trace id of the next launch
   LaunchEmbed(m_->embd(), tok_, 1, x_, pos_, out_ids_, s, false, NextTrace(&tid));
@@ -441,11 +469,18 @@ void Session::EnqueueStep(const SampleOpts& opt, uint64_t seed) {
     o.seg[0].w = L.o;
     o.total_rows = H;
     o.x = attn_;
-    o.out = x_;
-    o.resid = x_;
     o.err = err_;
     o.trace = NextTrace(&tid);
-    LaunchMatvec(o, Epi::kResid, 1, sms, s, true);
+    if (tp) {
+      o.out = y_;
+      LaunchMatvec(o, Epi::kStore, 1, sms, s, true);
+      ReduceIntoResidual(x_, y_, 1, s);
+      ++launches;
+    } else {
+      o.out = x_;
+      o.resid = x_;
+      LaunchMatvec(o, Epi::kResid, 1, sms, s, true);
+    }
 
     MvParams gu;
     gu.seg[0].w = L.gateup;
@@ -462,23 +497,37 @@ void Session::EnqueueStep(const SampleOpts& opt, uint64_t seed) {
     dn.seg[0].w = L.down;
     dn.total_rows = H;
     dn.x = h_;
-    dn.out = x_;
-    dn.resid = x_;
     dn.err = err_;
     dn.trace = NextTrace(&tid);
-    LaunchMatvec(dn, Epi::kResid, 1, sms, s, true);
+    if (tp) {
+      dn.out = y_;
+      LaunchMatvec(dn, Epi::kStore, 1, sms, s, true);
+      ReduceIntoResidual(x_, y_, 1, s);
+      ++launches;
+    } else {
+      dn.out = x_;
+      dn.resid = x_;
+      LaunchMatvec(dn, Epi::kResid, 1, sms, s, true);
+    }
     launches += 5;
   }
   MvParams lm;
   lm.seg[0].w = m_->lm_head();
-  lm.total_rows = c.vocab;
+  lm.total_rows = m_->lm_head().rows;
   lm.x = x_;
   lm.norm_w = m_->out_norm();
   lm.eps = c.rms_eps;
-  lm.out = logits_;
+  lm.out = logits_ + m_->shard().vocab0;
   lm.err = err_;
   lm.trace = NextTrace(&tid);
-  if (!(opt.temperature > 0.0f)) {
+  if (tp) {
+    // every rank samples the same gathered logits and so draws the same token
+    LaunchMatvec(lm, Epi::kStore, 4, sms, s, true);
+    GatherLogits(s);
+    EnqueueSample(opt, seed, 1, false, trace_rec_ != nullptr ? tid : -1);
+    const bool fast = opt.temperature > 0.0f && opt.top_k > 1 && opt.top_k <= kFastTopK && opt.top_k < c.vocab;
+    launches += fast ? 4 : 2;
+  } else if (!(opt.temperature > 0.0f)) {
     lm.part_val = am_val_;
     lm.part_idx = am_idx_;
     lm.ticket = tickets_ + c.n_kv_heads;
@@ -515,7 +564,9 @@ int Session::Generate(const SampleOpts& opt, uint64_t seed, int32_t max_tokens, 
   }
   EnqueueSample(opt, seed, 0);
 
-  if (LoopSupportsGroup(c.group()) && std::getenv("RPGB_DECODE_GRAPH") == nullptr) {
+  // The decode loop kernel is one GPU's; a tensor-parallel step runs as the
+  // step graph with the group's collectives between its launches.
+  if (LoopSupportsGroup(c.group()) && m_->tp() == nullptr && std::getenv("RPGB_DECODE_GRAPH") == nullptr) {
     return GenerateLoop(opt, seed, max_tokens, stop, n_stop, out, step_logits, start);
   }
 

@@ -69,6 +69,11 @@ class Session {
 
  private:
   void EnqueueStep(const SampleOpts& opt, uint64_t seed);
+  // Tensor parallel: out = W x (this rank's columns) into y, summed over the
+  // group, then added to the residual x (n rows of hidden).
+  void ReduceIntoResidual(float* x, float* y, int64_t n, cudaStream_t s);
+  // Tensor parallel: gathers every rank's vocabulary rows of the logits.
+  void GatherLogits(cudaStream_t s);
   int GenerateLoop(const SampleOpts& opt, uint64_t seed, int32_t max_tokens, const int32_t* stop, int32_t n_stop,
                    int32_t* out, float* step_logits, int64_t start);
   LoopParams MakeLoopParams(const SampleOpts& opt, uint64_t seed) const;
@@ -90,6 +95,7 @@ class Session {
   // decode state (device)
   uint8_t* dec_arena_ = nullptr;
   float *x_ = nullptr, *qkv_ = nullptr, *attn_ = nullptr, *h_ = nullptr, *logits_ = nullptr, *probs_ = nullptr;
+  float* y_ = nullptr;  // tensor parallel: this rank's partial of attn_output / ffn_down, then the sum
   int64_t* pos_ = nullptr;
   int32_t* tok_ = nullptr;
   int32_t* out_ids_ = nullptr;  // [max_seq]: token forwarded at each position
@@ -119,7 +125,7 @@ class Session {
   int64_t pf_cap_ = 0;
   uint8_t* pf_arena_ = nullptr;
   float *pf_x_ = nullptr, *pf_xn_ = nullptr, *pf_qkv_ = nullptr, *pf_q_ = nullptr, *pf_attn_ = nullptr,
-        *pf_h_ = nullptr;
+        *pf_h_ = nullptr, *pf_y_ = nullptr;
   int32_t* pf_tok_ = nullptr;
   __half* pf_tc_ = nullptr;  // fp16 operands of the tensor-core GEMM
   size_t pf_tc_halves_ = 0;

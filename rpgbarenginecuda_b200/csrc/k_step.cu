@@ -916,7 +916,7 @@ __device__ void AttnPhase(const LoopParams& p, const GeoTable& gt, int layer, in
       FenceProxyAsyncGlobal();
     }
   }
-  TraceMarkW0(p, clk, 1);  // q / k / v words arrived
+  //M1
   __syncthreads();
   if (vi <= G) {
     const double tot = as.sq[2 * vi] + as.sq[2 * vi + 1];
@@ -940,7 +940,7 @@ __device__ void AttnPhase(const LoopParams& p, const GeoTable& gt, int layer, in
     }
   }
   __syncthreads();
-  TraceMark(p, clk, 2);  // q / k normalised and rotated
+  //M2
 
   // ---- this warp's 4-position units.  Scores: 8 lanes per position (lane
   // sub holds dimensions 8 sub .. +7 and 64 + 8 sub .. +7, position pp = lane / 8);
@@ -959,7 +959,7 @@ __device__ void AttnPhase(const LoopParams& p, const GeoTable& gt, int layer, in
     const int n_valid = static_cast<int>(pos + 1 - r0 < kChunk ? pos + 1 - r0 : kChunk);
     const int n_old = static_cast<int>(pos - r0 < kChunk ? pos - r0 : kChunk);
     const uint8_t* slot = RingWait(rg, p);
-    if (ch == a.c0) TraceMarkW0(p, clk, 3);  // warp 0: first unit in shared memory
+    if (ch == a.c0) TraceMarkW0(p, clk, 1);
     float dd[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) dd[g] = 0.f;
@@ -1025,14 +1025,16 @@ __device__ void AttnPhase(const LoopParams& p, const GeoTable& gt, int layer, in
         }
       }
     }
+    if (ch == a.c0) TraceMarkW0(p, clk, 2);
     RingRelease(rg, p, gt, pos0, warp);
+    if (ch == a.c0) TraceMarkW0(p, clk, 3);
   }
+  TraceMarkW0(p, clk, 4);  // warp 0: its units done
   rg_io = rg;
 
   // ---- fold the warps into this block's record
   float* vred = reinterpret_cast<float*>(sm.scratch());  // [kNW][G][128]
   __syncthreads();
-  TraceMark(p, clk, 4);  // units done
   if (lane == 0) {
 #pragma unroll
     for (int g = 0; g < G; ++g) {
@@ -1161,28 +1163,23 @@ __global__ void __launch_bounds__(kNT, 1) DecodeLoopKernel(const LoopParams p) {
     }
     // Phases of a layer meet through tagged words, not barriers; a block only
     // synchronises its own threads between phases (shared memory is reused).
-    for (int l = 0; l < p.n_layers; ++l) {
-      MvPhase<G>(p, gt, kQkv, l, step, pos0, pos, tok, rg, sm, clk, s_xown, s_sq, s_bv, s_bi, &s_cnt, s_sel);
-      TraceEnd(p, clk, id0 + 5u * l + 0u);
-      __syncthreads();
-      const uint32_t se = static_cast<uint32_t>(EffSplits(p, pos));
-      AttnPhase<G>(p, gt, l, step, pos0, pos, tick_base + se - 1u, rg, sm, clk, as);
-      tick_base += se;  // every active block of each head took one ticket
-      TraceEnd(p, clk, id0 + 5u * l + 1u);
-      __syncthreads();
-      MvPhase<G>(p, gt, kO, l, step, pos0, pos, tok, rg, sm, clk, s_xown, s_sq, s_bv, s_bi, &s_cnt, s_sel);
-      TraceEnd(p, clk, id0 + 5u * l + 2u);
-      __syncthreads();
-      MvPhase<G>(p, gt, kGu, l, step, pos0, pos, tok, rg, sm, clk, s_xown, s_sq, s_bv, s_bi, &s_cnt, s_sel);
-      TraceEnd(p, clk, id0 + 5u * l + 3u);
-      __syncthreads();
-      MvPhase<G>(p, gt, kDown, l, step, pos0, pos, tok, rg, sm, clk, s_xown, s_sq, s_bv, s_bi, &s_cnt, s_sel);
-      TraceEnd(p, clk, id0 + 5u * l + 4u);
-      __syncthreads();
+    // One call site per phase kind keeps a single copy of the matvec code,
+    // which stays in the instruction cache from phase to phase.
+#pragma unroll 1
+    for (uint32_t q = 0; q + 1u < n_phase; ++q) {
+      const int l = static_cast<int>(q / 5u), ph = static_cast<int>(q - 5u * static_cast<uint32_t>(l));
+      if (l < p.n_layers && ph == 1) {
+        const uint32_t se = static_cast<uint32_t>(EffSplits(p, pos));
+        AttnPhase<G>(p, gt, l, step, pos0, pos, tick_base + se - 1u, rg, sm, clk, as);
+        tick_base += se;  // every active block of each head took one ticket
+      } else {
+        const int kind = l == p.n_layers ? kLm : (ph == 0 ? kQkv : (ph == 2 ? kO : (ph == 3 ? kGu : kDown)));
+        MvPhase<G>(p, gt, kind, l < p.n_layers ? l : p.n_layers - 1, step, pos0, pos, tok, rg, sm, clk, s_xown,
+                   s_sq, s_bv, s_bi, &s_cnt, s_sel);
+      }
+      TraceEnd(p, clk, id0 + q);
+      if (q + 2u < n_phase) __syncthreads();
     }
-    MvPhase<G>(p, gt, kLm, p.n_layers - 1, step, pos0, pos, tok, rg, sm, clk, s_xown, s_sq, s_bv, s_bi, &s_cnt,
-               s_sel);
-    TraceEnd(p, clk, id0 + n_phase - 2u);
     if (!(alive = GridBarrier(p, &s_flag))) break;
     TraceReady(p, clk);
 

@@ -235,13 +235,24 @@ Model::~Model() {
   }
 }
 
-std::unique_ptr<Model> Model::Load(const std::string& path, int device, int32_t max_pos) {
+std::unique_ptr<Model> Model::Load(const std::string& path, int device, int32_t max_pos,
+                                   std::shared_ptr<TpGroup> tp) {
   std::unique_ptr<Model> m(new Model());
   m->gguf_ = std::make_unique<GgufFile>();
   m->gguf_->Open(path);
   const GgufFile& g = *m->gguf_;
-  m->meta_ = ReadModelMeta(g);
-  const ModelMeta& c = m->meta_;
+  m->gmeta_ = ReadModelMeta(g);
+  const ModelMeta& c = m->gmeta_;
+  const int tp_rank = tp ? tp->rank() : 0, tp_size = tp ? tp->size() : 1;
+  RPGB_CHECK(!tp || tp->device() == device, "tensor parallel: the group is on device %d, the model on %d",
+             tp ? tp->device() : -1, device);
+  m->shard_ = MakeShardPlan(c.n_heads, c.n_kv_heads, c.head_dim, c.ffn, c.vocab, tp_rank, tp_size);
+  const ShardPlan& sp = m->shard_;
+  m->tp_ = tp;  // a group of one still takes the tensor-parallel path (tests run it on one GPU)
+  m->meta_ = c;
+  m->meta_.n_heads = sp.heads;
+  m->meta_.n_kv_heads = sp.kv_heads;
+  m->meta_.ffn = sp.ffn;
   m->device_ = device;
 
   int n_dev = 0;
@@ -278,10 +289,22 @@ std::unique_ptr<Model> Model::Load(const std::string& path, int device, int32_t 
   };
 
   // ---- plan the arena
+  // A matrix to repack: source rows [row0, row0 + rows) of a (and of b) and
+  // 256-column super-blocks [blk0, blk0 + nb) of each row.
   struct MatJob {
     const GgufTensor* a;
     const GgufTensor* b;  // interleaved partner (gate/up) or null
     DevMat* dst;
+    int64_t row0 = 0, rows = -1, blk0 = 0, nb = -1;
+  };
+  auto job = [](const GgufTensor* a, const GgufTensor* b, DevMat* dst, int64_t row0, int64_t rows, int64_t blk0,
+                int64_t nb) {
+    MatJob j{a, b, dst};
+    j.row0 = row0;
+    j.rows = rows;
+    j.blk0 = blk0;
+    j.nb = nb;
+    return j;
   };
   struct NormJob {
     const GgufTensor* t;
@@ -291,14 +314,15 @@ std::unique_ptr<Model> Model::Load(const std::string& path, int device, int32_t 
   std::vector<NormJob> norms;
   m->layers_.resize(static_cast<size_t>(c.n_layers));
 
+  const int64_t hb = c.hidden / 256;  // super-blocks of a hidden-wide row
   const GgufTensor& emb = require("token_embd.weight");
   check_mat(emb, c.vocab, c.hidden);
-  mats.push_back({&emb, nullptr, &m->embd_});
+  mats.push_back(job(&emb, nullptr, &m->embd_, 0, c.vocab, 0, hb));
   const GgufTensor* out_w = g.Find("output.weight");
   if (out_w == nullptr) out_w = g.Find("lm_head.weight");
   if (out_w != nullptr) {
     check_mat(*out_w, c.vocab, c.hidden);
-    mats.push_back({out_w, nullptr, &m->lm_head_});
+    mats.push_back(job(out_w, nullptr, &m->lm_head_, sp.vocab0, sp.vocab_rows, 0, hb));
   }
   const GgufTensor& on = require("output_norm.weight");
   check_norm(on, c.hidden);
@@ -334,20 +358,25 @@ std::unique_ptr<Model> Model::Load(const std::string& path, int device, int32_t 
     check_mat(dn, c.hidden, c.ffn);
     RPGB_CHECK(ga.type == up.type, "layer %d: ffn_gate (%s) and ffn_up (%s) must share a type", l,
                GgmlTypeName(ga.type), GgmlTypeName(up.type));
-    mats.push_back({&q, nullptr, &L.q});
-    mats.push_back({&k, nullptr, &L.k});
-    mats.push_back({&v, nullptr, &L.v});
-    mats.push_back({&o, nullptr, &L.o});
-    mats.push_back({&ga, &up, &L.gateup});
-    mats.push_back({&dn, nullptr, &L.down});
+    const int64_t lq = static_cast<int64_t>(sp.heads) * c.head_dim, lkv = static_cast<int64_t>(sp.kv_heads) * c.head_dim;
+    mats.push_back(job(&q, nullptr, &L.q, sp.rank * lq, lq, 0, hb));
+    mats.push_back(job(&k, nullptr, &L.k, sp.rank * lkv, lkv, 0, hb));
+    mats.push_back(job(&v, nullptr, &L.v, sp.rank * lkv, lkv, 0, hb));
+    mats.push_back(job(&o, nullptr, &L.o, 0, c.hidden, sp.rank * lq / 256, lq / 256));
+    mats.push_back(job(&ga, &up, &L.gateup, static_cast<int64_t>(sp.rank) * sp.ffn, sp.ffn, 0, hb));
+    mats.push_back(job(&dn, nullptr, &L.down, 0, c.hidden, static_cast<int64_t>(sp.rank) * sp.ffn / 256,
+                       sp.ffn / 256));
   }
 
   size_t total = 0;
   for (const MatJob& j : mats) {
-    const int64_t rows = j.a->rows() * (j.b ? 2 : 1);
+    const int64_t rows = j.rows * (j.b ? 2 : 1);
     RPGB_CHECK(rows % kTileRows == 0, "tensor %s: %lld rows are not a multiple of %d", j.a->name.c_str(),
                static_cast<long long>(rows), kTileRows);
-    total += AlignUp(DevMatBytes(j.a->type, rows, j.a->cols()));
+    RPGB_CHECK(j.row0 >= 0 && j.row0 + j.rows <= j.a->rows() && j.blk0 >= 0 && j.nb > 0 &&
+                   (j.blk0 + j.nb) * 256 <= j.a->cols(),
+               "tensor %s: shard out of range", j.a->name.c_str());
+    total += AlignUp(DevMatBytes(j.a->type, rows, j.nb * 256));
   }
   for (const NormJob& n : norms) total += AlignUp(static_cast<size_t>(n.t->n_elements) * 4);
   m->rope_pos_ = std::max<int32_t>(1, std::min<int32_t>(max_pos, c.context_length));
@@ -380,9 +409,8 @@ std::unique_ptr<Model> Model::Load(const std::string& path, int device, int32_t 
 
   for (const MatJob& j : mats) {
     const uint32_t type = j.a->type;
-    const int64_t cols = j.a->cols();
-    const int64_t src_rows = j.a->rows();
-    const int64_t rows = src_rows * (j.b ? 2 : 1);
+    const int64_t cols = j.nb * 256;
+    const int64_t rows = j.rows * (j.b ? 2 : 1);
     DevMat dm;
     dm.type = type;
     dm.rows = static_cast<int32_t>(rows);
@@ -392,7 +420,8 @@ std::unique_ptr<Model> Model::Load(const std::string& path, int device, int32_t 
     dm.q = dq;
     *j.dst = dm;
 
-    const int64_t row_src_bytes = GgmlRowBytes(type, cols);
+    const int64_t row_src_bytes = GgmlRowBytes(type, j.a->cols());
+    const int64_t col_off = GgmlRowBytes(type, 256) * j.blk0;  // first super-block of the shard
     const size_t tile_bytes = static_cast<size_t>(dm.nb) * GroupBytes(type);
     const int64_t tiles = rows / kTileRows;
     const int64_t tiles_per_chunk = std::max<int64_t>(1, static_cast<int64_t>(up.cap() / tile_bytes));
@@ -410,7 +439,7 @@ std::unique_ptr<Model> Model::Load(const std::string& path, int device, int32_t 
               src_t = (dst_row & 1) ? j.b : j.a;
               src_row = dst_row >> 1;
             }
-            ptrs[r] = g.TensorData(*src_t) + src_row * row_src_bytes;
+            ptrs[r] = g.TensorData(*src_t) + (j.row0 + src_row) * row_src_bytes + col_off;
           }
           RepackTile(type, ptrs, dm.nb, sq + ti * tile_bytes);
         }
@@ -419,7 +448,11 @@ std::unique_ptr<Model> Model::Load(const std::string& path, int device, int32_t 
       up.Wait();
     }
   }
-  if (out_w == nullptr) m->lm_head_ = m->embd_;
+  if (out_w == nullptr) {  // tied: this rank's vocabulary rows of the embedding (whole tiles)
+    m->lm_head_ = m->embd_;
+    m->lm_head_.rows = sp.vocab_rows;
+    m->lm_head_.q = m->embd_.q + static_cast<int64_t>(sp.vocab0 / kTileRows) * m->embd_.nb * GroupBytes(m->embd_.type);
+  }
 
   std::vector<float> tmp;
   for (const NormJob& n : norms) {

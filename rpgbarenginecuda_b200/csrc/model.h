@@ -21,6 +21,7 @@
 #include <cuda_runtime.h>
 
 #include "gguf.h"
+#include "tp.h"
 
 namespace rpgb {
 
@@ -70,10 +71,22 @@ size_t DevMatBytes(uint32_t type, int64_t rows, int64_t cols);
 class Model {
  public:
   // Loads weights onto `device`, builds the RoPE table for min(max_pos, context).
-  static std::unique_ptr<Model> Load(const std::string& path, int device, int32_t max_pos);
+  // With a tensor-parallel group (size > 1) only this rank's shard is loaded:
+  // its heads' q / k / v rows and attn_output columns, its FFN rows (gate, up)
+  // and columns (down), its vocabulary rows of lm_head; embedding and norms in
+  // full (ShardPlan in tp.h).
+  static std::unique_ptr<Model> Load(const std::string& path, int device, int32_t max_pos,
+                                     std::shared_ptr<TpGroup> tp = nullptr);
   ~Model();
 
+  // The shapes this device computes with: heads, KV heads and ffn are the
+  // shard's (the whole model without a group); hidden, vocab and the rest are
+  // the model's.
   const ModelMeta& meta() const { return meta_; }
+  // The model's own shapes (what the GGUF holds).
+  const ModelMeta& global_meta() const { return gmeta_; }
+  const TpGroup* tp() const { return tp_.get(); }
+  const ShardPlan& shard() const { return shard_; }
   const GgufFile& gguf() const { return *gguf_; }
   int device() const { return device_; }
   int num_sms() const { return num_sms_; }
@@ -89,7 +102,9 @@ class Model {
  private:
   Model() = default;
   std::unique_ptr<GgufFile> gguf_;
-  ModelMeta meta_;
+  ModelMeta meta_, gmeta_;
+  std::shared_ptr<TpGroup> tp_;
+  ShardPlan shard_;
   int device_ = 0;
   int num_sms_ = 0;
   uint8_t* arena_ = nullptr;

@@ -1,0 +1,61 @@
+"""One rank of the tensor-parallel GPU test (tests/test_gpu_tp.py).
+
+Joins a gloo group on 127.0.0.1 to pass rank 0's NCCL id, loads its shard of
+the model on GPU `rank`, runs the same calls as the one-GPU reference run of
+the test (prefill with logits, 32 greedy steps with per-step logits, a
+sampled append-and-decode round) and, on rank 0, saves what it got.
+"""
+
+import argparse
+import datetime
+import os
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+
+from rpgbarenginecuda_b200 import Model, SampleOptions, Session, TpGroup, synthetic  # noqa: E402
+
+
+def run(m, max_seq=512):
+    """The calls both the tensor-parallel ranks and the one-GPU reference make."""
+    s = Session(m, max_seq)
+    toks = synthetic.seeded_tokens(21, 0, m.vocab)
+    out = {"prefill": s.prefill(toks)}
+    ids, steps = s.generate(SampleOptions(0.0, 0, 1.0), 0, 32, step_logits=True)
+    out["greedy"], out["greedy_steps"] = np.asarray(ids), np.asarray(steps)
+    s.prefill(synthetic.seeded_tokens(40, 1, m.vocab), want_logits=False)
+    sids, ssteps = s.generate(SampleOptions(0.7, 20, 0.8), 1234, 24, step_logits=True)
+    out["sampled"], out["sampled_steps"] = np.asarray(sids), np.asarray(ssteps)
+    out["len"] = np.asarray(len(s))
+    s.close()
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--model", required=True)
+    ap.add_argument("--rank", type=int, required=True)
+    ap.add_argument("--size", type=int, required=True)
+    ap.add_argument("--port", type=int, required=True)
+    ap.add_argument("--out", required=True)
+    a = ap.parse_args()
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{a.port}", rank=a.rank, world_size=a.size,
+                            timeout=datetime.timedelta(seconds=120))
+    g = TpGroup.from_process_group(device=a.rank)
+    m = Model(a.model, a.rank, 1024, tp=g)
+    out = run(m)
+    m.close()
+    g.close()
+    if a.rank == 0:
+        np.savez(a.out, **out)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
