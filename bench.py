@@ -70,6 +70,9 @@ def parse():
     ap.add_argument("--decode-loop-ctx", type=int, default=0,
                     help="prefill this many tokens, then two generate calls (2 and 4 decode steps) and exit "
                          "(the second decode-loop launch is the one profiled for profiles/)")
+    ap.add_argument("--tp", action="store_true",
+                    help="tensor-parallel measurement of the 8B configuration: run under torchrun with N ranks "
+                         "(N = 1: the whole model on one GPU); 1024-token prefill + 128 greedy steps per turn")
     ap.add_argument("--with-ref-gpu", action="store_true",
                     help="also time the reference's own CUDA engine (built from its sources) on the same turn")
     return ap.parse_args()
@@ -508,6 +511,102 @@ def ours(args):
     return 0
 
 
+TP_MODEL, TP_PROMPT, TP_DECODE = "qwen3-8b", 1024, 128
+
+
+def tp_bench(args):
+    """The 8B configuration split over the torchrun ranks (one GPU each).
+
+    One turn = a TP_PROMPT-token prefill and TP_DECODE greedy steps on every
+    rank in lockstep (the ranks exchange partial sums after attn_output and
+    ffn_down and gather the logits).  Decode and prefill are timed with CUDA
+    events on each rank's session stream; the reported times are the max over
+    ranks.  With one rank the whole model runs on one GPU (decode loop kernel).
+    """
+    import datetime
+
+    import torch
+
+    from rpgbarenginecuda_b200 import Model, SampleOptions, Session, TpGroup, synthetic
+
+    world, rank, local = dist()
+    torch.cuda.set_device(local)
+    tdist = None
+    if world > 1:
+        import torch.distributed as tdist
+
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                 device_id=torch.device(f"cuda:{local}"))
+    name = TP_MODEL if args.model == MODEL else args.model
+    if rank == 0:
+        synthetic.cached_model(name, seed=0)  # one rank writes the file
+    if tdist is not None:
+        tdist.barrier()
+    path = synthetic.cached_model(name, seed=0)
+    group = TpGroup.from_process_group(device=local) if world > 1 else None
+    model = Model(path, device=local, max_pos=4096, tp=group)
+    sess = Session(model, 4096)
+    if group is not None:
+        sess.attach_tp()  # greedy decode in the one-launch loop, partials exchanged over NVLink
+    stream = torch.cuda.ExternalStream(sess.stream_ptr, device=local)
+    prompt = synthetic.seeded_tokens(TP_PROMPT, 1000, model.vocab)
+    greedy = SampleOptions(0.0, 0, 1.0)
+
+    def turn():
+        sess.set_len(0)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        ev[0].record(stream)
+        sess.prefill(prompt, want_logits=False)
+        ev[1].record(stream)
+        ids = sess.generate(greedy, 0, TP_DECODE)
+        ev[2].record(stream)
+        torch.cuda.synchronize()
+        return ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2]), len(ids)
+
+    for _ in range(args.warmup):
+        turn()
+    pre_ms = dec_ms = 0.0
+    n_dec = 0
+    with Clocks(local) as clk:
+        for _ in range(args.steps):
+            a, b, n = turn()
+            pre_ms, dec_ms, n_dec = pre_ms + a, dec_ms + b, n_dec + n
+    if tdist is not None:
+        t = torch.tensor([pre_ms, dec_ms], device=f"cuda:{local}", dtype=torch.float64)
+        tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
+        pre_ms, dec_ms = float(t[0]), float(t[1])
+    shape = synthetic.PRESETS[name]
+    w_tok, kv_pos = shape.weight_bytes_per_token(), shape.kv_bytes_per_position()
+    # algorithmic bytes of one turn's decode steps, summed over ranks (weights split, K/V rows split by head)
+    dec_bytes = sum(w_tok + kv_pos * (TP_PROMPT + i + 1) for i in range(TP_DECODE)) * args.steps
+    hbm_peak, hbm_kind = peaks()
+    per_rank_gbs = dec_bytes / world / (dec_ms * 1e-3) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": f"batch-1 greedy decode tok/s ({name} Q4_K_M, tensor parallel over {world} GPU(s))",
+            "value": round(n_dec / (dec_ms * 1e-3), 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round((pre_ms + dec_ms) / args.steps, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,0.02) weights quantised to Q4_K/Q6_K, seeded token ids)",
+            "prefill_tok_s": round(TP_PROMPT * args.steps / (pre_ms * 1e-3), 1),
+            "config": {"workload": f"{name}: {TP_PROMPT}-token prefill + {TP_DECODE} greedy steps per turn",
+                       "model": name, "global_batch": 1, "seq_len": TP_PROMPT + TP_DECODE,
+                       "parallelism": (f"tp{world}: decode loop kernel per GPU, partials over NVLink"
+                                       if world > 1 else "one GPU (decode loop kernel)")},
+            "roofline": {"bound": "hbm", "achieved": round(per_rank_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(per_rank_gbs / hbm_peak, 4), "traffic": None, "peak_kind": hbm_kind,
+                         "note": "per rank: algorithmic decode bytes / ranks / decode time"},
+            "clocks": clk.summary()}), flush=True)
+    sess.close()
+    model.close()
+    if group is not None:
+        group.close()
+    if tdist is not None:
+        tdist.barrier()
+        tdist.destroy_process_group()
+    return 0
+
+
 def reference_gpu_turn(path, prompt, appends):
     """The reference's own CUDA engine (compiled from its sources) on one turn."""
     from oracle.oracle import RefShim
@@ -541,6 +640,8 @@ def main():
     if args.decode_loop_ctx > 0:
         decode_loop_ctx(args)
         return
+    if args.tp:
+        return tp_bench(args)
     if args.impl == "reference":
         return reference_arm(args)
     return ours(args)

@@ -82,6 +82,14 @@ RPGB_API int32_t rpgb_tp_unique_id(uint8_t* id_out);
 RPGB_API int32_t rpgb_tp_group_create(const uint8_t* id, int32_t rank, int32_t size, int32_t device);
 RPGB_API void rpgb_tp_group_free(int32_t group);
 RPGB_API int32_t rpgb_model_load_tp(const char* gguf_path, int32_t device, int32_t max_pos, int32_t group);
+/* Greedy decode of a tensor-parallel session runs in the one-launch decode
+ * loop with the ranks' partials exchanged directly between the GPUs' memory:
+ * each rank's session exports a 64-byte CUDA IPC handle
+ * (rpgb_session_tp_handle) and attaches the handles of all ranks, in rank
+ * order (rpgb_session_tp_attach, collective).  Sessions not attached, and
+ * sampled decode, go through the step graph with NCCL. */
+RPGB_API int32_t rpgb_session_tp_handle(int32_t session, uint8_t* handle_out);
+RPGB_API int32_t rpgb_session_tp_attach(int32_t session, const uint8_t* handles);
 
 /* ------------------------------------------------------------------ session */
 

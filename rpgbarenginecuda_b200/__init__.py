@@ -130,6 +130,25 @@ class Session:
         self.max_seq = max_seq
         self.handle = check(self._lib.rpgb_session_create(model.handle, max_seq), "session_create")
 
+    def attach_tp(self, group=None):
+        """Joins the ranks' sessions for greedy decode in the one-launch loop
+        (rpgb_session_tp_attach).  Collective over the model's tensor-parallel
+        group: the 64-byte exchange-buffer handles go round over
+        torch.distributed (`group`), except for a group of one."""
+        tp = self.model.tp
+        if tp is None:
+            raise ValueError("the session's model is not tensor parallel")
+        own = (ctypes.c_uint8 * 64)()
+        check(self._lib.rpgb_session_tp_handle(self.handle, own), "session_tp_handle")
+        if tp.size == 1:
+            handles = [bytes(own)]
+        else:
+            import torch.distributed as dist
+            handles = [None] * tp.size
+            dist.all_gather_object(handles, bytes(own), group=group)
+        buf = (ctypes.c_uint8 * (64 * tp.size)).from_buffer_copy(b"".join(handles))
+        check(self._lib.rpgb_session_tp_attach(self.handle, buf), "session_tp_attach")
+
     def __len__(self) -> int:
         return int(self._lib.rpgb_session_len(self.handle))
 

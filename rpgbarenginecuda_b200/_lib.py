@@ -40,6 +40,8 @@ _SIGS = {
     "rpgb_tp_group_create": (c_i32, [c_p, c_i32, c_i32, c_i32]),
     "rpgb_tp_group_free": (None, [c_i32]),
     "rpgb_model_load_tp": (c_i32, [ctypes.c_char_p, c_i32, c_i32, c_i32]),
+    "rpgb_session_tp_handle": (c_i32, [c_i32, c_p]),
+    "rpgb_session_tp_attach": (c_i32, [c_i32, c_p]),
     "rpgb_model_shape": (c_i32, [c_i32, c_p, c_i32]),
     "rpgb_model_device_bytes": (c_i64, [c_i32]),
     "rpgb_session_create": (c_i32, [c_i32, c_i64]),

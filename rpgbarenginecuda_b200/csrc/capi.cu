@@ -181,6 +181,26 @@ int32_t rpgb_model_load_tp(const char* path, int32_t device, int32_t max_pos, in
   RPGB_CATCH(-1)
 }
 
+int32_t rpgb_session_tp_handle(int32_t session, uint8_t* handle_out) {
+  try {
+    SetLastError("");
+    RPGB_CHECK(handle_out != nullptr, "session_tp_handle: null buffer");
+    GetSession(session)->TpHandle(handle_out);
+    return 0;
+  }
+  RPGB_CATCH(-1)
+}
+
+int32_t rpgb_session_tp_attach(int32_t session, const uint8_t* handles) {
+  try {
+    SetLastError("");
+    RPGB_CHECK(handles != nullptr, "session_tp_attach: null handles");
+    GetSession(session)->TpAttach(handles);
+    return 0;
+  }
+  RPGB_CATCH(-1)
+}
+
 void rpgb_model_free(int32_t model) {
   try {
     std::lock_guard<std::mutex> lk(g_mu);

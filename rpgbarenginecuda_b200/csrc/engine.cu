@@ -138,13 +138,59 @@ Session::Session(const Model* m, int64_t max_seq) : m_(m), max_seq_(max_seq) {
   ll_ = cv.Take<uint64_t>(ll_words_);  // zeroed with the arena: tag 0 is never a valid tag
   tickets_loop_ = cv.Take<uint32_t>(c.n_kv_heads);
   RPGB_CUDA(cudaMallocHost(&loop_host_, sizeof(int32_t)));
+  if (m->tp() != nullptr) {  // its own allocation: the CUDA IPC handle covers exactly this buffer
+    xbuf_words_ = LoopExchangeWords(c.hidden, m->num_sms());
+    RPGB_CUDA(cudaMalloc(&xbuf_, sizeof(uint64_t) * xbuf_words_));
+    RPGB_CUDA(cudaMemsetAsync(xbuf_, 0, sizeof(uint64_t) * xbuf_words_, stream_));
+  }
   RPGB_CUDA(cudaStreamSynchronize(stream_));
+}
+
+void Session::TpHandle(uint8_t* out) const {
+  RPGB_CHECK(xbuf_ != nullptr, "the session's model is not tensor parallel");
+  cudaIpcMemHandle_t h;
+  RPGB_CUDA(cudaSetDevice(m_->device()));
+  RPGB_CUDA(cudaIpcGetMemHandle(&h, xbuf_));
+  std::memcpy(out, &h, sizeof(h));
+}
+
+void Session::TpAttach(const uint8_t* handles) {
+  RPGB_CHECK(xbuf_ != nullptr, "the session's model is not tensor parallel");
+  RPGB_CHECK(!tp_attached_, "the session is attached already");
+  const TpGroup& g = *m_->tp();
+  RPGB_CHECK(g.size() <= kLoopMaxTp, "tensor parallel decode loop: at most %d ranks", kLoopMaxTp);
+  RPGB_CUDA(cudaSetDevice(m_->device()));
+  for (int k = 0; k < g.size(); ++k) {
+    if (k == g.rank()) {
+      xpeer_[k] = xbuf_;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handles + static_cast<size_t>(k) * sizeof(h), sizeof(h));
+    void* p = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      for (int j = 0; j < k; ++j) {
+        if (j != g.rank() && xpeer_[j] != nullptr) cudaIpcCloseMemHandle(xpeer_[j]);
+        xpeer_[j] = nullptr;
+      }
+      Throw("tensor parallel: opening rank %d's exchange buffer failed: %s", k, cudaGetErrorString(e));
+    }
+    xpeer_[k] = static_cast<uint64_t*>(p);
+  }
+  tp_attached_ = true;
 }
 
 Session::~Session() {
   cudaSetDevice(m_->device());
   if (stream_ != nullptr) cudaStreamSynchronize(stream_);
   DropGraph();
+  if (m_->tp() != nullptr) {
+    for (int k = 0; k < kLoopMaxTp; ++k) {
+      if (xpeer_[k] != nullptr && xpeer_[k] != xbuf_) cudaIpcCloseMemHandle(xpeer_[k]);
+    }
+  }
+  cudaFree(xbuf_);
   cudaFree(kc_);
   cudaFree(vc_);
   cudaFree(dec_arena_);
@@ -564,9 +610,11 @@ int Session::Generate(const SampleOpts& opt, uint64_t seed, int32_t max_tokens, 
   }
   EnqueueSample(opt, seed, 0);
 
-  // The decode loop kernel is one GPU's; a tensor-parallel step runs as the
-  // step graph with the group's collectives between its launches.
-  if (LoopSupportsGroup(c.group()) && m_->tp() == nullptr && std::getenv("RPGB_DECODE_GRAPH") == nullptr) {
+  // Tensor parallel greedy decode runs in the loop kernel with the ranks'
+  // partials exchanged over NVLink (after TpAttach); otherwise a
+  // tensor-parallel step runs as the step graph with NCCL between launches.
+  const bool loop_tp = m_->tp() == nullptr || (tp_attached_ && !(opt.temperature > 0.0f) && step_logits == nullptr);
+  if (LoopSupportsGroup(c.group()) && loop_tp && std::getenv("RPGB_DECODE_GRAPH") == nullptr) {
     return GenerateLoop(opt, seed, max_tokens, stop, n_stop, out, step_logits, start);
   }
 
@@ -706,6 +754,12 @@ LoopParams Session::MakeLoopParams(const SampleOpts& opt, uint64_t seed) const {
   lp.bar = bar_;
   lp.err = err_;
   lp.splits = loop_splits_;
+  lp.vocab0 = m_->shard().vocab0;
+  if (m_->tp() != nullptr && tp_attached_) {
+    lp.tp = m_->tp()->size();
+    lp.tp_rank = m_->tp()->rank();
+    for (int k = 0; k < lp.tp; ++k) lp.xpeer[k] = xpeer_[k];
+  }
   if (trace_rec_ != nullptr) {
     int khz = 0;
     RPGB_CUDA(cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, m_->device()));
@@ -748,11 +802,18 @@ int Session::GenerateLoop(const SampleOpts& opt, uint64_t seed, int32_t max_toke
     const uint32_t need = LoopTagsPerLaunch(c.n_layers, todo);
     if (epoch_ > 0xFFFFFFFFu - need) {  // tags would wrap: clear every tag and start over
       RPGB_CUDA(cudaMemsetAsync(ll_, 0, sizeof(uint64_t) * ll_words_, s));
+      if (lp.tp > 0) {
+        // every rank wraps at the same launch; no rank may store into a peer's
+        // buffer before that peer cleared it, so the group meets after the clear
+        RPGB_CUDA(cudaMemsetAsync(xbuf_, 0, sizeof(uint64_t) * xbuf_words_, s));
+        m_->tp()->AllReduceSum(y_, 1, s);
+      }
       epoch_ = 1;
     }
     lp.epoch0 = epoch_;
     epoch_ += need;
     LaunchDecodeLoop(lp, c.group(), m_->num_sms(), s);
+    if (lp.tp > 0) GatherLogits(s);  // the next call samples its first token from the whole row
     loop_ready_ = true;
     if (step_logits != nullptr && produced + 1 < max_tokens) {
       RPGB_CUDA(cudaMemcpyAsync(step_logits + static_cast<int64_t>(produced + 1) * c.vocab, logits_,

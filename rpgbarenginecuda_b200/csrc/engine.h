@@ -60,6 +60,15 @@ class Session {
   bool graph_ready() const { return graph_ != nullptr || loop_ready_; }
   int kernels_per_step() const { return kernels_per_step_; }
 
+  // Tensor parallel decode inside the loop kernel: every rank's session
+  // exports its exchange buffer (a CUDA IPC handle, 64 bytes) and attaches
+  // the handles of all ranks in rank order (collective; its own is used in
+  // place).  Without it a tensor-parallel session decodes through the step
+  // graph and NCCL.
+  void TpHandle(uint8_t* out) const;
+  void TpAttach(const uint8_t* handles);
+  bool tp_attached() const { return tp_attached_; }
+
   // Device timeline of the decode-step launches (see Trace in kernels.h).
   // EnableTrace(cap) allocates room for `cap` records and re-records the step
   // graph with tracing on (cap 0 turns it off); TakeTrace copies the records
@@ -120,6 +129,11 @@ class Session {
   uint32_t* tickets_loop_ = nullptr;
   size_t ll_words_ = 0;
   uint32_t epoch_ = 1;      // first tag base of the next launch
+  // tensor parallel: this rank's exchange buffer and every rank's (peers' by IPC)
+  uint64_t* xbuf_ = nullptr;
+  size_t xbuf_words_ = 0;
+  uint64_t* xpeer_[kLoopMaxTp] = {};
+  bool tp_attached_ = false;
 
   // prefill scratch (grow-only)
   int64_t pf_cap_ = 0;

@@ -491,6 +491,42 @@ __device__ __forceinline__ float4 WaitLL4(const LoopParams& p, const uint64_t* a
 }
 
 // Tag of the output of (step, layer, kind); the lm_head phase is kind 5 of layer n_layers - 1.
+// ---- tensor parallel: tagged words in every rank's exchange buffer.  Peer
+// words cross NVLink, so stores and polls are system-scoped; a rank may start
+// a launch some time after its peers, so their waits allow more polls.
+constexpr uint32_t kPeerLimit = 1u << 24;
+__device__ __forceinline__ void StSys(uint64_t* a, uint64_t w) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a), "l"(w) : "memory");
+}
+__device__ __forceinline__ uint64_t LdSys(const uint64_t* a) {
+  uint64_t w;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(a) : "memory");
+  return w;
+}
+// The word at a (in this rank's own buffer) once a peer stored it with `tag`.
+__device__ __forceinline__ uint64_t WaitPeer(const LoopParams& p, const uint64_t* a, uint32_t tag) {
+  uint64_t w;
+  for (uint32_t it = 0;; ++it) {
+    w = LdSys(a);
+    if (TagOk(w, tag)) break;
+    if (it == kPeerLimit) {
+      atomicOr(p.err, 16u);
+      break;
+    }
+    if ((it & 511u) == 511u && *reinterpret_cast<volatile unsigned*>(p.err) != 0u) break;
+  }
+  return w;
+}
+// Exchange buffer offsets: partial row `row` of attn_output (sel 0) or
+// ffn_down (sel 1) from rank `src`; the lm_head argmax {value, index} of
+// block `blk` of rank `src`.
+__device__ __forceinline__ size_t XRed(const LoopParams& p, int sel, int src, int row) {
+  return static_cast<size_t>(sel * kLoopMaxTp + src) * p.hidden + row;
+}
+__device__ __forceinline__ size_t XAm(const LoopParams& p, int src, int blk) {
+  return static_cast<size_t>(2 * kLoopMaxTp) * p.hidden + 2 * (static_cast<size_t>(src) * gridDim.x + blk);
+}
+
 __device__ __forceinline__ uint32_t TagOf(const LoopParams& p, int step, int layer, int kind) {
   return p.epoch0 + static_cast<uint32_t>(step) * static_cast<uint32_t>(5 * p.n_layers + 2) +
          static_cast<uint32_t>(5 * layer + kind) + 1u;
@@ -806,18 +842,31 @@ __device__ void MvPhase(const LoopParams& p, const GeoTable& gt, int kind, int l
       StLL(p.llqkv + row, v, tag_out);
     } else if (kind == kO || kind == kDown) {
       // x += W h: this block owns these rows of x in both phases
-      const float xn = xown[lr] + v;
+      float add = v;
+      if (p.tp > 0) {
+        // this rank's columns give a partial of the row: send it to every
+        // rank, then add the ranks' partials in rank order (the same sum, so
+        // the same x, on every rank)
+        const int sel = kind == kDown ? 1 : 0;
+        const uint64_t w = Pack(v, tag_out);
+        const size_t off = XRed(p, sel, p.tp_rank, row);
+        for (int k = 0; k < p.tp; ++k) StSys(p.xpeer[k] + off, w);
+        const uint64_t* mine = p.xpeer[p.tp_rank];
+        add = 0.f;
+        for (int k = 0; k < p.tp; ++k) add += ValOf(WaitPeer(p, mine + XRed(p, sel, k, row), tag_out));
+      }
+      const float xn = xown[lr] + add;
       xown[lr] = xn;
       StLL(p.llx + row, xn, tag_out);
     } else if (kind == kGu) {
       // rows 2i (gate) and 2i+1 (up): (g / (1 + exp(-g))) * u, as src/kernels_gpu.cu:863-869
       StLL(p.llh + (row >> 1), (v / (1.0f + expf(-v))) * v2, tag_out);
-    } else if (row < p.vocab) {
-      p.logits[row] = v;
+    } else if (row < p.lm_head.rows) {
+      p.logits[p.vocab0 + row] = v;
       if (p.mode == 0) {
         if (v > best_v) {  // rows increase per thread: strict > keeps the lowest index
           best_v = v;
-          best_i = row;
+          best_i = p.vocab0 + row;
         }
       } else if (p.mode == 1) {
         vals[lr] = v;
@@ -850,8 +899,18 @@ __device__ void MvPhase(const LoopParams& p, const GeoTable& gt, int kind, int l
           bi = s_bi[i];
         }
       }
-      p.am_val[blockIdx.x] = bv;
-      p.am_idx[blockIdx.x] = bi;
+      if (p.tp > 0) {  // to every rank: the step's token is the argmax over all ranks' blocks
+        const size_t off = XAm(p, p.tp_rank, blockIdx.x);
+        const uint64_t wv = Pack(bv, tag_out);
+        const uint64_t wi = (static_cast<uint64_t>(tag_out) << 32) | static_cast<uint32_t>(bi);
+        for (int k = 0; k < p.tp; ++k) {
+          StSys(p.xpeer[k] + off, wv);
+          StSys(p.xpeer[k] + off + 1, wi);
+        }
+      } else {
+        p.am_val[blockIdx.x] = bv;
+        p.am_idx[blockIdx.x] = bi;
+      }
     }
   } else if (kind == kLm && p.mode == 1) {
     __syncthreads();
@@ -1188,12 +1247,26 @@ __global__ void __launch_bounds__(kNT, 1) DecodeLoopKernel(const LoopParams p) {
     if (p.mode == 0) {
       float bv = -FLT_MAX;
       int bi = INT_MAX;
-      for (int i = tid; i < static_cast<int>(gridDim.x); i += kNT) {
-        const float v = __ldcg(p.am_val + i);
-        const int ix = __ldcg(p.am_idx + i);
-        if (v > bv || (v == bv && ix < bi)) {
-          bv = v;
-          bi = ix;
+      if (p.tp > 0) {
+        const uint32_t tag_lm = TagOf(p, step, p.n_layers - 1, kLm);
+        const uint64_t* mine = p.xpeer[p.tp_rank];
+        for (int i = tid; i < p.tp * static_cast<int>(gridDim.x); i += kNT) {
+          const size_t off = XAm(p, 0, 0) + 2 * static_cast<size_t>(i);  // i = rank * grid + block
+          const float v = ValOf(WaitPeer(p, mine + off, tag_lm));
+          const int ix = static_cast<int>(static_cast<uint32_t>(WaitPeer(p, mine + off + 1, tag_lm)));
+          if (v > bv || (v == bv && ix < bi)) {
+            bv = v;
+            bi = ix;
+          }
+        }
+      } else {
+        for (int i = tid; i < static_cast<int>(gridDim.x); i += kNT) {
+          const float v = __ldcg(p.am_val + i);
+          const int ix = __ldcg(p.am_idx + i);
+          if (v > bv || (v == bv && ix < bi)) {
+            bv = v;
+            bi = ix;
+          }
         }
       }
 #pragma unroll
@@ -1281,6 +1354,10 @@ constexpr int kSmemMax = 227 * 1024;
 
 bool LoopSupportsGroup(int group) { return group == 2 || group == 4; }
 
+size_t LoopExchangeWords(int hidden, int grid) {
+  return static_cast<size_t>(2 * kLoopMaxTp) * hidden + static_cast<size_t>(2 * kLoopMaxTp) * grid;
+}
+
 size_t LoopPartialWords(int n_kv, int group, int splits) {
   return static_cast<size_t>(n_kv) * splits * RecWords(group);
 }
@@ -1319,6 +1396,12 @@ void LaunchDecodeLoop(const LoopParams& in, int group, int num_sms, cudaStream_t
              "decode loop: tagged buffers missing");
   RPGB_CHECK(p.n_layers >= 1 && p.n_layers <= kMaxLayers, "decode loop: %d layers (at most %d)", p.n_layers,
              kMaxLayers);
+  if (p.tp > 0) {
+    RPGB_CHECK(p.tp <= kLoopMaxTp && p.tp_rank >= 0 && p.tp_rank < p.tp, "decode loop: rank %d of %d", p.tp_rank,
+               p.tp);
+    RPGB_CHECK(p.mode == 0, "decode loop: tensor parallel decode is greedy");
+    for (int k = 0; k < p.tp; ++k) RPGB_CHECK(p.xpeer[k] != nullptr, "decode loop: rank %d's buffer missing", k);
+  }
   p.nb_max = std::max({p.hidden, qd, p.ffn}) / 256;
   p.x_max = std::max(p.hidden, qd);
   // most tiles of one block over the phases' row counts

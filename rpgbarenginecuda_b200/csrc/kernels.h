@@ -244,8 +244,19 @@ struct LoopParams {
   int32_t scratch_bytes = 0;
   Trace trace;  // records carry id = step * (5 n_layers + 2) + phase
   double ns_per_cycle = 0.0;  // SM clock period, to turn cycle counts of the trace into nanoseconds
+  // tensor parallel (tp >= 1; 0 = one GPU): the exchange buffer of every rank
+  // (xpeer[tp_rank] is this rank's own; the others are peers' memory mapped
+  // over NVLink), laid out by LoopExchangeWords.  lm_head holds vocabulary
+  // rows [vocab0, vocab0 + lm_head.rows).
+  int32_t tp = 0, tp_rank = 0, vocab0 = 0;
+  uint64_t* xpeer[8] = {};
 };
 constexpr int kLoopMaxStop = 16;
+constexpr int kLoopMaxTp = 8;
+// Tagged words of a rank's exchange buffer: partial rows of attn_output and
+// ffn_down from every rank ([2][kLoopMaxTp][hidden]) and the lm_head argmax
+// of every rank's blocks ([kLoopMaxTp][grid][2]).
+size_t LoopExchangeWords(int hidden, int grid);
 // Tagged words of the attention split records for `splits` blocks per KV head.
 size_t LoopPartialWords(int n_kv, int group, int splits);
 // Tags one launch of n_steps steps consumes (the next launch's epoch0 is at least this much higher).

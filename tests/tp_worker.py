@@ -19,8 +19,14 @@ import numpy as np  # noqa: E402
 from rpgbarenginecuda_b200 import Model, SampleOptions, Session, TpGroup, synthetic  # noqa: E402
 
 
-def run(m, max_seq=512):
-    """The calls both the tensor-parallel ranks and the one-GPU reference make."""
+def run(m, max_seq=512, attach=False):
+    """The calls both the tensor-parallel ranks and the one-GPU reference make.
+
+    The greedy run with per-step logits goes through the step graph (NCCL
+    between launches when split); the second session's greedy runs are the
+    one-launch decode loop (partials exchanged between the GPUs once
+    attached), and its second generate call starts from the logits gathered
+    after the first."""
     s = Session(m, max_seq)
     toks = synthetic.seeded_tokens(21, 0, m.vocab)
     out = {"prefill": s.prefill(toks)}
@@ -31,6 +37,14 @@ def run(m, max_seq=512):
     out["sampled"], out["sampled_steps"] = np.asarray(sids), np.asarray(ssteps)
     out["len"] = np.asarray(len(s))
     s.close()
+    s2 = Session(m, max_seq)
+    if attach:
+        s2.attach_tp()
+    s2.prefill(toks, want_logits=False)
+    out["greedy_loop"] = np.asarray(s2.generate(SampleOptions(0.0, 0, 1.0), 0, 32))
+    out["greedy_loop2"] = np.asarray(s2.generate(SampleOptions(0.0, 0, 1.0), 0, 16))
+    out["len_loop"] = np.asarray(len(s2))
+    s2.close()
     return out
 
 
@@ -48,7 +62,7 @@ def main():
                             timeout=datetime.timedelta(seconds=120))
     g = TpGroup.from_process_group(device=a.rank)
     m = Model(a.model, a.rank, 1024, tp=g)
-    out = run(m)
+    out = run(m, attach=True)
     m.close()
     g.close()
     if a.rank == 0:
