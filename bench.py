@@ -74,7 +74,8 @@ def parse():
                     help="tensor-parallel measurement of the 8B configuration: run under torchrun with N ranks "
                          "(N = 1: the whole model on one GPU); 1024-token prefill + 128 greedy steps per turn")
     ap.add_argument("--with-ref-gpu", action="store_true",
-                    help="also time the reference's own CUDA engine (built from its sources) on the same turn")
+                    help="the reference's own CUDA engine on the same turn: closed (it faulted in its own prefill); "
+                         "the line records it as unavailable")
     return ap.parse_args()
 
 
@@ -475,7 +476,8 @@ def ours(args):
                "sample": c["sample"], "prefill_tok_s": round(c["prefill_tok_s"], 3)}
     ref_gpu = None
     if rank == 0 and args.with_ref_gpu:
-        ref_gpu = reference_gpu_turn(path, prompt, appends)
+        from oracle.oracle import REF_GPU_CLOSED
+        ref_gpu = {"unavailable": REF_GPU_CLOSED}
 
     if rank == 0:
         line = {
@@ -605,28 +607,6 @@ def tp_bench(args):
         tdist.barrier()
         tdist.destroy_process_group()
     return 0
-
-
-def reference_gpu_turn(path, prompt, appends):
-    """The reference's own CUDA engine (compiled from its sources) on one turn."""
-    from oracle.oracle import RefShim
-
-    rs = RefShim()
-    s = rs.session(path, 4096, 4096)
-    V = 151936
-    t0 = time.perf_counter()
-    s.prefill(prompt, V)
-    t1 = time.perf_counter()
-    dec_t, dec_n = 0.0, 0
-    for a in appends:
-        s.prefill(a, V)
-        d0 = time.perf_counter()
-        ids = s.generate(*SAMPLE, SEED, DECODE, use_graph=True)
-        dec_t += time.perf_counter() - d0
-        dec_n += len(ids)
-    s.close()
-    return {"prefill_tok_s": round(PROMPT_LEN / (t1 - t0), 2), "decode_tok_s": round(dec_n / dec_t, 2),
-            "note": "reference GpuForwardFull / GpuGenerate(use_graph) built for sm_100a, host wall clock"}
 
 
 def main():

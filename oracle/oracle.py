@@ -24,6 +24,14 @@ ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_QUANT_SO = os.path.join(HERE, "_ref", "libref_quant.so")
 REF_SHIM_SO = os.path.join(HERE, "_ref", "libref_shim.so")
 
+# The reference's GPU engine raised an illegal memory access inside its own
+# prefill on a B200 (GpuForwardFull on the tiny-g4 synthetic model, 21 valid
+# token ids, after the same calls had passed in earlier runs), so no
+# reference GPU code (engine, matmul, sampler, dequant kernels) is run from
+# here any more; the shim's host functions (counter_uniform) stay in use.
+REF_GPU_CLOSED = ("the reference's GPU engine raised an illegal memory access in its own prefill "
+                  "(tiny-g4 synthetic model, valid ids); its GPU code is not run again")
+
 i32, i64, u32, u64, f32, vp = (ctypes.c_int32, ctypes.c_int64, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_float,
                                ctypes.c_void_p)
 
@@ -203,12 +211,14 @@ class RefShim:
         return float(self.L.ref_counter_uniform(seed, counter))
 
     def gpu_dequant(self, qtype, data, n):
+        raise RuntimeError(REF_GPU_CLOSED)
         out = np.empty(n, dtype=np.float32)
         self._chk(self.L.ref_gpu_dequant(qtype, np.ascontiguousarray(data).ctypes.data, n, out.ctypes.data),
                   "dequant")
         return out
 
     def gpu_matmul(self, qtype, wbytes, rows, cols, x):
+        raise RuntimeError(REF_GPU_CLOSED)
         x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, cols)
         out = np.empty((x.shape[0], rows), dtype=np.float32)
         self._chk(self.L.ref_gpu_matmul(qtype, np.ascontiguousarray(wbytes).ctypes.data, rows, cols,
@@ -216,6 +226,7 @@ class RefShim:
         return out
 
     def gpu_sample(self, logits, temperature, top_k, top_p, seed, counter, want_probs=True):
+        raise RuntimeError(REF_GPU_CLOSED)
         lg = np.ascontiguousarray(logits, dtype=np.float32)
         probs = np.empty_like(lg) if want_probs else None
         tok = ctypes.c_int32(-1)
@@ -224,6 +235,7 @@ class RefShim:
         return tok.value, probs
 
     def session(self, path, max_pos=4096, max_seq=4096):
+        raise RuntimeError(REF_GPU_CLOSED)
         return _RefSession(self, path, max_pos, max_seq)
 
 

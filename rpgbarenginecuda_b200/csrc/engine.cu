@@ -260,6 +260,9 @@ void Session::EnsurePrefill(int64_t n) {
   cv.Add(sizeof(float) * cap * c.q_dim());
   cv.Add(sizeof(float) * cap * c.ffn);
   cv.Add(sizeof(float) * (m_->tp() != nullptr ? cap * c.hidden : 0));
+  const size_t split_floats =
+      FlashSupports(c.group(), c.head_dim) ? FlashSplitFloats(c.n_heads, c.n_kv_heads, m_->num_sms()) : 0;
+  cv.Add(sizeof(float) * split_floats);
   cv.Add(sizeof(int32_t) * cap);
   // fp16 operands of the tensor-core GEMM: the largest layer matrix and the widest activations
   const int64_t kmax = std::max<int64_t>(c.hidden, std::max<int64_t>(c.q_dim(), c.ffn));
@@ -279,6 +282,7 @@ void Session::EnsurePrefill(int64_t n) {
   pf_attn_ = cv.Take<float>(cap * c.q_dim());
   pf_h_ = cv.Take<float>(cap * c.ffn);
   pf_y_ = m_->tp() != nullptr ? cv.Take<float>(cap * c.hidden) : nullptr;
+  pf_part_ = split_floats > 0 ? cv.Take<float>(split_floats) : nullptr;
   pf_tok_ = cv.Take<int32_t>(cap);
   pf_tc_ = cv.Take<__half>(tc_halves);
   pf_tc_halves_ = tc_halves;
@@ -344,7 +348,8 @@ void Session::Prefill(const int32_t* tokens, int64_t n, float* last_logits) {
     a.fused = 0;
     a.err = err_;
     if (FlashSupports(c.group(), c.head_dim)) {
-      LaunchFlashPrefill(a, nt, pos0, s);
+      a.part = pf_part_;
+      LaunchFlashPrefill(a, nt, pos0, m_->num_sms(), s);
     } else {
       LaunchAttention(a, nt, s);
     }

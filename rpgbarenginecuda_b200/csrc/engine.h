@@ -140,6 +140,7 @@ class Session {
   uint8_t* pf_arena_ = nullptr;
   float *pf_x_ = nullptr, *pf_xn_ = nullptr, *pf_qkv_ = nullptr, *pf_q_ = nullptr, *pf_attn_ = nullptr,
         *pf_h_ = nullptr, *pf_y_ = nullptr;
+  float* pf_part_ = nullptr;  // key-split partials of the flash attention (appended turns)
   int32_t* pf_tok_ = nullptr;
   __half* pf_tc_ = nullptr;  // fp16 operands of the tensor-core GEMM
   size_t pf_tc_halves_ = 0;

@@ -17,6 +17,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "common.h"
@@ -42,6 +43,10 @@ struct FlashArgs {
   int64_t pos0;  // position of query 0
   float scale;
   unsigned* err;
+  // key splits (gridDim.z > 1): unnormalised O [split][n][q_dim] and
+  // {row max, row sum} [split][n][n_heads][2]
+  float* part_o;
+  float* part_ml;
 };
 
 __device__ __forceinline__ uint32_t PackHalf2(float a, float b) {
@@ -106,10 +111,14 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   const int wt0 = tok0 + (warp % kWarpsPerHead) * 16;  // first token of this warp's rows
   const int qh = h * G + gq;
 
-  // keys 0 .. pos0 + last token of the block
+  // keys 0 .. pos0 + last token of the block, in 64-key tiles; split z of
+  // gridDim.z takes tiles [t_lo, t_lo + nsteps)
   const int64_t last_tok = (tok0 + kTQ < a.n ? tok0 + kTQ : a.n) - 1;
   const int64_t kend = a.pos0 + last_tok + 1;
-  const int nsteps = static_cast<int>((kend + kKT - 1) / kKT);
+  const int tiles = static_cast<int>((kend + kKT - 1) / kKT);
+  const int n_split = static_cast<int>(gridDim.z), z = static_cast<int>(blockIdx.z);
+  const int t_lo = static_cast<int>(static_cast<int64_t>(z) * tiles / n_split);
+  const int nsteps = static_cast<int>(static_cast<int64_t>(z + 1) * tiles / n_split) - t_lo;
 
   if (tid == 0) {
     dev::MbarInit(full + 0, 1);
@@ -117,11 +126,12 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     dev::MbarInitFence();
     for (int st = 0; st < 2 && st < nsteps; ++st) {
       uint8_t* b = smem + st * kStageBytes;
+      const int y = (t_lo + st) * kKT;
       dev::MbarExpectTx(full + st, kStageBytes);
-      TmaLoad3D(b, &mK, 0, st * kKT, h, full + st);
-      TmaLoad3D(b + kHalfTile, &mK, 64, st * kKT, h, full + st);
-      TmaLoad3D(b + 2 * kHalfTile, &mV, 0, st * kKT, h, full + st);
-      TmaLoad3D(b + 3 * kHalfTile, &mV, 64, st * kKT, h, full + st);
+      TmaLoad3D(b, &mK, 0, y, h, full + st);
+      TmaLoad3D(b + kHalfTile, &mK, 64, y, h, full + st);
+      TmaLoad3D(b + 2 * kHalfTile, &mV, 0, y, h, full + st);
+      TmaLoad3D(b + 3 * kHalfTile, &mV, 64, y, h, full + st);
     }
   }
 
@@ -161,7 +171,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     }
     const uint32_t kb = dev::SmemAddr(smem + stage * kStageBytes);
     const uint32_t vb = kb + 2 * kHalfTile;
-    const int64_t key0 = static_cast<int64_t>(st) * kKT;
+    const int64_t key0 = static_cast<int64_t>(t_lo + st) * kKT;
     // this warp's rows see no key of this stage: skip the math (stays in step for the barrier)
     const bool any = key0 <= a.pos0 + wt0 + 15;
     if (any) {
@@ -248,7 +258,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     if (tid == 0 && st + 2 < nsteps) {
       dev::FenceProxyAsync();
       uint8_t* b = smem + stage * kStageBytes;
-      const int y = (st + 2) * kKT;
+      const int y = (t_lo + st + 2) * kKT;
       dev::MbarExpectTx(full + stage, kStageBytes);
       TmaLoad3D(b, &mK, 0, y, h, full + stage);
       TmaLoad3D(b + kHalfTile, &mK, 64, y, h, full + stage);
@@ -268,9 +278,24 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   l0 += __shfl_xor_sync(0xFFFFFFFFu, l0, 2);
   l1 += __shfl_xor_sync(0xFFFFFFFFu, l1, 1);
   l1 += __shfl_xor_sync(0xFFFFFFFFu, l1, 2);
-  const float i0 = 1.0f / l0, i1 = 1.0f / l1;
   const int ta = wt0 + g4, tb = ta + 8;
   const int q_dim = a.n_heads * kD;
+  if (n_split > 1) {  // unnormalised partials; FlashMergeKernel combines the splits
+    float* po = a.part_o + static_cast<int64_t>(z) * a.n * q_dim + qh * kD;
+    float* pml = a.part_ml + (static_cast<int64_t>(z) * a.n * a.n_heads + qh) * 2;
+#pragma unroll
+    for (int dt = 0; dt < 16; ++dt) {
+      const int d = 8 * dt + 2 * t4;
+      if (ta < a.n) *reinterpret_cast<float2*>(po + static_cast<int64_t>(ta) * q_dim + d) = make_float2(o[dt][0], o[dt][1]);
+      if (tb < a.n) *reinterpret_cast<float2*>(po + static_cast<int64_t>(tb) * q_dim + d) = make_float2(o[dt][2], o[dt][3]);
+    }
+    if (t4 == 0) {
+      if (ta < a.n) *reinterpret_cast<float2*>(pml + static_cast<int64_t>(ta) * a.n_heads * 2) = make_float2(m0, l0);
+      if (tb < a.n) *reinterpret_cast<float2*>(pml + static_cast<int64_t>(tb) * a.n_heads * 2) = make_float2(m1, l1);
+    }
+    return;
+  }
+  const float i0 = 1.0f / l0, i1 = 1.0f / l1;
 #pragma unroll
   for (int dt = 0; dt < 16; ++dt) {
     const int d = 8 * dt + 2 * t4;
@@ -283,6 +308,39 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
           make_float2(o[dt][2] * i1, o[dt][3] * i1);
     }
   }
+}
+
+// out[t][head] = sum_z O_z e^(m_z - M) / sum_z l_z e^(m_z - M), M = max_z m_z;
+// one warp per (token, head), four dimensions per lane.  A split that saw no
+// key of the row carries m = -inf, l = 0 and adds nothing.
+__global__ void __launch_bounds__(256) FlashMergeKernel(const float* __restrict__ part_o,
+                                                        const float* __restrict__ part_ml, float* __restrict__ out,
+                                                        int n, int n_heads, int n_split) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + warp;  // t * n_heads + head
+  if (row >= static_cast<int64_t>(n) * n_heads) return;
+  const int64_t rows = static_cast<int64_t>(n) * n_heads;
+  const int t = static_cast<int>(row / n_heads), hd = static_cast<int>(row - static_cast<int64_t>(t) * n_heads);
+  const int64_t q_dim = static_cast<int64_t>(n_heads) * kD;
+  float M = -INFINITY;
+  for (int z = 0; z < n_split; ++z) M = fmaxf(M, part_ml[(z * rows + row) * 2]);
+  float L = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int z = 0; z < n_split; ++z) {
+    const float2 ml = *reinterpret_cast<const float2*>(part_ml + (z * rows + row) * 2);
+    if (ml.x == -INFINITY) continue;
+    const float w = expf(ml.x - M);
+    L += ml.y * w;
+    const float4 v = *reinterpret_cast<const float4*>(part_o + z * static_cast<int64_t>(n) * q_dim + t * q_dim +
+                                                      hd * kD + 4 * lane);
+    acc.x += v.x * w;
+    acc.y += v.y * w;
+    acc.z += v.z * w;
+    acc.w += v.w * w;
+  }
+  const float inv = 1.0f / L;
+  *reinterpret_cast<float4*>(out + t * q_dim + hd * kD + 4 * lane) =
+      make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 Encode() {
@@ -338,7 +396,15 @@ void PrepareFlashKernels() {
 
 bool FlashSupports(int group, int head_dim) { return head_dim == kD && (group == 1 || group == 2 || group == 4 || group == 8); }
 
-void LaunchFlashPrefill(const AttnParams& p, int n_queries, int64_t pos0, cudaStream_t s) {
+size_t FlashSplitFloats(int n_heads, int n_kv, int num_sms) {
+  // splitting happens only while query tiles x KV heads x splits <= num_sms,
+  // so split x token rows are at most num_sms / n_kv query tiles of 128 / G tokens
+  const int group = n_heads / n_kv;
+  const size_t rows = static_cast<size_t>(num_sms / n_kv + 1) * (kRows / group);
+  return rows * (static_cast<size_t>(n_heads) * kD + 2 * static_cast<size_t>(n_heads));
+}
+
+void LaunchFlashPrefill(const AttnParams& p, int n_queries, int64_t pos0, int num_sms, cudaStream_t s) {
   RPGB_CHECK(n_queries > 0 && p.n_kv > 0 && p.n_heads % p.n_kv == 0, "flash attention: bad shape");
   RPGB_CHECK(p.err != nullptr, "flash attention: no error word");
   const int G = p.n_heads / p.n_kv;
@@ -353,10 +419,34 @@ void LaunchFlashPrefill(const AttnParams& p, int n_queries, int64_t pos0, cudaSt
   a.scale = p.scale;
   a.err = p.err;
   const int tq = kRows / G;
-  const dim3 grid((n_queries + tq - 1) / tq, p.n_kv);
+  const int qtiles = (n_queries + tq - 1) / tq;
+  // key splits while the grid would fill at most half the SMs, each split at
+  // least two 64-key tiles of the longest query tile
+  int n_split = 1;
+  const int base = qtiles * p.n_kv;
+  const size_t q_dim = static_cast<size_t>(p.n_heads) * kD;
+  if (p.part != nullptr && 2 * base <= num_sms) {
+    const int64_t tiles = (pos0 + n_queries + kKT - 1) / kKT;
+    n_split = static_cast<int>(std::min<int64_t>({static_cast<int64_t>(num_sms / base), tiles / 2,
+                                                  static_cast<int64_t>(kMaxFlashSplits)}));
+    n_split = std::max(n_split, 1);
+    RPGB_CHECK(static_cast<size_t>(n_split) * n_queries * (q_dim + 2 * p.n_heads) <=
+                   FlashSplitFloats(p.n_heads, p.n_kv, num_sms),
+               "flash attention: split scratch too small");
+  }
+  a.part_o = n_split > 1 ? p.part : nullptr;
+  a.part_ml = n_split > 1 ? p.part + static_cast<size_t>(n_split) * n_queries * q_dim : nullptr;
+  const dim3 grid(qtiles, p.n_kv, n_split);
   PickFlash(G)<<<grid, kWarps * 32, kSmem, s>>>(mK, mV, a);
   RPGB_CUDA(cudaGetLastError());
   CountLaunches(1);
+  if (n_split > 1) {
+    const int64_t rows = static_cast<int64_t>(n_queries) * p.n_heads;
+    FlashMergeKernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, s>>>(a.part_o, a.part_ml, p.out, n_queries,
+                                                                          p.n_heads, n_split);
+    RPGB_CUDA(cudaGetLastError());
+    CountLaunches(1);
+  }
 }
 
 }  // namespace rpgb

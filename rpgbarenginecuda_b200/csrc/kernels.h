@@ -129,7 +129,13 @@ size_t AttentionPartialFloats(int n_kv, int group, int n_splits);
 // the layer's cache p.kc / p.vc, out = p.out [n][q_dim]; p.err receives
 // bounded-wait failures.  For head_dim 128 and group sizes 1, 2, 4, 8.
 bool FlashSupports(int group, int head_dim);
-void LaunchFlashPrefill(const AttnParams& p, int n_queries, int64_t pos0, cudaStream_t s);
+// Few query tiles (an appended turn at a long context) leave most SMs idle;
+// then the key range of each (query tile, KV head) is split over up to
+// kMaxFlashSplits blocks whose partial outputs p.part (at least
+// FlashSplitFloats floats; null = never split) are merged by a second launch.
+constexpr int kMaxFlashSplits = 16;
+size_t FlashSplitFloats(int n_heads, int n_kv, int num_sms);
+void LaunchFlashPrefill(const AttnParams& p, int n_queries, int64_t pos0, int num_sms, cudaStream_t s);
 void PrepareFlashKernels();
 
 // Prefill helpers: per-head RMSNorm + RoPE for q and k, fp16 cache write of k and v.

@@ -14,7 +14,7 @@ import os
 import numpy as np
 import pytest
 
-from oracle.oracle import REF_SHIM_SO, OracleModel, OracleSession
+from oracle.oracle import REF_GPU_CLOSED, REF_SHIM_SO, OracleModel, OracleSession
 from rpgbarenginecuda_b200 import Model, SampleOptions, Session, synthetic
 
 pytestmark = pytest.mark.gpu
@@ -125,6 +125,7 @@ def test_continue_after_generate(pair):
     assert list(one) == list(two)
 
 
+@pytest.mark.skip(reason=REF_GPU_CLOSED)
 @pytest.mark.skipif(not os.path.exists(REF_SHIM_SO), reason="oracle/_ref not built")
 def test_vs_reference_engine(pair):
     """Same synthetic GGUF and token ids through the reference's own GPU engine."""

@@ -15,7 +15,7 @@ import os
 import numpy as np
 import pytest
 
-from oracle.oracle import REF_SHIM_SO
+from oracle.oracle import REF_GPU_CLOSED, REF_SHIM_SO
 from rpgbarenginecuda_b200 import SampleOptions, sample
 
 pytestmark = pytest.mark.gpu
@@ -95,6 +95,7 @@ def test_sampler_vs_oracle(oracle, vocab, case):
                 assert near_boundary(ref_probs, u), (counter, got, want)
 
 
+@pytest.mark.skip(reason=REF_GPU_CLOSED)
 @pytest.mark.skipif(not os.path.exists(REF_SHIM_SO), reason="oracle/_ref not built")
 @pytest.mark.parametrize("vocab", [4096, 151936])
 @pytest.mark.parametrize("case", REF_CASES + SWEEP_CASES[::3])
