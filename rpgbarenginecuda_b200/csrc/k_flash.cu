@@ -106,7 +106,9 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g4 = lane >> 2, t4 = lane & 3;
   const int h = blockIdx.y;
-  const int tok0 = blockIdx.x * kTQ;
+  // the last query tiles see the most keys (causal): they are launched first,
+  // so the short tiles fill the final wave
+  const int tok0 = (gridDim.x - 1 - blockIdx.x) * kTQ;
   const int gq = warp / kWarpsPerHead;                // q head within the group
   const int wt0 = tok0 + (warp % kWarpsPerHead) * 16;  // first token of this warp's rows
   const int qh = h * G + gq;

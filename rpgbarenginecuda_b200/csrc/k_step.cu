@@ -675,7 +675,7 @@ __device__ void MergeHead(const LoopParams& p, int step, int layer, int64_t pos,
     double L = 0.0;
     for (int sp = 0; sp < se; ++sp) {
       const int k = sp * G + g;
-      const float w = wv[k] == -INFINITY ? 0.f : expf(wv[k] - M);
+      const float w = wv[k] == -INFINITY ? 0.f : exp2f(wv[k] - M);
       wv[k] = w;
       L += static_cast<double>(w) * lv[k];
     }
@@ -981,12 +981,15 @@ __device__ void AttnPhase(const LoopParams& p, const GeoTable& gt, int layer, in
     const double tot = as.sq[2 * vi] + as.sq[2 * vi + 1];
     const float sc = static_cast<float>(1.0 / sqrt(tot / static_cast<double>(kD) + static_cast<double>(p.eps)));
     const float* nw = vi < G ? Ly.norm[2] : Ly.norm[3];
+    // scores in log2 units (q times 1/sqrt(128) times log2(e)): the softmax
+    // then exponentiates with exp2f; the split records carry the same units
+    const float qscale = p.scale * 1.4426950408889634f;
     const float x0 = e0 * sc * nw[d], x1 = e1 * sc * nw[d + 64];
     const float rc = p.rope[pos * kD + d], rs = p.rope[pos * kD + kD / 2 + d];
     const float y0 = x0 * rc - x1 * rs, y1 = x1 * rc + x0 * rs;
     if (vi < G) {
-      as.qs[vi][d] = y0 * p.scale;
-      as.qs[vi][d + 64] = y1 * p.scale;
+      as.qs[vi][d] = y0 * qscale;
+      as.qs[vi][d + 64] = y1 * qscale;
     } else {
       const __half k0 = __float2half_rn(y0), k1 = __float2half_rn(y1);
       as.knew[d] = k0;
@@ -1013,6 +1016,20 @@ __device__ void AttnPhase(const LoopParams& p, const GeoTable& gt, int layer, in
 #pragma unroll
     for (int e = 0; e < 4; ++e) acc[g][e] = 0.f;
   }
+  // this lane's q dimensions (64 hf + 8 sub .. +7) do not change over the
+  // chunks: for G = 2 they stay in registers (32 floats)
+  constexpr int kQr = G == 2 ? G : 1;
+  float4 qr[kQr][2][2];
+  if constexpr (G == 2) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        qr[g][hf][0] = *reinterpret_cast<const float4*>(&as.qs[g][64 * hf + 8 * sub]);
+        qr[g][hf][1] = *reinterpret_cast<const float4*>(&as.qs[g][64 * hf + 8 * sub + 4]);
+      }
+    }
+  }
   for (int ch = a.c0 + warp; ch < a.c1; ch += kNW) {
     const int64_t r0 = static_cast<int64_t>(ch) * kChunk;
     const int n_valid = static_cast<int>(pos + 1 - r0 < kChunk ? pos + 1 - r0 : kChunk);
@@ -1032,8 +1049,14 @@ __device__ void AttnPhase(const LoopParams& p, const GeoTable& gt, int layer, in
         const float2 f2 = __half22float2(h2[2]), f3 = __half22float2(h2[3]);
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-          const float4 qa = *reinterpret_cast<const float4*>(&as.qs[g][64 * hf + 8 * sub]);
-          const float4 qb = *reinterpret_cast<const float4*>(&as.qs[g][64 * hf + 8 * sub + 4]);
+          float4 qa, qb;
+          if constexpr (G == 2) {
+            qa = qr[g][hf][0];
+            qb = qr[g][hf][1];
+          } else {
+            qa = *reinterpret_cast<const float4*>(&as.qs[g][64 * hf + 8 * sub]);
+            qb = *reinterpret_cast<const float4*>(&as.qs[g][64 * hf + 8 * sub + 4]);
+          }
           dd[g] = fmaf(qa.x, f0.x, dd[g]);
           dd[g] = fmaf(qa.y, f0.y, dd[g]);
           dd[g] = fmaf(qa.z, f1.x, dd[g]);
@@ -1056,8 +1079,8 @@ __device__ void AttnPhase(const LoopParams& p, const GeoTable& gt, int layer, in
       float mx = fmaxf(sc, __shfl_xor_sync(0xFFFFFFFFu, sc, 8));
       mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 16));
       const float nm = fmaxf(m[g], mx);
-      const float alpha = m[g] == -INFINITY ? 0.f : expf(m[g] - nm);
-      const float e = pp < n_valid ? expf(sc - nm) : 0.f;
+      const float alpha = m[g] == -INFINITY ? 0.f : exp2f(m[g] - nm);
+      const float e = pp < n_valid ? exp2f(sc - nm) : 0.f;
       float ps = e + __shfl_xor_sync(0xFFFFFFFFu, e, 8);
       ps += __shfl_xor_sync(0xFFFFFFFFu, ps, 16);
       m[g] = nm;
@@ -1110,14 +1133,14 @@ __device__ void AttnPhase(const LoopParams& p, const GeoTable& gt, int layer, in
     float M = as.fsh[g];
 #pragma unroll
     for (int w = 1; w < kNW; ++w) M = fmaxf(M, as.fsh[w * G + g]);
-    const float sw = m[g] == -INFINITY ? 0.f : expf(m[g] - M);
+    const float sw = m[g] == -INFINITY ? 0.f : exp2f(m[g] - M);
     *reinterpret_cast<float4*>(vred + (warp * G + g) * kD + 4 * lane) =
         make_float4(acc[g][0] * sw, acc[g][1] * sw, acc[g][2] * sw, acc[g][3] * sw);
     if (warp == 0) {  // lanes 0..15 weigh the warps' denominators
       double t = 0.0;
       if (lane < kNW) {
         const float mw = as.fsh[lane * G + g];
-        t = mw == -INFINITY ? 0.0 : static_cast<double>(expf(mw - M)) * as.dsh[lane * G + g];
+        t = mw == -INFINITY ? 0.0 : static_cast<double>(exp2f(mw - M)) * as.dsh[lane * G + g];
       }
       t = dev::WarpSumD(t);
       if (lane == 0) {
