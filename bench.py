@@ -70,6 +70,10 @@ def parse():
     ap.add_argument("--decode-loop-ctx", type=int, default=0,
                     help="prefill this many tokens, then two generate calls (2 and 4 decode steps) and exit "
                          "(the second decode-loop launch is the one profiled for profiles/)")
+    ap.add_argument("--suite", action="store_true",
+                    help="the other single-GPU configurations: 0.6B (21-id prompt + 32 greedy steps) and 4B "
+                         "(prefill at n = 1, 4, 16, 128, 2048; 256 greedy steps from contexts 512 and 3840); "
+                         "one JSON line each")
     ap.add_argument("--tp", action="store_true",
                     help="tensor-parallel measurement of the 8B configuration: run under torchrun with N ranks "
                          "(N = 1: the whole model on one GPU); 1024-token prefill + 128 greedy steps per turn")
@@ -516,6 +520,99 @@ def ours(args):
 TP_MODEL, TP_PROMPT, TP_DECODE = "qwen3-8b", 1024, 128
 
 
+def suite_bench(args):
+    """The 0.6B and 4B workloads on one GPU, timed with CUDA events on the
+    session stream (args.warmup untimed repetitions, then args.steps timed)."""
+    import torch
+
+    from rpgbarenginecuda_b200 import Model, SampleOptions, Session, synthetic
+
+    torch.cuda.set_device(0)
+    greedy = SampleOptions(0.0, 0, 1.0)
+
+    def timed(sess, fn):
+        stream = torch.cuda.ExternalStream(sess.stream_ptr, device=0)
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        tot, n = 0.0, 0
+        for _ in range(args.steps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            k = fn()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            tot += e0.elapsed_time(e1)
+            n += k
+        return n / (tot * 1e-3)
+
+    def line(name, metric, value, extra):
+        d = {"metric": metric, "value": round(value, 2), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+             "warmup": args.warmup, "higher_is_better": True, "dtype": "f32", "data": "synthetic",
+             "config": {"model": name, "global_batch": 1}}
+        d.update(extra)
+        print(json.dumps(d), flush=True)
+
+    # 0.6B: 21-id prompt, 32 greedy steps
+    m = Model(synthetic.cached_model("qwen3-0.6b", seed=0), 0, 4096)
+    s = Session(m, 4096)
+    prompt = synthetic.seeded_tokens(21, 0, m.vocab)
+
+    def pre06():
+        s.set_len(0)
+        s.prefill(prompt, want_logits=False)
+        return len(prompt)
+
+    def dec06():
+        s.set_len(0)
+        s.prefill(prompt, want_logits=False)
+        return len(s.generate(greedy, 0, 32))
+
+    p06 = timed(s, pre06)
+    # decode rate = 32 tokens over (prefill + decode) minus the prefill time
+    t_all = 1.0 / timed(s, dec06) * 32
+    t_pre = len(prompt) / p06
+    line("qwen3-0.6b", "batch-1 greedy decode tok/s (qwen3-0.6b, 21-id prompt, 32 steps)", 32 / (t_all - t_pre),
+         {"prefill_tok_s": round(p06, 1)})
+    s.close()
+    m.close()
+
+    # 4B: prefill at several prompt lengths; 256 greedy steps from contexts 512 and 3840
+    m = Model(synthetic.cached_model("qwen3-4b", seed=0), 0, 4096)
+    s = Session(m, 4096)
+    pre = {}
+    for n in (1, 4, 16, 128, 2048):
+        toks = synthetic.seeded_tokens(n, 7, m.vocab)
+
+        def pf(toks=toks):
+            s.set_len(0)
+            s.prefill(toks, want_logits=False)
+            return len(toks)
+
+        pre[str(n)] = round(timed(s, pf), 1)
+    dec = {}
+    for ctx in (512, 3840):
+        toks = synthetic.seeded_tokens(ctx, 9, m.vocab)
+        stream = torch.cuda.ExternalStream(s.stream_ptr, device=0)
+        rates = []
+        for it in range(args.warmup + args.steps):
+            s.set_len(0)
+            s.prefill(toks, want_logits=False)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            k = len(s.generate(greedy, 0, 256))
+            e1.record(stream)
+            torch.cuda.synchronize()
+            if it >= args.warmup:
+                rates.append(k / (e0.elapsed_time(e1) * 1e-3))
+        dec[str(ctx)] = round(sum(rates) / len(rates), 2)
+    line("qwen3-4b", "batch-1 greedy decode tok/s (qwen3-4b, 256 steps from context 512)", dec["512"],
+         {"decode_tok_s_by_context": dec, "prefill_tok_s_by_n": pre})
+    s.close()
+    m.close()
+    return 0
+
+
 def tp_bench(args):
     """The 8B configuration split over the torchrun ranks (one GPU each).
 
@@ -620,6 +717,8 @@ def main():
     if args.decode_loop_ctx > 0:
         decode_loop_ctx(args)
         return
+    if args.suite:
+        return suite_bench(args)
     if args.tp:
         return tp_bench(args)
     if args.impl == "reference":

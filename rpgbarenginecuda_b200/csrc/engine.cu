@@ -289,6 +289,26 @@ void Session::EnsurePrefill(int64_t n) {
   pf_cap_ = cap;
 }
 
+void Session::RowwiseMatvec(const DevMat* w, const int* out_off, int n_seg, const float* x, int ldx, float* out,
+                            int ldo, bool resid, Epi epi, int n_tok, cudaStream_t s) {
+  int total = 0;
+  for (int i = 0; i < n_seg; ++i) total += w[i].rows;
+  for (int t = 0; t < n_tok; ++t) {
+    MvParams p;
+    for (int i = 0; i < n_seg; ++i) {
+      p.seg[i].w = w[i];
+      p.seg[i].out_off = out_off[i];
+    }
+    p.n_seg = n_seg;
+    p.total_rows = total;
+    p.x = x + static_cast<int64_t>(t) * ldx;
+    p.out = out + static_cast<int64_t>(t) * ldo;
+    p.resid = resid ? p.out : nullptr;
+    p.err = err_;
+    LaunchMatvec(p, epi, 1, m_->num_sms(), s);
+  }
+}
+
 void Session::Prefill(const int32_t* tokens, int64_t n, float* last_logits) {
   const ModelMeta& c = m_->meta();
   RPGB_CHECK(n > 0, "prompt is empty");
@@ -307,30 +327,41 @@ void Session::Prefill(const int32_t* tokens, int64_t n, float* last_logits) {
 
   const int H = c.hidden, qd = c.q_dim(), kvd = c.kv_dim(), qkv = qd + 2 * kvd;
   const int nt = static_cast<int>(n);
+  // Short prompts: GEMM tiles would leave most SMs idle (and the tensor-core
+  // path would first expand every weight to fp16), so each token runs the
+  // decode matvec on its normalised row instead; from the second token on the
+  // layer's weights come from L2.
+  const bool rowwise = nt < kTcMinTokens;
   LaunchEmbed(m_->embd(), pf_tok_, nt, pf_x_, nullptr, nullptr, s);
   for (int l = 0; l < c.n_layers; ++l) {
     const DevLayer& L = m_->layers()[static_cast<size_t>(l)];
     __half* kc = kc_ + layer_elems_ * l;
     __half* vc = vc_ + layer_elems_ * l;
     LaunchRmsNormRows(pf_x_, L.attn_norm, nt, H, c.rms_eps, pf_xn_, s);
-    GemmParams g;
-    g.tc_scratch = pf_tc_;
-    g.tc_scratch_halves = pf_tc_halves_;
-    g.err = err_;
-    g.X = pf_xn_;
-    g.n_tok = nt;
-    g.ldx = H;
-    g.out = pf_qkv_;
-    g.ldo = qkv;
-    g.w = L.q;
-    g.out_off = 0;
-    LaunchGemm(g, Epi::kStore, s);
-    g.w = L.k;
-    g.out_off = qd;
-    LaunchGemm(g, Epi::kStore, s);
-    g.w = L.v;
-    g.out_off = qd + kvd;
-    LaunchGemm(g, Epi::kStore, s);
+    if (rowwise) {
+      const DevMat w3[3] = {L.q, L.k, L.v};
+      const int off3[3] = {0, qd, qd + kvd};
+      RowwiseMatvec(w3, off3, 3, pf_xn_, H, pf_qkv_, qkv, false, Epi::kStore, nt, s);
+    } else {
+      GemmParams g;
+      g.tc_scratch = pf_tc_;
+      g.tc_scratch_halves = pf_tc_halves_;
+      g.err = err_;
+      g.X = pf_xn_;
+      g.n_tok = nt;
+      g.ldx = H;
+      g.out = pf_qkv_;
+      g.ldo = qkv;
+      g.w = L.q;
+      g.out_off = 0;
+      LaunchGemm(g, Epi::kStore, s);
+      g.w = L.k;
+      g.out_off = qd;
+      LaunchGemm(g, Epi::kStore, s);
+      g.w = L.v;
+      g.out_off = qd + kvd;
+      LaunchGemm(g, Epi::kStore, s);
+    }
     LaunchQkRopeKv(pf_qkv_, nt, qd, kvd, L.q_norm, L.k_norm, m_->rope(), c.rms_eps, pos_, kc, vc,
                    static_cast<int32_t>(max_seq_), c.n_heads, c.n_kv_heads, pf_q_, s);
     AttnParams a;
@@ -353,26 +384,47 @@ void Session::Prefill(const int32_t* tokens, int64_t n, float* last_logits) {
     } else {
       LaunchAttention(a, nt, s);
     }
-    GemmParams o;
-    o.tc_scratch = pf_tc_;
-    o.tc_scratch_halves = pf_tc_halves_;
-    o.err = err_;
-    o.w = L.o;
-    o.X = pf_attn_;
-    o.n_tok = nt;
-    o.ldx = qd;
-    o.ldo = H;
-    if (m_->tp() != nullptr) {
-      o.out = pf_y_;
-      LaunchGemm(o, Epi::kStore, s);
-      ReduceIntoResidual(pf_x_, pf_y_, n, s);
+    if (rowwise) {
+      const int off0[1] = {0};
+      if (m_->tp() != nullptr) {
+        RowwiseMatvec(&L.o, off0, 1, pf_attn_, qd, pf_y_, H, false, Epi::kStore, nt, s);
+        ReduceIntoResidual(pf_x_, pf_y_, n, s);
+      } else {
+        RowwiseMatvec(&L.o, off0, 1, pf_attn_, qd, pf_x_, H, true, Epi::kResid, nt, s);
+      }
     } else {
-      o.out = pf_x_;
-      o.resid = pf_x_;
-      o.ldr = H;
-      LaunchGemm(o, Epi::kResid, s);
+      GemmParams o;
+      o.tc_scratch = pf_tc_;
+      o.tc_scratch_halves = pf_tc_halves_;
+      o.err = err_;
+      o.w = L.o;
+      o.X = pf_attn_;
+      o.n_tok = nt;
+      o.ldx = qd;
+      o.ldo = H;
+      if (m_->tp() != nullptr) {
+        o.out = pf_y_;
+        LaunchGemm(o, Epi::kStore, s);
+        ReduceIntoResidual(pf_x_, pf_y_, n, s);
+      } else {
+        o.out = pf_x_;
+        o.resid = pf_x_;
+        o.ldr = H;
+        LaunchGemm(o, Epi::kResid, s);
+      }
     }
     LaunchRmsNormRows(pf_x_, L.ffn_norm, nt, H, c.rms_eps, pf_xn_, s);
+    if (rowwise) {
+      const int off0[1] = {0};
+      RowwiseMatvec(&L.gateup, off0, 1, pf_xn_, H, pf_h_, c.ffn, false, Epi::kSilu, nt, s);
+      if (m_->tp() != nullptr) {
+        RowwiseMatvec(&L.down, off0, 1, pf_h_, c.ffn, pf_y_, H, false, Epi::kStore, nt, s);
+        ReduceIntoResidual(pf_x_, pf_y_, n, s);
+      } else {
+        RowwiseMatvec(&L.down, off0, 1, pf_h_, c.ffn, pf_x_, H, true, Epi::kResid, nt, s);
+      }
+      continue;
+    }
     GemmParams gu;
     gu.tc_scratch = pf_tc_;
     gu.tc_scratch_halves = pf_tc_halves_;

@@ -78,6 +78,10 @@ class Session {
 
  private:
   void EnqueueStep(const SampleOpts& opt, uint64_t seed);
+  // Prefill of fewer than kTcMinTokens tokens: out[t] = W x[t] per token with
+  // the decode matvec (segments of w stacked at out_off; resid: out += W x).
+  void RowwiseMatvec(const DevMat* w, const int* out_off, int n_seg, const float* x, int ldx, float* out, int ldo,
+                     bool resid, Epi epi, int n_tok, cudaStream_t s);
   // Tensor parallel: out = W x (this rank's columns) into y, summed over the
   // group, then added to the residual x (n rows of hidden).
   void ReduceIntoResidual(float* x, float* y, int64_t n, cudaStream_t s);

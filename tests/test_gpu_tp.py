@@ -36,6 +36,7 @@ def full_scale_err(ours, ref):
 
 def check_same(got, ref):
     assert full_scale_err(got["prefill"], ref["prefill"]) <= FULL_SCALE
+    assert full_scale_err(got["short_prefill"], ref["short_prefill"]) <= FULL_SCALE
     for key in ("greedy", "sampled"):
         ids, rids, rsteps = got[key], ref[key], ref[key + "_steps"]
         n = min(len(ids), len(rids))

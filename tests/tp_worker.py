@@ -35,6 +35,8 @@ def run(m, max_seq=512, attach=False):
     s.prefill(synthetic.seeded_tokens(40, 1, m.vocab), want_logits=False)
     sids, ssteps = s.generate(SampleOptions(0.7, 20, 0.8), 1234, 24, step_logits=True)
     out["sampled"], out["sampled_steps"] = np.asarray(sids), np.asarray(ssteps)
+    # a short prompt (fewer than 16 tokens) takes the per-token matvec prefill
+    out["short_prefill"] = s.prefill(synthetic.seeded_tokens(5, 2, m.vocab))
     out["len"] = np.asarray(len(s))
     s.close()
     s2 = Session(m, max_seq)
