@@ -384,15 +384,18 @@ __device__ __forceinline__ const uint8_t* RingWait(Ring& r, const LoopParams& p)
 }
 
 // Marks the current unit consumed and refills free slots from the stream.
+// attn_only: refill only while the next unit is an attention chunk (the
+// chunk loop defers the walk into the following phases' weights to the next
+// phase's start, where the warp waits for its input anyway).
 __device__ __forceinline__ void RingRelease(Ring& r, const LoopParams& p, const GeoTable& gt, int64_t pos0,
-                                            int warp) {
+                                            int warp, bool attn_only = false) {
   __syncwarp();
   ++r.kc;
   if (++r.cs == r.R) {
     r.cs = 0;
     r.cpar ^= 1u;
   }
-  if ((threadIdx.x & 31) == 0) {
+  if ((threadIdx.x & 31) == 0 && (!attn_only || r.cur.kind == kAttn)) {
     dev::FenceProxyAsync();
     RingPump(r, p, gt, pos0, warp);
   }
@@ -714,6 +717,10 @@ __device__ void MvPhase(const LoopParams& p, const GeoTable& gt, int kind, int l
                         float* s_bv, int* s_bi, int* s_cnt, uint32_t* s_sel) {
   Ring rg = rg_io;  // in registers for the unit loop
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (lane == 0) {  // refills the attention phase deferred (a no-op when the ring is full)
+    dev::FenceProxyAsync();
+    RingPump(rg, p, gt, pos0, warp);
+  }
   const MvShape sh = ShapeOf(p, kind);
   const Geo g = gt.g[kind][warp];
   const int K = sh.K, nb = g.nb;
@@ -1108,7 +1115,7 @@ __device__ void AttnPhase(const LoopParams& p, const GeoTable& gt, int layer, in
       }
     }
     if (ch == a.c0) TraceMarkW0(p, clk, 2);
-    RingRelease(rg, p, gt, pos0, warp);
+    RingRelease(rg, p, gt, pos0, warp, true);
     if (ch == a.c0) TraceMarkW0(p, clk, 3);
   }
   TraceMarkW0(p, clk, 4);  // warp 0: its units done
