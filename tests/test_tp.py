@@ -46,6 +46,25 @@ def test_shard_plan_rejects(shape, size, what):
         shard_plan(shape, rank, size)
 
 
+# Which configurations split over 2 / 4 / 8 GPUs: FFN columns per rank must
+# be whole 256-column super-blocks (0.6B ffn 3072 / 8 = 384 and 4B ffn
+# 9728 / 4 = 2432 are not).
+SUPPORT = {"qwen3-0.6b": (2, 4), "qwen3-1.7b": (2, 4, 8), "qwen3-4b": (2,), "qwen3-8b": (2, 4, 8)}
+
+
+@pytest.mark.parametrize("name", sorted(SUPPORT))
+@pytest.mark.parametrize("size", [2, 4, 8])
+def test_shard_plan_support_matrix(name, size):
+    sh = synthetic.PRESETS[name]
+    shape = dict(n_heads=sh.n_heads, n_kv_heads=sh.n_kv_heads, head_dim=sh.head_dim, ffn=sh.ffn, vocab=sh.vocab)
+    if size in SUPPORT[name]:
+        plans = [shard_plan(shape, r, size) for r in range(size)]
+        assert sum(p["ffn"] for p in plans) == sh.ffn and sum(p["heads"] for p in plans) == sh.n_heads
+    else:
+        with pytest.raises(EngineError):
+            shard_plan(shape, 0, size)
+
+
 def _q(rows, cols, qt, seed):
     w = synthetic.normal(seed, rows * cols, 0.0, 0.02)
     return synthetic.quantize(w, qt).reshape(rows, -1)
