@@ -93,9 +93,9 @@ RPGB_API int32_t rpgb_session_tp_attach(int32_t session, const uint8_t* handles)
 
 /* ------------------------------------------------------------------ session */
 
-/* A session owns an fp16 KV cache of max_seq positions, scratch buffers, a
- * stream and its decode graph (GpuKvCache + GpuScratch,
- * src/kv_cache_gpu.cu:16-36, src/qwen3_gpu.h:79-98). */
+/* A session owns an fp16 KV cache of max_seq positions, scratch buffers and
+ * a stream (GpuKvCache + GpuScratch, src/kv_cache_gpu.cu:16-36,
+ * src/qwen3_gpu.h:79-98). */
 RPGB_API int32_t rpgb_session_create(int32_t model, int64_t max_seq);
 RPGB_API void rpgb_session_free(int32_t session);
 RPGB_API int64_t rpgb_session_len(int32_t session);
@@ -128,13 +128,18 @@ RPGB_API int32_t rpgb_session_stats(int32_t session, int32_t* kernels_per_step, 
  * session's work with CUDA events recorded on that stream. */
 RPGB_API void* rpgb_session_stream(int32_t session);
 
-/* Device timeline of the decode step (no counterpart in the reference, which
- * times whole steps only): every block of every launch recorded in the step
- * graph appends one record {launch index within the step, block, start,
- * ready = after the wait on the previous launch, end}, times in %globaltimer
- * nanoseconds.  trace_enable(cap) sets room for `cap` records (0 = off) and
- * re-records the graph; trace_take copies up to `cap` records into `out`
- * (host memory, 32 bytes each), clears the buffer and returns the count. */
+/* Device timeline of decoding (no counterpart in the reference, which times
+ * whole steps only).  In the decode loop kernel every block writes, per step
+ * phase, a record {launch = step * (5 n_layers + 2) + phase, block, start =
+ * end of the block's previous phase, ready = after the grid barrier where
+ * there is one, end} and up to four mark records inside the phase (block
+ * field | mark << 24, end = time of the mark); times are nanoseconds of the
+ * SM clock anchored to %globaltimer.  In the step graph (other group sizes)
+ * every block of every launch writes {launch index within the step, block,
+ * start, ready = after the wait on the previous launch, end}.
+ * trace_enable(cap) sets room for `cap` records (0 = off); trace_take copies
+ * up to `cap` records into `out` (host memory, 32 bytes each), clears the
+ * buffer and returns the count. */
 typedef struct rpgb_trace_rec {
   uint32_t launch, block;
   uint64_t t_start, t_ready, t_end;
@@ -142,8 +147,9 @@ typedef struct rpgb_trace_rec {
 RPGB_API int32_t rpgb_session_trace_enable(int32_t session, int32_t cap);
 RPGB_API int32_t rpgb_session_trace_take(int32_t session, rpgb_trace_rec* out, int32_t cap);
 
-/* Kernels this library has launched so far in the process, counting every
- * node of a replayed decode graph (instrumentation for benchmarks). */
+/* Kernels this library has launched so far in the process (a decode loop
+ * launch counts once, every node of a replayed step graph once per replay;
+ * instrumentation for benchmarks). */
 RPGB_API int64_t rpgb_launch_count(void);
 
 /* ------------------------------------------------------------------ operators */

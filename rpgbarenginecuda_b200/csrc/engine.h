@@ -1,17 +1,20 @@
-// engine.h -- a decoding session: fp16 KV cache, scratch, stream, decode graph.
+// engine.h -- a decoding session: fp16 KV cache, scratch, stream, decode loop.
 //
 // Reference counterparts: GpuKvCache (src/kv_cache_gpu.h:50-100), GpuScratch
 // (src/qwen3_gpu.h:79-98), GpuForwardFull (src/qwen3_gpu.cu:236-276),
 // GpuGenerate / GenerateGraph / GenerateNoGraph (src/qwen3_gpu.cu:451-640).
 //
 // Differences by design:
-//  * every session owns its stream, position counter and graph (the reference
-//    keeps a process-global stream and pos0 staging), so sessions on several
-//    GPUs run concurrently;
-//  * one decode step = embedding -> 5 fused launches per layer -> lm_head with a
-//    fused argmax (or the sampler), recorded once as a CUDA graph;
+//  * every session owns its stream, position counter and buffers (the
+//    reference keeps a process-global stream and pos0 staging), so sessions on
+//    several GPUs run concurrently;
+//  * a generate call is one cooperative launch of the decode loop kernel
+//    (k_step.cu) that runs every step on the device; the step graph (embedding
+//    -> 5 fused launches per layer -> lm_head with a fused argmax or the
+//    sampler, recorded once as a CUDA graph) remains for group sizes the loop
+//    kernel is not built for and for tensor-parallel sampled decode;
 //  * the sampled token, its position and the position counter never leave the
-//    device inside the loop; the host reads the generated ids once per chunk.
+//    device inside the loop; the host reads the generated ids once per launch.
 #pragma once
 
 #include <cuda_fp16.h>
