@@ -177,7 +177,7 @@ class RefQuant:
 
 
 class RefShim:
-    """The reference engine compiled from its own sources (GPU side needs a GPU)."""
+    """Host functions of the reference engine compiled from its own sources."""
 
     def __init__(self):
         if not os.path.exists(REF_SHIM_SO):
@@ -187,89 +187,15 @@ class RefShim:
             "ref_last_error": (ctypes.c_char_p, []),
             "ref_dequantize_row": (ctypes.c_int, [u32, vp, i64, vp]),
             "ref_counter_uniform": (f32, [u64, u64]),
-            "ref_gpu_dequant": (ctypes.c_int, [u32, vp, i64, vp]),
-            "ref_gpu_matmul": (ctypes.c_int, [u32, vp, i64, i64, vp, i64, vp]),
-            "ref_gpu_sample": (ctypes.c_int, [vp, i64, f32, i32, f32, u64, u64, vp, vp]),
-            "ref_session_open": (ctypes.c_int, [ctypes.c_char_p, i32, i32]),
-            "ref_session_close": (None, [ctypes.c_int]),
-            "ref_session_prefill": (ctypes.c_int, [ctypes.c_int, vp, i64, vp]),
-            "ref_session_generate": (ctypes.c_int, [ctypes.c_int, f32, i32, f32, u64, i32, vp, i32, ctypes.c_int,
-                                                    vp, vp, vp]),
-            "ref_session_len": (i64, [ctypes.c_int]),
         }
         for k, (r, a) in sig.items():
             fn = getattr(L, k)
             fn.restype, fn.argtypes = r, a
         self.L = L
 
-    def _chk(self, rc, what):
-        if rc < 0:
-            raise RuntimeError(f"reference {what}: {self.L.ref_last_error().decode(errors='replace')}")
-        return rc
-
     def counter_uniform(self, seed, counter):
         return float(self.L.ref_counter_uniform(seed, counter))
 
-    def gpu_dequant(self, qtype, data, n):
-        raise RuntimeError(REF_GPU_CLOSED)
-        out = np.empty(n, dtype=np.float32)
-        self._chk(self.L.ref_gpu_dequant(qtype, np.ascontiguousarray(data).ctypes.data, n, out.ctypes.data),
-                  "dequant")
-        return out
-
-    def gpu_matmul(self, qtype, wbytes, rows, cols, x):
-        raise RuntimeError(REF_GPU_CLOSED)
-        x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, cols)
-        out = np.empty((x.shape[0], rows), dtype=np.float32)
-        self._chk(self.L.ref_gpu_matmul(qtype, np.ascontiguousarray(wbytes).ctypes.data, rows, cols,
-                                        x.ctypes.data, x.shape[0], out.ctypes.data), "matmul")
-        return out
-
-    def gpu_sample(self, logits, temperature, top_k, top_p, seed, counter, want_probs=True):
-        raise RuntimeError(REF_GPU_CLOSED)
-        lg = np.ascontiguousarray(logits, dtype=np.float32)
-        probs = np.empty_like(lg) if want_probs else None
-        tok = ctypes.c_int32(-1)
-        self._chk(self.L.ref_gpu_sample(lg.ctypes.data, lg.size, temperature, top_k, top_p, seed, counter,
-                                        _ptr(probs), ctypes.byref(tok)), "sample")
-        return tok.value, probs
-
-    def session(self, path, max_pos=4096, max_seq=4096):
-        raise RuntimeError(REF_GPU_CLOSED)
-        return _RefSession(self, path, max_pos, max_seq)
-
-
-class _RefSession:
-    def __init__(self, shim: RefShim, path, max_pos, max_seq):
-        self.s = shim
-        self.h = shim._chk(shim.L.ref_session_open(path.encode(), max_pos, max_seq), "session_open")
-        self.vocab = None
-
-    def prefill(self, tokens, vocab):
-        toks = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
-        logits = np.empty(vocab, dtype=np.float32)
-        self.vocab = vocab
-        self.s._chk(self.s.L.ref_session_prefill(self.h, toks.ctypes.data, toks.size, logits.ctypes.data),
-                    "prefill")
-        return logits
-
-    def generate(self, temperature=0.0, top_k=0, top_p=1.0, seed=0, max_tokens=32, stop=(), use_graph=False,
-                 step_logits=False):
-        out = np.empty(max_tokens, dtype=np.int32)
-        n = ctypes.c_int32(0)
-        st = np.ascontiguousarray(np.asarray(list(stop), dtype=np.int32))
-        steps = np.empty((max_tokens, self.vocab), dtype=np.float32) if step_logits else None
-        self.s._chk(self.s.L.ref_session_generate(self.h, temperature, top_k, top_p, seed, max_tokens,
-                                                  st.ctypes.data if st.size else None, st.size,
-                                                  1 if use_graph else 0, out.ctypes.data, ctypes.byref(n),
-                                                  _ptr(steps)), "generate")
-        k = n.value
-        return (out[:k].copy(), steps[:k].copy()) if step_logits else out[:k].copy()
-
-    def __len__(self):
-        return int(self.s.L.ref_session_len(self.h))
-
-    def close(self):
-        if self.h is not None:
-            self.s.L.ref_session_close(self.h)
-            self.h = None
+    # The shim's GPU entries (ref_gpu_dequant, ref_gpu_matmul, ref_gpu_sample,
+    # ref_session_*) drive the reference's own GPU code, which is no longer run
+    # (REF_GPU_CLOSED); they are not bound here.

@@ -9,12 +9,10 @@ Criteria (tests/cmp_gen.py:65-90, tools/gen_check.cu:216-283, north star):
   is forwarded, the decode step runs as a recorded graph.
 """
 
-import os
-
 import numpy as np
 import pytest
 
-from oracle.oracle import REF_GPU_CLOSED, REF_SHIM_SO, OracleModel, OracleSession
+from oracle.oracle import OracleModel, OracleSession
 from rpgbarenginecuda_b200 import Model, SampleOptions, Session, synthetic
 
 pytestmark = pytest.mark.gpu
@@ -123,30 +121,6 @@ def test_continue_after_generate(pair):
     two = np.concatenate([b.generate(SampleOptions(0.0, 0, 1.0), 0, 10),
                           b.generate(SampleOptions(0.0, 0, 1.0), 0, 10)])
     assert list(one) == list(two)
-
-
-@pytest.mark.skip(reason=REF_GPU_CLOSED)
-@pytest.mark.skipif(not os.path.exists(REF_SHIM_SO), reason="oracle/_ref not built")
-def test_vs_reference_engine(pair):
-    """Same synthetic GGUF and token ids through the reference's own GPU engine."""
-    from oracle.oracle import RefShim
-
-    m, _ = pair
-    toks = synthetic.seeded_tokens(21, 0, m.vocab)
-    s = Session(m, 512)
-    lg = s.prefill(toks)
-    ids, steps = s.generate(SampleOptions(0.0, 0, 1.0), 0, 32, step_logits=True)
-    rsess = RefShim().session(m.path, 1024, 512)
-    rlg = rsess.prefill(toks, m.vocab)
-    assert full_scale_err(lg, rlg) <= FULL_SCALE
-    rids, rsteps = rsess.generate(0.0, 0, 1.0, 0, 32, step_logits=True)
-    ok, at = tokens_agree(ids, rids, rsteps)
-    assert ok, (at, ids, rids)
-    for i in range(at):
-        assert full_scale_err(steps[i], rsteps[i]) <= FULL_SCALE
-    assert len(rsess) == len(s)
-    rsess.close()
-    s.close()
 
 
 @pytest.mark.parametrize("splits", ["1", "2", "3"])
