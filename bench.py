@@ -1,5 +1,5 @@
 #!/usr/bin/env python3
-"""Benchmark of the token loop on the BASELINE.json configs[1] workload.
+"""Benchmark of the token loop on the 1.7B chat-turn workload (the reference's headline configuration).
 
 One step = one chat turn of the Qwen3-1.7B-shaped Q4_K_M synthetic model:
 a 2811-token seeded prompt prefill, then three rounds of (append 40 seeded
@@ -77,9 +77,6 @@ def parse():
     ap.add_argument("--tp", action="store_true",
                     help="tensor-parallel measurement of the 8B configuration: run under torchrun with N ranks "
                          "(N = 1: the whole model on one GPU); 1024-token prefill + 128 greedy steps per turn")
-    ap.add_argument("--with-ref-gpu", action="store_true",
-                    help="the reference's own CUDA engine on the same turn: closed (it faulted in its own prefill); "
-                         "the line records it as unavailable")
     return ap.parse_args()
 
 
@@ -478,10 +475,6 @@ def ours(args):
         c = cpu_baseline(path)
         cpu = {"value": round(c["decode_tok_s"], 4), "unit": "tok/s", "cores": c["cores"], "kind": "port",
                "sample": c["sample"], "prefill_tok_s": round(c["prefill_tok_s"], 3)}
-    ref_gpu = None
-    if rank == 0 and args.with_ref_gpu:
-        from oracle.oracle import REF_GPU_CLOSED
-        ref_gpu = {"unavailable": REF_GPU_CLOSED}
 
     if rank == 0:
         line = {
@@ -509,8 +502,6 @@ def ours(args):
             line["roofline_matvec"] = roof
         if cpu is not None:
             line["cpu_baseline"] = cpu
-        if ref_gpu is not None:
-            line["reference_gpu"] = ref_gpu
         print(json.dumps(line), flush=True)
     if pg is not None:
         pg.destroy_process_group()

@@ -8,8 +8,18 @@ is measured or shipped.
   (rpg_oracle.c, see rpg_oracle.h for the reference lines each part follows).
 * ``RefQuant`` -- the reference's own src/quant.cc compiled by oracle/Makefile
   (bit-exact dequant pin).
-* ``RefShim`` -- the reference engine compiled from its own sources for
-  sm_100a (GPU golden outputs; needs a GPU).
+* ``RefEmu`` -- the reference engine and sampler, CUDA sources included,
+  compiled by oracle/Makefile for the host CPU against the SIMT emulation
+  layer in oracle/emu: the reference's own outputs with no GPU.
+* ``RefText`` -- the reference's host text layer (tokenizer, chat template,
+  tool parser).
+
+The reference's GPU build is never run: its RopeKernel
+(src/kernels_gpu.cu:598-621) has no bounds check and reads and writes one row
+past the end of its k buffer whenever rows x KV heads x head_dim / 2 is not a
+multiple of 256 (two KV heads and an odd token count) -- the illegal memory
+access it once raised on a B200.  The emulation runs the same code on the
+host with slack after every allocation.
 """
 
 from __future__ import annotations
@@ -22,15 +32,9 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_QUANT_SO = os.path.join(HERE, "_ref", "libref_quant.so")
-REF_SHIM_SO = os.path.join(HERE, "_ref", "libref_shim.so")
-
-# The reference's GPU engine raised an illegal memory access inside its own
-# prefill on a B200 (GpuForwardFull on the tiny-g4 synthetic model, 21 valid
-# token ids, after the same calls had passed in earlier runs), so no
-# reference GPU code (engine, matmul, sampler, dequant kernels) is run from
-# here any more; the shim's host functions (counter_uniform) stay in use.
-REF_GPU_CLOSED = ("the reference's GPU engine raised an illegal memory access in its own prefill "
-                  "(tiny-g4 synthetic model, valid ids); its GPU code is not run again")
+REF_EMU_SO = os.path.join(HERE, "_ref", "libref_emu.so")
+REF_ENGINE_EMU_SO = os.path.join(HERE, "_ref", "librpg_engine_emu.so")
+REF_TEXT_SO = os.path.join(HERE, "_ref", "libref_text.so")
 
 i32, i64, u32, u64, f32, vp = (ctypes.c_int32, ctypes.c_int64, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_float,
                                ctypes.c_void_p)
@@ -176,26 +180,153 @@ class RefQuant:
         return out
 
 
-class RefShim:
-    """Host functions of the reference engine compiled from its own sources."""
+class RefEmu:
+    """The reference engine and sampler compiled for the host (oracle/emu)."""
 
     def __init__(self):
-        if not os.path.exists(REF_SHIM_SO):
-            raise FileNotFoundError(REF_SHIM_SO)
-        L = ctypes.CDLL(REF_SHIM_SO)
+        if not os.path.exists(REF_EMU_SO):
+            raise FileNotFoundError(REF_EMU_SO)
+        L = ctypes.CDLL(REF_EMU_SO)
         sig = {
             "ref_last_error": (ctypes.c_char_p, []),
             "ref_dequantize_row": (ctypes.c_int, [u32, vp, i64, vp]),
+            "ref_kernel_dequant": (ctypes.c_int, [u32, vp, i64, vp]),
             "ref_counter_uniform": (f32, [u64, u64]),
+            "ref_matmul": (ctypes.c_int, [u32, vp, i64, i64, vp, i64, vp]),
+            "ref_sample": (ctypes.c_int, [vp, i64, f32, i32, f32, u64, u64, vp, vp]),
+            "ref_session_open": (ctypes.c_int, [ctypes.c_char_p, i32, i32]),
+            "ref_session_close": (None, [ctypes.c_int]),
+            "ref_session_prefill": (ctypes.c_int, [ctypes.c_int, vp, i64, vp, vp]),
+            "ref_session_generate": (ctypes.c_int, [ctypes.c_int, f32, i32, f32, u64, i32, vp, i32, vp, vp, vp]),
+            "ref_session_len": (i64, [ctypes.c_int]),
         }
         for k, (r, a) in sig.items():
             fn = getattr(L, k)
             fn.restype, fn.argtypes = r, a
         self.L = L
 
-    def counter_uniform(self, seed, counter):
+    def _check(self, rc):
+        if rc != 0:
+            raise RuntimeError(self.L.ref_last_error().decode(errors="replace"))
+
+    def counter_uniform(self, seed, counter) -> float:
         return float(self.L.ref_counter_uniform(seed, counter))
 
-    # The shim's GPU entries (ref_gpu_dequant, ref_gpu_matmul, ref_gpu_sample,
-    # ref_session_*) drive the reference's own GPU code, which is no longer run
-    # (REF_GPU_CLOSED); they are not bound here.
+    def kernel_dequant(self, qtype, data, n) -> np.ndarray:
+        out = np.empty(n, dtype=np.float32)
+        self._check(self.L.ref_kernel_dequant(qtype, np.ascontiguousarray(data).ctypes.data, n, out.ctypes.data))
+        return out
+
+    def matmul(self, qtype, wbytes, rows, cols, x) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, cols)
+        out = np.empty((x.shape[0], rows), dtype=np.float32)
+        self._check(self.L.ref_matmul(qtype, np.ascontiguousarray(wbytes).ctypes.data, rows, cols, x.ctypes.data,
+                                      x.shape[0], out.ctypes.data))
+        return out
+
+    def sample(self, logits, temperature, top_k, top_p, seed, counter, want_probs=False):
+        lg = np.ascontiguousarray(logits, dtype=np.float32)
+        probs = np.empty_like(lg) if want_probs else None
+        tok = ctypes.c_int32(-1)
+        self._check(self.L.ref_sample(lg.ctypes.data, lg.size, temperature, top_k, top_p, seed, counter, _ptr(probs),
+                                      ctypes.byref(tok)))
+        return tok.value, probs
+
+    def session(self, gguf_path, max_pos, max_seq):
+        return RefEmuSession(self, gguf_path, max_pos, max_seq)
+
+
+class RefEmuSession:
+    def __init__(self, ref: RefEmu, gguf_path: str, max_pos: int, max_seq: int):
+        self.r = ref
+        self.h = ref.L.ref_session_open(gguf_path.encode(), max_pos, max_seq)
+        if self.h <= 0:
+            raise RuntimeError(ref.L.ref_last_error().decode(errors="replace"))
+
+    def __len__(self):
+        return int(self.r.L.ref_session_len(self.h))
+
+    def prefill(self, tokens, vocab, n_layers=None, hidden=None):
+        toks = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        lg = np.empty(vocab, dtype=np.float32)
+        hid = None
+        if n_layers is not None:
+            hid = np.empty((n_layers + 1, toks.size, hidden), dtype=np.float32)
+        self.r._check(self.r.L.ref_session_prefill(self.h, toks.ctypes.data, toks.size, lg.ctypes.data, _ptr(hid)))
+        return (lg, hid) if hid is not None else lg
+
+    def generate(self, temperature, top_k, top_p, seed, max_tokens, vocab, stop=(), step_logits=False):
+        out = np.empty(max_tokens, dtype=np.int32)
+        n = ctypes.c_int32(0)
+        st = np.ascontiguousarray(np.asarray(list(stop), dtype=np.int32))
+        steps = np.empty((max_tokens, vocab), dtype=np.float32) if step_logits else None
+        self.r._check(self.r.L.ref_session_generate(self.h, temperature, top_k, top_p, seed, max_tokens,
+                                                    st.ctypes.data if st.size else None, st.size, out.ctypes.data,
+                                                    ctypes.byref(n), _ptr(steps)))
+        k = n.value
+        return (out[:k].copy(), steps[:k].copy()) if step_logits else out[:k].copy()
+
+    def close(self):
+        if self.h > 0:
+            self.r.L.ref_session_close(self.h)
+            self.h = 0
+
+
+class RefText:
+    """The reference's host text layer (tokenizer, ChatML template, tool parser)."""
+
+    def __init__(self, gguf_path: str):
+        if not os.path.exists(REF_TEXT_SO):
+            raise FileNotFoundError(REF_TEXT_SO)
+        L = ctypes.CDLL(REF_TEXT_SO)
+        sig = {
+            "reft_last_error": (ctypes.c_char_p, []),
+            "reft_free": (None, [vp]),
+            "reft_open": (vp, [ctypes.c_char_p]),
+            "reft_close": (None, [vp]),
+            "reft_encode": (i64, [vp, ctypes.c_char_p, i64, ctypes.c_int, vp, i64]),
+            "reft_decode": (vp, [vp, vp, i64, ctypes.c_int, ctypes.POINTER(i64)]),
+            "reft_render": (vp, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_int, ctypes.c_int]),
+            "reft_parse": (vp, [ctypes.c_char_p, i64]),
+        }
+        for k, (r, a) in sig.items():
+            fn = getattr(L, k)
+            fn.restype, fn.argtypes = r, a
+        self.L = L
+        self.h = L.reft_open(gguf_path.encode())
+        if not self.h:
+            raise RuntimeError(L.reft_last_error().decode(errors="replace"))
+
+    def _take(self, p, n=None) -> bytes:
+        if not p:
+            raise RuntimeError(self.L.reft_last_error().decode(errors="replace"))
+        b = ctypes.string_at(p, n) if n is not None else ctypes.string_at(p)
+        self.L.reft_free(p)
+        return b
+
+    def encode(self, text: bytes, parse_special=True) -> list:
+        cap = 4 * len(text) + 16
+        out = np.empty(cap, dtype=np.int32)
+        n = self.L.reft_encode(self.h, text, len(text), int(parse_special), out.ctypes.data, cap)
+        if n < 0:
+            raise RuntimeError(self.L.reft_last_error().decode(errors="replace"))
+        return [int(v) for v in out[:n]]
+
+    def decode(self, ids, skip_special=False) -> bytes:
+        a = np.ascontiguousarray(np.asarray(ids, dtype=np.int32))
+        n = i64(0)
+        p = self.L.reft_decode(self.h, a.ctypes.data if a.size else None, a.size, int(skip_special), ctypes.byref(n))
+        return self._take(p, n.value)
+
+    def render(self, messages_json: str, tools_json=None, add_generation_prompt=True, enable_thinking=True) -> bytes:
+        p = self.L.reft_render(messages_json.encode(), tools_json.encode() if tools_json is not None else None,
+                               int(add_generation_prompt), int(enable_thinking))
+        return self._take(p)
+
+    def parse(self, raw: bytes) -> str:
+        return self._take(self.L.reft_parse(raw, len(raw))).decode()
+
+    def close(self):
+        if self.h:
+            self.L.reft_close(self.h)
+            self.h = None

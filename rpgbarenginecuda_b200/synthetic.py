@@ -50,7 +50,7 @@ class ModelShape:
 
     def weight_bytes_per_token(self) -> int:
         """Quantised bytes one decode step streams: every layer matrix, the tied
-        lm_head and the f32 norms (SURVEY 8(d) formula)."""
+        lm_head and the f32 norms."""
         q4 = lambda m, k: m * k // 256 * 144  # noqa: E731
         q6 = lambda m, k: m * k // 256 * 210  # noqa: E731
         total = 0
@@ -161,7 +161,7 @@ def normal(seed: int, n: int, mean: float = 0.0, std: float = 1.0, offset: int =
 
 
 def seeded_tokens(n: int, seed: int, vocab: int = 151936) -> np.ndarray:
-    """Token ids drawn uniformly from [0, vocab) (BASELINE prompts)."""
+    """Token ids drawn uniformly from [0, vocab) (the seeded benchmark prompts)."""
     rng = np.random.Generator(np.random.PCG64(seed))
     return rng.integers(0, vocab, size=n, dtype=np.int64).astype(np.int32)
 

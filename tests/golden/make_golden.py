@@ -22,7 +22,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
 
-from oracle.oracle import RefQuant, RefShim  # noqa: E402
+from oracle.oracle import RefEmu, RefQuant  # noqa: E402
 from rpgbarenginecuda_b200 import synthetic  # noqa: E402
 
 SEEDS = [0, 11, 12, 22, 2 ** 63 + 5, 2 ** 64 - 1]
@@ -44,7 +44,7 @@ def blocks(code, blk, n_blocks, seed):
 
 
 def main():
-    rq, rs = RefQuant(), RefShim()
+    rq, rs = RefQuant(), RefEmu()
     out = {}
     for code, blk in ((12, 144), (14, 210)):
         b = blocks(code, blk, 32, 5)

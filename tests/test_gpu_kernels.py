@@ -3,7 +3,7 @@
 Mirrors tools/dequant_check.cu (0 differing bits vs src/quant.cc) and
 tools/matmul_bench.cu --verify (matmul outputs), with the CPU oracle and the
 reference's own GpuMatMulQuant (built from its sources) as checkers.  The
-operator sweep shapes are BASELINE.json configs[4].
+operator sweep shapes are the Q4_K/Q6_K matrices of the 1.7B and 4B models.
 """
 
 import numpy as np

@@ -1,6 +1,6 @@
 """Pins the CPU oracle to the reference's own code (no GPU needed).
 
-Reference checks restated here (SURVEY 4 / reference tests):
+Reference checks restated here (the reference's own tests):
 * dequant bit-exact vs src/quant.cc::DequantizeRow (tools/dequant_check.cu:75-125);
 * exhaustive f16 -> f32 sweep vs src/dtypes.h::F16ToF32 (tools/dequant_check.cu:186-210);
 * counter RNG u table bit-exact vs DevCounterUniform (tools/sample_check.cu:228,
@@ -14,11 +14,11 @@ import os
 import numpy as np
 import pytest
 
-from oracle.oracle import REF_QUANT_SO, REF_SHIM_SO, Oracle, RefQuant
+from oracle.oracle import REF_EMU_SO, REF_QUANT_SO, Oracle, RefQuant
 from rpgbarenginecuda_b200 import synthetic
 
 needs_ref_quant = pytest.mark.skipif(not os.path.exists(REF_QUANT_SO), reason="oracle/_ref not built")
-needs_ref_shim = pytest.mark.skipif(not os.path.exists(REF_SHIM_SO), reason="oracle/_ref not built")
+needs_ref_emu = pytest.mark.skipif(not os.path.exists(REF_EMU_SO), reason="oracle/_ref not built")
 
 
 @needs_ref_quant
@@ -74,11 +74,11 @@ def test_f32_to_f16_is_round_to_nearest_even(oracle):
     assert np.array_equal(ours, vals.astype(np.float16).view(np.uint16))
 
 
-@needs_ref_shim
+@needs_ref_emu
 def test_counter_uniform_bitexact_vs_reference():
-    from oracle.oracle import RefShim
+    from oracle.oracle import RefEmu
 
-    o, rs = Oracle(), RefShim()
+    o, rs = Oracle(), RefEmu()
     for seed in (0, 11, 12, 22, 2 ** 63 + 5, 2 ** 64 - 1):
         for c in list(range(64)) + [4095, 151935, 2 ** 40 + 3]:
             assert o.counter_uniform(seed, c) == rs.counter_uniform(seed, c)
