@@ -198,6 +198,36 @@ RPGB_API int32_t rpgb_sample_noalloc(const float* logits_dev, int32_t n, const r
 /* u = H(seed, counter) in [0, 1) (DevCounterUniform, src/sampler_gpu.cu:364). */
 RPGB_API float rpgb_counter_uniform(uint64_t seed, uint64_t counter);
 
+/* ------------------------------------------------------------------ text layer
+ *
+ * The host text layer rpg_engine_generate runs, without a GPU: the same token
+ * ids, prompt and parse a request turns into.  Errors return NULL / -1 with
+ * the text in rpg_engine_last_error(); strings are freed with
+ * rpg_engine_free(). */
+
+/* Tokenizer of a GGUF (Tokenizer::FromGguf, src/tokenizer.cc:132-200). */
+RPGB_API void* rpgb_text_open(const char* gguf_path);
+RPGB_API void rpgb_text_close(void* text);
+
+/* Token ids of len bytes of text, special tokens matched when parse_special
+ * (Tokenizer::Encode, src/tokenizer.cc:314); writes up to cap ids, returns
+ * the full count. */
+RPGB_API int64_t rpgb_text_encode(void* text, const char* bytes, int64_t len, int32_t parse_special, int32_t* out,
+                                  int64_t cap);
+
+/* Bytes of ids, specials kept (Tokenizer::Decode, src/tokenizer.cc:353);
+ * *out_len receives the length (the bytes may hold NUL). */
+RPGB_API char* rpgb_text_decode(void* text, const int32_t* ids, int64_t n, int64_t* out_len);
+
+/* The ChatML prompt of a generate request's messages / tools /
+ * enable_thinking (ParseMessages + RenderChatml, src/chat_template.cc:85-206). */
+RPGB_API char* rpgb_text_render(const char* request_json);
+
+/* The parse of raw model output (ParseModelOutput, src/tool_parser.cc:125-178)
+ * as JSON: {text, tool_calls: [{name, arguments}], unterminated_think,
+ * unterminated_tool_call}. */
+RPGB_API char* rpgb_text_parse(const char* raw, int64_t len);
+
 #ifdef __cplusplus
 }
 #endif

@@ -247,3 +247,50 @@ def launch_count() -> int:
 
 def counter_uniform(seed: int, counter: int) -> float:
     return float(load_engine().rpgb_counter_uniform(seed, counter))
+
+
+class TextLayer:
+    """The host text layer of rpg_engine_generate (tokenizer, ChatML prompt,
+    output parse) over a GGUF's tokenizer; runs on the CPU."""
+
+    def __init__(self, gguf_path: str):
+        self.L = load_engine()
+        self.h = self.L.rpgb_text_open(gguf_path.encode())
+        if not self.h:
+            raise EngineError(f"text layer: {self._err()}")
+
+    def _err(self) -> str:
+        m = self.L.rpg_engine_last_error()
+        return m.decode(errors="replace") if m else ""
+
+    def _take(self, p, n=None) -> bytes:
+        if not p:
+            raise EngineError(f"text layer: {self._err()}")
+        b = ctypes.string_at(p, n) if n is not None else ctypes.string_at(p)
+        self.L.rpg_engine_free(p)
+        return b
+
+    def encode(self, text: bytes, parse_special: bool = True) -> list:
+        cap = 4 * len(text) + 16
+        out = np.empty(cap, dtype=np.int32)
+        n = self.L.rpgb_text_encode(self.h, text, len(text), int(parse_special), out.ctypes.data, cap)
+        if n < 0:
+            raise EngineError(f"text layer: {self._err()}")
+        return [int(v) for v in out[:n]]
+
+    def decode(self, ids) -> bytes:
+        a = np.ascontiguousarray(np.asarray(ids, dtype=np.int32))
+        n = ctypes.c_int64(0)
+        return self._take(self.L.rpgb_text_decode(self.h, a.ctypes.data if a.size else None, a.size,
+                                                  ctypes.byref(n)), n.value)
+
+    def render(self, request_json: str) -> bytes:
+        return self._take(self.L.rpgb_text_render(request_json.encode()))
+
+    def parse(self, raw: bytes) -> str:
+        return self._take(self.L.rpgb_text_parse(raw, len(raw))).decode()
+
+    def close(self):
+        if self.h:
+            self.L.rpgb_text_close(self.h)
+            self.h = None

@@ -62,6 +62,12 @@ _SIGS = {
     "rpgb_sample": (c_i32, [c_p, c_i32, ctypes.POINTER(SampleOptions), c_u64, c_u64, c_p, c_p, c_p]),
     "rpgb_sample_noalloc": (c_i32, [c_p, c_i32, ctypes.POINTER(SampleOptions), c_u64, c_u64, c_p, c_p]),
     "rpgb_counter_uniform": (c_f32, [c_u64, c_u64]),
+    "rpgb_text_open": (c_p, [ctypes.c_char_p]),
+    "rpgb_text_close": (None, [c_p]),
+    "rpgb_text_encode": (c_i64, [c_p, ctypes.c_char_p, c_i64, c_i32, c_p, c_i64]),
+    "rpgb_text_decode": (c_p, [c_p, c_p, c_i64, ctypes.POINTER(c_i64)]),
+    "rpgb_text_render": (c_p, [ctypes.c_char_p]),
+    "rpgb_text_parse": (c_p, [ctypes.c_char_p, c_i64]),
     # the public ten-function ABI (include/rpg_engine.h)
     "rpg_engine_version": (ctypes.c_char_p, []),
     "rpg_engine_last_error": (ctypes.c_char_p, []),

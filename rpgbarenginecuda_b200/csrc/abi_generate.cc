@@ -592,16 +592,37 @@ void AddStop(const Tokenizer& tok, const std::string& s, std::vector<int32_t>* i
 
 }  // namespace
 
+std::string RenderRequestPrompt(const Json& req) {
+  const std::vector<Message> msgs = ParseMessages(req.Get("messages"));
+  RPGB_CHECK(!msgs.empty(), "messages is empty: at least one message is required");
+  const Json tools = req.Get("tools").IsArray() ? req.Get("tools") : Json::Array();
+  const bool thinking = req.Get("enable_thinking").AsBool(true);
+  return RenderChatml(msgs, tools, thinking);
+}
+
+Json ParseOutputJson(const std::string& raw) {
+  const Parsed p = ParseOutput(raw);
+  Json o = Json::Object();
+  o.Set("text", Json::Str(p.text));
+  Json calls = Json::Array();
+  for (const ParsedCall& pc : p.calls) {
+    Json one = Json::Object();
+    one.Set("name", Json::Str(pc.name));
+    one.Set("arguments", pc.ok ? pc.arguments : Json());
+    calls.Push(one);
+  }
+  o.Set("tool_calls", calls);
+  o.Set("unterminated_think", Json::Bool(p.open_think));
+  o.Set("unterminated_tool_call", Json::Bool(p.open_call));
+  return o;
+}
+
 std::string RunGenerate(const GenerateState& st, const Json& req) {
   Session& sess = *st.sess;
   const Tokenizer& tok = *st.tok;
   const ModelMeta& c = sess.model().meta();
 
-  const std::vector<Message> msgs = ParseMessages(req.Get("messages"));
-  RPGB_CHECK(!msgs.empty(), "messages is empty: at least one message is required");
-  const Json tools = req.Get("tools").IsArray() ? req.Get("tools") : Json::Array();
-  const bool thinking = req.Get("enable_thinking").AsBool(true);
-  const std::string prompt = RenderChatml(msgs, tools, thinking);
+  const std::string prompt = RenderRequestPrompt(req);
   std::vector<int32_t> ids = tok.Encode(prompt, true);
   if (c.add_bos && c.bos_id >= 0) ids.insert(ids.begin(), c.bos_id);
   const int64_t total = static_cast<int64_t>(ids.size());

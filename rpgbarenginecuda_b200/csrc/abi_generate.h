@@ -40,4 +40,13 @@ struct GenerateState {
 // Runs one rpg_engine_generate request; returns the response JSON text.
 std::string RunGenerate(const GenerateState& st, const Json& req);
 
+// The ChatML prompt rpg_engine_generate renders for a request (its messages,
+// tools and enable_thinking keys).
+std::string RenderRequestPrompt(const Json& req);
+
+// The model-output parse rpg_engine_generate applies to the decoded text:
+// {text, tool_calls: [{name, arguments (object or null)}],
+// unterminated_think, unterminated_tool_call}.
+Json ParseOutputJson(const std::string& raw);
+
 }  // namespace rpgb

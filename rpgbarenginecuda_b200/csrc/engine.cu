@@ -197,6 +197,7 @@ Session::~Session() {
   cudaFree(pf_arena_);
   cudaFree(trace_rec_);
   cudaFree(trace_count_);
+  cudaFree(step_logits_dev_);
   if (host_ids_ != nullptr) cudaFreeHost(host_ids_);
   if (loop_host_ != nullptr) cudaFreeHost(loop_host_);
   if (stream_ != nullptr) cudaStreamDestroy(stream_);
@@ -216,6 +217,7 @@ void Session::EnableTrace(int32_t cap) {
   DropGraph();
   cudaFree(trace_rec_);
   cudaFree(trace_count_);
+  cudaFree(step_logits_dev_);
   trace_rec_ = nullptr;
   trace_count_ = nullptr;
   trace_cap_ = 0;
@@ -850,7 +852,19 @@ int Session::GenerateLoop(const SampleOpts& opt, uint64_t seed, int32_t max_toke
   }
   lp.n_stop = dev_stop ? n_stop : 0;
   // With stop ids the device cannot see, chunks stay short so little work runs past a stop.
-  const int chunk = step_logits != nullptr ? 1 : (dev_stop ? max_tokens : 8);
+  const int chunk = dev_stop ? max_tokens : 8;
+  if (step_logits != nullptr) {
+    // every step's logits row is kept on the device and copied after the
+    // launch, so the launch runs the same steps as without them
+    if (step_logits_cap_ < chunk) {
+      cudaFree(step_logits_dev_);
+      step_logits_dev_ = nullptr;
+      step_logits_cap_ = 0;
+      RPGB_CUDA(cudaMalloc(&step_logits_dev_, sizeof(float) * static_cast<size_t>(chunk) * c.vocab));
+      step_logits_cap_ = chunk;
+    }
+    lp.step_logits = step_logits_dev_;
+  }
   int produced = 0, launched = 0;
   bool stopped = false;
   while (produced < max_tokens && !stopped) {
@@ -872,10 +886,6 @@ int Session::GenerateLoop(const SampleOpts& opt, uint64_t seed, int32_t max_toke
     LaunchDecodeLoop(lp, c.group(), m_->num_sms(), s);
     if (lp.tp > 0) GatherLogits(s);  // the next call samples its first token from the whole row
     loop_ready_ = true;
-    if (step_logits != nullptr && produced + 1 < max_tokens) {
-      RPGB_CUDA(cudaMemcpyAsync(step_logits + static_cast<int64_t>(produced + 1) * c.vocab, logits_,
-                                sizeof(float) * c.vocab, cudaMemcpyDeviceToHost, s));
-    }
     RPGB_CUDA(cudaMemcpyAsync(loop_host_, steps_done_, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
     RPGB_CUDA(cudaMemcpyAsync(host_ids_ + produced, out_ids_ + start + produced, sizeof(int32_t) * todo,
                               cudaMemcpyDeviceToHost, s));
@@ -901,6 +911,14 @@ int Session::GenerateLoop(const SampleOpts& opt, uint64_t seed, int32_t max_toke
         take = i + 1;
         stopped = true;
         break;
+      }
+    }
+    if (step_logits != nullptr) {
+      // launch step i forwarded token produced + i; its logits choose token produced + i + 1
+      const int rows = std::min(take, max_tokens - produced - 1);
+      if (rows > 0) {
+        RPGB_CUDA(cudaMemcpy(step_logits + static_cast<int64_t>(produced + 1) * c.vocab, step_logits_dev_,
+                             sizeof(float) * static_cast<size_t>(rows) * c.vocab, cudaMemcpyDeviceToHost));
       }
     }
     produced += take;

@@ -130,6 +130,8 @@ class Session {
   int32_t* steps_done_ = nullptr;
   int32_t* stop_dev_ = nullptr;   // [kLoopMaxStop]
   int32_t* loop_host_ = nullptr;  // pinned: steps done
+  float* step_logits_dev_ = nullptr;  // [cap][vocab]: per-step logits of a loop launch (parity checks)
+  int64_t step_logits_cap_ = 0;
   int loop_splits_ = 1;
   bool loop_ready_ = false;
   uint64_t* ll_ = nullptr;  // tagged words (x, qkv, ffn activation, attention records, merged attention)

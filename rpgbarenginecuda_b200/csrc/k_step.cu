@@ -870,6 +870,7 @@ __device__ void MvPhase(const LoopParams& p, const GeoTable& gt, int kind, int l
       StLL(p.llh + (row >> 1), (v / (1.0f + expf(-v))) * v2, tag_out);
     } else if (row < p.lm_head.rows) {
       p.logits[p.vocab0 + row] = v;
+      if (p.step_logits != nullptr) p.step_logits[static_cast<int64_t>(step) * p.vocab + p.vocab0 + row] = v;
       if (p.mode == 0) {
         if (v > best_v) {  // rows increase per thread: strict > keeps the lowest index
           best_v = v;

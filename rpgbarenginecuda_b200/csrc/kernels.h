@@ -224,6 +224,9 @@ struct LoopParams {
   uint32_t* tickets = nullptr;    // [n_kv]: blocks of each head done with the attention phase
   uint32_t epoch0 = 1;  // tags of this launch start above it; strictly increasing across launches
   float *logits = nullptr, *probs = nullptr;
+  // optional [n_steps][vocab]: step i's logits row is also stored at
+  // step_logits + i * vocab (parity checks of multi-step launches)
+  float* step_logits = nullptr;
   int64_t* pos = nullptr;
   int32_t* tok = nullptr;
   int32_t* out_ids = nullptr;

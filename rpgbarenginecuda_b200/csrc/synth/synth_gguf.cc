@@ -405,6 +405,10 @@ struct rpgs_config {
   uint64_t seed;
   // Q6_K for attn_v / ffn_down on layers with (layer % 2 == q6k_parity); Q4_K otherwise.
   int32_t q6k_parity;
+  // standard deviations of the weights and of the norms around 1 (0: the
+  // defaults 0.02 and 0.05)
+  float weight_std;
+  float norm_std;
 };
 
 int rpgs_quantize_q4k(const float* x, int64_t n, uint8_t* out) {
@@ -562,7 +566,8 @@ int rpgs_write_qwen3_gguf(const char* path, const rpgs_config* cfg, char* err, i
       std::vector<float> row(static_cast<size_t>(t.cols));
       for (int64_t r = tid; r < t.rows; r += nthreads) {
         const float mean = t.kind == 1 ? 1.0f : 0.0f;
-        const float stdv = t.kind == 1 ? 0.05f : 0.02f;
+        const float stdv = t.kind == 1 ? (c.norm_std > 0.0f ? c.norm_std : 0.05f)
+                                       : (c.weight_std > 0.0f ? c.weight_std : 0.02f);
         FillNormal(key, r * t.cols, t.cols, mean, stdv, row.data());
         uint8_t* dst = data.data() + static_cast<uint64_t>(r) * rb;
         if (t.type == kTypeF32) {

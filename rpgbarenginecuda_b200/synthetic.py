@@ -39,6 +39,8 @@ class ModelShape:
     context: int = 4096
     rope_theta: float = 1e6
     rms_eps: float = 1e-6
+    weight_std: float = 0.02
+    norm_std: float = 0.05
 
     @property
     def q_dim(self) -> int:
@@ -95,6 +97,8 @@ class _Cfg(ctypes.Structure):
         ("rms_eps", ctypes.c_float),
         ("seed", ctypes.c_uint64),
         ("q6k_parity", ctypes.c_int32),
+        ("weight_std", ctypes.c_float),
+        ("norm_std", ctypes.c_float),
     ]
 
 
@@ -122,7 +126,7 @@ def write_model(path: str, model="qwen3-1.7b", seed: int = 0, **overrides) -> st
     """Writes a synthetic GGUF for ``model`` (preset name or ModelShape)."""
     s = replace(shape(model), **overrides) if overrides else shape(model)
     cfg = _Cfg(s.n_layers, s.hidden, s.ffn, s.n_heads, s.n_kv_heads, s.head_dim, s.vocab, s.context,
-               s.rope_theta, s.rms_eps, seed, 0)
+               s.rope_theta, s.rms_eps, seed, 0, s.weight_std, s.norm_std)
     err = ctypes.create_string_buffer(256)
     rc = _synth().rpgs_write_qwen3_gguf(path.encode(), ctypes.byref(cfg), err, 256)
     if rc != 0:
@@ -135,7 +139,7 @@ def cached_model(model="qwen3-1.7b", seed: int = 0, cache_dir: str | None = None
     s = shape(model)
     cache_dir = cache_dir or os.environ.get("RPGB_MODEL_CACHE", "/tmp/rpgb_models")
     os.makedirs(cache_dir, exist_ok=True)
-    path = os.path.join(cache_dir, f"{s.name}-L{s.n_layers}-H{s.hidden}-s{seed}.gguf")
+    path = os.path.join(cache_dir, f"{s.name}-L{s.n_layers}-H{s.hidden}-w{s.weight_std:g}-n{s.norm_std:g}-s{seed}.gguf")
     if not os.path.exists(path):
         tmp = path + f".tmp{os.getpid()}"
         write_model(tmp, s, seed)
