@@ -148,8 +148,12 @@ def dist():
     return world, rank, local
 
 
-def cpu_baseline(path, n_prompt=64, n_decode=8):
-    """The oracle (CPU restatement of the reference loop) on all host cores, bounded sample."""
+def cpu_baseline(path, n_prompt=64, n_decode=8, ctx=None):
+    """The oracle (CPU restatement of the reference loop) on all host cores, bounded
+    sample.  With ctx, the prompt is prefilled at positions ctx - n_prompt ..
+    ctx - 1, so the decode steps attend over ctx positions as the benchmark's
+    do (the KV rows below the prompt are zero-filled: the work per step is
+    that of a full context, the values are not)."""
     from oracle.oracle import OracleModel, OracleSession
     from rpgbarenginecuda_b200 import synthetic
 
@@ -157,6 +161,8 @@ def cpu_baseline(path, n_prompt=64, n_decode=8):
     om = OracleModel(path, 4096)
     s = OracleSession(om, 4096, cores)
     prompt = synthetic.seeded_tokens(n_prompt, 0, om.vocab)
+    if ctx is not None:
+        s.set_len(ctx - n_prompt)
     t0 = time.perf_counter()
     s.prefill(prompt)
     t1 = time.perf_counter()
@@ -164,8 +170,10 @@ def cpu_baseline(path, n_prompt=64, n_decode=8):
     t2 = time.perf_counter()
     s.close()
     om.close()
+    where = f" at context {ctx}" if ctx is not None else ""
     return {"decode_tok_s": n_decode / (t2 - t1), "prefill_tok_s": n_prompt / (t1 - t0), "cores": cores,
-            "sample": f"{n_prompt}-token prefill + {n_decode}-token decode (T=0.7,k=20,p=0.8) of the {MODEL} turn",
+            "sample": f"{n_prompt}-token prefill + {n_decode}-token decode (T=0.7,k=20,p=0.8){where} of the "
+                      f"{MODEL} turn (the builder's C port of the reference loop, oracle/rpg_oracle.c)",
             "seconds": t2 - t0}
 
 
@@ -178,7 +186,7 @@ def reference_arm(args):
     path = synthetic.cached_model(args.model, seed=0)
     vals, pre = [], []
     for i in range(args.warmup + args.steps):
-        r = cpu_baseline(path, 32, 4)
+        r = cpu_baseline(path, 8, 4, ctx=PROMPT_LEN + APPEND)
         if i >= args.warmup:
             vals.append(r["decode_tok_s"])
             pre.append(r["prefill_tok_s"])
@@ -188,10 +196,11 @@ def reference_arm(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000.0 * 4 / v, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "prefill_tok_s": round(statistics.mean(pre), 4),
-        "config": {"workload": f"{MODEL} turn sample: 32-token prefill + 4-token decode per step, "
-                               "T=0.7 top_k=20 top_p=0.8", "model": args.model},
+        "config": {"workload": f"{MODEL} turn sample: 4-token decode at context {PROMPT_LEN + APPEND} per step "
+                               "(after an 8-token prefill), T=0.7 top_k=20 top_p=0.8", "model": args.model},
         "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
-                         "sample": "32-token prefill + 4-token decode per step (the reference's CPU engine "
+                         "sample": f"4-token decode at context {PROMPT_LEN + APPEND} per step, by the builder's C "
+                                   "port of the reference loop (oracle/rpg_oracle.c; the reference's CPU engine "
                                    "tools/cpu_ref_gen links sources that are not vendored)"},
         "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -472,7 +481,7 @@ def ours(args):
         roof["peak_kind"] = kind
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        c = cpu_baseline(path)
+        c = cpu_baseline(path, 16, 8, ctx=PROMPT_LEN + APPEND)
         cpu = {"value": round(c["decode_tok_s"], 4), "unit": "tok/s", "cores": c["cores"], "kind": "port",
                "sample": c["sample"], "prefill_tok_s": round(c["prefill_tok_s"], 3)}
 
@@ -489,8 +498,10 @@ def ours(args):
                        "parallelism": f"sessions x{world}",
                        "l2": "inputs larger than L2 (1.1 GB of weights streamed per token)"},
             "e2e": {"value": round(e2e, 2), "unit": "tok/s",
-                    "h2d_bytes_per_step": 4 * (PROMPT_LEN + ROUNDS * APPEND) + 8 * (1 + 2 * ROUNDS),
-                    "d2h_bytes_per_step": 4 * ROUNDS * DECODE},
+                    # copies of the timed generate calls: the start position in,
+                    # the step count, error word and generated ids out
+                    "h2d_bytes_per_step": 8 * ROUNDS,
+                    "d2h_bytes_per_step": ROUNDS * (8 + 4 * DECODE)},
             "gpu_launches": int(launches),
             "kernels_per_decode_step": stats["kernels_per_step"],
             "wall_s": round(wall, 3),

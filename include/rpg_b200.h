@@ -186,11 +186,14 @@ RPGB_API int32_t rpgb_sample(const float* logits_dev, int32_t n, const rpgb_samp
  * cudaFree synchronise the whole device), or a process whose GPU memory is
  * already fully owned by another allocator's pool.  Same sampling as
  * rpgb_sample with probs_dev == NULL; its scratch is a fixed array inside the
- * library (about 1.1 MiB, held on every GPU that loads the library), so n must
- * not exceed RPGB_SAMPLE_NOALLOC_MAX_VOCAB.  All calls on a device share that
- * array: calls whose GPU work overlaps race and must be serialised.  The first
- * call on a device looks up the array's address and should come before any
- * stream capture begins. */
+ * library (about 1.1 MiB), so n must not exceed RPGB_SAMPLE_NOALLOC_MAX_VOCAB.
+ * CUDA loads the library's code lazily: the array is placed on a GPU by the
+ * first call on that device (or when the context starts, with
+ * CUDA_MODULE_LOADING=EAGER) and held until the process exits, so make one
+ * call per device at set-up, before the GPU's memory is handed to another
+ * allocator and before any stream capture begins.  All calls on a device
+ * share the array: calls whose GPU work overlaps race and must be
+ * serialised. */
 #define RPGB_SAMPLE_NOALLOC_MAX_VOCAB 262144
 RPGB_API int32_t rpgb_sample_noalloc(const float* logits_dev, int32_t n, const rpgb_sample_options* opt,
                                      uint64_t seed, uint64_t counter, int32_t* out_tok_dev, void* stream);

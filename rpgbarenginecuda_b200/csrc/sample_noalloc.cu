@@ -12,12 +12,20 @@
 //
 // Limits and sharing rules:
 //  * vocabulary size n <= kNoAllocMaxVocab (262144); larger n is rejected;
-//  * the scratch array (about 1.1 MiB) is held on every GPU that loads this
-//    library until the process exits;
+//  * the scratch array (about 1.1 MiB) belongs to this file's code module.
+//    CUDA loads modules lazily by default, so the array is placed on a GPU
+//    when the first call on that device looks up its address (and the sampler
+//    kernels' module with it); from then on it is held until the process
+//    exits.  With CUDA_MODULE_LOADING=EAGER it is placed when the library's
+//    context starts instead.  A host whose GPU memory will later belong to
+//    another allocator should make one call per device at set-up;
 //  * every call on a device uses the same array and leaves its contents
-//    behind; the flag that must start at zero is cleared by each call.  Two
-//    calls whose GPU work overlaps (different streams, or another thread)
-//    race on the array and may return wrong tokens -- serialise them;
+//    behind.  Nothing in it needs to start at zero: the candidate kernel
+//    writes every count it reads and the small sampler kernel always writes
+//    the fast-path flag before the general kernel reads it (the flag is also
+//    cleared up front, defensively).  Two calls whose GPU work overlaps
+//    (different streams, or another thread) race on the array and may return
+//    wrong tokens -- serialise them;
 //  * the first call on a device looks up the array's device address
 //    (cudaGetSymbolAddress) and sets the sampler kernels' shared-memory limit;
 //    make that first call before any stream capture is in progress.
@@ -93,7 +101,7 @@ int32_t rpgb_sample_noalloc(const float* logits_dev, int32_t n, const rpgb_sampl
     int64_t* d_counter = reinterpret_cast<int64_t*>(base + kOffCounter);
     int32_t* d_flag = reinterpret_cast<int32_t*>(base + kOffFlag);
     RPGB_CUDA(cudaMemcpyAsync(d_counter, &ctr, sizeof(int64_t), cudaMemcpyHostToDevice, s));
-    RPGB_CUDA(cudaMemsetAsync(d_flag, 0, sizeof(int32_t), s));
+    RPGB_CUDA(cudaMemsetAsync(d_flag, 0, sizeof(int32_t), s));  // defensive: the small kernel writes it
     SampleParams p;
     p.logits = logits_dev;
     p.n = n;

@@ -5,9 +5,10 @@ Criteria of the reference (tests/cmp_sample.py):
   2. filtered distribution within 1e-5 full-scale AND identical kept set;
   3. tokens identical, a divergence allowed only when u lies within 1e-6 of a
      cumulative-probability boundary.
-Checkers: the reference's own GPU sampler (built from its sources) when
-available, and the CPU oracle.  Runs at V = 4096 and 151936, the 12-case matrix
-of sample_check.cu:71-84 plus the BASELINE configs[4] sweep, 16 draws each.
+Checker: the CPU oracle, itself pinned to the reference's sampler outputs
+(tests/test_ref_fixtures.py; tests/test_gpu_ref_fixtures.py compares the
+engine with them directly).  Runs at V = 4096 and 151936, the 12-case matrix
+of sample_check.cu:71-84 plus the 36-case operator sweep, 16 draws each.
 """
 
 import numpy as np
@@ -18,49 +19,7 @@ from rpgbarenginecuda_b200 import SampleOptions, sample
 pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
-MASK = (1 << 64) - 1
-
-# (temperature, top_k, top_p, seed, tie) -- the reference's sample_check case matrix
-REF_CASES = [
-    (0.0, 0, 1.0, 11, False), (0.0, 8, 0.9, 12, False), (1.0, 0, 1.0, 13, False), (0.7, 40, 1.0, 14, False),
-    (1.3, 0, 0.9, 15, False), (0.5, 20, 0.95, 16, False), (1.0, 2, 1.0, 17, False), (1.0, 0, 0.05, 18, False),
-    (0.001, 0, 1.0, 19, False), (5.0, 0, 1.0, 20, False), (1.0, 8, 1.0, 21, True), (0.0, 0, 1.0, 22, True),
-]
-# T in {0, 0.7, 1.0} x top_k in {0,2,20,40} x top_p in {1.0, 0.8, 0.95}
-SWEEP_CASES = [(t, k, p, 100 + i, False) for i, (t, k, p) in enumerate(
-    (t, k, p) for t in (0.0, 0.7, 1.0) for k in (0, 2, 20, 40) for p in (1.0, 0.8, 0.95))]
-
-
-def splitmix64(x):
-    x = (x + 0x9E3779B97F4A7C15) & MASK
-    x = ((x ^ (x >> 30)) * 0xBF58476D1CE4E5B9) & MASK
-    x = ((x ^ (x >> 27)) * 0x94D049BB133111EB) & MASK
-    return x ^ (x >> 31)
-
-
-def ref_case_logits(seed, tie, n):
-    """The logits of tools/sample_check.cu:94-105: SplitMix64 -> [-8, 8), 1/8 grid for ties."""
-    idx = np.arange(n, dtype=np.uint64)
-    x = (np.uint64(seed) * np.uint64(1000003) + idx).astype(np.uint64)
-    x = x + np.uint64(0x9E3779B97F4A7C15)
-    x = (x ^ (x >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
-    x = (x ^ (x >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
-    x = x ^ (x >> np.uint64(31))
-    u = (x >> np.uint64(40)).astype(np.float32) * np.float32(1.0 / 16777216.0)
-    v = (u - np.float32(0.5)) * np.float32(16.0)
-    if tie:
-        v = np.round(v * np.float32(8.0)) / np.float32(8.0)
-    return v.astype(np.float32)
-
-
-def sweep_logits(seed, n):
-    """BASELINE configs[4] sampler input: N(0, 3^2)."""
-    return (np.random.default_rng(seed).standard_normal(n) * 3.0).astype(np.float32)
-
-
-def near_boundary(probs, u, tol=1e-6):
-    cum = np.cumsum(probs.astype(np.float64))
-    return np.min(np.abs(cum - u)) < tol
+from parity import REF_CASES, SWEEP_CASES, near_boundary, ref_case_logits, sweep_logits  # noqa: E402
 
 
 def run_ours(logits_d, n, t, k, p, seed, counter, want_probs):

@@ -90,3 +90,52 @@ def test_rejects_vocabulary_beyond_limit():
     rc = lib.rpgb_sample_noalloc(logits.data_ptr(), MAX_VOCAB + 1, ctypes.byref(opts), 0, 0, tok.data_ptr(), None)
     assert rc == -1
     assert "exceeds the fixed scratch limit" in _err(lib)
+
+
+FRESH = r"""
+import ctypes, sys
+import numpy as np
+import torch
+sys.path.insert(0, {root!r})
+from rpgbarenginecuda_b200 import SampleOptions
+from rpgbarenginecuda_b200._lib import load_engine
+lib = load_engine()
+n = 151936
+logits = torch.from_numpy((np.random.default_rng(3).standard_normal(n) * 3.0).astype(np.float32)).cuda()
+toks = torch.full((8,), -1, dtype=torch.int32, device="cuda")
+cases = [SampleOptions(0.7, 20, 0.8), SampleOptions(1.0, 0, 0.95), SampleOptions(0.0, 0, 1.0)]
+torch.cuda.synchronize()
+# the first sampler call of this process: it places the fixed array on the GPU
+assert lib.rpgb_sample_noalloc(logits.data_ptr(), n, ctypes.byref(cases[0]), 9, 1, toks.data_ptr(), None) == 0
+torch.cuda.synchronize()
+free0 = torch.cuda.mem_get_info()[0]
+for i, o in enumerate(cases):
+    for c in (2, 3):
+        assert lib.rpgb_sample_noalloc(logits.data_ptr(), n, ctypes.byref(o), 9, c,
+                                       toks[1 + 2 * i + c - 2:].data_ptr(), None) == 0
+torch.cuda.synchronize()
+free1 = torch.cuda.mem_get_info()[0]
+got = toks.cpu().tolist()
+want = []
+ref = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+for o, c in [(cases[0], 1)] + [(o, c) for o in cases for c in (2, 3)]:
+    assert lib.rpgb_sample(logits.data_ptr(), n, ctypes.byref(o), 9, c, None, ref.data_ptr(), None) == 0
+    want.append(int(ref.item()))
+print("RESULT", free0, free1, got[:7], want)
+assert free0 == free1, (free0, free1)
+assert got[:7] == want, (got, want)
+"""
+
+
+def test_fresh_process_first_call_then_no_device_memory_change():
+    """In a process whose first sampler call is rpgb_sample_noalloc: free device
+    memory is unchanged across the calls after the first one, and the tokens
+    equal rpgb_sample's."""
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", FRESH.format(root=root)], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "RESULT" in r.stdout
