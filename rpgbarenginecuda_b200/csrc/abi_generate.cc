@@ -672,8 +672,18 @@ std::string RunGenerate(const GenerateState& st, const Json& req) {
   opt.top_k = 0;
   opt.top_p = 0.95f;
   std::vector<int32_t> gen(static_cast<size_t>(max_tokens));
-  const int n = sess.Generate(opt, seed, max_tokens, stop_ids.data(), static_cast<int32_t>(stop_ids.size()),
-                              gen.data(), nullptr);
+  int n = 0;
+  try {
+    n = sess.Generate(opt, seed, max_tokens, stop_ids.data(), static_cast<int32_t>(stop_ids.size()), gen.data(),
+                      nullptr);
+  } catch (...) {
+    // a failed decode leaves the cache at a length the cached ids do not
+    // describe: start the session over, so the next request prefills again
+    // (src/engine.cc:531-537 does the same after a failed prefill)
+    sess.SetLen(0);
+    cached.clear();
+    throw;
+  }
   gen.resize(static_cast<size_t>(n));
   cached.insert(cached.end(), gen.begin(), gen.end());
 

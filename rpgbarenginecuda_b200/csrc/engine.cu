@@ -760,6 +760,8 @@ int Session::Generate(const SampleOpts& opt, uint64_t seed, int32_t max_tokens, 
 LoopParams Session::MakeLoopParams(const SampleOpts& opt, uint64_t seed) const {
   const ModelMeta& c = m_->meta();
   LoopParams lp;
+  if (const char* e = std::getenv("RPGB_TEST_WAIT_LIMIT")) lp.ll_limit = static_cast<uint32_t>(std::strtoul(e, nullptr, 10));
+  if (const char* e = std::getenv("RPGB_TEST_DROP_WORD")) lp.test_drop_word = std::atoi(e);
   lp.layers = m_->layers_dev();
   lp.n_layers = c.n_layers;
   lp.embd = m_->embd();

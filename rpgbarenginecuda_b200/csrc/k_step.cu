@@ -450,7 +450,7 @@ constexpr uint32_t kLLLimit = 1u << 21;  // polls of one tagged word group befor
 // A wait gives up after kLLLimit polls, or early once another block has
 // reported an error (checked every 512 polls).
 __device__ __forceinline__ bool LLGiveUp(const LoopParams& p, uint32_t it) {
-  if (it == kLLLimit) {
+  if (it == (p.ll_limit != 0u ? p.ll_limit : kLLLimit)) {
     atomicOr(p.err, 8u);
     return true;
   }
@@ -846,7 +846,7 @@ __device__ void MvPhase(const LoopParams& p, const GeoTable& gt, int kind, int l
     v2 *= scale;
     const int row = g.t0 * kTile + lr;
     if (kind == kQkv) {
-      StLL(p.llqkv + row, v, tag_out);
+      if (!(p.test_drop_word != 0 && step == 0 && layer == 0 && row == 0)) StLL(p.llqkv + row, v, tag_out);
     } else if (kind == kO || kind == kDown) {
       // x += W h: this block owns these rows of x in both phases
       float add = v;

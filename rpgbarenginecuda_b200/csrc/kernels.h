@@ -248,6 +248,12 @@ struct LoopParams {
   unsigned* bar = nullptr;  // grid barrier word
   unsigned* err = nullptr;  // nonzero after a bounded wait gave up
   int32_t splits = 1;       // attention blocks per KV head
+  // Failure path: polls of one tagged-word wait before it gives up (0: the
+  // built-in limit), and a test hook that leaves one word of the first qkv
+  // phase unpublished, so the attention phase's wait for it runs out
+  // (RPGB_TEST_WAIT_LIMIT / RPGB_TEST_DROP_WORD, read by the host per launch).
+  uint32_t ll_limit = 0;
+  int32_t test_drop_word = 0;
   // shared-memory plan, filled in by the launcher
   int32_t ring = 0, max_tiles = 0, nb_max = 0, x_max = 0;
   int32_t scratch_bytes = 0;
