@@ -279,6 +279,61 @@ def matvec_roofline(path, device, peak):
                         "frac": round(big_gbs / peak, 4)}}
 
 
+SWEEP_SHAPES = [(2048, 2048), (6144, 2048), (2048, 6144), (151936, 2048), (9728, 2560)]
+SWEEP_N = [1, 2, 4, 8, 64]
+
+
+def matvec_sweep(device, peak, l2_bytes=126 << 20):
+    """The Q4_K / Q6_K operator sweep: every (type, M x K) of SWEEP_SHAPES at
+    n = 1, 2, 4, 8, 64 activation columns.  Each shape is uploaded in enough
+    copies that one pass over them exceeds L2 twice (weights stream from HBM
+    as in decode), the copies are launched back to back, CUDA events time the
+    pass; achieved = algorithmic bytes (quantised weights + 4n(M+K)) per
+    launch / average launch time."""
+    import numpy as np
+    import torch
+
+    from rpgbarenginecuda_b200 import Matrix, synthetic
+
+    out = {}
+    stream = torch.cuda.current_stream(device)
+    sp = stream.cuda_stream
+    for qtype, qname, blk in ((12, "q4k", 144), (14, "q6k", 210)):
+        for rows, cols in SWEEP_SHAPES:
+            wbytes = rows * cols // 256 * blk
+            copies = max(1, min(128, -(-2 * l2_bytes // wbytes)))
+            b = synthetic.quantize(synthetic.normal(7 + rows + cols, rows * cols, 0.0, 0.02),
+                                   {"q4k": "q4_k", "q6k": "q6_k"}[qname])
+            mats = [Matrix(qtype, rows, cols, b, device) for _ in range(copies)]
+            del b
+            x = torch.randn(max(SWEEP_N), cols, device=f"cuda:{device}")
+            y = torch.empty(max(SWEEP_N), rows, device=f"cuda:{device}")
+            for n in SWEEP_N:
+                for m in mats:  # warm-up pass
+                    m.matvec(x.data_ptr(), n, y.data_ptr(), sp)
+                reps = max(1, 64 // copies)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                for _ in range(reps):
+                    for m in mats:
+                        m.matvec(x.data_ptr(), n, y.data_ptr(), sp)
+                e1.record(stream)
+                e1.synchronize()
+                us = 1000.0 * e0.elapsed_time(e1) / (reps * copies)
+                alg = wbytes + 4 * n * (rows + cols)
+                gbs = alg / (us * 1e-6) / 1e9
+                out[f"{qname}_{rows}x{cols}_n{n}"] = {"us": round(us, 2), "gbs": round(gbs, 1),
+                                                      "frac": round(gbs / peak, 4)}
+            for m in mats:
+                m.close()
+            del x, y
+            torch.cuda.empty_cache()
+    n1 = [v["frac"] for k, v in out.items() if k.endswith("_n1")]
+    return {"kernel": "rpgb_matrix_matvec: Q4_K/Q6_K operator sweep (weights > L2, launches back to back)",
+            "bound": "hbm", "peak": peak, "unit": "GB/s", "frac_n1_mean": round(sum(n1) / len(n1), 4),
+            "shapes": out}
+
+
 def matvec_shapes(args):
     """One decode-matvec launch per distinct (type, rows, cols) of the model, after one warm-up launch each."""
     import numpy as np
@@ -471,13 +526,14 @@ def ours(args):
         with open(tf) as f:
             loop_roof["traffic"] = json.load(f).get("dram_bytes_per_token")
 
-    roof = None
+    roof = sweep = None
     if rank == 0 and not args.no_roofline:
         sess.close()
         model.close()
         torch.cuda.empty_cache()
         hbm, kind = peaks()
         roof = matvec_roofline(path, local, hbm)
+        sweep = matvec_sweep(local, hbm)
         roof["peak_kind"] = kind
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -511,6 +567,7 @@ def ours(args):
         line["roofline"] = loop_roof
         if roof is not None:
             line["roofline_matvec"] = roof
+            line["roofline_matvec_sweep"] = sweep
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)

@@ -573,12 +573,22 @@ typedef struct {
   int64_t pos0, n;
 } attn_ctx;
 
+/* f16 -> f32 of every bit pattern (the attention loops convert each cached
+ * element; a table keeps long contexts fast) */
+static float g_f16_table[65536];
+static pthread_once_t g_f16_once = PTHREAD_ONCE_INIT;
+static void f16_table_init(void) {
+  for (uint32_t h = 0; h < 65536u; ++h) g_f16_table[h] = orc_f16_to_f32((uint16_t)h);
+}
+
 static void attn_range(void* p, int64_t a, int64_t b) {
   attn_ctx* c = (attn_ctx*)p;
   const orc_model* m = c->s->m;
   const int hd = m->head_dim, nh = m->n_heads, group = m->n_heads / m->n_kv;
   const double scale = (double)(1.0f / sqrtf((float)hd));
   double* sc = (double*)malloc((size_t)(c->pos0 + c->n) * sizeof(double));
+  double* acc = (double*)malloc((size_t)hd * sizeof(double));
+  const float* f16 = g_f16_table;
   for (int64_t job = a; job < b; ++job) {
     const int64_t t = job / nh;
     const int h = (int)(job % nh), kh = h / group;
@@ -588,9 +598,9 @@ static void attn_range(void* p, int64_t a, int64_t b) {
     double mx = -DBL_MAX;
     for (int64_t s = 0; s <= pos; ++s) {
       const uint16_t* k = c->s->kc + lbase + (size_t)s * hd;
-      double acc = 0.0;
-      for (int d = 0; d < hd; ++d) acc += (double)q[d] * (double)orc_f16_to_f32(k[d]);
-      sc[s] = acc * scale;
+      double dot = 0.0;
+      for (int d = 0; d < hd; ++d) dot += (double)q[d] * (double)f16[k[d]];
+      sc[s] = dot * scale;
       if (sc[s] > mx) mx = sc[s];
     }
     double sum = 0.0;
@@ -598,13 +608,17 @@ static void attn_range(void* p, int64_t a, int64_t b) {
       sc[s] = exp(sc[s] - mx);
       sum += sc[s];
     }
-    float* o = c->out + t * (int64_t)nh * hd + (int64_t)h * hd;
-    for (int d = 0; d < hd; ++d) {
-      double acc = 0.0;
-      for (int64_t s = 0; s <= pos; ++s) acc += sc[s] * (double)orc_f16_to_f32(c->s->vc[lbase + (size_t)s * hd + d]);
-      o[d] = (float)(acc / sum);
+    /* each acc[d] adds its terms in position order, as a per-dimension loop would */
+    for (int d = 0; d < hd; ++d) acc[d] = 0.0;
+    for (int64_t s = 0; s <= pos; ++s) {
+      const uint16_t* v = c->s->vc + lbase + (size_t)s * hd;
+      const double w = sc[s];
+      for (int d = 0; d < hd; ++d) acc[d] += w * (double)f16[v[d]];
     }
+    float* o = c->out + t * (int64_t)nh * hd + (int64_t)h * hd;
+    for (int d = 0; d < hd; ++d) o[d] = (float)(acc[d] / sum);
   }
+  free(acc);
   free(sc);
 }
 
@@ -673,6 +687,7 @@ int orc_prefill(orc_session* s, const int32_t* tokens, int64_t n, float* last_lo
         }
       }
     }
+    pthread_once(&g_f16_once, f16_table_init);
     attn_ctx ac = {s, l, q, att, pos0, n};
     parallel_for(s->n_threads, n * m->n_heads, attn_range, &ac);
     matvec_into(wo->type, wo->data, H, qd, att, n, qd, proj, H, 0, s->n_threads);
