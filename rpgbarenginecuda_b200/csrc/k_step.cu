@@ -685,24 +685,35 @@ __device__ void MergeHead(const LoopParams& p, int step, int layer, int64_t pos,
     inv[g] = static_cast<float>(1.0 / L);
   }
   __syncthreads();
-  for (int i = tid; i < G * kD; i += kNT) {
+  // kPer threads per output value, each over every kPer-th split, so all the
+  // loads of a head's records are in flight at once (one L2 round trip for
+  // up to 10 kPer splits)
+  constexpr int kPer = kNT / (G * kD) > 0 ? kNT / (G * kD) : 1;
+  static_assert(kPer == 1 || (kPer == 2 && 32 % kPer == 0), "merge thread split");
+  for (int t = tid; t < G * kD * kPer; t += kNT) {
+    const int i = t / kPer, part = t - i * kPer;
     const int g = i / kD, d = i - g * kD;
     const uint64_t* base = recs + g * kD + d;
     float o = 0.f;
-    constexpr int kB = 8;
-    for (int s0 = 0; s0 < se; s0 += kB) {
+    constexpr int kB = 10;
+    for (int s0 = part; s0 < se; s0 += kB * kPer) {
       uint64_t w[kB];
 #pragma unroll
-      for (int j = 0; j < kB; ++j) w[j] = s0 + j < se ? LdLL(base + static_cast<size_t>(s0 + j) * kRec) : 0ull;
+      for (int j = 0; j < kB; ++j) {
+        const int sp = s0 + j * kPer;
+        w[j] = sp < se ? LdLL(base + static_cast<size_t>(sp) * kRec) : 0ull;
+      }
 #pragma unroll
       for (int j = 0; j < kB; ++j) {
-        if (s0 + j < se) {
-          const float v = TagOk(w[j], tag) ? ValOf(w[j]) : WaitLL1(p, base + static_cast<size_t>(s0 + j) * kRec, tag);
-          o = fmaf(wv[(s0 + j) * G + g], v, o);
+        const int sp = s0 + j * kPer;
+        if (sp < se) {
+          const float v = TagOk(w[j], tag) ? ValOf(w[j]) : WaitLL1(p, base + static_cast<size_t>(sp) * kRec, tag);
+          o = fmaf(wv[sp * G + g], v, o);
         }
       }
     }
-    StLL(p.llattn + static_cast<size_t>(h * G + g) * kD + d, o * inv[g], tag);
+    if constexpr (kPer == 2) o += __shfl_xor_sync(0xFFFFFFFFu, o, 1);
+    if (part == 0) StLL(p.llattn + static_cast<size_t>(h * G + g) * kD + d, o * inv[g], tag);
   }
 }
 
@@ -964,6 +975,16 @@ __device__ void AttnPhase(const LoopParams& p, const GeoTable& gt, int layer, in
   const uint32_t tag = TagOf(p, step, layer, kQkv);
   const int vi = tid >> 6, d = tid & 63;
   float e0 = 0.f, e1 = 0.f;
+  // the norm weights and this position's rotation do not depend on the qkv
+  // phase: load them before waiting for its words
+  float nw0 = 0.f, nw1 = 0.f, rc = 0.f, rs = 0.f;
+  if (vi <= G) {
+    const float* nw = vi < G ? Ly.norm[2] : Ly.norm[3];
+    nw0 = nw[d];
+    nw1 = nw[d + 64];
+    rc = p.rope[pos * kD + d];
+    rs = p.rope[pos * kD + kD / 2 + d];
+  }
   if (vi <= G) {
     const int64_t off = vi < G ? static_cast<int64_t>(h * G + vi) * kD : qd + h * kD;
     uint64_t w0 = LdLL(p.llqkv + off + d), w1 = LdLL(p.llqkv + off + d + 64);
@@ -988,12 +1009,10 @@ __device__ void AttnPhase(const LoopParams& p, const GeoTable& gt, int layer, in
   if (vi <= G) {
     const double tot = as.sq[2 * vi] + as.sq[2 * vi + 1];
     const float sc = static_cast<float>(1.0 / sqrt(tot / static_cast<double>(kD) + static_cast<double>(p.eps)));
-    const float* nw = vi < G ? Ly.norm[2] : Ly.norm[3];
     // scores in log2 units (q times 1/sqrt(128) times log2(e)): the softmax
     // then exponentiates with exp2f; the split records carry the same units
     const float qscale = p.scale * 1.4426950408889634f;
-    const float x0 = e0 * sc * nw[d], x1 = e1 * sc * nw[d + 64];
-    const float rc = p.rope[pos * kD + d], rs = p.rope[pos * kD + kD / 2 + d];
+    const float x0 = e0 * sc * nw0, x1 = e1 * sc * nw1;
     const float y0 = x0 * rc - x1 * rs, y1 = x1 * rc + x0 * rs;
     if (vi < G) {
       as.qs[vi][d] = y0 * qscale;

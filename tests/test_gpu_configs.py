@@ -12,7 +12,8 @@ outputs by tests/test_ref_fixtures.py -- on:
 Every decode call is one multi-step loop launch (the benchmarked mode).
 Criteria as everywhere (tests/parity.py): logits within 1e-3 of full scale,
 greedy tokens identical up to a gap-rule divergence, sampled tokens identical
-except where u is within 1e-6 of a cumulative boundary.
+except where u lies within the distance a cumulative boundary can move given
+the step's logit difference.
 """
 
 import os
@@ -20,7 +21,7 @@ import os
 import numpy as np
 import pytest
 
-from parity import FULL_SCALE, greedy_agree, kept_probs, row_err, sampled_agree
+from parity import FULL_SCALE, greedy_agree, kept_probs, row_delta, row_err, sampled_agree
 from rpgbarenginecuda_b200 import Model, SampleOptions, Session, counter_uniform, launch_count, synthetic
 
 pytestmark = pytest.mark.gpu
@@ -63,7 +64,8 @@ def test_17b_benchmark_turn(fix, model_cache):
         assert launch_count() - before <= 4
         ref_ids = fix[f"{kr}/ids"]
         ok, n = sampled_agree(ids, ref_ids, lambda i: kept_probs(fix, kr, i, V),
-                              lambda i: counter_uniform(SAMPLE_SEED, start + i))
+                              lambda i: counter_uniform(SAMPLE_SEED, start + i),
+                              lambda i: row_delta(fix, f"{kr}/steps", i, steps[i], rand_idx), SAMPLE[0])
         assert ok, (r, n, list(ids), list(ref_ids))
         for i in range(min(n + 1, len(ids))):
             assert row_err(fix, f"{kr}/steps", i, steps[i], rand_idx) <= FULL_SCALE, (r, i)

@@ -7,8 +7,9 @@ reference's tests/cmp_gen.py and tests/cmp_sample.py):
 * prefill / per-step logits within 1e-3 of full scale;
 * greedy tokens identical; a divergence only where the two tokens' logits
   differ by <= 1e-2 of the logit span, and the comparison stops there;
-* sampled tokens identical; a divergence only where u lies within 1e-6 of a
-  cumulative boundary of the oracle's filtered distribution;
+* sampled tokens identical; a divergence only where u lies within the
+  distance a cumulative boundary of the oracle's filtered distribution can
+  move given the logit difference measured at that step;
 * cache.len == prompt + generated (src/qwen3_gpu.cu:585-593), the stop token
   is forwarded.
 Every generate call with step logits runs its steps in one decode-loop launch
@@ -40,7 +41,8 @@ def check_sampled(oracle, ids, steps, rids, rsteps, opts, seed, start):
     """Sampled tokens against the oracle's; returns how many agree."""
     t, k, p = opts
     ok, n = sampled_agree(ids, rids, lambda i: oracle.filter_to_probs(rsteps[i], t, k, p),
-                          lambda i: counter_uniform(seed, start + i))
+                          lambda i: counter_uniform(seed, start + i),
+                          lambda i: float(np.abs(steps[i].astype(np.float64) - rsteps[i]).max()), t)
     assert ok, (n, list(ids), list(rids))
     for i in range(min(n + 1, len(ids))):
         assert full_scale_err(steps[i], rsteps[i]) <= FULL_SCALE, i

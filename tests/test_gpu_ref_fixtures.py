@@ -16,7 +16,7 @@ from dataclasses import replace
 import numpy as np
 import pytest
 
-from parity import (FULL_SCALE, REF_CASES, case_logits, greedy_agree, kept_probs, near_boundary, row_err,
+from parity import (FULL_SCALE, REF_CASES, case_logits, greedy_agree, kept_probs, row_delta, near_boundary, row_err,
                     sampled_agree)
 from rpgbarenginecuda_b200 import Model, SampleOptions, Session, counter_uniform, launch_count, sample, synthetic
 
@@ -92,7 +92,8 @@ def test_engine_sampled_turns_vs_reference(eng, model_cache, name):
         ids, steps = generate_one_launch(s, SAMPLE, SAMPLE_SEED, 16)
         ref_ids = eng[f"{kr}/ids"]
         ok, n = sampled_agree(ids, ref_ids, lambda i: kept_probs(eng, kr, i, V),
-                              lambda i: counter_uniform(SAMPLE_SEED, start + i))
+                              lambda i: counter_uniform(SAMPLE_SEED, start + i),
+                              lambda i: row_delta(eng, f"{kr}/steps", i, steps[i], rand_idx), SAMPLE[0])
         assert ok, (r, n, ids, ref_ids)
         for i in range(min(n + 1, len(ids))):
             assert row_err(eng, f"{kr}/steps", i, steps[i], rand_idx) <= FULL_SCALE, (r, i)
