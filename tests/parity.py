@@ -10,14 +10,14 @@ Criteria are the reference's own:
   lies within 1e-6 of a cumulative-probability boundary (tests/cmp_sample.py
   criterion 3);
 * sampled tokens after the model: the two sides' logits differ by float
-  rounding, which moves every cumulative boundary (the reference's own
-  tools/gen_sample_check.cu:6-9 declines token identity there for this
-  reason).  A divergence is accepted only where u lies within the distance a
-  boundary can move given the logit difference d measured at that step:
-  tau = 2 (exp(2 d / T) - 1) + 1e-6 (each probability changes by a factor
-  within exp(+-2 d / T) after renormalisation, so each cumulative sum by less
-  than exp(2 d / T) - 1; the factor 2 covers a kept set that differs at the
-  top-p cut), and the comparison stops there;
+  rounding, so a draw near a cumulative boundary can select different tokens
+  (the reference's own tools/gen_sample_check.cu:6-9 declines token identity
+  there for this reason).  Tokens must agree up to the first divergence; there
+  each side's token must be the draw the checker's sampler (pinned to the
+  reference's sampler on identical logits) makes from that side's own logits
+  with the same u, and the logits themselves are held to the 1e-3 full-scale
+  bound -- so a divergence is explained exactly by the logit difference.  The
+  comparison stops there (later steps have different histories);
 * filtered distributions: within 1e-5 of full scale and the same kept set
   (tests/cmp_sample.py criterion 2).
 """
@@ -86,23 +86,23 @@ def greedy_agree(ours, ref, ours_steps):
     return len(ours) == len(ref), min(len(ours), len(ref))
 
 
-def boundary_tol(delta, temperature):
-    """How far a cumulative boundary can move when logits differ by delta."""
-    if delta is None or not (temperature > 0.0):
-        return 1e-6
-    return 2.0 * float(np.expm1(2.0 * delta / temperature)) + 1e-6
+def draw_ok(oracle, row, opts, u, tok):
+    """tok is the token the checker's sampler draws from logits row with u
+    (or u lies within 1e-6 of a boundary of that distribution)."""
+    t, k, p = opts
+    row = np.ascontiguousarray(row, dtype=np.float32)
+    if oracle.sample_token(row, t, k, p, u) == int(tok):
+        return True
+    return near_boundary(oracle.filter_to_probs(row, t, k, p), u)
 
 
-def sampled_agree(ours, ref, probs_at, u_at, delta_at=None, temperature=1.0):
-    """(ok, n): ours == ref for the first n tokens; a first divergence at n is
-    ok only when u of that draw lies within boundary_tol of a cumulative
-    boundary of the checker's filtered distribution (probs_at(i)); delta_at(i)
-    is the logit difference measured at that step (None: identical logits,
-    1e-6)."""
+def sampled_agree(ours, ref, ours_ok, ref_ok):
+    """(ok, n): ours == ref for the first n tokens; at a first divergence n,
+    ours_ok(n, token) and ref_ok(n, token) must both hold (each side drew its
+    token correctly from its own logits)."""
     for i, (a, b) in enumerate(zip(ours, ref)):
         if a != b:
-            tol = boundary_tol(delta_at(i) if delta_at is not None else None, temperature)
-            return near_boundary(probs_at(i), u_at(i), tol), i
+            return bool(ours_ok(i, a) and ref_ok(i, b)), i
     return len(ours) == len(ref), min(len(ours), len(ref))
 
 
@@ -142,9 +142,12 @@ def row_err(fix, key, i, ours_row, rand_idx):
                       rand_idx, fix[f"{key}/rand_val"][i])
 
 
-def row_delta(fix, key, i, ours_row, rand_idx):
-    """Largest absolute logit difference over the stored entries of row i."""
-    return row_err(fix, key, i, ours_row, rand_idx) * float(fix[f"{key}/scale"][i])
+def top_row(fix, key, i, vocab):
+    """Stored row i with only its top entries (the rest -inf): enough to
+    recompute a top_k <= 32 filtered distribution exactly."""
+    row = np.full(vocab, -np.inf, dtype=np.float32)
+    row[fix[f"{key}/top_idx"][i]] = fix[f"{key}/top_val"][i]
+    return row
 
 
 def kept_probs(fix, key, i, vocab):

@@ -7,9 +7,8 @@ reference's tests/cmp_gen.py and tests/cmp_sample.py):
 * prefill / per-step logits within 1e-3 of full scale;
 * greedy tokens identical; a divergence only where the two tokens' logits
   differ by <= 1e-2 of the logit span, and the comparison stops there;
-* sampled tokens identical; a divergence only where u lies within the
-  distance a cumulative boundary of the oracle's filtered distribution can
-  move given the logit difference measured at that step;
+* sampled tokens identical; at a divergence each side's token must be the
+  checker's draw from that side's own logits with the same u;
 * cache.len == prompt + generated (src/qwen3_gpu.cu:585-593), the stop token
   is forwarded.
 Every generate call with step logits runs its steps in one decode-loop launch
@@ -20,7 +19,7 @@ import numpy as np
 import pytest
 
 from oracle.oracle import OracleModel, OracleSession
-from parity import FULL_SCALE, full_scale_err, greedy_agree, sampled_agree
+from parity import FULL_SCALE, draw_ok, full_scale_err, greedy_agree, sampled_agree
 from rpgbarenginecuda_b200 import Model, SampleOptions, Session, counter_uniform, launch_count, synthetic
 
 pytestmark = pytest.mark.gpu
@@ -39,10 +38,9 @@ def pair(request, tiny_model, tiny_g4_model, small_model):
 
 def check_sampled(oracle, ids, steps, rids, rsteps, opts, seed, start):
     """Sampled tokens against the oracle's; returns how many agree."""
-    t, k, p = opts
-    ok, n = sampled_agree(ids, rids, lambda i: oracle.filter_to_probs(rsteps[i], t, k, p),
-                          lambda i: counter_uniform(seed, start + i),
-                          lambda i: float(np.abs(steps[i].astype(np.float64) - rsteps[i]).max()), t)
+    u = lambda i: counter_uniform(seed, start + i)  # noqa: E731
+    ok, n = sampled_agree(ids, rids, lambda i, tok: draw_ok(oracle, steps[i], opts, u(i), tok),
+                          lambda i, tok: draw_ok(oracle, rsteps[i], opts, u(i), tok))
     assert ok, (n, list(ids), list(rids))
     for i in range(min(n + 1, len(ids))):
         assert full_scale_err(steps[i], rsteps[i]) <= FULL_SCALE, i

@@ -16,7 +16,7 @@ from dataclasses import replace
 import numpy as np
 import pytest
 
-from parity import (FULL_SCALE, REF_CASES, case_logits, greedy_agree, kept_probs, row_delta, near_boundary, row_err,
+from parity import (draw_ok, FULL_SCALE, REF_CASES, case_logits, greedy_agree, top_row, near_boundary, row_err,
                     sampled_agree)
 from rpgbarenginecuda_b200 import Model, SampleOptions, Session, counter_uniform, launch_count, sample, synthetic
 
@@ -76,7 +76,7 @@ def test_engine_greedy_vs_reference(eng, model_cache, name):
 
 
 @pytest.mark.parametrize("name", list(TOY))
-def test_engine_sampled_turns_vs_reference(eng, model_cache, name):
+def test_engine_sampled_turns_vs_reference(eng, model_cache, oracle, name):
     """Prompt, then rounds of (16 tokens at T=0.7 top_k=20 top_p=0.8, append 9 ids)."""
     m = Model(toy_path(name, eng, model_cache), 0, 1024)
     s = Session(m, 512)
@@ -91,9 +91,9 @@ def test_engine_sampled_turns_vs_reference(eng, model_cache, name):
         assert len(s) == start
         ids, steps = generate_one_launch(s, SAMPLE, SAMPLE_SEED, 16)
         ref_ids = eng[f"{kr}/ids"]
-        ok, n = sampled_agree(ids, ref_ids, lambda i: kept_probs(eng, kr, i, V),
-                              lambda i: counter_uniform(SAMPLE_SEED, start + i),
-                              lambda i: row_delta(eng, f"{kr}/steps", i, steps[i], rand_idx), SAMPLE[0])
+        u = lambda i: counter_uniform(SAMPLE_SEED, start + i)  # noqa: E731
+        ok, n = sampled_agree(ids, ref_ids, lambda i, tok: draw_ok(oracle, steps[i], SAMPLE, u(i), tok),
+                              lambda i, tok: draw_ok(oracle, top_row(eng, f"{kr}/steps", i, V), SAMPLE, u(i), tok))
         assert ok, (r, n, ids, ref_ids)
         for i in range(min(n + 1, len(ids))):
             assert row_err(eng, f"{kr}/steps", i, steps[i], rand_idx) <= FULL_SCALE, (r, i)
