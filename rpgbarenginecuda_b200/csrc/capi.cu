@@ -360,6 +360,7 @@ int32_t rpgb_matrix_upload(int32_t device, uint32_t type, int64_t rows, int64_t 
     RPGB_CUDA(cudaSetDevice(device));
     RPGB_CUDA(cudaDeviceGetAttribute(&e->num_sms, cudaDevAttrMultiProcessorCount, device));
     PrepareMatvecKernels();
+    PrepareMatvecTokensKernels();
     PrepareSampleKernels();
     PrepareTcGemmKernels();
     const int64_t rb = GgmlRowBytes(type, cols);
@@ -431,7 +432,18 @@ int32_t rpgb_matrix_matvec(int32_t matrix, const float* x_dev, int64_t n_tok, fl
       p.x = x_dev;
       p.out = out_dev;
       const int rw = e->m.rows % 4 == 0 ? 4 : (e->m.rows % 2 == 0 ? 2 : 1);
-      LaunchMatvec(p, Epi::kStore, rw, e->num_sms, s);
+      // programmatic launch: the weights stream in while the previous kernel
+      // on the stream finishes (the kernel waits for it before reading x)
+      LaunchMatvec(p, Epi::kStore, rw, e->num_sms, s, true);
+    } else if (n_tok < kTcMinTokens || e->m.rows % 128 != 0) {
+      MvnParams q;
+      q.w = e->m;
+      q.x = x_dev;
+      q.out = out_dev;
+      q.n_tok = static_cast<int32_t>(n_tok);
+      q.ldx = e->m.cols;
+      q.ldo = e->m.rows;
+      LaunchMatvecTokens(q, e->num_sms, s, true);
     } else {
       GemmParams g;
       g.w = e->m;

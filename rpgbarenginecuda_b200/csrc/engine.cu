@@ -293,21 +293,20 @@ void Session::EnsurePrefill(int64_t n) {
 
 void Session::RowwiseMatvec(const DevMat* w, const int* out_off, int n_seg, const float* x, int ldx, float* out,
                             int ldo, bool resid, Epi epi, int n_tok, cudaStream_t s) {
-  int total = 0;
-  for (int i = 0; i < n_seg; ++i) total += w[i].rows;
-  for (int t = 0; t < n_tok; ++t) {
-    MvParams p;
-    for (int i = 0; i < n_seg; ++i) {
-      p.seg[i].w = w[i];
-      p.seg[i].out_off = out_off[i];
-    }
-    p.n_seg = n_seg;
-    p.total_rows = total;
-    p.x = x + static_cast<int64_t>(t) * ldx;
-    p.out = out + static_cast<int64_t>(t) * ldo;
-    p.resid = resid ? p.out : nullptr;
+  // one multi-token launch per matrix: its weights stream once per pass of
+  // up to four tokens (k_matvec_n.cu)
+  for (int i = 0; i < n_seg; ++i) {
+    MvnParams p;
+    p.w = w[i];
+    p.x = x;
+    p.out = out;
+    p.n_tok = n_tok;
+    p.ldx = ldx;
+    p.ldo = ldo;
+    p.out_off = out_off[i];
+    p.epi = resid ? Epi::kResid : epi;
     p.err = err_;
-    LaunchMatvec(p, epi, 1, m_->num_sms(), s);
+    LaunchMatvecTokens(p, m_->num_sms(), s);
   }
 }
 
@@ -330,9 +329,9 @@ void Session::Prefill(const int32_t* tokens, int64_t n, float* last_logits) {
   const int H = c.hidden, qd = c.q_dim(), kvd = c.kv_dim(), qkv = qd + 2 * kvd;
   const int nt = static_cast<int>(n);
   // Short prompts: GEMM tiles would leave most SMs idle (and the tensor-core
-  // path would first expand every weight to fp16), so each token runs the
-  // decode matvec on its normalised row instead; from the second token on the
-  // layer's weights come from L2.
+  // path would first expand every weight to fp16), so they run the
+  // multi-token matvec: the decode matvec's units applied to up to four
+  // tokens per pass while each weight unit is in shared memory.
   const bool rowwise = nt < kTcMinTokens;
   LaunchEmbed(m_->embd(), pf_tok_, nt, pf_x_, nullptr, nullptr, s);
   for (int l = 0; l < c.n_layers; ++l) {

@@ -80,6 +80,26 @@ void LaunchMatvec(const MvParams& p, Epi epi, int rows_per_warp, int num_sms, cu
 // Scratch sizes needed by kArgmax for a given launch.
 int MatvecGrid(int total_rows, int rows_per_warp, int num_sms);
 
+// out[t][r] = sum_c W[r][c] x[t][c] for a few tokens (k_matvec_n.cu): the
+// decode matvec's integer tensor-core units applied to every token of a pass
+// while each weight unit is in shared memory.
+struct MvnParams {
+  DevMat w;
+  const float* x = nullptr;  // [n_tok][ldx], rows 16-byte aligned
+  float* out = nullptr;      // [n_tok][ldo]
+  int32_t n_tok = 0, ldx = 0, ldo = 0;
+  // epilogue: kStore out[t][out_off + r] = v; kResid out[t][r] += v (the
+  // residual stream in place); kSilu rows 2i / 2i+1 (gate / up) give
+  // out[t][i] = silu(gate) * up
+  int32_t out_off = 0;
+  Epi epi = Epi::kStore;
+  unsigned* err = nullptr;  // set to nonzero if a bounded device wait gave up
+  // launch geometry, filled in by LaunchMatvecTokens
+  int32_t ring = 0, slot_bytes = 0, max_tiles = 0, tp = 0;
+};
+void PrepareMatvecTokensKernels();
+void LaunchMatvecTokens(const MvnParams& p, int num_sms, cudaStream_t s, bool pdl = false);
+
 // ------------------------------------------------------------------ embedding
 
 // x[t, :] = dequant(embd row tok[t]); if out_ids != nullptr also out_ids[*pos + t] = tok[t].

@@ -261,6 +261,7 @@ std::unique_ptr<Model> Model::Load(const std::string& path, int device, int32_t 
   RPGB_CUDA(cudaSetDevice(device));
   RPGB_CUDA(cudaDeviceGetAttribute(&m->num_sms_, cudaDevAttrMultiProcessorCount, device));
   PrepareMatvecKernels();
+  PrepareMatvecTokensKernels();
   PrepareSampleKernels();
   PrepareAttentionKernels();
   PrepareLoopKernels(m->num_sms_);
