@@ -80,6 +80,9 @@ PRESETS = {
     "tiny": ModelShape("tiny", 2, 512, 1024, 4, 2, vocab=4096, context=512),
     "small": ModelShape("small", 4, 1024, 3072, 16, 8, vocab=8192, context=1024),
     "tiny-g4": ModelShape("tiny-g4", 2, 512, 1536, 8, 2, vocab=4096, context=512),
+    # the 8B model's widths with two layers: its tensor-parallel splits (up to
+    # eight ranks) at a test's cost
+    "wide": ModelShape("wide", 2, 4096, 12288, 32, 8, vocab=8192, context=1024),
 }
 
 

@@ -63,6 +63,11 @@ def small_model(model_cache):
 
 
 @pytest.fixture(scope="session")
+def wide_model(model_cache):
+    return toy_model("wide", 4, model_cache)
+
+
+@pytest.fixture(scope="session")
 def oracle():
     from oracle.oracle import Oracle
 

@@ -6,8 +6,10 @@ only at a top-2 tie of the reference's logits (the forward tests' rule).
 * TP = 1 through an NCCL group of one rank: the same shard code path
   (partials, sum, residual add, gathered logits, sampler on the gathered row)
   on one GPU, so the driver's one-GPU run covers it.
-* TP = 2 (and 4 where the box has four GPUs): one process per GPU
-  (tests/tp_worker.py), NVLS off, each process under a time limit.
+* TP = 2, 4 and 8 where the box has the GPUs: one process per GPU
+  (tests/tp_worker.py), NVLS off, each process under a time limit; the
+  "wide" model (the 8B model's widths, two layers) splits like the 8B plan
+  over up to eight ranks.
 """
 
 import os
@@ -62,9 +64,9 @@ def check_same(got, ref):
     assert int(got["len_loop"]) == int(ref["len_loop"])
 
 
-@pytest.fixture(scope="module", params=["tiny", "tiny_g4", "small"])
-def model_path(request, tiny_model, tiny_g4_model, small_model):
-    return {"tiny": tiny_model, "tiny_g4": tiny_g4_model, "small": small_model}[request.param]
+@pytest.fixture(scope="module", params=["tiny", "tiny_g4", "small", "wide"])
+def model_path(request, tiny_model, tiny_g4_model, small_model, wide_model):
+    return {"tiny": tiny_model, "tiny_g4": tiny_g4_model, "small": small_model, "wide": wide_model}[request.param]
 
 
 def test_tp1_group_matches_one_gpu(model_path):
@@ -87,12 +89,13 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("size", [2, 4])
+@pytest.mark.parametrize("size", [2, 4, 8])
 def test_tp_ranks_match_one_gpu(model_path, size, tmp_path):
     if torch.cuda.device_count() < size:
         pytest.skip(f"needs {size} GPUs")
-    if "tiny" in os.path.basename(model_path) and size > 2:
-        pytest.skip("the tiny models split over two ranks at most")
+    base = os.path.basename(model_path)
+    if ("tiny" in base and size > 2) or ("small" in base and size > 4):
+        pytest.skip("the model does not split over that many ranks (whole super-blocks per rank)")
     port, out = _free_port(), str(tmp_path / "tp.npz")
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     procs = [subprocess.Popen([sys.executable, os.path.join(HERE, "tp_worker.py"), "--model", model_path,
