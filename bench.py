@@ -287,8 +287,8 @@ def matvec_sweep(device, peak, l2_bytes=126 << 20):
     """The Q4_K / Q6_K operator sweep: every (type, M x K) of SWEEP_SHAPES at
     n = 1, 2, 4, 8, 64 activation columns.  Each shape is uploaded in enough
     copies that one pass over them exceeds L2 twice (weights stream from HBM
-    as in decode), the copies are launched back to back, CUDA events time the
-    pass; achieved = algorithmic bytes (quantised weights + 4n(M+K)) per
+    as in decode), one pass of launches over the copies is captured in a CUDA
+    graph and replayed, CUDA events time the replays; achieved = algorithmic bytes (quantised weights + 4n(M+K)) per
     launch / average launch time."""
     import numpy as np
     import torch
@@ -309,16 +309,25 @@ def matvec_sweep(device, peak, l2_bytes=126 << 20):
             x = torch.randn(max(SWEEP_N), cols, device=f"cuda:{device}")
             y = torch.empty(max(SWEEP_N), rows, device=f"cuda:{device}")
             for n in SWEEP_N:
-                for m in mats:  # warm-up pass
+                for m in mats:  # warm-up pass (sizes the tensor-core scratch)
                     m.matvec(x.data_ptr(), n, y.data_ptr(), sp)
-                reps = max(1, 64 // copies)
+                torch.cuda.synchronize(device)
+                # one pass over the copies as a CUDA graph: the launches run
+                # back to back without the host's per-call cost in between
+                graph, cap = torch.cuda.CUDAGraph(), torch.cuda.Stream(device)
+                with torch.cuda.graph(graph, stream=cap, capture_error_mode="thread_local"):
+                    cs = torch.cuda.current_stream(device).cuda_stream
+                    for m in mats:
+                        m.matvec(x.data_ptr(), n, y.data_ptr(), cs)
+                graph.replay()
+                reps = max(3, 192 // copies)
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
                 for _ in range(reps):
-                    for m in mats:
-                        m.matvec(x.data_ptr(), n, y.data_ptr(), sp)
+                    graph.replay()
                 e1.record(stream)
                 e1.synchronize()
+                del graph
                 us = 1000.0 * e0.elapsed_time(e1) / (reps * copies)
                 alg = wbytes + 4 * n * (rows + cols)
                 gbs = alg / (us * 1e-6) / 1e9
@@ -329,7 +338,7 @@ def matvec_sweep(device, peak, l2_bytes=126 << 20):
             del x, y
             torch.cuda.empty_cache()
     n1 = [v["frac"] for k, v in out.items() if k.endswith("_n1")]
-    return {"kernel": "rpgb_matrix_matvec: Q4_K/Q6_K operator sweep (weights > L2, launches back to back)",
+    return {"kernel": "rpgb_matrix_matvec: Q4_K/Q6_K operator sweep (weights > L2, launches back to back in a CUDA graph)",
             "bound": "hbm", "peak": peak, "unit": "GB/s", "frac_n1_mean": round(sum(n1) / len(n1), 4),
             "shapes": out}
 

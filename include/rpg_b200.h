@@ -169,7 +169,11 @@ RPGB_API int32_t rpgb_matrix_dequant(int32_t matrix, int64_t row0, int64_t n_row
  * src/kernels_gpu.cu:939-975): n_tok == 1 uses the decode matvec, larger n
  * the prefill GEMM -- from 16 tokens (and rows a multiple of 128) the
  * tcgen05 tensor-core GEMM, which keeps fp16 operand scratch with the matrix
- * and returns only after the GEMM has finished. */
+ * (so calls on one matrix must be ordered: one stream, or events between
+ * streams).  Every path returns without waiting for the GPU and can be
+ * captured in a CUDA graph once a first call with the largest n_tok has run;
+ * a bounded device wait of the tensor-core GEMM that gave up is reported
+ * (-1) by the next call on the same matrix. */
 RPGB_API int32_t rpgb_matrix_matvec(int32_t matrix, const float* x_dev, int64_t n_tok, float* out_dev,
                                     void* stream);
 

@@ -30,11 +30,13 @@ struct MatrixEntry {
   int64_t rows = 0;  // logical rows (storage is padded to whole 32-row groups)
   DevMat m;
   void* mem = nullptr;
-  // tensor-core GEMM scratch (grown on demand) and its error word
+  // tensor-core GEMM scratch (grown on demand), its error word and the
+  // pinned host copy of that word the next call reads
   std::mutex tc_mu;
   __half* tc = nullptr;
   size_t tc_halves = 0;
   unsigned* err = nullptr;
+  unsigned* err_host = nullptr;
 };
 
 std::mutex g_mu;
@@ -397,6 +399,7 @@ void rpgb_matrix_free(int32_t matrix) {
     cudaFree(e->mem);
     cudaFree(e->tc);
     cudaFree(e->err);
+    if (e->err_host != nullptr) cudaFreeHost(e->err_host);
   } catch (...) {
   }
 }
@@ -453,9 +456,24 @@ int32_t rpgb_matrix_matvec(int32_t matrix, const float* x_dev, int64_t n_tok, fl
       g.out = out_dev;
       g.ldo = e->m.rows;
       if (n_tok >= kTcMinTokens && e->m.rows % 128 == 0) {
-        // tensor-core path: fp16 operand scratch kept with the matrix; the
-        // call waits for the GEMM to read its error word
+        // tensor-core path: fp16 operand scratch kept with the matrix.  The
+        // call does not wait for the GEMM (launches can be captured in a
+        // graph); the GEMM's error word is copied to pinned host memory
+        // behind it and the next call on the matrix reports a wait that gave up
         std::lock_guard<std::mutex> lk(e->tc_mu);
+        if (e->err == nullptr) {
+          RPGB_CUDA(cudaMalloc(&e->err, sizeof(unsigned)));
+          RPGB_CUDA(cudaMemset(e->err, 0, sizeof(unsigned)));
+          RPGB_CUDA(cudaMallocHost(&e->err_host, sizeof(unsigned)));
+          *e->err_host = 0;
+        }
+        const unsigned prev = *reinterpret_cast<volatile unsigned*>(e->err_host);
+        if (prev != 0) {
+          RPGB_CUDA(cudaStreamSynchronize(s));
+          RPGB_CUDA(cudaMemset(e->err, 0, sizeof(unsigned)));
+          *e->err_host = 0;
+          Throw("matvec: a bounded device wait of an earlier tensor-core GEMM on this matrix gave up (0x%x)", prev);
+        }
         const size_t need = TcGemmScratchHalves(e->m.rows, n_tok, e->m.cols);
         if (e->tc_halves < need) {
           RPGB_CUDA(cudaStreamSynchronize(s));
@@ -465,21 +483,11 @@ int32_t rpgb_matrix_matvec(int32_t matrix, const float* x_dev, int64_t n_tok, fl
           RPGB_CUDA(cudaMalloc(&e->tc, need * sizeof(__half)));
           e->tc_halves = need;
         }
-        if (e->err == nullptr) {
-          RPGB_CUDA(cudaMalloc(&e->err, sizeof(unsigned)));
-          RPGB_CUDA(cudaMemset(e->err, 0, sizeof(unsigned)));
-        }
         g.tc_scratch = e->tc;
         g.tc_scratch_halves = e->tc_halves;
         g.err = e->err;
         LaunchGemm(g, Epi::kStore, s);
-        unsigned err = 0;
-        RPGB_CUDA(cudaMemcpyAsync(&err, e->err, sizeof(unsigned), cudaMemcpyDeviceToHost, s));
-        RPGB_CUDA(cudaStreamSynchronize(s));
-        if (err != 0) {
-          RPGB_CUDA(cudaMemset(e->err, 0, sizeof(unsigned)));
-          Throw("matvec: a bounded device wait of the tensor-core GEMM gave up (0x%x)", err);
-        }
+        RPGB_CUDA(cudaMemcpyAsync(e->err_host, e->err, sizeof(unsigned), cudaMemcpyDeviceToHost, s));
       } else {
         LaunchGemm(g, Epi::kStore, s);
       }

@@ -106,7 +106,7 @@ Session::Session(const Model* m, int64_t max_seq) : m_(m), max_seq_(max_seq) {
   cv.Add(sizeof(int32_t));
   cv.Add(sizeof(unsigned));
   cv.Add(sizeof(unsigned));                   // grid barrier word
-  cv.Add(sizeof(int32_t));                    // steps done
+  cv.Add(sizeof(int32_t) * 2);                // steps done, host-sample request
   cv.Add(sizeof(int32_t) * kLoopMaxStop);     // stop ids
   cv.Add(sizeof(uint64_t) * ll_words_);       // tagged words of the decode loop
   cv.Add(sizeof(uint32_t) * c.n_kv_heads);    // attention tickets
@@ -133,11 +133,11 @@ Session::Session(const Model* m, int64_t max_seq) : m_(m), max_seq_(max_seq) {
   flag_ = cv.Take<int32_t>(1);
   err_ = cv.Take<unsigned>(1);
   bar_ = cv.Take<unsigned>(1);
-  steps_done_ = cv.Take<int32_t>(1);
+  steps_done_ = cv.Take<int32_t>(2);
   stop_dev_ = cv.Take<int32_t>(kLoopMaxStop);
   ll_ = cv.Take<uint64_t>(ll_words_);  // zeroed with the arena: tag 0 is never a valid tag
   tickets_loop_ = cv.Take<uint32_t>(c.n_kv_heads);
-  RPGB_CUDA(cudaMallocHost(&loop_host_, sizeof(int32_t)));
+  RPGB_CUDA(cudaMallocHost(&loop_host_, sizeof(int32_t) * 2));
   if (m->tp() != nullptr) {  // its own allocation: the CUDA IPC handle covers exactly this buffer
     xbuf_words_ = LoopExchangeWords(c.hidden, m->num_sms());
     RPGB_CUDA(cudaMalloc(&xbuf_, sizeof(uint64_t) * xbuf_words_));
@@ -668,10 +668,11 @@ int Session::Generate(const SampleOpts& opt, uint64_t seed, int32_t max_tokens, 
   }
   EnqueueSample(opt, seed, 0);
 
-  // Tensor parallel greedy decode runs in the loop kernel with the ranks'
-  // partials exchanged over NVLink (after TpAttach); otherwise a
-  // tensor-parallel step runs as the step graph with NCCL between launches.
-  const bool loop_tp = m_->tp() == nullptr || (tp_attached_ && !(opt.temperature > 0.0f) && step_logits == nullptr);
+  // Tensor parallel decode runs in the loop kernel with the ranks' partials
+  // and sampler candidates exchanged over NVLink (after TpAttach; greedy or
+  // the fast sampler); otherwise a tensor-parallel step runs as the step
+  // graph with NCCL between launches.
+  const bool loop_tp = m_->tp() == nullptr || (tp_attached_ && LoopMode(opt) != 2 && step_logits == nullptr);
   if (LoopSupportsGroup(c.group()) && loop_tp && std::getenv("RPGB_DECODE_GRAPH") == nullptr) {
     return GenerateLoop(opt, seed, max_tokens, stop, n_stop, out, step_logits, start);
   }
@@ -756,6 +757,20 @@ int Session::Generate(const SampleOpts& opt, uint64_t seed, int32_t max_tokens, 
   return produced;
 }
 
+// The decode loop's sampler: 0 greedy, 1 the fast candidate path (1 <
+// top_k <= kFastTopK, each block's lm_head rows one candidate slice), 2 the
+// general one-block sampler.
+int Session::LoopMode(const SampleOpts& opt) const {
+  const int sms = m_->num_sms();
+  const int rows = m_->lm_head().rows;  // this GPU's rows of the vocabulary
+  const int lm_rows_per_block = (rows / 16 + sms - 1) / sms * 16;
+  if (!(opt.temperature > 0.0f)) return 0;
+  if (opt.top_k > 1 && opt.top_k <= kFastTopK && opt.top_k < rows && sms <= kCandBlocks && lm_rows_per_block <= 2048) {
+    return 1;
+  }
+  return 2;
+}
+
 LoopParams Session::MakeLoopParams(const SampleOpts& opt, uint64_t seed) const {
   const ModelMeta& c = m_->meta();
   LoopParams lp;
@@ -794,16 +809,7 @@ LoopParams Session::MakeLoopParams(const SampleOpts& opt, uint64_t seed) const {
   lp.top_k = opt.top_k;
   lp.top_p = opt.top_p;
   lp.seed = seed;
-  const int sms = m_->num_sms();
-  const int lm_rows_per_block = (m_->lm_head().rows / 16 + sms - 1) / sms * 16;
-  if (!(opt.temperature > 0.0f)) {
-    lp.mode = 0;
-  } else if (opt.top_k > 1 && opt.top_k <= kFastTopK && opt.top_k < c.vocab && sms <= kCandBlocks &&
-             lm_rows_per_block <= 2048) {
-    lp.mode = 1;
-  } else {
-    lp.mode = 2;
-  }
+  lp.mode = LoopMode(opt);
   lp.cand_val = cand_val_;
   lp.cand_idx = cand_idx_;
   lp.cand_cnt = cand_cnt_;
@@ -852,6 +858,7 @@ int Session::GenerateLoop(const SampleOpts& opt, uint64_t seed, int32_t max_toke
     RPGB_CUDA(cudaMemcpyAsync(stop_dev_, stop, sizeof(int32_t) * n_stop, cudaMemcpyHostToDevice, s));
   }
   lp.n_stop = dev_stop ? n_stop : 0;
+  RPGB_CUDA(cudaMemsetAsync(steps_done_ + 1, 0, sizeof(int32_t), s));
   // With stop ids the device cannot see, chunks stay short so little work runs past a stop.
   const int chunk = dev_stop ? max_tokens : 8;
   if (step_logits != nullptr) {
@@ -887,11 +894,12 @@ int Session::GenerateLoop(const SampleOpts& opt, uint64_t seed, int32_t max_toke
     LaunchDecodeLoop(lp, c.group(), m_->num_sms(), s);
     if (lp.tp > 0) GatherLogits(s);  // the next call samples its first token from the whole row
     loop_ready_ = true;
-    RPGB_CUDA(cudaMemcpyAsync(loop_host_, steps_done_, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    RPGB_CUDA(cudaMemcpyAsync(loop_host_, steps_done_, sizeof(int32_t) * 2, cudaMemcpyDeviceToHost, s));
     RPGB_CUDA(cudaMemcpyAsync(host_ids_ + produced, out_ids_ + start + produced, sizeof(int32_t) * todo,
                               cudaMemcpyDeviceToHost, s));
     RPGB_CUDA(cudaStreamSynchronize(s));
-    const int done = *loop_host_;
+    const int done = loop_host_[0];
+    const bool host_sample = loop_host_[1] != 0;
     unsigned err = 0;
     RPGB_CUDA(cudaMemcpy(&err, err_, sizeof(unsigned), cudaMemcpyDeviceToHost));
     if (err != 0 || done < 1 || done > todo) {
@@ -923,6 +931,12 @@ int Session::GenerateLoop(const SampleOpts& opt, uint64_t seed, int32_t max_toke
       }
     }
     produced += take;
+    if (host_sample) {
+      // the tensor-parallel sampler's candidates overflowed at the last step:
+      // the next token comes from the gathered row (counter = the new len)
+      RPGB_CUDA(cudaMemsetAsync(steps_done_ + 1, 0, sizeof(int32_t), s));
+      if (!stopped && produced < max_tokens) EnqueueSample(opt, seed, 0);
+    }
   }
   kernels_per_step_ = 1;
   std::memcpy(out, host_ids_, sizeof(int32_t) * produced);

@@ -93,6 +93,7 @@ class Session {
   int GenerateLoop(const SampleOpts& opt, uint64_t seed, int32_t max_tokens, const int32_t* stop, int32_t n_stop,
                    int32_t* out, float* step_logits, int64_t start);
   LoopParams MakeLoopParams(const SampleOpts& opt, uint64_t seed) const;
+  int LoopMode(const SampleOpts& opt) const;
   void EnqueueSample(const SampleOpts& opt, uint64_t seed, int pos_bump, bool pdl = false, int32_t trace_id = -1);
   void EnsurePrefill(int64_t n);
   void DropGraph();
@@ -129,7 +130,7 @@ class Session {
   unsigned* bar_ = nullptr;       // grid barrier word
   int32_t* steps_done_ = nullptr;
   int32_t* stop_dev_ = nullptr;   // [kLoopMaxStop]
-  int32_t* loop_host_ = nullptr;  // pinned: steps done
+  int32_t* loop_host_ = nullptr;  // pinned: steps done, host-sample request
   float* step_logits_dev_ = nullptr;  // [cap][vocab]: per-step logits of a loop launch (parity checks)
   int64_t step_logits_cap_ = 0;
   int loop_splits_ = 1;

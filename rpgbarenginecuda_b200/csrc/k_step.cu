@@ -529,6 +529,12 @@ __device__ __forceinline__ size_t XRed(const LoopParams& p, int sel, int src, in
 __device__ __forceinline__ size_t XAm(const LoopParams& p, int src, int blk) {
   return static_cast<size_t>(2 * kLoopMaxTp) * p.hidden + 2 * (static_cast<size_t>(src) * gridDim.x + blk);
 }
+// The sampler's candidates of rank `src`: a count word, kFastTopK values,
+// kFastTopK vocabulary ids.
+constexpr int kXCandWords = 1 + 2 * kFastTopK;
+__device__ __forceinline__ size_t XCand(const LoopParams& p, int src) {
+  return static_cast<size_t>(2 * kLoopMaxTp) * (p.hidden + gridDim.x) + static_cast<size_t>(src) * kXCandWords;
+}
 
 __device__ __forceinline__ uint32_t TagOf(const LoopParams& p, int step, int layer, int kind) {
   return p.epoch0 + static_cast<uint32_t>(step) * static_cast<uint32_t>(5 * p.n_layers + 2) +
@@ -933,12 +939,13 @@ __device__ void MvPhase(const LoopParams& p, const GeoTable& gt, int kind, int l
     }
   } else if (kind == kLm && p.mode == 1) {
     __syncthreads();
-    const int row0 = g.t0 * kTile;
+    const int row0 = g.t0 * kTile;  // this GPU's rows of the vocabulary start at vocab0
     int len = n_rows;
-    if (row0 + len > p.vocab) len = p.vocab - row0 > 0 ? p.vocab - row0 : 0;
+    if (row0 + len > p.lm_head.rows) len = p.lm_head.rows - row0 > 0 ? p.lm_head.rows - row0 : 0;
     unsigned* hist = reinterpret_cast<unsigned*>(scratch + kSliceRows * 4);
-    smp::SliceCandidates(vals, len, row0, p.top_k, hist, s_sel, s_cnt, p.cand_val + blockIdx.x * kFastTopK,
-                         p.cand_idx + blockIdx.x * kFastTopK, p.cand_cnt + blockIdx.x);
+    smp::SliceCandidates(vals, len, p.vocab0 + row0, p.top_k, hist, s_sel, s_cnt,
+                         p.cand_val + blockIdx.x * kFastTopK, p.cand_idx + blockIdx.x * kFastTopK,
+                         p.cand_cnt + blockIdx.x);
   }
 }
 
@@ -1196,6 +1203,61 @@ __device__ void AttnPhase(const LoopParams& p, const GeoTable& gt, int layer, in
 
 // ------------------------------------------------------------------ the kernel
 
+// ------------------------------------------------------------------ tensor parallel sampling
+
+// The candidates every rank sent into this rank's exchange buffer (tagged
+// words; each read waits for its tag).
+struct PeerCands {
+  const LoopParams* p;
+  const uint64_t* base;  // this rank's XCand(0)
+  uint32_t tag;
+  __device__ __forceinline__ int Count(int s) const {
+    return static_cast<int>(static_cast<uint32_t>(WaitPeer(*p, base + static_cast<size_t>(s) * kXCandWords, tag)));
+  }
+  __device__ __forceinline__ void Load(int j, float& v, int& i) const {
+    const int s = j / kFastTopK, k = j - s * kFastTopK;
+    const uint64_t* w = base + static_cast<size_t>(s) * kXCandWords + 1 + k;
+    v = ValOf(WaitPeer(*p, w, tag));
+    i = static_cast<int>(static_cast<uint32_t>(WaitPeer(*p, w + kFastTopK, tag)));
+  }
+};
+
+// The fast sampler over the whole vocabulary when each rank holds the
+// lm_head rows of one slice of it.  Every block reduces this rank's slice
+// candidates to its survivors (the candidates at or above this rank's k-th
+// largest scaled value: a superset of the global top_k's members from this
+// slice); blocks 0 .. tp-1 send them to ranks 0 .. tp-1; then every block
+// of every rank runs the small sampler on the tp survivor sets (values
+// already scaled, so temperature 1) and draws the same token.  Returns -1 in
+// every block of every rank when a survivor set overflows (ties at the
+// k-th value): the host then samples that token from the gathered row.
+template <class Mark>
+__device__ int TpSample(const LoopParams& p, int step, int64_t pos, const Smem& sm, Mark mark) {
+  unsigned char* scratch = sm.scratch();
+  const int tid = threadIdx.x;
+  const uint32_t tag = TagOf(p, step, p.n_layers - 1, kLm);
+  const int c = smp::SmallSurvivors<kNT>(smp::GlobalCands{p.cand_val, p.cand_idx, p.cand_cnt},
+                                         static_cast<int>(gridDim.x), p.temperature, p.top_k, scratch, kSmallCap,
+                                         mark);
+  if (static_cast<int>(blockIdx.x) < p.tp) {
+    const float* cv = reinterpret_cast<const float*>(scratch);
+    const int* ci = reinterpret_cast<const int*>(cv + kSmallCap);
+    uint64_t* dst = p.xpeer[blockIdx.x] + XCand(p, p.tp_rank);
+    const int cnt = c < 0 || c > kFastTopK ? -1 : c;
+    const uint64_t hi = static_cast<uint64_t>(tag) << 32;
+    for (int i = tid; i < cnt; i += kNT) {
+      StSys(dst + 1 + i, Pack(cv[i], tag));
+      StSys(dst + 1 + kFastTopK + i, hi | static_cast<uint32_t>(ci[i]));
+    }
+    if (tid == 0) StSys(dst, hi | static_cast<uint32_t>(cnt));
+  }
+  __syncthreads();  // the survivors' scratch is reused below
+  const int c2 = smp::SmallSurvivors<kNT>(PeerCands{&p, p.xpeer[p.tp_rank] + XCand(p, 0), tag}, p.tp, 1.0f,
+                                          p.top_k, scratch, kSmallCap, mark);
+  if (c2 < 0) return -1;
+  return smp::SmallDraw<kNT>(c2, p.top_p, p.seed, pos + 1, scratch, kSmallCap, mark);
+}
+
 template <int G>
 __global__ void __launch_bounds__(kNT, 1) DecodeLoopKernel(const LoopParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -1345,7 +1407,16 @@ __global__ void __launch_bounds__(kNT, 1) DecodeLoopKernel(const LoopParams p) {
       __syncthreads();
       next = s_tok;
     } else {
-      if (p.mode == 1) {
+      if (p.mode == 1 && p.tp > 0) {
+        next = TpSample(p, step, pos, sm, [&](int k) { TraceMark(p, clk, k); });
+        if (next < 0) {
+          // every block of every rank alike: the launch ends after this step
+          // and the host samples the next token from the gathered row
+          if (blockIdx.x == 0 && tid == 0) p.steps_done[1] = 1;
+          steps = step + 1;
+          break;
+        }
+      } else if (p.mode == 1) {
         next = smp::SmallSample<kNT>(p.cand_val, p.cand_idx, p.cand_cnt, static_cast<int>(gridDim.x), p.temperature,
                                      p.top_k, p.top_p, p.seed, pos + 1, sm.scratch(), kSmallCap,
                                      [&](int k) { TraceMark(p, clk, k); });
@@ -1405,7 +1476,7 @@ constexpr int kSmemMax = 227 * 1024;
 bool LoopSupportsGroup(int group) { return group == 2 || group == 4; }
 
 size_t LoopExchangeWords(int hidden, int grid) {
-  return static_cast<size_t>(2 * kLoopMaxTp) * hidden + static_cast<size_t>(2 * kLoopMaxTp) * grid;
+  return static_cast<size_t>(2 * kLoopMaxTp) * (hidden + grid) + static_cast<size_t>(kLoopMaxTp) * kXCandWords;
 }
 
 size_t LoopPartialWords(int n_kv, int group, int splits) {
@@ -1449,7 +1520,8 @@ void LaunchDecodeLoop(const LoopParams& in, int group, int num_sms, cudaStream_t
   if (p.tp > 0) {
     RPGB_CHECK(p.tp <= kLoopMaxTp && p.tp_rank >= 0 && p.tp_rank < p.tp, "decode loop: rank %d of %d", p.tp_rank,
                p.tp);
-    RPGB_CHECK(p.mode == 0, "decode loop: tensor parallel decode is greedy");
+    RPGB_CHECK(p.mode == 0 || (p.mode == 1 && p.top_k < p.lm_head.rows && num_sms >= p.tp),
+               "decode loop: tensor parallel decode is greedy or the fast sampler (1 < top_k <= %d)", kFastTopK);
     for (int k = 0; k < p.tp; ++k) RPGB_CHECK(p.xpeer[k] != nullptr, "decode loop: rank %d's buffer missing", k);
   }
   p.nb_max = std::max({p.hidden, qd, p.ffn}) / 256;

@@ -264,7 +264,7 @@ struct LoopParams {
   int32_t n_steps = 1;
   const int32_t* stop = nullptr;  // device [n_stop]
   int32_t n_stop = 0;
-  int32_t* steps_done = nullptr;
+  int32_t* steps_done = nullptr;  // [2]: steps run; 1 when the host must sample the next token
   unsigned* bar = nullptr;  // grid barrier word
   unsigned* err = nullptr;  // nonzero after a bounded wait gave up
   int32_t splits = 1;       // attention blocks per KV head

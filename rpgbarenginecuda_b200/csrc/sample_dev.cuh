@@ -407,24 +407,37 @@ __device__ int GeneralSample(const float* logits, int n, float temperature, int 
 }
 
 // The fast path's second half: the whole pipeline on the candidates of
-// n_slices slices (cand_cnt[s] candidates at cand_val/cand_idx + 64 s).
-// Returns the token in every thread, or -1 when a slice overflowed or more
-// than `cap` candidates lie above the lower bound (the caller then runs
-// GeneralSample).  scratch: 16 * cap bytes of shared memory.  mark(k) is
-// called by every thread after stage k (1: bound and compaction, 2: k-th
-// value, 3: softmax, 4: top_p), for timelines.
+// n_slices slices (slice s: src.Count(s) candidates at src.Load(64 s + i)).
+// SmallSurvivors keeps the candidates at or above the k-th largest
+// temperature-scaled value, ordered by vocabulary index, in scratch (values
+// at cv, ids at ci) and returns their count -- or -1 when a slice
+// overflowed or more than `cap` candidates lie above the lower bound (the
+// caller then runs GeneralSample).  SmallDraw turns survivors into the
+// token (softmax, top_p, the inverse draw); SmallSample is both.  scratch:
+// 16 * cap bytes of shared memory.  mark(k) is called by every thread after
+// stage k (1: bound and compaction, 2: k-th value, 3: softmax, 4: top_p),
+// for timelines.
 struct NoMark {
   __device__ void operator()(int) const {}
 };
-template <int NT, class Mark = NoMark>
-__device__ int SmallSample(const float* cand_val, const int32_t* cand_idx, const int32_t* cand_cnt, int n_slices,
-                           float temperature, int top_k, float top_p, uint64_t seed, int64_t counter,
-                           unsigned char* scratch, int cap, Mark mark = Mark()) {
+// Candidates in global memory (the lm_head slices of this GPU).
+struct GlobalCands {
+  const float* val;
+  const int32_t* idx;
+  const int32_t* cnt;
+  __device__ __forceinline__ int Count(int s) const { return __ldcg(cnt + s); }
+  __device__ __forceinline__ void Load(int j, float& v, int& i) const {
+    v = __ldcg(val + j);
+    i = __ldcg(idx + j);
+  }
+};
+template <int NT, class Src, class Mark = NoMark>
+__device__ int SmallSurvivors(const Src& src, int n_slices, float temperature, int top_k, unsigned char* scratch,
+                              int cap, Mark mark = Mark()) {
   float* cv = reinterpret_cast<float*>(scratch);  // [cap]
   int* ci = reinterpret_cast<int*>(cv + cap);     // [cap]
   float* kv = reinterpret_cast<float*>(ci + cap);  // kept values / probs [cap]
   int* kix = reinterpret_cast<int*>(kv + cap);     // kept indices
-  __shared__ int s_tok;
   __shared__ unsigned hist[256];
   __shared__ uint32_t s_sel[2];
   __shared__ int s_bad, s_m, s_c;
@@ -433,7 +446,7 @@ __device__ int SmallSample(const float* cand_val, const int32_t* cand_idx, const
   __shared__ int s_cnt[kCandBlocks];
   __shared__ float s_hmin[(kCandBlocks * kFastTopK + 31) / 32];
   __shared__ float s_t0;
-  if (tid < n_slices) s_cnt[tid] = __ldcg(cand_cnt + tid);
+  if (tid < n_slices) s_cnt[tid] = src.Count(tid);
   if (tid == 0) {
     s_bad = 0;
     s_m = 0;
@@ -453,9 +466,11 @@ __device__ int SmallSample(const float* cand_val, const int32_t* cand_idx, const
   for (int r = 0; r < kRounds; ++r) {
     const int j = tid + r * NT;
     const int b = j / kFastTopK, i = j - b * kFastTopK;
-    const bool use = j < total && i < s_cnt[b];
-    rv[r] = use ? __ldcg(cand_val + j) : INFINITY;
-    ri[r] = use ? __ldcg(cand_idx + j) : -1;
+    float v = INFINITY;
+    int ix = -1;
+    if (j < total && i < s_cnt[b]) src.Load(j, v, ix);
+    rv[r] = v;
+    ri[r] = ix;
   }
 #pragma unroll
   for (int r = 0; r < kRounds; ++r) {
@@ -515,6 +530,17 @@ __device__ int SmallSample(const float* cand_val, const int32_t* cand_idx, const
     ci[rank] = kix[i];
   }
   __syncthreads();
+  return c;
+}
+
+template <int NT, class Mark = NoMark>
+__device__ __noinline__ int SmallDraw(int c, float top_p, uint64_t seed, int64_t counter, unsigned char* scratch, int cap,
+                         Mark mark = Mark()) {
+  float* cv = reinterpret_cast<float*>(scratch);  // [cap]
+  int* ci = reinterpret_cast<int*>(cv + cap);     // [cap]
+  float* kv = reinterpret_cast<float*>(ci + cap);  // [cap]
+  const int tid = threadIdx.x;
+  __shared__ int s_tok;
   // ---- softmax over the survivors (serial, index order; c is k plus ties)
   float* v = cv;  // probabilities, index-ordered
   const int* ix = ci;
@@ -623,6 +649,16 @@ __device__ int SmallSample(const float* cand_val, const int32_t* cand_idx, const
   }
   __syncthreads();
   return s_tok;
+}
+
+template <int NT, class Mark = NoMark>
+__device__ int SmallSample(const float* cand_val, const int32_t* cand_idx, const int32_t* cand_cnt, int n_slices,
+                           float temperature, int top_k, float top_p, uint64_t seed, int64_t counter,
+                           unsigned char* scratch, int cap, Mark mark = Mark()) {
+  const int c = SmallSurvivors<NT>(GlobalCands{cand_val, cand_idx, cand_cnt}, n_slices, temperature, top_k, scratch,
+                                   cap, mark);
+  if (c < 0) return -1;
+  return SmallDraw<NT>(c, top_p, seed, counter, scratch, cap, mark);
 }
 
 }  // namespace smp

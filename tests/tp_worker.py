@@ -32,7 +32,9 @@ def run(m, max_seq=512, attach=False):
     out = {"prefill": s.prefill(toks)}
     ids, steps = s.generate(SampleOptions(0.0, 0, 1.0), 0, 32, step_logits=True)
     out["greedy"], out["greedy_steps"] = np.asarray(ids), np.asarray(steps)
-    s.prefill(synthetic.seeded_tokens(40, 1, m.vocab), want_logits=False)
+    app = synthetic.seeded_tokens(40, 1, m.vocab)
+    s.prefill(app, want_logits=False)
+    out["sampled_start"] = np.asarray(len(s))
     sids, ssteps = s.generate(SampleOptions(0.7, 20, 0.8), 1234, 24, step_logits=True)
     out["sampled"], out["sampled_steps"] = np.asarray(sids), np.asarray(ssteps)
     # a short prompt (fewer than 16 tokens) takes the per-token matvec prefill
@@ -47,6 +49,14 @@ def run(m, max_seq=512, attach=False):
     out["greedy_loop2"] = np.asarray(s2.generate(SampleOptions(0.0, 0, 1.0), 0, 16))
     out["len_loop"] = np.asarray(len(s2))
     s2.close()
+    # the sampled tokens again, from the same history, in the one-launch loop
+    # (the fast sampler; split: candidates exchanged between the GPUs)
+    s3 = Session(m, max_seq)
+    if attach:
+        s3.attach_tp()
+    s3.prefill(np.concatenate([toks, out["greedy"], app]).astype(np.int32), want_logits=False)
+    out["sampled_loop"] = np.asarray(s3.generate(SampleOptions(0.7, 20, 0.8), 1234, 24))
+    s3.close()
     return out
 
 
