@@ -37,7 +37,7 @@ using namespace smp;
 constexpr int kGenThreads = 1024;
 constexpr int kCandThreads = 256;
 constexpr int kSliceMax = 2048;
-constexpr int kSmallThreads = 1024;
+constexpr int kSmallThreads = 512;
 constexpr int kMaxCand = kCandBlocks * kFastTopK;
 
 __device__ __forceinline__ int64_t Counter(const SampleParams& p) {

@@ -130,7 +130,7 @@ __device__ __forceinline__ MvShape ShapeOf(const LoopParams& p, int kind) {
 
 struct Geo {
   int t0, t1, nb, u0, u1;
-  int seg0, uoff0, run0;  // first unit of the warp: segment, unit offset inside it, units to the segment's end
+  int uoff0;  // first unit of the warp: block-group offset inside its matrix
 };
 
 // Segments of a phase's row space: q, k, v for the qkv phase, one matrix otherwise.
@@ -167,9 +167,8 @@ __device__ __forceinline__ Geo MvGeo(const LoopParams& p, int kind, int warp) {
   g.u1 = (warp + 1) * U / kNW;
   const int tile = g.t0 + g.u0 / g.nb, b = g.u0 % g.nb;
   int st0 = 0;
-  g.seg0 = SegOfTile(p, kind, tile, &st0);
+  SegOfTile(p, kind, tile, &st0);
   g.uoff0 = (tile - st0) * g.nb + b;
-  g.run0 = (st0 + SegTiles(p, kind, g.seg0) - tile) * g.nb - b;
   return g;
 }
 
@@ -177,7 +176,28 @@ __device__ __forceinline__ Geo MvGeo(const LoopParams& p, int kind, int warp) {
 // once per launch (it is the same for all layers and steps).
 struct GeoTable {
   Geo g[6][kNW];  // indexed by Kind (the attention row is unused)
+  int att_h, att_s;  // this block's KV head and split (att_h = n_kv: no attention work)
 };
+
+// A warp's attention chunks at one step: the weight stream's walk enters an
+// attention phase once per layer, the geometry changes once per step.
+struct AttnCache {
+  int step, n, c0;
+};
+__shared__ AttnCache g_attc[kNW];
+
+// A warp's weight stream of one layer as runs of consecutive block groups
+// (built once per launch): slots 0-2 the q, k and v parts of its qkv units,
+// 3 the attention chunks (counted per step, g_attc), 4 o, 5 gate/up, 6 down,
+// 7 lm_head (after the last layer).  Within one matrix the block groups of
+// consecutive units are contiguous (tile-major), so a run is (offset, count).
+constexpr int kRunAttn = 3, kRunDown = 6, kRunLm = 7, kRuns = 8;
+struct Run {
+  int off;  // first block group inside the matrix
+  int n;    // units
+  int mat;  // the layer's matrix (0-5: q, k, v, o, gate/up, down); lm_head for kRunLm
+};
+__shared__ Run g_runs[kNW][kRuns];
 
 // Per layer: block-group bases of q, k, v, o, gate/up, down, the four norm
 // weights and which matrices are Q6_K -- a copy of the layer table in shared
@@ -188,6 +208,11 @@ struct LayerRow {
   uint32_t q6;           // bit i: matrix i is Q6_K (else Q4_K)
 };
 
+// Matrix `seg` of a phase in layer `layer`: its block groups and type.
+__device__ __forceinline__ int MatIdx(int kind, int seg) {
+  return kind == kQkv ? seg : (kind == kO ? 3 : (kind == kGu ? 4 : 5));
+}
+
 __shared__ GeoTable g_geo;
 __shared__ LayerRow g_layers[kMaxLayers];
 
@@ -195,7 +220,35 @@ __device__ __forceinline__ void FillTables(const LoopParams& p) {
   const int tid = threadIdx.x;
   if (tid < 6 * kNW) {
     const int kind = tid / kNW, warp = tid - kind * kNW;
-    if (kind != kAttn) g_geo.g[kind][warp] = MvGeo(p, kind, warp);
+    if (kind != kAttn) {
+      const Geo g = MvGeo(p, kind, warp);
+      g_geo.g[kind][warp] = g;
+      if (kind == kQkv) {
+        // split the warp's units at the q / k / v boundaries
+        for (int sg = 0; sg < 3; ++sg) g_runs[warp][sg] = Run{0, 0, sg};
+        int u = g.u0;
+        while (u < g.u1) {
+          const int tile = g.t0 + u / g.nb, b = u % g.nb;
+          int st0 = 0;
+          const int sg = SegOfTile(p, kind, tile, &st0);
+          const int seg_end = (st0 + SegTiles(p, kind, sg) - g.t0) * g.nb;  // block unit index where sg ends
+          const int n = (seg_end < g.u1 ? seg_end : g.u1) - u;
+          g_runs[warp][sg] = Run{(tile - st0) * g.nb + b, n, sg};
+          u += n;
+        }
+      } else {
+        const int slot = kind == kLm ? kRunLm : kind + 2;  // o 4, gate/up 5, down 6
+        g_runs[warp][slot] = Run{g.uoff0, g.u1 - g.u0, kind == kLm ? 6 : MatIdx(kind, 0)};
+      }
+    } else {
+      g_attc[warp].step = -1;
+      g_runs[warp][kRunAttn] = Run{0, 0, -1};
+    }
+    if (tid == 0) {
+      const int c = static_cast<int>(blockIdx.x), S = p.splits;
+      g_geo.att_h = c < p.n_kv * S ? c / S : p.n_kv;
+      g_geo.att_s = c < p.n_kv * S ? c - (c / S) * S : 0;
+    }
   } else if (tid - 6 * kNW < p.n_layers) {
     const int l = tid - 6 * kNW;
     const DevLayer& L = p.layers[l];
@@ -214,17 +267,9 @@ __device__ __forceinline__ void FillTables(const LoopParams& p) {
   }
 }
 
-// Matrix `seg` of a phase in layer `layer`: its block groups and type.
-__device__ __forceinline__ int MatIdx(int kind, int seg) {
-  return kind == kQkv ? seg : (kind == kO ? 3 : (kind == kGu ? 4 : 5));
-}
 __device__ __forceinline__ uint32_t SegType(const LoopParams& p, int kind, int layer, int seg) {
   if (kind == kLm) return p.lm_head.type;
   return (g_layers[layer].q6 >> MatIdx(kind, seg)) & 1u ? 14u : 12u;
-}
-__device__ __forceinline__ const uint8_t* SegBase(const LoopParams& p, int kind, int layer, int seg) {
-  if (kind == kLm) return p.lm_head.q;
-  return g_layers[layer].w[MatIdx(kind, seg)];
 }
 
 // Splits of a KV head that hold positions at this step: sixteen chunks (one
@@ -240,14 +285,12 @@ struct AttnGeo {
   int h, c0, c1;  // KV head, chunk range of this block (empty for an idle block)
 };
 
-__device__ __forceinline__ AttnGeo AttnOf(const LoopParams& p, int64_t pos) {
+__device__ __forceinline__ AttnGeo AttnOf(const LoopParams& p, const GeoTable& gt, int64_t pos) {
   AttnGeo a;
-  const int S = p.splits;
-  const int c = static_cast<int>(blockIdx.x);
-  a.h = c / S;
-  const int s = c - a.h * S;
+  a.h = gt.att_h;
+  const int s = gt.att_s;
   const int se = EffSplits(p, pos);
-  if (c >= p.n_kv * S || s >= se) {
+  if (a.h >= p.n_kv || s >= se) {
     a.c0 = a.c1 = 0;
     return a;
   }
@@ -265,48 +308,66 @@ __device__ __forceinline__ int WarpChunks(const AttnGeo& a, int warp) {
 // ------------------------------------------------------------------ the per-warp weight stream
 
 struct Cursor {
-  int step, layer, kind, j, n;
-  int seg, run;        // matvec: segment and units left in the current contiguous run of block groups
-  uint32_t bytes;      // matvec: bytes of one unit of the run
-  const uint8_t* src;  // matvec: next block group; attention: K row 0 of (layer, head)
-  int c0;              // attention: first chunk of this block
+  int step, layer, ri, j, n;  // run slot ri of (step, layer); unit j of its n
+  uint32_t bytes;             // matvec: bytes of one unit of the run
+  const uint8_t* src;         // matvec: next block group; attention: K row 0 of (layer, head)
+  int c0;                     // attention: first chunk of this block
 };
 
-// Enters the next phase with units (lane 0).
-__device__ __forceinline__ void NextPhase(const LoopParams& p, const GeoTable& gt, Cursor& c, int64_t pos0,
-                                          int warp) {
-  while (c.j >= c.n && c.step < p.n_steps) {
-    if (c.kind == kLm) {
-      ++c.step;
-      c.layer = 0;
-      c.kind = kQkv;
-    } else if (c.kind == kDown) {
-      ++c.layer;
-      c.kind = c.layer == p.n_layers ? kLm : kQkv;
-    } else {
-      ++c.kind;
+// Loads run slot c.ri of (c.step, c.layer) into the cursor (lane 0).
+__device__ __forceinline__ void EnterRun(const LoopParams& p, const GeoTable& gt, Cursor& c, int64_t pos0, int warp) {
+  if (c.ri == kRunAttn) {
+    AttnCache& ac = g_attc[warp];
+    if (ac.step != c.step) {
+      const AttnGeo a = AttnOf(p, gt, pos0 + c.step);
+      ac.step = c.step;
+      ac.n = WarpChunks(a, warp);
+      ac.c0 = a.c0;
     }
-    c.j = 0;
-    c.n = 0;
-    if (c.step >= p.n_steps) break;
-    if (c.kind == kAttn) {
-      const AttnGeo a = AttnOf(p, pos0 + c.step);
-      c.n = WarpChunks(a, warp);
-      c.c0 = a.c0;
-      c.src = reinterpret_cast<const uint8_t*>(p.kc + static_cast<int64_t>(c.layer) * p.layer_elems +
-                                               static_cast<int64_t>(a.h) * p.max_seq * kD);
-    } else {
-      const Geo& g = gt.g[c.kind][warp];
-      c.n = g.u1 - g.u0;
-      c.run = 0;
-    }
+    c.n = ac.n;
+    c.c0 = ac.c0;
+    c.src = reinterpret_cast<const uint8_t*>(p.kc + static_cast<int64_t>(c.layer) * p.layer_elems +
+                                             static_cast<int64_t>(gt.att_h) * p.max_seq * kD);
+    return;
+  }
+  const Run r = g_runs[warp][c.ri];
+  c.n = r.n;
+  if (r.n > 0) {
+    const bool lm = c.ri == kRunLm;
+    const uint32_t type = lm ? p.lm_head.type : ((g_layers[c.layer].q6 >> r.mat) & 1u ? 14u : 12u);
+    c.bytes = static_cast<uint32_t>(dev::GroupBytesOf(type));
+    c.src = (lm ? p.lm_head.q : g_layers[c.layer].w[r.mat]) + static_cast<int64_t>(r.off) * c.bytes;
   }
 }
 
-// Requests unit c.j of the cursor's phase into `dst` and advances (lane 0 only).
+// Moves past finished and empty runs to the next unit of the stream (lane 0).
+__device__ __forceinline__ void NextRun(const LoopParams& p, const GeoTable& gt, Cursor& c, int64_t pos0, int warp) {
+  while (c.j >= c.n && c.step < p.n_steps) {
+    c.j = 0;
+    if (c.ri == kRunLm) {
+      ++c.step;
+      c.layer = 0;
+      c.ri = 0;
+    } else if (c.ri == kRunDown) {
+      if (c.layer + 1 == p.n_layers) {
+        c.ri = kRunLm;
+      } else {
+        ++c.layer;
+        c.ri = 0;
+      }
+    } else {
+      ++c.ri;
+    }
+    c.n = 0;
+    if (c.step >= p.n_steps) break;
+    EnterRun(p, gt, c, pos0, warp);
+  }
+}
+
+// Requests unit c.j of the cursor's run into `dst` and advances (lane 0 only).
 __device__ __forceinline__ void IssueUnit(const LoopParams& p, const GeoTable& gt, Cursor& c, int64_t pos0, int warp,
                                           uint8_t* dst, uint64_t* bar) {
-  if (c.kind == kAttn) {
+  if (c.ri == kRunAttn) {
     // K rows then V rows (at +1024 B) of the chunk's positions from earlier steps
     const int64_t pos = pos0 + c.step;
     const int64_t r0 = static_cast<int64_t>(c.c0 + warp + kNW * c.j) * kChunk;
@@ -320,28 +381,11 @@ __device__ __forceinline__ void IssueUnit(const LoopParams& p, const GeoTable& g
       dev::BulkG2S(dst + kChunk * kD * 2, src + p.v_minus_k, bytes, bar);
     }
   } else {
-    if (c.run == 0) {  // start of the warp's units in this phase, or of the next segment
-      const Geo& g = gt.g[c.kind][warp];
-      int uoff;
-      if (c.j == 0) {
-        c.seg = g.seg0;
-        uoff = g.uoff0;
-        c.run = g.run0;
-      } else {
-        ++c.seg;
-        uoff = 0;
-        c.run = SegTiles(p, c.kind, c.seg) * g.nb;
-      }
-      c.bytes = static_cast<uint32_t>(dev::GroupBytesOf(SegType(p, c.kind, c.layer, c.seg)));
-      c.src = SegBase(p, c.kind, c.layer, c.seg) + static_cast<int64_t>(uoff) * c.bytes;
-    }
     dev::MbarExpectTx(bar, c.bytes);
     dev::BulkG2S(dst, c.src, c.bytes, bar);
     c.src += c.bytes;  // block groups of one matrix are contiguous in tile-major order
-    --c.run;
   }
-  ++c.j;
-  NextPhase(p, gt, c, pos0, warp);
+  if (++c.j >= c.n) NextRun(p, gt, c, pos0, warp);
 }
 
 struct Ring {
@@ -361,7 +405,7 @@ struct Ring {
 // cache row that the running step writes in the same layer.
 __device__ __forceinline__ void RingPump(Ring& r, const LoopParams& p, const GeoTable& gt, int64_t pos0, int warp) {
   while (r.ki - r.kc < static_cast<uint32_t>(r.R) && r.cur.step < p.n_steps &&
-         !(r.cur.kind == kAttn && r.cur.step > r.step)) {
+         !(r.cur.ri == kRunAttn && r.cur.step > r.step)) {
     IssueUnit(p, gt, r.cur, pos0, warp, r.base + static_cast<size_t>(r.is) * kSlot, r.bars + r.is);
     ++r.ki;
     if (++r.is == r.R) r.is = 0;
@@ -395,7 +439,7 @@ __device__ __forceinline__ void RingRelease(Ring& r, const LoopParams& p, const 
     r.cs = 0;
     r.cpar ^= 1u;
   }
-  if ((threadIdx.x & 31) == 0 && (!attn_only || r.cur.kind == kAttn)) {
+  if ((threadIdx.x & 31) == 0 && (!attn_only || r.cur.ri == kRunAttn)) {
     dev::FenceProxyAsync();
     RingPump(r, p, gt, pos0, warp);
   }
@@ -770,15 +814,15 @@ __device__ void MvPhase(const LoopParams& p, const GeoTable& gt, int kind, int l
     }
     double ssq = 0.0;
     for (int b = warp; b < nb; b += kNW) {
-      float v[8];
+      float v[8], w[8];
+      // the norm weights are constant: requested before the wait for x
+      if (norm_w != nullptr) Ld8(norm_w + b * 256 + 8 * lane, true, w);
       if (ll != nullptr) {
         WaitLL8(p, ll + b * 256 + 8 * lane, tag, v);
       } else {
         Ld8(xs + b * 256 + 8 * lane, true, v);
       }
       if (norm_w != nullptr) {
-        float w[8];
-        Ld8(norm_w + b * 256 + 8 * lane, true, w);  // constant: cached loads
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           ssq += static_cast<double>(v[i]) * v[i];
@@ -965,7 +1009,7 @@ template <int G>
 __device__ void AttnPhase(const LoopParams& p, const GeoTable& gt, int layer, int step, int64_t pos0, int64_t pos,
                           uint32_t tick_last, Ring& rg_io, const Smem& sm, PhaseClock& clk, AttnShared<G>& as) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const AttnGeo a = AttnOf(p, pos);
+  const AttnGeo a = AttnOf(p, gt, pos);
   if (a.c1 <= a.c0) return;  // no positions for this block at this step
   Ring rg = rg_io;           // in registers for the chunk loop
   const int h = a.h, S = p.splits, s = static_cast<int>(blockIdx.x) - h * S;
@@ -1214,11 +1258,15 @@ struct PeerCands {
   __device__ __forceinline__ int Count(int s) const {
     return static_cast<int>(static_cast<uint32_t>(WaitPeer(*p, base + static_cast<size_t>(s) * kXCandWords, tag)));
   }
-  __device__ __forceinline__ void Load(int j, float& v, int& i) const {
-    const int s = j / kFastTopK, k = j - s * kFastTopK;
-    const uint64_t* w = base + static_cast<size_t>(s) * kXCandWords + 1 + k;
-    v = ValOf(WaitPeer(*p, w, tag));
-    i = static_cast<int>(static_cast<uint32_t>(WaitPeer(*p, w + kFastTopK, tag)));
+  __device__ __forceinline__ void Load(bool use, int j, float& v, int& i) const {
+    v = INFINITY;
+    i = -1;
+    if (use) {  // only words a rank wrote: the others never get this tag
+      const int s = j / kFastTopK, k = j - s * kFastTopK;
+      const uint64_t* w = base + static_cast<size_t>(s) * kXCandWords + 1 + k;
+      v = ValOf(WaitPeer(*p, w, tag));
+      i = static_cast<int>(static_cast<uint32_t>(WaitPeer(*p, w + kFastTopK, tag)));
+    }
   }
 };
 
@@ -1290,10 +1338,9 @@ __global__ void __launch_bounds__(kNT, 1) DecodeLoopKernel(const LoopParams p) {
   rg.bad = false;
   rg.cur.step = 0;
   rg.cur.layer = 0;
-  rg.cur.kind = kQkv;
+  rg.cur.ri = 0;
   rg.cur.j = 0;
-  rg.cur.n = gt.g[kQkv][warp].u1 - gt.g[kQkv][warp].u0;
-  rg.cur.run = 0;
+  rg.cur.n = 0;
   rg.cur.bytes = 0;
   rg.cur.src = nullptr;
   rg.cur.c0 = 0;
@@ -1301,7 +1348,8 @@ __global__ void __launch_bounds__(kNT, 1) DecodeLoopKernel(const LoopParams p) {
   if (lane == 0) {
     for (int i = 0; i < rg.R; ++i) dev::MbarInit(rg.bars + i, 1);
     dev::MbarInitFence();
-    NextPhase(p, gt, rg.cur, pos0, warp);
+    EnterRun(p, gt, rg.cur, pos0, warp);
+    NextRun(p, gt, rg.cur, pos0, warp);
     RingPump(rg, p, gt, pos0, warp);
   }
   __syncwarp();

@@ -407,7 +407,7 @@ __device__ int GeneralSample(const float* logits, int n, float temperature, int 
 }
 
 // The fast path's second half: the whole pipeline on the candidates of
-// n_slices slices (slice s: src.Count(s) candidates at src.Load(64 s + i)).
+// n_slices slices (slice s: src.Count(s) candidates, loaded by src.Load).
 // SmallSurvivors keeps the candidates at or above the k-th largest
 // temperature-scaled value, ordered by vocabulary index, in scratch (values
 // at cv, ids at ci) and returns their count -- or -1 when a slice
@@ -426,13 +426,14 @@ struct GlobalCands {
   const int32_t* idx;
   const int32_t* cnt;
   __device__ __forceinline__ int Count(int s) const { return __ldcg(cnt + s); }
-  __device__ __forceinline__ void Load(int j, float& v, int& i) const {
-    v = __ldcg(val + j);
-    i = __ldcg(idx + j);
+  // candidate j when `use` (else v = +inf, i = -1)
+  __device__ __forceinline__ void Load(bool use, int j, float& v, int& i) const {
+    v = use ? __ldcg(val + j) : INFINITY;
+    i = use ? __ldcg(idx + j) : -1;
   }
 };
 template <int NT, class Src, class Mark = NoMark>
-__device__ int SmallSurvivors(const Src& src, int n_slices, float temperature, int top_k, unsigned char* scratch,
+__device__ int SmallSurvivors(const Src src, int n_slices, float temperature, int top_k, unsigned char* scratch,
                               int cap, Mark mark = Mark()) {
   float* cv = reinterpret_cast<float*>(scratch);  // [cap]
   int* ci = reinterpret_cast<int*>(cv + cap);     // [cap]
@@ -466,11 +467,7 @@ __device__ int SmallSurvivors(const Src& src, int n_slices, float temperature, i
   for (int r = 0; r < kRounds; ++r) {
     const int j = tid + r * NT;
     const int b = j / kFastTopK, i = j - b * kFastTopK;
-    float v = INFINITY;
-    int ix = -1;
-    if (j < total && i < s_cnt[b]) src.Load(j, v, ix);
-    rv[r] = v;
-    ri[r] = ix;
+    src.Load(j < total && i < s_cnt[b], j, rv[r], ri[r]);
   }
 #pragma unroll
   for (int r = 0; r < kRounds; ++r) {
@@ -534,7 +531,7 @@ __device__ int SmallSurvivors(const Src& src, int n_slices, float temperature, i
 }
 
 template <int NT, class Mark = NoMark>
-__device__ __noinline__ int SmallDraw(int c, float top_p, uint64_t seed, int64_t counter, unsigned char* scratch, int cap,
+__device__ __forceinline__ int SmallDraw(int c, float top_p, uint64_t seed, int64_t counter, unsigned char* scratch, int cap,
                          Mark mark = Mark()) {
   float* cv = reinterpret_cast<float*>(scratch);  // [cap]
   int* ci = reinterpret_cast<int*>(cv + cap);     // [cap]
