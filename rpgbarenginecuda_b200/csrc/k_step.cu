@@ -814,15 +814,15 @@ __device__ void MvPhase(const LoopParams& p, const GeoTable& gt, int kind, int l
     }
     double ssq = 0.0;
     for (int b = warp; b < nb; b += kNW) {
-      float v[8], w[8];
-      // the norm weights are constant: requested before the wait for x
-      if (norm_w != nullptr) Ld8(norm_w + b * 256 + 8 * lane, true, w);
+      float v[8];
       if (ll != nullptr) {
         WaitLL8(p, ll + b * 256 + 8 * lane, tag, v);
       } else {
         Ld8(xs + b * 256 + 8 * lane, true, v);
       }
       if (norm_w != nullptr) {
+        float w[8];
+        Ld8(norm_w + b * 256 + 8 * lane, true, w);  // constant: cached loads
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           ssq += static_cast<double>(v[i]) * v[i];

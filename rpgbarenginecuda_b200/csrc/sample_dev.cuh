@@ -446,7 +446,7 @@ __device__ int SmallSurvivors(const Src src, int n_slices, float temperature, in
   // slice counts; an overflowed slice sends this draw to the general kernel
   __shared__ int s_cnt[kCandBlocks];
   __shared__ float s_hmin[(kCandBlocks * kFastTopK + 31) / 32];
-  __shared__ float s_t0;
+  __shared__ float s_t0, s_t1;
   if (tid < n_slices) s_cnt[tid] = src.Count(tid);
   if (tid == 0) {
     s_bad = 0;
@@ -456,9 +456,15 @@ __device__ int SmallSurvivors(const Src src, int n_slices, float temperature, in
   if (tid < n_slices && s_cnt[tid] < 0) s_bad = 1;
   __syncthreads();
   if (s_bad) return -1;
-  // Every slice with at least k candidates holds k values >= its smallest
-  // candidate, so the largest such minimum bounds the k-th largest logit from
-  // below: candidates under it cannot survive top_k and are dropped here.
+  // Two lower bounds of the k-th largest logit; candidates under the larger
+  // cannot survive top_k and are dropped here.  (1) Every slice with at least
+  // k candidates holds k values >= its smallest candidate: the largest such
+  // minimum.  (2) The k slices with the largest maxima hold k distinct values
+  // >= the k-th largest slice maximum.  With the top values spread over many
+  // slices (2) is far tighter: a few dozen candidates stay above it instead of
+  // thousands.  Every value at or above the k-th largest is a candidate of
+  // its slice (a slice's candidates are all its values above a bound that is
+  // at most its own k-th largest), so nothing the filter keeps is lost.
   constexpr int kRounds = (kCandBlocks * kFastTopK + NT - 1) / NT;
   const int total = n_slices * kFastTopK;
   float rv[kRounds];
@@ -469,15 +475,25 @@ __device__ int SmallSurvivors(const Src src, int n_slices, float temperature, in
     const int b = j / kFastTopK, i = j - b * kFastTopK;
     src.Load(j < total && i < s_cnt[b], j, rv[r], ri[r]);
   }
+  float* hmax = kv;        // half-slice maxima (kv is free until the survivors)
+  float* smax = kv + 320;  // slice maxima, -inf for an empty slice
 #pragma unroll
   for (int r = 0; r < kRounds; ++r) {
     const int j = tid + r * NT;
-    float mn = rv[r];
+    float mn = rv[r], mx = ri[r] >= 0 ? rv[r] : -INFINITY;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mn = fminf(mn, __shfl_xor_sync(0xFFFFFFFFu, mn, o));
-    if ((tid & 31) == 0 && j < total) s_hmin[j >> 5] = mn;  // one half slice per warp
+    for (int o = 16; o > 0; o >>= 1) {
+      mn = fminf(mn, __shfl_xor_sync(0xFFFFFFFFu, mn, o));
+      mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+    }
+    if ((tid & 31) == 0 && j < total) {  // one half slice per warp
+      s_hmin[j >> 5] = mn;
+      hmax[j >> 5] = mx;
+    }
   }
+  if (tid == 0) s_t1 = -INFINITY;
   __syncthreads();
+  if (tid < n_slices) smax[tid] = fmaxf(hmax[2 * tid], hmax[2 * tid + 1]);
   if (tid < 32) {
     float t0 = -INFINITY;
     for (int b = tid; b < n_slices; b += 32) {
@@ -487,7 +503,17 @@ __device__ int SmallSurvivors(const Src src, int n_slices, float temperature, in
     if (tid == 0) s_t0 = t0;
   }
   __syncthreads();
-  const float t0 = s_t0;
+  if (tid < n_slices && n_slices >= top_k) {  // the k-th largest slice maximum, by counting
+    const float me = smax[tid];
+    int gt = 0, ge = 0;
+    for (int c = 0; c < n_slices; ++c) {
+      gt += smax[c] > me;
+      ge += smax[c] >= me;
+    }
+    if (gt < top_k && top_k <= ge && me > -INFINITY) s_t1 = me;
+  }
+  __syncthreads();
+  const float t0 = fmaxf(s_t0, s_t1);
   const float inv_t = 1.0f / temperature;
 #pragma unroll
   for (int r = 0; r < kRounds; ++r) {

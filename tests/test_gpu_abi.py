@@ -39,11 +39,20 @@ def lib():
     return L
 
 
-def take_json(L, ptr):
+def take_json(L, ptr, exact=None):
+    """The reply as JSON; exact (a list) receives whether its bytes were valid
+    UTF-8, i.e. whether its text round-trips to the same tokens."""
     assert ptr, L.rpg_engine_last_error().decode()
     try:
+        raw = ctypes.string_at(ptr)
+        if exact is not None:
+            try:
+                raw.decode("utf-8")
+                exact.append(True)
+            except UnicodeDecodeError:
+                exact.append(False)
         # replies of a random-weight model may hold bytes that are not UTF-8
-        return json.loads(ctypes.string_at(ptr).decode(errors="replace"))
+        return json.loads(raw.decode(errors="replace"))
     finally:
         L.rpg_engine_free(ptr)
 
@@ -60,15 +69,29 @@ def test_chat_round_trip(lib, tiny_model):
     req = {"messages": [{"role": "system", "content": "You are a shopkeeper."},
                         {"role": "user", "content": "What do you sell?"}],
            "max_tokens": 8, "temperature": 0.0}
-    r1 = take_json(L, L.rpg_engine_generate(s, json.dumps(req).encode()))
+    exact = []
+    r1 = take_json(L, L.rpg_engine_generate(s, json.dumps(req).encode()), exact)
     assert isinstance(r1["text"], str)
     assert r1["finish_reason"] in ("stop", "length")
     assert 1 <= r1["usage"]["completion_tokens"] <= 8 and r1["usage"]["prompt_tokens"] > 0
-    # a second turn reuses the cached prompt prefix
-    req2 = dict(req, messages=req["messages"] + [{"role": "assistant", "content": r1["text"]},
+    # A second turn reuses the cached prompt prefix (src/engine.cc:468-500):
+    # the session keeps the KV rows of the longest common prefix and prefills
+    # only the rest.  The reply must equal a fresh session's reply to the same
+    # messages.  The assistant message is the first reply's text when its bytes
+    # round-trip (then the whole first turn, generated tokens included, is
+    # reused), else a fixed text (then the cache is cut back to the rendered
+    # first prompt and reused up to there).
+    assistant = r1["text"] if exact[0] else "We sell potions and maps."
+    req2 = dict(req, messages=req["messages"] + [{"role": "assistant", "content": assistant},
                                                   {"role": "user", "content": "And the price?"}])
     r2 = take_json(L, L.rpg_engine_generate(s, json.dumps(req2).encode()))
     assert r2["usage"]["prompt_tokens"] > r1["usage"]["prompt_tokens"]
+    fresh = L.rpg_engine_session_create(m, json.dumps({"max_seq": 512, "max_tokens": 8, "temperature": 0.0,
+                                                       "seed": 1}).encode())
+    assert fresh >= 0, L.rpg_engine_last_error().decode()
+    r2f = take_json(L, L.rpg_engine_generate(fresh, json.dumps(req2).encode()))
+    assert r2["text"] == r2f["text"] and r2["usage"] == r2f["usage"], (r2, r2f)
+    L.rpg_engine_session_destroy(fresh)
     # greedy replies are deterministic: after a reset the first turn repeats
     assert L.rpg_engine_session_reset(s) == 0
     r3 = take_json(L, L.rpg_engine_generate(s, json.dumps(req).encode()))
