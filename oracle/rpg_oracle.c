@@ -124,13 +124,48 @@ static void deq_q6k(const uint8_t* src, int64_t n, float* out) { /* quant.cc:321
   }
 }
 
+static void deq_q5k(const uint8_t* src, int64_t n, float* y) { /* quant.cc:281-313 */
+  /* 176-byte block: d, dmin (fp16), 12 bytes of packed 6-bit scales/mins,
+     32 bytes of fifth bits, 128 bytes of low nibbles; a 64-column group j
+     takes nibble halves of qs[32 j ..) and bits 2j, 2j+1 of qh */
+  for (int64_t b = 0; b < n / 256; ++b) {
+    const uint8_t* p = src + b * 176;
+    const float d = half_at(p), dmin = half_at(p + 2);
+    const uint8_t* qh = p + 16;
+    for (int j = 0; j < 4; ++j) {
+      const uint8_t* ql = p + 48 + 32 * j;
+      for (int half = 0; half < 2; ++half) {
+        uint8_t s, m;
+        get_scale_min_k4(2 * j + half, p + 4, &s, &m);
+        const float dl = d * (float)s, ml = dmin * (float)m;
+        const int bit = 2 * j + half;
+        for (int l = 0; l < 32; ++l) {
+          const int q = (half ? ql[l] >> 4 : ql[l] & 0x0F) + (((qh[l] >> bit) & 1) ? 16 : 0);
+          *y++ = dl * (float)q - ml;
+        }
+      }
+    }
+  }
+}
+
+static void deq_q8_0(const uint8_t* src, int64_t n, float* y) { /* quant.cc:132-141 */
+  /* 34-byte block of 32: fp16 scale, then 32 signed bytes */
+  for (int64_t b = 0; b < n / 32; ++b) {
+    const uint8_t* p = src + b * 34;
+    const float d = half_at(p);
+    for (int l = 0; l < 32; ++l) *y++ = (float)(int8_t)p[2 + l] * d;
+  }
+}
+
 int orc_dequant_row(uint32_t type, const uint8_t* src, int64_t n, float* dst) {
   switch (type) {
     case 0: memcpy(dst, src, (size_t)n * 4); return 0;
     case 1:
       for (int64_t i = 0; i < n; ++i) dst[i] = half_at(src + 2 * i);
       return 0;
+    case 8: if (n % 32) return -1; deq_q8_0(src, n, dst); return 0;
     case 12: if (n % 256) return -1; deq_q4k(src, n, dst); return 0;
+    case 13: if (n % 256) return -1; deq_q5k(src, n, dst); return 0;
     case 14: if (n % 256) return -1; deq_q6k(src, n, dst); return 0;
     default: return -1;
   }
@@ -140,7 +175,9 @@ static int64_t row_bytes(uint32_t type, int64_t cols) {
   switch (type) {
     case 0: return cols * 4;
     case 1: return cols * 2;
+    case 8: return cols / 32 * 34;
     case 12: return cols / 256 * 144;
+    case 13: return cols / 256 * 176;
     case 14: return cols / 256 * 210;
     default: return -1;
   }

@@ -18,9 +18,11 @@ import numpy as np
 from ._lib import EngineError, SampleOptions, check, load_engine  # noqa: F401
 
 __all__ = ["Model", "Session", "Matrix", "SampleOptions", "EngineError", "TpGroup", "shard_plan", "sample",
-           "counter_uniform", "launch_count", "library_path", "GGML_Q4_K", "GGML_Q6_K"]
+           "counter_uniform", "launch_count", "library_path", "GGML_Q4_K", "GGML_Q5_K", "GGML_Q6_K", "GGML_Q8_0"]
 
+GGML_Q8_0 = 8
 GGML_Q4_K = 12
+GGML_Q5_K = 13
 GGML_Q6_K = 14
 
 

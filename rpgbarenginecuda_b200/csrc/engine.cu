@@ -778,6 +778,10 @@ LoopParams Session::MakeLoopParams(const SampleOpts& opt, uint64_t seed) const {
   if (const char* e = std::getenv("RPGB_TEST_DROP_WORD")) lp.test_drop_word = std::atoi(e);
   lp.layers = m_->layers_dev();
   lp.n_layers = c.n_layers;
+  lp.slot = std::max(2048, GroupBytes(m_->lm_head().type));  // 2048: a K + V attention chunk
+  for (const DevLayer& L : m_->layers()) {
+    for (const DevMat* w : {&L.q, &L.k, &L.v, &L.o, &L.gateup, &L.down}) lp.slot = std::max(lp.slot, GroupBytes(w->type));
+  }
   lp.embd = m_->embd();
   lp.lm_head = m_->lm_head();
   lp.out_norm = m_->out_norm();

@@ -92,8 +92,14 @@ int64_t GgmlRowBytes(uint32_t type, int64_t n) {
     case kGgmlQ6_K:
       RPGB_CHECK(n % 256 == 0, "Q6_K row of %lld elements is not a multiple of 256", static_cast<long long>(n));
       return n / 256 * 210;
+    case kGgmlQ5_K:
+      RPGB_CHECK(n % 256 == 0, "Q5_K row of %lld elements is not a multiple of 256", static_cast<long long>(n));
+      return n / 256 * 176;
+    case kGgmlQ8_0:
+      RPGB_CHECK(n % 32 == 0, "Q8_0 row of %lld elements is not a multiple of 32", static_cast<long long>(n));
+      return n / 32 * 34;
     default:
-      Throw("ggml type %u (%s) is not supported by this engine (F32, F16, Q4_K and Q6_K are)", type,
+      Throw("ggml type %u (%s) is not supported by this engine (F32, F16, Q4_K, Q5_K, Q6_K and Q8_0 are)", type,
             GgmlTypeName(type));
   }
 }
@@ -206,7 +212,7 @@ void GgufFile::Open(const std::string& path) {
   for (size_t i = 0; i < tensors_.size(); ++i) {
     GgufTensor& t = tensors_[i];
     t.offset += data_start;
-    if (t.type == kGgmlF32 || t.type == kGgmlF16 || t.type == kGgmlQ4_K || t.type == kGgmlQ6_K) {
+    if (t.type == kGgmlF32 || t.type == kGgmlF16 || MatrixTypeSupported(t.type)) {
       t.n_bytes = GgmlRowBytes(t.type, t.cols()) * (t.n_elements / t.cols());
       RPGB_CHECK(t.offset + t.n_bytes <= size_, "tensor %s runs past the end of the file", t.name.c_str());
     } else {

@@ -17,9 +17,17 @@ namespace rpgb {
 enum GgmlType : uint32_t {
   kGgmlF32 = 0,
   kGgmlF16 = 1,
+  kGgmlQ8_0 = 8,
   kGgmlQ4_K = 12,
+  kGgmlQ5_K = 13,
   kGgmlQ6_K = 14,
 };
+
+// The quantised matrix types the kernels run: Q4_K and Q6_K (the reference's
+// GPU set, src/gpu_model.cu:26-38) plus Q5_K and Q8_0.
+inline bool MatrixTypeSupported(uint32_t t) {
+  return t == kGgmlQ4_K || t == kGgmlQ6_K || t == kGgmlQ5_K || t == kGgmlQ8_0;
+}
 
 // Bytes per 256-element super-block (or per element for F32/F16).
 int64_t GgmlRowBytes(uint32_t type, int64_t n_elems);

@@ -39,7 +39,10 @@ __global__ void __launch_bounds__(256) GemmKernel(const GemmParams p) {
     const int b = kb >> 3;
     const uint8_t* grp = dev::GroupPtr(w, row, b);
     const int r16 = static_cast<int>(row & 15), g = r16 & 7, rs = r16 >> 3;
-    if (w.type == 12u) {
+    if (w.type == 13u || w.type == 8u) {  // one byte per weight: element by element
+#pragma unroll
+      for (int i = 0; i < 8; ++i) wv[i] = dev::DeqElem(w, row, kb * BK + lk + i);
+    } else if (w.type == 12u) {
       const int j = kb & 7;
       const uint4 hd = *reinterpret_cast<const uint4*>(grp + 2048 + 16 * r16);
       int sc, m;

@@ -249,11 +249,7 @@ __global__ void __launch_bounds__(32 * NW, NW == 8 ? 2 : 1) MatvecKernel(const M
       const uint8_t* grp = ring + static_cast<size_t>(slot) * p.slot_bytes;
       LoadB(bfrag, b, lane, lo_half, bA, bB);
       const float s = sscale[b];
-      if (type == 12u) {
-        UnitQ4K(grp, bA, bB, sx + b * 8, s, lk, lane, rg, rg8);
-      } else {
-        UnitQ6K(grp, bA, bB, s, lk, lane, rg, rg8);
-      }
+      UnitOf(type, grp, bA, bB, sx + b * 8, s, lk, lane, rg, rg8);
       __syncwarp();
       if (lane == 0 && issued < n_units) {
         dev::FenceProxyAsync();
@@ -472,7 +468,7 @@ void LaunchMatvec(const MvParams& in, Epi epi, int /*rows_per_warp*/, int num_sm
     RPGB_CHECK(w.cols == K, "matvec: segments differ in width");
     RPGB_CHECK(p.seg[i].out_off == rows, "matvec: segments must be contiguous");
     RPGB_CHECK(w.rows % kTile == 0, "matvec: rows %d not a multiple of %d", w.rows, kTile);
-    RPGB_CHECK(w.type == kGgmlQ4_K || w.type == kGgmlQ6_K, "matvec: unsupported type");
+    RPGB_CHECK(MatrixTypeSupported(w.type), "matvec: unsupported type");
     slot = std::max(slot, GroupBytes(w.type));
     rows += w.rows;
   }

@@ -131,12 +131,8 @@ __global__ void __launch_bounds__(32 * NW, 1) MatvecTokensKernel(const MvnParams
             for (int q = 0; q < 8; ++q) bA[q] = bB[q] = 0u;
             LoadB(smem + L.bfrag + static_cast<size_t>(t) * nb * 1024, b, lane, lo_half, bA, bB);
             const float s = reinterpret_cast<const float*>(smem + L.sscale)[t * nb + b];
-            if (p.w.type == 12u) {
-              UnitQ4K(grp, bA, bB, reinterpret_cast<const float*>(smem + L.sx) + (t * nb + b) * 8, s, lk, lane, rg[t],
-                      rg8[t]);
-            } else {
-              UnitQ6K(grp, bA, bB, s, lk, lane, rg[t], rg8[t]);
-            }
+            UnitOf(p.w.type, grp, bA, bB, reinterpret_cast<const float*>(smem + L.sx) + (t * nb + b) * 8, s, lk,
+                   lane, rg[t], rg8[t]);
           }
         }
         __syncwarp();
@@ -215,7 +211,7 @@ void PrepareMatvecTokensKernels() {
 void LaunchMatvecTokens(const MvnParams& in, int num_sms, cudaStream_t s, bool pdl) {
   MvnParams p = in;
   const DevMat& w = p.w;
-  RPGB_CHECK(w.type == kGgmlQ4_K || w.type == kGgmlQ6_K, "matvec: unsupported type");
+  RPGB_CHECK(MatrixTypeSupported(w.type), "matvec: unsupported type");
   RPGB_CHECK(w.cols % 256 == 0 && w.cols > 0 && w.cols <= 16384, "matvec: width %d must be a multiple of 256",
              w.cols);
   RPGB_CHECK(w.rows % kTile == 0, "matvec: rows %d not a multiple of %d", w.rows, kTile);

@@ -49,7 +49,6 @@ using namespace mv;
 
 constexpr int kNW = 16;        // warps per block
 constexpr int kNT = 32 * kNW;  // threads per block
-constexpr int kSlot = 3360;    // ring slot: one Q6_K block group (Q4_K 2304 B, a K or V chunk 3072 B)
 constexpr int kChunk = 4;      // attention positions per unit (their K rows, then their V rows at +1024 B)
 constexpr int kD = 128;        // head dimension
 constexpr int kMaxRing = 8;
@@ -76,9 +75,12 @@ struct Plan {
 
 __host__ __device__ inline size_t Al(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-__host__ __device__ inline Plan MakePlan(int ring, int nb_max, int x_max, int scratch_bytes, int max_tiles) {
+// Ring slots are `slot` bytes: the largest block group of the model (Q6_K
+// 3360 B for the Q4_K_M mix, 4352 B with Q5_K or Q8_0 matrices; a K + V
+// attention chunk is 2048 B).
+__host__ __device__ inline Plan MakePlan(int ring, int slot, int nb_max, int x_max, int scratch_bytes, int max_tiles) {
   Plan l;
-  l.bars = static_cast<size_t>(kNW) * ring * kSlot;
+  l.bars = static_cast<size_t>(kNW) * ring * slot;
   l.scratch = Al(l.bars + static_cast<size_t>(kNW) * ring * 8, 128);
   l.bfrag = 0;
   l.sx = l.bfrag + static_cast<size_t>(nb_max) * 1024;
@@ -205,7 +207,7 @@ __shared__ Run g_runs[kNW][kRuns];
 struct LayerRow {
   const uint8_t* w[6];
   const float* norm[4];  // attn, ffn, q, k
-  uint32_t q6;           // bit i: matrix i is Q6_K (else Q4_K)
+  uint8_t type[6];       // ggml type of matrix i
 };
 
 // Matrix `seg` of a phase in layer `layer`: its block groups and type.
@@ -254,10 +256,9 @@ __device__ __forceinline__ void FillTables(const LoopParams& p) {
     const DevLayer& L = p.layers[l];
     const DevMat* m[6] = {&L.q, &L.k, &L.v, &L.o, &L.gateup, &L.down};
     LayerRow r;
-    r.q6 = 0;
     for (int i = 0; i < 6; ++i) {
       r.w[i] = m[i]->q;
-      if (m[i]->type != 12u) r.q6 |= 1u << i;
+      r.type[i] = static_cast<uint8_t>(m[i]->type);
     }
     r.norm[0] = L.attn_norm;
     r.norm[1] = L.ffn_norm;
@@ -269,7 +270,7 @@ __device__ __forceinline__ void FillTables(const LoopParams& p) {
 
 __device__ __forceinline__ uint32_t SegType(const LoopParams& p, int kind, int layer, int seg) {
   if (kind == kLm) return p.lm_head.type;
-  return (g_layers[layer].q6 >> MatIdx(kind, seg)) & 1u ? 14u : 12u;
+  return g_layers[layer].type[MatIdx(kind, seg)];
 }
 
 // Splits of a KV head that hold positions at this step: sixteen chunks (one
@@ -334,7 +335,7 @@ __device__ __forceinline__ void EnterRun(const LoopParams& p, const GeoTable& gt
   c.n = r.n;
   if (r.n > 0) {
     const bool lm = c.ri == kRunLm;
-    const uint32_t type = lm ? p.lm_head.type : ((g_layers[c.layer].q6 >> r.mat) & 1u ? 14u : 12u);
+    const uint32_t type = lm ? p.lm_head.type : g_layers[c.layer].type[r.mat];
     c.bytes = static_cast<uint32_t>(dev::GroupBytesOf(type));
     c.src = (lm ? p.lm_head.q : g_layers[c.layer].w[r.mat]) + static_cast<int64_t>(r.off) * c.bytes;
   }
@@ -406,7 +407,7 @@ struct Ring {
 __device__ __forceinline__ void RingPump(Ring& r, const LoopParams& p, const GeoTable& gt, int64_t pos0, int warp) {
   while (r.ki - r.kc < static_cast<uint32_t>(r.R) && r.cur.step < p.n_steps &&
          !(r.cur.ri == kRunAttn && r.cur.step > r.step)) {
-    IssueUnit(p, gt, r.cur, pos0, warp, r.base + static_cast<size_t>(r.is) * kSlot, r.bars + r.is);
+    IssueUnit(p, gt, r.cur, pos0, warp, r.base + static_cast<size_t>(r.is) * p.slot, r.bars + r.is);
     ++r.ki;
     if (++r.is == r.R) r.is = 0;
   }
@@ -424,7 +425,7 @@ __device__ __forceinline__ const uint8_t* RingWait(Ring& r, const LoopParams& p)
       if ((threadIdx.x & 31) == 0) atomicOr(p.err, 1u);
     }
   }
-  return r.base + static_cast<size_t>(slot) * kSlot;
+  return r.base + static_cast<size_t>(slot) * p.slot;
 }
 
 // Marks the current unit consumed and refills free slots from the stream.
@@ -681,7 +682,7 @@ struct Smem {
   uint8_t* base;
   const LoopParams* p;
   __device__ __forceinline__ Plan plan() const {
-    return MakePlan(p->ring, p->nb_max, p->x_max, p->scratch_bytes, p->max_tiles);
+    return MakePlan(p->ring, p->slot, p->nb_max, p->x_max, p->scratch_bytes, p->max_tiles);
   }
   __device__ __forceinline__ uint8_t* scratch() const { return base + plan().scratch; }
 };
@@ -863,11 +864,7 @@ __device__ void MvPhase(const LoopParams& p, const GeoTable& gt, int kind, int l
       const uint8_t* grp = RingWait(rg, p);
       LoadB(bfrag, b, lane, lo_half, bA, bB);
       const float s = sscale[b];
-      if (type == 12u) {
-        UnitQ4K(grp, bA, bB, sx + b * 8, s, lk, lane, rgv, rg8);
-      } else {
-        UnitQ6K(grp, bA, bB, s, lk, lane, rgv, rg8);
-      }
+      UnitOf(type, grp, bA, bB, sx + b * 8, s, lk, lane, rgv, rg8);
       RingRelease(rg, p, gt, pos0, warp);
       if (++b == nb || i + 1 == n_units) {
         FlushPiece(red, tl + warp, lk, rgv, rg8);
@@ -1330,7 +1327,7 @@ __global__ void __launch_bounds__(kNT, 1) DecodeLoopKernel(const LoopParams p) {
 
   Ring rg;
   rg.R = p.ring;
-  rg.base = smem + static_cast<size_t>(warp) * p.ring * kSlot;
+  rg.base = smem + static_cast<size_t>(warp) * p.ring * p.slot;
   rg.bars = reinterpret_cast<uint64_t*>(smem + sm.plan().bars) + warp * p.ring;
   rg.kc = rg.ki = 0;
   rg.cs = rg.is = 0;
@@ -1584,13 +1581,14 @@ void LaunchDecodeLoop(const LoopParams& in, int group, int num_sms, cudaStream_t
   p.scratch_bytes = static_cast<int32_t>(ScratchBytes(p.nb_max, p.x_max, group, p.n_kv, p.splits));
   cudaFuncAttributes fa;
   RPGB_CUDA(cudaFuncGetAttributes(&fa, reinterpret_cast<const void*>(fn)));
-  const size_t fixed = MakePlan(0, p.nb_max, p.x_max, p.scratch_bytes, p.max_tiles).total;
+  RPGB_CHECK(p.slot >= 2048 && p.slot % 16 == 0 && p.slot <= 8192, "decode loop: slot of %d bytes", p.slot);
+  const size_t fixed = MakePlan(0, p.slot, p.nb_max, p.x_max, p.scratch_bytes, p.max_tiles).total;
   const size_t avail = static_cast<size_t>(kSmemMax) - fa.sharedSizeBytes;
   RPGB_CHECK(avail > fixed, "decode loop: shared memory plan does not fit");
-  const int ring = static_cast<int>((avail - fixed) / (static_cast<size_t>(kNW) * (kSlot + 8)));
+  const int ring = static_cast<int>((avail - fixed) / (static_cast<size_t>(kNW) * (p.slot + 8)));
   RPGB_CHECK(ring >= 2, "decode loop: room for only %d ring slots per warp", ring);
   p.ring = std::min(ring, kMaxRing);
-  const size_t total = MakePlan(p.ring, p.nb_max, p.x_max, p.scratch_bytes, p.max_tiles).total;
+  const size_t total = MakePlan(p.ring, p.slot, p.nb_max, p.x_max, p.scratch_bytes, p.max_tiles).total;
   if (p.mode == 1) {
     // the candidate slices are the blocks' lm_head rows
     RPGB_CHECK(num_sms <= kCandBlocks && p.max_tiles * kTile <= kSliceRows, "decode loop: fast sampler geometry");

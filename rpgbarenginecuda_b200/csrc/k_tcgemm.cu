@@ -75,7 +75,10 @@ __global__ void __launch_bounds__(256) DequantSplitKernel(const DevMat w, __half
     const uint8_t* grp = dev::GroupPtr(w, row, b);
     const int r16 = static_cast<int>(row & 15), g = r16 & 7, rs = r16 >> 3;
     float v[8];
-    if (w.type == 12u) {
+    if (w.type == 13u || w.type == 8u) {  // one byte per weight: element by element
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = dev::DeqElem(w, row, col + i);
+    } else if (w.type == 12u) {
       const uint4 hd = *reinterpret_cast<const uint4*>(grp + 2048 + 16 * r16);
       int sc, m;
       dev::Q4kScaleMin(hd.y, hd.z, hd.w, kb, &sc, &m);

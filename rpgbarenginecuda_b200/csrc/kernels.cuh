@@ -58,7 +58,9 @@ __device__ __forceinline__ int Q6kScale(const uint4& s, int i) {
 // L = 4g + t of a warp owns tile rows g and g + 8 in the integer MMA
 // fragments; the accessors below address single elements for the bit-exact
 // dequant paths.
-__host__ __device__ __forceinline__ int GroupBytesOf(uint32_t type) { return type == 12u ? 2304 : 3360; }
+__host__ __device__ __forceinline__ int GroupBytesOf(uint32_t type) {
+  return type == 12u ? 2304 : (type == 14u ? 3360 : kByteGroupBytes);
+}
 
 __device__ __forceinline__ const uint8_t* GroupPtr(const DevMat& w, int64_t row, int b) {
   return w.q + ((row >> 4) * w.nb + b) * GroupBytesOf(w.type);
@@ -83,6 +85,13 @@ __device__ __forceinline__ int Q6kValue(const uint8_t* grp, int r, int e) {
   if (hb == 0) return (rs == 0 ? w[ee] : w[4 + ee]) & 63;
   if (rs == 0) return w[8 + ee] & 63;
   return (w[ee] >> 6) | ((w[4 + ee] >> 6) << 2) | ((w[8 + ee] >> 6) << 4);
+}
+
+// Byte of element e (0..255) of tile row r (0..15) in a Q5_K / Q8_0 group.
+__device__ __forceinline__ uint8_t ByteGroupValue(const uint8_t* grp, int r, int e) {
+  const int c = e >> 6, half = (e >> 5) & 1, h = (e >> 4) & 1, t = (e >> 2) & 3, ee = e & 3;
+  const int g = r & 7, rs = r >> 3;
+  return grp[(c * 32 + 4 * g + t) * 32 + 4 * (4 * h + 2 * half + rs) + ee];
 }
 
 // ------------------------------------------------------------------ element dequant (bit-exact)
@@ -111,8 +120,36 @@ __device__ __forceinline__ float DeqQ6K(const DevMat& w, int64_t row, int b, int
   return __fmul_rn(__fmul_rn(d, static_cast<float>(sc)), static_cast<float>(raw));
 }
 
+// Element e (0..255) of Q5_K block b of `row` (src/quant.cc:281-313).
+__device__ __forceinline__ float DeqQ5K(const DevMat& w, int64_t row, int b, int e) {
+  const uint8_t* grp = GroupPtr(w, row, b);
+  const int r = static_cast<int>(row & 15);
+  const uint4 h = *reinterpret_cast<const uint4*>(grp + 4096 + 16 * r);
+  int sc, m;
+  Q4kScaleMin(h.y, h.z, h.w, e >> 5, &sc, &m);
+  const int raw = ByteGroupValue(grp, r, e);
+  const float d = Half(h.x & 0xFFFFu), dmin = Half(h.x >> 16);
+  const float d1 = __fmul_rn(d, static_cast<float>(sc));
+  const float m1 = __fmul_rn(dmin, static_cast<float>(m));
+  return __fsub_rn(__fmul_rn(d1, static_cast<float>(raw)), m1);
+}
+
+// Element e (0..255) of the 256 columns b of a Q8_0 `row` (src/quant.cc:132-141).
+__device__ __forceinline__ float DeqQ8(const DevMat& w, int64_t row, int b, int e) {
+  const uint8_t* grp = GroupPtr(w, row, b);
+  const int r = static_cast<int>(row & 15);
+  const int8_t q = static_cast<int8_t>(ByteGroupValue(grp, r, e));
+  const float d = Half(*reinterpret_cast<const uint16_t*>(grp + 4096 + 16 * r + 2 * (e >> 5)));
+  return __fmul_rn(static_cast<float>(q), d);
+}
+
 __device__ __forceinline__ float DeqElem(const DevMat& w, int64_t row, int col) {
-  return w.type == 12u ? DeqQ4K(w, row, col >> 8, col & 255) : DeqQ6K(w, row, col >> 8, col & 255);
+  switch (w.type) {
+    case 12u: return DeqQ4K(w, row, col >> 8, col & 255);
+    case 13u: return DeqQ5K(w, row, col >> 8, col & 255);
+    case 8u: return DeqQ8(w, row, col >> 8, col & 255);
+    default: return DeqQ6K(w, row, col >> 8, col & 255);
+  }
 }
 
 // ------------------------------------------------------------------ async copy / PDL primitives

@@ -276,6 +276,7 @@ struct LoopParams {
   int32_t test_drop_word = 0;
   // shared-memory plan, filled in by the launcher
   int32_t ring = 0, max_tiles = 0, nb_max = 0, x_max = 0;
+  int32_t slot = 0;  // ring slot bytes: the largest block group of the model's matrices
   int32_t scratch_bytes = 0;
   Trace trace;  // records carry id = step * (5 n_layers + 2) + phase
   double ns_per_cycle = 0.0;  // SM clock period, to turn cycle counts of the trace into nanoseconds

@@ -133,7 +133,8 @@ ModelMeta ReadModelMeta(const GgufFile& g) {
 int GroupBytes(uint32_t type) {
   if (type == kGgmlQ4_K) return 16 * 144;
   if (type == kGgmlQ6_K) return 16 * 210;
-  Throw("matrix type %s is not supported (Q4_K and Q6_K are)", GgmlTypeName(type));
+  if (type == kGgmlQ5_K || type == kGgmlQ8_0) return kByteGroupBytes;
+  Throw("matrix type %s is not supported (Q4_K, Q5_K, Q6_K and Q8_0 are)", GgmlTypeName(type));
 }
 
 size_t DevMatBytes(uint32_t type, int64_t rows, int64_t cols) {
@@ -153,6 +154,16 @@ inline int Q6kRaw(const uint8_t* blk, int e) {
   return nib | (hi << 4);
 }
 
+// 5-bit value (0..31) of element e of a GGUF Q5_K block (src/quant.cc:281-313
+// layout: low nibbles in qs[32 j + l] for the 64-column group j, fifth bits in
+// bit 2 j (first 32 columns) or 2 j + 1 (next 32) of qh[l]).
+inline int Q5kRaw(const uint8_t* blk, int e) {
+  const int j = e >> 6, hi = (e >> 5) & 1, l = e & 31;
+  const uint8_t q = blk[48 + 32 * j + l];
+  const int nib = hi ? (q >> 4) : (q & 15);
+  return nib | (((blk[16 + l] >> (2 * j + hi)) & 1) << 4);
+}
+
 }  // namespace
 
 // Block-group byte order (lane = 4 * g + t, g = 0..7, t = 0..3; rows g and g + 8
@@ -169,11 +180,45 @@ inline int Q6kRaw(const uint8_t* blk, int e) {
 //                       adjacent (48 B), so a lane reads them as 3 x 16 B.
 //         [3072, 3328)  row r: sc[16] (int8)
 //         [3328, 3360)  d (f16) of row g + 8rs at index 2g + rs
+//   Q5_K, Q8_0 (one byte per weight)
+//         [0, 4096)     per pair c (0..3) and lane, 32 B = words (h, half, rs)
+//                       at 4 (4h + 2 half + rs): the values of columns
+//                       64c + 32 half + 16h + 4t .. +3 of row g + 8rs (Q5_K:
+//                       0..31; Q8_0: int8) -- the four A registers of the MMA
+//                       of (c, h) read as one 16-byte load
+//         [4096, 4352)  row r: Q5_K the 16 header bytes (d, dmin, scales[12]);
+//                       Q8_0 the 8 f16 scales of its 32-column blocks
 void RepackTile(uint32_t type, const uint8_t* const* src, int64_t nb, uint8_t* dst) {
   const int gb = GroupBytes(type);
   for (int64_t b = 0; b < nb; ++b) {
     uint8_t* o = dst + b * gb;
-    if (type == kGgmlQ4_K) {
+    if (type == kGgmlQ5_K || type == kGgmlQ8_0) {
+      for (int r = 0; r < 16; ++r) {
+        if (type == kGgmlQ5_K) {
+          std::memcpy(o + 4096 + 16 * r, src[r] + b * 176, 16);
+        } else {
+          for (int k = 0; k < 8; ++k) std::memcpy(o + 4096 + 16 * r + 2 * k, src[r] + (b * 8 + k) * 34, 2);
+        }
+      }
+      for (int c = 0; c < 4; ++c) {
+        for (int lane = 0; lane < 32; ++lane) {
+          const int g = lane >> 2, t = lane & 3;
+          for (int h = 0; h < 2; ++h) {
+            for (int half = 0; half < 2; ++half) {
+              for (int rs = 0; rs < 2; ++rs) {
+                uint8_t* w = o + (c * 32 + lane) * 32 + 4 * (4 * h + 2 * half + rs);
+                for (int e = 0; e < 4; ++e) {
+                  const int col = 64 * c + 32 * half + 16 * h + 4 * t + e;
+                  const uint8_t* row = src[g + 8 * rs];
+                  w[e] = type == kGgmlQ5_K ? static_cast<uint8_t>(Q5kRaw(row + b * 176, col))
+                                           : row[(b * 8 + (col >> 5)) * 34 + 2 + (col & 31)];
+                }
+              }
+            }
+          }
+        }
+      }
+    } else if (type == kGgmlQ4_K) {
       for (int r = 0; r < 16; ++r) std::memcpy(o + 2048 + 16 * r, src[r] + b * 144, 16);
       for (int c = 0; c < 4; ++c) {
         for (int lane = 0; lane < 32; ++lane) {
@@ -278,8 +323,8 @@ std::unique_ptr<Model> Model::Load(const std::string& path, int device, int32_t 
                "tensor %s has shape [%lld,%lld], expected [%lld,%lld]", t.name.c_str(),
                static_cast<long long>(t.rows()), static_cast<long long>(t.cols()), static_cast<long long>(rows),
                static_cast<long long>(cols));
-    RPGB_CHECK(t.type == kGgmlQ4_K || t.type == kGgmlQ6_K,
-               "tensor %s has type %s; the kernels implement Q4_K and Q6_K", t.name.c_str(),
+    RPGB_CHECK(MatrixTypeSupported(t.type),
+               "tensor %s has type %s; the kernels implement Q4_K, Q5_K, Q6_K and Q8_0", t.name.c_str(),
                GgmlTypeName(t.type));
   };
   auto check_norm = [&](const GgufTensor& t, int64_t n) {

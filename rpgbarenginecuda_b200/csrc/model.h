@@ -43,7 +43,7 @@ ModelMeta ReadModelMeta(const GgufFile& g);
 // One quantised matrix in the repacked device layout (passed to kernels by value).
 // Block group (tile t, super-block b) starts at q + (t * nb + b) * GroupBytes(type).
 struct DevMat {
-  uint32_t type = 0;  // kGgmlQ4_K or kGgmlQ6_K
+  uint32_t type = 0;  // kGgmlQ4_K, kGgmlQ5_K, kGgmlQ6_K or kGgmlQ8_0
   int32_t rows = 0, cols = 0, nb = 0;
   const uint8_t* q = nullptr;
 };
@@ -63,6 +63,9 @@ struct DevLayer {
 // nb block groups; RepackRows takes `rows` (a multiple of 16) contiguous GGUF
 // rows.  DevMatBytes = rows / 16 * nb * GroupBytes(type).
 constexpr int kTileRows = 16;
+// Bytes of a Q5_K or Q8_0 block group (one byte per weight plus 256 bytes of
+// per-row scales); Q4_K groups are 2304 bytes, Q6_K 3360.
+constexpr int kByteGroupBytes = 4352;
 int GroupBytes(uint32_t type);
 void RepackTile(uint32_t type, const uint8_t* const* src_rows, int64_t nb, uint8_t* dst);
 void RepackRows(uint32_t type, const uint8_t* src, int64_t rows, int64_t cols, uint8_t* dst);

@@ -166,6 +166,87 @@ __device__ __forceinline__ void UnitQ6K(const uint8_t* grp, const uint32_t (&bA)
   rg8 += dg8 * s * (static_cast<float>(acc[2]) * k.w6g8[0] + static_cast<float>(acc[3]) * k.w6g8[1]);
 }
 
+// One Q5_K (tile, super-block) unit: the Q4_K unit with the 5-bit values
+// stored one per byte (no nibble masks, both halves at weight 1).
+__device__ __forceinline__ void UnitQ5K(const uint8_t* grp, const uint32_t (&bA)[8], const uint32_t (&bB)[8],
+                                        const float* sx, float s, const LaneK& k, int lane, float& rg, float& rg8) {
+  const uint4 R0 = Lds128(grp + 4096 + 16 * k.g);
+  const uint4 R1 = Lds128(grp + 4096 + 16 * (k.g + 8));
+  const uint32_t sclo0 = R0.y & 0x3F3F3F3Fu, sclo1 = R1.y & 0x3F3F3F3Fu;
+  const uint32_t schi0 = (R0.w & 0x0F0F0F0Fu) | ((R0.y >> 2) & 0x30303030u);
+  const uint32_t schi1 = (R1.w & 0x0F0F0F0Fu) | ((R1.y >> 2) & 0x30303030u);
+  int acc[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const uint8_t* base = grp + (c * 32 + lane) * 32;
+    const uint4 W0 = Lds128(base), W1 = Lds128(base + 16);
+    int d[4] = {0, 0, 0, 0};
+    MmaU8(d, W0.x, W0.y, W0.z, W0.w, bA[2 * c], bB[2 * c]);
+    MmaU8(d, W1.x, W1.y, W1.z, W1.w, bA[2 * c + 1], bB[2 * c + 1]);
+    const int s0 = ByteU(c < 2 ? sclo0 : schi0, k.sel_q4[c & 1]);
+    const int s1 = ByteU(c < 2 ? sclo1 : schi1, k.sel_q4[c & 1]);
+    acc[0] += s0 * d[0];
+    acc[1] += s0 * d[1];
+    acc[2] += s1 * d[2];
+    acc[3] += s1 * d[3];
+  }
+  const uint32_t mlo0 = R0.z & 0x3F3F3F3Fu, mlo1 = R1.z & 0x3F3F3F3Fu;
+  const uint32_t mhi0 = ((R0.w >> 4) & 0x0F0F0F0Fu) | ((R0.z >> 2) & 0x30303030u);
+  const uint32_t mhi1 = ((R1.w >> 4) & 0x0F0F0F0Fu) | ((R1.z >> 2) & 0x30303030u);
+  const uint32_t m0 = k.p ? mhi0 : mlo0, m1 = k.p ? mhi1 : mlo1;
+  const float2 sxv = *reinterpret_cast<const float2*>(sx + 2 * k.tig);
+  const float mn0 =
+      static_cast<float>(ByteU(m0, k.sel_m[0])) * sxv.x + static_cast<float>(ByteU(m0, k.sel_m[1])) * sxv.y;
+  const float mn1 =
+      static_cast<float>(ByteU(m1, k.sel_m[0])) * sxv.x + static_cast<float>(ByteU(m1, k.sel_m[1])) * sxv.y;
+  const float d0 = dev::Half(R0.x & 0xFFFFu), dm0 = dev::Half(R0.x >> 16);
+  const float d1 = dev::Half(R1.x & 0xFFFFu), dm1 = dev::Half(R1.x >> 16);
+  const float f0 = s * k.w6g[0], f1 = s * k.w6g[1];
+  rg += d0 * (static_cast<float>(acc[0]) * f0 + static_cast<float>(acc[1]) * f1) - dm0 * mn0;
+  rg8 += d1 * (static_cast<float>(acc[2]) * f0 + static_cast<float>(acc[3]) * f1) - dm1 * mn1;
+}
+
+// One Q8_0 (tile, 256 columns) unit: signed bytes times the signed digits;
+// each 32-column block has its own f16 scale, so the block sums are scaled
+// in FP32 (they are exact integers below 2^24).
+__device__ __forceinline__ void UnitQ8(const uint8_t* grp, const uint32_t (&bA)[8], const uint32_t (&bB)[8], float s,
+                                       const LaneK& k, int lane, float& rg, float& rg8) {
+  const uint4 S0 = Lds128(grp + 4096 + 16 * k.g);
+  const uint4 S1 = Lds128(grp + 4096 + 16 * (k.g + 8));
+  const uint32_t s0w[4] = {S0.x, S0.y, S0.z, S0.w}, s1w[4] = {S1.x, S1.y, S1.z, S1.w};
+  float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const uint8_t* base = grp + (c * 32 + lane) * 32;
+    const uint4 W0 = Lds128(base), W1 = Lds128(base + 16);
+    int d[4] = {0, 0, 0, 0};
+    MmaS8(d, W0.x, W0.y, W0.z, W0.w, bA[2 * c], bB[2 * c]);
+    MmaS8(d, W1.x, W1.y, W1.z, W1.w, bA[2 * c + 1], bB[2 * c + 1]);
+    // this lane's columns are block 2c + p of rows g and g + 8: f16 at word c, half p
+    const float q0 = dev::Half(k.p ? s0w[c] >> 16 : s0w[c] & 0xFFFFu);
+    const float q1 = dev::Half(k.p ? s1w[c] >> 16 : s1w[c] & 0xFFFFu);
+    a0 += q0 * (static_cast<float>(d[0]) * k.w6g[0] + static_cast<float>(d[1]) * k.w6g[1]);
+    a1 += q1 * (static_cast<float>(d[2]) * k.w6g[0] + static_cast<float>(d[3]) * k.w6g[1]);
+  }
+  rg += s * a0;
+  rg8 += s * a1;
+}
+
+// One unit of a matrix of type `type` (ggml codes 12 Q4_K, 13 Q5_K, 14 Q6_K, 8 Q8_0).
+__device__ __forceinline__ void UnitOf(uint32_t type, const uint8_t* grp, const uint32_t (&bA)[8],
+                                       const uint32_t (&bB)[8], const float* sx, float s, const LaneK& k, int lane,
+                                       float& rg, float& rg8) {
+  if (type == 12u) {
+    UnitQ4K(grp, bA, bB, sx, s, k, lane, rg, rg8);
+  } else if (type == 14u) {
+    UnitQ6K(grp, bA, bB, s, k, lane, rg, rg8);
+  } else if (type == 13u) {
+    UnitQ5K(grp, bA, bB, sx, s, k, lane, rg, rg8);
+  } else {
+    UnitQ8(grp, bA, bB, s, k, lane, rg, rg8);
+  }
+}
+
 __device__ __forceinline__ void FlushPiece(float* red, int piece, const LaneK& k, float& rg, float& rg8) {
   rg += __shfl_xor_sync(0xFFFFFFFFu, rg, 1);
   rg += __shfl_xor_sync(0xFFFFFFFFu, rg, 2);

@@ -27,7 +27,9 @@
 namespace {
 
 constexpr uint32_t kTypeF32 = 0;
+constexpr uint32_t kTypeQ8_0 = 8;
 constexpr uint32_t kTypeQ4K = 12;
+constexpr uint32_t kTypeQ5K = 13;
 constexpr uint32_t kTypeQ6K = 14;
 constexpr int kQK = 256;
 
@@ -130,7 +132,7 @@ float F16ToF32(uint16_t h) {
 
 inline int Clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
 
-// ---------------------------------------------------------------- Q4_K encoder
+// ---------------------------------------------------------------- Q4_K / Q5_K encoder
 //
 // Block (144 B): d f16 | dmin f16 | scales[12] | qs[128].
 // Element e of sub-block j (32 wide) decodes as (d*sc_j)*q - (dmin*m_j), q in
@@ -138,7 +140,11 @@ inline int Clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v
 // the 4-bit step (hi-lo)/15 and offset -lo; the super-block stores d and dmin as
 // the largest step / offset over 63, then everything is requantised against the
 // f16-rounded d and dmin so the stored q match the decoder exactly.
-void EncodeQ4KBlock(const float* x, uint8_t* out) {
+// Q5_K (176 B: d | dmin | scales[12] | qh[32] | qs[128]) is the same with
+// 5-bit q in [0, 31]: low nibbles packed as Q4_K's, the fifth bit of column
+// 64 g + l in bit 2 g of qh[l] and of column 64 g + 32 + l in bit 2 g + 1.
+void EncodeQ45KBlock(const float* x, uint8_t* out, bool five) {
+  const int levels = five ? 31 : 15;
   float step[8], off[8];
   for (int j = 0; j < 8; ++j) {
     float lo = 0.0f, hi = 0.0f;
@@ -147,7 +153,7 @@ void EncodeQ4KBlock(const float* x, uint8_t* out) {
       lo = v < lo ? v : lo;
       hi = v > hi ? v : hi;
     }
-    step[j] = (hi - lo) / 15.0f;
+    step[j] = (hi - lo) / static_cast<float>(levels);
     off[j] = -lo;
   }
   float smax = 0.0f, omax = 0.0f;
@@ -184,13 +190,59 @@ void EncodeQ4KBlock(const float* x, uint8_t* out) {
     for (int l = 0; l < 32; ++l) {
       const float v = x[32 * j + l];
       const int qi = ds > 0.0f ? static_cast<int>(std::lround((v + dm) / ds)) : 0;
-      q[32 * j + l] = static_cast<uint8_t>(Clampi(qi, 0, 15));
+      q[32 * j + l] = static_cast<uint8_t>(Clampi(qi, 0, levels));
     }
   }
-  uint8_t* qs = out + 16;
+  uint8_t* qs = out + (five ? 48 : 16);
   for (int g = 0; g < 4; ++g) {
     for (int l = 0; l < 32; ++l) {
-      qs[32 * g + l] = static_cast<uint8_t>(q[64 * g + l] | (q[64 * g + 32 + l] << 4));
+      qs[32 * g + l] = static_cast<uint8_t>((q[64 * g + l] & 15) | ((q[64 * g + 32 + l] & 15) << 4));
+    }
+  }
+  if (five) {
+    uint8_t* qh = out + 16;
+    for (int l = 0; l < 32; ++l) {
+      uint8_t h = 0;
+      for (int g = 0; g < 4; ++g) {
+        h |= static_cast<uint8_t>(((q[64 * g + l] >> 4) & 1) << (2 * g));
+        h |= static_cast<uint8_t>(((q[64 * g + 32 + l] >> 4) & 1) << (2 * g + 1));
+      }
+      qh[l] = h;
+    }
+  }
+}
+void EncodeQ4KBlock(const float* x, uint8_t* out) { EncodeQ45KBlock(x, out, false); }
+void EncodeQ5KBlock(const float* x, uint8_t* out) { EncodeQ45KBlock(x, out, true); }
+
+// ---------------------------------------------------------------- Q8_0 encoder
+//
+// Block of 32 (34 B): d f16 | qs[32] int8, decoding as q * d; d = max|x| / 127
+// rounded to f16, q requantised against the rounded d.
+void EncodeQ80Block(const float* x, uint8_t* out) {
+  float amax = 0.0f;
+  for (int l = 0; l < 32; ++l) amax = std::fabs(x[l]) > amax ? std::fabs(x[l]) : amax;
+  const uint16_t dh = F32ToF16Rne(amax / 127.0f);
+  const float d = F16ToF32(dh);
+  std::memcpy(out, &dh, 2);
+  for (int l = 0; l < 32; ++l) {
+    const int qi = d > 0.0f ? static_cast<int>(std::lround(x[l] / d)) : 0;
+    out[2 + l] = static_cast<uint8_t>(static_cast<int8_t>(Clampi(qi, -127, 127)));
+  }
+}
+
+void EncodeQ6KBlock(const float* x, uint8_t* out);
+
+// Encodes n elements (a multiple of 256) of type `type` into out.
+void EncodeRow(uint32_t type, const float* x, int64_t n, uint8_t* out) {
+  for (int64_t b = 0; b < n / kQK; ++b) {
+    if (type == kTypeQ4K) {
+      EncodeQ4KBlock(x + b * kQK, out + b * 144);
+    } else if (type == kTypeQ5K) {
+      EncodeQ5KBlock(x + b * kQK, out + b * 176);
+    } else if (type == kTypeQ6K) {
+      EncodeQ6KBlock(x + b * kQK, out + b * 210);
+    } else {
+      for (int k = 0; k < 8; ++k) EncodeQ80Block(x + b * kQK + 32 * k, out + (b * 8 + k) * 34);
     }
   }
 }
@@ -277,7 +329,12 @@ struct TensorPlan {
 uint64_t RowBytes(uint32_t type, int64_t cols) {
   if (type == kTypeF32) return static_cast<uint64_t>(cols) * 4;
   const uint64_t nb = static_cast<uint64_t>(cols / kQK);
-  return nb * (type == kTypeQ4K ? 144u : 210u);
+  switch (type) {
+    case kTypeQ4K: return nb * 144u;
+    case kTypeQ5K: return nb * 176u;
+    case kTypeQ6K: return nb * 210u;
+    default: return nb * 8u * 34u;  // Q8_0
+  }
 }
 
 // GPT-2 byte-level alphabet: byte -> code point.
@@ -409,11 +466,25 @@ struct rpgs_config {
   // defaults 0.02 and 0.05)
   float weight_std;
   float norm_std;
+  // type mix: 0 Q4_K_M (Q4_K, Q6_K), 1 Q5_K_M (Q5_K in place of Q4_K), 2 Q8_0 everywhere
+  int32_t mix;
 };
 
 int rpgs_quantize_q4k(const float* x, int64_t n, uint8_t* out) {
   if (n <= 0 || n % kQK != 0) return -1;
   for (int64_t b = 0; b < n / kQK; ++b) EncodeQ4KBlock(x + b * kQK, out + b * 144);
+  return 0;
+}
+
+int rpgs_quantize_q5k(const float* x, int64_t n, uint8_t* out) {
+  if (n <= 0 || n % kQK != 0) return -1;
+  EncodeRow(kTypeQ5K, x, n, out);
+  return 0;
+}
+
+int rpgs_quantize_q8_0(const float* x, int64_t n, uint8_t* out) {
+  if (n <= 0 || n % kQK != 0) return -1;
+  EncodeRow(kTypeQ8_0, x, n, out);
   return 0;
 }
 
@@ -442,23 +513,26 @@ int rpgs_write_qwen3_gguf(const char* path, const rpgs_config* cfg, char* err, i
   const int64_t q_dim = static_cast<int64_t>(c.n_heads) * c.head_dim;
   const int64_t kv_dim = static_cast<int64_t>(c.n_kv_heads) * c.head_dim;
 
+  if (c.mix < 0 || c.mix > 2) return fail("mix must be 0 (Q4_K_M), 1 (Q5_K_M) or 2 (Q8_0)");
+  const uint32_t t4 = c.mix == 0 ? kTypeQ4K : (c.mix == 1 ? kTypeQ5K : kTypeQ8_0);
+  const uint32_t t6 = c.mix == 2 ? kTypeQ8_0 : kTypeQ6K;
   std::vector<TensorPlan> plan;
-  plan.push_back({"token_embd.weight", kTypeQ6K, c.vocab, c.hidden, 0});
+  plan.push_back({"token_embd.weight", t6, c.vocab, c.hidden, 0});
   plan.push_back({"output_norm.weight", kTypeF32, 1, c.hidden, 1});
   for (int l = 0; l < c.n_layers; ++l) {
     const std::string p = "blk." + std::to_string(l) + ".";
     const bool q6 = (l % 2) == c.q6k_parity;
     plan.push_back({p + "attn_norm.weight", kTypeF32, 1, c.hidden, 1});
-    plan.push_back({p + "attn_q.weight", kTypeQ4K, q_dim, c.hidden, 0});
-    plan.push_back({p + "attn_k.weight", kTypeQ4K, kv_dim, c.hidden, 0});
-    plan.push_back({p + "attn_v.weight", q6 ? kTypeQ6K : kTypeQ4K, kv_dim, c.hidden, 0});
-    plan.push_back({p + "attn_output.weight", kTypeQ4K, c.hidden, q_dim, 0});
+    plan.push_back({p + "attn_q.weight", t4, q_dim, c.hidden, 0});
+    plan.push_back({p + "attn_k.weight", t4, kv_dim, c.hidden, 0});
+    plan.push_back({p + "attn_v.weight", q6 ? t6 : t4, kv_dim, c.hidden, 0});
+    plan.push_back({p + "attn_output.weight", t4, c.hidden, q_dim, 0});
     plan.push_back({p + "attn_q_norm.weight", kTypeF32, 1, c.head_dim, 1});
     plan.push_back({p + "attn_k_norm.weight", kTypeF32, 1, c.head_dim, 1});
     plan.push_back({p + "ffn_norm.weight", kTypeF32, 1, c.hidden, 1});
-    plan.push_back({p + "ffn_gate.weight", kTypeQ4K, c.ffn, c.hidden, 0});
-    plan.push_back({p + "ffn_up.weight", kTypeQ4K, c.ffn, c.hidden, 0});
-    plan.push_back({p + "ffn_down.weight", q6 ? kTypeQ6K : kTypeQ4K, c.hidden, c.ffn, 0});
+    plan.push_back({p + "ffn_gate.weight", t4, c.ffn, c.hidden, 0});
+    plan.push_back({p + "ffn_up.weight", t4, c.ffn, c.hidden, 0});
+    plan.push_back({p + "ffn_down.weight", q6 ? t6 : t4, c.hidden, c.ffn, 0});
   }
 
   const uint64_t align = 32;
@@ -572,10 +646,8 @@ int rpgs_write_qwen3_gguf(const char* path, const rpgs_config* cfg, char* err, i
         uint8_t* dst = data.data() + static_cast<uint64_t>(r) * rb;
         if (t.type == kTypeF32) {
           std::memcpy(dst, row.data(), rb);
-        } else if (t.type == kTypeQ4K) {
-          for (int64_t b = 0; b < t.cols / kQK; ++b) EncodeQ4KBlock(row.data() + b * kQK, dst + b * 144);
         } else {
-          for (int64_t b = 0; b < t.cols / kQK; ++b) EncodeQ6KBlock(row.data() + b * kQK, dst + b * 210);
+          EncodeRow(t.type, row.data(), t.cols, dst);
         }
       }
     };

@@ -41,6 +41,7 @@ class ModelShape:
     rms_eps: float = 1e-6
     weight_std: float = 0.02
     norm_std: float = 0.05
+    mix: str = "q4_k_m"  # "q4_k_m" (Q4_K + Q6_K), "q5_k_m" (Q5_K + Q6_K) or "q8_0"
 
     @property
     def q_dim(self) -> int:
@@ -53,8 +54,9 @@ class ModelShape:
     def weight_bytes_per_token(self) -> int:
         """Quantised bytes one decode step streams: every layer matrix, the tied
         lm_head and the f32 norms."""
-        q4 = lambda m, k: m * k // 256 * 144  # noqa: E731
-        q6 = lambda m, k: m * k // 256 * 210  # noqa: E731
+        b4, b6 = {"q4_k_m": (144, 210), "q5_k_m": (176, 210), "q8_0": (272, 272)}[self.mix]
+        q4 = lambda m, k: m * k // 256 * b4  # noqa: E731
+        q6 = lambda m, k: m * k // 256 * b6  # noqa: E731
         total = 0
         for layer in range(self.n_layers):
             six = layer % 2 == 0
@@ -102,6 +104,7 @@ class _Cfg(ctypes.Structure):
         ("q6k_parity", ctypes.c_int32),
         ("weight_std", ctypes.c_float),
         ("norm_std", ctypes.c_float),
+        ("mix", ctypes.c_int32),
     ]
 
 
@@ -112,6 +115,10 @@ def _synth():
     lib.rpgs_quantize_q4k.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]
     lib.rpgs_quantize_q4k.restype = ctypes.c_int
     lib.rpgs_quantize_q6k.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]
+    lib.rpgs_quantize_q5k.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]
+    lib.rpgs_quantize_q5k.restype = ctypes.c_int
+    lib.rpgs_quantize_q8_0.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]
+    lib.rpgs_quantize_q8_0.restype = ctypes.c_int
     lib.rpgs_quantize_q6k.restype = ctypes.c_int
     lib.rpgs_normal.argtypes = [ctypes.c_uint64, ctypes.c_int64, ctypes.c_int64, ctypes.c_float,
                                 ctypes.c_float, ctypes.c_void_p]
@@ -129,7 +136,7 @@ def write_model(path: str, model="qwen3-1.7b", seed: int = 0, **overrides) -> st
     """Writes a synthetic GGUF for ``model`` (preset name or ModelShape)."""
     s = replace(shape(model), **overrides) if overrides else shape(model)
     cfg = _Cfg(s.n_layers, s.hidden, s.ffn, s.n_heads, s.n_kv_heads, s.head_dim, s.vocab, s.context,
-               s.rope_theta, s.rms_eps, seed, 0, s.weight_std, s.norm_std)
+               s.rope_theta, s.rms_eps, seed, 0, s.weight_std, s.norm_std, MIXES[s.mix])
     err = ctypes.create_string_buffer(256)
     rc = _synth().rpgs_write_qwen3_gguf(path.encode(), ctypes.byref(cfg), err, 256)
     if rc != 0:
@@ -142,7 +149,9 @@ def cached_model(model="qwen3-1.7b", seed: int = 0, cache_dir: str | None = None
     s = shape(model)
     cache_dir = cache_dir or os.environ.get("RPGB_MODEL_CACHE", "/tmp/rpgb_models")
     os.makedirs(cache_dir, exist_ok=True)
-    path = os.path.join(cache_dir, f"{s.name}-L{s.n_layers}-H{s.hidden}-w{s.weight_std:g}-n{s.norm_std:g}-s{seed}.gguf")
+    mix = "" if s.mix == "q4_k_m" else f"-{s.mix}"
+    path = os.path.join(cache_dir,
+                        f"{s.name}-L{s.n_layers}-H{s.hidden}-w{s.weight_std:g}-n{s.norm_std:g}{mix}-s{seed}.gguf")
     if not os.path.exists(path):
         tmp = path + f".tmp{os.getpid()}"
         write_model(tmp, s, seed)
@@ -150,12 +159,19 @@ def cached_model(model="qwen3-1.7b", seed: int = 0, cache_dir: str | None = None
     return path
 
 
+MIXES = {"q4_k_m": 0, "q5_k_m": 1, "q8_0": 2}
+# bytes per 256 elements, ggml type code
+QTYPES = {"q4_k": (144, 12), "q5_k": (176, 13), "q6_k": (210, 14), "q8_0": (272, 8)}
+
+
 def quantize(x: np.ndarray, qtype: str) -> np.ndarray:
-    """Quantises a float32 row (length a multiple of 256) to Q4_K or Q6_K bytes."""
+    """Quantises a float32 row (length a multiple of 256) to Q4_K, Q5_K, Q6_K or Q8_0 bytes."""
     x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
     nb = x.size // 256
-    out = np.zeros(nb * (144 if qtype == "q4_k" else 210), dtype=np.uint8)
-    fn = _synth().rpgs_quantize_q4k if qtype == "q4_k" else _synth().rpgs_quantize_q6k
+    out = np.zeros(nb * QTYPES[qtype][0], dtype=np.uint8)
+    lib = _synth()
+    fn = {"q4_k": lib.rpgs_quantize_q4k, "q5_k": lib.rpgs_quantize_q5k, "q6_k": lib.rpgs_quantize_q6k,
+          "q8_0": lib.rpgs_quantize_q8_0}[qtype]
     if fn(x.ctypes.data, x.size, out.ctypes.data) != 0:
         raise ValueError("length must be a positive multiple of 256")
     return out

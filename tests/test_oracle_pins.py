@@ -33,23 +33,27 @@ def test_dequant_bitexact_vs_reference_quant_cc(qtype, code, seed):
     assert np.array_equal(a.view(np.uint32), c.view(np.uint32))
 
 
+# (type code, bytes per block, elements per block, byte offsets of fp16 scales)
+BLOCKS = {12: (144, 256, (0, 2)), 13: (176, 256, (0, 2)), 14: (210, 256, (208,)), 8: (34, 32, (0,))}
+
+
 @needs_ref_quant
-@pytest.mark.parametrize("code,blk", [(12, 144), (14, 210)])
-def test_dequant_bitexact_random_bytes(code, blk):
-    """Arbitrary bytes (all scale / sign / subnormal-d patterns), not only encoder output."""
+@pytest.mark.parametrize("code", [12, 13, 14, 8])
+def test_dequant_bitexact_random_bytes(code):
+    """Arbitrary bytes (all scale / sign / subnormal-d patterns), not only
+    encoder output.  Q5_K and Q8_0 are on the reference's host path only
+    (src/quant.cc:29-45; its GPU loader rejects them, src/gpu_model.cu:26-38)."""
     o, rq = Oracle(), RefQuant()
+    blk, per, halves = BLOCKS[code]
+    n_blocks = 64 * 256 // per
     rng = np.random.default_rng(code)
-    b = rng.integers(0, 256, size=blk * 64, dtype=np.uint8)
-    # keep d / dmin finite so the comparison is on numbers, not NaN payloads
-    if code == 12:
-        for i in range(64):
-            b[i * blk + 1] &= 0x7B
-            b[i * blk + 3] &= 0x7B
-    else:
-        for i in range(64):
-            b[i * blk + 209] &= 0x7B
-    a = rq.dequant(code, b, 256 * 64)
-    c = o.dequant(code, b, 256 * 64)
+    b = rng.integers(0, 256, size=blk * n_blocks, dtype=np.uint8)
+    # keep the fp16 scales finite so the comparison is on numbers, not NaN payloads
+    for i in range(n_blocks):
+        for h in halves:
+            b[i * blk + h + 1] &= 0x7B
+    a = rq.dequant(code, b, per * n_blocks)
+    c = o.dequant(code, b, per * n_blocks)
     assert np.array_equal(a.view(np.uint32), c.view(np.uint32))
 
 
@@ -94,3 +98,18 @@ def test_quantiser_round_trip_error():
         rel[qt] = float(np.sqrt(np.mean((y - x) ** 2)) / np.sqrt(np.mean(x ** 2)))
     assert rel["q4_k"] < 0.10
     assert rel["q6_k"] < 0.03
+
+
+@needs_ref_quant
+@pytest.mark.parametrize("qtype,code,bound", [("q4_k", 12, 0.07), ("q5_k", 13, 0.035), ("q6_k", 14, 0.02),
+                                               ("q8_0", 8, 0.005)])
+def test_synthetic_encoders_decode_with_reference_quant(qtype, code, bound):
+    """The synthetic writer's encoders (csrc/synth/synth_gguf.cc) produce blocks
+    the reference's own dequantiser reads back close to the input (error under
+    `bound` of the largest |x|), and the oracle reads them identically."""
+    o, rq = Oracle(), RefQuant()
+    x = synthetic.normal(11, 256 * 64, 0.0, 0.02)
+    b = synthetic.quantize(x, qtype)
+    a = rq.dequant(code, b, x.size)
+    assert np.array_equal(a.view(np.uint32), o.dequant(code, b, x.size).view(np.uint32))
+    assert np.abs(a - x).max() <= bound * np.abs(x).max()
