@@ -188,6 +188,21 @@ struct AttnCache {
 };
 __shared__ AttnCache g_attc[kNW];
 
+// Per super-block of a matvec phase's input: the phase's output tag once the
+// warp computing its digits has stored them, so a warp's units start as soon
+// as their own super-blocks are ready instead of after every input word of
+// the phase has arrived.
+constexpr int kMaxSb = 64;  // K <= 16384
+__shared__ uint32_t g_sbready[kMaxSb];
+__device__ __forceinline__ void SbPublish(int b, uint32_t tag) {
+  asm volatile("st.release.cta.shared.u32 [%0], %1;" ::"r"(dev::SmemAddr(&g_sbready[b])), "r"(tag) : "memory");
+}
+__device__ __forceinline__ uint32_t SbLoad(int b) {
+  uint32_t v;
+  asm volatile("ld.acquire.cta.shared.u32 %0, [%1];" : "=r"(v) : "r"(dev::SmemAddr(&g_sbready[b])) : "memory");
+  return v;
+}
+
 // A warp's weight stream of one layer as runs of consecutive block groups
 // (built once per launch): slots 0-2 the q, k and v parts of its qkv units,
 // 3 the attention chunks (counted per step, g_attc), 4 o, 5 gate/up, 6 down,
@@ -244,6 +259,7 @@ __device__ __forceinline__ void FillTables(const LoopParams& p) {
       }
     } else {
       g_attc[warp].step = -1;
+      for (int i = warp; i < kMaxSb; i += kNW) g_sbready[i] = 0u;  // tags start at 1
       g_runs[warp][kRunAttn] = Run{0, 0, -1};
     }
     if (tid == 0) {
@@ -722,18 +738,21 @@ __device__ void MergeHead(const LoopParams& p, int step, int layer, int64_t pos,
     lv[i] = static_cast<double>(ml.y) + ml.z;
   }
   __syncthreads();
-  if (tid < G) {
-    const int g = tid;
-    float M = -INFINITY;
-    for (int sp = 0; sp < se; ++sp) M = fmaxf(M, wv[sp * G + g]);
-    double L = 0.0;
-    for (int sp = 0; sp < se; ++sp) {
+  if ((tid >> 5) < G) {  // warp g: lane sp holds split sp's (m, l) of q head g
+    const int g = tid >> 5, lane = tid & 31;
+    float m = -INFINITY;
+    double wl = 0.0;
+    float w = 0.f;
+    for (int sp = lane; sp < se; sp += 32) m = fmaxf(m, wv[sp * G + g]);
+    const float M = dev::WarpMax(m);
+    for (int sp = lane; sp < se; sp += 32) {
       const int k = sp * G + g;
-      const float w = wv[k] == -INFINITY ? 0.f : exp2f(wv[k] - M);
+      w = wv[k] == -INFINITY ? 0.f : exp2f(wv[k] - M);
       wv[k] = w;
-      L += static_cast<double>(w) * lv[k];
+      wl += static_cast<double>(w) * lv[k];
     }
-    inv[g] = static_cast<float>(1.0 / L);
+    const double L = dev::WarpSumD(wl);
+    if (lane == 0) inv[g] = static_cast<float>(1.0 / L);
   }
   __syncthreads();
   // kPer threads per output value, each over every kPer-th split, so all the
@@ -831,22 +850,15 @@ __device__ void MvPhase(const LoopParams& p, const GeoTable& gt, int kind, int l
         }
       }
       PutDigits(v, b, lane, bfrag, sx, sscale);
+      __syncwarp();  // the warp's digit stores, then the release of its flag
+      if (lane == 0) SbPublish(b, TagOf(p, step, layer, kind));
     }
     if (norm_w != nullptr) {
       ssq = dev::WarpSumD(ssq);
       if (lane == 0) s_sq[warp] = ssq;
     }
-    __syncthreads();
   }
-  TraceMark(p, clk, 1);  // input and digits ready in every warp
-  // RMSNorm scale (applied to W x in the epilogue), computed here so its
-  // double-precision latency overlaps the units
-  float scale = 1.f;
-  if (norm_w != nullptr && any) {
-    double tot = 0.0;
-    for (int w = 0; w < kNW; ++w) tot += s_sq[w];
-    scale = static_cast<float>(1.0 / sqrt(tot / static_cast<double>(K) + static_cast<double>(p.eps)));
-  }
+  TraceMark(p, clk, 1);  // this warp's digits stored
 
   // ---- units
   const int n_units = g.u1 - g.u0;
@@ -862,6 +874,12 @@ __device__ void MvPhase(const LoopParams& p, const GeoTable& gt, int kind, int l
     uint32_t type = SegType(p, kind, layer, SegOfTile(p, kind, g.t0 + tl, &st0));
     for (int i = 0; i < n_units; ++i) {
       const uint8_t* grp = RingWait(rg, p);
+      for (uint32_t it = 0; SbLoad(b) != TagOf(p, step, layer, kind); ++it) {  // bounded: set by the block's warps
+        if (it == (1u << 24)) {
+          atomicOr(p.err, 32u);
+          break;
+        }
+      }
       LoadB(bfrag, b, lane, lo_half, bA, bB);
       const float s = sscale[b];
       UnitOf(type, grp, bA, bB, sx + b * 8, s, lk, lane, rgv, rg8);
@@ -879,12 +897,19 @@ __device__ void MvPhase(const LoopParams& p, const GeoTable& gt, int kind, int l
   rg_io = rg;
   __syncthreads();
   TraceMark(p, clk, 2);  // all units done
+  // RMSNorm scale (applied to W x in the epilogue) from every warp's sum of squares
+  float scale = 1.f;
+  if (norm_w != nullptr && any) {
+    double tot = 0.0;
+    for (int w = 0; w < kNW; ++w) tot += s_sq[w];
+    scale = static_cast<float>(1.0 / sqrt(tot / static_cast<double>(K) + static_cast<double>(p.eps)));
+  }
 
   // ---- epilogue
   TraceMark(p, clk, 3);
+  const uint32_t tag_out = TagOf(p, step, layer, kind);
   const int U = (g.t1 - g.t0) * nb;
   const int n_rows = (g.t1 - g.t0) * kTile;
-  const uint32_t tag_out = TagOf(p, step, layer, kind);
   const int rstep = kind == kGu ? 2 : 1;
   float best_v = -FLT_MAX;
   int best_i = INT_MAX;
@@ -1582,6 +1607,8 @@ void LaunchDecodeLoop(const LoopParams& in, int group, int num_sms, cudaStream_t
   cudaFuncAttributes fa;
   RPGB_CUDA(cudaFuncGetAttributes(&fa, reinterpret_cast<const void*>(fn)));
   RPGB_CHECK(p.slot >= 2048 && p.slot % 16 == 0 && p.slot <= 8192, "decode loop: slot of %d bytes", p.slot);
+  RPGB_CHECK(std::max({p.hidden, p.n_heads * kD, p.ffn}) / 256 <= kMaxSb, "decode loop: inputs wider than %d",
+             kMaxSb * 256);
   const size_t fixed = MakePlan(0, p.slot, p.nb_max, p.x_max, p.scratch_bytes, p.max_tiles).total;
   const size_t avail = static_cast<size_t>(kSmemMax) - fa.sharedSizeBytes;
   RPGB_CHECK(avail > fixed, "decode loop: shared memory plan does not fit");
