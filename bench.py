@@ -67,6 +67,8 @@ def parse():
     ap.add_argument("--tcgemm-shape", action="store_true",
                     help="run the tcgen05 prefill GEMM twice on a Q4_K 6144x2048 matrix x 1024 tokens and exit "
                          "(the command profiled by ncu for profiles/)")
+    ap.add_argument("--decode-trace", type=int, default=0,
+                    help="print the decode loop's per-phase critical times at this context")
     ap.add_argument("--decode-loop-ctx", type=int, default=0,
                     help="prefill this many tokens, then two generate calls (2 and 4 decode steps) and exit "
                          "(the second decode-loop launch is the one profiled for profiles/)")
@@ -405,6 +407,84 @@ def decode_loop_ctx(args):
     m.close()
 
 
+def decode_trace(args):
+    """Per-phase critical times of the decode loop kernel at one context.
+
+    Prefills args.decode_trace seeded tokens, runs a 16-token sampled generate
+    (one loop launch, untimed warm-up) and then a traced one, and prints, per
+    phase kind, the mean over layers and steps of the phase's critical time:
+    the latest block's end of the phase minus the latest block's end of the
+    phase before it (the step's first phase: minus the previous step's
+    sampler).  Times come from the kernel's own device timeline (SM cycle
+    counter anchored to %globaltimer)."""
+    import numpy as np
+
+    from rpgbarenginecuda_b200 import Model, SampleOptions, Session, synthetic
+
+    m = Model(synthetic.cached_model(args.model, seed=0), 0, 4096)
+    s = Session(m, 4096)
+    ctx, n_steps = args.decode_trace, 16
+    toks = synthetic.seeded_tokens(ctx, 0, m.vocab)
+    s.prefill(toks, want_logits=False)
+    opts = SampleOptions(*SAMPLE)
+    s.generate(opts, SEED, n_steps)
+    s.set_len(ctx - 1)
+    s.prefill(toks[-1:], want_logits=False)  # the next position's logits again
+    s.trace_enable(1 << 20)
+    s.generate(opts, SEED, n_steps)
+    rec = s.trace_take(1 << 20)
+    s.trace_enable(0)
+    L = m.shape["n_layers"]
+    per = 5 * L + 2
+    main = rec[(rec["launch"] != 0xFFFFFFFF) & ((rec["block"] >> 24) == 0)]
+    ends = {}
+    for r in main:
+        k = int(r["launch"])
+        ends[k] = max(ends.get(k, 0), int(r["t_end"]))
+    names = ["qkv", "attention", "o", "gate/up", "down"]
+    acc = {n: [] for n in names + ["lm_head", "sampler", "step"]}
+    keys = sorted(ends)
+    for i in range(1, len(keys)):
+        k, kp = keys[i], keys[i - 1]
+        if k != kp + 1:
+            continue
+        ph = k % per
+        dt = (ends[k] - ends[kp]) / 1000.0
+        acc[names[ph % 5] if ph < 5 * L else ("lm_head" if ph == 5 * L else "sampler")].append(dt)
+    steps = sorted({k // per for k in keys})
+    for st in steps[1:]:
+        a, b = (st - 1) * per + per - 1, st * per + per - 1
+        if a in ends and b in ends:
+            acc["step"].append((ends[b] - ends[a]) / 1000.0)
+    print(f"decode loop trace: {args.model}, context {ctx}, {n_steps} sampled steps (T=0.7, top_k=20, top_p=0.8)")
+    print("| phase | mean us | min us | max us | per token us |")
+    print("|---|---|---|---|---|")
+    for n in names + ["lm_head", "sampler", "step"]:
+        v = np.array(acc[n]) if acc[n] else np.zeros(1)
+        mult = L if n in names else 1
+        print(f"| {n} | {v.mean():.2f} | {v.min():.2f} | {v.max():.2f} | {v.mean() * mult:.1f} |")
+    # inside a block: mean times from the end of the block's previous phase
+    # to its marks (matvec phases: 1 digits of warp 0 stored, 2 every unit
+    # done, 4 epilogue stores issued; attention: 1 first chunk's data there,
+    # 2 first chunk computed, 3 its slot refilled, 4 warp 0's chunks done)
+    # and to the end of the phase
+    kinds = {}
+    for r in rec[rec["launch"] != 0xFFFFFFFF]:
+        ph = int(r["launch"]) % per
+        n = names[ph % 5] if ph < 5 * L else ("lm_head" if ph == 5 * L else "sampler")
+        k = int(r["block"]) >> 24
+        if int(r["t_end"]) and int(r["t_start"]):
+            kinds.setdefault(n, {}).setdefault(k, []).append((int(r["t_end"]) - int(r["t_start"])) / 1000.0)
+    print("| phase | to mark 1 | mark 2 | mark 3 | mark 4 | end (us, per block) |")
+    print("|---|---|---|---|---|---|")
+    for n in names + ["lm_head", "sampler"]:
+        d = kinds.get(n, {})
+        cells = [f"{np.mean(d[k]):.2f}" if d.get(k) else "-" for k in (1, 2, 3, 4, 0)]
+        print(f"| {n} | " + " | ".join(cells) + " |")
+    s.close()
+    m.close()
+
+
 def ours(args):
     import numpy as np
     import torch
@@ -557,6 +637,8 @@ def ours(args):
             "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded N(0,0.02) weights quantised to Q4_K/Q6_K, seeded token ids)",
             "prefill_tok_s": round(prefill_tok_s, 1),
+            # the 40-token appends at context ~2900 (prefill calls of their own)
+            "append_ms": round(timing["append"][0] / max(1, args.steps * ROUNDS), 3),
             "config": {"workload": f"{args.model} turn: {PROMPT_LEN}-token prefill + {ROUNDS} x ({APPEND} appended "
                                    f"+ {DECODE} decoded) tokens, T=0.7 top_k=20 top_p=0.8",
                        "model": args.model, "global_batch": world, "seq_len": PROMPT_LEN + ROUNDS * (APPEND + DECODE),
@@ -784,6 +866,9 @@ def main():
         return
     if args.decode_loop_ctx > 0:
         decode_loop_ctx(args)
+        return
+    if args.decode_trace > 0:
+        decode_trace(args)
         return
     if args.suite:
         return suite_bench(args)

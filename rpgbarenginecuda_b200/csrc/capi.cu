@@ -35,6 +35,12 @@ struct MatrixEntry {
   std::mutex tc_mu;
   __half* tc = nullptr;
   size_t tc_halves = 0;
+  // the matrix dequantised once into fp16 hi/lo terms for the tensor-core
+  // GEMM (made by the first call that runs it; lo follows hi)
+  __half* wh = nullptr;
+  // split-K partial tiles (grown on demand)
+  float* part = nullptr;
+  size_t part_floats = 0;
   unsigned* err = nullptr;
   unsigned* err_host = nullptr;
 };
@@ -398,6 +404,8 @@ void rpgb_matrix_free(int32_t matrix) {
     cudaSetDevice(e->device);
     cudaFree(e->mem);
     cudaFree(e->tc);
+    cudaFree(e->wh);
+    cudaFree(e->part);
     cudaFree(e->err);
     if (e->err_host != nullptr) cudaFreeHost(e->err_host);
   } catch (...) {
@@ -474,7 +482,14 @@ int32_t rpgb_matrix_matvec(int32_t matrix, const float* x_dev, int64_t n_tok, fl
           *e->err_host = 0;
           Throw("matvec: a bounded device wait of an earlier tensor-core GEMM on this matrix gave up (0x%x)", prev);
         }
-        const size_t need = TcGemmScratchHalves(e->m.rows, n_tok, e->m.cols);
+        const size_t wn = static_cast<size_t>(e->m.rows) * e->m.cols;
+        if (e->wh == nullptr) {
+          RPGB_CUDA(cudaMalloc(&e->wh, 2 * wn * sizeof(__half)));
+          LaunchDequantSplit(e->m, e->wh, e->wh + wn, s);
+        }
+        g.w.wh = e->wh;
+        g.w.wl = e->wh + wn;
+        const size_t need = TcGemmScratchHalves(e->m.rows, n_tok, e->m.cols, true);
         if (e->tc_halves < need) {
           RPGB_CUDA(cudaStreamSynchronize(s));
           cudaFree(e->tc);
@@ -485,6 +500,20 @@ int32_t rpgb_matrix_matvec(int32_t matrix, const float* x_dev, int64_t n_tok, fl
         }
         g.tc_scratch = e->tc;
         g.tc_scratch_halves = e->tc_halves;
+        // split-K partials: exactly what this shape's split needs
+        const int sp = TcGemmSplits(e->m.rows, n_tok, e->m.cols, e->num_sms, TcGemmPartFloats(e->num_sms));
+        const size_t pneed = sp > 1 ? static_cast<size_t>(sp) * n_tok * e->m.rows : 0;
+        if (e->part_floats < pneed) {
+          RPGB_CUDA(cudaStreamSynchronize(s));
+          cudaFree(e->part);
+          e->part = nullptr;
+          e->part_floats = 0;
+          RPGB_CUDA(cudaMalloc(&e->part, pneed * sizeof(float)));
+          e->part_floats = pneed;
+        }
+        g.part = e->part;
+        g.part_floats = e->part_floats;
+        g.num_sms = e->num_sms;
         g.err = e->err;
         LaunchGemm(g, Epi::kStore, s);
         RPGB_CUDA(cudaMemcpyAsync(e->err_host, e->err, sizeof(unsigned), cudaMemcpyDeviceToHost, s));

@@ -266,12 +266,16 @@ void Session::EnsurePrefill(int64_t n) {
       FlashSupports(c.group(), c.head_dim) ? FlashSplitFloats(c.n_heads, c.n_kv_heads, m_->num_sms()) : 0;
   cv.Add(sizeof(float) * split_floats);
   cv.Add(sizeof(int32_t) * cap);
-  // fp16 operands of the tensor-core GEMM: the largest layer matrix and the widest activations
+  // fp16 operands of the tensor-core GEMM: the widest activations' hi/lo
+  // terms, and the largest layer matrix's unless the model keeps fp16 copies
   const int64_t kmax = std::max<int64_t>(c.hidden, std::max<int64_t>(c.q_dim(), c.ffn));
-  const int64_t wmax = std::max<int64_t>(static_cast<int64_t>(2) * c.ffn * c.hidden,
-                                         static_cast<int64_t>(c.q_dim()) * c.hidden);
+  const int64_t wmax = m_->half_bytes() > 0 ? 0
+                                            : std::max<int64_t>(static_cast<int64_t>(2) * c.ffn * c.hidden,
+                                                                static_cast<int64_t>(c.q_dim()) * c.hidden);
   const size_t tc_halves = 2 * static_cast<size_t>(wmax) + 2 * static_cast<size_t>(cap) * kmax;
   cv.Add(sizeof(__half) * tc_halves);
+  const size_t gpart_floats = TcGemmPartFloats(m_->num_sms());  // split-K partial tiles
+  cv.Add(sizeof(float) * gpart_floats);
   RPGB_CUDA(cudaStreamSynchronize(stream_));
   cudaFree(pf_arena_);
   pf_arena_ = nullptr;
@@ -288,6 +292,8 @@ void Session::EnsurePrefill(int64_t n) {
   pf_tok_ = cv.Take<int32_t>(cap);
   pf_tc_ = cv.Take<__half>(tc_halves);
   pf_tc_halves_ = tc_halves;
+  pf_gpart_ = cv.Take<float>(gpart_floats);
+  pf_gpart_floats_ = gpart_floats;
   pf_cap_ = cap;
 }
 
@@ -347,21 +353,29 @@ void Session::Prefill(const int32_t* tokens, int64_t n, float* last_logits) {
       GemmParams g;
       g.tc_scratch = pf_tc_;
       g.tc_scratch_halves = pf_tc_halves_;
+      g.part = pf_gpart_;
+      g.part_floats = pf_gpart_floats_;
+      g.num_sms = m_->num_sms();
       g.err = err_;
       g.X = pf_xn_;
       g.n_tok = nt;
       g.ldx = H;
       g.out = pf_qkv_;
       g.ldo = qkv;
-      g.w = L.q;
       g.out_off = 0;
-      LaunchGemm(g, Epi::kStore, s);
-      g.w = L.k;
-      g.out_off = qd;
-      LaunchGemm(g, Epi::kStore, s);
-      g.w = L.v;
-      g.out_off = qd + kvd;
-      LaunchGemm(g, Epi::kStore, s);
+      if (L.qkv.wh != nullptr && L.qkv.rows % 128 == 0) {  // one GEMM over the fp16 [q; k; v] terms
+        g.w = L.qkv;
+        LaunchGemm(g, Epi::kStore, s);
+      } else {
+        g.w = L.q;
+        LaunchGemm(g, Epi::kStore, s);
+        g.w = L.k;
+        g.out_off = qd;
+        LaunchGemm(g, Epi::kStore, s);
+        g.w = L.v;
+        g.out_off = qd + kvd;
+        LaunchGemm(g, Epi::kStore, s);
+      }
     }
     LaunchQkRopeKv(pf_qkv_, nt, qd, kvd, L.q_norm, L.k_norm, m_->rope(), c.rms_eps, pos_, kc, vc,
                    static_cast<int32_t>(max_seq_), c.n_heads, c.n_kv_heads, pf_q_, s);
@@ -397,6 +411,9 @@ void Session::Prefill(const int32_t* tokens, int64_t n, float* last_logits) {
       GemmParams o;
       o.tc_scratch = pf_tc_;
       o.tc_scratch_halves = pf_tc_halves_;
+      o.part = pf_gpart_;
+      o.part_floats = pf_gpart_floats_;
+      o.num_sms = m_->num_sms();
       o.err = err_;
       o.w = L.o;
       o.X = pf_attn_;
@@ -429,6 +446,9 @@ void Session::Prefill(const int32_t* tokens, int64_t n, float* last_logits) {
     GemmParams gu;
     gu.tc_scratch = pf_tc_;
     gu.tc_scratch_halves = pf_tc_halves_;
+    gu.part = pf_gpart_;
+    gu.part_floats = pf_gpart_floats_;
+    gu.num_sms = m_->num_sms();
     gu.err = err_;
     gu.w = L.gateup;
     gu.X = pf_xn_;
@@ -440,6 +460,9 @@ void Session::Prefill(const int32_t* tokens, int64_t n, float* last_logits) {
     GemmParams dn;
     dn.tc_scratch = pf_tc_;
     dn.tc_scratch_halves = pf_tc_halves_;
+    dn.part = pf_gpart_;
+    dn.part_floats = pf_gpart_floats_;
+    dn.num_sms = m_->num_sms();
     dn.err = err_;
     dn.w = L.down;
     dn.X = pf_h_;

@@ -154,6 +154,8 @@ class Session {
   int32_t* pf_tok_ = nullptr;
   __half* pf_tc_ = nullptr;  // fp16 operands of the tensor-core GEMM
   size_t pf_tc_halves_ = 0;
+  float* pf_gpart_ = nullptr;  // split-K partial tiles of the tensor-core GEMM
+  size_t pf_gpart_floats_ = 0;
   int32_t* host_ids_ = nullptr;  // pinned staging
   int64_t host_ids_cap_ = 0;
 

@@ -11,10 +11,15 @@
 // 22 significant bits of each operand survive, so results differ from the
 // FP32 path at the 1e-6 relative level (the dropped Wl*Xl term is ~2^-22).
 //
+// (Dropping the Wl*Xh term -- weights rounded to fp16 -- was measured: two
+// MMAs instead of three, but 1.8e-3 of full scale on the 1.7B model's logits
+// after a 2811-token prefill, over the 1e-3 bound.)
+//
 // Pipeline (one 128 x 128 output tile per block of 4 warps):
-//  * DequantSplitKernel writes the layer matrix once per call as Wh / Wl
-//    (row-major, fp16) with the bit-exact per-element dequant formulas;
-//    SplitKernel writes Xh / Xl;
+//  * DequantSplitKernel writes a matrix as Wh / Wl (row-major, fp16) with the
+//    bit-exact per-element dequant formulas -- once at model load into the
+//    model's own copy (Model::Load), or per call into the call's scratch for
+//    a matrix without one; SplitKernel writes Xh / Xl;
 //  * thread 0 streams 64-column k-slices of Wh, Wl, Xh, Xl into three
 //    shared-memory stages with 2-D TMA tensor copies (128-byte swizzle);
 //  * thread 32 issues tcgen05.mma.cta_group::1.kind::f16 (M 128, N 128,
@@ -200,6 +205,11 @@ struct TcArgs {
   const float* resid;
   int32_t ldr;
   unsigned* err;
+  // split-K (gridDim.z > 1): block z sums k-slices [z nk / S, (z + 1) nk / S)
+  // and stores its raw tile into part[z][n_tok][rows]; SplitReduceKernel
+  // adds the S partials in order and applies the epilogue
+  float* part;
+  int32_t rows;
 };
 
 template <int EPI>
@@ -212,7 +222,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tok0 = blockIdx.x * kBN, row0 = blockIdx.y * kBM;
-  const int nk = a.K / kBK;
+  const int nk_all = a.K / kBK;
+  const int kb0 = static_cast<int>(blockIdx.z * nk_all / gridDim.z);
+  const int nk = static_cast<int>((blockIdx.z + 1) * nk_all / gridDim.z) - kb0;
 
   if (warp == 0) {  // the accumulator: 128 TMEM columns x 128 lanes (fp32)
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dev::SmemAddr(&s_tmem)),
@@ -243,11 +255,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       uint8_t* st = smem + s * kStageBytes;
+      const int kx = (kb0 + kb) * kBK;
       dev::MbarExpectTx(full + s, kStageBytes);
-      TmaLoad2D(st, &mWh, kb * kBK, row0, full + s);
-      TmaLoad2D(st + kTileBytes, &mWl, kb * kBK, row0, full + s);
-      TmaLoad2D(st + 2 * kTileBytes, &mXh, kb * kBK, tok0, full + s);
-      TmaLoad2D(st + 3 * kTileBytes, &mXl, kb * kBK, tok0, full + s);
+      TmaLoad2D(st, &mWh, kx, row0, full + s);
+      TmaLoad2D(st + kTileBytes, &mWl, kx, row0, full + s);
+      TmaLoad2D(st + 2 * kTileBytes, &mXh, kx, tok0, full + s);
+      TmaLoad2D(st + 3 * kTileBytes, &mXl, kx, tok0, full + s);
       issued = kb + 1;
     }
     // the copies of the last stages land before the block may exit
@@ -293,7 +306,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < 16; ++j) {
         const int t = tok0 + c0 + j;
         const float acc = __uint_as_float(v[j]);
-        if (EPI == static_cast<int>(Epi::kSilu)) {
+        if (gridDim.z > 1) {
+          if (t < a.n_tok) a.part[(static_cast<int64_t>(blockIdx.z) * a.n_tok + t) * a.rows + r] = acc;
+        } else if (EPI == static_cast<int>(Epi::kSilu)) {
           // rows 2i (gate) and 2i+1 (up) sit in neighbouring lanes
           const float u = __shfl_xor_sync(0xFFFFFFFFu, acc, 1);
           if (t < a.n_tok && (lane & 1) == 0) {
@@ -315,6 +330,35 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     FenceAfterSync();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(128u) : "memory");
+  }
+}
+
+// Sum of the split-K partials in split order, then the GEMM's epilogue.
+template <int EPI>
+__global__ void __launch_bounds__(256) SplitReduceKernel(const TcArgs a, int splits) {
+  const int64_t per = EPI == static_cast<int>(Epi::kSilu) ? a.rows / 2 : a.rows;
+  const int64_t items = static_cast<int64_t>(a.n_tok) * per;
+  const int64_t plane = static_cast<int64_t>(a.n_tok) * a.rows;
+  for (int64_t it = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; it < items;
+       it += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = it / per, i = it - t * per;
+    if (EPI == static_cast<int>(Epi::kSilu)) {
+      float g = 0.f, u = 0.f;
+      for (int z = 0; z < splits; ++z) {
+        const float2 gu = *reinterpret_cast<const float2*>(a.part + z * plane + t * a.rows + 2 * i);
+        g += gu.x;
+        u += gu.y;
+      }
+      a.out[t * a.ldo + i] = (g / (1.0f + expf(-g))) * u;
+    } else {
+      float v = 0.f;
+      for (int z = 0; z < splits; ++z) v += a.part[z * plane + t * a.rows + i];
+      if (EPI == static_cast<int>(Epi::kResid)) {
+        a.out[t * a.ldo + i] = a.resid[t * a.ldr + i] + v;
+      } else {
+        a.out[t * a.ldo + a.out_off + i] = v;
+      }
+    }
   }
 }
 
@@ -369,8 +413,30 @@ void PrepareTcGemmKernels() {
   }
 }
 
-size_t TcGemmScratchHalves(int64_t rows, int64_t n_tok, int K) {
-  return 2 * static_cast<size_t>(rows) * K + 2 * static_cast<size_t>(n_tok) * K;
+size_t TcGemmScratchHalves(int64_t rows, int64_t n_tok, int K, bool has_wh) {
+  return (has_wh ? 0 : 2 * static_cast<size_t>(rows) * K) + 2 * static_cast<size_t>(n_tok) * K;
+}
+
+int TcGemmSplits(int64_t rows, int64_t n_tok, int K, int num_sms, size_t part_floats) {
+  const int64_t tiles = (rows / kBM) * ((n_tok + kBN - 1) / kBN);
+  const int nk = K / kBK;
+  if (num_sms <= 0 || tiles * 2 > num_sms || nk < 8) return 1;
+  // enough splits to fill the SMs, at least four k-slices each, and room
+  // for the partial tiles
+  int64_t sp = std::min<int64_t>(num_sms / tiles, nk / 4);
+  const int64_t plane = rows * n_tok;
+  if (plane > 0) sp = std::min<int64_t>(sp, static_cast<int64_t>(part_floats / static_cast<size_t>(plane)));
+  return sp >= 2 ? static_cast<int>(sp) : 1;
+}
+
+size_t TcGemmPartFloats(int num_sms) { return static_cast<size_t>(num_sms) * kBM * kBN; }
+
+void LaunchDequantSplit(const DevMat& w, __half* hi, __half* lo, cudaStream_t s) {
+  const int64_t items = static_cast<int64_t>(w.rows) * (w.cols / 8);
+  const int blocks = static_cast<int>(std::min<int64_t>((items + 255) / 256, 148 * 16));
+  DequantSplitKernel<<<blocks, 256, 0, s>>>(w, hi, lo);
+  RPGB_CUDA(cudaGetLastError());
+  CountLaunches(1);
 }
 
 void LaunchTcGemm(const GemmParams& p, Epi epi, __half* scratch, size_t scratch_halves, cudaStream_t s) {
@@ -380,19 +446,21 @@ void LaunchTcGemm(const GemmParams& p, Epi epi, __half* scratch, size_t scratch_
   RPGB_CHECK(K % 256 == 0, "tcgen05 gemm: cols %d not a multiple of 256", K);
   RPGB_CHECK(p.n_tok > 0 && p.ldx % 4 == 0, "tcgen05 gemm: bad activations");
   RPGB_CHECK(p.err != nullptr, "tcgen05 gemm: no error word");
-  const size_t need = TcGemmScratchHalves(w.rows, p.n_tok, K);
+  RPGB_CHECK((w.wh != nullptr && w.wl != nullptr) || w.q != nullptr, "tcgen05 gemm: matrix without weights");
+  const bool has_wh = w.wh != nullptr && w.wl != nullptr;
+  const size_t need = TcGemmScratchHalves(w.rows, p.n_tok, K, has_wh);
   RPGB_CHECK(scratch != nullptr && scratch_halves >= need, "tcgen05 gemm: scratch of %zu halves < %zu",
              scratch_halves, need);
-  __half* wh = scratch;
-  __half* wl = wh + static_cast<size_t>(w.rows) * K;
-  __half* xh = wl + static_cast<size_t>(w.rows) * K;
-  __half* xl = xh + static_cast<size_t>(p.n_tok) * K;
-  {
-    const int64_t items = static_cast<int64_t>(w.rows) * (K / 8);
-    const int blocks = static_cast<int>(std::min<int64_t>((items + 255) / 256, 148 * 16));
-    DequantSplitKernel<<<blocks, 256, 0, s>>>(w, wh, wl);
-    RPGB_CUDA(cudaGetLastError());
+  const __half* wh = w.wh;
+  const __half* wl = w.wl;
+  __half* xh = scratch;
+  if (!has_wh) {
+    LaunchDequantSplit(w, scratch, scratch + static_cast<size_t>(w.rows) * K, s);
+    wh = scratch;
+    wl = scratch + static_cast<size_t>(w.rows) * K;
+    xh = scratch + 2 * static_cast<size_t>(w.rows) * K;
   }
+  __half* xl = xh + static_cast<size_t>(p.n_tok) * K;
   {
     const int64_t items = static_cast<int64_t>(p.n_tok) * (K / 8);
     const int blocks = static_cast<int>(std::min<int64_t>((items + 255) / 256, 148 * 16));
@@ -410,11 +478,26 @@ void LaunchTcGemm(const GemmParams& p, Epi epi, __half* scratch, size_t scratch_
   a.resid = p.resid;
   a.ldr = p.ldr;
   a.err = p.err;
-  const dim3 grid((p.n_tok + kBN - 1) / kBN, w.rows / kBM);
+  a.part = p.part;
+  a.rows = w.rows;
+  const int splits = TcGemmSplits(w.rows, p.n_tok, K, p.num_sms, p.part_floats);
+  const dim3 grid((p.n_tok + kBN - 1) / kBN, w.rows / kBM, splits);
   RPGB_CHECK(grid.y < 65536, "tcgen05 gemm: too many rows");
   PickTc(epi)<<<grid, kThreads, kSmemBytes, s>>>(mWh, mWl, mXh, mXl, a);
   RPGB_CUDA(cudaGetLastError());
-  CountLaunches(3);
+  CountLaunches(2);
+  if (splits > 1) {
+    const int64_t items = static_cast<int64_t>(p.n_tok) * w.rows;
+    const int blocks = static_cast<int>(std::min<int64_t>((items + 255) / 256, 148 * 8));
+    switch (epi) {
+      case Epi::kStore: SplitReduceKernel<0><<<blocks, 256, 0, s>>>(a, splits); break;
+      case Epi::kResid: SplitReduceKernel<1><<<blocks, 256, 0, s>>>(a, splits); break;
+      case Epi::kSilu: SplitReduceKernel<2><<<blocks, 256, 0, s>>>(a, splits); break;
+      default: Throw("tcgen05 gemm: unsupported epilogue");
+    }
+    RPGB_CUDA(cudaGetLastError());
+    CountLaunches(1);
+  }
 }
 
 }  // namespace rpgb

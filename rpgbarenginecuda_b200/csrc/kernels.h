@@ -176,17 +176,35 @@ struct GemmParams {
   const float* resid = nullptr;
   int32_t ldr = 0;
   // tensor-core path (k_tcgemm.cu): fp16 operand scratch of at least
-  // TcGemmScratchHalves(rows, n_tok, cols) halves, and an error word
+  // TcGemmScratchHalves(rows, n_tok, cols, w.wh != nullptr) halves, and an
+  // error word.  With w.wh / w.wl set the weights are read from that fp16
+  // copy and w.q may be null (the fused q|k|v matrix of a layer).
   __half* tc_scratch = nullptr;
   size_t tc_scratch_halves = 0;
   unsigned* err = nullptr;
+  // split-K for GEMMs with few output tiles (short prompts, appended turns):
+  // a float buffer for the partial tiles (TcGemmPartFloats(num_sms) is
+  // enough for any shape; null = no split) and the SM count to fill
+  float* part = nullptr;
+  size_t part_floats = 0;
+  int32_t num_sms = 0;
 };
 // Prompts of at least kTcMinTokens tokens (and weight rows a multiple of 128)
 // run on the tcgen05 GEMM when scratch is given; others on the FP32 SIMT tile.
 constexpr int kTcMinTokens = 16;
 void LaunchGemm(const GemmParams& p, Epi epi, cudaStream_t s);
 void LaunchTcGemm(const GemmParams& p, Epi epi, __half* scratch, size_t scratch_halves, cudaStream_t s);
-size_t TcGemmScratchHalves(int64_t rows, int64_t n_tok, int K);
+// fp16 operand scratch of one GEMM: the activations' hi/lo terms, plus the
+// weights' hi/lo expansion unless the matrix carries its own (w.wh, w.wl)
+size_t TcGemmScratchHalves(int64_t rows, int64_t n_tok, int K, bool has_wh = false);
+// W (repacked) -> hi, lo [rows][cols] fp16 with hi + lo the bit-exact
+// dequantised value to ~22 bits (the prefill GEMM's weight operands)
+void LaunchDequantSplit(const DevMat& w, __half* hi, __half* lo, cudaStream_t s);
+// Splits of the K range the GEMM uses for this shape (1 = none): with fewer
+// 128 x 128 output tiles than half the SMs, enough to fill the SMs with at
+// least four 64-column k-slices each, bounded by the partial buffer.
+int TcGemmSplits(int64_t rows, int64_t n_tok, int K, int num_sms, size_t part_floats);
+size_t TcGemmPartFloats(int num_sms);
 void PrepareTcGemmKernels();
 
 // ------------------------------------------------------------------ sampler

@@ -271,11 +271,12 @@ void RepackRows(uint32_t type, const uint8_t* src, int64_t rows, int64_t cols, u
 }
 
 Model::~Model() {
-  if (arena_ != nullptr) {
+  if (arena_ != nullptr || half_arena_ != nullptr) {
     int cur = 0;
     cudaGetDevice(&cur);
     cudaSetDevice(device_);
-    cudaFree(arena_);
+    if (arena_ != nullptr) cudaFree(arena_);
+    if (half_arena_ != nullptr) cudaFree(half_arena_);
     cudaSetDevice(cur);
   }
 }
@@ -535,6 +536,43 @@ std::unique_ptr<Model> Model::Load(const std::string& path, int device, int32_t 
     m->rope_ = reinterpret_cast<float*>(carve(rope_bytes));
     upload_plain(m->rope_, rope.data(), rope_bytes);
   }
+  // fp16 hi/lo copies of the layer matrices for the tensor-core prefill GEMM,
+  // made once here instead of per prefill call (all hi terms, then all lo
+  // terms at the same offsets; q, k, v adjacent so that one GEMM covers
+  // them); kept only when the device has room to spare (4 GiB beyond them),
+  // otherwise the GEMM expands each matrix into its scratch per call
+  {
+    size_t halves = 0;
+    for (const DevLayer& L : m->layers_) {
+      for (const DevMat* w : {&L.q, &L.k, &L.v, &L.o, &L.gateup, &L.down}) {
+        halves += static_cast<size_t>(w->rows) * w->cols;
+      }
+    }
+    size_t free_b = 0, total_b = 0;
+    RPGB_CUDA(cudaMemGetInfo(&free_b, &total_b));
+    if (halves > 0 && free_b > halves * 4 + (static_cast<size_t>(4) << 30) &&
+        cudaMalloc(&m->half_arena_, halves * 4) == cudaSuccess) {
+      m->half_bytes_ = static_cast<int64_t>(halves * 4);
+      __half* h = m->half_arena_;
+      for (DevLayer& L : m->layers_) {
+        L.qkv = DevMat{};
+        L.qkv.rows = L.q.rows + L.k.rows + L.v.rows;
+        L.qkv.cols = L.q.cols;
+        L.qkv.nb = L.q.nb;
+        L.qkv.wh = h;
+        L.qkv.wl = h + halves;
+        for (DevMat* w : {&L.q, &L.k, &L.v, &L.o, &L.gateup, &L.down}) {
+          LaunchDequantSplit(*w, h, h + halves, nullptr);
+          w->wh = h;
+          w->wl = h + halves;
+          h += static_cast<size_t>(w->rows) * w->cols;
+        }
+      }
+      RPGB_CUDA(cudaDeviceSynchronize());
+    } else {
+      cudaGetLastError();  // a failed allocation leaves no sticky error
+    }
+  }
   // the layer table read by the decode loop kernel (pointers into this arena)
   {
     DevLayer* t = reinterpret_cast<DevLayer*>(carve(layer_table_bytes));
@@ -543,8 +581,9 @@ std::unique_ptr<Model> Model::Load(const std::string& path, int device, int32_t 
   }
   up.Wait();
   RPGB_CHECK(cursor <= total, "arena overflow (%zu > %zu)", cursor, total);
-  RPGB_INFO("loaded %s: %d layers, hidden %d, vocab %d, %.2f GiB on device %d", c.name.c_str(), c.n_layers,
-            c.hidden, c.vocab, static_cast<double>(total) / (1 << 30), device);
+  RPGB_INFO("loaded %s: %d layers, hidden %d, vocab %d, %.2f GiB (+ %.2f GiB fp16 prefill operands) on device %d",
+            c.name.c_str(), c.n_layers, c.hidden, c.vocab, static_cast<double>(total) / (1 << 30),
+            static_cast<double>(m->half_bytes_) / (1 << 30), device);
   return m;
 }
 

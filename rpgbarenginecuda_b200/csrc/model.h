@@ -18,6 +18,7 @@
 #include <string>
 #include <vector>
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "gguf.h"
@@ -42,10 +43,16 @@ ModelMeta ReadModelMeta(const GgufFile& g);
 
 // One quantised matrix in the repacked device layout (passed to kernels by value).
 // Block group (tile t, super-block b) starts at q + (t * nb + b) * GroupBytes(type).
+// wh / wl, when set, are the same matrix dequantised once into two fp16
+// terms (row-major [rows][cols]; wh + wl is the bit-exact dequantised value
+// to ~22 bits): the operands of the tensor-core prefill GEMM, which then
+// needs no per-call expansion.
 struct DevMat {
   uint32_t type = 0;  // kGgmlQ4_K, kGgmlQ5_K, kGgmlQ6_K or kGgmlQ8_0
   int32_t rows = 0, cols = 0, nb = 0;
   const uint8_t* q = nullptr;
+  const __half* wh = nullptr;
+  const __half* wl = nullptr;
 };
 
 struct DevLayer {
@@ -56,6 +63,10 @@ struct DevLayer {
   DevMat q, k, v, o;
   DevMat gateup;  // rows interleaved: 2i = ffn_gate row i, 2i+1 = ffn_up row i
   DevMat down;
+  // q, k and v as one fp16 matrix [q rows; k rows; v rows] (only wh / wl
+  // are set; null when the model keeps no fp16 copy): one prefill GEMM
+  // writes the concatenated q | k | v row of every token
+  DevMat qkv;
 };
 
 // Host-side repack of GGUF blocks into the device layout.  RepackTile takes
@@ -100,7 +111,9 @@ class Model {
   const float* out_norm() const { return out_norm_; }
   const float* rope() const { return rope_; }
   int32_t rope_positions() const { return rope_pos_; }
-  int64_t device_bytes() const { return arena_bytes_; }
+  int64_t device_bytes() const { return arena_bytes_ + half_bytes_; }
+  // Bytes of the fp16 hi/lo copies of the layer matrices (0 when there is no room for them).
+  int64_t half_bytes() const { return half_bytes_; }
 
  private:
   Model() = default;
@@ -112,6 +125,8 @@ class Model {
   int num_sms_ = 0;
   uint8_t* arena_ = nullptr;
   int64_t arena_bytes_ = 0;
+  __half* half_arena_ = nullptr;
+  int64_t half_bytes_ = 0;
   std::vector<DevLayer> layers_;
   const DevLayer* layers_dev_ = nullptr;
   DevMat embd_, lm_head_;

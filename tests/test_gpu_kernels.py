@@ -84,4 +84,9 @@ def test_tcgemm_many_token_tiles(oracle, qtype, rows, cols):
     ref = oracle.matvec(qtype, b, rows, cols, x)
     err = np.abs(out.cpu().numpy() - ref).max() / np.abs(ref).max()
     assert err < 5e-5, err  # same bound as the other tensor-core cases
+    # a second call reads the fp16 operands the first one left with the matrix
+    out2 = torch.empty_like(out)
+    m.matvec(xd.data_ptr(), n_tok, out2.data_ptr())
+    torch.cuda.synchronize()
+    assert torch.equal(out, out2)
     m.close()
