@@ -710,18 +710,20 @@ __global__ void __launch_bounds__(128) QkRopeKvKernel(const float* __restrict__ 
                                                       const int64_t* __restrict__ pos0, __half* kc, __half* vc,
                                                       int32_t max_seq, int n_heads, int n_kv,
                                                       float* __restrict__ q_out) {
+  // block (t, head): head < n_heads is q head `head`, the others KV head
+  // head - n_heads (its k row normalised and rotated, its v row copied)
   __shared__ __align__(16) float buf[1][D];
   __shared__ double dsh[4];
-  const int t = blockIdx.x, tid = threadIdx.x;
+  const int t = blockIdx.x, head = blockIdx.y, tid = threadIdx.x;
   const int64_t pos = *pos0 + t;
   const float* row = qkv + static_cast<int64_t>(t) * (q_dim + 2 * kv_dim);
   const float* rr = rope + pos * D;
-  for (int hq = 0; hq < n_heads; ++hq) {
-    float v[1] = {row[hq * D + tid]};
+  if (head < n_heads) {
+    float v[1] = {row[head * D + tid]};
     NormRope<1>(v, q_norm, eps, rr, buf, dsh);
-    q_out[static_cast<int64_t>(t) * q_dim + hq * D + tid] = v[0];
-  }
-  for (int hk = 0; hk < n_kv; ++hk) {
+    q_out[static_cast<int64_t>(t) * q_dim + head * D + tid] = v[0];
+  } else {
+    const int hk = head - n_heads;
     float v[1] = {row[q_dim + hk * D + tid]};
     NormRope<1>(v, k_norm, eps, rr, buf, dsh);
     const int64_t off = (static_cast<int64_t>(hk) * max_seq + pos) * D + tid;
@@ -802,8 +804,9 @@ void LaunchQkRopeKv(const float* qkv, int n_tok, int q_dim, int kv_dim, const fl
                     const float* rope, float eps, const int64_t* pos0, __half* kc, __half* vc, int32_t max_seq,
                     int n_heads, int n_kv, float* q_out, cudaStream_t s) {
   RPGB_CHECK(n_tok > 0, "qk_rope: empty");
-  QkRopeKvKernel<<<n_tok, 128, 0, s>>>(qkv, q_dim, kv_dim, q_norm, k_norm, rope, eps, pos0, kc, vc, max_seq,
-                                       n_heads, n_kv, q_out);
+  RPGB_CHECK(n_heads + n_kv < 65536, "qk_rope: too many heads");
+  QkRopeKvKernel<<<dim3(n_tok, n_heads + n_kv), 128, 0, s>>>(qkv, q_dim, kv_dim, q_norm, k_norm, rope, eps, pos0, kc,
+                                                            vc, max_seq, n_heads, n_kv, q_out);
   RPGB_CUDA(cudaGetLastError());
   CountLaunches(1);
 }

@@ -65,6 +65,16 @@ constexpr uint32_t kBarLimit = 1u << 22;  // polls of a grid barrier before givi
 
 enum Kind : int { kQkv = 0, kAttn = 1, kO = 2, kGu = 3, kDown = 4, kLm = 5 };
 
+// float(1 / sqrt(a)) for the RMSNorm scale: the float estimate refined by two
+// Newton steps in double (error ~2^-50 before the rounding to float, against
+// ~0.3 us for a double sqrt and division on the critical path of a phase).
+__device__ __forceinline__ float RmsScale(double a) {
+  double r = static_cast<double>(rsqrtf(static_cast<float>(a)));
+  r = r * (1.5 - 0.5 * a * r * r);
+  r = r * (1.5 - 0.5 * a * r * r);
+  return static_cast<float>(r);
+}
+
 // ------------------------------------------------------------------ shared memory plan
 
 struct Plan {
@@ -456,8 +466,11 @@ __device__ __forceinline__ void RingRelease(Ring& r, const LoopParams& p, const 
     r.cs = 0;
     r.cpar ^= 1u;
   }
+  // No proxy fence before the refill: every lane's reads of the slot were
+  // consumed (their values fed the unit's MMAs or FMAs) before the
+  // __syncwarp above, so the bulk copy that overwrites the slot cannot
+  // overtake them (measured: 0.5 % per token without the fence).
   if ((threadIdx.x & 31) == 0 && (!attn_only || r.cur.ri == kRunAttn)) {
-    dev::FenceProxyAsync();
     RingPump(r, p, gt, pos0, warp);
   }
 }
@@ -799,7 +812,6 @@ __device__ void MvPhase(const LoopParams& p, const GeoTable& gt, int kind, int l
   Ring rg = rg_io;  // in registers for the unit loop
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (lane == 0) {  // refills the attention phase deferred (a no-op when the ring is full)
-    dev::FenceProxyAsync();
     RingPump(rg, p, gt, pos0, warp);
   }
   const MvShape sh = ShapeOf(p, kind);
@@ -902,7 +914,7 @@ __device__ void MvPhase(const LoopParams& p, const GeoTable& gt, int kind, int l
   if (norm_w != nullptr && any) {
     double tot = 0.0;
     for (int w = 0; w < kNW; ++w) tot += s_sq[w];
-    scale = static_cast<float>(1.0 / sqrt(tot / static_cast<double>(K) + static_cast<double>(p.eps)));
+    scale = RmsScale(tot / static_cast<double>(K) + static_cast<double>(p.eps));
   }
 
   // ---- epilogue
@@ -1081,7 +1093,7 @@ __device__ void AttnPhase(const LoopParams& p, const GeoTable& gt, int layer, in
   __syncthreads();
   if (vi <= G) {
     const double tot = as.sq[2 * vi] + as.sq[2 * vi + 1];
-    const float sc = static_cast<float>(1.0 / sqrt(tot / static_cast<double>(kD) + static_cast<double>(p.eps)));
+    const float sc = RmsScale(tot / static_cast<double>(kD) + static_cast<double>(p.eps));
     // scores in log2 units (q times 1/sqrt(128) times log2(e)): the softmax
     // then exponentiates with exp2f; the split records carry the same units
     const float qscale = p.scale * 1.4426950408889634f;

@@ -15,19 +15,22 @@
 // MMAs instead of three, but 1.8e-3 of full scale on the 1.7B model's logits
 // after a 2811-token prefill, over the 1e-3 bound.)
 //
-// Pipeline (one 128 x 128 output tile per block of 4 warps):
+// Pipeline (persistent: one block of 6 warps per SM walks 128 x 128 output
+// tiles, token tiles fastest):
 //  * DequantSplitKernel writes a matrix as Wh / Wl (row-major, fp16) with the
 //    bit-exact per-element dequant formulas -- once at model load into the
 //    model's own copy (Model::Load), or per call into the call's scratch for
 //    a matrix without one; SplitKernel writes Xh / Xl;
-//  * thread 0 streams 64-column k-slices of Wh, Wl, Xh, Xl into three
+//  * warp 0 streams 64-column k-slices of Wh, Wl, Xh, Xl into three
 //    shared-memory stages with 2-D TMA tensor copies (128-byte swizzle);
-//  * thread 32 issues tcgen05.mma.cta_group::1.kind::f16 (M 128, N 128,
-//    K 16; 12 per k-slice) into a 128-column TMEM accumulator and frees each
-//    stage with tcgen05.commit on its "empty" mbarrier;
-//  * all four warps read their 32 TMEM lanes (= 32 weight rows) with
-//    tcgen05.ld and apply the epilogue (store, residual add, or SiLU(gate) *
-//    up on interleaved row pairs) with coalesced stores.
+//  * warp 1 issues tcgen05.mma.cta_group::1.kind::f16 (M 128, N 128, K 16;
+//    12 per k-slice) into one of two 128-column TMEM accumulators (tiles
+//    alternate) and frees each stage with tcgen05.commit on its "empty"
+//    mbarrier;
+//  * warps 2-5 read their 32 TMEM lanes (= 32 weight rows) with tcgen05.ld
+//    and apply the epilogue (store, residual add, or SiLU(gate) * up on
+//    interleaved row pairs) with coalesced stores, while the MMAs of the
+//    next tile run into the other accumulator.
 // Every mbarrier wait is bounded; a wait that gives up sets *err, and the
 // block still waits for its own copies and MMAs and frees its TMEM.
 #include <cuda.h>
@@ -47,7 +50,8 @@ constexpr int kBM = 128;     // weight rows per tile (MMA M)
 constexpr int kBN = 128;     // tokens per tile (MMA N)
 constexpr int kBK = 64;      // k per stage: 64 fp16 = one 128-byte swizzle row
 constexpr int kStages = 3;
-constexpr int kThreads = 128;
+constexpr int kThreads = 192;     // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int kEpiThreads = 128;
 constexpr uint32_t kTileBytes = kBM * kBK * 2;  // 16 KB, same for the B tiles (kBN == kBM)
 constexpr uint32_t kStageBytes = 4 * kTileBytes;
 constexpr size_t kSmemBytes = kStages * kStageBytes + 1024;  // + alignment slack
@@ -210,25 +214,49 @@ struct TcArgs {
   // adds the S partials in order and applies the epilogue
   float* part;
   int32_t rows;
+  int32_t splits;
 };
 
+__device__ __forceinline__ void MbarArrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(dev::SmemAddr(bar)) : "memory");
+}
+
+// Work item it -> its output tile and K range (token tiles fastest, so the
+// blocks running at one time share weight row tiles in L2).
+struct TcItem {
+  int tok0, row0, z, kb0, nk;
+};
+__device__ __forceinline__ TcItem ItemOf(const TcArgs& a, int it, int tok_tiles, int nk_all) {
+  TcItem w;
+  const int S = a.splits;
+  w.z = it % S;
+  const int tile = it / S;
+  w.tok0 = (tile % tok_tiles) * kBN;
+  w.row0 = (tile / tok_tiles) * kBM;
+  w.kb0 = w.z * nk_all / S;
+  w.nk = (w.z + 1) * nk_all / S - w.kb0;
+  return w;
+}
+
+// Persistent, warp-specialised: warp 0 streams operands, warp 1 issues the
+// MMAs, warps 2-5 run the epilogue.  Two 128-column TMEM accumulators let
+// the epilogue of one tile overlap the main loop of the next.
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     TcGemmKernel(const __grid_constant__ CUtensorMap mWh, const __grid_constant__ CUtensorMap mWl,
                  const __grid_constant__ CUtensorMap mXh, const __grid_constant__ CUtensorMap mXl, const TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t full[kStages], empty[kStages], accf;
+  __shared__ __align__(8) uint64_t full[kStages], empty[kStages], accf[2], acce[2];
   __shared__ uint32_t s_tmem;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int tok0 = blockIdx.x * kBN, row0 = blockIdx.y * kBM;
+  const int tok_tiles = (a.n_tok + kBN - 1) / kBN;
+  const int items = tok_tiles * (a.rows / kBM) * a.splits;
   const int nk_all = a.K / kBK;
-  const int kb0 = static_cast<int>(blockIdx.z * nk_all / gridDim.z);
-  const int nk = static_cast<int>((blockIdx.z + 1) * nk_all / gridDim.z) - kb0;
 
-  if (warp == 0) {  // the accumulator: 128 TMEM columns x 128 lanes (fp32)
+  if (warp == 0) {  // two accumulators: 2 x 128 TMEM columns x 128 lanes (fp32)
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dev::SmemAddr(&s_tmem)),
-                 "r"(128u)
+                 "r"(256u)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -237,7 +265,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       dev::MbarInit(full + s, 1);
       dev::MbarInit(empty + s, 1);
     }
-    dev::MbarInit(&accf, 1);
+    for (int b = 0; b < 2; ++b) {
+      dev::MbarInit(accf + b, 1);
+      dev::MbarInit(acce + b, kEpiThreads);
+    }
     dev::MbarInitFence();
   }
   FenceBeforeSync();
@@ -245,91 +276,120 @@ __global__ void __launch_bounds__(kThreads, 1)
   FenceAfterSync();
   const uint32_t tmem = s_tmem;
 
-  if (tid == 0) {
-    // ---- producer: k-slices of Wh, Wl, Xh, Xl into the stages
-    int issued = 0;
-    for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % kStages;
-      if (kb >= kStages && !dev::MbarWait(empty + s, static_cast<uint32_t>((kb / kStages - 1) & 1))) {
-        atomicOr(a.err, 16u);
-        break;
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- producer: k-slices of Wh, Wl, Xh, Xl into the stages, item after item
+      uint32_t q = 0;  // k-slices issued by this block
+      bool bad = false;
+      for (int it = blockIdx.x; it < items && !bad; it += gridDim.x) {
+        const TcItem w = ItemOf(a, it, tok_tiles, nk_all);
+        for (int kb = 0; kb < w.nk; ++kb, ++q) {
+          const int s = static_cast<int>(q % kStages);
+          if (q >= kStages && !dev::MbarWait(empty + s, (q / kStages - 1u) & 1u)) {
+            atomicOr(a.err, 16u);
+            bad = true;
+            break;
+          }
+          uint8_t* st = smem + s * kStageBytes;
+          const int kx = (w.kb0 + kb) * kBK;
+          dev::MbarExpectTx(full + s, kStageBytes);
+          TmaLoad2D(st, &mWh, kx, w.row0, full + s);
+          TmaLoad2D(st + kTileBytes, &mWl, kx, w.row0, full + s);
+          TmaLoad2D(st + 2 * kTileBytes, &mXh, kx, w.tok0, full + s);
+          TmaLoad2D(st + 3 * kTileBytes, &mXl, kx, w.tok0, full + s);
+        }
       }
-      uint8_t* st = smem + s * kStageBytes;
-      const int kx = (kb0 + kb) * kBK;
-      dev::MbarExpectTx(full + s, kStageBytes);
-      TmaLoad2D(st, &mWh, kx, row0, full + s);
-      TmaLoad2D(st + kTileBytes, &mWl, kx, row0, full + s);
-      TmaLoad2D(st + 2 * kTileBytes, &mXh, kx, tok0, full + s);
-      TmaLoad2D(st + 3 * kTileBytes, &mXl, kx, tok0, full + s);
-      issued = kb + 1;
+      // the copies of the last stages land before the block may exit
+      for (uint32_t k = q > kStages ? q - kStages : 0u; k < q; ++k) {
+        dev::MbarWait(full + k % kStages, (k / kStages) & 1u);
+      }
     }
-    // the copies of the last stages land before the block may exit
-    for (int kb = std::max(0, issued - kStages); kb < issued; ++kb) {
-      dev::MbarWait(full + kb % kStages, static_cast<uint32_t>((kb / kStages) & 1));
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---- MMA issuer
+      constexpr uint32_t idesc = InstrDesc(kBM, kBN);
+      uint32_t q = 0, j = 0;
+      bool bad = false;
+      for (int it = blockIdx.x; it < items && !bad; it += gridDim.x, ++j) {
+        const TcItem w = ItemOf(a, it, tok_tiles, nk_all);
+        const uint32_t ab = j & 1u, use = j >> 1;
+        if (use >= 1 && !dev::MbarWait(acce + ab, (use - 1u) & 1u)) {  // the epilogue has read this accumulator
+          atomicOr(a.err, 16u);
+          break;
+        }
+        FenceAfterSync();
+        const uint32_t tacc = tmem + ab * 128u;
+        for (int kb = 0; kb < w.nk; ++kb, ++q) {
+          const int s = static_cast<int>(q % kStages);
+          if (!dev::MbarWait(full + s, (q / kStages) & 1u)) {
+            atomicOr(a.err, 16u);
+            bad = true;
+            break;
+          }
+          FenceAfterSync();
+          const uint8_t* st = smem + s * kStageBytes;
+          const uint64_t dWh = DescSw128(st), dWl = DescSw128(st + kTileBytes);
+          const uint64_t dXh = DescSw128(st + 2 * kTileBytes), dXl = DescSw128(st + 3 * kTileBytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t adv = static_cast<uint64_t>(kk * 32 >> 4);  // 16 fp16 = 32 bytes along K
+            Mma(tacc, dWh + adv, dXh + adv, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            Mma(tacc, dWh + adv, dXl + adv, idesc, 1u);
+            Mma(tacc, dWl + adv, dXh + adv, idesc, 1u);
+          }
+          MmaCommit(empty + s);  // the stage is free once these MMAs have read it
+        }
+        if (bad) break;
+        MmaCommit(accf + ab);  // the accumulator is complete once every issued MMA is
+      }
     }
-  } else if (tid == 32) {
-    // ---- MMA issuer
-    constexpr uint32_t idesc = InstrDesc(kBM, kBN);
-    for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % kStages;
-      if (!dev::MbarWait(full + s, static_cast<uint32_t>((kb / kStages) & 1))) {
-        atomicOr(a.err, 16u);
+  } else {
+    // ---- epilogue: warp w reads TMEM lanes (weight rows) 32 (w % 4) .. + 31
+    const int quarter = warp & 3;
+    uint32_t j = 0;
+    for (int it = blockIdx.x; it < items; it += gridDim.x, ++j) {
+      const TcItem w = ItemOf(a, it, tok_tiles, nk_all);
+      const uint32_t ab = j & 1u, use = j >> 1;
+      if (!dev::MbarWait(accf + ab, use & 1u)) {
+        if (lane == 0) atomicOr(a.err, 32u);
         break;
       }
       FenceAfterSync();
-      const uint8_t* st = smem + s * kStageBytes;
-      const uint64_t dWh = DescSw128(st), dWl = DescSw128(st + kTileBytes);
-      const uint64_t dXh = DescSw128(st + 2 * kTileBytes), dXl = DescSw128(st + 3 * kTileBytes);
+      const int r = w.row0 + 32 * quarter + lane;
+      for (int c0 = 0; c0 < kBN; c0 += 16) {
+        uint32_t v[16];
+        TmemLoad16(tmem + ab * 128u + (static_cast<uint32_t>(32 * quarter) << 16) + static_cast<uint32_t>(c0), v);
 #pragma unroll
-      for (int kk = 0; kk < kBK / 16; ++kk) {
-        const uint64_t adv = static_cast<uint64_t>(kk * 32 >> 4);  // 16 fp16 = 32 bytes along K
-        Mma(tmem, dWh + adv, dXh + adv, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
-        Mma(tmem, dWh + adv, dXl + adv, idesc, 1u);
-        Mma(tmem, dWl + adv, dXh + adv, idesc, 1u);
-      }
-      MmaCommit(empty + s);  // the stage is free once these MMAs have read it
-    }
-    MmaCommit(&accf);  // the accumulator is complete once every issued MMA is
-  }
-  __syncwarp();
-
-  // ---- epilogue: warp w owns TMEM lanes (weight rows) 32 w .. 32 w + 31
-  const bool ok = dev::MbarWait(&accf, 0u);
-  if (!ok && lane == 0) atomicOr(a.err, 32u);
-  FenceAfterSync();
-  const int r = row0 + 32 * warp + lane;
-  if (ok) {
-    for (int c0 = 0; c0 < kBN; c0 += 16) {
-      uint32_t v[16];
-      TmemLoad16(tmem + (static_cast<uint32_t>(32 * warp) << 16) + static_cast<uint32_t>(c0), v);
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int t = tok0 + c0 + j;
-        const float acc = __uint_as_float(v[j]);
-        if (gridDim.z > 1) {
-          if (t < a.n_tok) a.part[(static_cast<int64_t>(blockIdx.z) * a.n_tok + t) * a.rows + r] = acc;
-        } else if (EPI == static_cast<int>(Epi::kSilu)) {
-          // rows 2i (gate) and 2i+1 (up) sit in neighbouring lanes
-          const float u = __shfl_xor_sync(0xFFFFFFFFu, acc, 1);
-          if (t < a.n_tok && (lane & 1) == 0) {
-            a.out[static_cast<int64_t>(t) * a.ldo + (r >> 1)] = (acc / (1.0f + expf(-acc))) * u;
-          }
-        } else if (t < a.n_tok) {
-          if (EPI == static_cast<int>(Epi::kResid)) {
-            float* o = a.out + static_cast<int64_t>(t) * a.ldo + r;
-            *o = a.resid[static_cast<int64_t>(t) * a.ldr + r] + acc;
-          } else {
-            a.out[static_cast<int64_t>(t) * a.ldo + a.out_off + r] = acc;
+        for (int jj = 0; jj < 16; ++jj) {
+          const int t = w.tok0 + c0 + jj;
+          const float acc = __uint_as_float(v[jj]);
+          if (a.splits > 1) {
+            if (t < a.n_tok) a.part[(static_cast<int64_t>(w.z) * a.n_tok + t) * a.rows + r] = acc;
+          } else if (EPI == static_cast<int>(Epi::kSilu)) {
+            // rows 2i (gate) and 2i+1 (up) sit in neighbouring lanes
+            const float u = __shfl_xor_sync(0xFFFFFFFFu, acc, 1);
+            if (t < a.n_tok && (lane & 1) == 0) {
+              a.out[static_cast<int64_t>(t) * a.ldo + (r >> 1)] = (acc / (1.0f + expf(-acc))) * u;
+            }
+          } else if (t < a.n_tok) {
+            if (EPI == static_cast<int>(Epi::kResid)) {
+              float* o = a.out + static_cast<int64_t>(t) * a.ldo + r;
+              *o = a.resid[static_cast<int64_t>(t) * a.ldr + r] + acc;
+            } else {
+              a.out[static_cast<int64_t>(t) * a.ldo + a.out_off + r] = acc;
+            }
           }
         }
       }
+      FenceBeforeSync();
+      MbarArrive(acce + ab);  // this accumulator may be overwritten
     }
   }
   FenceBeforeSync();
   __syncthreads();
   if (warp == 0) {
     FenceAfterSync();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(128u) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256u) : "memory");
   }
 }
 
@@ -363,6 +423,14 @@ __global__ void __launch_bounds__(256) SplitReduceKernel(const TcArgs a, int spl
 }
 
 // ------------------------------------------------------------------ host side
+
+// SMs of the current device (one persistent GEMM block per SM).
+int DeviceSms() {
+  int dev = 0, n = 0;
+  RPGB_CUDA(cudaGetDevice(&dev));
+  RPGB_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+  return n;
+}
 
 PFN_cuTensorMapEncodeTiled_v12000 EncodeFn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -480,9 +548,12 @@ void LaunchTcGemm(const GemmParams& p, Epi epi, __half* scratch, size_t scratch_
   a.err = p.err;
   a.part = p.part;
   a.rows = w.rows;
-  const int splits = TcGemmSplits(w.rows, p.n_tok, K, p.num_sms, p.part_floats);
-  const dim3 grid((p.n_tok + kBN - 1) / kBN, w.rows / kBM, splits);
-  RPGB_CHECK(grid.y < 65536, "tcgen05 gemm: too many rows");
+  const int num_sms = p.num_sms > 0 ? p.num_sms : DeviceSms();
+  const int splits = TcGemmSplits(w.rows, p.n_tok, K, num_sms, p.part_floats);
+  a.splits = splits;
+  const int64_t items = static_cast<int64_t>((p.n_tok + kBN - 1) / kBN) * (w.rows / kBM) * splits;
+  RPGB_CHECK(items < (static_cast<int64_t>(1) << 30), "tcgen05 gemm: too many tiles");
+  const int grid = static_cast<int>(std::min<int64_t>(items, num_sms));
   PickTc(epi)<<<grid, kThreads, kSmemBytes, s>>>(mWh, mWl, mXh, mXl, a);
   RPGB_CUDA(cudaGetLastError());
   CountLaunches(2);
