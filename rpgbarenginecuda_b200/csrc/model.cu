@@ -2,6 +2,7 @@
 #include "model.h"
 
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <functional>
 #include <thread>
@@ -550,7 +551,10 @@ std::unique_ptr<Model> Model::Load(const std::string& path, int device, int32_t 
     }
     size_t free_b = 0, total_b = 0;
     RPGB_CUDA(cudaMemGetInfo(&free_b, &total_b));
-    if (halves > 0 && free_b > halves * 4 + (static_cast<size_t>(4) << 30) &&
+    // RPGB_PREFILL_COPIES=0: keep no copies (a host that needs the memory)
+    const char* env = std::getenv("RPGB_PREFILL_COPIES");
+    const bool want = env == nullptr || std::atoi(env) != 0;
+    if (want && halves > 0 && free_b > halves * 4 + (static_cast<size_t>(4) << 30) &&
         cudaMalloc(&m->half_arena_, halves * 4) == cudaSuccess) {
       m->half_bytes_ = static_cast<int64_t>(halves * 4);
       __half* h = m->half_arena_;
