@@ -1,19 +1,18 @@
-// k_flash.cu -- prefill attention on the tensor cores (flash-attention style).
+// k_flash.cu -- prefill attention on the 5th-generation tensor cores
+// (tcgen05, flash-attention style).
 //
 // Replaces AttentionFromCacheKernel for prompts (src/kernels_gpu.cu:737-823,
 // GpuAttentionFromCache at 1038-1087): causal GQA over the fp16 KV cache,
 // scale 1/sqrt(128), softmax with max subtraction, output = P V / sum P.
 //
-// One block of 8 warps per (tile of 128 / G query tokens, KV head h): its
-// 128 rows are the (token, q head) pairs of the G q heads sharing h, so every
-// K/V tile is read once per query tile instead of once per token.  K and V
-// tiles of 64 positions arrive by 3-D TMA (128-byte swizzle) in two stages;
-// each warp owns 16 rows and computes
-//   S = Q K^T   and   O += P V
-// with mma.sync m16n8k16 (fp16 in, fp32 accumulate), keeping S, the online
-// softmax state and O in registers.  K and V are fp16 already (exact); Q and
-// P are split into two fp16 terms (hi + lo), so scores and outputs keep about
-// 22 significant bits (the reference computes them in FP32).
+// One block per (tile of 128 / G query tokens, KV head h): its 128 rows are
+// the (q head, token) pairs of the G q heads sharing h, so every K/V tile is
+// read once per query tile instead of once per token; the rows are the 128
+// TMEM lanes of the score tile S = Q K^T and of the output accumulator
+// O += P V, both tcgen05 MMAs with operands in shared memory.  K and V are
+// fp16 already (exact); Q and P are split into two fp16 terms (hi + lo), so
+// scores and outputs keep about 22 significant bits (the reference computes
+// them in FP32).  FlashTcKernel below has the pipeline.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -23,17 +22,15 @@
 #include "common.h"
 #include "kernels.cuh"
 #include "kernels.h"
+#include "tc_dev.cuh"
 
 namespace rpgb {
 namespace {
 
 constexpr int kD = 128;
 constexpr int kKT = 64;        // key positions per stage
-constexpr int kWarps = 8;
-constexpr int kRows = 16 * kWarps;  // (token, q head) rows per block
+constexpr int kRows = 128;  // (q head, token) rows per block
 constexpr uint32_t kHalfTile = kKT * 64 * 2;  // 64 positions x 64 dims fp16 = 8 KB (one swizzled box)
-constexpr uint32_t kStageBytes = 4 * kHalfTile;  // K dims 0-63, K dims 64-127, V dims 0-63, V dims 64-127
-constexpr size_t kSmem = 2 * kStageBytes + 1024;
 
 struct FlashArgs {
   const float* q;  // [n][q_stride], normalised and rotated
@@ -61,24 +58,6 @@ __device__ __forceinline__ void SplitPair(float a, float b, uint32_t& hi, uint32
   lo = PackHalf2(a - hf.x, b - hf.y);
 }
 
-__device__ __forceinline__ void MmaF16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ void LdMatrixX4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ void LdMatrixX4T(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-
 __device__ __forceinline__ void TmaLoad3D(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
@@ -87,34 +66,55 @@ __device__ __forceinline__ void TmaLoad3D(void* dst, const CUtensorMap* map, int
       : "memory");
 }
 
-// Address of the 16-byte chunk `chunk` (0..15 over the 128 dims) of position
-// `row` (0..63) in a stage half written by TMA with the 128-byte swizzle.
-__device__ __forceinline__ uint32_t SwzAddr(uint32_t half_base, int row, int chunk) {
-  const int sub = chunk >> 3, c = chunk & 7;
-  return half_base + static_cast<uint32_t>(sub) * kHalfTile + static_cast<uint32_t>(row * 128 + ((c ^ (row & 7)) << 4));
+// ------------------------------------------------------------------ tcgen05 version
+//
+// The same computation with the two products on the 5th-generation tensor
+// cores and the tiles in TMEM.  One block of 6 warps per (128 / G query
+// tokens, KV head); its 128 rows are (q head g, token) pairs, head-major
+// (row r = g * 128 / G + token), and they are the 128 TMEM lanes:
+//  * warp 4 streams K and V tiles of 64 positions (3-D TMA, 128-byte
+//    swizzle, two stages);
+//  * warp 5 issues S = Q K^T (M 128, N 64: Qh K + Ql K, 16 MMAs) into one of
+//    two 64-column TMEM tiles, one tile ahead of the softmax, then
+//    O += P V (M 128, N 128: Ph Vt + Pl Vt, 8 MMAs) into a 128-column TMEM
+//    accumulator;
+//  * warps 0-3 (thread = row) read their S row, apply the causal mask and
+//    the online softmax in log2 units, rescale their O row in TMEM when the
+//    row maximum grew, write P = Ph + Pl (fp16 terms) into a K-major
+//    swizzled tile, and transpose V into a K-major tile Vt (thread = dim),
+//    which the MMA needs as its B operand.
+// Q (times scale * log2 e) is split into Qh + Ql fp16 terms once per block.
+// Every mbarrier wait is bounded; a wait that gives up sets *err (64).
+constexpr int kTcWarps = 6;
+constexpr uint32_t kQBox = 128 * 128;          // 128 rows x 64 dims fp16 (one swizzled box)
+constexpr uint32_t kTcQ = 2 * kQBox;            // 128 rows x 128 dims
+constexpr uint32_t kTcStage = 4 * kHalfTile;    // K dims 0-63, K dims 64-127, V dims 0-63, V dims 64-127
+constexpr uint32_t kTcTile = 128 * 128;         // 128 rows x 64 keys fp16 (P, Vt)
+constexpr size_t kTcSmem = 2 * kTcQ + 2 * kTcStage + 3 * kTcTile + 1024;
+
+__device__ __forceinline__ uint32_t Swz(int row, int chunk) {
+  return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
 template <int G>
-__global__ void __launch_bounds__(kWarps * 32, 1)
-    FlashPrefillKernel(const __grid_constant__ CUtensorMap mK, const __grid_constant__ CUtensorMap mV,
-                       const FlashArgs a) {
-  constexpr int kTQ = kRows / G;           // query tokens per block
-  constexpr int kWarpsPerHead = kWarps / G;  // warps per q head (16 tokens each)
+__global__ void __launch_bounds__(kTcWarps * 32, 1)
+    FlashTcKernel(const __grid_constant__ CUtensorMap mK, const __grid_constant__ CUtensorMap mV, const FlashArgs a) {
+  using namespace tc;
+  constexpr int kTQ = kRows / G;  // query tokens per block
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t full[2];
+  __shared__ __align__(8) uint64_t kv_full[2], kv_empty[2], s_full[2], s_free[2], p_full, o_done, fin;
+  __shared__ uint32_t s_tmem;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQh = smem;
+  uint8_t* sQl = sQh + kTcQ;
+  uint8_t* sKV = sQl + kTcQ;
+  uint8_t* sVt = sKV + 2 * kTcStage;
+  uint8_t* sPh = sVt + kTcTile;
+  uint8_t* sPl = sPh + kTcTile;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g4 = lane >> 2, t4 = lane & 3;
   const int h = blockIdx.y;
-  // the last query tiles see the most keys (causal): they are launched first,
-  // so the short tiles fill the final wave
+  // the last query tiles see the most keys (causal): they are launched first
   const int tok0 = (gridDim.x - 1 - blockIdx.x) * kTQ;
-  const int gq = warp / kWarpsPerHead;                // q head within the group
-  const int wt0 = tok0 + (warp % kWarpsPerHead) * 16;  // first token of this warp's rows
-  const int qh = h * G + gq;
-
-  // keys 0 .. pos0 + last token of the block, in 64-key tiles; split z of
-  // gridDim.z takes tiles [t_lo, t_lo + nsteps)
   const int64_t last_tok = (tok0 + kTQ < a.n ? tok0 + kTQ : a.n) - 1;
   const int64_t kend = a.pos0 + last_tok + 1;
   const int tiles = static_cast<int>((kend + kKT - 1) / kKT);
@@ -122,193 +122,270 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   const int t_lo = static_cast<int>(static_cast<int64_t>(z) * tiles / n_split);
   const int nsteps = static_cast<int>(static_cast<int64_t>(z + 1) * tiles / n_split) - t_lo;
 
+  if (warp == 0) TmemAlloc(&s_tmem, 256u);  // O: columns 0-127, S tiles: 128-191, 192-255
   if (tid == 0) {
-    dev::MbarInit(full + 0, 1);
-    dev::MbarInit(full + 1, 1);
+    for (int b = 0; b < 2; ++b) {
+      dev::MbarInit(kv_full + b, 1);
+      dev::MbarInit(kv_empty + b, 1);
+      dev::MbarInit(s_full + b, 1);
+      dev::MbarInit(s_free + b, 128);
+    }
+    dev::MbarInit(&p_full, 128);
+    dev::MbarInit(&o_done, 1);
+    dev::MbarInit(&fin, 1);
     dev::MbarInitFence();
-    for (int st = 0; st < 2 && st < nsteps; ++st) {
-      uint8_t* b = smem + st * kStageBytes;
-      const int y = (t_lo + st) * kKT;
-      dev::MbarExpectTx(full + st, kStageBytes);
-      TmaLoad3D(b, &mK, 0, y, h, full + st);
-      TmaLoad3D(b + kHalfTile, &mK, 64, y, h, full + st);
-      TmaLoad3D(b + 2 * kHalfTile, &mV, 0, y, h, full + st);
-      TmaLoad3D(b + 3 * kHalfTile, &mV, 64, y, h, full + st);
-    }
   }
-
-  // ---- Q fragments (A operand): rows g4 and g4 + 8 of this warp, hi and lo
-  uint32_t qa_hi[8][4], qa_lo[8][4];
-  {
-    const int ta = wt0 + g4, tb = wt0 + g4 + 8;
-    const float* qa = a.q + static_cast<int64_t>(ta < a.n ? ta : 0) * a.q_stride + qh * kD;
-    const float* qb = a.q + static_cast<int64_t>(tb < a.n ? tb : 0) * a.q_stride + qh * kD;
+  // ---- Q rows (warps 0-3, thread = row): q * scale * log2 e as fp16 hi + lo, swizzled
+  const int row = tid;
+  const int g = row / kTQ, tl = row - g * kTQ;
+  const int qh = h * G + g;
+  const int64_t qpos = a.pos0 + tok0 + tl;
+  if (warp < 4) {
+    const bool valid = tok0 + tl < a.n;
+    const float* q = a.q + static_cast<int64_t>(valid ? tok0 + tl : 0) * a.q_stride + qh * kD;
+    const float qs = a.scale * 1.4426950408889634f;
+#pragma unroll 4
+    for (int c = 0; c < 16; ++c) {  // 8 dims per chunk
+      const float4 x0 = *reinterpret_cast<const float4*>(q + 8 * c);
+      const float4 x1 = *reinterpret_cast<const float4*>(q + 8 * c + 4);
+      const float v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+      uint32_t hi[4], lo[4];
 #pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      const float2 x0 = *reinterpret_cast<const float2*>(qa + 16 * ks + 2 * t4);
-      const float2 x1 = *reinterpret_cast<const float2*>(qb + 16 * ks + 2 * t4);
-      const float2 x2 = *reinterpret_cast<const float2*>(qa + 16 * ks + 8 + 2 * t4);
-      const float2 x3 = *reinterpret_cast<const float2*>(qb + 16 * ks + 8 + 2 * t4);
-      SplitPair(x0.x * a.scale, x0.y * a.scale, qa_hi[ks][0], qa_lo[ks][0]);
-      SplitPair(x1.x * a.scale, x1.y * a.scale, qa_hi[ks][1], qa_lo[ks][1]);
-      SplitPair(x2.x * a.scale, x2.y * a.scale, qa_hi[ks][2], qa_lo[ks][2]);
-      SplitPair(x3.x * a.scale, x3.y * a.scale, qa_hi[ks][3], qa_lo[ks][3]);
+      for (int i = 0; i < 4; ++i) {
+        const float u0 = valid ? v[2 * i] * qs : 0.f, u1 = valid ? v[2 * i + 1] * qs : 0.f;
+        SplitPair(u0, u1, hi[i], lo[i]);
+      }
+      const uint32_t off = (c >> 3) * kQBox + Swz(row, c & 7);
+      *reinterpret_cast<uint4*>(sQh + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      *reinterpret_cast<uint4*>(sQl + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
     }
+    dev::FenceProxyAsync();  // generic-proxy writes, read by the MMAs (async proxy)
   }
-  const int64_t pa = a.pos0 + wt0 + g4, pb = pa + 8;  // positions of the thread's two rows
-
-  float o[16][4];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  FenceBeforeSync();
   __syncthreads();
+  FenceAfterSync();
+  const uint32_t tmem = s_tmem;
 
-  bool failed = false;
-  for (int st = 0; st < nsteps; ++st) {
-    const int stage = st & 1;
-    const bool ok = dev::MbarWait(full + stage, static_cast<uint32_t>((st >> 1) & 1));
-    if (!ok) {
-      failed = true;
-      if (tid == 0) atomicOr(a.err, 64u);
+  if (warp == 4) {
+    if (lane == 0) {
+      // ---- producer: K and V tiles t_lo .. t_lo + nsteps - 1
+      int issued = 0;
+      for (int i = 0; i < nsteps; ++i) {
+        const int b = i & 1;
+        if (i >= 2 && !dev::MbarWait(kv_empty + b, static_cast<uint32_t>(((i >> 1) - 1) & 1))) {
+          atomicOr(a.err, 64u);
+          break;
+        }
+        uint8_t* st = sKV + b * kTcStage;
+        const int y = (t_lo + i) * kKT;
+        dev::MbarExpectTx(kv_full + b, kTcStage);
+        TmaLoad3D(st, &mK, 0, y, h, kv_full + b);
+        TmaLoad3D(st + kHalfTile, &mK, 64, y, h, kv_full + b);
+        TmaLoad3D(st + 2 * kHalfTile, &mV, 0, y, h, kv_full + b);
+        TmaLoad3D(st + 3 * kHalfTile, &mV, 64, y, h, kv_full + b);
+        issued = i + 1;
+      }
+      for (int i = issued - 2 > 0 ? issued - 2 : 0; i < issued; ++i) {  // copies land before exit
+        dev::MbarWait(kv_full + (i & 1), static_cast<uint32_t>((i >> 1) & 1));
+      }
     }
-    const uint32_t kb = dev::SmemAddr(smem + stage * kStageBytes);
-    const uint32_t vb = kb + 2 * kHalfTile;
-    const int64_t key0 = static_cast<int64_t>(t_lo + st) * kKT;
-    // this warp's rows see no key of this stage: skip the math (stays in step for the barrier)
-    const bool any = key0 <= a.pos0 + wt0 + 15;
-    if (any) {
-      // ---- S = Q K^T for 64 keys: 8 n-tiles of 8 keys
-      float s[8][4];
+  } else if (warp == 5) {
+    if (lane == 0) {
+      // ---- MMA issuer
+      constexpr uint32_t id_s = InstrDesc(128, kKT), id_o = InstrDesc(128, kD);
+      const uint64_t dQh = DescSw128(sQh), dQl = DescSw128(sQl);
+      const uint64_t dPh = DescSw128(sPh), dPl = DescSw128(sPl), dVt = DescSw128(sVt);
+      bool bad = false;
+      auto issue_s = [&](int j) {
+        const int b = j & 1;
+        if (!dev::MbarWait(kv_full + b, static_cast<uint32_t>((j >> 1) & 1)) ||
+            (j >= 2 && !dev::MbarWait(s_free + b, static_cast<uint32_t>(((j >> 1) - 1) & 1)))) {
+          atomicOr(a.err, 64u);
+          bad = true;
+          return;
+        }
+        FenceAfterSync();
+        const uint8_t* st = sKV + b * kTcStage;
+        const uint32_t ts = tmem + 128u + static_cast<uint32_t>(b) * kKT;
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          const uint64_t adv = static_cast<uint64_t>((kk & 3) * 2);  // 16 fp16 = 32 bytes along K
+          const uint64_t dK = DescSw128(st + (kk >> 2) * kHalfTile) + adv;
+          Mma(ts, dQh + (kk >> 2) * (kQBox >> 4) + adv, dK, id_s, kk > 0 ? 1u : 0u);
+          Mma(ts, dQl + (kk >> 2) * (kQBox >> 4) + adv, dK, id_s, 1u);
+        }
+        MmaCommit(s_full + b);
+      };
+      if (nsteps > 0) issue_s(0);
+      for (int j = 0; j < nsteps && !bad; ++j) {
+        if (j + 1 < nsteps) {
+          issue_s(j + 1);
+          if (bad) break;
+        }
+        if (!dev::MbarWait(&p_full, static_cast<uint32_t>(j & 1))) {
+          atomicOr(a.err, 64u);
+          break;
+        }
+        FenceAfterSync();
 #pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
+        for (int kk = 0; kk < kKT / 16; ++kk) {
+          const uint64_t adv = static_cast<uint64_t>(kk * 2);
+          Mma(tmem, dPh + adv, dVt + adv, id_o, (j > 0 || kk > 0) ? 1u : 0u);
+          Mma(tmem, dPl + adv, dVt + adv, id_o, 1u);
+        }
+        MmaCommit(&o_done);
+        MmaCommit(kv_empty + (j & 1));
+      }
+      // every MMA issued by this thread has completed before the block may exit
+      MmaCommit(&fin);
+      dev::MbarWait(&fin, 0u);
+    }
+  } else {
+    // ---- softmax, P, Vt and the output (warps 0-3, thread = row)
+    const uint32_t lrow = static_cast<uint32_t>(32 * warp) << 16;  // this warp's TMEM lanes
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nsteps; ++j) {
+      const int b = j & 1;
+      // every wait's outcome is made warp-uniform: the TMEM loads and stores
+      // below are warp-collective
+      if (!__all_sync(0xFFFFFFFFu, dev::MbarWait(s_full + b, static_cast<uint32_t>((j >> 1) & 1)))) {
+        ok = false;
+        break;
+      }
+      FenceAfterSync();
+      float p[kKT];
 #pragma unroll
-        for (int np = 0; np < 4; ++np) {
-          // matrices: keys 16np + {0..7, 0..7, 8..15, 8..15}, dims 16ks + {0..7, 8..15, 0..7, 8..15}
-          const int mi = lane >> 3, row = 16 * np + ((mi >> 1) << 3) + (lane & 7);
-          uint32_t b0, b1, b2, b3;
-          LdMatrixX4(SwzAddr(kb, row, 2 * ks + (mi & 1)), b0, b1, b2, b3);
-          MmaF16(s[2 * np], qa_hi[ks], b0, b1);
-          MmaF16(s[2 * np], qa_lo[ks], b0, b1);
-          MmaF16(s[2 * np + 1], qa_hi[ks], b2, b3);
-          MmaF16(s[2 * np + 1], qa_lo[ks], b2, b3);
+      for (int c0 = 0; c0 < kKT; c0 += 16) {
+        uint32_t v[16];
+        TmemLoad16(tmem + lrow + 128u + static_cast<uint32_t>(b * kKT + c0), v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) p[c0 + i] = __uint_as_float(v[i]);
+      }
+      FenceBeforeSync();
+      MbarArrive(s_free + b);
+      // causal mask, row maximum, probabilities in log2 units
+      const int64_t key0 = static_cast<int64_t>(t_lo + j) * kKT;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kKT; ++c) {
+        if (key0 + c > qpos) p[c] = -INFINITY;
+        mx = fmaxf(mx, p[c]);
+      }
+      const float m_new = fmaxf(m_run, mx);
+      const float alpha = m_run == -INFINITY ? 0.f : exp2f(m_run - m_new);
+      float ps = 0.f;
+#pragma unroll
+      for (int c = 0; c < kKT; ++c) {
+        p[c] = p[c] == -INFINITY ? 0.f : exp2f(p[c] - m_new);
+        ps += p[c];
+      }
+      l_run = l_run * alpha + ps;
+      m_run = m_new;
+      // O, P and Vt are free once the previous tile's P V has completed
+      if (j > 0) {
+        if (!__all_sync(0xFFFFFFFFu, dev::MbarWait(&o_done, static_cast<uint32_t>((j - 1) & 1)))) {
+          ok = false;
+          break;
+        }
+        FenceAfterSync();
+        if (__any_sync(0xFFFFFFFFu, alpha != 1.f)) {
+#pragma unroll 2
+          for (int c0 = 0; c0 < kD; c0 += 16) {
+            uint32_t v[16];
+            TmemLoad16(tmem + lrow + static_cast<uint32_t>(c0), v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+            TmemStore16(tmem + lrow + static_cast<uint32_t>(c0), v);
+          }
+          TmemStoreWait();
         }
       }
-      // ---- causal mask and online softmax (rows g4: s[.][0..1], g4 + 8: s[.][2..3])
-      float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        const int64_t k = key0 + 8 * nt + 2 * t4;
-        if (k > pa) s[nt][0] = -INFINITY;
-        if (k + 1 > pa) s[nt][1] = -INFINITY;
-        if (k > pb) s[nt][2] = -INFINITY;
-        if (k + 1 > pb) s[nt][3] = -INFINITY;
-        mx0 = fmaxf(mx0, fmaxf(s[nt][0], s[nt][1]));
-        mx1 = fmaxf(mx1, fmaxf(s[nt][2], s[nt][3]));
+      for (int c = 0; c < kKT / 8; ++c) {
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) SplitPair(p[8 * c + 2 * i], p[8 * c + 2 * i + 1], hi[i], lo[i]);
+        *reinterpret_cast<uint4*>(sPh + Swz(row, c)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4*>(sPl + Swz(row, c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
       }
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xFFFFFFFFu, mx0, 1));
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xFFFFFFFFu, mx0, 2));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xFFFFFFFFu, mx1, 1));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xFFFFFFFFu, mx1, 2));
-      const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
-      const float al0 = m0 == -INFINITY ? 0.f : expf(m0 - n0);
-      const float al1 = m1 == -INFINITY ? 0.f : expf(m1 - n1);
-      m0 = n0;
-      m1 = n1;
-      float ps0 = 0.f, ps1 = 0.f;
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        s[nt][0] = s[nt][0] == -INFINITY ? 0.f : expf(s[nt][0] - n0);
-        s[nt][1] = s[nt][1] == -INFINITY ? 0.f : expf(s[nt][1] - n0);
-        s[nt][2] = s[nt][2] == -INFINITY ? 0.f : expf(s[nt][2] - n1);
-        s[nt][3] = s[nt][3] == -INFINITY ? 0.f : expf(s[nt][3] - n1);
-        ps0 += s[nt][0] + s[nt][1];
-        ps1 += s[nt][2] + s[nt][3];
+      // V^T (thread = dim d): the K-major B operand of P V
+      if (!__all_sync(0xFFFFFFFFu, dev::MbarWait(kv_full + b, static_cast<uint32_t>((j >> 1) & 1)))) {
+        ok = false;
+        break;
       }
-      l0 = l0 * al0 + ps0;
-      l1 = l1 * al1 + ps1;
+      {
+        const int d = row, box = d >> 6, col = d & 63, cc = col >> 3;
+        const uint8_t* vb = sKV + b * kTcStage + 2 * kHalfTile + box * kHalfTile + (col & 7) * 2;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        o[i][0] *= al0;
-        o[i][1] *= al0;
-        o[i][2] *= al1;
-        o[i][3] *= al1;
+        for (int c = 0; c < kKT / 8; ++c) {
+          uint32_t w[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int k0 = 8 * c + 2 * i;
+            const uint32_t lo16 = *reinterpret_cast<const uint16_t*>(vb + Swz(k0, cc));
+            const uint32_t hi16 = *reinterpret_cast<const uint16_t*>(vb + Swz(k0 + 1, cc));
+            w[i] = lo16 | (hi16 << 16);
+          }
+          *reinterpret_cast<uint4*>(sVt + Swz(d, c)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
       }
-      // ---- O += P V: P (A operand, keys 16 kk .. +15) from the S tiles 2 kk, 2 kk + 1
+      dev::FenceProxyAsync();  // P and Vt (generic writes) are read by the MMAs
+      FenceBeforeSync();
+      MbarArrive(&p_full);
+    }
+    if (!ok && lane == 0) atomicOr(a.err, 64u);
+    if (ok && nsteps > 0 &&
+        !__all_sync(0xFFFFFFFFu, dev::MbarWait(&o_done, static_cast<uint32_t>((nsteps - 1) & 1)))) {
+      ok = false;
+      if (lane == 0) atomicOr(a.err, 64u);
+    }
+    FenceAfterSync();
+    // ---- O / l (or the unnormalised partial of this key split)
+    const int t = tok0 + tl;
+    const int q_dim = a.n_heads * kD;
+    const bool store = ok && t < a.n && nsteps > 0;  // (every split holds at least two key tiles)
+    if (n_split > 1) {
+      float* po = a.part_o + (static_cast<int64_t>(z) * a.n + t) * q_dim + qh * kD;
+      if (store) {
+        float* pml = a.part_ml + ((static_cast<int64_t>(z) * a.n + t) * a.n_heads + qh) * 2;
+        *reinterpret_cast<float2*>(pml) = make_float2(m_run * 0.6931471805599453f, l_run);
+      }
+#pragma unroll 2
+      for (int c0 = 0; c0 < kD; c0 += 16) {
+        uint32_t v[16];
+        TmemLoad16(tmem + lrow + static_cast<uint32_t>(c0), v);
+        if (store) {
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        uint32_t ph[4], pl[4];
-        SplitPair(s[2 * kk][0], s[2 * kk][1], ph[0], pl[0]);
-        SplitPair(s[2 * kk][2], s[2 * kk][3], ph[1], pl[1]);
-        SplitPair(s[2 * kk + 1][0], s[2 * kk + 1][1], ph[2], pl[2]);
-        SplitPair(s[2 * kk + 1][2], s[2 * kk + 1][3], ph[3], pl[3]);
+          for (int i = 0; i < 16; i += 4) {
+            *reinterpret_cast<float4*>(po + c0 + i) = make_float4(
+                __uint_as_float(v[i]), __uint_as_float(v[i + 1]), __uint_as_float(v[i + 2]), __uint_as_float(v[i + 3]));
+          }
+        }
+      }
+    } else {
+      float* out = a.out + static_cast<int64_t>(t) * q_dim + qh * kD;
+      const float inv = 1.0f / l_run;
+#pragma unroll 2
+      for (int c0 = 0; c0 < kD; c0 += 16) {
+        uint32_t v[16];
+        TmemLoad16(tmem + lrow + static_cast<uint32_t>(c0), v);
+        if (store) {
 #pragma unroll
-        for (int dp = 0; dp < 8; ++dp) {
-          // matrices (transposed): keys 16kk + {0..7, 8..15, 0..7, 8..15}, dims 16dp + {0..7, 0..7, 8..15, 8..15}
-          const int mi = lane >> 3, row = 16 * kk + ((mi & 1) << 3) + (lane & 7);
-          uint32_t b0, b1, b2, b3;
-          LdMatrixX4T(SwzAddr(vb, row, 2 * dp + (mi >> 1)), b0, b1, b2, b3);
-          MmaF16(o[2 * dp], ph, b0, b1);
-          MmaF16(o[2 * dp], pl, b0, b1);
-          MmaF16(o[2 * dp + 1], ph, b2, b3);
-          MmaF16(o[2 * dp + 1], pl, b2, b3);
+          for (int i = 0; i < 16; i += 4) {
+            *reinterpret_cast<float4*>(out + c0 + i) =
+                make_float4(__uint_as_float(v[i]) * inv, __uint_as_float(v[i + 1]) * inv,
+                            __uint_as_float(v[i + 2]) * inv, __uint_as_float(v[i + 3]) * inv);
+          }
         }
       }
     }
-    __syncthreads();  // every warp is done with this stage
-    if (tid == 0 && st + 2 < nsteps) {
-      dev::FenceProxyAsync();
-      uint8_t* b = smem + stage * kStageBytes;
-      const int y = (t_lo + st + 2) * kKT;
-      dev::MbarExpectTx(full + stage, kStageBytes);
-      TmaLoad3D(b, &mK, 0, y, h, full + stage);
-      TmaLoad3D(b + kHalfTile, &mK, 64, y, h, full + stage);
-      TmaLoad3D(b + 2 * kHalfTile, &mV, 0, y, h, full + stage);
-      TmaLoad3D(b + 3 * kHalfTile, &mV, 64, y, h, full + stage);
-    }
   }
-
-  if (failed && tid == 0) {  // copies that may still be landing in this block's shared memory
-    for (int st = nsteps - 2 > 0 ? nsteps - 2 : 0; st < nsteps; ++st) {
-      dev::MbarWait(full + (st & 1), static_cast<uint32_t>((st >> 1) & 1));
-    }
-  }
-
-  // ---- O / l for the thread's rows
-  l0 += __shfl_xor_sync(0xFFFFFFFFu, l0, 1);
-  l0 += __shfl_xor_sync(0xFFFFFFFFu, l0, 2);
-  l1 += __shfl_xor_sync(0xFFFFFFFFu, l1, 1);
-  l1 += __shfl_xor_sync(0xFFFFFFFFu, l1, 2);
-  const int ta = wt0 + g4, tb = ta + 8;
-  const int q_dim = a.n_heads * kD;
-  if (n_split > 1) {  // unnormalised partials; FlashMergeKernel combines the splits
-    float* po = a.part_o + static_cast<int64_t>(z) * a.n * q_dim + qh * kD;
-    float* pml = a.part_ml + (static_cast<int64_t>(z) * a.n * a.n_heads + qh) * 2;
-#pragma unroll
-    for (int dt = 0; dt < 16; ++dt) {
-      const int d = 8 * dt + 2 * t4;
-      if (ta < a.n) *reinterpret_cast<float2*>(po + static_cast<int64_t>(ta) * q_dim + d) = make_float2(o[dt][0], o[dt][1]);
-      if (tb < a.n) *reinterpret_cast<float2*>(po + static_cast<int64_t>(tb) * q_dim + d) = make_float2(o[dt][2], o[dt][3]);
-    }
-    if (t4 == 0) {
-      if (ta < a.n) *reinterpret_cast<float2*>(pml + static_cast<int64_t>(ta) * a.n_heads * 2) = make_float2(m0, l0);
-      if (tb < a.n) *reinterpret_cast<float2*>(pml + static_cast<int64_t>(tb) * a.n_heads * 2) = make_float2(m1, l1);
-    }
-    return;
-  }
-  const float i0 = 1.0f / l0, i1 = 1.0f / l1;
-#pragma unroll
-  for (int dt = 0; dt < 16; ++dt) {
-    const int d = 8 * dt + 2 * t4;
-    if (ta < a.n) {
-      *reinterpret_cast<float2*>(a.out + static_cast<int64_t>(ta) * q_dim + qh * kD + d) =
-          make_float2(o[dt][0] * i0, o[dt][1] * i0);
-    }
-    if (tb < a.n) {
-      *reinterpret_cast<float2*>(a.out + static_cast<int64_t>(tb) * q_dim + qh * kD + d) =
-          make_float2(o[dt][2] * i1, o[dt][3] * i1);
-    }
+  FenceBeforeSync();
+  __syncthreads();
+  if (warp == 0) {
+    FenceAfterSync();
+    TmemDealloc(tmem, 256u);
   }
 }
 
@@ -380,10 +457,10 @@ using FlashFn = void (*)(const CUtensorMap, const CUtensorMap, const FlashArgs);
 
 FlashFn PickFlash(int group) {
   switch (group) {
-    case 1: return FlashPrefillKernel<1>;
-    case 2: return FlashPrefillKernel<2>;
-    case 4: return FlashPrefillKernel<4>;
-    case 8: return FlashPrefillKernel<8>;
+    case 1: return FlashTcKernel<1>;
+    case 2: return FlashTcKernel<2>;
+    case 4: return FlashTcKernel<4>;
+    case 8: return FlashTcKernel<8>;
   }
   Throw("flash attention: group size %d is not built", group);
 }
@@ -392,7 +469,7 @@ FlashFn PickFlash(int group) {
 
 void PrepareFlashKernels() {
   for (int g : {1, 2, 4, 8}) {
-    RPGB_CUDA(cudaFuncSetAttribute(PickFlash(g), cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmem)));
+    RPGB_CUDA(cudaFuncSetAttribute(PickFlash(g), cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kTcSmem)));
   }
 }
 
@@ -439,7 +516,7 @@ void LaunchFlashPrefill(const AttnParams& p, int n_queries, int64_t pos0, int nu
   a.part_o = n_split > 1 ? p.part : nullptr;
   a.part_ml = n_split > 1 ? p.part + static_cast<size_t>(n_split) * n_queries * q_dim : nullptr;
   const dim3 grid(qtiles, p.n_kv, n_split);
-  PickFlash(G)<<<grid, kWarps * 32, kSmem, s>>>(mK, mV, a);
+  PickFlash(G)<<<grid, kTcWarps * 32, kTcSmem, s>>>(mK, mV, a);
   RPGB_CUDA(cudaGetLastError());
   CountLaunches(1);
   if (n_split > 1) {

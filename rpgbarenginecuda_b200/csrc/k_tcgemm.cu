@@ -42,9 +42,12 @@
 #include "common.h"
 #include "kernels.cuh"
 #include "kernels.h"
+#include "tc_dev.cuh"
 
 namespace rpgb {
 namespace {
+
+using namespace tc;
 
 constexpr int kBM = 128;     // weight rows per tile (MMA M)
 constexpr int kBN = 128;     // tokens per tile (MMA N)
@@ -158,48 +161,6 @@ __device__ __forceinline__ void TmaLoad2D(void* dst, const CUtensorMap* map, int
       : "memory");
 }
 
-// Shared-memory matrix descriptor of a K-major tile written by TMA with the
-// 128-byte swizzle: rows of 128 bytes, 8-row groups 1024 bytes apart.
-__device__ __forceinline__ uint64_t DescSw128(const void* tile) {
-  const uint32_t a = dev::SmemAddr(tile);
-  uint64_t d = static_cast<uint64_t>((a >> 4) & 0x3FFFu);  // start address
-  d |= static_cast<uint64_t>(1) << 16;                     // leading byte offset (unused with swizzle)
-  d |= static_cast<uint64_t>(1024 >> 4) << 32;             // stride byte offset: one 8-row group
-  d |= static_cast<uint64_t>(1) << 46;                     // descriptor version
-  d |= static_cast<uint64_t>(2) << 61;                     // 128-byte swizzle
-  return d;
-}
-
-// Instruction descriptor: kind::f16, A and B fp16, D fp32, both K-major.
-__host__ __device__ constexpr uint32_t InstrDesc(int m, int n) {
-  return (1u << 4) | (0u << 7) | (0u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
-         (static_cast<uint32_t>(m >> 4) << 24);
-}
-
-__device__ __forceinline__ void Mma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-__device__ __forceinline__ void MmaCommit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   dev::SmemAddr(bar))
-               : "memory");
-}
-__device__ __forceinline__ void FenceBeforeSync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void FenceAfterSync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void TmemLoad16(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
 // ------------------------------------------------------------------ the GEMM
 
 struct TcArgs {
@@ -216,10 +177,6 @@ struct TcArgs {
   int32_t rows;
   int32_t splits;
 };
-
-__device__ __forceinline__ void MbarArrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(dev::SmemAddr(bar)) : "memory");
-}
 
 // Work item it -> its output tile and K range (token tiles fastest, so the
 // blocks running at one time share weight row tiles in L2).
