@@ -68,24 +68,26 @@ __device__ __forceinline__ void TmaLoad3D(void* dst, const CUtensorMap* map, int
 
 // ------------------------------------------------------------------ tcgen05 version
 //
-// The same computation with the two products on the 5th-generation tensor
-// cores and the tiles in TMEM.  One block of 6 warps per (128 / G query
-// tokens, KV head); its 128 rows are (q head g, token) pairs, head-major
-// (row r = g * 128 / G + token), and they are the 128 TMEM lanes:
-//  * warp 4 streams K and V tiles of 64 positions (3-D TMA, 128-byte
+// One block of 10 warps per (128 / G query tokens, KV head); its 128 rows
+// are (q head g, token) pairs, head-major (row r = g * 128 / G + token), and
+// they are the 128 TMEM lanes:
+//  * warp 8 streams K and V tiles of 64 positions (3-D TMA, 128-byte
 //    swizzle, two stages);
-//  * warp 5 issues S = Q K^T (M 128, N 64: Qh K + Ql K, 16 MMAs) into one of
+//  * warp 9 issues S = Q K^T (M 128, N 64: Qh K + Ql K, 16 MMAs) into one of
 //    two 64-column TMEM tiles, one tile ahead of the softmax, then
 //    O += P V (M 128, N 128: Ph Vt + Pl Vt, 8 MMAs) into a 128-column TMEM
 //    accumulator;
-//  * warps 0-3 (thread = row) read their S row, apply the causal mask and
-//    the online softmax in log2 units, rescale their O row in TMEM when the
-//    row maximum grew, write P = Ph + Pl (fp16 terms) into a K-major
-//    swizzled tile, and transpose V into a K-major tile Vt (thread = dim),
-//    which the MMA needs as its B operand.
+//  * warps 0-7, two per row (warp w and w + 4 share TMEM lanes 32 (w % 4) ..
+//    and take 32 of the 64 keys and 64 of the 128 dims each) read their S
+//    half-row, apply the causal mask and the online softmax in log2 units
+//    (the row maximum exchanged through shared memory), rescale their O
+//    half-row in TMEM when the maximum grew, write P = Ph + Pl (fp16 terms)
+//    into a K-major swizzled tile, and transpose V into a K-major tile Vt
+//    (thread = dim), which the MMA needs as its B operand.
 // Q (times scale * log2 e) is split into Qh + Ql fp16 terms once per block.
 // Every mbarrier wait is bounded; a wait that gives up sets *err (64).
-constexpr int kTcWarps = 6;
+constexpr int kTcWarps = 10;  // 8 softmax warps, the TMA warp, the MMA warp
+constexpr int kSoftThreads = 256;
 constexpr uint32_t kQBox = 128 * 128;          // 128 rows x 64 dims fp16 (one swizzled box)
 constexpr uint32_t kTcQ = 2 * kQBox;            // 128 rows x 128 dims
 constexpr uint32_t kTcStage = 4 * kHalfTile;    // K dims 0-63, K dims 64-127, V dims 0-63, V dims 64-127
@@ -128,24 +130,24 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1)
       dev::MbarInit(kv_full + b, 1);
       dev::MbarInit(kv_empty + b, 1);
       dev::MbarInit(s_full + b, 1);
-      dev::MbarInit(s_free + b, 128);
+      dev::MbarInit(s_free + b, kSoftThreads);
     }
-    dev::MbarInit(&p_full, 128);
+    dev::MbarInit(&p_full, kSoftThreads);
     dev::MbarInit(&o_done, 1);
     dev::MbarInit(&fin, 1);
     dev::MbarInitFence();
   }
-  // ---- Q rows (warps 0-3, thread = row): q * scale * log2 e as fp16 hi + lo, swizzled
-  const int row = tid;
+  // ---- Q rows (warps 0-7: thread = row, half hh of the dims): q * scale * log2 e as fp16 hi + lo, swizzled
+  const int row = tid & 127, hh = (tid >> 7) & 1;
   const int g = row / kTQ, tl = row - g * kTQ;
   const int qh = h * G + g;
   const int64_t qpos = a.pos0 + tok0 + tl;
-  if (warp < 4) {
+  if (warp < 8) {
     const bool valid = tok0 + tl < a.n;
     const float* q = a.q + static_cast<int64_t>(valid ? tok0 + tl : 0) * a.q_stride + qh * kD;
     const float qs = a.scale * 1.4426950408889634f;
 #pragma unroll 4
-    for (int c = 0; c < 16; ++c) {  // 8 dims per chunk
+    for (int c = 8 * hh; c < 8 * hh + 8; ++c) {  // 8 dims per chunk
       const float4 x0 = *reinterpret_cast<const float4*>(q + 8 * c);
       const float4 x1 = *reinterpret_cast<const float4*>(q + 8 * c + 4);
       const float v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
@@ -166,7 +168,7 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1)
   FenceAfterSync();
   const uint32_t tmem = s_tmem;
 
-  if (warp == 4) {
+  if (warp == 8) {
     if (lane == 0) {
       // ---- producer: K and V tiles t_lo .. t_lo + nsteps - 1
       int issued = 0;
@@ -189,7 +191,7 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1)
         dev::MbarWait(kv_full + (i & 1), static_cast<uint32_t>((i >> 1) & 1));
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     if (lane == 0) {
       // ---- MMA issuer
       constexpr uint32_t id_s = InstrDesc(128, kKT), id_o = InstrDesc(128, kD);
@@ -241,57 +243,71 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1)
       dev::MbarWait(&fin, 0u);
     }
   } else {
-    // ---- softmax, P, Vt and the output (warps 0-3, thread = row)
-    const uint32_t lrow = static_cast<uint32_t>(32 * warp) << 16;  // this warp's TMEM lanes
+    // ---- softmax, P, Vt and the output (warps 0-7: thread = row, half hh of
+    // the 64 keys of S and of the 128 dims of O)
+    __shared__ float s_mx[2][2][128];  // [tile parity][half][row]
+    __shared__ float s_l[128];
+    const uint32_t lrow = static_cast<uint32_t>(32 * (warp & 3)) << 16;  // this warp's TMEM lanes
+    constexpr int kHK = kKT / 2;  // keys per half
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
+    // A wait that gives up clears ok (warp-uniform); the loop still runs
+    // every iteration's named barrier, so the other half never waits alone.
     for (int j = 0; j < nsteps; ++j) {
       const int b = j & 1;
-      // every wait's outcome is made warp-uniform: the TMEM loads and stores
-      // below are warp-collective
-      if (!__all_sync(0xFFFFFFFFu, dev::MbarWait(s_full + b, static_cast<uint32_t>((j >> 1) & 1)))) {
-        ok = false;
-        break;
-      }
-      FenceAfterSync();
-      float p[kKT];
-#pragma unroll
-      for (int c0 = 0; c0 < kKT; c0 += 16) {
-        uint32_t v[16];
-        TmemLoad16(tmem + lrow + 128u + static_cast<uint32_t>(b * kKT + c0), v);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) p[c0 + i] = __uint_as_float(v[i]);
-      }
-      FenceBeforeSync();
-      MbarArrive(s_free + b);
-      // causal mask, row maximum, probabilities in log2 units
-      const int64_t key0 = static_cast<int64_t>(t_lo + j) * kKT;
+      if (ok && !__all_sync(0xFFFFFFFFu, dev::MbarWait(s_full + b, static_cast<uint32_t>((j >> 1) & 1)))) ok = false;
+      float p[kHK];
       float mx = -INFINITY;
+      if (ok) {
+        FenceAfterSync();
 #pragma unroll
-      for (int c = 0; c < kKT; ++c) {
-        if (key0 + c > qpos) p[c] = -INFINITY;
-        mx = fmaxf(mx, p[c]);
+        for (int c0 = 0; c0 < kHK; c0 += 16) {
+          uint32_t v[16];
+          TmemLoad16(tmem + lrow + 128u + static_cast<uint32_t>(b * kKT + hh * kHK + c0), v);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) p[c0 + i] = __uint_as_float(v[i]);
+        }
+        FenceBeforeSync();
+        MbarArrive(s_free + b);
+        // causal mask: keys past this row's position (lim = last visible key of the half)
+        const int64_t rel = qpos - (static_cast<int64_t>(t_lo + j) * kKT + hh * kHK);
+        const int lim = rel < -1 ? -1 : (rel > kHK ? kHK : static_cast<int>(rel));
+        if (__any_sync(0xFFFFFFFFu, lim < kHK - 1)) {
+#pragma unroll
+          for (int c = 0; c < kHK; ++c) p[c] = c > lim ? -INFINITY : p[c];
+        }
+#pragma unroll
+        for (int c = 0; c < kHK; ++c) mx = fmaxf(mx, p[c]);
       }
+      // the row maximum over both halves
+      s_mx[b][hh][row] = mx;
+      asm volatile("bar.sync 1, %0;" ::"r"(kSoftThreads) : "memory");
+      if (!ok) continue;
+      mx = fmaxf(mx, s_mx[b][hh ^ 1][row]);
       const float m_new = fmaxf(m_run, mx);
       const float alpha = m_run == -INFINITY ? 0.f : exp2f(m_run - m_new);
       float ps = 0.f;
+      if (m_new == -INFINITY) {  // no visible key yet in this row
 #pragma unroll
-      for (int c = 0; c < kKT; ++c) {
-        p[c] = p[c] == -INFINITY ? 0.f : exp2f(p[c] - m_new);
-        ps += p[c];
+        for (int c = 0; c < kHK; ++c) p[c] = 0.f;
+      } else {
+#pragma unroll
+        for (int c = 0; c < kHK; ++c) {
+          p[c] = exp2f(p[c] - m_new);  // exp2(-inf) = 0 for masked keys
+          ps += p[c];
+        }
       }
-      l_run = l_run * alpha + ps;
+      l_run = l_run * alpha + ps;  // this half's share of the row sum
       m_run = m_new;
-      // O, P and Vt are free once the previous tile's P V has completed
       if (j > 0) {
         if (!__all_sync(0xFFFFFFFFu, dev::MbarWait(&o_done, static_cast<uint32_t>((j - 1) & 1)))) {
           ok = false;
-          break;
+          continue;
         }
         FenceAfterSync();
         if (__any_sync(0xFFFFFFFFu, alpha != 1.f)) {
 #pragma unroll 2
-          for (int c0 = 0; c0 < kD; c0 += 16) {
+          for (int c0 = 64 * hh; c0 < 64 * hh + 64; c0 += 16) {
             uint32_t v[16];
             TmemLoad16(tmem + lrow + static_cast<uint32_t>(c0), v);
 #pragma unroll
@@ -302,32 +318,35 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1)
         }
       }
 #pragma unroll
-      for (int c = 0; c < kKT / 8; ++c) {
+      for (int c = 0; c < kHK / 8; ++c) {
         uint32_t hi[4], lo[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) SplitPair(p[8 * c + 2 * i], p[8 * c + 2 * i + 1], hi[i], lo[i]);
-        *reinterpret_cast<uint4*>(sPh + Swz(row, c)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        *reinterpret_cast<uint4*>(sPl + Swz(row, c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        *reinterpret_cast<uint4*>(sPh + Swz(row, 4 * hh + c)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4*>(sPl + Swz(row, 4 * hh + c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
       }
-      // V^T (thread = dim d): the K-major B operand of P V
       if (!__all_sync(0xFFFFFFFFu, dev::MbarWait(kv_full + b, static_cast<uint32_t>((j >> 1) & 1)))) {
         ok = false;
-        break;
+        continue;
       }
       {
+        // V^T: thread = dim d (row), keys of half hh
         const int d = row, box = d >> 6, col = d & 63, cc = col >> 3;
-        const uint8_t* vb = sKV + b * kTcStage + 2 * kHalfTile + box * kHalfTile + (col & 7) * 2;
+        const uint8_t* vb = sKV + b * kTcStage + 2 * kHalfTile + box * kHalfTile + (col & 7) * 2 + 32 * hh * 128;
+        // key k = 32 hh + 8 c + i sits in swizzled chunk cc ^ i of its row
+        const uint8_t* vi[8];
 #pragma unroll
-        for (int c = 0; c < kKT / 8; ++c) {
+        for (int i = 0; i < 8; ++i) vi[i] = vb + ((cc ^ i) << 4);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
           uint32_t w[4];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const int k0 = 8 * c + 2 * i;
-            const uint32_t lo16 = *reinterpret_cast<const uint16_t*>(vb + Swz(k0, cc));
-            const uint32_t hi16 = *reinterpret_cast<const uint16_t*>(vb + Swz(k0 + 1, cc));
+            const uint32_t lo16 = *reinterpret_cast<const uint16_t*>(vi[2 * i] + (8 * c + 2 * i) * 128);
+            const uint32_t hi16 = *reinterpret_cast<const uint16_t*>(vi[2 * i + 1] + (8 * c + 2 * i + 1) * 128);
             w[i] = lo16 | (hi16 << 16);
           }
-          *reinterpret_cast<uint4*>(sVt + Swz(d, c)) = make_uint4(w[0], w[1], w[2], w[3]);
+          *reinterpret_cast<uint4*>(sVt + Swz(d, 4 * hh + c)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
       dev::FenceProxyAsync();  // P and Vt (generic writes) are read by the MMAs
@@ -341,18 +360,27 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1)
       if (lane == 0) atomicOr(a.err, 64u);
     }
     FenceAfterSync();
-    // ---- O / l (or the unnormalised partial of this key split)
+    // the row sum over both halves (a failed half skips the exchange: the
+    // other half's wait on the named barrier is then the block's own)
+    if (hh == 1) s_l[row] = l_run;
+    asm volatile("bar.sync 1, %0;" ::"r"(kSoftThreads) : "memory");
+    const float l_row = hh == 0 ? l_run + s_l[row] : s_l[row] + 0.f;
+    asm volatile("bar.sync 1, %0;" ::"r"(kSoftThreads) : "memory");
+    if (hh == 0) s_l[row] = l_row;
+    asm volatile("bar.sync 1, %0;" ::"r"(kSoftThreads) : "memory");
+    const float l_all = s_l[row];
+    // ---- O / l (or the unnormalised partial of this key split): dims of half hh
     const int t = tok0 + tl;
     const int q_dim = a.n_heads * kD;
     const bool store = ok && t < a.n && nsteps > 0;  // (every split holds at least two key tiles)
     if (n_split > 1) {
       float* po = a.part_o + (static_cast<int64_t>(z) * a.n + t) * q_dim + qh * kD;
-      if (store) {
+      if (store && hh == 0) {
         float* pml = a.part_ml + ((static_cast<int64_t>(z) * a.n + t) * a.n_heads + qh) * 2;
-        *reinterpret_cast<float2*>(pml) = make_float2(m_run * 0.6931471805599453f, l_run);
+        *reinterpret_cast<float2*>(pml) = make_float2(m_run * 0.6931471805599453f, l_all);
       }
 #pragma unroll 2
-      for (int c0 = 0; c0 < kD; c0 += 16) {
+      for (int c0 = 64 * hh; c0 < 64 * hh + 64; c0 += 16) {
         uint32_t v[16];
         TmemLoad16(tmem + lrow + static_cast<uint32_t>(c0), v);
         if (store) {
@@ -365,9 +393,9 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1)
       }
     } else {
       float* out = a.out + static_cast<int64_t>(t) * q_dim + qh * kD;
-      const float inv = 1.0f / l_run;
+      const float inv = 1.0f / l_all;
 #pragma unroll 2
-      for (int c0 = 0; c0 < kD; c0 += 16) {
+      for (int c0 = 64 * hh; c0 < 64 * hh + 64; c0 += 16) {
         uint32_t v[16];
         TmemLoad16(tmem + lrow + static_cast<uint32_t>(c0), v);
         if (store) {
