@@ -276,6 +276,7 @@ void Session::EnsurePrefill(int64_t n) {
   cv.Add(sizeof(__half) * tc_halves);
   const size_t gpart_floats = TcGemmPartFloats(m_->num_sms());  // split-K partial tiles
   cv.Add(sizeof(float) * gpart_floats);
+  cv.Add(sizeof(__half) * 2 * cap * c.hidden);  // normalised rows as fp16 hi/lo GEMM operands
   RPGB_CUDA(cudaStreamSynchronize(stream_));
   cudaFree(pf_arena_);
   pf_arena_ = nullptr;
@@ -294,6 +295,7 @@ void Session::EnsurePrefill(int64_t n) {
   pf_tc_halves_ = tc_halves;
   pf_gpart_ = cv.Take<float>(gpart_floats);
   pf_gpart_floats_ = gpart_floats;
+  pf_xs_ = cv.Take<__half>(2 * cap * c.hidden);
   pf_cap_ = cap;
 }
 
@@ -339,12 +341,21 @@ void Session::Prefill(const int32_t* tokens, int64_t n, float* last_logits) {
   // multi-token matvec: the decode matvec's units applied to up to four
   // tokens per pass while each weight unit is in shared memory.
   const bool rowwise = nt < kTcMinTokens;
+  // the RMSNorm kernels write the GEMM's fp16 activation terms directly when
+  // every GEMM reading their output runs on the tensor cores
+  __half* xs_h = pf_xs_;
+  __half* xs_l = pf_xs_ + static_cast<size_t>(pf_cap_) * H;
   LaunchEmbed(m_->embd(), pf_tok_, nt, pf_x_, nullptr, nullptr, s);
   for (int l = 0; l < c.n_layers; ++l) {
     const DevLayer& L = m_->layers()[static_cast<size_t>(l)];
     __half* kc = kc_ + layer_elems_ * l;
     __half* vc = vc_ + layer_elems_ * l;
-    LaunchRmsNormRows(pf_x_, L.attn_norm, nt, H, c.rms_eps, pf_xn_, s);
+    const bool split_a = !rowwise && L.q.rows % 128 == 0 && L.k.rows % 128 == 0 && L.v.rows % 128 == 0;
+    if (split_a) {
+      LaunchRmsNormRows(pf_x_, L.attn_norm, nt, H, c.rms_eps, nullptr, s, xs_h, xs_l);
+    } else {
+      LaunchRmsNormRows(pf_x_, L.attn_norm, nt, H, c.rms_eps, pf_xn_, s);
+    }
     if (rowwise) {
       const DevMat w3[3] = {L.q, L.k, L.v};
       const int off3[3] = {0, qd, qd + kvd};
@@ -358,6 +369,8 @@ void Session::Prefill(const int32_t* tokens, int64_t n, float* last_logits) {
       g.num_sms = m_->num_sms();
       g.err = err_;
       g.X = pf_xn_;
+      g.xh = split_a ? xs_h : nullptr;
+      g.xl = split_a ? xs_l : nullptr;
       g.n_tok = nt;
       g.ldx = H;
       g.out = pf_qkv_;
@@ -431,7 +444,12 @@ void Session::Prefill(const int32_t* tokens, int64_t n, float* last_logits) {
         LaunchGemm(o, Epi::kResid, s);
       }
     }
-    LaunchRmsNormRows(pf_x_, L.ffn_norm, nt, H, c.rms_eps, pf_xn_, s);
+    const bool split_f = !rowwise && L.gateup.rows % 128 == 0;
+    if (split_f) {
+      LaunchRmsNormRows(pf_x_, L.ffn_norm, nt, H, c.rms_eps, nullptr, s, xs_h, xs_l);
+    } else {
+      LaunchRmsNormRows(pf_x_, L.ffn_norm, nt, H, c.rms_eps, pf_xn_, s);
+    }
     if (rowwise) {
       const int off0[1] = {0};
       RowwiseMatvec(&L.gateup, off0, 1, pf_xn_, H, pf_h_, c.ffn, false, Epi::kSilu, nt, s);
@@ -452,6 +470,8 @@ void Session::Prefill(const int32_t* tokens, int64_t n, float* last_logits) {
     gu.err = err_;
     gu.w = L.gateup;
     gu.X = pf_xn_;
+    gu.xh = split_f ? xs_h : nullptr;
+    gu.xl = split_f ? xs_l : nullptr;
     gu.n_tok = nt;
     gu.ldx = H;
     gu.out = pf_h_;

@@ -156,6 +156,7 @@ class Session {
   size_t pf_tc_halves_ = 0;
   float* pf_gpart_ = nullptr;  // split-K partial tiles of the tensor-core GEMM
   size_t pf_gpart_floats_ = 0;
+  __half* pf_xs_ = nullptr;  // normalised rows as fp16 hi / lo GEMM operands ([cap][hidden] each)
   int32_t* host_ids_ = nullptr;  // pinned staging
   int64_t host_ids_cap_ = 0;
 

@@ -732,11 +732,15 @@ __global__ void __launch_bounds__(128) QkRopeKvKernel(const float* __restrict__ 
   }
 }
 
+// out (when given) gets the normalised row in FP32; hi / lo (when given) get
+// it as the two fp16 terms of the tensor-core GEMM's activation operand
+// (hi = fp16(v), lo = fp16(v - hi), the values SplitKernel would write).
 __global__ void __launch_bounds__(256) RmsNormRowsKernel(const float* __restrict__ x, const float* __restrict__ w,
-                                                         int n, float eps, float* __restrict__ out) {
+                                                         int n, float eps, float* __restrict__ out,
+                                                         __half* __restrict__ hi, __half* __restrict__ lo) {
   __shared__ double dsh[32];
-  const float* xr = x + static_cast<int64_t>(blockIdx.x) * n;
-  float* orow = out + static_cast<int64_t>(blockIdx.x) * n;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * n;
+  const float* xr = x + r0;
   double ss = 0.0;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const double v = static_cast<double>(xr[i]);
@@ -744,7 +748,15 @@ __global__ void __launch_bounds__(256) RmsNormRowsKernel(const float* __restrict
   }
   const double tot = dev::BlockSumD(ss, dsh);
   const float scale = static_cast<float>(1.0 / sqrt(tot / static_cast<double>(n) + static_cast<double>(eps)));
-  for (int i = threadIdx.x; i < n; i += blockDim.x) orow[i] = xr[i] * scale * w[i];
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = xr[i] * scale * w[i];
+    if (out != nullptr) out[r0 + i] = v;
+    if (hi != nullptr) {
+      const __half h = __float2half_rn(v);
+      hi[r0 + i] = h;
+      lo[r0 + i] = __float2half_rn(v - __half2float(h));
+    }
+  }
 }
 
 }  // namespace
@@ -811,9 +823,11 @@ void LaunchQkRopeKv(const float* qkv, int n_tok, int q_dim, int kv_dim, const fl
   CountLaunches(1);
 }
 
-void LaunchRmsNormRows(const float* x, const float* w, int n_rows, int n, float eps, float* out, cudaStream_t s) {
+void LaunchRmsNormRows(const float* x, const float* w, int n_rows, int n, float eps, float* out, cudaStream_t s,
+                       __half* hi, __half* lo) {
   RPGB_CHECK(n_rows > 0 && n > 0, "rmsnorm: empty");
-  RmsNormRowsKernel<<<n_rows, 256, 0, s>>>(x, w, n, eps, out);
+  RPGB_CHECK((hi == nullptr) == (lo == nullptr) && (out != nullptr || hi != nullptr), "rmsnorm: bad outputs");
+  RmsNormRowsKernel<<<n_rows, 256, 0, s>>>(x, w, n, eps, out, hi, lo);
   RPGB_CUDA(cudaGetLastError());
   CountLaunches(1);
 }

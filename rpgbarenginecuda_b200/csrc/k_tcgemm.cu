@@ -486,7 +486,11 @@ void LaunchTcGemm(const GemmParams& p, Epi epi, __half* scratch, size_t scratch_
     xh = scratch + 2 * static_cast<size_t>(w.rows) * K;
   }
   __half* xl = xh + static_cast<size_t>(p.n_tok) * K;
-  {
+  if (p.xh != nullptr) {  // split by the kernel that produced the activations
+    RPGB_CHECK(p.xl != nullptr, "tcgen05 gemm: activation terms incomplete");
+    xh = const_cast<__half*>(p.xh);
+    xl = const_cast<__half*>(p.xl);
+  } else {
     const int64_t items = static_cast<int64_t>(p.n_tok) * (K / 8);
     const int blocks = static_cast<int>(std::min<int64_t>((items + 255) / 256, 148 * 16));
     SplitKernel<<<blocks, 256, 0, s>>>(p.X, p.n_tok, p.ldx, K, xh, xl);

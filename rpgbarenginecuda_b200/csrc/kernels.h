@@ -163,8 +163,11 @@ void LaunchQkRopeKv(const float* qkv, int n_tok, int q_dim, int kv_dim, const fl
                     const float* k_norm, const float* rope, float eps, const int64_t* pos0, __half* kc,
                     __half* vc, int32_t max_seq, int n_heads, int n_kv, float* q_out, cudaStream_t s);
 
-// Row-wise RMSNorm (double sum of squares, as src/kernels_gpu.cu:564-591).
-void LaunchRmsNormRows(const float* x, const float* w, int n_rows, int n, float eps, float* out, cudaStream_t s);
+// Row-wise RMSNorm (double sum of squares, as src/kernels_gpu.cu:564-591):
+// the normalised rows in FP32 (out) and/or as the fp16 hi/lo terms of the
+// tensor-core GEMM's activation operand (hi, lo: [n_rows][n] each).
+void LaunchRmsNormRows(const float* x, const float* w, int n_rows, int n, float eps, float* out, cudaStream_t s,
+                       __half* hi = nullptr, __half* lo = nullptr);
 
 // ------------------------------------------------------------------ prefill GEMM
 struct GemmParams {
@@ -188,6 +191,10 @@ struct GemmParams {
   float* part = nullptr;
   size_t part_floats = 0;
   int32_t num_sms = 0;
+  // the activations already split into fp16 terms ([n][cols] each, from
+  // LaunchRmsNormRows): the tensor-core path then skips its own split
+  const __half* xh = nullptr;
+  const __half* xl = nullptr;
 };
 // Prompts of at least kTcMinTokens tokens (and weight rows a multiple of 128)
 // run on the tcgen05 GEMM when scratch is given; others on the FP32 SIMT tile.
