@@ -274,7 +274,10 @@ void Session::EnsurePrefill(int64_t n) {
                                                                 static_cast<int64_t>(c.q_dim()) * c.hidden);
   const size_t tc_halves = 2 * static_cast<size_t>(wmax) + 2 * static_cast<size_t>(cap) * kmax;
   cv.Add(sizeof(__half) * tc_halves);
-  const size_t gpart_floats = TcGemmPartFloats(m_->num_sms());  // split-K partial tiles
+  // split-K partial tiles: the few-tiles case, or two halves of the
+  // hidden-size outputs (attn_output, ffn_down) of the whole prompt
+  const size_t gpart_floats =
+      std::max(TcGemmPartFloats(m_->num_sms()), 2 * static_cast<size_t>(cap) * static_cast<size_t>(c.hidden));
   cv.Add(sizeof(float) * gpart_floats);
   cv.Add(sizeof(__half) * 2 * cap * c.hidden);  // normalised rows as fp16 hi/lo GEMM operands
   RPGB_CUDA(cudaStreamSynchronize(stream_));

@@ -445,7 +445,15 @@ size_t TcGemmScratchHalves(int64_t rows, int64_t n_tok, int K, bool has_wh) {
 int TcGemmSplits(int64_t rows, int64_t n_tok, int K, int num_sms, size_t part_floats) {
   const int64_t tiles = (rows / kBM) * ((n_tok + kBN - 1) / kBN);
   const int nk = K / kBK;
-  if (num_sms <= 0 || tiles * 2 > num_sms || nk < 8) return 1;
+  if (num_sms <= 0 || nk < 8) return 1;
+  if (tiles * 2 > num_sms) {
+    // many tiles: split in two when the last wave of whole tiles would be
+    // short (two waves and a fifth of whole tiles take three tile times,
+    // five waves of half tiles two and a half), if the partials fit
+    const int64_t w1 = (tiles + num_sms - 1) / num_sms, w2 = (2 * tiles + num_sms - 1) / num_sms;
+    const bool fits = static_cast<size_t>(2 * rows * n_tok) <= part_floats;
+    return fits && nk >= 16 && 20 * w2 <= 17 * 2 * w1 ? 2 : 1;
+  }
   // enough splits to fill the SMs, at least four k-slices each, and room
   // for the partial tiles
   int64_t sp = std::min<int64_t>(num_sms / tiles, nk / 4);
