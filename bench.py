@@ -17,8 +17,9 @@ tokens, 64-token decode) with T=0.7, top_k=20, top_p=0.8 and a fixed seed.
            per cached position), divided by the decode device time from CUDA
            events on the session stream.
 * roofline_matvec  the standalone decode matvec: every matrix of the model
-           plus lm_head, one launch each, CUDA events on the launching stream,
-           algorithmic bytes = M*K/256*{144,210} + x + y.
+           plus lm_head, one launch each, back to back in a CUDA graph, CUDA
+           events on the launching stream, algorithmic bytes =
+           M*K/256*{144,210} + x + y.
 * cpu_baseline  the CPU restatement of the reference loop (oracle/, the
            reference's own CPU engine is not vendored), bounded sample.
 
@@ -212,10 +213,11 @@ def reference_arm(args):
 
 def matvec_roofline(path, device, peak):
     """Decode matvec roofline: every matrix of the model launched back to back
-    on one stream (one decode's weight stream, 1.1 GB > L2), three passes,
-    CUDA events around each pass; algorithmic bytes = M*K/256*{144,210} +
-    4(M+K) per launch.  The lm_head shape (151936 x 2048 Q6_K, 255 MB) is also
-    timed alone, 20 launches back to back."""
+    (one decode's weight stream, 1.1 GB > L2), one pass captured in a CUDA
+    graph so that the host's per-call cost stays out of the device timeline,
+    three replays timed with CUDA events; algorithmic bytes =
+    M*K/256*{144,210} + 4(M+K) per launch.  The lm_head shape (151936 x 2048
+    Q6_K, 255 MB) is also timed alone, 20 launches back to back."""
     import numpy as np
     import torch
     from gguf import GGUFReader
@@ -241,14 +243,20 @@ def matvec_roofline(path, device, peak):
     for m, _, _, _, _ in handles:  # warm-up pass
         m.matvec(x.data_ptr(), 1, y.data_ptr(), sp)
     torch.cuda.synchronize(device)
+    graph, cap = torch.cuda.CUDAGraph(), torch.cuda.Stream(device)
+    with torch.cuda.graph(graph, stream=cap, capture_error_mode="thread_local"):
+        cs = torch.cuda.current_stream(device).cuda_stream
+        for m, _, _, _, _ in handles:
+            m.matvec(x.data_ptr(), 1, y.data_ptr(), cs)
+    graph.replay()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     passes = 3
     e0.record(stream)
     for _ in range(passes):
-        for m, _, _, _, _ in handles:
-            m.matvec(x.data_ptr(), 1, y.data_ptr(), sp)
+        graph.replay()
     e1.record(stream)
     e1.synchronize()
+    del graph
     ms = e0.elapsed_time(e1)
     total_bytes = passes * sum(nbytes(q, r, c) for _, q, r, c, _ in handles)
     launches = passes * len(handles)
@@ -274,7 +282,7 @@ def matvec_roofline(path, device, peak):
             traffic = round(sum(per[k] for k in keys) / len(keys))
     return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
             "frac": round(achieved / peak, 4), "traffic": traffic,
-            "kernel": "MatvecKernel (decode Q4_K/Q6_K dequant-matvec, n=1): all matrices of the model, back to back",
+            "kernel": "MatvecKernel (decode Q4_K/Q6_K dequant-matvec, n=1): all matrices of the model, back to back in a CUDA graph",
             "bytes_per_launch": round(total_bytes / launches), "avg_launch_us": round(1000 * ms / launches, 2),
             "lm_head": {"shape": f"{'q4k' if q == 12 else 'q6k'}_{r}x{c}", "bytes": nbytes(q, r, c),
                         "avg_launch_us": round(1000 * big_ms, 2), "gbs": round(big_gbs, 1),
