@@ -20,7 +20,11 @@
 //  * DequantSplitKernel writes a matrix as Wh / Wl (row-major, fp16) with the
 //    bit-exact per-element dequant formulas -- once at model load into the
 //    model's own copy (Model::Load), or per call into the call's scratch for
-//    a matrix without one; SplitKernel writes Xh / Xl;
+//    a matrix without one; SplitKernel writes Xh / Xl (unless the producer
+//    of X already wrote them: the prefill's RMSNorm does);
+//  * a GEMM with few output tiles, or whose whole tiles would leave a short
+//    last wave, splits its K range (blockIdx-free: the work items carry the
+//    split) and SplitReduceKernel adds the partials in split order;
 //  * warp 0 streams 64-column k-slices of Wh, Wl, Xh, Xl into three
 //    shared-memory stages with 2-D TMA tensor copies (128-byte swizzle);
 //  * warp 1 issues tcgen05.mma.cta_group::1.kind::f16 (M 128, N 128, K 16;
