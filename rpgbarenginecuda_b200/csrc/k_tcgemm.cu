@@ -356,7 +356,33 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // Sum of the split-K partials in split order, then the GEMM's epilogue.
 template <int EPI>
-__global__ void __launch_bounds__(256) SplitReduceKernel(const TcArgs a, int splits) {
+// With vec4 (16-byte aligned output, residual and offsets) the store and
+// residual epilogues move four consecutive rows per thread.
+__global__ void __launch_bounds__(256) SplitReduceKernel(const TcArgs a, int splits, bool vec4) {
+  if (EPI != static_cast<int>(Epi::kSilu) && vec4) {
+    const int64_t per4 = a.rows / 4;
+    const int64_t items = static_cast<int64_t>(a.n_tok) * per4;
+    const int64_t plane = static_cast<int64_t>(a.n_tok) * a.rows;
+    for (int64_t it = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; it < items;
+         it += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+      const int64_t t = it / per4, i = (it - t * per4) * 4;
+      float4 v = *reinterpret_cast<const float4*>(a.part + t * a.rows + i);
+      for (int z = 1; z < splits; ++z) {
+        const float4 w = *reinterpret_cast<const float4*>(a.part + z * plane + t * a.rows + i);
+        v.x += w.x;
+        v.y += w.y;
+        v.z += w.z;
+        v.w += w.w;
+      }
+      if (EPI == static_cast<int>(Epi::kResid)) {
+        const float4 r = *reinterpret_cast<const float4*>(a.resid + t * a.ldr + i);
+        *reinterpret_cast<float4*>(a.out + t * a.ldo + i) = make_float4(r.x + v.x, r.y + v.y, r.z + v.z, r.w + v.w);
+      } else {
+        *reinterpret_cast<float4*>(a.out + t * a.ldo + a.out_off + i) = v;
+      }
+    }
+    return;
+  }
   const int64_t per = EPI == static_cast<int>(Epi::kSilu) ? a.rows / 2 : a.rows;
   const int64_t items = static_cast<int64_t>(a.n_tok) * per;
   const int64_t plane = static_cast<int64_t>(a.n_tok) * a.rows;
@@ -531,12 +557,15 @@ void LaunchTcGemm(const GemmParams& p, Epi epi, __half* scratch, size_t scratch_
   RPGB_CUDA(cudaGetLastError());
   CountLaunches(2);
   if (splits > 1) {
-    const int64_t items = static_cast<int64_t>(p.n_tok) * w.rows;
+    const auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    const bool vec4 = epi != Epi::kSilu && a.ldo % 4 == 0 && a.out_off % 4 == 0 && al16(a.out) && al16(a.part) &&
+                      (epi != Epi::kResid || (a.ldr % 4 == 0 && al16(a.resid)));
+    const int64_t items = static_cast<int64_t>(p.n_tok) * w.rows / (vec4 ? 4 : 1);
     const int blocks = static_cast<int>(std::min<int64_t>((items + 255) / 256, 148 * 8));
     switch (epi) {
-      case Epi::kStore: SplitReduceKernel<0><<<blocks, 256, 0, s>>>(a, splits); break;
-      case Epi::kResid: SplitReduceKernel<1><<<blocks, 256, 0, s>>>(a, splits); break;
-      case Epi::kSilu: SplitReduceKernel<2><<<blocks, 256, 0, s>>>(a, splits); break;
+      case Epi::kStore: SplitReduceKernel<0><<<blocks, 256, 0, s>>>(a, splits, vec4); break;
+      case Epi::kResid: SplitReduceKernel<1><<<blocks, 256, 0, s>>>(a, splits, vec4); break;
+      case Epi::kSilu: SplitReduceKernel<2><<<blocks, 256, 0, s>>>(a, splits, false); break;
       default: Throw("tcgen05 gemm: unsupported epilogue");
     }
     RPGB_CUDA(cudaGetLastError());
