@@ -479,6 +479,15 @@ void Session::Prefill(const int32_t* tokens, int64_t n, float* last_logits) {
     gu.ldx = H;
     gu.out = pf_h_;
     gu.ldo = c.ffn;
+    // the gate/up epilogue writes ffn_down's fp16 operand terms into pf_h_'s
+    // space (2 cap ffn halves) in place of the FP32 rows
+    const bool split_d = split_f && L.down.rows % 128 == 0;
+    __half* const hd_h = reinterpret_cast<__half*>(pf_h_);
+    __half* const hd_l = hd_h + static_cast<size_t>(pf_cap_) * c.ffn;
+    if (split_d) {
+      gu.out_h = hd_h;
+      gu.out_l = hd_l;
+    }
     LaunchGemm(gu, Epi::kSilu, s);
     GemmParams dn;
     dn.tc_scratch = pf_tc_;
@@ -489,6 +498,8 @@ void Session::Prefill(const int32_t* tokens, int64_t n, float* last_logits) {
     dn.err = err_;
     dn.w = L.down;
     dn.X = pf_h_;
+    dn.xh = split_d ? hd_h : nullptr;
+    dn.xl = split_d ? hd_l : nullptr;
     dn.n_tok = nt;
     dn.ldx = c.ffn;
     dn.ldo = H;

@@ -149,6 +149,7 @@ void LaunchGemm(const GemmParams& p, Epi epi, cudaStream_t s) {
     return;
   }
   RPGB_CHECK(p.w.q != nullptr, "gemm: the FP32 tile path needs the quantised matrix");
+  RPGB_CHECK(p.out_h == nullptr, "gemm: fp16 output terms need the tensor-core path");
   RPGB_CHECK(p.w.rows % BM == 0, "gemm: rows %d not a multiple of %d", p.w.rows, BM);
   RPGB_CHECK(p.w.cols % 256 == 0, "gemm: cols %d not a multiple of 256", p.w.cols);
   RPGB_CHECK(p.n_tok > 0, "gemm: no tokens");

@@ -21,7 +21,8 @@
 //    bit-exact per-element dequant formulas -- once at model load into the
 //    model's own copy (Model::Load), or per call into the call's scratch for
 //    a matrix without one; SplitKernel writes Xh / Xl (unless the producer
-//    of X already wrote them: the prefill's RMSNorm does);
+//    of X already wrote them: the prefill's RMSNorm does, and so does the
+//    SiLU epilogue for ffn_down when given out_h / out_l);
 //  * a GEMM with few output tiles, or whose whole tiles would leave a short
 //    last wave, splits its K range (blockIdx-free: the work items carry the
 //    split) and SplitReduceKernel adds the partials in split order;
@@ -180,7 +181,20 @@ struct TcArgs {
   float* part;
   int32_t rows;
   int32_t splits;
+  // SiLU epilogue: fp16 hi/lo terms of the output instead of out (or null)
+  __half* oh;
+  __half* ol;
 };
+
+__device__ __forceinline__ void StoreSilu(const TcArgs& a, int64_t idx, float y) {
+  if (a.oh != nullptr) {
+    const __half h = __float2half_rn(y);
+    a.oh[idx] = h;
+    a.ol[idx] = __float2half_rn(y - __half2float(h));
+  } else {
+    a.out[idx] = y;
+  }
+}
 
 // Work item it -> its output tile and K range (token tiles fastest, so the
 // blocks running at one time share weight row tiles in L2).
@@ -330,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // rows 2i (gate) and 2i+1 (up) sit in neighbouring lanes
             const float u = __shfl_xor_sync(0xFFFFFFFFu, acc, 1);
             if (t < a.n_tok && (lane & 1) == 0) {
-              a.out[static_cast<int64_t>(t) * a.ldo + (r >> 1)] = (acc / (1.0f + expf(-acc))) * u;
+              StoreSilu(a, static_cast<int64_t>(t) * a.ldo + (r >> 1), (acc / (1.0f + expf(-acc))) * u);
             }
           } else if (t < a.n_tok) {
             if (EPI == static_cast<int>(Epi::kResid)) {
@@ -396,7 +410,7 @@ __global__ void __launch_bounds__(256) SplitReduceKernel(const TcArgs a, int spl
         g += gu.x;
         u += gu.y;
       }
-      a.out[t * a.ldo + i] = (g / (1.0f + expf(-g))) * u;
+      StoreSilu(a, t * a.ldo + i, (g / (1.0f + expf(-g))) * u);
     } else {
       float v = 0.f;
       for (int z = 0; z < splits; ++z) v += a.part[z * plane + t * a.rows + i];
@@ -547,6 +561,10 @@ void LaunchTcGemm(const GemmParams& p, Epi epi, __half* scratch, size_t scratch_
   a.err = p.err;
   a.part = p.part;
   a.rows = w.rows;
+  RPGB_CHECK((p.out_h == nullptr) == (p.out_l == nullptr) && (p.out_h == nullptr || epi == Epi::kSilu),
+             "tcgen05 gemm: fp16 output terms are for the SiLU epilogue");
+  a.oh = p.out_h;
+  a.ol = p.out_l;
   const int num_sms = p.num_sms > 0 ? p.num_sms : DeviceSms();
   const int splits = TcGemmSplits(w.rows, p.n_tok, K, num_sms, p.part_floats);
   a.splits = splits;

@@ -195,6 +195,11 @@ struct GemmParams {
   // LaunchRmsNormRows): the tensor-core path then skips its own split
   const __half* xh = nullptr;
   const __half* xl = nullptr;
+  // SiLU epilogue of the tensor-core path: write SiLU(g) * u as its fp16
+  // hi/lo terms ([n][ldo] each, the values SplitKernel would make) instead
+  // of FP32 out, to be the next GEMM's xh / xl
+  __half* out_h = nullptr;
+  __half* out_l = nullptr;
 };
 // Prompts of at least kTcMinTokens tokens (and weight rows a multiple of 128)
 // run on the tcgen05 GEMM when scratch is given; others on the FP32 SIMT tile.
